@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""bench.py — the fused rANS-decode + MXFP4 MoE layer on B200.
+
+Workload (one "step"): one gpt-oss-120b MoE layer for one token. 128 experts (gate, up, down
+2880 x 2880 MXFP4 each, seeded synthetic weights, see troncons_b200/synth.py) are resident in
+HBM as `.trc` v1.2 parts; x is bf16[2880]; the router (f32 128 x 2880) picks 4 experts; the
+layer decodes their DELTA and CODES_CTX streams fused into the gate/up GEMV, applies the clamped
+SwiGLU, the fused down projection, and adds the weighted combine to the f32 residual.
+
+Metric: GB/s of algorithmic bytes per step = the useful bytes of the 4 routed experts' parts
+(what the layer must read) + the router's f32 weights and biases + the layer's LUTs + x and
+the residual read and written. `value`: inputs already in HBM, L2 flushed (256 MB written)
+between steps, each step timed with CUDA events on its stream. `e2e`: the same through the C-ABI
+from pinned host buffers (x and residual copied in, residual copied out, inside the timing).
+`--impl reference`: the reference's path on host cores (the oracle's C port of trc-codec's
+decoder and the layer's numerics; the reference's Rust CPU codec cannot be built here).
+
+Multi-GPU (torchrun): one process per GPU, each runs its own replica of the workload (weak
+scaling, no collective on the data path yet); times are the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+RACINE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, RACINE)
+
+METRIQUE = "fused rANS+MXFP4 GEMV GB/s vs HBM peak; gpt-oss-120b tok/s at 1/2/4/8 B200"
+UNITE = "GB/s"
+
+
+def arguments():
+    a = argparse.ArgumentParser()
+    a.add_argument("--gpus", type=int, default=1)
+    a.add_argument("--steps", type=int, default=30)
+    a.add_argument("--warmup", type=int, default=5)
+    a.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    a.add_argument("--experts", type=int, default=128)
+    a.add_argument("--k", type=int, default=4)
+    a.add_argument("--graine", type=int, default=20261201)
+    a.add_argument("--n-delta", type=int, default=256, help="macro-steps per DELTA tile the parts are encoded with")
+    a.add_argument("--n-codes", type=int, default=256, help="macro-steps per CODES_CTX tile")
+    a.add_argument("--no-cpu-baseline", action="store_true")
+    return a.parse_args()
+
+
+def rang():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def pics():
+    try:
+        with open(os.path.join(RACINE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Horloges:
+    """nvidia-smi clock samples while the timed region runs (the GPU named by its UUID)."""
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+        self.lignes = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._lire, daemon=True)
+            self.t.start()
+        except Exception:
+            self.p = None
+        return self
+
+    def _lire(self):
+        for l in self.p.stdout:
+            self.lignes.append(l.strip())
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def resume(self):
+        sm, mx, raisons = [], 0.0, set()
+        noms = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lignes:
+            c = [x.strip() for x in l.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx = max(mx, float(c[2]))
+            except ValueError:
+                continue
+            for nom, v in zip(noms, c[5:9]):
+                if v.lower() == "active":
+                    raisons.add(nom)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(raisons), "samples": len(sm)}
+
+
+def construire_couche(args):
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+
+    t0 = time.time()
+    c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=False, n_delta=args.n_delta,
+                 n_codes=args.n_codes)
+    return c, time.time() - t0
+
+
+def octets_pas(c, idx, k):
+    """Algorithmic bytes of one step with experts `idx` routed."""
+    utiles = sum(int.from_bytes(c.parties[int(e)][12:16], "little") for e in idx[:k])
+    E, C = c.experts, c.dims.colonnes[0]
+    return utiles + 4 * E * C + 4 * E + 3 * 4 * 4 * 4096 + 2 * C + 2 * 4 * c.dims.lignes[2]
+
+
+def octets_codes_porte_haut(c, idx, k):
+    """Compressed CODES_CTX bytes of gate and up of the routed experts: what the dominant
+    launch (k_moe_codes, gate/up) must stream from HBM."""
+    total = 0
+    for e in idx[:k]:
+        p = c.parties[int(e)]
+        n = int.from_bytes(p[10:12], "little")
+        for i in range(n):
+            d = p[64 + 16 * i:80 + 16 * i]
+            if d[0] == 0x04 and d[1] in (0, 1):
+                total += int.from_bytes(d[8:12], "little")
+    return total
+
+
+def notre_bras(args):
+    import numpy as np
+    import torch
+
+    r, w, lr = rang()
+    torch.cuda.set_device(lr)
+    dist = None
+    if w > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    import troncons_b200 as T  # noqa: F401
+    from troncons_b200.carte import CoucheCarte
+
+    c, t_gen = construire_couche(args)
+    cc = CoucheCarte(c, k=args.k, brut=False, n_delta=args.n_delta, n_codes=args.n_codes)
+    n_pas = args.warmup + args.steps
+    rng = np.random.default_rng(args.graine + r)
+    xs = torch.from_numpy(rng.standard_normal((n_pas, c.dims.colonnes[0])).astype(np.float32)).to(torch.bfloat16)
+    xs_dev = xs.cuda()
+    x_hote = xs.pin_memory()
+    res0 = torch.from_numpy(rng.standard_normal((n_pas, c.dims.lignes[2])).astype(np.float32))
+    res_hote = res0.pin_memory()
+    res_sortie = torch.empty_like(res_hote).pin_memory()
+    residu = torch.empty(c.dims.lignes[2], dtype=torch.float32, device="cuda")
+    x_dev = torch.empty(c.dims.colonnes[0], dtype=torch.bfloat16, device="cuda")
+    vidange = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2 (126 MB)
+    flux = torch.cuda.current_stream()
+    idx_journal = torch.zeros(n_pas, args.k, dtype=torch.int32, device="cuda")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    for e in ev:
+        e.record()
+    torch.cuda.synchronize()
+    phases = [e.cuda_event for e in ev[1:7]]
+
+    def pas_carte(s):
+        vidange.zero_()
+        residu.copy_(res0[s].cuda(non_blocking=False))
+        ev[0].record()
+        cc.couche(xs_dev[s], residu, evenements=phases)
+        ev[7].record()
+        idx_journal[s].copy_(cc.idx)
+
+    # ---- device-timed region
+    torch.cuda.synchronize()
+    for s in range(args.warmup):
+        pas_carte(s)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t_pas, t_phase = [], [[] for _ in range(5)]
+    uuid = str(getattr(torch.cuda.get_device_properties(lr), "uuid", lr))
+    with Horloges(uuid if uuid.startswith("GPU-") else (f"GPU-{uuid}" if len(uuid) > 8 else lr)) as horl:
+        t0 = time.time()
+        for s in range(args.warmup, n_pas):
+            pas_carte(s)
+            torch.cuda.synchronize()
+            t_pas.append(ev[0].elapsed_time(ev[7]))
+            for i in range(5):
+                t_phase[i].append(ev[1 + i].elapsed_time(ev[2 + i]))
+        mur = time.time() - t0
+    assert (cc.controle.cpu().numpy() == 0).all(), "integrity counters set during the bench"
+    idx = idx_journal.cpu().numpy()
+    octets = sum(octets_pas(c, idx[s], args.k) for s in range(args.warmup, n_pas))
+    octets_dom = sum(octets_codes_porte_haut(c, idx[s], args.k) for s in range(args.warmup, n_pas))
+    t_total_ms = sum(t_pas)
+
+    # ---- end to end through the C-ABI with host buffers
+    torch.cuda.synchronize()
+    e2e = []
+    for s in range(n_pas):
+        vidange.zero_()
+        ev[0].record()
+        x_dev.copy_(x_hote[s], non_blocking=True)
+        residu.copy_(res_hote[s], non_blocking=True)
+        cc.couche(x_dev, residu)
+        res_sortie[s].copy_(residu, non_blocking=True)
+        ev[7].record()
+        torch.cuda.synchronize()
+        if s >= args.warmup:
+            e2e.append(ev[0].elapsed_time(ev[7]))
+    t_e2e_ms = sum(e2e)
+
+    if dist:
+        tt = torch.tensor([t_total_ms, t_e2e_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_total_ms, t_e2e_ms = float(tt[0]), float(tt[1])
+    pic, sorte_pic = pics()
+    dom_ms = sum(t_phase[1]) / len(t_phase[1])
+    atteint = (octets_dom / args.steps) / (dom_ms * 1e-3) / 1e9
+    ligne = {
+        "metric": METRIQUE,
+        "value": round(w * octets / (t_total_ms * 1e-3) / 1e9, 2),
+        "unit": UNITE,
+        "n_gpus": w,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
+        "config": {
+            "workload": "config 1: one gpt-oss-120b MoE layer, batch 1, 128 experts, top-4, x bf16[2880], "
+                        "router f32 128x2880, SwiGLU alpha 1.702 limit 7, weights resident as .trc v1.2 parts",
+            "experts": args.experts, "k": args.k, "n_delta": args.n_delta, "n_codes": args.n_codes,
+            "l2": "flushed between steps (256 MB written)", "bytes_per_step": round(octets / args.steps),
+            "parallelism": f"replicas x{w}",
+        },
+        "e2e": {"value": round(w * octets / (t_e2e_ms * 1e-3) / 1e9, 2), "unit": UNITE,
+                "h2d_bytes_per_step": 2 * c.dims.colonnes[0] + 4 * c.dims.lignes[2],
+                "d2h_bytes_per_step": 4 * c.dims.lignes[2]},
+        "gpu_launches": args.steps * 7,
+        "roofline": {"bound": "hbm", "kernel": "k_moe_codes (gate/up: CODES_CTX decode fused into the GEMV)",
+                     "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
+                     "peak_source": sorte_pic, "traffic": None,
+                     "algorithmic_bytes_per_launch": round(octets_dom / args.steps)},
+        "phases_ms": {n: round(sum(v) / len(v), 4) for n, v in
+                      zip(["delta", "gate_up", "swiglu", "down", "combine"], t_phase)},
+        "clocks": horl.resume(),
+        "wall_s_timed_region": round(mur, 3),
+        "generation_s": round(t_gen, 1),
+    }
+    if r == 0 and w == 1 and not args.no_cpu_baseline:
+        ligne["cpu_baseline"] = base_cpu(c, args, bornes_s=12.0)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if r == 0:
+        print(json.dumps(ligne), flush=True)
+
+
+def base_cpu(c, args, bornes_s: float, pas_min: int = 3):
+    """The reference's path on host cores (oracle/couche_cpu.c), all cores, a bounded sample."""
+    import numpy as np
+
+    import oracle as O
+
+    rng = np.random.default_rng(args.graine)
+    n_fils = os.cpu_count() or 1
+    octets, t, n = 0, 0.0, 0
+    while n < pas_min or t < bornes_s:
+        x = rng.standard_normal(c.dims.colonnes[0]).astype(np.float32)
+        r0 = rng.standard_normal(c.dims.lignes[2]).astype(np.float32)
+        t0 = time.perf_counter()
+        _, idx, _ = O.couche_moe_cpu(c.parties, c.luts, c.dims.lignes, c.dims.colonnes, c.wr, c.br, x, args.k, r0, n_fils)
+        t += time.perf_counter() - t0
+        octets += octets_pas(c, idx, args.k)
+        n += 1
+        if n >= 200:
+            break
+    cpu = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu = next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), "")
+    except Exception:
+        pass
+    return {"value": round(octets / t / 1e9, 3), "unit": UNITE, "cores": n_fils, "kind": "port",
+            "sample": f"{n} layer steps (router, decode of the 4 routed experts, GEMVs, SwiGLU, combine), "
+                      f"{round(t, 1)} s; CPU: {cpu}"}
+
+
+def bras_reference(args):
+    r, w, _ = rang()
+    if r != 0:
+        return
+    c, t_gen = construire_couche(args)
+    import numpy as np
+
+    import oracle as O
+
+    rng = np.random.default_rng(args.graine)
+    n_fils = os.cpu_count() or 1
+    mesures = []
+    for s in range(args.warmup + args.steps):
+        x = rng.standard_normal(c.dims.colonnes[0]).astype(np.float32)
+        r0 = rng.standard_normal(c.dims.lignes[2]).astype(np.float32)
+        t0 = time.perf_counter()
+        _, idx, _ = O.couche_moe_cpu(c.parties, c.luts, c.dims.lignes, c.dims.colonnes, c.wr, c.br, x, args.k, r0, n_fils)
+        dt = time.perf_counter() - t0
+        if s >= args.warmup:
+            mesures.append((dt, octets_pas(c, idx, args.k)))
+    t = sum(m[0] for m in mesures)
+    v = round(sum(m[1] for m in mesures) / t / 1e9, 3)
+    ligne = {
+        "impl": "reference", "metric": METRIQUE, "value": v, "unit": UNITE, "n_gpus": w, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
+        "config": {"workload": "config 1 (one MoE layer, batch 1, 128 experts, top-4) on host cores",
+                   "experts": args.experts, "k": args.k},
+        "cpu_baseline": {"value": v, "unit": UNITE, "cores": n_fils, "kind": "port",
+                         "sample": f"{args.steps} layer steps after {args.warmup} warm-up, {round(t, 2)} s"},
+        "e2e": {"value": v, "unit": UNITE, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "generation_s": round(t_gen, 1),
+    }
+    print(json.dumps(ligne), flush=True)
+
+
+def main():
+    args = arguments()
+    if args.impl == "reference":
+        bras_reference(args)
+    else:
+        notre_bras(args)
+
+
+if __name__ == "__main__":
+    main()

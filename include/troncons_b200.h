@@ -1,0 +1,227 @@
+/*
+ * troncons_b200 — the C-ABI of the B200 (sm_100a) kernels for troncons' hot path: on-GPU rANS
+ * decoding of `.trc` v1.x MXFP4 expert parts, fused into the MoE expert GEMV.
+ *
+ * This is the drop-in boundary for the reference's kernel contract (crate trc-noyaux, struct
+ * `Noyaux`, moteur/crates/trc-noyaux/src/lib.rs): the same structs, byte for byte, the same
+ * argument meaning and the same error behaviour. A Rust host binds it with `extern "C"`
+ * declarations. Every launch is asynchronous on the caller's stream
+ * (`flux`, a cudaStream_t; NULL is the legacy default stream). The caller owns every device
+ * buffer; the library allocates nothing on the device.
+ *
+ * Status codes: TRC_OK, TRC_ERR_USAGE (a size, alignment or shape the reference's host wrapper
+ * also refuses, noyaux/src/lib.rs:70-72 `Erreur::Usage`; nothing was launched), TRC_ERR_CUDA (a
+ * launch error). `trc_derniere_erreur()` gives the message of the calling thread's last error.
+ *
+ * Device-side integrity (commun.cuh:36-44 of the reference): kernels never trap. `controle` is a
+ * u32[4] the caller zeroes before a decode; after it, [0] counts rANS lanes whose final state is
+ * not L, [1] counts format errors (bad magic, missing stream, inconsistent sizes), [2] counts
+ * tiles that did not consume exactly their words. Any non-zero counter is a fatal, named error
+ * for the caller (trc-ordo/src/lib.rs:1292-1300). Words read past the end of a tile read as 0,
+ * as in the normative CPU decoder (trc-codec/src/rans.rs:427-436).
+ */
+#ifndef TRONCONS_B200_H
+#define TRONCONS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TRC_OK 0
+#define TRC_ERR_USAGE 1
+#define TRC_ERR_CUDA 2
+
+/* Rows/columns of an expert's three matrices (gate j=0, up j=1, down j=2): 24 bytes, align 4.
+ * Same layout as `abi::DimsExpert` (trc-noyaux/src/abi.rs:8-13; noyaux/commun.cuh:49-52). */
+typedef struct trc_dims_expert {
+    uint32_t lignes[3];
+    uint32_t colonnes[3];
+} trc_dims_expert;
+
+/* One product of a GEMV batch: 32 bytes. Same layout as `abi::DescGemv` (abi.rs:16-27). */
+typedef struct trc_desc_gemv {
+    uint64_t matrice; /* device address of the matrix in a slot (its codes; multiple of 256) */
+    uint64_t x;       /* device address of x, f32[colonnes] (multiple of 16) */
+    uint64_t y;       /* device address of y, f32[lignes] */
+    uint32_t lignes;
+    uint32_t colonnes;
+} trc_desc_gemv;
+
+/* One expert of a decode batch: 32 bytes. Same layout as `abi::DescDecodage` (abi.rs:32-53). */
+typedef struct trc_desc_decodage {
+    uint64_t partie;      /* level-0 part as read from the file (16-byte aligned) */
+    uint64_t emplacement; /* SoA slot (multiple of 256) */
+    uint64_t luts;        /* the layer's LUTs, u32[3][4][4096] */
+    uint64_t controle;    /* u32[4], zeroed by the caller */
+} trc_desc_decodage;
+
+/* Message of the calling thread's last error ("" when none). */
+const char* trc_derniere_erreur(void);
+
+/* Bytes of an expert slot: the SoA layout of abi.rs:69-122 (codes, scales at al256, biases at
+ * al256, matrix stride al256), summed over the three matrices. 13,254,144 for gpt-oss. */
+uint64_t trc_taille_emplacement(const trc_dims_expert* dims);
+
+/* ---------------------------------------------------------------- the reference's contract */
+
+/* Decodes a level-0 v1.0/v1.2 part (MEDIANES, BIAIS, DELTA, CODES_CTX of the three matrices)
+ * into an SoA slot. Replaces `Noyaux::decoder_expert` / `decoder_expert_grilles`
+ * (trc-noyaux/src/lib.rs:118-181). `luts`: the layer's u32[3][4][4096] (>= 196,608 bytes; see
+ * trc_luts_couche). Slot 256-aligned and >= trc_taille_emplacement; part 16-aligned, >= 64 B;
+ * controle >= 16 B. Any tile size N is accepted. */
+int trc_decoder_expert(const void* partie, size_t partie_octets, void* emplacement, size_t emplacement_octets,
+                       const uint32_t* luts, size_t luts_octets, const trc_dims_expert* dims, uint32_t* controle,
+                       size_t controle_octets, void* flux);
+
+/* n experts of the same dimensions in one launch; `descs`: device trc_desc_decodage[n].
+ * Expert by expert, the same bytes and counters as trc_decoder_expert. Replaces
+ * `Noyaux::decoder_lot` (lib.rs:190-206). */
+int trc_decoder_lot(const trc_desc_decodage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
+                    void* flux);
+
+/* Raw part (file flag bit 2: ECHELLES_BRUTES, CODES_BRUTS, BIAIS) into the same slot layout.
+ * Replaces `Noyaux::copier_brut` (lib.rs:210-235). controle[1] counts format errors. */
+int trc_copier_brut(const void* partie, size_t partie_octets, void* emplacement, size_t emplacement_octets,
+                    const trc_dims_expert* dims, uint32_t* controle, size_t controle_octets, void* flux);
+
+/* y = W x + b for one matrix of a slot (`matrice` = its codes). x f32[colonnes], 16-aligned;
+ * y f32[lignes]. Replaces `Noyaux::gemv` (lib.rs:239-262). The reduction order is fixed by the
+ * shape only: the same bits as the fused path on the same weights. */
+int trc_gemv(const void* matrice, size_t matrice_octets, const float* x, size_t x_octets, float* y, size_t y_octets,
+             uint32_t lignes, uint32_t colonnes, void* flux);
+
+/* n independent products (`descs`: device trc_desc_gemv[n]); lignes_max bounds their rows.
+ * Product by product, the same bits as trc_gemv. Replaces `Noyaux::gemv_lot` (lib.rs:274-283). */
+int trc_gemv_lot(const trc_desc_gemv* descs, size_t descs_octets, uint32_t n, uint32_t lignes_max, void* flux);
+
+/* y = W x (+ b), W f32 row-major [lignes][colonnes] (16-aligned, colonnes % 4 == 0): the router
+ * logits. `biais` may be NULL. Replaces `Noyaux::gemv_f32` (lib.rs:307-319). */
+int trc_gemv_f32(const float* w, size_t w_octets, const float* x, size_t x_octets, const float* biais,
+                 size_t biais_octets, float* y, size_t y_octets, uint32_t lignes, uint32_t colonnes, void* flux);
+
+/* Top-k of `experts` logits (value decreasing, then index increasing; NaN never chosen),
+ * weights = softmax of the k chosen, in f64, rounded to f32. experts <= 256, k <= 8. If `boite`
+ * (a device address of host-mapped memory) is not 0, words 1..k receive the indices, words
+ * k+1..2k the weights' bits, then word 0 `sequence`, written last after a system fence.
+ * Replaces `Noyaux::routeur_topk` (lib.rs:418-430; passe.cuh:455-514). */
+int trc_routeur_topk(const float* logits, size_t logits_octets, uint32_t experts, uint32_t k, uint32_t* indices,
+                     size_t indices_octets, float* poids, size_t poids_octets, uint64_t boite, uint32_t sequence,
+                     void* flux);
+
+/* Clamped SwiGLU of gpt-oss on n pairs, in f64 rounded once to f32:
+ * g <- min(g, 7); u <- clamp(u, -7, 7); y = g * sigma(1.702 g) * (u + 1).
+ * Replaces `Noyaux::swiglu_oai` (lib.rs:451-458; passe.cuh:598-605). */
+int trc_swiglu_oai(const float* g, size_t g_octets, const float* u, size_t u_octets, float* y, size_t y_octets,
+                   uint32_t n, void* flux);
+
+/* residu[i] += ((w0 s0[i] + w1 s1[i]) + w2 s2[i]) + ..., j = 0..n-1 in order, products and sums
+ * rounded separately (no FMA); s_j = sorties + j*pas floats; `poids` NULL means weights 1.
+ * Replaces `Noyaux::combiner` (lib.rs:463-475; passe.cuh:611-622). */
+int trc_combiner(float* residu, size_t residu_octets, const float* sorties, size_t sorties_octets, uint32_t pas,
+                 const float* poids, size_t poids_octets, uint32_t n, uint32_t d, void* flux);
+
+/* ---------------------------------------------------------------- host helpers (no device) */
+
+/* Normalises counts to 12-bit frequencies summing to 4096 (trc-codec/src/rans.rs:83-127);
+ * geometrie 1: 256 symbols, 2: 16 symbols. */
+int trc_table_depuis_comptes(const uint64_t* comptes, uint32_t geometrie, uint16_t* freq);
+
+/* Geometry-1 LUT of 256 frequencies summing to 4096: lut[i] = s | (f-1) << 8 | (i - c) << 20.
+ * Replaces `abi::lut_geometrie1` (abi.rs:187-205). */
+int trc_lut_geometrie1(const uint16_t* freq, uint32_t* lut);
+
+/* The layer's LUTs in the kernels' layout (abi.rs:207-221): for matrix j, [j][0] DELTA,
+ * [j][1+k] CODES_CTX of scale class k. freqs: u16[3][4][256]; presentes[3][4]: 0 for a table
+ * the file lacks (an all-zero LUT, never read by a correct stream). luts: u32[3][4][4096]. */
+int trc_luts_couche(const uint16_t* freqs, const uint8_t* presentes, uint32_t* luts);
+
+/* ---------------------------------------------------------------- the encoder (trc-codeur) */
+
+/* Adds one matrix's symbols to a layer's counts u64[4][256] ([0] DELTA, [1+k] CODES_CTX class
+ * k; padding counted): preparer_matrice_avec + ComptesMatrice::ajouter
+ * (trc-codec/src/lib.rs:348-401). blocs: R*B 17-byte MXFP4 blocks [e, qs x 16] in beta order. */
+int trc_comptes_matrice(const uint8_t* blocs, uint32_t lignes, uint32_t blocs_par_ligne, int canonique,
+                        uint64_t* comptes);
+
+/* Encodes one expert into a level-0 part (12 streams: MEDIANES, BIAIS, DELTA, CODES_CTX per
+ * matrix), the part trc-codeur writes (bins/trc-codeur/src/coder.rs:243-313 with
+ * trc-codec/src/lib.rs:417-428 and trc-format/src/lib.rs:882-908). blocs[j]: the matrix's R*B
+ * 17-byte blocks; biais[j]: f32[R] bytes; freqs: u16[3][4][256] (the layer's tables);
+ * canonique: v1.2 (nibble 8 folded to 0). n_delta / n_codes: macro-steps per tile (256 is
+ * what trc-codeur writes). Returns the part length (a multiple of 4096) and writes it into
+ * `sortie` when `capacite` suffices; returns -1 on bad input. *utiles receives the useful bytes. */
+int64_t trc_coder_partie(const uint8_t* const* blocs, const uint8_t* const* biais, const trc_dims_expert* dims,
+                         const uint16_t* freqs, int canonique, uint16_t couche, uint16_t expert, uint32_t n_delta,
+                         uint32_t n_codes, uint8_t* sortie, size_t capacite, uint32_t* utiles);
+
+/* The raw part of the same expert (file flag bit 2: 9 streams ECHELLES_BRUTES, CODES_BRUTS,
+ * BIAIS per matrix; trc-codec/src/lib.rs:432-445). Origin bytes, not canonicalised. */
+int64_t trc_coder_partie_brute(const uint8_t* const* blocs, const uint8_t* const* biais,
+                               const trc_dims_expert* dims, uint16_t couche, uint16_t expert, uint8_t* sortie,
+                               size_t capacite, uint32_t* utiles);
+
+/* Seeded synthetic MXFP4 matrices: per row sigma = 0.02 * exp(0.3 N(0,1)), weights N(0, sigma),
+ * per 32-block E8M0 = floor(log2 max|w|) - 2 (+127), E2M1 round-to-nearest-even with the sign
+ * kept (so -0 codes exist, as in gpt-oss's GGUF), biases N(0, 0.01) rounded to bf16 and stored
+ * as f32. n matrices of R x C, stream `graine` + matrix index; blocs: n*R*(C/32)*17 bytes,
+ * biais: n*R floats. Runs on up to `fils` host threads (0: all). */
+int trc_synth_matrices(uint64_t graine, uint32_t lignes, uint32_t colonnes, uint32_t n, uint8_t* blocs, float* biais,
+                       int fils);
+
+/* ---------------------------------------------------------------- new: the fused MoE layer */
+
+/* One MoE layer of one token, fused: routed experts' DELTA -> scales, CODES_CTX decoded in
+ * registers and multiplied at once (gate, up), SwiGLU, then down, then the weighted combine
+ * into the residual. The decoded nibbles and scales never go to the slot layout in HBM. No
+ * reference counterpart (the reference decodes into slots, then runs gemv, swiglu_oai and
+ * combiner: trc-modele/src/lib.rs:533-553). Bit for bit the same result as trc_decoder_lot +
+ * trc_gemv + trc_swiglu_oai + trc_combiner on the same weights, and as the raw path (`brut`)
+ * on the raw parts of the same experts. */
+typedef struct trc_moe_couche {
+    const uint64_t* parties;        /* device u64[experts]: each expert's level-0 part (16-aligned) */
+    const uint64_t* parties_octets; /* device u64[experts]: their sizes */
+    uint32_t experts;               /* experts of the layer */
+    uint32_t k;                     /* active experts per token (<= 8) */
+    const uint32_t* luts;           /* device: the layer's u32[3][4][4096] (unused when brut) */
+    trc_dims_expert dims;           /* hidden d = colonnes[0] = colonnes[1] = lignes[2];
+                                       ffn width f = lignes[0] = lignes[1] = colonnes[2] */
+    const uint32_t* indices;        /* device u32[k]: the chosen experts (router output) */
+    const float* poids;             /* device f32[k]: their weights */
+    const void* x;                  /* device activation [d], bf16 (x_bf16 = 1) or f32 */
+    uint32_t x_bf16;
+    uint32_t brut;                  /* 1: raw parts (ECHELLES_BRUTES / CODES_BRUTS / BIAIS) */
+    float* residu;                  /* device f32[d]: updated in place */
+    uint32_t* controle;             /* device u32[4*k]: counters per active expert, zeroed by caller */
+    uint32_t n_delta, n_codes;      /* macro-steps per tile the parts were encoded with (0: 256, what
+                                       trc-codeur writes); they only size the grids */
+} trc_moe_couche;
+
+/* Workspace bytes the fused layer needs for these dimensions and k (device memory the caller
+ * allocates once and reuses; contents need no initialisation). */
+uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k);
+
+/* Runs the fused layer. `espace` (256-aligned) >= trc_moe_espace_octets. Compressed parts need
+ * CODES_CTX tiles whose N is a multiple of 32 (trc-codeur writes 256); other N are counted as
+ * format errors (decode them with trc_decoder_expert instead). */
+int trc_moe_couche_fusionnee(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);
+
+/* trc_moe_couche_fusionnee, recording evenements[0..5] (cudaEvent_t, each may be NULL) on the
+ * stream: before the DELTA phase, after it, after gate/up, after SwiGLU, after down, after the
+ * combine (raw parts: no DELTA phase, [1] is recorded with [0]). For timing each phase with CUDA
+ * events on the launching stream; the launches are those of trc_moe_couche_fusionnee. */
+int trc_moe_couche_chrono(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux,
+                          void* const* evenements);
+
+/* Router of the layer: logits = Wr x + br (f32 weights [experts][colonnes]; x bf16 or f32),
+ * then top-k and f64 softmax as trc_routeur_topk. `logits` f32[experts] is written too. */
+int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts,
+                uint32_t colonnes, uint32_t k, float* logits, uint32_t* indices, float* poids, void* flux);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRONCONS_B200_H */

@@ -1,0 +1,310 @@
+"""TEST INFRASTRUCTURE — ctypes access to the CPU oracle (oracle/_build/liboracle.so).
+
+The oracle restates, in plain C, the reference's CPU codec and format (rANS tables, LUT,
+coder, normative decoder, part layout, v1.2 expert reconstruction, empreinte64) and the
+single-vector numerics of the MoE layer. Only tests/, ``__graft_entry__.smoke()`` and
+bench.py's CPU-baseline leg may use it, as the checker or as the timed CPU baseline; the
+product never does.
+
+``ref`` gives the reference's own CUDA kernels (oracle/_ref/libtrc_ref.so, compiled from the
+reference checkout by ``make ref``) when that library is present.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+ICI = os.path.dirname(os.path.abspath(__file__))
+_LIB = os.path.join(ICI, "_build", "liboracle.so")
+_REF = os.path.join(ICI, "_ref", "libtrc_ref.so")
+
+P8 = C.POINTER(C.c_uint8)
+P16 = C.POINTER(C.c_uint16)
+P32 = C.POINTER(C.c_uint32)
+P64 = C.POINTER(C.c_uint64)
+PF = C.POINTER(C.c_float)
+PD = C.POINTER(C.c_double)
+
+
+class Bilan(C.Structure):
+    """Integrity record of a decode (rans.rs:357-382)."""
+
+    _fields_ = [("voies_hors_l", C.c_uint64), ("tuiles_mots_faux", C.c_uint64), ("premiere_tuile", C.c_int64)]
+
+    def intact(self) -> bool:
+        return self.voies_hors_l == 0 and self.tuiles_mots_faux == 0
+
+
+def construire() -> None:
+    """Builds liboracle.so (gcc) when it is missing or older than its sources."""
+    sources = [os.path.join(ICI, f) for f in ("trc_oracle.c", "ordre_b200.c", "couche_cpu.c")]
+    if os.path.exists(_LIB) and all(os.path.getmtime(_LIB) >= os.path.getmtime(s) for s in sources):
+        return
+    subprocess.run(["make", "-C", ICI, "all"], check=True, capture_output=True)
+
+
+def _charger() -> C.CDLL:
+    construire()
+    lib = C.CDLL(_LIB)
+    sig = {
+        "orc_sha256_octets": (None, [P8, C.c_size_t, P8]),
+        "orc_empreinte64": (C.c_uint64, [P8, C.c_size_t]),
+        "orc_table_depuis_comptes": (None, [P64, C.c_int, P16]),
+        "orc_lut": (C.c_int, [P16, C.c_int, P32]),
+        "orc_coder_g1": (C.c_size_t, [P8, C.c_uint32, C.c_uint32, P8, C.c_size_t, P16, C.c_uint32, P8, C.c_size_t]),
+        "orc_flux_valide": (C.c_int, [P8, C.c_size_t]),
+        "orc_decoder": (C.c_int, [P8, C.c_size_t, P8, C.c_size_t, P32, C.c_uint32, P8, C.POINTER(Bilan)]),
+        "orc_trouver_flux": (C.c_int, [P8, C.c_size_t, C.c_uint8, C.c_uint8, P32, P32, P32]),
+        "orc_assembler_partie": (C.c_size_t, [C.c_uint16, C.c_uint16, C.c_uint8, C.c_uint8, C.c_uint32, P8, P32, P32, P8, P8, P32]),
+        "orc_preparer_matrice": (None, [P8, C.c_uint32, C.c_uint32, C.c_int, P8, P8, P8]),
+        "orc_ajouter_comptes": (None, [P8, C.c_size_t, P8, C.c_size_t, P64]),
+        "orc_decoder_matrice_v10": (C.c_int, [P8, C.c_size_t, C.c_uint8, C.c_uint32, C.c_uint32, P32, P8, P8, PF, C.POINTER(Bilan), C.POINTER(Bilan)]),
+        "orc_decoder_expert": (C.c_int, [P8, C.c_size_t, P32, P32, P32, P8, P32]),
+        "orc_gemv_f64": (None, [P8, P8, PF, PD, C.c_uint32, C.c_uint32, PD]),
+        "orc_routeur_topk": (None, [PF, C.c_uint32, C.c_uint32, P32, PF]),
+        "orc_swiglu": (None, [PF, PF, PF, C.c_uint32]),
+        "orc_combiner": (None, [PF, PF, C.c_uint32, PF, C.c_uint32, C.c_uint32]),
+        "ord_gemv": (None, [P8, P8, PF, PF, C.c_uint32, C.c_uint32, PF]),
+        "ord_gemv_f32": (None, [PF, PF, PF, C.c_uint32, C.c_uint32, PF]),
+        "orc_couche_moe_cpu": (C.c_int, [C.POINTER(P8), C.POINTER(C.c_size_t), C.c_uint32, P32, P32, P32,
+                                         PF, PF, PF, C.c_uint32, PF, P32, PF, C.c_int]),
+    }
+    for nom, (res, args) in sig.items():
+        f = getattr(lib, nom)
+        f.restype = res
+        f.argtypes = args
+    return lib
+
+
+lib = _charger()
+
+
+def p(a: np.ndarray, t):
+    """Pointer of a C-contiguous numpy array."""
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(t)
+
+
+def empreinte64(b: bytes) -> int:
+    a = np.frombuffer(b, dtype=np.uint8) if len(b) else np.zeros(1, np.uint8)
+    return int(lib.orc_empreinte64(p(a, P8), len(b)))
+
+
+def sha256(b: bytes) -> bytes:
+    a = np.frombuffer(b, dtype=np.uint8) if len(b) else np.zeros(1, np.uint8)
+    out = np.zeros(32, np.uint8)
+    lib.orc_sha256_octets(p(a, P8), len(b), p(out, P8))
+    return out.tobytes()
+
+
+def table_depuis_comptes(comptes, geometrie: int = 1) -> np.ndarray:
+    n = 256 if geometrie == 1 else 16
+    c = np.ascontiguousarray(comptes, dtype=np.uint64)
+    assert c.size == n
+    f = np.zeros(n, np.uint16)
+    lib.orc_table_depuis_comptes(p(c, P64), geometrie, p(f, P16))
+    return f
+
+
+def lut(freq, geometrie: int = 1) -> np.ndarray:
+    f = np.ascontiguousarray(freq, dtype=np.uint16)
+    out = np.zeros(4096, np.uint32)
+    if lib.orc_lut(p(f, P16), geometrie, p(out, P32)) != 0:
+        raise ValueError("frequencies do not sum to 4096")
+    return out
+
+
+def coder_g1(src, freqs, kappa=None, N: int = 256) -> bytes:
+    """Geometry-1 stream of `src` (padded by the caller to a multiple of 128)."""
+    s = np.ascontiguousarray(src, dtype=np.uint8)
+    f = np.ascontiguousarray(freqs, dtype=np.uint16).reshape(-1)
+    cap = 16 + 132 * (s.size // 128 // max(N, 1) + 2) + 2 * s.size + 4096
+    out = np.zeros(cap, np.uint8)
+    k = None if kappa is None else np.ascontiguousarray(kappa, dtype=np.uint8)
+    n = lib.orc_coder_g1(p(s, P8), s.size, N, p(k, P8) if k is not None else None, 0 if k is None else k.size,
+                         p(f, P16), f.size // 256, p(out, P8), cap)
+    if n == 0 or n == (1 << 64) - 1:
+        raise ValueError("coding failed (symbol absent from its table, or bad size)")
+    return out[:n].tobytes()
+
+
+def decoder(flux: bytes, luts, kappa=None):
+    """(decoded P bytes, Bilan) of a geometry-1 stream (decoder_avec, rans.rs:388-451)."""
+    b = np.frombuffer(flux, np.uint8)
+    P = int.from_bytes(flux[0:4], "little")
+    out = np.zeros(max(P, 1), np.uint8)
+    l = np.ascontiguousarray(luts, dtype=np.uint32).reshape(-1)
+    k = None if kappa is None else np.ascontiguousarray(kappa, dtype=np.uint8)
+    bil = Bilan()
+    r = lib.orc_decoder(p(b, P8), b.size, p(k, P8) if k is not None else None, 0 if k is None else k.size,
+                        p(l, P32), l.size // 4096, p(out, P8), C.byref(bil))
+    if r != 0:
+        raise ValueError(f"malformed stream ({r})")
+    return out[:P], bil
+
+
+def flux_valide(flux: bytes) -> int:
+    b = np.frombuffer(flux, np.uint8)
+    return int(lib.orc_flux_valide(p(b, P8), b.size))
+
+
+def trouver_flux(partie: bytes, sorte: int, matrice: int):
+    b = np.frombuffer(partie, np.uint8)
+    d, lg, pr = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    r = lib.orc_trouver_flux(p(b, P8), b.size, sorte, matrice, C.byref(d), C.byref(lg), C.byref(pr))
+    return r, d.value, lg.value, pr.value
+
+
+def assembler_partie(couche: int, expert: int, niveau: int, n_matrices: int, flux):
+    """flux: list of (sorte, matrice, contexte, produits, bytes) -> (part bytes, useful bytes)."""
+    n = len(flux)
+    descs = np.array([[f[0], f[1], f[2]] for f in flux], np.uint8).reshape(-1)
+    lg = np.array([len(f[4]) for f in flux], np.uint32)
+    pr = np.array([f[3] for f in flux], np.uint32)
+    data = np.frombuffer(b"".join(f[4] for f in flux) or b"\0", np.uint8)
+    ut = C.c_uint32()
+    total = lib.orc_assembler_partie(couche, expert, niveau, n_matrices, n, p(descs, P8), p(lg, P32), p(pr, P32),
+                                     p(data, P8), None, C.byref(ut))
+    out = np.zeros(total, np.uint8)
+    lib.orc_assembler_partie(couche, expert, niveau, n_matrices, n, p(descs, P8), p(lg, P32), p(pr, P32),
+                             p(data, P8), p(out, P8), C.byref(ut))
+    return out.tobytes(), ut.value
+
+
+def preparer_matrice(blocs, R: int, B: int, canonique: bool):
+    """(medians, padded delta, padded qs) of R*B 17-byte MXFP4 blocks (lib.rs:348-373)."""
+    bl = np.ascontiguousarray(blocs, dtype=np.uint8).reshape(-1)
+    nb = R * B
+    med = np.zeros(R, np.uint8)
+    delta = np.zeros((nb + 127) // 128 * 128, np.uint8)
+    qs = np.zeros((16 * nb + 127) // 128 * 128, np.uint8)
+    lib.orc_preparer_matrice(p(bl, P8), R, B, int(canonique), p(med, P8), p(delta, P8), p(qs, P8))
+    return med, delta, qs
+
+
+def ajouter_comptes(delta, qs, comptes: np.ndarray) -> None:
+    lib.orc_ajouter_comptes(p(delta, P8), delta.size, p(qs, P8), qs.size, p(comptes, P64))
+
+
+def decoder_matrice_v10(partie: bytes, j: int, R: int, B: int, luts4):
+    b = np.frombuffer(partie, np.uint8)
+    l = np.ascontiguousarray(luts4, dtype=np.uint32).reshape(-1)
+    codes = np.zeros(16 * R * B, np.uint8)
+    ech = np.zeros(R * B, np.uint8)
+    bi = np.zeros(R, np.float32)
+    bd, bc = Bilan(), Bilan()
+    r = lib.orc_decoder_matrice_v10(p(b, P8), b.size, j, R, B, p(l, P32), p(codes, P8), p(ech, P8), p(bi, PF),
+                                    C.byref(bd), C.byref(bc))
+    if r != 0:
+        raise ValueError(f"format error ({r})")
+    return codes, ech, bi, bd, bc
+
+
+def decoder_expert(partie: bytes, luts, lignes, colonnes, taille_emplacement: int):
+    """(slot bytes, controle[4]) of a whole level-0 part, decoded by the CPU codec."""
+    b = np.frombuffer(partie, np.uint8)
+    l = np.ascontiguousarray(luts, dtype=np.uint32).reshape(-1)
+    R = np.array(lignes, np.uint32)
+    Cc = np.array(colonnes, np.uint32)
+    e = np.zeros(taille_emplacement, np.uint8)
+    ctl = np.zeros(4, np.uint32)
+    lib.orc_decoder_expert(p(b, P8), b.size, p(l, P32), p(R, P32), p(Cc, P32), p(e, P8), p(ctl, P32))
+    return e, ctl
+
+
+def gemv_f64(codes, ech, biais, x, R: int, C_: int) -> np.ndarray:
+    xd = np.ascontiguousarray(x, dtype=np.float64)
+    y = np.zeros(R, np.float64)
+    bi = None if biais is None else np.ascontiguousarray(biais, dtype=np.float32)
+    lib.orc_gemv_f64(p(codes, P8), p(ech, P8), p(bi, PF) if bi is not None else None, p(xd, PD), R, C_, p(y, PD))
+    return y
+
+
+def ordre_gemv(codes, ech, biais, x, R: int, C_: int) -> np.ndarray:
+    """troncons_b200's GEMV reduction order, bit for bit (oracle/ordre_b200.c)."""
+    xf = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(R, np.float32)
+    bi = None if biais is None else np.ascontiguousarray(biais, dtype=np.float32)
+    lib.ord_gemv(p(np.ascontiguousarray(codes), P8), p(np.ascontiguousarray(ech), P8),
+                 p(bi, PF) if bi is not None else None, p(xf, PF), R, C_, p(y, PF))
+    return y
+
+
+def ordre_gemv_f32(W, x, biais, R: int, C_: int) -> np.ndarray:
+    Wf = np.ascontiguousarray(W, dtype=np.float32)
+    xf = np.ascontiguousarray(x, dtype=np.float32)
+    bi = None if biais is None else np.ascontiguousarray(biais, dtype=np.float32)
+    y = np.zeros(R, np.float32)
+    lib.ord_gemv_f32(p(Wf, PF), p(xf, PF), p(bi, PF) if bi is not None else None, R, C_, p(y, PF))
+    return y
+
+
+def routeur_topk(logits, k: int):
+    l = np.ascontiguousarray(logits, dtype=np.float32)
+    idx = np.zeros(k, np.uint32)
+    w = np.zeros(k, np.float32)
+    lib.orc_routeur_topk(p(l, PF), l.size, k, p(idx, P32), p(w, PF))
+    return idx, w
+
+
+def swiglu(g, u) -> np.ndarray:
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    y = np.zeros_like(g)
+    lib.orc_swiglu(p(g, PF), p(u, PF), p(y, PF), g.size)
+    return y
+
+
+def combiner(residu, sorties, pas: int, poids, n: int, d: int) -> np.ndarray:
+    r = np.array(residu, dtype=np.float32, copy=True)
+    s = np.ascontiguousarray(sorties, dtype=np.float32)
+    w = None if poids is None else np.ascontiguousarray(poids, dtype=np.float32)
+    lib.orc_combiner(p(r, PF), p(s, PF), pas, p(w, PF) if w is not None else None, n, d)
+    return r
+
+
+def couche_moe_cpu(parties, luts, lignes, colonnes, Wr, br, x, k: int, residu, n_fils: int = 0):
+    """One MoE layer on host cores (lignes/colonnes: the three matrices' shapes): returns
+    (residual out, indices, weights)."""
+    E = len(parties)
+    bufs = [np.frombuffer(q, np.uint8) for q in parties]
+    ptrs = (P8 * E)(*[p(b, P8) for b in bufs])
+    tailles = (C.c_size_t * E)(*[b.size for b in bufs])
+    l = np.ascontiguousarray(luts, dtype=np.uint32).reshape(-1)
+    res = np.array(residu, dtype=np.float32, copy=True)
+    idx = np.zeros(k, np.uint32)
+    w = np.zeros(k, np.float32)
+    lg = np.array(list(lignes), np.uint32)
+    cl = np.array(list(colonnes), np.uint32)
+    r = lib.orc_couche_moe_cpu(ptrs, tailles, E, p(l, P32), p(lg, P32), p(cl, P32), p(np.ascontiguousarray(Wr, np.float32), PF),
+                               p(np.ascontiguousarray(br, np.float32), PF), p(np.ascontiguousarray(x, np.float32), PF),
+                               k, p(res, PF), p(idx, P32), p(w, PF), n_fils)
+    if r != 0:
+        raise ValueError(f"CPU layer failed ({r})")
+    return res, idx, w
+
+
+def ref():
+    """The reference's own CUDA kernels (oracle/_ref/libtrc_ref.so), or None when absent."""
+    if not os.path.exists(_REF):
+        return None
+    r = C.CDLL(_REF)
+    vp = C.c_void_p
+    for nom, args in {
+        "ref_decoder_expert": [vp, vp, vp, P32, vp, vp],
+        "ref_copier_brut": [vp, vp, P32, vp, vp],
+        "ref_gemv": [vp, vp, vp, C.c_uint32, C.c_uint32, vp],
+        "ref_gemv_lot": [vp, C.c_uint32, C.c_uint32, vp],
+        "ref_decoder_lot": [vp, C.c_uint32, P32, vp],
+        "ref_gemv_f32": [vp, vp, vp, vp, C.c_uint32, C.c_uint32, vp],
+        "ref_routeur_topk": [vp, C.c_uint32, C.c_uint32, vp, vp, vp],
+        "ref_swiglu": [vp, vp, vp, C.c_uint32, vp],
+        "ref_combiner": [vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint32, vp],
+    }.items():
+        f = getattr(r, nom)
+        f.restype = C.c_int
+        f.argtypes = args
+    return r

@@ -1,0 +1,224 @@
+"""troncons_b200 — B200 (sm_100a) kernels for troncons' hot path, behind a C-ABI.
+
+The product is ``_lib/libtroncons_b200.so`` and its C interface ``include/troncons_b200.h``.
+This module binds that interface with ctypes and mirrors the reference's host wrapper
+(``trc_noyaux::Noyaux``, moteur/crates/trc-noyaux/src/lib.rs): the same method names, argument
+meaning (device views = address + bytes) and error behaviour (``ErreurUsage`` where the
+reference returns ``Erreur::Usage``). There is no fallback: importing fails loudly when the
+library is missing, and every call runs the CUDA kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+ICI = os.path.dirname(os.path.abspath(__file__))
+CHEMIN_LIB = os.path.join(ICI, "_lib", "libtroncons_b200.so")
+
+TRC_OK, TRC_ERR_USAGE, TRC_ERR_CUDA = 0, 1, 2
+
+
+class ErreurUsage(ValueError):
+    """A size, alignment or shape the kernels refuse before launching (Erreur::Usage)."""
+
+
+class ErreurCuda(RuntimeError):
+    """A CUDA launch error."""
+
+
+class DimsExpert(C.Structure):
+    """Rows and columns of an expert's three matrices (abi.rs:8-13): 24 bytes."""
+
+    _fields_ = [("lignes", C.c_uint32 * 3), ("colonnes", C.c_uint32 * 3)]
+
+    @classmethod
+    def de(cls, lignes, colonnes) -> "DimsExpert":
+        d = cls()
+        for j in range(3):
+            d.lignes[j] = lignes[j]
+            d.colonnes[j] = colonnes[j]
+        return d
+
+    @classmethod
+    def gpt_oss(cls) -> "DimsExpert":
+        return cls.de([2880] * 3, [2880] * 3)
+
+
+class DescGemv(C.Structure):
+    """One product of a GEMV batch (abi.rs:16-27): 32 bytes."""
+
+    _fields_ = [("matrice", C.c_uint64), ("x", C.c_uint64), ("y", C.c_uint64), ("lignes", C.c_uint32),
+                ("colonnes", C.c_uint32)]
+
+
+class DescDecodage(C.Structure):
+    """One expert of a decode batch (abi.rs:32-53): 32 bytes."""
+
+    _fields_ = [("partie", C.c_uint64), ("emplacement", C.c_uint64), ("luts", C.c_uint64), ("controle", C.c_uint64)]
+
+
+class MoeCouche(C.Structure):
+    """The fused MoE layer descriptor (trc_moe_couche)."""
+
+    _fields_ = [("parties", C.c_void_p), ("parties_octets", C.c_void_p), ("experts", C.c_uint32), ("k", C.c_uint32),
+                ("luts", C.c_void_p), ("dims", DimsExpert), ("indices", C.c_void_p), ("poids", C.c_void_p),
+                ("x", C.c_void_p), ("x_bf16", C.c_uint32), ("brut", C.c_uint32), ("residu", C.c_void_p),
+                ("controle", C.c_void_p), ("n_delta", C.c_uint32), ("n_codes", C.c_uint32)]
+
+
+def _charger() -> C.CDLL:
+    if not os.path.exists(CHEMIN_LIB):
+        raise ImportError(f"troncons_b200: {CHEMIN_LIB} is missing; build it with `python troncons_b200/construire.py` "
+                          "(there is no CPU fallback)")
+    lib = C.CDLL(CHEMIN_LIB)
+    vp, sz, u32, u64, i32, i64 = C.c_void_p, C.c_size_t, C.c_uint32, C.c_uint64, C.c_int, C.c_int64
+    pd = C.POINTER(DimsExpert)
+    sig = {
+        "trc_derniere_erreur": (C.c_char_p, []),
+        "trc_taille_emplacement": (u64, [pd]),
+        "trc_decoder_expert": (i32, [vp, sz, vp, sz, vp, sz, pd, vp, sz, vp]),
+        "trc_decoder_lot": (i32, [vp, sz, u32, pd, vp]),
+        "trc_copier_brut": (i32, [vp, sz, vp, sz, pd, vp, sz, vp]),
+        "trc_gemv": (i32, [vp, sz, vp, sz, vp, sz, u32, u32, vp]),
+        "trc_gemv_lot": (i32, [vp, sz, u32, u32, vp]),
+        "trc_gemv_f32": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
+        "trc_routeur_topk": (i32, [vp, sz, u32, u32, vp, sz, vp, sz, u64, u32, vp]),
+        "trc_swiglu_oai": (i32, [vp, sz, vp, sz, vp, sz, u32, vp]),
+        "trc_combiner": (i32, [vp, sz, vp, sz, u32, vp, sz, u32, u32, vp]),
+        "trc_table_depuis_comptes": (i32, [vp, u32, vp]),
+        "trc_lut_geometrie1": (i32, [vp, vp]),
+        "trc_luts_couche": (i32, [vp, vp, vp]),
+        "trc_comptes_matrice": (i32, [vp, u32, u32, i32, vp]),
+        "trc_coder_partie": (i64, [vp, vp, pd, vp, i32, C.c_uint16, C.c_uint16, u32, u32, vp, sz, C.POINTER(u32)]),
+        "trc_coder_partie_brute": (i64, [vp, vp, pd, C.c_uint16, C.c_uint16, vp, sz, C.POINTER(u32)]),
+        "trc_synth_matrices": (i32, [u64, u32, u32, u32, vp, vp, i32]),
+        "trc_moe_espace_octets": (u64, [pd, u32]),
+        "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
+        "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
+        "trc_routeur": (i32, [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, vp]),
+    }
+    for nom, (res, args) in sig.items():
+        f = getattr(lib, nom)
+        f.restype = res
+        f.argtypes = args
+    return lib
+
+
+lib = _charger()
+
+
+def verifier(statut: int) -> None:
+    """Raises the error a non-zero status stands for."""
+    if statut == TRC_OK:
+        return
+    msg = lib.trc_derniere_erreur().decode()
+    if statut == TRC_ERR_USAGE:
+        raise ErreurUsage(msg)
+    raise ErreurCuda(msg)
+
+
+@dataclass(frozen=True)
+class VueCarte:
+    """A non-owning view of device memory: address and bytes (ARCHITECTURE.md 5.6 `VueCarte`)."""
+
+    adresse: int
+    octets: int
+
+    @classmethod
+    def de(cls, t) -> "VueCarte":
+        """View of a CUDA torch tensor (contiguous)."""
+        return cls(int(t.data_ptr()), int(t.numel() * t.element_size()))
+
+    def vue(self, decalage: int, octets: int) -> "VueCarte":
+        assert decalage + octets <= self.octets
+        return VueCarte(self.adresse + decalage, octets)
+
+
+def _v(x) -> VueCarte:
+    if x is None:
+        return VueCarte(0, 0)
+    return x if isinstance(x, VueCarte) else VueCarte.de(x)
+
+
+def _flux(flux) -> int:
+    if flux is None:
+        import torch
+
+        return int(torch.cuda.current_stream().cuda_stream)
+    return int(flux.cuda_stream) if hasattr(flux, "cuda_stream") else int(flux)
+
+
+def taille_emplacement(dims: DimsExpert) -> int:
+    return int(lib.trc_taille_emplacement(C.byref(dims)))
+
+
+class Noyaux:
+    """The reference's kernel contract (trc_noyaux::Noyaux), over the C-ABI. Views are
+    ``VueCarte`` or CUDA tensors; ``flux`` is a torch stream, a raw handle, or None (torch's
+    current stream)."""
+
+    def decoder_expert(self, partie, emplacement, luts, dims: DimsExpert, controle, flux=None) -> None:
+        p, e, l, c = _v(partie), _v(emplacement), _v(luts), _v(controle)
+        verifier(lib.trc_decoder_expert(p.adresse, p.octets, e.adresse, e.octets, l.adresse, l.octets, C.byref(dims),
+                                        c.adresse, c.octets, _flux(flux)))
+
+    def decoder_lot(self, descs, n: int, dims: DimsExpert, flux=None) -> None:
+        d = _v(descs)
+        verifier(lib.trc_decoder_lot(d.adresse, d.octets, n, C.byref(dims), _flux(flux)))
+
+    def copier_brut(self, partie, emplacement, dims: DimsExpert, controle, flux=None) -> None:
+        p, e, c = _v(partie), _v(emplacement), _v(controle)
+        verifier(lib.trc_copier_brut(p.adresse, p.octets, e.adresse, e.octets, C.byref(dims), c.adresse, c.octets,
+                                     _flux(flux)))
+
+    def gemv(self, matrice, x, y, lignes: int, colonnes: int, flux=None) -> None:
+        m, xv, yv = _v(matrice), _v(x), _v(y)
+        verifier(lib.trc_gemv(m.adresse, m.octets, xv.adresse, xv.octets, yv.adresse, yv.octets, lignes, colonnes,
+                              _flux(flux)))
+
+    def gemv_lot(self, descs, n: int, lignes_max: int, flux=None) -> None:
+        d = _v(descs)
+        verifier(lib.trc_gemv_lot(d.adresse, d.octets, n, lignes_max, _flux(flux)))
+
+    def gemv_f32(self, w, x, biais, y, lignes: int, colonnes: int, flux=None) -> None:
+        wv, xv, bv, yv = _v(w), _v(x), _v(biais), _v(y)
+        verifier(lib.trc_gemv_f32(wv.adresse, wv.octets, xv.adresse, xv.octets, bv.adresse or None, bv.octets,
+                                  yv.adresse, yv.octets, lignes, colonnes, _flux(flux)))
+
+    def routeur_topk(self, logits, experts: int, k: int, indices, poids, boite: int = 0, sequence: int = 0,
+                     flux=None) -> None:
+        lv, iv, pv = _v(logits), _v(indices), _v(poids)
+        verifier(lib.trc_routeur_topk(lv.adresse, lv.octets, experts, k, iv.adresse, iv.octets, pv.adresse, pv.octets,
+                                      boite, sequence, _flux(flux)))
+
+    def swiglu_oai(self, g, u, y, n: int, flux=None) -> None:
+        gv, uv, yv = _v(g), _v(u), _v(y)
+        verifier(lib.trc_swiglu_oai(gv.adresse, gv.octets, uv.adresse, uv.octets, yv.adresse, yv.octets, n,
+                                    _flux(flux)))
+
+    def combiner(self, residu, sorties, pas: int, poids, n: int, d: int, flux=None) -> None:
+        rv, sv, pv = _v(residu), _v(sorties), _v(poids)
+        verifier(lib.trc_combiner(rv.adresse, rv.octets, sv.adresse, sv.octets, pas, pv.adresse or None, pv.octets, n,
+                                  d, _flux(flux)))
+
+    # ---------------------------------------------------------------- new entry points
+
+    def routeur(self, wr, br, x, x_bf16: bool, experts: int, colonnes: int, k: int, logits, indices, poids,
+                flux=None) -> None:
+        verifier(lib.trc_routeur(_v(wr).adresse, _v(br).adresse or None, _v(x).adresse, int(x_bf16), experts, colonnes,
+                                 k, _v(logits).adresse, _v(indices).adresse, _v(poids).adresse, _flux(flux)))
+
+    def moe_couche(self, desc: MoeCouche, espace, flux=None, evenements=None) -> None:
+        """The fused layer; `evenements`: 6 raw cudaEvent_t handles (ints) recorded between its
+        phases (trc_moe_couche_chrono), or None."""
+        e = _v(espace)
+        if evenements is None:
+            verifier(lib.trc_moe_couche_fusionnee(C.byref(desc), e.adresse, e.octets, _flux(flux)))
+        else:
+            ev = (C.c_void_p * 6)(*[int(v) if v else None for v in evenements])
+            verifier(lib.trc_moe_couche_chrono(C.byref(desc), e.adresse, e.octets, _flux(flux), ev))
+
+
+def espace_octets(dims: DimsExpert, k: int) -> int:
+    return int(lib.trc_moe_espace_octets(C.byref(dims), k))

@@ -1,0 +1,167 @@
+"""Device plumbing around the C-ABI for a synthetic MoE layer: uploads a layer's parts, LUTs and
+router to HBM (PyTorch allocations), and runs the layer three ways on the same stream:
+
+- ``fusionnee``: the fused path (trc_routeur + trc_moe_couche_fusionnee) on v1.2 parts;
+- ``brute``: the same entry on the raw parts (the uncompressed MXFP4 path);
+- ``decodee``: the reference's decode-then-multiply sequence (trc_decoder_lot into slots, then
+  trc_gemv_lot, trc_swiglu_oai, trc_gemv_lot, trc_combiner), as trc-modele's fin_couche does.
+
+All three give the same bits. PyTorch only provides memory and streams here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import DescDecodage, DescGemv, DimsExpert, MoeCouche, Noyaux, espace_octets, taille_emplacement
+from .synth import Couche
+
+
+def _octets(b: bytes, alignement: int = 4096) -> int:
+    return (len(b) + alignement - 1) // alignement * alignement
+
+
+class CoucheCarte:
+    def __init__(self, c: Couche, k: int = 4, brut: bool = True, device: str = "cuda", n_delta: int = 0,
+                 n_codes: int = 0):
+        self.c = c
+        self.k = k
+        self.dims = c.dims
+        self.dev = torch.device(device)
+        self.n = Noyaux()
+        E = c.experts
+        self.parties, self.adresses, self.tailles = self._monter(c.parties)
+        if brut and c.parties_brutes and c.parties_brutes[0] is not None:
+            self.parties_b, self.adresses_b, self.tailles_b = self._monter(c.parties_brutes)
+        else:
+            self.parties_b = None
+        self.octets_compresses = [len(p) for p in c.parties]
+        self.luts = torch.from_numpy(c.luts.view(np.int32).copy()).to(self.dev)
+        self.wr = torch.from_numpy(c.wr).to(self.dev)
+        self.br = torch.from_numpy(c.br).to(self.dev)
+        self.logits = torch.zeros(E, dtype=torch.float32, device=self.dev)
+        self.idx = torch.zeros(k, dtype=torch.int32, device=self.dev)
+        self.poids = torch.zeros(k, dtype=torch.float32, device=self.dev)
+        self.controle = torch.zeros(4 * k, dtype=torch.int32, device=self.dev)
+        self.espace = torch.empty(espace_octets(self.dims, k) + 256, dtype=torch.uint8, device=self.dev)
+        self.n_delta, self.n_codes = n_delta, n_codes
+        d = self.dims
+        self.R0, self.C0, self.R2 = d.lignes[0], d.colonnes[0], d.lignes[2]
+
+    def _monter(self, parties):
+        tailles = [len(p) for p in parties]
+        decal = np.cumsum([0] + [_octets(p) for p in parties])
+        buf = np.zeros(int(decal[-1]), np.uint8)
+        for i, p in enumerate(parties):
+            buf[decal[i]:decal[i] + len(p)] = np.frombuffer(p, np.uint8)
+        t = torch.from_numpy(buf).to(self.dev)
+        base = t.data_ptr()
+        adresses = torch.tensor([base + int(o) for o in decal[:-1]], dtype=torch.int64, device=self.dev)
+        tl = torch.tensor(tailles, dtype=torch.int64, device=self.dev)
+        return t, adresses, tl
+
+    def partie(self, x: int, brute: bool = False) -> torch.Tensor:
+        """Device view (tensor slice) of expert x's part."""
+        src = self.c.parties_brutes if brute else self.c.parties
+        buf = self.parties_b if brute else self.parties
+        o = sum(_octets(p) for p in src[:x])
+        return buf[o:o + len(src[x])]
+
+    def routeur(self, x: torch.Tensor, flux=None) -> None:
+        self.n.routeur(self.wr, self.br, x, x.dtype == torch.bfloat16, self.c.experts, self.C0, self.k, self.logits,
+                       self.idx, self.poids, flux)
+
+    def descripteur(self, x: torch.Tensor, residu: torch.Tensor, brute: bool) -> MoeCouche:
+        if x.numel() != self.C0 or not x.is_contiguous() or x.device.type != "cuda":
+            raise ValueError(f"x: {self.C0} contiguous elements on the device expected")
+        if residu.numel() != self.R2 or residu.dtype != torch.float32 or not residu.is_contiguous():
+            raise ValueError(f"residual: {self.R2} contiguous f32 expected")
+        desc = MoeCouche()
+        if brute:
+            desc.parties, desc.parties_octets = self.adresses_b.data_ptr(), self.tailles_b.data_ptr()
+        else:
+            desc.parties, desc.parties_octets = self.adresses.data_ptr(), self.tailles.data_ptr()
+        desc.experts = self.c.experts
+        desc.k = self.k
+        desc.luts = self.luts.data_ptr()
+        desc.dims = self.dims
+        desc.indices = self.idx.data_ptr()
+        desc.poids = self.poids.data_ptr()
+        desc.x = x.data_ptr()
+        desc.x_bf16 = int(x.dtype == torch.bfloat16)
+        desc.brut = int(brute)
+        desc.residu = residu.data_ptr()
+        desc.controle = self.controle.data_ptr()
+        desc.n_delta, desc.n_codes = self.n_delta, self.n_codes
+        return desc
+
+    def _espace(self):
+        a = self.espace.data_ptr()
+        d = (-a) % 256
+        return self.espace[d:]
+
+    def couche(self, x: torch.Tensor, residu: torch.Tensor, brute: bool = False, flux=None, routeur: bool = True,
+               evenements=None):
+        """Router then the fused layer; `residu` (f32) is updated in place."""
+        if routeur:
+            self.routeur(x, flux)
+        self._desc = self.descripteur(x, residu, brute)  # keep it alive while the launch reads it
+        self.n.moe_couche(self._desc, self._espace(), flux, evenements)
+
+    # ---------------------------------------------------------------- decode-then-multiply
+
+    def preparer_decodee(self):
+        """Slots and descriptors for the decode-then-multiply sequence (k slots)."""
+        te = taille_emplacement(self.dims)
+        self.te = (te + 255) // 256 * 256
+        self.emplacements = torch.empty(self.k * self.te + 256, dtype=torch.uint8, device=self.dev)
+        self.ctl_d = torch.zeros(4 * self.k, dtype=torch.int32, device=self.dev)
+        self.g = torch.zeros(self.k, self.R0, dtype=torch.float32, device=self.dev)
+        self.u = torch.zeros_like(self.g)
+        self.h = torch.zeros_like(self.g)
+        self.s = torch.zeros(self.k, self.R2, dtype=torch.float32, device=self.dev)
+        self.x32 = torch.zeros(self.C0, dtype=torch.float32, device=self.dev)
+
+    def decodee(self, x: torch.Tensor, residu: torch.Tensor, flux=None):
+        """Router, then decoder_lot into slots, gemv_lot (gate, up), swiglu, gemv_lot (down),
+        combiner. Reads the router's indices on the host, as the reference's scheduler does."""
+        self.routeur(x, flux)
+        self.x32.copy_(x.float())
+        idx = self.idx.cpu().numpy()
+        base = self.emplacements.data_ptr()
+        base += (-base) % 256
+        d = self.dims
+        descs = (DescDecodage * self.k)()
+        for i, e in enumerate(idx):
+            descs[i] = DescDecodage(int(self.adresses[int(e)].item()), base + i * self.te, self.luts.data_ptr(),
+                                    self.ctl_d.data_ptr() + 16 * i)
+        dd = torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).to(self.dev)
+        self.n.decoder_lot(dd, self.k, d, flux)
+        from . import lib
+
+        pas = [0, 0, 0]
+        for j in range(3):
+            R, Cc = d.lignes[j], d.colonnes[j]
+            nb = R * (Cc // 32)
+            eo = (nb * 16 + 255) & ~255
+            bo = (eo + nb + 255) & ~255
+            pas[j] = (bo + 4 * R + 255) & ~255
+        off = [0, pas[0], pas[0] + pas[1]]
+        gu = (DescGemv * (2 * self.k))()
+        for i in range(self.k):
+            for j in range(2):
+                gu[2 * i + j] = DescGemv(base + i * self.te + off[j], self.x32.data_ptr(),
+                                         (self.g if j == 0 else self.u)[i].data_ptr(), d.lignes[j], d.colonnes[j])
+        dg = torch.frombuffer(bytearray(bytes(gu)), dtype=torch.uint8).to(self.dev)
+        self.n.gemv_lot(dg, 2 * self.k, self.R0, flux)
+        self.n.swiglu_oai(self.g, self.u, self.h, self.k * self.R0, flux)
+        dn = (DescGemv * self.k)()
+        for i in range(self.k):
+            dn[i] = DescGemv(base + i * self.te + off[2], self.h[i].data_ptr(), self.s[i].data_ptr(), d.lignes[2],
+                             d.colonnes[2])
+        ddn = torch.frombuffer(bytearray(bytes(dn)), dtype=torch.uint8).to(self.dev)
+        self.n.gemv_lot(ddn, self.k, self.R2, flux)
+        self.n.combiner(residu, self.s, self.R2, self.poids, self.k, self.R2, flux)
+        self._garde = (dd, dg, ddn)

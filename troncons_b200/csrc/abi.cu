@@ -1,0 +1,281 @@
+// troncons_b200 — the C-ABI entry points (include/troncons_b200.h): argument checks with the
+// reference's rules (trc-noyaux/src/lib.rs `Noyaux`, `Erreur::Usage`), then the launches.
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "../../include/troncons_b200.h"
+#include "commun.cuh"
+#include "mxfp4.cuh"
+#include "noyaux.h"
+
+namespace {
+
+thread_local std::string g_erreur;
+
+int usage(const char* fmt, ...) {
+    char b[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(b, sizeof b, fmt, ap);
+    va_end(ap);
+    g_erreur = b;
+    return TRC_ERR_USAGE;
+}
+
+int statut(cudaError_t e) {
+    if (e == cudaSuccess) {
+        g_erreur.clear();
+        return TRC_OK;
+    }
+    g_erreur = std::string("CUDA: ") + cudaGetErrorString(e);
+    return TRC_ERR_CUDA;
+}
+
+bool aligne(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// This library links its own (static) CUDA runtime: before launching on the caller's stream,
+// make this runtime's current device the stream's device (the caller may have chosen it
+// through another runtime instance, e.g. PyTorch's).
+cudaError_t sur_le_device_du_flux(void* flux) {
+    if (flux == nullptr) return cudaSuccess;
+    int d = -1, cur = -1;
+    cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(flux), &d);
+    if (e != cudaSuccess) return e;
+    e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return e;
+    return cur == d ? cudaSuccess : cudaSetDevice(d);
+}
+
+#define SUR_LE_FLUX(f)                                        \
+    do {                                                      \
+        const cudaError_t e_ = sur_le_device_du_flux(f);      \
+        if (e_ != cudaSuccess) return statut(e_);             \
+    } while (0)
+
+tb::Dims dims_de(const trc_dims_expert* d) {
+    tb::Dims r;
+    for (int j = 0; j < 3; ++j) {
+        r.lignes[j] = d->lignes[j];
+        r.colonnes[j] = d->colonnes[j];
+    }
+    return r;
+}
+
+// DimsExpert::verifier (abi.rs:98-108).
+int verifier_dims(const trc_dims_expert* d) {
+    if (d == nullptr) return usage("dims absent");
+    for (int j = 0; j < 3; ++j) {
+        const uint32_t r = d->lignes[j], c = d->colonnes[j];
+        if (r == 0 || c == 0 || c % 32 != 0) return usage("matrix %d: shape %u x %u (columns must be a multiple of 32)", j, r, c);
+        if (uint64_t(r) * (c / 32) * 16 > 0xFFFFFFFFull) return usage("matrix %d: more than 4 GiB of codes", j);
+    }
+    return TRC_OK;
+}
+
+}  // namespace
+
+namespace tb {
+
+cudaError_t assurer_smem(const void* noyau, int octets) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> fait;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> g(mu);
+    int& v = fait[{noyau, dev}];
+    if (v >= octets) return cudaSuccess;
+    e = cudaFuncSetAttribute(noyau, cudaFuncAttributeMaxDynamicSharedMemorySize, octets);
+    if (e == cudaSuccess) v = octets;
+    return e;
+}
+
+}  // namespace tb
+
+extern "C" {
+
+const char* trc_derniere_erreur(void) { return g_erreur.c_str(); }
+
+uint64_t trc_taille_emplacement(const trc_dims_expert* dims) {
+    if (dims == nullptr) return 0;
+    uint64_t s = 0;
+    for (int j = 0; j < 3; ++j) s += tb::disposition_matrice(dims->lignes[j], dims->colonnes[j]).pas;
+    return s;
+}
+
+int trc_decoder_expert(const void* partie, size_t partie_octets, void* emplacement, size_t emplacement_octets,
+                       const uint32_t* luts, size_t luts_octets, const trc_dims_expert* dims, uint32_t* controle,
+                       size_t controle_octets, void* flux) {
+    if (int s = verifier_dims(dims)) return s;
+    if (partie == nullptr || partie_octets < 64) return usage("part of %zu bytes (a 64-byte header at least)", partie_octets);
+    if (!aligne(partie, 16)) return usage("part not aligned on 16");
+    if (emplacement == nullptr || emplacement_octets < trc_taille_emplacement(dims))
+        return usage("slot of %zu bytes, %llu needed", emplacement_octets, (unsigned long long)trc_taille_emplacement(dims));
+    if (!aligne(emplacement, 256)) return usage("slot not aligned on 256");
+    if (luts == nullptr || luts_octets < 3u * 4u * 4096u * 4u || !aligne(luts, 16)) return usage("LUTs of %zu bytes (196,608, 16-aligned)", luts_octets);
+    if (controle == nullptr || controle_octets < 16 || !aligne(controle, 4)) return usage("control buffer under 16 bytes");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_decodage(nullptr, 1, partie, partie_octets, emplacement, luts, dims_de(dims), controle,
+                                      static_cast<cudaStream_t>(flux)));
+}
+
+int trc_decoder_lot(const trc_desc_decodage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
+                    void* flux) {
+    if (int s = verifier_dims(dims)) return s;
+    if (n == 0 || n > 65535) return usage("batch of %u experts", n);
+    if (descs == nullptr || descs_octets < size_t(n) * sizeof(trc_desc_decodage) || !aligne(descs, 8))
+        return usage("descriptors too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_decodage(reinterpret_cast<const tb::DescDecodage*>(descs), n, nullptr, 0, nullptr, nullptr,
+                                      dims_de(dims), nullptr, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_copier_brut(const void* partie, size_t partie_octets, void* emplacement, size_t emplacement_octets,
+                    const trc_dims_expert* dims, uint32_t* controle, size_t controle_octets, void* flux) {
+    if (int s = verifier_dims(dims)) return s;
+    if (partie == nullptr || partie_octets < 64 || !aligne(partie, 16)) return usage("part too short or not 16-aligned");
+    if (emplacement == nullptr || emplacement_octets < trc_taille_emplacement(dims) || !aligne(emplacement, 256))
+        return usage("slot too short or not 256-aligned");
+    if (controle == nullptr || controle_octets < 16 || !aligne(controle, 4)) return usage("control buffer under 16 bytes");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_copier_brut(partie, partie_octets, emplacement, dims_de(dims), controle,
+                                         static_cast<cudaStream_t>(flux)));
+}
+
+int trc_gemv(const void* matrice, size_t matrice_octets, const float* x, size_t x_octets, float* y, size_t y_octets,
+             uint32_t lignes, uint32_t colonnes, void* flux) {
+    if (lignes == 0 || colonnes == 0 || colonnes % 32 != 0) return usage("shape %u x %u", lignes, colonnes);
+    if (uint64_t(lignes) * (colonnes / 32) * 16 > 0xFFFFFFFFull) return usage("more than 4 GiB of codes");
+    const uint64_t pas = tb::disposition_matrice(lignes, colonnes).pas;
+    if (matrice == nullptr || matrice_octets < pas) return usage("matrix of %zu bytes, %llu needed", matrice_octets, (unsigned long long)pas);
+    if (!aligne(matrice, 256)) return usage("matrix not aligned on 256");
+    if (x == nullptr || x_octets < 4ull * colonnes || !aligne(x, 16)) return usage("x too short or not aligned on 16");
+    if (y == nullptr || y_octets < 4ull * lignes) return usage("y too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_gemv(matrice, x, y, lignes, colonnes, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_gemv_lot(const trc_desc_gemv* descs, size_t descs_octets, uint32_t n, uint32_t lignes_max, void* flux) {
+    if (n == 0 || n > 65535) return usage("batch of %u products", n);
+    if (descs == nullptr || descs_octets < size_t(n) * sizeof(trc_desc_gemv) || !aligne(descs, 8))
+        return usage("descriptors too short");
+    if (lignes_max == 0) return usage("lignes_max = 0");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_gemv_lot(reinterpret_cast<const tb::DescGemv*>(descs), n, lignes_max,
+                                      static_cast<cudaStream_t>(flux)));
+}
+
+int trc_gemv_f32(const float* w, size_t w_octets, const float* x, size_t x_octets, const float* biais,
+                 size_t biais_octets, float* y, size_t y_octets, uint32_t lignes, uint32_t colonnes, void* flux) {
+    if (lignes == 0 || colonnes == 0 || colonnes % 4 != 0) return usage("shape %u x %u", lignes, colonnes);
+    if (w == nullptr || w_octets < 4ull * lignes * colonnes || !aligne(w, 16)) return usage("f32 matrix too short or not aligned on 16");
+    if (x == nullptr || x_octets < 4ull * colonnes || !aligne(x, 16)) return usage("x too short or not aligned on 16");
+    if (y == nullptr || y_octets < 4ull * lignes) return usage("y too short");
+    if (biais != nullptr && biais_octets < 4ull * lignes) return usage("bias too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_gemv_f32(w, x, 0, biais, y, lignes, colonnes, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_routeur_topk(const float* logits, size_t logits_octets, uint32_t experts, uint32_t k, uint32_t* indices,
+                     size_t indices_octets, float* poids, size_t poids_octets, uint64_t boite, uint32_t sequence,
+                     void* flux) {
+    if (experts == 0 || experts > 256 || k == 0 || k > 8 || k > experts) return usage("top-%u of %u", k, experts);
+    if (logits == nullptr || logits_octets < 4ull * experts || indices == nullptr || indices_octets < 4ull * k ||
+        poids == nullptr || poids_octets < 4ull * k)
+        return usage("router: buffers too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_topk(logits, experts, k, indices, poids, reinterpret_cast<uint32_t*>(boite), sequence,
+                                  static_cast<cudaStream_t>(flux)));
+}
+
+int trc_swiglu_oai(const float* g, size_t g_octets, const float* u, size_t u_octets, float* y, size_t y_octets,
+                   uint32_t n, void* flux) {
+    const uint64_t o = 4ull * n;
+    if (n == 0 || g == nullptr || u == nullptr || y == nullptr || g_octets < o || u_octets < o || y_octets < o)
+        return usage("swiglu: buffers too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_swiglu(g, u, y, n, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_combiner(float* residu, size_t residu_octets, const float* sorties, size_t sorties_octets, uint32_t pas,
+                 const float* poids, size_t poids_octets, uint32_t n, uint32_t d, void* flux) {
+    if (n == 0 || d == 0 || (n > 1 && pas < d)) return usage("combine %u outputs of %u (stride %u)", n, d, pas);
+    if (residu == nullptr || residu_octets < 4ull * d || sorties == nullptr ||
+        sorties_octets < 4ull * ((uint64_t(n) - 1) * pas + d))
+        return usage("combine: buffers too short");
+    if (poids != nullptr && poids_octets < 4ull * n) return usage("weights too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_combiner(residu, sorties, pas, poids, n, d, static_cast<cudaStream_t>(flux)));
+}
+
+uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k) {
+    if (dims == nullptr || k == 0) return 0;
+    return tb::plan_espace(dims->lignes, dims->colonnes, k).total;
+}
+
+int trc_moe_couche_fusionnee(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
+    return trc_moe_couche_chrono(c, espace, espace_octets, flux, nullptr);
+}
+
+int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux,
+                          void* const* evenements) {
+    if (c == nullptr) return usage("layer descriptor absent");
+    if (int s = verifier_dims(&c->dims)) return s;
+    const trc_dims_expert& d = c->dims;
+    if (c->k == 0 || c->k > 8 || c->k > c->experts) return usage("k = %u of %u experts", c->k, c->experts);
+    if (d.lignes[0] != d.lignes[1] || d.colonnes[0] != d.colonnes[1] || d.colonnes[2] != d.lignes[0] ||
+        d.lignes[2] != d.colonnes[0])
+        return usage("gate/up/down shapes do not chain (hidden -> ffn -> hidden)");
+    for (int j = 0; j < 3; ++j) {
+        if (d.colonnes[j] > 32768) return usage("matrix %d: %u columns (32,768 at most)", j, d.colonnes[j]);
+        if (!c->brut && d.colonnes[j] < 256) return usage("matrix %d: %u columns (256 at least)", j, d.colonnes[j]);
+    }
+    if (c->parties == nullptr || c->parties_octets == nullptr || c->indices == nullptr || c->poids == nullptr ||
+        c->x == nullptr || c->residu == nullptr || c->controle == nullptr || (!c->brut && c->luts == nullptr))
+        return usage("layer descriptor: a device buffer is missing");
+    if (!aligne(c->x, c->x_bf16 ? 2 : 4)) return usage("x misaligned");
+    const uint64_t besoin = tb::plan_espace(d.lignes, d.colonnes, c->k).total;
+    if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
+        return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
+    tb::Couche k{};
+    k.parties = c->parties;
+    k.parties_octets = c->parties_octets;
+    k.experts = c->experts;
+    k.k = c->k;
+    k.luts = c->luts;
+    for (int j = 0; j < 3; ++j) {
+        k.lignes[j] = d.lignes[j];
+        k.colonnes[j] = d.colonnes[j];
+    }
+    k.indices = c->indices;
+    k.poids = c->poids;
+    k.x = c->x;
+    k.x_bf16 = c->x_bf16 ? 1u : 0u;
+    k.brut = c->brut ? 1u : 0u;
+    k.residu = c->residu;
+    k.controle = c->controle;
+    k.n_delta = c->n_delta;
+    k.n_codes = c->n_codes;
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_moe(k, espace, static_cast<cudaStream_t>(flux),
+                                 reinterpret_cast<cudaEvent_t const*>(evenements)));
+}
+
+int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts, uint32_t colonnes,
+                uint32_t k, float* logits, uint32_t* indices, float* poids, void* flux) {
+    if (experts == 0 || experts > 256 || k == 0 || k > 8 || k > experts) return usage("top-%u of %u", k, experts);
+    if (colonnes == 0 || colonnes % 4 != 0) return usage("%u columns (a multiple of 4)", colonnes);
+    if (wr == nullptr || !aligne(wr, 16) || x == nullptr || !aligne(x, x_bf16 ? 8 : 16) || logits == nullptr ||
+        indices == nullptr || poids == nullptr)
+        return usage("router: a buffer is missing or misaligned");
+    SUR_LE_FLUX(flux);
+    cudaStream_t s = static_cast<cudaStream_t>(flux);
+    cudaError_t e = tb::lancer_gemv_f32(wr, x, x_bf16 ? 1u : 0u, br, logits, experts, colonnes, s);
+    if (e == cudaSuccess) e = tb::lancer_topk(logits, experts, k, indices, poids, nullptr, 0, s);
+    return statut(e);
+}
+
+}  // extern "C"

@@ -1,0 +1,270 @@
+// troncons_b200 — device definitions shared by every kernel: the `.trc` part and rANS stream
+// layouts, the SoA slot layout, and the warp-level interleaved rANS decoder.
+//
+// Formats (read, never changed): part = 64-byte header + 16-byte stream descriptors + streams
+// aligned to 16 (trc-format/src/lib.rs:779-908; ARCHITECTURE.md 4.8); rANS stream = 16-byte
+// header, tile starts u32[T], lane states u32[32T], words u16[W] (rans.rs:169-280, 4.9.1).
+//
+// Decoding (rans.rs:388-451, the normative form): one warp decodes one tile, lane l holding
+// the rANS state of lane l. Per sub-step every lane looks its state up in the LUT, and lanes
+// whose state drops under L pull a 16-bit word, lanes in increasing order, from the tile's
+// shared word stream: the word position is the tile pointer plus the number of lower lanes
+// that also pull (ballot + popc). B200 specifics:
+//   - the tile's words are staged in a per-warp shared-memory ring by asynchronous 16-byte
+//     copies (cp.async, zero-filled past the tile's end) issued three 512-byte chunks ahead,
+//     so a renormalisation is one shared-memory load, not a pair of shuffles and selects;
+//   - the LUTs live in shared memory; the output byte is inserted with one byte permute.
+// No floating-point atomics; integer counters only (the determinism rule of commun.cuh:11-12).
+#pragma once
+
+#include <cstdint>
+
+namespace tb {
+
+constexpr uint32_t M = 4096u;     // 12-bit probabilities
+constexpr uint32_t L = 65536u;    // lower bound of the state
+constexpr uint32_t VOIES = 32u;   // lanes per tile
+constexpr uint32_t MAGIE_PARTIE0 = 0x30435254u;  // "TRC0"
+
+constexpr uint8_t SORTE_MEDIANES = 0x01;
+constexpr uint8_t SORTE_BIAIS = 0x02;
+constexpr uint8_t SORTE_DELTA = 0x03;
+constexpr uint8_t SORTE_CODES_CTX = 0x04;
+constexpr uint8_t SORTE_CODES_BRUTS = 0x06;
+constexpr uint8_t SORTE_ECHELLES_BRUTES = 0x07;
+
+constexpr int CTL_HORS_L = 0;
+constexpr int CTL_FORMAT = 1;
+constexpr int CTL_POINTEUR = 2;
+
+// Per-warp word ring: 1024 words (2 KiB), refilled by chunks of 256 words (32 lanes x 16 B).
+constexpr uint32_t ANNEAU_MOTS = 1024u;
+constexpr uint32_t TRANCHE_MOTS = 256u;
+
+struct Dims {
+    uint32_t lignes[3];
+    uint32_t colonnes[3];
+};
+
+__host__ __device__ __forceinline__ uint64_t al256(uint64_t x) { return (x + 255u) & ~uint64_t(255); }
+
+// SoA slot layout of one matrix (abi.rs:69-89): codes at 0, scales at al256(16 nb), biases at
+// al256(scales + nb), stride al256(biases + 4R). `base` = offset of the matrix in the slot.
+struct Disposition {
+    uint64_t base, echelles, biais, pas;
+};
+
+__host__ __device__ inline Disposition disposition_matrice(uint32_t R, uint32_t C) {
+    const uint64_t nb = uint64_t(R) * (C / 32u);
+    Disposition d;
+    d.base = 0;
+    d.echelles = al256(nb * 16u);
+    d.biais = al256(d.echelles + nb);
+    d.pas = al256(d.biais + 4ull * R);
+    return d;
+}
+
+__host__ __device__ __forceinline__ uint32_t choisir(const uint32_t (&a)[3], uint32_t j) {
+    return j == 0 ? a[0] : (j == 1 ? a[1] : a[2]);
+}
+
+__host__ __device__ inline Disposition disposition(const Dims& d, uint32_t j) {
+    uint64_t base = 0;
+    for (uint32_t i = 0; i < 3; ++i)
+        if (i < j) base += disposition_matrice(d.lignes[i], d.colonnes[i]).pas;
+    Disposition r = disposition_matrice(choisir(d.lignes, j), choisir(d.colonnes, j));
+    r.base = base;
+    return r;
+}
+
+// ------------------------------------------------------------------ parts and streams
+
+struct Flux {
+    const uint8_t* p;    // stream start (16-aligned when the part is)
+    uint32_t longueur;   // stream bytes
+    uint32_t produits;   // bytes its decoding produces (stream table)
+};
+
+// First stream (sorte, matrice) of a level-0 part of `taille` bytes (at least 64), with the
+// structural checks the kernels can afford (trouver_flux, commun.cuh:111-129 of the reference,
+// plus the part size the host knows): magic and level 0, stream table and stream inside the
+// useful bytes, useful bytes inside the buffer, stream offset 16-aligned.
+__device__ inline bool trouver_flux(const uint8_t* partie, uint64_t taille, uint8_t sorte, uint32_t matrice, Flux& f) {
+    const uint4 tete = *reinterpret_cast<const uint4*>(partie);
+    if (tete.x != MAGIE_PARTIE0) return false;
+    if ((tete.z & 0xFFu) != 0) return false;  // level 0
+    const uint32_t n_flux = tete.z >> 16;
+    const uint32_t utiles = tete.w;
+    if (utiles > taille || n_flux > 255u || 64u + 16u * n_flux > utiles) return false;
+    for (uint32_t i = 0; i < n_flux; ++i) {
+        const uint4 e = *reinterpret_cast<const uint4*>(partie + 64 + 16 * i);
+        if ((e.x & 0xFFu) == sorte && ((e.x >> 8) & 0xFFu) == matrice) {
+            if ((e.y & 15u) != 0 || uint64_t(e.y) + e.z > utiles) return false;
+            f.p = partie + e.y;
+            f.longueur = e.z;
+            f.produits = e.w;
+            return true;
+        }
+    }
+    return false;
+}
+
+// A validated rANS stream header (rans.rs:231-280; commun.cuh:146-165 of the reference).
+struct EnteteRans {
+    uint32_t P, N, T, W;
+    const uint32_t* debut;  // T tile starts (word indices)
+    const uint32_t* etats;  // 32 T lane states
+    const uint8_t* mots;    // words u16[W] (4-byte aligned)
+};
+
+// `besoin`: the useful bytes the stream must produce; P is besoin rounded up to 128.
+__device__ inline bool lire_entete(const Flux& f, uint32_t besoin, EnteteRans& h) {
+    if (f.longueur < 16) return false;
+    const uint4 t = *reinterpret_cast<const uint4*>(f.p);
+    h.P = t.x;
+    h.N = t.y & 0xFFFFu;
+    const uint32_t geo = (t.y >> 16) & 0xFFu, reserve = t.y >> 24;
+    h.T = t.z;
+    h.W = t.w;
+    if (geo != 1u || reserve != 0 || h.N == 0 || (h.P & 127u) != 0) return false;
+    if (h.P < besoin || h.P - besoin >= 128u) return false;
+    if (f.produits != h.P && f.produits != besoin) return false;
+    const uint32_t macro = h.P / 128u;
+    if (h.T != (macro + h.N - 1) / h.N) return false;
+    if (16ull + 132ull * h.T + 2ull * h.W > f.longueur) return false;
+    h.debut = reinterpret_cast<const uint32_t*>(f.p + 16);
+    h.etats = reinterpret_cast<const uint32_t*>(f.p + 16 + 4ull * h.T);
+    h.mots = f.p + 16 + 132ull * h.T;
+    return true;
+}
+
+// ------------------------------------------------------------------ async copies
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, uint32_t src_octets) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_octets) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// ------------------------------------------------------------------ the warp decoder
+
+// One warp decoding one tile. All fields but `x` are warp-uniform.
+struct Decodeur {
+    uint32_t x;            // rANS state of this lane
+    uint32_t ptr;          // next word index in the stream
+    uint32_t fin;          // end of the tile's words (debut[t+1], or W for the last tile)
+    uint32_t lim;          // words at or past `lim` read as 0: min(fin, W)
+    uint32_t dec;          // words between the 16-aligned base `ga` and mots[0]
+    uint32_t tranche;      // chunk (of 256 aligned words from ga) the pointer is in
+    const uint8_t* ga;     // 16-aligned address at or below mots[0]
+    uint16_t* anneau;      // this warp's ring (ANNEAU_MOTS words, shared memory)
+    uint32_t masque_inf;   // lanes below this one
+
+    // Chunk c (aligned words [256c, 256c + 256)) into its ring slot; each lane copies 16 bytes,
+    // zero-filled past `lim`.
+    __device__ __forceinline__ void charger(uint32_t c, uint32_t voie) {
+        const uint32_t a0 = c * TRANCHE_MOTS + 8u * voie;   // aligned index of the lane's first word
+        const int64_t i0 = int64_t(a0) - int64_t(dec);      // stream word index
+        int64_t utiles = int64_t(lim) - i0;                 // words this lane may read
+        utiles = utiles < 0 ? 0 : (utiles > 8 ? 8 : utiles);
+        const uint8_t* src = utiles > 0 ? ga + 2ull * a0 : ga;
+        cp_async16(anneau + (a0 & (ANNEAU_MOTS - 1u)), src, uint32_t(2 * utiles));
+    }
+
+    __device__ __forceinline__ void debut(const EnteteRans& h, uint32_t t, uint32_t voie, uint16_t* ring) {
+        anneau = ring;
+        masque_inf = (1u << voie) - 1u;
+        x = h.etats[t * VOIES + voie];
+        ptr = h.debut[t];
+        fin = (t + 1 < h.T) ? h.debut[t + 1] : h.W;
+        lim = fin < h.W ? fin : h.W;
+        const uintptr_t m = reinterpret_cast<uintptr_t>(h.mots);
+        ga = reinterpret_cast<const uint8_t*>(m & ~uintptr_t(15));
+        dec = uint32_t(m & 15u) >> 1;
+        tranche = (ptr + dec) / TRANCHE_MOTS;
+        __syncwarp();
+#pragma unroll
+        for (uint32_t c = 0; c < 4; ++c) {
+            charger(tranche + c, voie);
+            cp_async_commit();
+        }
+        cp_async_wait<2>();
+        __syncwarp();
+    }
+
+    // At the start of each macro-step: when the pointer entered a new chunk, refill the slot
+    // of the chunk left behind with the chunk three ahead, and make sure the current and next
+    // chunks (all this macro-step can read: at most 128 words) have landed.
+    __device__ __forceinline__ void avancer(uint32_t voie) {
+        const uint32_t c = (ptr + dec) / TRANCHE_MOTS;
+        if (c != tranche) {
+            tranche = c;
+            __syncwarp();
+            charger(c + 3u, voie);
+            cp_async_commit();
+            cp_async_wait<2>();
+            __syncwarp();
+        }
+    }
+
+    // One sub-step; returns the LUT entry (its low byte is the symbol).
+    __device__ __forceinline__ uint32_t pas(const uint32_t* __restrict__ lut) {
+        const uint32_t e = lut[x & (M - 1u)];
+        const uint32_t y = (((e >> 8) & 0xFFFu) + 1u) * (x >> 12) + (e >> 20);
+        const bool besoin = y < L;
+        const uint32_t vote = __ballot_sync(0xFFFFFFFFu, besoin);
+        const uint32_t pos = ptr + __popc(vote & masque_inf);
+        const uint32_t w = anneau[(pos + dec) & (ANNEAU_MOTS - 1u)];
+        x = besoin ? ((y << 16) | w) : y;
+        ptr += __popc(vote);
+        return e;
+    }
+
+    // Four sub-steps: the lane's 32-bit output word (byte k = sub-step k).
+    __device__ __forceinline__ uint32_t macro(const uint32_t* __restrict__ lut) {
+        uint32_t m = pas(lut);
+        m = __byte_perm(m, pas(lut), 0x0040);
+        m = __byte_perm(m, pas(lut), 0x0410);
+        m = __byte_perm(m, pas(lut), 0x4210);
+        return m;
+    }
+
+    // End-of-tile integrity: lanes off L; the word pointer must end at the tile's end.
+    __device__ __forceinline__ void bilan(uint32_t voie, uint32_t& hors_l, uint32_t& pointeur) const {
+        hors_l += x != L ? 1u : 0u;
+        pointeur += (voie == 0 && ptr != fin) ? 1u : 0u;
+    }
+
+    // Drains the copies still in flight (the ring must not be written after the warp leaves).
+    __device__ __forceinline__ void terminer() {
+        cp_async_wait<0>();
+        __syncwarp();
+    }
+};
+
+__device__ __forceinline__ uint32_t somme_warp(uint32_t v) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, d);
+    return v;
+}
+
+__device__ __forceinline__ void verser_controle(uint32_t* controle, uint32_t voie, uint32_t hors_l, uint32_t pointeur) {
+    hors_l = somme_warp(hors_l);
+    pointeur = somme_warp(pointeur);
+    if (voie == 0) {
+        if (hors_l) atomicAdd(&controle[CTL_HORS_L], hors_l);
+        if (pointeur) atomicAdd(&controle[CTL_POINTEUR], pointeur);
+    }
+}
+
+// Scale class of a block from its scale and its row's median (4.9.3): delta = e - med + 128.
+__device__ __forceinline__ uint32_t classe_echelle(uint32_t e, uint32_t med) {
+    const uint32_t d = (e - med + 128u) & 255u;
+    return d < 128u ? 0u : (d == 128u ? 1u : 2u);
+}
+
+}  // namespace tb

@@ -1,0 +1,276 @@
+// troncons_b200 — decoding a level-0 part into the SoA slot (the reference's decode-then-
+// multiply contract, trc-noyaux/noyaux/decodeur.cuh; the spec ARCHITECTURE.md 4.9 and 4.11).
+//
+// Two launches on the caller's stream, because CODES_CTX's per-lane table is chosen by the
+// scale class that DELTA gives (4.9.3: DELTA is always decoded first):
+//   k_echelles  grid (X, 3, n), 4 warps: DELTA_j -> scales e = (med[r] + delta - 128) mod 256,
+//               BIAIS_j copied bit for bit;
+//   k_codes     grid (X, 3, n), 8 warps: CODES_CTX_j with the lane's table kappa(w/4), from the
+//               scale just written and the row's median -> codes.
+// One warp per tile, tiles strided over the grid, so every grid gives the same bytes; `n`
+// experts of a batch are blockIdx.z (their descriptors carry their own part, slot, LUTs and
+// counters). Padding blocks past R*B use class 0 (the coder pads delta with 0).
+#include "commun.cuh"
+#include "noyaux.h"
+
+namespace tb {
+
+struct ArgsDecodage {
+    const DescDecodage* descs;  // batch: descriptors (device); single: null
+    const uint8_t* partie;
+    uint64_t taille;            // part bytes (UINT64_MAX in a batch: the header's useful bytes rule)
+    uint8_t* emplacement;
+    const uint32_t* luts;
+    uint32_t* controle;
+    Dims dims;
+};
+
+__device__ __forceinline__ void choisir_expert(const ArgsDecodage& a, const uint8_t*& partie, uint64_t& taille,
+                                               uint8_t*& emplacement, const uint32_t*& luts, uint32_t*& controle) {
+    if (a.descs) {
+        const DescDecodage d = a.descs[blockIdx.z];
+        partie = reinterpret_cast<const uint8_t*>(d.partie);
+        taille = ~uint64_t(0);
+        emplacement = reinterpret_cast<uint8_t*>(d.emplacement);
+        luts = reinterpret_cast<const uint32_t*>(d.luts);
+        controle = reinterpret_cast<uint32_t*>(d.controle);
+    } else {
+        partie = a.partie;
+        taille = a.taille;
+        emplacement = a.emplacement;
+        luts = a.luts;
+        controle = a.controle;
+    }
+}
+
+constexpr uint32_t ECH_WARPS = 4;
+constexpr uint32_t CODES_WARPS = 8;
+
+__global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
+    __shared__ uint32_t lut[M];
+    __shared__ uint8_t med_s[8192];
+    __shared__ __align__(16) uint16_t anneaux[ECH_WARPS][ANNEAU_MOTS];
+    const uint8_t* partie;
+    uint64_t taille;
+    uint8_t* emplacement;
+    const uint32_t* luts;
+    uint32_t* controle;
+    choisir_expert(a, partie, taille, emplacement, luts, controle);
+    const uint32_t j = blockIdx.y, voie = threadIdx.x & 31u;
+    const uint32_t R = choisir(a.dims.lignes, j), C = choisir(a.dims.colonnes, j);
+    const uint32_t B = C / 32u, nblocs = R * B;
+    Flux fd, fm, fb;
+    EnteteRans h;
+    const bool bon = B > 0 && R > 0 && trouver_flux(partie, taille, SORTE_DELTA, j, fd) &&
+                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && trouver_flux(partie, taille, SORTE_BIAIS, j, fb) &&
+                     fm.produits == R && fm.longueur >= R && fb.produits == 4u * R && fb.longueur >= 4u * R &&
+                     lire_entete(fd, nblocs, h);
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const Disposition disp = disposition(a.dims, j);
+    uint8_t* mat = emplacement + disp.base;
+    {
+        const uint32_t* bs = reinterpret_cast<const uint32_t*>(fb.p);
+        uint32_t* bd = reinterpret_cast<uint32_t*>(mat + disp.biais);
+        for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < R; i += gridDim.x * blockDim.x) bd[i] = bs[i];
+    }
+    const uint32_t warp0 = blockIdx.x * ECH_WARPS;
+    if (warp0 >= h.T) return;  // block-uniform: no tile for this block
+    const uint32_t* src = luts + (uint64_t(j) * 4u) * M;
+    for (uint32_t i = threadIdx.x; i < M; i += blockDim.x) lut[i] = src[i];
+    const uint8_t* med = fm.p;
+    if (R <= 8192u) {
+        for (uint32_t i = threadIdx.x; i < R; i += blockDim.x) med_s[i] = fm.p[i];
+        med = med_s;
+    }
+    __syncthreads();
+
+    uint8_t* ech = mat + disp.echelles;
+    const uint32_t nmacro = h.P / 128u;
+    uint32_t hors_l = 0, pointeur = 0;
+    Decodeur d;
+    for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * ECH_WARPS) {
+        d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
+        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+        // Word w = 32 m + lane carries delta of blocks 4w .. 4w + 3.
+        uint32_t b0 = 4u * (m0 * 32u + voie);
+        uint32_t ligne = b0 / B, reste = b0 - ligne * B;
+        for (uint32_t m = m0; m < m1; ++m) {
+            d.avancer(voie);
+            const uint32_t mot = d.macro(lut);
+            uint32_t sortie = 0;
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+                uint32_t rk = ligne, qk = reste + k;
+                while (qk >= B) {
+                    qk -= B;
+                    ++rk;
+                }
+                const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
+                sortie |= ((mk + ((mot >> (8u * k)) & 255u) - 128u) & 255u) << (8u * k);
+            }
+            if (b0 + 3u < nblocs) {
+                *reinterpret_cast<uint32_t*>(ech + b0) = sortie;
+            } else {
+                for (uint32_t k = 0; k < 4; ++k)
+                    if (b0 + k < nblocs) ech[b0 + k] = uint8_t(sortie >> (8u * k));
+            }
+            b0 += 128u;
+            reste += 128u;
+            if (B >= 32u) {
+                while (reste >= B) {
+                    reste -= B;
+                    ++ligne;
+                }
+            } else {
+                ligne += reste / B;
+                reste %= B;
+            }
+        }
+        d.bilan(voie, hors_l, pointeur);
+        d.terminer();
+    }
+    verser_controle(controle, voie, hors_l, pointeur);
+}
+
+__global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);                            // [3][M]
+    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);           // [8][ANNEAU_MOTS]
+    const uint8_t* partie;
+    uint64_t taille;
+    uint8_t* emplacement;
+    const uint32_t* luts;
+    uint32_t* controle;
+    choisir_expert(a, partie, taille, emplacement, luts, controle);
+    const uint32_t j = blockIdx.y, voie = threadIdx.x & 31u;
+    const uint32_t R = choisir(a.dims.lignes, j), C = choisir(a.dims.colonnes, j);
+    const uint32_t B = C / 32u, nblocs = R * B;
+    Flux fc, fm;
+    EnteteRans h;
+    const bool bon = B > 0 && R > 0 && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+                     lire_entete(fc, nblocs * 16u, h);
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const uint32_t warp0 = blockIdx.x * CODES_WARPS;
+    if (warp0 >= h.T) return;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(luts + (uint64_t(j) * 4u + 1u) * M);
+        uint4* dst = reinterpret_cast<uint4*>(lut);
+        for (uint32_t i = threadIdx.x; i < 3u * M / 4u; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    const Disposition disp = disposition(a.dims, j);
+    uint8_t* mat = emplacement + disp.base;
+    uint32_t* codes = reinterpret_cast<uint32_t*>(mat);
+    const uint8_t* __restrict__ ech = mat + disp.echelles;  // written by k_echelles
+    const uint8_t* __restrict__ med = fm.p;
+    const uint32_t nmacro = h.P / 128u;
+    const uint32_t mots_utiles = nblocs * 4u;
+    uint32_t hors_l = 0, pointeur = 0;
+    Decodeur d;
+    for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * CODES_WARPS) {
+        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_MOTS);
+        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+        // Word w = 32 m + lane belongs to block w / 4 = 8 m + lane / 4; its class needs the
+        // block's scale and its row's median, fetched one macro-step ahead.
+        uint32_t bloc = (m0 * 32u + voie) >> 2;
+        uint32_t ligne = bloc / B, reste = bloc - ligne * B;
+        bool valide = bloc < nblocs;
+        uint32_t e_s = valide ? __ldg(ech + bloc) : 0u;
+        uint32_t m_s = valide ? __ldg(med + ligne) : 0u;
+        for (uint32_t m = m0; m < m1; ++m) {
+            const uint32_t ctx = valide ? classe_echelle(e_s, m_s) : 0u;
+            bloc += 8u;
+            reste += 8u;
+            while (reste >= B) {
+                reste -= B;
+                ++ligne;
+            }
+            valide = (m + 1u < m1) && bloc < nblocs;
+            if (valide) {
+                e_s = __ldg(ech + bloc);
+                m_s = __ldg(med + ligne);
+            }
+            d.avancer(voie);
+            const uint32_t mot = d.macro(lut + ctx * M);
+            const uint32_t w = m * 32u + voie;
+            if (w < mots_utiles) codes[w] = mot;
+        }
+        d.bilan(voie, hors_l, pointeur);
+        d.terminer();
+    }
+    verser_controle(controle, voie, hors_l, pointeur);
+}
+
+// Raw part (file flag bit 2): ECHELLES_BRUTES_j, CODES_BRUTS_j, BIAIS_j copied into the slot.
+__global__ void __launch_bounds__(256) k_copier_brut(const uint8_t* partie, uint64_t taille, uint8_t* emplacement, Dims dims,
+                                                      uint32_t* controle) {
+    const uint32_t j = blockIdx.y;
+    const uint32_t R = choisir(dims.lignes, j), C = choisir(dims.colonnes, j);
+    const uint32_t B = C / 32u, nblocs = R * B;
+    Flux fe, fc, fb;
+    const bool bon = B > 0 && R > 0 && trouver_flux(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
+                     trouver_flux(partie, taille, SORTE_CODES_BRUTS, j, fc) && trouver_flux(partie, taille, SORTE_BIAIS, j, fb) &&
+                     fe.produits == nblocs && fe.longueur >= nblocs && fc.produits == 16u * nblocs &&
+                     fc.longueur >= 16u * nblocs && fb.produits == 4u * R && fb.longueur >= 4u * R;
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const Disposition disp = disposition(dims, j);
+    uint8_t* mat = emplacement + disp.base;
+    const uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x, pas = gridDim.x * blockDim.x;
+    const uint4* cs = reinterpret_cast<const uint4*>(fc.p);
+    uint4* cd = reinterpret_cast<uint4*>(mat);
+    for (uint32_t i = i0; i < nblocs; i += pas) cd[i] = cs[i];
+    const uint32_t n4 = nblocs / 4u;
+    const uint32_t* es = reinterpret_cast<const uint32_t*>(fe.p);
+    uint32_t* ed = reinterpret_cast<uint32_t*>(mat + disp.echelles);
+    for (uint32_t i = i0; i < n4; i += pas) ed[i] = es[i];
+    for (uint32_t i = 4u * n4 + i0; i < nblocs; i += pas) mat[disp.echelles + i] = fe.p[i];
+    const uint32_t* bs = reinterpret_cast<const uint32_t*>(fb.p);
+    uint32_t* bd = reinterpret_cast<uint32_t*>(mat + disp.biais);
+    for (uint32_t i = i0; i < R; i += pas) bd[i] = bs[i];
+}
+
+// ------------------------------------------------------------------ launchers
+
+static uint32_t tuiles_256(uint64_t octets) { return uint32_t(((octets + 127) / 128 + 255) / 256); }
+
+cudaError_t lancer_decodage(const DescDecodage* descs, uint32_t n, const void* partie, uint64_t taille, void* emplacement,
+                            const uint32_t* luts, const Dims& dims, uint32_t* controle, cudaStream_t flux) {
+    // Grids sized for the tiles trc-codeur writes (N = 256); any other N decodes too (the warps
+    // stride over the tiles), only with a different occupancy.
+    uint32_t td = 1, tc = 1;
+    for (int j = 0; j < 3; ++j) {
+        const uint64_t nb = uint64_t(dims.lignes[j]) * (dims.colonnes[j] / 32u);
+        td = std::max(td, tuiles_256(nb));
+        tc = std::max(tc, tuiles_256(16 * nb));
+    }
+    ArgsDecodage a{descs, static_cast<const uint8_t*>(partie), taille, static_cast<uint8_t*>(emplacement), luts, controle, dims};
+    const uint32_t z = descs ? n : 1u;
+    k_echelles<<<dim3((td + ECH_WARPS - 1) / ECH_WARPS, 3, z), ECH_WARPS * 32, 0, flux>>>(a);
+    const size_t smem = 3u * M * 4u + CODES_WARPS * ANNEAU_MOTS * 2u;
+    const cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_codes), int(smem));
+    if (e != cudaSuccess) return e;
+    k_codes<<<dim3((tc + CODES_WARPS - 1) / CODES_WARPS, 3, z), CODES_WARPS * 32, smem, flux>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t lancer_copier_brut(const void* partie, uint64_t taille, void* emplacement, const Dims& dims, uint32_t* controle,
+                               cudaStream_t flux) {
+    uint64_t n = 1;
+    for (int j = 0; j < 3; ++j) n = std::max<uint64_t>(n, uint64_t(dims.lignes[j]) * (dims.colonnes[j] / 32u));
+    const uint32_t g = uint32_t(std::min<uint64_t>(std::max<uint64_t>((n + 255) / 256, 1), 296));
+    k_copier_brut<<<dim3(g, 3, 1), 256, 0, flux>>>(static_cast<const uint8_t*>(partie), taille,
+                                                    static_cast<uint8_t*>(emplacement), dims, controle);
+    return cudaGetLastError();
+}
+
+}  // namespace tb

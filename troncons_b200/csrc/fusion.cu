@@ -1,0 +1,399 @@
+// troncons_b200 — the fused MoE layer: rANS decoding of the routed experts' parts fused into
+// the MXFP4 GEMV, then SwiGLU, the down projection and the weighted combine.
+//
+// The reference runs, per layer and routed expert, decoder_echelles + decoder_codes into an
+// SoA slot in VRAM, then gemv_mxfp4 x3, swiglu_oai, and combiner over the k experts
+// (trc-modele/src/lib.rs:533-553, trc-ordo/src/lib.rs:1328-1367). Here, on the caller's stream:
+//   1. k_moe_delta   DELTA_j of the k routed experts -> per block (scale | class << 8), into the
+//                    workspace (it stays in L2: 259,200 u16 per matrix);
+//   2. k_moe_codes   (gate, up) one warp per CODES_CTX tile decodes a macro-step (8 blocks) into
+//                    registers and multiplies it at once against 2x staged in shared memory;
+//                    the codes never leave the SM. Rows are closed where they end and at every
+//                    segment end (256 blocks), giving per-(row, segment) partials;
+//   3. k_moe_swiglu  gate and up rows = fold of their partials + bias; h = SwiGLU (f64);
+//   4. k_moe_codes   (down) the same on h;
+//   5. k_moe_combiner down rows + bias, then residual += ((w0 s0 + w1 s1) + ...), no FMA.
+// The raw path (`brut`) replaces 1-2 and 4 by k_moe_brut, a row-centric GEMV on CODES_BRUTS /
+// ECHELLES_BRUTES writing the same partials, so compressed and raw parts give the same bits.
+// Integrity counters go to controle[4 i ..] of active expert i (format errors included).
+#include <cuda_bf16.h>
+
+#include "commun.cuh"
+#include "mxfp4.cuh"
+#include "noyaux.h"
+
+namespace tb {
+
+Espace plan_espace(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t k) {
+    Espace e{};
+    uint64_t p = 0;
+    for (int j = 0; j < 3; ++j) {
+        const uint64_t nb = uint64_t(lignes[j]) * (colonnes[j] / 32u);
+        e.ek[j] = p;
+        p = al256(p + 2ull * nb * k);
+    }
+    for (int j = 0; j < 3; ++j) {
+        e.K[j] = parts_par_ligne(colonnes[j] / 32u);
+        e.parts[j] = p;
+        p = al256(p + 4ull * lignes[j] * e.K[j] * k);
+    }
+    e.h = p;
+    p = al256(p + 4ull * lignes[0] * k);
+    e.total = p;
+    return e;
+}
+
+struct ArgsMoe {
+    Couche c;
+    uint8_t* espace;
+    Espace plan;
+    uint32_t j0;  // first matrix of this launch (0: gate and up; 2: down)
+};
+
+// The part of active expert i, if it is addressable.
+__device__ __forceinline__ bool partie_de(const Couche& c, uint32_t i, const uint8_t*& partie, uint64_t& taille) {
+    const uint32_t e = c.indices[i];
+    if (e >= c.experts) return false;
+    partie = reinterpret_cast<const uint8_t*>(c.parties[e]);
+    taille = c.parties_octets[e];
+    return partie != nullptr && taille >= 64 && (reinterpret_cast<uintptr_t>(partie) & 15u) == 0;
+}
+
+constexpr uint32_t DELTA_WARPS = 4;
+constexpr uint32_t MOE_WARPS = 4;
+
+// ------------------------------------------------------------------ 1. DELTA -> scales, classes
+
+__global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
+    __shared__ uint32_t lut[M];
+    __shared__ uint8_t med_s[8192];
+    __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_MOTS];
+    const Couche& c = a.c;
+    const uint32_t j = blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
+    uint32_t* controle = c.controle + 4u * i;
+    const uint32_t R = c.lignes[j], B = c.colonnes[j] / 32u, nblocs = R * B;
+    const uint8_t* partie;
+    uint64_t taille;
+    Flux fd, fm;
+    EnteteRans h;
+    const bool bon = partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_DELTA, j, fd) &&
+                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+                     lire_entete(fd, nblocs, h);
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const uint32_t warp0 = blockIdx.x * DELTA_WARPS;
+    if (warp0 >= h.T) return;
+    const uint32_t* src = c.luts + (uint64_t(j) * 4u) * M;
+    for (uint32_t t = threadIdx.x; t < M; t += blockDim.x) lut[t] = src[t];
+    const uint8_t* med = fm.p;
+    if (R <= 8192u) {
+        for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med_s[t] = fm.p[t];
+        med = med_s;
+    }
+    __syncthreads();
+    uint16_t* ek = reinterpret_cast<uint16_t*>(a.espace + a.plan.ek[j]) + uint64_t(i) * nblocs;
+    const uint32_t nmacro = h.P / 128u;
+    uint32_t hors_l = 0, pointeur = 0;
+    Decodeur d;
+    for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * DELTA_WARPS) {
+        d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
+        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+        uint32_t b0 = 4u * (m0 * 32u + voie);
+        uint32_t ligne = b0 / B, reste = b0 - ligne * B;
+        for (uint32_t m = m0; m < m1; ++m) {
+            d.avancer(voie);
+            const uint32_t mot = d.macro(lut);
+            uint32_t v[4];
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+                uint32_t rk = ligne, qk = reste + k;
+                while (qk >= B) {
+                    qk -= B;
+                    ++rk;
+                }
+                const uint32_t dk = (mot >> (8u * k)) & 255u;
+                const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
+                const uint32_t kap = dk < 128u ? 0u : (dk == 128u ? 1u : 2u);
+                v[k] = ((mk + dk - 128u) & 255u) | (kap << 8);
+            }
+            if (b0 + 3u < nblocs) {
+                *reinterpret_cast<uint2*>(ek + b0) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
+            } else {
+                for (uint32_t k = 0; k < 4; ++k)
+                    if (b0 + k < nblocs) ek[b0 + k] = uint16_t(v[k]);
+            }
+            b0 += 128u;
+            reste += 128u;
+            if (B >= 32u) {
+                while (reste >= B) {
+                    reste -= B;
+                    ++ligne;
+                }
+            } else {
+                ligne += reste / B;
+                reste %= B;
+            }
+        }
+        d.bilan(voie, hors_l, pointeur);
+        d.terminer();
+    }
+    verser_controle(controle, voie, hors_l, pointeur);
+}
+
+// ------------------------------------------------------------------ shared-memory x2 = 2 x
+
+__device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t bf16, uint32_t C) {
+    if (bf16) {
+        const uint16_t* xb = static_cast<const uint16_t*>(x);
+        for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) x2s[t] = 2.0f * __uint_as_float(uint32_t(xb[t]) << 16);
+    } else {
+        const float* xf = static_cast<const float*>(x);
+        for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) x2s[t] = 2.0f * xf[t];
+    }
+}
+
+// ------------------------------------------------------------------ 2/4. CODES_CTX decoded into the GEMV
+
+__global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const Couche& c = a.c;
+    const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
+    uint32_t* controle = c.controle + 4u * i;
+    const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
+    const uint8_t* partie;
+    uint64_t taille;
+    Flux fc;
+    EnteteRans h;
+    const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                     lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const uint32_t warp0 = blockIdx.x * MOE_WARPS;
+    if (warp0 >= h.T) return;
+    uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);                                  // [3][M]
+    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);                 // [W][ANNEAU_MOTS]
+    float* x2s = reinterpret_cast<float*>(dyn + 3u * M * 4u + MOE_WARPS * ANNEAU_MOTS * 2u);
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M);
+        uint4* dst = reinterpret_cast<uint4*>(lut);
+        for (uint32_t t = threadIdx.x; t < 3u * M / 4u; t += blockDim.x) dst[t] = src[t];
+    }
+    if (j < 2)
+        charger_x2(x2s, c.x, c.x_bf16, C);
+    else
+        charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    __syncthreads();
+    const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
+    const uint16_t* __restrict__ ek = reinterpret_cast<const uint16_t*>(a.espace + a.plan.ek[j]) + uint64_t(i) * nblocs;
+    const uint32_t K = a.plan.K[j];
+    float* __restrict__ parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
+    const uint32_t nmacro = h.P / 128u;
+    const uint32_t q = voie & 3u, g = voie >> 2;
+    uint32_t hors_l = 0, pointeur = 0;
+    Decodeur d;
+    for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * MOE_WARPS) {
+        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_MOTS);
+        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+        // This lane's block (8 m + g) and its column block b; the warp's current row r and the
+        // first block of the next row.
+        uint32_t bloc = 8u * m0 + g;
+        uint32_t b = bloc % B;
+        uint32_t r = (8u * m0) / B;
+        uint32_t fin_r = (r + 1u) * B;
+        float acc = 0.0f, acc_s = 0.0f;
+        uint32_t ekv = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
+        for (uint32_t m = m0; m < m1; ++m) {
+            const bool valide = bloc < nblocs;
+            const uint32_t ctx = valide ? (ekv >> 8) : 0u;
+            const float sc = echelle_e8m0(ekv & 255u);
+            const uint32_t bloc_s = bloc + 8u;
+            ekv = (m + 1u < m1 && bloc_s < nblocs) ? uint32_t(__ldg(ek + bloc_s)) : 0u;
+            d.avancer(voie);
+            const uint32_t mot = d.macro(lut + ctx * M);
+            float s = produit_quad(mot, x2s4[8u * b + q], x2s4[8u * b + 4u + q]);
+            s = somme_quad(s);
+            if (valide) {
+                if (bloc < fin_r)
+                    acc = fmaf(s, sc, acc);
+                else
+                    acc_s = fmaf(s, sc, acc_s);
+            }
+            const uint32_t seg = m / SEGMENT_MACRO;
+            if (fin_r <= 8u * m + 8u) {  // row r ends in this macro-step
+                const float P = arbre8(acc);
+                if (voie == 0 && r < R) parts[uint64_t(r) * K + (seg - (r * B) / SEGMENT_BLOCS)] = P;
+                acc = acc_s;
+                acc_s = 0.0f;
+                ++r;
+                fin_r += B;
+            }
+            if ((m + 1u) % SEGMENT_MACRO == 0 || m + 1u == m1) {  // segment (or tile) ends
+                if (r * B < 8u * m + 8u && r < R) {
+                    const float P = arbre8(acc);
+                    if (voie == 0) parts[uint64_t(r) * K + (seg - (r * B) / SEGMENT_BLOCS)] = P;
+                }
+                acc = 0.0f;
+            }
+            bloc = bloc_s;
+            b += 8u;
+            if (b >= B) b -= B;
+        }
+        d.bilan(voie, hors_l, pointeur);
+        d.terminer();
+    }
+    verser_controle(controle, voie, hors_l, pointeur);
+}
+
+// ------------------------------------------------------------------ raw parts: row-centric
+
+__global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const Couche& c = a.c;
+    const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
+    uint32_t* controle = c.controle + 4u * i;
+    const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
+    const uint8_t* partie;
+    uint64_t taille;
+    Flux fe, fc;
+    const bool bon = B > 0 && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
+                     trouver_flux(partie, taille, SORTE_CODES_BRUTS, j, fc) && fe.produits == nblocs &&
+                     fe.longueur >= nblocs && fc.produits == 16u * nblocs && fc.longueur >= 16u * nblocs;
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    float* x2s = reinterpret_cast<float*>(dyn);
+    if (j < 2)
+        charger_x2(x2s, c.x, c.x_bf16, C);
+    else
+        charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    __syncthreads();
+    const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
+    auto x2f4 = [x2s4](uint32_t t) { return x2s4[t]; };
+    const uint32_t K = a.plan.K[j];
+    float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
+    for (uint32_t r = blockIdx.x * MOE_WARPS + (threadIdx.x >> 5); r < R; r += gridDim.x * MOE_WARPS)
+        ligne_segments(fc.p, fe.p, x2f4, r, B, voie, parts + uint64_t(r) * K);
+}
+
+// ------------------------------------------------------------------ 3. SwiGLU of the gate/up rows
+
+__device__ __forceinline__ float swiglu_f64(float g, float u) {
+    const double gv = fmin(double(g), 7.0);
+    const double uv = fmin(fmax(double(u), -7.0), 7.0);
+    return float(gv / (1.0 + exp(-1.702 * gv)) * (uv + 1.0));
+}
+
+__global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
+    __shared__ const float* biais[2];
+    const Couche& c = a.c;
+    const uint32_t i = blockIdx.y;
+    if (threadIdx.x < 2) {
+        const uint8_t* partie;
+        uint64_t taille;
+        Flux fb;
+        const uint32_t j = threadIdx.x;
+        biais[j] = (partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_BIAIS, j, fb) &&
+                    fb.longueur >= 4u * c.lignes[j])
+                       ? reinterpret_cast<const float*>(fb.p)
+                       : nullptr;
+    }
+    __syncthreads();
+    const uint32_t R = c.lignes[0], r = blockIdx.x * 256u + threadIdx.x;
+    if (r >= R) return;
+    float* h = reinterpret_cast<float*>(a.espace + a.plan.h) + uint64_t(i) * R;
+    if (biais[0] == nullptr || biais[1] == nullptr) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&c.controle[4u * i + CTL_FORMAT], 1u);
+        h[r] = 0.0f;
+        return;
+    }
+    const float* p0 = reinterpret_cast<const float*>(a.espace + a.plan.parts[0]) + (uint64_t(i) * R + r) * a.plan.K[0];
+    const float* p1 = reinterpret_cast<const float*>(a.espace + a.plan.parts[1]) + (uint64_t(i) * R + r) * a.plan.K[1];
+    const float gv = finir_ligne(p0, r, c.colonnes[0] / 32u) + biais[0][r];
+    const float uv = finir_ligne(p1, r, c.colonnes[1] / 32u) + biais[1][r];
+    h[r] = swiglu_f64(gv, uv);
+}
+
+// ------------------------------------------------------------------ 5. down rows, combine
+
+__global__ void __launch_bounds__(256) k_moe_combiner(ArgsMoe a) {
+    __shared__ const float* biais[8];
+    const Couche& c = a.c;
+    if (threadIdx.x < c.k) {
+        const uint8_t* partie;
+        uint64_t taille;
+        Flux fb;
+        biais[threadIdx.x] = (partie_de(c, threadIdx.x, partie, taille) && trouver_flux(partie, taille, SORTE_BIAIS, 2, fb) &&
+                              fb.longueur >= 4u * c.lignes[2])
+                                 ? reinterpret_cast<const float*>(fb.p)
+                                 : nullptr;
+    }
+    __syncthreads();
+    const uint32_t R = c.lignes[2], r = blockIdx.x * 256u + threadIdx.x;
+    if (r >= R) return;
+    const uint32_t B = c.colonnes[2] / 32u, K = a.plan.K[2];
+    const float* parts = reinterpret_cast<const float*>(a.espace + a.plan.parts[2]);
+    float s = 0.0f;
+    for (uint32_t i = 0; i < c.k; ++i) {
+        const float b = biais[i] != nullptr ? biais[i][r] : 0.0f;
+        const float si = finir_ligne(parts + (uint64_t(i) * R + r) * K, r, B) + b;
+        const float p = __fmul_rn(c.poids[i], si);
+        s = i == 0 ? p : __fadd_rn(s, p);
+    }
+    c.residu[r] = __fadd_rn(c.residu[r], s);
+}
+
+// ------------------------------------------------------------------ launcher
+
+cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEvent_t const* ev) {
+    auto marque = [&](int i) {
+        if (ev != nullptr && ev[i] != nullptr) cudaEventRecord(ev[i], flux);
+    };
+    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, c.k), 0};
+    const uint32_t nd = c.n_delta ? c.n_delta : 256u, nc = c.n_codes ? c.n_codes : 256u;
+    uint32_t td = 1, tc = 1;
+    for (int j = 0; j < 3; ++j) {
+        const uint64_t nb = uint64_t(c.lignes[j]) * (c.colonnes[j] / 32u);
+        td = std::max<uint32_t>(td, uint32_t(((nb + 127) / 128 + nd - 1) / nd));
+        tc = std::max<uint32_t>(tc, uint32_t(((16 * nb + 127) / 128 + nc - 1) / nc));
+    }
+    const uint32_t cmax = std::max(c.colonnes[0], c.colonnes[2]);
+    cudaError_t e;
+    marque(0);
+    if (!c.brut) {
+        k_moe_delta<<<dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.k), DELTA_WARPS * 32, 0, flux>>>(a);
+        const size_t smem = 3u * M * 4u + MOE_WARPS * ANNEAU_MOTS * 2u + 4u * cmax;
+        if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem))) != cudaSuccess) return e;
+        marque(1);
+        const dim3 grille((tc + MOE_WARPS - 1) / MOE_WARPS, 2, c.k);
+        k_moe_codes<<<grille, MOE_WARPS * 32, smem, flux>>>(a);
+        marque(2);
+        k_moe_swiglu<<<dim3((c.lignes[0] + 255) / 256, c.k, 1), 256, 0, flux>>>(a);
+        marque(3);
+        a.j0 = 2;
+        k_moe_codes<<<dim3(grille.x, 1, c.k), MOE_WARPS * 32, smem, flux>>>(a);
+        marque(4);
+    } else {
+        const size_t smem = 4u * cmax;
+        if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_brut), int(smem))) != cudaSuccess) return e;
+        const uint32_t rmax = std::max(c.lignes[0], c.lignes[2]);
+        const uint32_t gx = (rmax + MOE_WARPS - 1) / MOE_WARPS;
+        marque(1);
+        k_moe_brut<<<dim3(gx, 2, c.k), MOE_WARPS * 32, smem, flux>>>(a);
+        marque(2);
+        k_moe_swiglu<<<dim3((c.lignes[0] + 255) / 256, c.k, 1), 256, 0, flux>>>(a);
+        marque(3);
+        a.j0 = 2;
+        k_moe_brut<<<dim3(gx, 1, c.k), MOE_WARPS * 32, smem, flux>>>(a);
+        marque(4);
+    }
+    k_moe_combiner<<<(c.lignes[2] + 255) / 256, 256, 0, flux>>>(a);
+    marque(5);
+    return cudaGetLastError();
+}
+
+}  // namespace tb

@@ -1,0 +1,96 @@
+// troncons_b200 — y = W x + b on a decoded SoA slot (the reference's gemv_mxfp4 /
+// gemv_mxfp4_lot contract, trc-noyaux/noyaux/gemv.cuh:140-161), and the router's f32 GEMV
+// (gemv_f32, passe.cuh:104-130, 225-233).
+//
+// MXFP4: one warp per row (row-centric, no cross-warp reduction), the reduction order of
+// mxfp4.cuh, so a slot GEMV gives the bits of the fused path. x is read through L1 (the same
+// x for every row) and doubled in registers.
+// Router: one warp per row; lane l takes float4 chunks l, l+32, ... in an fmaf chain, then an
+// xor butterfly over 16, 8, 4, 2, 1; x may be f32 or bf16 (converted exactly).
+#include <cuda_bf16.h>
+
+#include "commun.cuh"
+#include "mxfp4.cuh"
+#include "noyaux.h"
+
+namespace tb {
+
+constexpr uint32_t GEMV_WARPS = 8;
+
+__device__ __forceinline__ void gemv_lignes(const uint8_t* __restrict__ mat, const float* __restrict__ x, float* __restrict__ y,
+                                            uint32_t R, uint32_t C, uint32_t ligne0, uint32_t pas) {
+    const uint32_t voie = threadIdx.x & 31u;
+    const uint32_t B = C / 32u;
+    const Disposition d = disposition_matrice(R, C);
+    const uint8_t* ech = mat + d.echelles;
+    const float* biais = reinterpret_cast<const float*>(mat + d.biais);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    auto x2f4 = [x4](uint32_t i) { return fois2(__ldg(x4 + i)); };
+    for (uint32_t r = ligne0; r < R; r += pas) {
+        const float t = ligne_segments(mat, ech, x2f4, r, B, voie, nullptr);
+        if (voie == 0) y[r] = t + biais[r];
+    }
+}
+
+__global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(const uint8_t* __restrict__ mat, const float* __restrict__ x,
+                                                          float* __restrict__ y, uint32_t R, uint32_t C) {
+    gemv_lignes(mat, x, y, R, C, blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5), gridDim.x * GEMV_WARPS);
+}
+
+__global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv_lot(const DescGemv* __restrict__ descs) {
+    const DescGemv d = descs[blockIdx.y];
+    if (d.colonnes % 32u != 0 || d.lignes == 0) return;
+    gemv_lignes(reinterpret_cast<const uint8_t*>(d.matrice), reinterpret_cast<const float*>(d.x), reinterpret_cast<float*>(d.y),
+                d.lignes, d.colonnes, blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5), gridDim.x * GEMV_WARPS);
+}
+
+__device__ __forceinline__ float4 charger_x4(const void* x, uint32_t x_bf16, uint32_t c) {
+    if (x_bf16) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(x) + c);
+        return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u), __uint_as_float(v.y << 16),
+                           __uint_as_float(v.y & 0xFFFF0000u));
+    }
+    return __ldg(reinterpret_cast<const float4*>(x) + c);
+}
+
+__global__ void __launch_bounds__(256) k_gemv_f32(const float* __restrict__ w, const void* __restrict__ x, uint32_t x_bf16,
+                                                  const float* __restrict__ biais, float* __restrict__ y, uint32_t R,
+                                                  uint32_t C) {
+    const uint32_t voie = threadIdx.x & 31u;
+    const uint32_t r = blockIdx.x * 8u + (threadIdx.x >> 5);
+    if (r >= R) return;
+    const uint32_t C4 = C / 4u;
+    const float4* w4 = reinterpret_cast<const float4*>(w) + uint64_t(r) * C4;
+    float acc = 0.0f;
+    for (uint32_t c = voie; c < C4; c += 32u) {
+        const float4 a = __ldcs(w4 + c);
+        const float4 b = charger_x4(x, x_bf16, c);
+        acc = fmaf(a.x, b.x, acc);
+        acc = fmaf(a.y, b.y, acc);
+        acc = fmaf(a.z, b.z, acc);
+        acc = fmaf(a.w, b.w, acc);
+    }
+#pragma unroll
+    for (int dd = 16; dd > 0; dd >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, dd);
+    if (voie == 0) y[r] = biais != nullptr ? acc + biais[r] : acc;
+}
+
+cudaError_t lancer_gemv(const void* matrice, const float* x, float* y, uint32_t R, uint32_t C, cudaStream_t flux) {
+    const uint32_t blocs = std::min<uint32_t>((R + GEMV_WARPS - 1) / GEMV_WARPS, 65535u);
+    k_gemv<<<blocs, GEMV_WARPS * 32, 0, flux>>>(static_cast<const uint8_t*>(matrice), x, y, R, C);
+    return cudaGetLastError();
+}
+
+cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_max, cudaStream_t flux) {
+    const uint32_t blocs = std::min<uint32_t>((lignes_max + GEMV_WARPS - 1) / GEMV_WARPS, 65535u);
+    k_gemv_lot<<<dim3(blocs, n, 1), GEMV_WARPS * 32, 0, flux>>>(descs);
+    return cudaGetLastError();
+}
+
+cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
+                            uint32_t C, cudaStream_t flux) {
+    k_gemv_f32<<<(R + 7) / 8, 256, 0, flux>>>(w, x, x_bf16, biais, y, R, C);
+    return cudaGetLastError();
+}
+
+}  // namespace tb

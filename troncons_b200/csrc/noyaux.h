@@ -1,0 +1,67 @@
+// troncons_b200 — internal declarations shared by the host entry points (abi.cpp) and the
+// kernel launchers (*.cu). Not a public header: the boundary is include/troncons_b200.h.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+namespace tb {
+
+struct Dims;
+
+// Device twins of the C-ABI batch descriptors (32 bytes each; abi.rs:16-53 of the reference).
+struct DescDecodage {
+    uint64_t partie, emplacement, luts, controle;
+};
+struct DescGemv {
+    uint64_t matrice, x, y;
+    uint32_t lignes, colonnes;
+};
+
+// The fused layer, as the kernels see it (mirror of trc_moe_couche).
+struct Couche {
+    const uint64_t* parties;
+    const uint64_t* parties_octets;
+    uint32_t experts, k;
+    const uint32_t* luts;
+    uint32_t lignes[3], colonnes[3];
+    const uint32_t* indices;
+    const float* poids;
+    const void* x;
+    uint32_t x_bf16, brut;
+    float* residu;
+    uint32_t* controle;
+    uint32_t n_delta, n_codes;
+};
+
+// Workspace of the fused layer (offsets in bytes from its 256-aligned base).
+struct Espace {
+    uint64_t ek[3];      // u16 (scale | class << 8) per block, per matrix, times k
+    uint64_t parts[3];   // f32 per-segment row partials [k][R][K] per matrix
+    uint64_t h;          // f32 [k][lignes[0]] SwiGLU output
+    uint64_t total;
+    uint32_t K[3];       // partial slots per row
+};
+Espace plan_espace(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t k);
+
+cudaError_t lancer_decodage(const DescDecodage* descs, uint32_t n, const void* partie, uint64_t taille, void* emplacement,
+                            const uint32_t* luts, const Dims& dims, uint32_t* controle, cudaStream_t flux);
+cudaError_t lancer_copier_brut(const void* partie, uint64_t taille, void* emplacement, const Dims& dims, uint32_t* controle,
+                               cudaStream_t flux);
+cudaError_t lancer_gemv(const void* matrice, const float* x, float* y, uint32_t R, uint32_t C, cudaStream_t flux);
+cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_max, cudaStream_t flux);
+cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
+                            uint32_t C, cudaStream_t flux);
+cudaError_t lancer_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids, uint32_t* boite,
+                        uint32_t sequence, cudaStream_t flux);
+cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, cudaStream_t flux);
+cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, const float* poids, uint32_t n, uint32_t d,
+                            cudaStream_t flux);
+cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEvent_t const* ev = nullptr);
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
+cudaError_t assurer_smem(const void* noyau, int octets);
+
+}  // namespace tb
