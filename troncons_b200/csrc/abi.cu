@@ -41,6 +41,12 @@ bool aligne(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p)
 // through another runtime instance, e.g. PyTorch's).
 cudaError_t sur_le_device_du_flux(void* flux) {
     if (flux == nullptr) return cudaSuccess;
+    // A stream under graph capture refuses the device query; launches into it are recorded on
+    // the device it was captured on, which an earlier eager call on the stream aligned.
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(static_cast<cudaStream_t>(flux), &capture) == cudaSuccess &&
+        capture != cudaStreamCaptureStatusNone)
+        return cudaSuccess;
     int d = -1, cur = -1;
     cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(flux), &d);
     if (e != cudaSuccess) return e;

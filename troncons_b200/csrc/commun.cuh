@@ -11,15 +11,22 @@
 // shared word stream: the word position is the tile pointer plus the number of lower lanes
 // that also pull (ballot + popc). B200 specifics:
 //   - the tile's words are staged in a per-warp shared-memory ring by asynchronous 16-byte
-//     copies (cp.async, zero-filled past the tile's end) issued three 512-byte chunks ahead,
-//     so a renormalisation is one shared-memory load, not a pair of shuffles and selects;
-//   - the LUTs live in shared memory; the output byte is inserted with one byte permute.
+//     copies (cp.async, zero-filled past the tile's end) issued three 512-byte chunks ahead;
+//   - every lane pre-loads the ring word at (pointer + lane) while its LUT entry is in flight,
+//     so a renormalisation costs one shuffle on the dependent chain;
+//   - the LUTs live in shared memory; the output byte is inserted with one byte permute;
+//   - the kernels software-pipeline their per-macro-step consumer (scales, GEMV) one macro-step
+//     behind the decode, branch-free, so it overlaps the decode chain's latency.
 // No floating-point atomics; integer counters only (the determinism rule of commun.cuh:11-12).
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 
 namespace tb {
+
+template <int K>
+using Etape = std::integral_constant<int, K>;
 
 constexpr uint32_t M = 4096u;     // 12-bit probabilities
 constexpr uint32_t L = 65536u;    // lower bound of the state
@@ -37,8 +44,11 @@ constexpr int CTL_HORS_L = 0;
 constexpr int CTL_FORMAT = 1;
 constexpr int CTL_POINTEUR = 2;
 
-// Per-warp word ring: 1024 words (2 KiB), refilled by chunks of 256 words (32 lanes x 16 B).
+// Per-warp word ring: 1024 words (2 KiB) refilled by chunks of 256 words (32 lanes x 16 B),
+// followed by a 64-word mirror of its first 64 words so that ring index + lane never wraps.
 constexpr uint32_t ANNEAU_MOTS = 1024u;
+constexpr uint32_t MIROIR_MOTS = 64u;
+constexpr uint32_t ANNEAU_ALLOC = ANNEAU_MOTS + MIROIR_MOTS;  // words allocated per warp
 constexpr uint32_t TRANCHE_MOTS = 256u;
 
 struct Dims {
@@ -138,6 +148,14 @@ __device__ inline bool lire_entete(const Flux& f, uint32_t besoin, EnteteRans& h
     return true;
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+
+// Waits until the previous kernel on the stream has completed and its writes are visible (a no-op
+// when the kernel was not launched with programmatic serialization).
+__device__ __forceinline__ void attendre_amont() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+// Lets the next kernel on the stream start its prologue.
+__device__ __forceinline__ void liberer_aval() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 // ------------------------------------------------------------------ async copies
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, uint32_t src_octets) {
@@ -150,46 +168,73 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+__device__ __forceinline__ uint32_t adresse_partagee(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+
 // ------------------------------------------------------------------ the warp decoder
 
 // One warp decoding one tile. All fields but `x` are warp-uniform.
+//
+// Sub-step (the dependent chain, measured ~87 ns on B200 with one warp per SM): the LUT entry
+// of the state; meanwhile every lane pre-loads the ring word at (pointer + its lane index);
+// y = f (x >> 12) + b; a ballot of the lanes with y < L; the lane that renormalises takes its
+// word from the lane whose index is its prefix count (one shuffle), merged by a byte permute.
 struct Decodeur {
     uint32_t x;            // rANS state of this lane
-    uint32_t ptr;          // next word index in the stream
-    uint32_t fin;          // end of the tile's words (debut[t+1], or W for the last tile)
-    uint32_t lim;          // words at or past `lim` read as 0: min(fin, W)
+    uint32_t pa;           // next word, as an aligned index (stream word index + dec)
+    uint32_t fin_a;        // end of the tile's words (debut[t+1], or W for the last), aligned
+    uint32_t lim;          // stream words at or past `lim` read as 0: min(fin, W)
     uint32_t dec;          // words between the 16-aligned base `ga` and mots[0]
-    uint32_t tranche;      // chunk (of 256 aligned words from ga) the pointer is in
+    uint32_t tranche;      // chunk (256 aligned words from ga) the pointer is in
     const uint8_t* ga;     // 16-aligned address at or below mots[0]
-    uint16_t* anneau;      // this warp's ring (ANNEAU_MOTS words, shared memory)
+    uint16_t* anneau;      // this warp's ring (ANNEAU_ALLOC words, shared memory)
+    uint32_t anneau_s;     // its shared-space address
     uint32_t masque_inf;   // lanes below this one
+    uint32_t voie;
 
     // Chunk c (aligned words [256c, 256c + 256)) into its ring slot; each lane copies 16 bytes,
-    // zero-filled past `lim`.
-    __device__ __forceinline__ void charger(uint32_t c, uint32_t voie) {
+    // zero-filled past `lim`. The chunk landing at slot 0 is also copied into the mirror.
+    __device__ __forceinline__ void charger(uint32_t c) {
         const uint32_t a0 = c * TRANCHE_MOTS + 8u * voie;   // aligned index of the lane's first word
         const int64_t i0 = int64_t(a0) - int64_t(dec);      // stream word index
         int64_t utiles = int64_t(lim) - i0;                 // words this lane may read
         utiles = utiles < 0 ? 0 : (utiles > 8 ? 8 : utiles);
         const uint8_t* src = utiles > 0 ? ga + 2ull * a0 : ga;
-        cp_async16(anneau + (a0 & (ANNEAU_MOTS - 1u)), src, uint32_t(2 * utiles));
+        const uint32_t fente = a0 & (ANNEAU_MOTS - 1u);
+        cp_async16(anneau + fente, src, uint32_t(2 * utiles));
+        if (fente < MIROIR_MOTS) cp_async16(anneau + ANNEAU_MOTS + fente, src, uint32_t(2 * utiles));
     }
 
-    __device__ __forceinline__ void debut(const EnteteRans& h, uint32_t t, uint32_t voie, uint16_t* ring) {
+    __device__ __forceinline__ void debut(const EnteteRans& h, uint32_t t, uint32_t v, uint16_t* ring) {
+        voie = v;
         anneau = ring;
+        anneau_s = adresse_partagee(ring);
         masque_inf = (1u << voie) - 1u;
         x = h.etats[t * VOIES + voie];
-        ptr = h.debut[t];
-        fin = (t + 1 < h.T) ? h.debut[t + 1] : h.W;
+        const uint32_t ptr = h.debut[t];
+        const uint32_t fin = (t + 1 < h.T) ? h.debut[t + 1] : h.W;
         lim = fin < h.W ? fin : h.W;
         const uintptr_t m = reinterpret_cast<uintptr_t>(h.mots);
         ga = reinterpret_cast<const uint8_t*>(m & ~uintptr_t(15));
         dec = uint32_t(m & 15u) >> 1;
-        tranche = (ptr + dec) / TRANCHE_MOTS;
+        pa = ptr + dec;
+        fin_a = fin + dec;
+        tranche = pa / TRANCHE_MOTS;
         __syncwarp();
 #pragma unroll
         for (uint32_t c = 0; c < 4; ++c) {
-            charger(tranche + c, voie);
+            charger(tranche + c);
             cp_async_commit();
         }
         cp_async_wait<2>();
@@ -199,50 +244,92 @@ struct Decodeur {
     // At the start of each macro-step: when the pointer entered a new chunk, refill the slot
     // of the chunk left behind with the chunk three ahead, and make sure the current and next
     // chunks (all this macro-step can read: at most 128 words) have landed.
-    __device__ __forceinline__ void avancer(uint32_t voie) {
-        const uint32_t c = (ptr + dec) / TRANCHE_MOTS;
+    __device__ __forceinline__ void avancer() {
+        const uint32_t c = pa / TRANCHE_MOTS;
         if (c != tranche) {
             tranche = c;
             __syncwarp();
-            charger(c + 3u, voie);
+            charger(c + 3u);
             cp_async_commit();
             cp_async_wait<2>();
             __syncwarp();
         }
     }
 
-    // One sub-step; returns the LUT entry (its low byte is the symbol).
-    __device__ __forceinline__ uint32_t pas(const uint32_t* __restrict__ lut) {
-        const uint32_t e = lut[x & (M - 1u)];
+    // One sub-step; `lut_s`: shared address of the table. Returns the LUT entry (its low byte
+    // is the symbol).
+    __device__ __forceinline__ uint32_t pas(uint32_t lut_s) {
+        const uint32_t e = lds32(lut_s + 4u * (x & (M - 1u)));
+        const uint32_t pre = lds16(anneau_s + 2u * ((pa & (ANNEAU_MOTS - 1u)) + voie));
         const uint32_t y = (((e >> 8) & 0xFFFu) + 1u) * (x >> 12) + (e >> 20);
         const bool besoin = y < L;
         const uint32_t vote = __ballot_sync(0xFFFFFFFFu, besoin);
-        const uint32_t pos = ptr + __popc(vote & masque_inf);
-        const uint32_t w = anneau[(pos + dec) & (ANNEAU_MOTS - 1u)];
-        x = besoin ? ((y << 16) | w) : y;
-        ptr += __popc(vote);
+        const uint32_t w = __shfl_sync(0xFFFFFFFFu, pre, __popc(vote & masque_inf));
+        x = besoin ? __byte_perm(w, y, 0x5410) : y;
+        pa += __popc(vote);
         return e;
     }
 
     // Four sub-steps: the lane's 32-bit output word (byte k = sub-step k).
-    __device__ __forceinline__ uint32_t macro(const uint32_t* __restrict__ lut) {
-        uint32_t m = pas(lut);
-        m = __byte_perm(m, pas(lut), 0x0040);
-        m = __byte_perm(m, pas(lut), 0x0410);
-        m = __byte_perm(m, pas(lut), 0x4210);
+    __device__ __forceinline__ uint32_t macro(uint32_t lut_s) {
+        uint32_t m = pas(lut_s);
+        m = __byte_perm(m, pas(lut_s), 0x0040);
+        m = __byte_perm(m, pas(lut_s), 0x0410);
+        m = __byte_perm(m, pas(lut_s), 0x4210);
+        return m;
+    }
+
+    // Four sub-steps, with the caller's independent work f(Etape<k>) placed after sub-step k:
+    // it fills the decode chain's latency instead of following it.
+    template <typename F>
+    __device__ __forceinline__ uint32_t macro(uint32_t lut_s, F&& f) {
+        uint32_t m = pas(lut_s);
+        f(Etape<0>{});
+        m = __byte_perm(m, pas(lut_s), 0x0040);
+        f(Etape<1>{});
+        m = __byte_perm(m, pas(lut_s), 0x0410);
+        f(Etape<2>{});
+        m = __byte_perm(m, pas(lut_s), 0x4210);
+        f(Etape<3>{});
         return m;
     }
 
     // End-of-tile integrity: lanes off L; the word pointer must end at the tile's end.
-    __device__ __forceinline__ void bilan(uint32_t voie, uint32_t& hors_l, uint32_t& pointeur) const {
+    __device__ __forceinline__ void bilan(uint32_t& hors_l, uint32_t& pointeur) const {
         hors_l += x != L ? 1u : 0u;
-        pointeur += (voie == 0 && ptr != fin) ? 1u : 0u;
+        pointeur += (voie == 0 && pa != fin_a) ? 1u : 0u;
     }
 
     // Drains the copies still in flight (the ring must not be written after the warp leaves).
     __device__ __forceinline__ void terminer() {
         cp_async_wait<0>();
         __syncwarp();
+    }
+};
+
+// Rows of the blocks a lane's DELTA word covers: word w = 32 m + lane carries delta of blocks
+// 4w .. 4w+3; the lane keeps the row and the position in the row of block 4w, advanced by 128
+// blocks per macro-step without division or branch (q = 128 / B, r = 128 % B precomputed).
+struct LignesDelta {
+    uint32_t ligne, reste, B, q, r;
+    __device__ __forceinline__ void debut(uint32_t b0, uint32_t B_) {
+        B = B_;
+        ligne = b0 / B;
+        reste = b0 - ligne * B;
+        q = 128u / B;
+        r = 128u - q * B;
+    }
+    // Row of block 4w + k (B >= 4: the four blocks span at most two rows).
+    __device__ __forceinline__ uint32_t rang(uint32_t k) const {
+        const uint32_t qk = reste + k;
+        return B >= 4u ? ligne + (qk >= B ? 1u : 0u) : ligne + qk / B;
+    }
+    __device__ __forceinline__ void avancer() {
+        reste += r;
+        ligne += q;
+        const bool c = reste >= B;
+        reste -= c ? B : 0u;
+        ligne += c ? 1u : 0u;
     }
 };
 

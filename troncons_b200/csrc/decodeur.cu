@@ -46,10 +46,30 @@ __device__ __forceinline__ void choisir_expert(const ArgsDecodage& a, const uint
 constexpr uint32_t ECH_WARPS = 4;
 constexpr uint32_t CODES_WARPS = 8;
 
+// Scales of the 4 blocks of a DELTA word: e = (med[r] + delta - 128) mod 256, to the slot.
+__device__ __forceinline__ void ecrire_echelles(uint8_t* ech, const uint8_t* med, uint32_t R, uint32_t nblocs,
+                                                uint32_t b0, uint32_t mot, const LignesDelta& lg) {
+    uint32_t sortie = 0;
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t rk = lg.rang(k);
+        const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
+        sortie |= ((mk + ((mot >> (8u * k)) & 255u) - 128u) & 255u) << (8u * k);
+    }
+    if (b0 + 3u < nblocs) {
+        *reinterpret_cast<uint32_t*>(ech + b0) = sortie;
+    } else {
+        for (uint32_t k = 0; k < 4; ++k)
+            if (b0 + k < nblocs) ech[b0 + k] = uint8_t(sortie >> (8u * k));
+    }
+}
+
 __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
     __shared__ uint32_t lut[M];
     __shared__ uint8_t med_s[8192];
-    __shared__ __align__(16) uint16_t anneaux[ECH_WARPS][ANNEAU_MOTS];
+    __shared__ __align__(16) uint16_t anneaux[ECH_WARPS][ANNEAU_ALLOC];
+    attendre_amont();  // first kernel of the decode: the part may come from the previous kernel
+    liberer_aval();
     const uint8_t* partie;
     uint64_t taille;
     uint8_t* emplacement;
@@ -86,7 +106,7 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
         med = med_s;
     }
     __syncthreads();
-
+    const uint32_t lut_s = adresse_partagee(lut);
     uint8_t* ech = mat + disp.echelles;
     const uint32_t nmacro = h.P / 128u;
     uint32_t hors_l = 0, pointeur = 0;
@@ -94,42 +114,34 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * ECH_WARPS) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
-        // Word w = 32 m + lane carries delta of blocks 4w .. 4w + 3.
+        // Word w = 32 m + lane carries delta of blocks 4w .. 4w + 3. The scales of macro-step m - 1
+        // are written while macro-step m decodes.
         uint32_t b0 = 4u * (m0 * 32u + voie);
-        uint32_t ligne = b0 / B, reste = b0 - ligne * B;
-        for (uint32_t m = m0; m < m1; ++m) {
-            d.avancer(voie);
-            const uint32_t mot = d.macro(lut);
+        LignesDelta lg;
+        lg.debut(b0, B);
+        d.avancer();
+        uint32_t mot_p = d.macro(lut_s);
+        for (uint32_t m = m0 + 1; m < m1; ++m) {
+            d.avancer();
             uint32_t sortie = 0;
-#pragma unroll
-            for (uint32_t k = 0; k < 4; ++k) {
-                uint32_t rk = ligne, qk = reste + k;
-                while (qk >= B) {
-                    qk -= B;
-                    ++rk;
-                }
+            const uint32_t mot = d.macro(lut_s, [&](auto k) {
+                constexpr int K = decltype(k)::value;  // block 4w + K of the previous word
+                const uint32_t rk = lg.rang(K);
                 const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
-                sortie |= ((mk + ((mot >> (8u * k)) & 255u) - 128u) & 255u) << (8u * k);
-            }
+                sortie |= ((mk + ((mot_p >> (8u * K)) & 255u) - 128u) & 255u) << (8u * K);
+            });
             if (b0 + 3u < nblocs) {
                 *reinterpret_cast<uint32_t*>(ech + b0) = sortie;
             } else {
                 for (uint32_t k = 0; k < 4; ++k)
                     if (b0 + k < nblocs) ech[b0 + k] = uint8_t(sortie >> (8u * k));
             }
+            mot_p = mot;
             b0 += 128u;
-            reste += 128u;
-            if (B >= 32u) {
-                while (reste >= B) {
-                    reste -= B;
-                    ++ligne;
-                }
-            } else {
-                ligne += reste / B;
-                reste %= B;
-            }
+            lg.avancer();
         }
-        d.bilan(voie, hors_l, pointeur);
+        ecrire_echelles(ech, med, R, nblocs, b0, mot_p, lg);
+        d.bilan(hors_l, pointeur);
         d.terminer();
     }
     verser_controle(controle, voie, hors_l, pointeur);
@@ -138,7 +150,7 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
 __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);                            // [3][M]
-    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);           // [8][ANNEAU_MOTS]
+    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);           // [8][ANNEAU_ALLOC]
     const uint8_t* partie;
     uint64_t taille;
     uint8_t* emplacement;
@@ -164,7 +176,10 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
         uint4* dst = reinterpret_cast<uint4*>(lut);
         for (uint32_t i = threadIdx.x; i < 3u * M / 4u; i += blockDim.x) dst[i] = src[i];
     }
+    attendre_amont();  // the scales come from k_echelles
+    liberer_aval();
     __syncthreads();
+    const uint32_t lut_s = adresse_partagee(lut);
     const Disposition disp = disposition(a.dims, j);
     uint8_t* mat = emplacement + disp.base;
     uint32_t* codes = reinterpret_cast<uint32_t*>(mat);
@@ -175,34 +190,43 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
     uint32_t hors_l = 0, pointeur = 0;
     Decodeur d;
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * CODES_WARPS) {
-        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_MOTS);
+        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_ALLOC);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         // Word w = 32 m + lane belongs to block w / 4 = 8 m + lane / 4; its class needs the
-        // block's scale and its row's median, fetched one macro-step ahead.
+        // block's scale and its row's median, fetched two macro-steps ahead.
         uint32_t bloc = (m0 * 32u + voie) >> 2;
+        const uint32_t q8 = 8u / B, r8 = 8u - q8 * B;  // advance of 8 blocks in rows
         uint32_t ligne = bloc / B, reste = bloc - ligne * B;
-        bool valide = bloc < nblocs;
-        uint32_t e_s = valide ? __ldg(ech + bloc) : 0u;
-        uint32_t m_s = valide ? __ldg(med + ligne) : 0u;
+        auto avancer_ligne = [&](uint32_t& lg, uint32_t& rs) {
+            rs += r8;
+            lg += q8;
+            const bool c = rs >= B;
+            rs -= c ? B : 0u;
+            lg += c ? 1u : 0u;
+        };
+        uint32_t l1 = ligne, r1 = reste;
+        avancer_ligne(l1, r1);
+        const bool v0 = bloc < nblocs, v1 = m0 + 1 < m1 && bloc + 8u < nblocs;
+        uint32_t e0 = v0 ? __ldg(ech + bloc) : 0u, md0 = v0 ? __ldg(med + ligne) : 0u;
+        uint32_t e1 = v1 ? __ldg(ech + bloc + 8u) : 0u, md1 = v1 ? __ldg(med + l1) : 0u;
+        uint32_t l2 = l1, r2 = r1;
+        avancer_ligne(l2, r2);
         for (uint32_t m = m0; m < m1; ++m) {
-            const uint32_t ctx = valide ? classe_echelle(e_s, m_s) : 0u;
-            bloc += 8u;
-            reste += 8u;
-            while (reste >= B) {
-                reste -= B;
-                ++ligne;
-            }
-            valide = (m + 1u < m1) && bloc < nblocs;
-            if (valide) {
-                e_s = __ldg(ech + bloc);
-                m_s = __ldg(med + ligne);
-            }
-            d.avancer(voie);
-            const uint32_t mot = d.macro(lut + ctx * M);
+            const uint32_t ctx = bloc < nblocs ? classe_echelle(e0, md0) : 0u;
+            const bool v2 = m + 2u < m1 && bloc + 16u < nblocs;
+            const uint32_t e2 = v2 ? __ldg(ech + bloc + 16u) : 0u, md2 = v2 ? __ldg(med + l2) : 0u;
+            d.avancer();
+            const uint32_t mot = d.macro(lut_s + ctx * (M * 4u));
             const uint32_t w = m * 32u + voie;
             if (w < mots_utiles) codes[w] = mot;
+            bloc += 8u;
+            e0 = e1;
+            md0 = md1;
+            e1 = e2;
+            md1 = md2;
+            avancer_ligne(l2, r2);
         }
-        d.bilan(voie, hors_l, pointeur);
+        d.bilan(hors_l, pointeur);
         d.terminer();
     }
     verser_controle(controle, voie, hors_l, pointeur);
@@ -211,6 +235,8 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
 // Raw part (file flag bit 2): ECHELLES_BRUTES_j, CODES_BRUTS_j, BIAIS_j copied into the slot.
 __global__ void __launch_bounds__(256) k_copier_brut(const uint8_t* partie, uint64_t taille, uint8_t* emplacement, Dims dims,
                                                       uint32_t* controle) {
+    attendre_amont();
+    liberer_aval();
     const uint32_t j = blockIdx.y;
     const uint32_t R = choisir(dims.lignes, j), C = choisir(dims.colonnes, j);
     const uint32_t B = C / 32u, nblocs = R * B;
@@ -255,12 +281,11 @@ cudaError_t lancer_decodage(const DescDecodage* descs, uint32_t n, const void* p
     }
     ArgsDecodage a{descs, static_cast<const uint8_t*>(partie), taille, static_cast<uint8_t*>(emplacement), luts, controle, dims};
     const uint32_t z = descs ? n : 1u;
-    k_echelles<<<dim3((td + ECH_WARPS - 1) / ECH_WARPS, 3, z), ECH_WARPS * 32, 0, flux>>>(a);
-    const size_t smem = 3u * M * 4u + CODES_WARPS * ANNEAU_MOTS * 2u;
-    const cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_codes), int(smem));
+    cudaError_t e = lancer_pdl(k_echelles, dim3((td + ECH_WARPS - 1) / ECH_WARPS, 3, z), dim3(ECH_WARPS * 32), 0, flux, a);
     if (e != cudaSuccess) return e;
-    k_codes<<<dim3((tc + CODES_WARPS - 1) / CODES_WARPS, 3, z), CODES_WARPS * 32, smem, flux>>>(a);
-    return cudaGetLastError();
+    const size_t smem = 3u * M * 4u + CODES_WARPS * ANNEAU_ALLOC * 2u;
+    if ((e = assurer_smem(reinterpret_cast<const void*>(k_codes), int(smem))) != cudaSuccess) return e;
+    return lancer_pdl(k_codes, dim3((tc + CODES_WARPS - 1) / CODES_WARPS, 3, z), dim3(CODES_WARPS * 32), smem, flux, a);
 }
 
 cudaError_t lancer_copier_brut(const void* partie, uint64_t taille, void* emplacement, const Dims& dims, uint32_t* controle,
@@ -268,9 +293,8 @@ cudaError_t lancer_copier_brut(const void* partie, uint64_t taille, void* emplac
     uint64_t n = 1;
     for (int j = 0; j < 3; ++j) n = std::max<uint64_t>(n, uint64_t(dims.lignes[j]) * (dims.colonnes[j] / 32u));
     const uint32_t g = uint32_t(std::min<uint64_t>(std::max<uint64_t>((n + 255) / 256, 1), 296));
-    k_copier_brut<<<dim3(g, 3, 1), 256, 0, flux>>>(static_cast<const uint8_t*>(partie), taille,
-                                                    static_cast<uint8_t*>(emplacement), dims, controle);
-    return cudaGetLastError();
+    return lancer_pdl(k_copier_brut, dim3(g, 3, 1), dim3(256), 0, flux, static_cast<const uint8_t*>(partie), taille,
+                      static_cast<uint8_t*>(emplacement), dims, controle);
 }
 
 }  // namespace tb

@@ -64,10 +64,32 @@ constexpr uint32_t MOE_WARPS = 4;
 
 // ------------------------------------------------------------------ 1. DELTA -> scales, classes
 
+// (scale | class << 8) of the 4 blocks of a DELTA word, into the workspace.
+__device__ __forceinline__ void ecrire_ek(uint16_t* ek, const uint8_t* med, uint32_t R, uint32_t nblocs, uint32_t b0,
+                                          uint32_t mot, const LignesDelta& lg) {
+    uint32_t v[4];
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k) {
+        const uint32_t rk = lg.rang(k);
+        const uint32_t dk = (mot >> (8u * k)) & 255u;
+        const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
+        const uint32_t kap = dk < 128u ? 0u : (dk == 128u ? 1u : 2u);
+        v[k] = ((mk + dk - 128u) & 255u) | (kap << 8);
+    }
+    if (b0 + 3u < nblocs) {
+        *reinterpret_cast<uint2*>(ek + b0) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
+    } else {
+        for (uint32_t k = 0; k < 4; ++k)
+            if (b0 + k < nblocs) ek[b0 + k] = uint16_t(v[k]);
+    }
+}
+
 __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     __shared__ uint32_t lut[M];
     __shared__ uint8_t med_s[8192];
-    __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_MOTS];
+    __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_ALLOC];
+    attendre_amont();  // first kernel of the layer: every input may come from the previous kernel
+    liberer_aval();
     const Couche& c = a.c;
     const uint32_t j = blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
     uint32_t* controle = c.controle + 4u * i;
@@ -93,6 +115,7 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
         med = med_s;
     }
     __syncthreads();
+    const uint32_t lut_s = adresse_partagee(lut);
     uint16_t* ek = reinterpret_cast<uint16_t*>(a.espace + a.plan.ek[j]) + uint64_t(i) * nblocs;
     const uint32_t nmacro = h.P / 128u;
     uint32_t hors_l = 0, pointeur = 0;
@@ -101,42 +124,32 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         uint32_t b0 = 4u * (m0 * 32u + voie);
-        uint32_t ligne = b0 / B, reste = b0 - ligne * B;
-        for (uint32_t m = m0; m < m1; ++m) {
-            d.avancer(voie);
-            const uint32_t mot = d.macro(lut);
+        LignesDelta lg;
+        lg.debut(b0, B);
+        d.avancer();
+        uint32_t mot_p = d.macro(lut_s);
+        for (uint32_t m = m0 + 1; m < m1; ++m) {
+            d.avancer();
             uint32_t v[4];
-#pragma unroll
-            for (uint32_t k = 0; k < 4; ++k) {
-                uint32_t rk = ligne, qk = reste + k;
-                while (qk >= B) {
-                    qk -= B;
-                    ++rk;
-                }
-                const uint32_t dk = (mot >> (8u * k)) & 255u;
+            const uint32_t mot = d.macro(lut_s, [&](auto k) {
+                constexpr int K = decltype(k)::value;  // block 4w + K of the previous word
+                const uint32_t rk = lg.rang(K);
+                const uint32_t dk = (mot_p >> (8u * K)) & 255u;
                 const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
-                const uint32_t kap = dk < 128u ? 0u : (dk == 128u ? 1u : 2u);
-                v[k] = ((mk + dk - 128u) & 255u) | (kap << 8);
-            }
+                v[K] = ((mk + dk - 128u) & 255u) | ((dk < 128u ? 0u : (dk == 128u ? 1u : 2u)) << 8);
+            });
             if (b0 + 3u < nblocs) {
                 *reinterpret_cast<uint2*>(ek + b0) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
             } else {
                 for (uint32_t k = 0; k < 4; ++k)
                     if (b0 + k < nblocs) ek[b0 + k] = uint16_t(v[k]);
             }
+            mot_p = mot;
             b0 += 128u;
-            reste += 128u;
-            if (B >= 32u) {
-                while (reste >= B) {
-                    reste -= B;
-                    ++ligne;
-                }
-            } else {
-                ligne += reste / B;
-                reste %= B;
-            }
+            lg.avancer();
         }
-        d.bilan(voie, hors_l, pointeur);
+        ecrire_ek(ek, med, R, nblocs, b0, mot_p, lg);
+        d.bilan(hors_l, pointeur);
         d.terminer();
     }
     verser_controle(controle, voie, hors_l, pointeur);
@@ -155,6 +168,87 @@ __device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t b
 }
 
 // ------------------------------------------------------------------ 2/4. CODES_CTX decoded into the GEMV
+
+// The GEMV of one decoded macro-step (8 blocks, one word per lane) into the row partials: the
+// block's sum (quad tree), scaled and accumulated on the current row or the next; rows closed
+// where they end, and the row in progress closed at the segment's (or the tile's) end.
+struct GemvTuile {
+    float acc, acc_s;     // current row r, next row
+    uint32_t r, fin_r;    // warp-uniform: current row, first block of the next row
+    uint32_t R, B, K, voie, q;
+    float* parts;
+    const float4* x2s4;
+
+    __device__ __forceinline__ void debut(uint32_t m0) {
+        acc = 0.0f;
+        acc_s = 0.0f;
+        r = (8u * m0) / B;
+        fin_r = (r + 1u) * B;
+    }
+
+    // Branch-free part: the block's scaled contribution (overlaps the next decode).
+    __device__ __forceinline__ void accumuler(uint32_t mot, uint32_t bloc, uint32_t b, uint32_t ekv, bool valide) {
+        float s = produit_quad(mot, x2s4[8u * b + q], x2s4[8u * b + 4u + q]);
+        s = somme_quad(s);
+        const float sc = echelle_e8m0(ekv & 255u);
+        const bool cour = bloc < fin_r;
+        acc = (valide && cour) ? fmaf(s, sc, acc) : acc;
+        acc_s = (valide && !cour) ? fmaf(s, sc, acc_s) : acc_s;
+    }
+
+    // The same, in four stages to interleave with the four sub-steps of the next decode.
+    struct Etapes {
+        float lo[4], hi[4];
+        float4 xa, xb;
+        float p;
+    };
+    template <int K>
+    __device__ __forceinline__ void etape(Etapes& e, uint32_t mot, uint32_t bloc, uint32_t b, uint32_t ekv, bool valide) {
+        if constexpr (K == 0) {
+            e.xa = x2s4[8u * b + q];
+            e.xb = x2s4[8u * b + 4u + q];
+            e2m1_mot(mot, e.lo, e.hi);
+        } else if constexpr (K == 1) {
+            float p = 0.0f;
+            p = fmaf(e.lo[0], e.xa.x, p);
+            p = fmaf(e.hi[0], e.xb.x, p);
+            p = fmaf(e.lo[1], e.xa.y, p);
+            p = fmaf(e.hi[1], e.xb.y, p);
+            p = fmaf(e.lo[2], e.xa.z, p);
+            p = fmaf(e.hi[2], e.xb.z, p);
+            p = fmaf(e.lo[3], e.xa.w, p);
+            p = fmaf(e.hi[3], e.xb.w, p);
+            e.p = p;
+        } else if constexpr (K == 2) {
+            e.p = somme_quad(e.p);
+        } else {
+            const float sc = echelle_e8m0(ekv & 255u);
+            const bool cour = bloc < fin_r;
+            acc = (valide && cour) ? fmaf(e.p, sc, acc) : acc;
+            acc_s = (valide && !cour) ? fmaf(e.p, sc, acc_s) : acc_s;
+        }
+    }
+
+    // Row and segment closing after macro-step m (warp-uniform branches).
+    __device__ __forceinline__ void fermer(uint32_t m, uint32_t m1) {
+        const uint32_t seg = m / SEGMENT_MACRO;
+        if (fin_r <= 8u * m + 8u) {  // row r ends in this macro-step
+            const float P = arbre8(acc);
+            if (voie == 0 && r < R) parts[uint64_t(r) * K + (seg - (r * B) / SEGMENT_BLOCS)] = P;
+            acc = acc_s;
+            acc_s = 0.0f;
+            ++r;
+            fin_r += B;
+        }
+        if ((m + 1u) % SEGMENT_MACRO == 0 || m + 1u == m1) {  // segment (or tile) ends
+            if (r * B < 8u * m + 8u && r < R) {
+                const float P = arbre8(acc);
+                if (voie == 0) parts[uint64_t(r) * K + (seg - (r * B) / SEGMENT_BLOCS)] = P;
+            }
+            acc = 0.0f;
+        }
+    }
+};
 
 __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
@@ -175,74 +269,82 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
     const uint32_t warp0 = blockIdx.x * MOE_WARPS;
     if (warp0 >= h.T) return;
     uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);                                  // [3][M]
-    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);                 // [W][ANNEAU_MOTS]
-    float* x2s = reinterpret_cast<float*>(dyn + 3u * M * 4u + MOE_WARPS * ANNEAU_MOTS * 2u);
+    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);                 // [W][ANNEAU_ALLOC]
+    float* x2s = reinterpret_cast<float*>(dyn + 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u);
     {
         const uint4* src = reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M);
         uint4* dst = reinterpret_cast<uint4*>(lut);
         for (uint32_t t = threadIdx.x; t < 3u * M / 4u; t += blockDim.x) dst[t] = src[t];
     }
-    if (j < 2)
-        charger_x2(x2s, c.x, c.x_bf16, C);
-    else
-        charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    if (j < 2) charger_x2(x2s, c.x, c.x_bf16, C);
+    // Everything above reads inputs the layer's first kernel waited for; the scales and classes
+    // (and h for the down projection) come from the previous kernel.
+    attendre_amont();
+    liberer_aval();
+    if (j == 2) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
-    const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
+    const uint32_t lut_s = adresse_partagee(lut);
     const uint16_t* __restrict__ ek = reinterpret_cast<const uint16_t*>(a.espace + a.plan.ek[j]) + uint64_t(i) * nblocs;
-    const uint32_t K = a.plan.K[j];
-    float* __restrict__ parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
+    GemvTuile gv;
+    gv.R = R;
+    gv.B = B;
+    gv.K = a.plan.K[j];
+    gv.voie = voie;
+    gv.q = voie & 3u;
+    gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
+    gv.x2s4 = reinterpret_cast<const float4*>(x2s);
     const uint32_t nmacro = h.P / 128u;
-    const uint32_t q = voie & 3u, g = voie >> 2;
+    const uint32_t g = voie >> 2;
     uint32_t hors_l = 0, pointeur = 0;
     Decodeur d;
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * MOE_WARPS) {
-        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_MOTS);
+        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_ALLOC);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
-        // This lane's block (8 m + g) and its column block b; the warp's current row r and the
-        // first block of the next row.
+        gv.debut(m0);
+        // This lane's block at macro-step m is 8 m + g, column block b; (scale | class) read two
+        // macro-steps ahead; the GEMV of macro-step m - 1 runs while m decodes.
         uint32_t bloc = 8u * m0 + g;
         uint32_t b = bloc % B;
-        uint32_t r = (8u * m0) / B;
-        uint32_t fin_r = (r + 1u) * B;
-        float acc = 0.0f, acc_s = 0.0f;
-        uint32_t ekv = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
-        for (uint32_t m = m0; m < m1; ++m) {
-            const bool valide = bloc < nblocs;
-            const uint32_t ctx = valide ? (ekv >> 8) : 0u;
-            const float sc = echelle_e8m0(ekv & 255u);
-            const uint32_t bloc_s = bloc + 8u;
-            ekv = (m + 1u < m1 && bloc_s < nblocs) ? uint32_t(__ldg(ek + bloc_s)) : 0u;
-            d.avancer(voie);
-            const uint32_t mot = d.macro(lut + ctx * M);
-            float s = produit_quad(mot, x2s4[8u * b + q], x2s4[8u * b + 4u + q]);
-            s = somme_quad(s);
-            if (valide) {
-                if (bloc < fin_r)
-                    acc = fmaf(s, sc, acc);
-                else
-                    acc_s = fmaf(s, sc, acc_s);
-            }
-            const uint32_t seg = m / SEGMENT_MACRO;
-            if (fin_r <= 8u * m + 8u) {  // row r ends in this macro-step
-                const float P = arbre8(acc);
-                if (voie == 0 && r < R) parts[uint64_t(r) * K + (seg - (r * B) / SEGMENT_BLOCS)] = P;
-                acc = acc_s;
-                acc_s = 0.0f;
-                ++r;
-                fin_r += B;
-            }
-            if ((m + 1u) % SEGMENT_MACRO == 0 || m + 1u == m1) {  // segment (or tile) ends
-                if (r * B < 8u * m + 8u && r < R) {
-                    const float P = arbre8(acc);
-                    if (voie == 0) parts[uint64_t(r) * K + (seg - (r * B) / SEGMENT_BLOCS)] = P;
-                }
-                acc = 0.0f;
-            }
-            bloc = bloc_s;
+        uint32_t ek0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
+        uint32_t ek1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
+        uint32_t mot_p, bloc_p, b_p, ek_p;
+        {
+            const uint32_t ctx = bloc < nblocs ? (ek0 >> 8) : 0u;
+            const uint32_t ek2 = (m0 + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
+            d.avancer();
+            mot_p = d.macro(lut_s + ctx * (M * 4u));
+            bloc_p = bloc;
+            b_p = b;
+            ek_p = ek0;
+            bloc += 8u;
             b += 8u;
-            if (b >= B) b -= B;
+            b -= b >= B ? B : 0u;
+            ek0 = ek1;
+            ek1 = ek2;
         }
-        d.bilan(voie, hors_l, pointeur);
+        for (uint32_t m = m0 + 1; m < m1; ++m) {
+            const uint32_t ctx = bloc < nblocs ? (ek0 >> 8) : 0u;
+            const uint32_t ek2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
+            d.avancer();
+            GemvTuile::Etapes et;
+            const bool valide_p = bloc_p < nblocs;
+            const uint32_t mot = d.macro(lut_s + ctx * (M * 4u), [&](auto k) {
+                gv.etape<decltype(k)::value>(et, mot_p, bloc_p, b_p, ek_p, valide_p);
+            });
+            gv.fermer(m - 1u, m1);
+            mot_p = mot;
+            bloc_p = bloc;
+            b_p = b;
+            ek_p = ek0;
+            bloc += 8u;
+            b += 8u;
+            b -= b >= B ? B : 0u;
+            ek0 = ek1;
+            ek1 = ek2;
+        }
+        gv.accumuler(mot_p, bloc_p, b_p, ek_p, bloc_p < nblocs);
+        gv.fermer(m1 - 1u, m1);
+        d.bilan(hors_l, pointeur);
         d.terminer();
     }
     verser_controle(controle, voie, hors_l, pointeur);
@@ -252,6 +354,8 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
 
 __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
+    attendre_amont();
+    liberer_aval();
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
     uint32_t* controle = c.controle + 4u * i;
@@ -303,6 +407,8 @@ __global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
                        : nullptr;
     }
     __syncthreads();
+    attendre_amont();
+    liberer_aval();
     const uint32_t R = c.lignes[0], r = blockIdx.x * 256u + threadIdx.x;
     if (r >= R) return;
     float* h = reinterpret_cast<float*>(a.espace + a.plan.h) + uint64_t(i) * R;
@@ -333,6 +439,8 @@ __global__ void __launch_bounds__(256) k_moe_combiner(ArgsMoe a) {
                                  : nullptr;
     }
     __syncthreads();
+    attendre_amont();
+    liberer_aval();
     const uint32_t R = c.lignes[2], r = blockIdx.x * 256u + threadIdx.x;
     if (r >= R) return;
     const uint32_t B = c.colonnes[2] / 32u, K = a.plan.K[2];
@@ -365,17 +473,21 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
     cudaError_t e;
     marque(0);
     if (!c.brut) {
-        k_moe_delta<<<dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.k), DELTA_WARPS * 32, 0, flux>>>(a);
-        const size_t smem = 3u * M * 4u + MOE_WARPS * ANNEAU_MOTS * 2u + 4u * cmax;
+        if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.k), dim3(DELTA_WARPS * 32), 0,
+                            flux, a)) != cudaSuccess)
+            return e;
+        const size_t smem = 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u + 4u * cmax;
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem))) != cudaSuccess) return e;
         marque(1);
         const dim3 grille((tc + MOE_WARPS - 1) / MOE_WARPS, 2, c.k);
-        k_moe_codes<<<grille, MOE_WARPS * 32, smem, flux>>>(a);
+        if ((e = lancer_pdl(k_moe_codes, grille, dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
         marque(2);
-        k_moe_swiglu<<<dim3((c.lignes[0] + 255) / 256, c.k, 1), 256, 0, flux>>>(a);
+        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, c.k, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+            return e;
         marque(3);
         a.j0 = 2;
-        k_moe_codes<<<dim3(grille.x, 1, c.k), MOE_WARPS * 32, smem, flux>>>(a);
+        if ((e = lancer_pdl(k_moe_codes, dim3(grille.x, 1, c.k), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess)
+            return e;
         marque(4);
     } else {
         const size_t smem = 4u * cmax;
@@ -383,15 +495,16 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
         const uint32_t rmax = std::max(c.lignes[0], c.lignes[2]);
         const uint32_t gx = (rmax + MOE_WARPS - 1) / MOE_WARPS;
         marque(1);
-        k_moe_brut<<<dim3(gx, 2, c.k), MOE_WARPS * 32, smem, flux>>>(a);
+        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 2, c.k), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
         marque(2);
-        k_moe_swiglu<<<dim3((c.lignes[0] + 255) / 256, c.k, 1), 256, 0, flux>>>(a);
+        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, c.k, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+            return e;
         marque(3);
         a.j0 = 2;
-        k_moe_brut<<<dim3(gx, 1, c.k), MOE_WARPS * 32, smem, flux>>>(a);
+        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 1, c.k), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
         marque(4);
     }
-    k_moe_combiner<<<(c.lignes[2] + 255) / 256, 256, 0, flux>>>(a);
+    if ((e = lancer_pdl(k_moe_combiner, dim3((c.lignes[2] + 255) / 256), dim3(256), 0, flux, a)) != cudaSuccess) return e;
     marque(5);
     return cudaGetLastError();
 }

@@ -34,10 +34,14 @@ __device__ __forceinline__ void gemv_lignes(const uint8_t* __restrict__ mat, con
 
 __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(const uint8_t* __restrict__ mat, const float* __restrict__ x,
                                                           float* __restrict__ y, uint32_t R, uint32_t C) {
+    attendre_amont();
+    liberer_aval();
     gemv_lignes(mat, x, y, R, C, blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5), gridDim.x * GEMV_WARPS);
 }
 
 __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv_lot(const DescGemv* __restrict__ descs) {
+    attendre_amont();
+    liberer_aval();
     const DescGemv d = descs[blockIdx.y];
     if (d.colonnes % 32u != 0 || d.lignes == 0) return;
     gemv_lignes(reinterpret_cast<const uint8_t*>(d.matrice), reinterpret_cast<const float*>(d.x), reinterpret_cast<float*>(d.y),
@@ -56,12 +60,15 @@ __device__ __forceinline__ float4 charger_x4(const void* x, uint32_t x_bf16, uin
 __global__ void __launch_bounds__(256) k_gemv_f32(const float* __restrict__ w, const void* __restrict__ x, uint32_t x_bf16,
                                                   const float* __restrict__ biais, float* __restrict__ y, uint32_t R,
                                                   uint32_t C) {
+    attendre_amont();
+    liberer_aval();
     const uint32_t voie = threadIdx.x & 31u;
     const uint32_t r = blockIdx.x * 8u + (threadIdx.x >> 5);
     if (r >= R) return;
     const uint32_t C4 = C / 4u;
     const float4* w4 = reinterpret_cast<const float4*>(w) + uint64_t(r) * C4;
     float acc = 0.0f;
+#pragma unroll 8
     for (uint32_t c = voie; c < C4; c += 32u) {
         const float4 a = __ldcs(w4 + c);
         const float4 b = charger_x4(x, x_bf16, c);
@@ -77,20 +84,17 @@ __global__ void __launch_bounds__(256) k_gemv_f32(const float* __restrict__ w, c
 
 cudaError_t lancer_gemv(const void* matrice, const float* x, float* y, uint32_t R, uint32_t C, cudaStream_t flux) {
     const uint32_t blocs = std::min<uint32_t>((R + GEMV_WARPS - 1) / GEMV_WARPS, 65535u);
-    k_gemv<<<blocs, GEMV_WARPS * 32, 0, flux>>>(static_cast<const uint8_t*>(matrice), x, y, R, C);
-    return cudaGetLastError();
+    return lancer_pdl(k_gemv, dim3(blocs), dim3(GEMV_WARPS * 32), 0, flux, static_cast<const uint8_t*>(matrice), x, y, R, C);
 }
 
 cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_max, cudaStream_t flux) {
     const uint32_t blocs = std::min<uint32_t>((lignes_max + GEMV_WARPS - 1) / GEMV_WARPS, 65535u);
-    k_gemv_lot<<<dim3(blocs, n, 1), GEMV_WARPS * 32, 0, flux>>>(descs);
-    return cudaGetLastError();
+    return lancer_pdl(k_gemv_lot, dim3(blocs, n, 1), dim3(GEMV_WARPS * 32), 0, flux, descs);
 }
 
 cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
                             uint32_t C, cudaStream_t flux) {
-    k_gemv_f32<<<(R + 7) / 8, 256, 0, flux>>>(w, x, x_bf16, biais, y, R, C);
-    return cudaGetLastError();
+    return lancer_pdl(k_gemv_f32, dim3((R + 7) / 8), dim3(256), 0, flux, w, x, x_bf16, biais, y, R, C);
 }
 
 }  // namespace tb

@@ -91,7 +91,10 @@ __device__ __forceinline__ float4 fois2(float4 v) {
 // Segment partials of row r, row-centric: one warp walks the row's macro-steps (blocks 8m..8m+7,
 // quad g = lane / 4 on block 8m + g), so every lane of a quad holds the block's s. `x2f4(i)`
 // gives float4 i of 2x. When `parts` is given, lane 0 writes P of the row's k-th segment to
-// parts[k]. Returns the fold of the partials (without bias).
+// parts[k]. Returns the fold of the partials (without bias). The row's code words and scales are
+// loaded up to 16 macro-steps at a time before any is used (memory-level parallelism).
+constexpr uint32_t LIGNE_LOT = 16u;
+
 template <typename X2>
 __device__ __forceinline__ float ligne_segments(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ ech,
                                                 X2 x2f4, uint32_t r, uint32_t B, uint32_t voie, float* __restrict__ parts) {
@@ -101,35 +104,34 @@ __device__ __forceinline__ float ligne_segments(const uint8_t* __restrict__ code
     float acc = 0.0f, total = 0.0f;
     uint64_t seg = ma / SEGMENT_MACRO;
     uint32_t k = 0;
-    // The next macro-step's loads are issued before the current one is reduced.
-    uint64_t beta = 8u * ma + g;
-    bool valide = beta >= b0 && beta < b1;
-    uint32_t mot = valide ? __ldg(reinterpret_cast<const uint32_t*>(codes + 16u * beta) + q) : 0u;
-    uint32_t e = valide ? uint32_t(__ldg(ech + beta)) : 0u;
-    for (uint64_t m = ma; m <= mb; ++m) {
-        if (m / SEGMENT_MACRO != seg) {
-            const float P = arbre8(acc);
-            if (parts != nullptr && voie == 0) parts[k] = P;
-            total = k == 0 ? P : total + P;
-            ++k;
-            acc = 0.0f;
-            seg = m / SEGMENT_MACRO;
+    for (uint64_t mc = ma; mc <= mb; mc += LIGNE_LOT) {
+        uint32_t mots[LIGNE_LOT], es[LIGNE_LOT];
+#pragma unroll
+        for (uint32_t i = 0; i < LIGNE_LOT; ++i) {
+            const uint64_t beta = 8u * (mc + i) + g;
+            const bool v = mc + i <= mb && beta >= b0 && beta < b1;
+            mots[i] = v ? __ldg(reinterpret_cast<const uint32_t*>(codes + 16u * beta) + q) : 0u;
+            es[i] = v ? uint32_t(__ldg(ech + beta)) : 0u;
         }
-        const uint64_t beta_s = beta + 8u;
-        const bool valide_s = m < mb && beta_s >= b0 && beta_s < b1;
-        const uint32_t mot_s = valide_s ? __ldg(reinterpret_cast<const uint32_t*>(codes + 16u * beta_s) + q) : 0u;
-        const uint32_t e_s = valide_s ? uint32_t(__ldg(ech + beta_s)) : 0u;
-        float s = 0.0f;
-        if (valide) {
-            const uint32_t bc = uint32_t(beta - b0);
-            s = produit_quad(mot, x2f4(8u * bc + q), x2f4(8u * bc + 4u + q));
+#pragma unroll
+        for (uint32_t i = 0; i < LIGNE_LOT; ++i) {
+            const uint64_t m = mc + i;
+            if (m > mb) break;
+            if (m / SEGMENT_MACRO != seg) {
+                const float P = arbre8(acc);
+                if (parts != nullptr && voie == 0) parts[k] = P;
+                total = k == 0 ? P : total + P;
+                ++k;
+                acc = 0.0f;
+                seg = m / SEGMENT_MACRO;
+            }
+            const uint64_t beta = 8u * m + g;
+            const bool valide = beta >= b0 && beta < b1;
+            const uint32_t bc = valide ? uint32_t(beta - b0) : 0u;
+            float s = produit_quad(mots[i], x2f4(8u * bc + q), x2f4(8u * bc + 4u + q));
+            s = somme_quad(s);
+            if (valide) acc = fmaf(s, echelle_e8m0(es[i]), acc);
         }
-        s = somme_quad(s);
-        if (valide) acc = fmaf(s, echelle_e8m0(e), acc);
-        beta = beta_s;
-        valide = valide_s;
-        mot = mot_s;
-        e = e_s;
     }
     const float P = arbre8(acc);
     if (parts != nullptr && voie == 0) parts[k] = P;

@@ -64,4 +64,22 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 cudaError_t assurer_smem(const void* noyau, int octets);
 
+// Launch with programmatic dependent launch allowed: the kernel may start while the previous
+// kernel on the stream finishes, and must call attendre_amont() before it reads what that kernel
+// (or anything before it) wrote. Kernels call liberer_aval() once their own wait is done.
+template <typename... P, typename... A>
+cudaError_t lancer_pdl(void (*noyau)(P...), dim3 grille, dim3 bloc, size_t smem, cudaStream_t flux, A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grille;
+    cfg.blockDim = bloc;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = flux;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, noyau, static_cast<A&&>(args)...);
+}
+
 }  // namespace tb

@@ -17,6 +17,8 @@ __device__ __forceinline__ bool meilleur(float va, uint32_t ia, float vb, uint32
 __global__ void __launch_bounds__(32) k_topk(const float* __restrict__ logits, uint32_t E, uint32_t k,
                                              uint32_t* __restrict__ indices, float* __restrict__ poids, uint32_t* boite,
                                              uint32_t sequence) {
+    attendre_amont();
+    liberer_aval();
     const uint32_t voie = threadIdx.x;
     float v[8];
     uint32_t pris = 0;
@@ -82,6 +84,8 @@ __device__ __forceinline__ float swiglu_oai(float g, float u) {
 
 __global__ void __launch_bounds__(256) k_swiglu(const float* __restrict__ g, const float* __restrict__ u,
                                                 float* __restrict__ y, uint32_t n) {
+    attendre_amont();
+    liberer_aval();
     const uint32_t i = blockIdx.x * 256u + threadIdx.x;
     if (i < n) y[i] = swiglu_oai(g[i], u[i]);
 }
@@ -89,6 +93,8 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* __restrict__ g, con
 // residu[i] += ((w0 s0 + w1 s1) + w2 s2) + ..., no contraction (passe.cuh:611-622).
 __global__ void __launch_bounds__(256) k_combiner(float* __restrict__ residu, const float* __restrict__ sorties, uint32_t pas,
                                                   const float* __restrict__ poids, uint32_t n, uint32_t d) {
+    attendre_amont();
+    liberer_aval();
     const uint32_t i = blockIdx.x * 256u + threadIdx.x;
     if (i >= d || n == 0) return;
     float s = poids != nullptr ? __fmul_rn(poids[0], sorties[i]) : sorties[i];
@@ -101,19 +107,16 @@ __global__ void __launch_bounds__(256) k_combiner(float* __restrict__ residu, co
 
 cudaError_t lancer_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids, uint32_t* boite,
                         uint32_t sequence, cudaStream_t flux) {
-    k_topk<<<1, 32, 0, flux>>>(logits, E, k, indices, poids, boite, sequence);
-    return cudaGetLastError();
+    return lancer_pdl(k_topk, dim3(1), dim3(32), 0, flux, logits, E, k, indices, poids, boite, sequence);
 }
 
 cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, cudaStream_t flux) {
-    k_swiglu<<<(n + 255) / 256, 256, 0, flux>>>(g, u, y, n);
-    return cudaGetLastError();
+    return lancer_pdl(k_swiglu, dim3((n + 255) / 256), dim3(256), 0, flux, g, u, y, n);
 }
 
 cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, const float* poids, uint32_t n, uint32_t d,
                             cudaStream_t flux) {
-    k_combiner<<<(d + 255) / 256, 256, 0, flux>>>(residu, sorties, pas, poids, n, d);
-    return cudaGetLastError();
+    return lancer_pdl(k_combiner, dim3((d + 255) / 256), dim3(256), 0, flux, residu, sorties, pas, poids, n, d);
 }
 
 }  // namespace tb
