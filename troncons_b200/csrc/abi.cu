@@ -238,6 +238,7 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
     for (int j = 0; j < 3; ++j) {
         if (d.colonnes[j] > 32768) return usage("matrix %d: %u columns (32,768 at most)", j, d.colonnes[j]);
         if (!c->brut && d.colonnes[j] < 256) return usage("matrix %d: %u columns (256 at least)", j, d.colonnes[j]);
+        if (!c->brut && d.lignes[j] > 8192) return usage("matrix %d: %u rows (8,192 at most)", j, d.lignes[j]);
     }
     if (c->parties == nullptr || c->parties_octets == nullptr || c->indices == nullptr || c->poids == nullptr ||
         c->x == nullptr || c->residu == nullptr || c->controle == nullptr || (!c->brut && c->luts == nullptr))

@@ -4,12 +4,15 @@
 // The reference runs, per layer and routed expert, decoder_echelles + decoder_codes into an
 // SoA slot in VRAM, then gemv_mxfp4 x3, swiglu_oai, and combiner over the k experts
 // (trc-modele/src/lib.rs:533-553, trc-ordo/src/lib.rs:1328-1367). Here, on the caller's stream:
-//   1. k_moe_delta   DELTA_j of the k routed experts -> per block (scale | class << 8), into the
-//                    workspace (it stays in L2: 259,200 u16 per matrix);
-//   2. k_moe_codes   (gate, up) one warp per CODES_CTX tile decodes a macro-step (8 blocks) into
-//                    registers and multiplies it at once against 2x staged in shared memory;
-//                    the codes never leave the SM. Rows are closed where they end and at every
-//                    segment end (256 blocks), giving per-(row, segment) partials;
+//   1. k_moe_delta   DELTA_j of the k routed experts -> the delta byte of every block, into the
+//                    workspace (259,200 bytes per matrix: it stays in L2);
+//   2. k_moe_codes   (gate, up) one warp per CODES_CTX tile decodes a macro-step (8 blocks, one
+//                    word per lane, table chosen by the block's scale class) into registers and
+//                    multiplies it against 2x staged in shared memory, in four stages placed
+//                    between the four sub-steps of the next macro-step's decode; the block's
+//                    scale = median + delta - 128. The codes never leave the SM. Rows are closed
+//                    where they end and at every segment end (256 blocks), giving per-(row,
+//                    segment) partials;
 //   3. k_moe_swiglu  gate and up rows = fold of their partials + bias; h = SwiGLU (f64);
 //   4. k_moe_codes   (down) the same on h;
 //   5. k_moe_combiner down rows + bias, then residual += ((w0 s0 + w1 s1) + ...), no FMA.
@@ -30,7 +33,7 @@ Espace plan_espace(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_
     for (int j = 0; j < 3; ++j) {
         const uint64_t nb = uint64_t(lignes[j]) * (colonnes[j] / 32u);
         e.ek[j] = p;
-        p = al256(p + 2ull * nb * k);
+        p = al256(p + nb * k);
     }
     for (int j = 0; j < 3; ++j) {
         e.K[j] = parts_par_ligne(colonnes[j] / 32u);
@@ -64,29 +67,8 @@ constexpr uint32_t MOE_WARPS = 4;
 
 // ------------------------------------------------------------------ 1. DELTA -> scales, classes
 
-// (scale | class << 8) of the 4 blocks of a DELTA word, into the workspace.
-__device__ __forceinline__ void ecrire_ek(uint16_t* ek, const uint8_t* med, uint32_t R, uint32_t nblocs, uint32_t b0,
-                                          uint32_t mot, const LignesDelta& lg) {
-    uint32_t v[4];
-#pragma unroll
-    for (uint32_t k = 0; k < 4; ++k) {
-        const uint32_t rk = lg.rang(k);
-        const uint32_t dk = (mot >> (8u * k)) & 255u;
-        const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
-        const uint32_t kap = dk < 128u ? 0u : (dk == 128u ? 1u : 2u);
-        v[k] = ((mk + dk - 128u) & 255u) | (kap << 8);
-    }
-    if (b0 + 3u < nblocs) {
-        *reinterpret_cast<uint2*>(ek + b0) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
-    } else {
-        for (uint32_t k = 0; k < 4; ++k)
-            if (b0 + k < nblocs) ek[b0 + k] = uint16_t(v[k]);
-    }
-}
-
 __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     __shared__ uint32_t lut[M];
-    __shared__ uint8_t med_s[8192];
     __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_ALLOC];
     attendre_amont();  // first kernel of the layer: every input may come from the previous kernel
     liberer_aval();
@@ -96,10 +78,9 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     const uint32_t R = c.lignes[j], B = c.colonnes[j] / 32u, nblocs = R * B;
     const uint8_t* partie;
     uint64_t taille;
-    Flux fd, fm;
+    Flux fd;
     EnteteRans h;
     const bool bon = partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_DELTA, j, fd) &&
-                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
                      lire_entete(fd, nblocs, h);
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
@@ -109,46 +90,27 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     if (warp0 >= h.T) return;
     const uint32_t* src = c.luts + (uint64_t(j) * 4u) * M;
     for (uint32_t t = threadIdx.x; t < M; t += blockDim.x) lut[t] = src[t];
-    const uint8_t* med = fm.p;
-    if (R <= 8192u) {
-        for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med_s[t] = fm.p[t];
-        med = med_s;
-    }
     __syncthreads();
     const uint32_t lut_s = adresse_partagee(lut);
-    uint16_t* ek = reinterpret_cast<uint16_t*>(a.espace + a.plan.ek[j]) + uint64_t(i) * nblocs;
+    uint8_t* delta = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;
     const uint32_t nmacro = h.P / 128u;
     uint32_t hors_l = 0, pointeur = 0;
     Decodeur d;
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * DELTA_WARPS) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
-        uint32_t b0 = 4u * (m0 * 32u + voie);
-        LignesDelta lg;
-        lg.debut(b0, B);
-        d.avancer();
-        uint32_t mot_p = d.macro(lut_s);
-        for (uint32_t m = m0 + 1; m < m1; ++m) {
+        // Word w = 32 m + lane is the delta of blocks 4w .. 4w + 3, stored as it comes.
+        for (uint32_t m = m0; m < m1; ++m) {
             d.avancer();
-            uint32_t v[4];
-            const uint32_t mot = d.macro(lut_s, [&](auto k) {
-                constexpr int K = decltype(k)::value;  // block 4w + K of the previous word
-                const uint32_t rk = lg.rang(K);
-                const uint32_t dk = (mot_p >> (8u * K)) & 255u;
-                const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
-                v[K] = ((mk + dk - 128u) & 255u) | ((dk < 128u ? 0u : (dk == 128u ? 1u : 2u)) << 8);
-            });
+            const uint32_t mot = d.macro(lut_s);
+            const uint32_t b0 = 4u * (m * 32u + voie);
             if (b0 + 3u < nblocs) {
-                *reinterpret_cast<uint2*>(ek + b0) = make_uint2(v[0] | (v[1] << 16), v[2] | (v[3] << 16));
+                *reinterpret_cast<uint32_t*>(delta + b0) = mot;
             } else {
                 for (uint32_t k = 0; k < 4; ++k)
-                    if (b0 + k < nblocs) ek[b0 + k] = uint16_t(v[k]);
+                    if (b0 + k < nblocs) delta[b0 + k] = uint8_t(mot >> (8u * k));
             }
-            mot_p = mot;
-            b0 += 128u;
-            lg.avancer();
         }
-        ecrire_ek(ek, med, R, nblocs, b0, mot_p, lg);
         d.bilan(hors_l, pointeur);
         d.terminer();
     }
@@ -175,22 +137,32 @@ __device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t b
 struct GemvTuile {
     float acc, acc_s;     // current row r, next row
     uint32_t r, fin_r;    // warp-uniform: current row, first block of the next row
+    uint32_t med_r, med_s;  // medians of rows r and r + 1 (clamped to the last row)
     uint32_t R, B, K, voie, q;
     float* parts;
     const float4* x2s4;
+    const uint8_t* med;   // row medians (shared memory)
 
     __device__ __forceinline__ void debut(uint32_t m0) {
         acc = 0.0f;
         acc_s = 0.0f;
         r = (8u * m0) / B;
         fin_r = (r + 1u) * B;
+        med_r = med[min(r, R - 1u)];
+        med_s = med[min(r + 1u, R - 1u)];
     }
 
-    // Branch-free part: the block's scaled contribution (overlaps the next decode).
-    __device__ __forceinline__ void accumuler(uint32_t mot, uint32_t bloc, uint32_t b, uint32_t ekv, bool valide) {
+    // The block's scale: its row's median + delta - 128 (mod 256); the row is r or r + 1.
+    __device__ __forceinline__ float echelle(uint32_t bloc, uint32_t delta) const {
+        const uint32_t e = ((bloc < fin_r ? med_r : med_s) + delta - 128u) & 255u;
+        return echelle_e8m0(e);
+    }
+
+    // Branch-free part: the block's scaled contribution.
+    __device__ __forceinline__ void accumuler(uint32_t mot, uint32_t bloc, uint32_t b, uint32_t delta, bool valide) {
         float s = produit_quad(mot, x2s4[8u * b + q], x2s4[8u * b + 4u + q]);
         s = somme_quad(s);
-        const float sc = echelle_e8m0(ekv & 255u);
+        const float sc = echelle(bloc, delta);
         const bool cour = bloc < fin_r;
         acc = (valide && cour) ? fmaf(s, sc, acc) : acc;
         acc_s = (valide && !cour) ? fmaf(s, sc, acc_s) : acc_s;
@@ -222,7 +194,7 @@ struct GemvTuile {
         } else if constexpr (K == 2) {
             e.p = somme_quad(e.p);
         } else {
-            const float sc = echelle_e8m0(ekv & 255u);
+            const float sc = echelle(bloc, ekv);
             const bool cour = bloc < fin_r;
             acc = (valide && cour) ? fmaf(e.p, sc, acc) : acc;
             acc_s = (valide && !cour) ? fmaf(e.p, sc, acc_s) : acc_s;
@@ -239,6 +211,8 @@ struct GemvTuile {
             acc_s = 0.0f;
             ++r;
             fin_r += B;
+            med_r = med_s;
+            med_s = med[min(r + 1u, R - 1u)];
         }
         if ((m + 1u) % SEGMENT_MACRO == 0 || m + 1u == m1) {  // segment (or tile) ends
             if (r * B < 8u * m + 8u && r < R) {
@@ -250,7 +224,12 @@ struct GemvTuile {
     }
 };
 
-__global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
+// Shared bytes for the row medians of the largest matrix (16-aligned so that 2x stays aligned).
+__host__ __device__ __forceinline__ uint32_t medianes_octets(const Couche& c) {
+    return (max(c.lignes[0], c.lignes[2]) + 15u) & ~15u;
+}
+
+__global__ void __launch_bounds__(MOE_WARPS * 32, 1) k_moe_codes(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
@@ -260,8 +239,10 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
     uint64_t taille;
     Flux fc;
     EnteteRans h;
+    Flux fm;
     const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
-                     lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
+                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+                     R <= 8192u && lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
         return;
@@ -270,12 +251,14 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
     if (warp0 >= h.T) return;
     uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);                                  // [3][M]
     uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);                 // [W][ANNEAU_ALLOC]
-    float* x2s = reinterpret_cast<float*>(dyn + 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u);
+    uint8_t* med = dyn + 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u;                    // [medianes_octets]
+    float* x2s = reinterpret_cast<float*>(med + medianes_octets(c));
     {
         const uint4* src = reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M);
         uint4* dst = reinterpret_cast<uint4*>(lut);
         for (uint32_t t = threadIdx.x; t < 3u * M / 4u; t += blockDim.x) dst[t] = src[t];
     }
+    for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
     if (j < 2) charger_x2(x2s, c.x, c.x_bf16, C);
     // Everything above reads inputs the layer's first kernel waited for; the scales and classes
     // (and h for the down projection) come from the previous kernel.
@@ -284,7 +267,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
     if (j == 2) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
     const uint32_t lut_s = adresse_partagee(lut);
-    const uint16_t* __restrict__ ek = reinterpret_cast<const uint16_t*>(a.espace + a.plan.ek[j]) + uint64_t(i) * nblocs;
+    const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
     GemvTuile gv;
     gv.R = R;
     gv.B = B;
@@ -293,6 +276,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
     gv.q = voie & 3u;
     gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
     gv.x2s4 = reinterpret_cast<const float4*>(x2s);
+    gv.med = med;
     const uint32_t nmacro = h.P / 128u;
     const uint32_t g = voie >> 2;
     uint32_t hors_l = 0, pointeur = 0;
@@ -301,15 +285,16 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
         d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_ALLOC);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         gv.debut(m0);
-        // This lane's block at macro-step m is 8 m + g, column block b; (scale | class) read two
-        // macro-steps ahead; the GEMV of macro-step m - 1 runs while m decodes.
+        // This lane's block at macro-step m is 8 m + g, column block b; its delta read two
+        // macro-steps ahead (class -> table; with the median -> scale); the GEMV of macro-step
+        // m - 1 runs in stages between the sub-steps of macro-step m.
         uint32_t bloc = 8u * m0 + g;
         uint32_t b = bloc % B;
         uint32_t ek0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
         uint32_t ek1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
         uint32_t mot_p, bloc_p, b_p, ek_p;
         {
-            const uint32_t ctx = bloc < nblocs ? (ek0 >> 8) : 0u;
+            const uint32_t ctx = bloc < nblocs ? (ek0 < 128u ? 0u : (ek0 == 128u ? 1u : 2u)) : 0u;
             const uint32_t ek2 = (m0 + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
             d.avancer();
             mot_p = d.macro(lut_s + ctx * (M * 4u));
@@ -323,7 +308,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_codes(ArgsMoe a) {
             ek1 = ek2;
         }
         for (uint32_t m = m0 + 1; m < m1; ++m) {
-            const uint32_t ctx = bloc < nblocs ? (ek0 >> 8) : 0u;
+            const uint32_t ctx = bloc < nblocs ? (ek0 < 128u ? 0u : (ek0 == 128u ? 1u : 2u)) : 0u;
             const uint32_t ek2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
             d.avancer();
             GemvTuile::Etapes et;
@@ -476,7 +461,7 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
         if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.k), dim3(DELTA_WARPS * 32), 0,
                             flux, a)) != cudaSuccess)
             return e;
-        const size_t smem = 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u + 4u * cmax;
+        const size_t smem = 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u + medianes_octets(c) + 4u * cmax;
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem))) != cudaSuccess) return e;
         marque(1);
         const dim3 grille((tc + MOE_WARPS - 1) / MOE_WARPS, 2, c.k);
