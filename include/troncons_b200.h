@@ -215,6 +215,17 @@ int trc_moe_couche_fusionnee(const trc_moe_couche* couche, void* espace, size_t 
 int trc_moe_couche_chrono(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux,
                           void* const* evenements);
 
+/* No counterpart in the reference. trc_moe_couche_fusionnee without a workspace argument, for
+ * callers that cannot allocate device memory where they run the layer (an FFI caller holding only
+ * the buffers it was given, a serving loop whose device memory is fixed up front). The workspace
+ * is a fixed 8 MiB (8,388,608-byte) area of this library's device memory, one per device: a layer
+ * whose trc_moe_espace_octets exceeds it is refused with TRC_ERR_USAGE before any launch. Nothing
+ * is allocated. The first call on each device looks up the area's address there, so make it
+ * before any stream capture. All calls on a device share the area: calls that may overlap in
+ * time (different streams, different threads) race on it; calls on one stream are safe. Nothing
+ * in the area needs zeroing. Results and launches are those of trc_moe_couche_fusionnee. */
+int trc_moe_couche_sans_alloc(const trc_moe_couche* couche, void* flux);
+
 /* Router of the layer: logits = Wr x + br (f32 weights [experts][colonnes]; x bf16 or f32),
  * then top-k and f64 softmax as trc_routeur_topk. `logits` f32[experts] is written too. */
 int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts,

@@ -96,6 +96,7 @@ def _charger() -> C.CDLL:
         "trc_moe_espace_octets": (u64, [pd, u32]),
         "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
+        "trc_moe_couche_sans_alloc": (i32, [C.POINTER(MoeCouche), vp]),
         "trc_routeur": (i32, [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, vp]),
     }
     for nom, (res, args) in sig.items():
@@ -218,6 +219,13 @@ class Noyaux:
         else:
             ev = (C.c_void_p * 6)(*[int(v) if v else None for v in evenements])
             verifier(lib.trc_moe_couche_chrono(C.byref(desc), e.adresse, e.octets, _flux(flux), ev))
+
+    def moe_couche_sans_alloc(self, desc: MoeCouche, flux=None) -> None:
+        """The fused layer on the library's fixed 8 MiB device workspace (no workspace argument,
+        nothing allocated), for callers that cannot allocate device memory where they run the
+        layer. Calls that may overlap in time on one device race on that workspace; the first
+        call on each device looks its address up, so make it before any stream capture."""
+        verifier(lib.trc_moe_couche_sans_alloc(C.byref(desc), _flux(flux)))
 
 
 def espace_octets(dims: DimsExpert, k: int) -> int:

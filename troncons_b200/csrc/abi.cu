@@ -99,6 +99,10 @@ cudaError_t assurer_smem(const void* noyau, int octets) {
     return e;
 }
 
+int erreur_usage(const char* message) { return usage("%s", message); }
+int erreur_cuda(cudaError_t e) { return statut(e); }
+cudaError_t aligner_device(void* flux) { return sur_le_device_du_flux(flux); }
+
 }  // namespace tb
 
 extern "C" {

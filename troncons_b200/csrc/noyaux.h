@@ -64,6 +64,13 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 cudaError_t assurer_smem(const void* noyau, int octets);
 
+// For entry points outside abi.cu: set this thread's error message (usage error, or the CUDA
+// error's text; cudaSuccess clears it) and return the status; make the caller's stream's device
+// current in this library's runtime.
+int erreur_usage(const char* message);
+int erreur_cuda(cudaError_t e);
+cudaError_t aligner_device(void* flux);
+
 // Launch with programmatic dependent launch allowed: the kernel may start while the previous
 // kernel on the stream finishes, and must call attendre_amont() before it reads what that kernel
 // (or anything before it) wrote. Kernels call liberer_aval() once their own wait is done.
