@@ -20,6 +20,7 @@ import numpy as np
 ICI = os.path.dirname(os.path.abspath(__file__))
 _LIB = os.path.join(ICI, "_build", "liboracle.so")
 _REF = os.path.join(ICI, "_ref", "libtrc_ref.so")
+_BANC = os.path.join(ICI, "_ref", "libtrc_banc.so")
 
 P8 = C.POINTER(C.c_uint8)
 P16 = C.POINTER(C.c_uint16)
@@ -63,6 +64,7 @@ def _charger() -> C.CDLL:
         "orc_ajouter_comptes": (None, [P8, C.c_size_t, P8, C.c_size_t, P64]),
         "orc_decoder_matrice_v10": (C.c_int, [P8, C.c_size_t, C.c_uint8, C.c_uint32, C.c_uint32, P32, P8, P8, PF, C.POINTER(Bilan), C.POINTER(Bilan)]),
         "orc_decoder_expert": (C.c_int, [P8, C.c_size_t, P32, P32, P32, P8, P32]),
+        "orc_disposition": (None, [C.c_uint32, C.c_uint32, P64, P64, P64]),
         "orc_gemv_f64": (None, [P8, P8, PF, PD, C.c_uint32, C.c_uint32, PD]),
         "orc_routeur_topk": (None, [PF, C.c_uint32, C.c_uint32, P32, PF]),
         "orc_swiglu": (None, [PF, PF, PF, C.c_uint32]),
@@ -203,6 +205,13 @@ def decoder_matrice_v10(partie: bytes, j: int, R: int, B: int, luts4):
     return codes, ech, bi, bd, bc
 
 
+def disposition(R: int, C_: int):
+    """(scales offset, bias offset, stride) of an R x C matrix in the SoA slot (abi.rs:69-122)."""
+    e, b, s = C.c_uint64(), C.c_uint64(), C.c_uint64()
+    lib.orc_disposition(R, C_, C.byref(e), C.byref(b), C.byref(s))
+    return e.value, b.value, s.value
+
+
 def decoder_expert(partie: bytes, luts, lignes, colonnes, taille_emplacement: int):
     """(slot bytes, controle[4]) of a whole level-0 part, decoded by the CPU codec."""
     b = np.frombuffer(partie, np.uint8)
@@ -308,3 +317,53 @@ def ref():
         f.restype = C.c_int
         f.argtypes = args
     return r
+
+
+class Banc:
+    """The reference bench's independent encoder (oracle/_ref/libtrc_banc.so, compiled from
+    trc-noyaux/banc/banc_k.cu by ``make ref``): geometry-1 coder, LUT and part assembler."""
+
+    def __init__(self, chemin: str):
+        self.lib = C.CDLL(chemin)
+        sz = C.c_size_t
+        self.lib.refb_coder_g1.restype = sz
+        self.lib.refb_coder_g1.argtypes = [P8, C.c_uint32, C.c_uint32, P16, C.c_uint32, P8, C.c_uint32, P8, sz]
+        self.lib.refb_lut_g1.restype = None
+        self.lib.refb_lut_g1.argtypes = [P16, P32]
+        self.lib.refb_assembler_partie.restype = sz
+        self.lib.refb_assembler_partie.argtypes = [C.c_uint16, C.c_uint16, C.c_uint32, P8, P32, P32, P8, P8, sz]
+
+    def coder_g1(self, src, freqs, kappa=None, N: int = 256) -> bytes:
+        s = np.ascontiguousarray(src, dtype=np.uint8)
+        f = np.ascontiguousarray(freqs, dtype=np.uint16).reshape(-1)
+        k = None if kappa is None else np.ascontiguousarray(kappa, dtype=np.uint8)
+        cap = 16 + 132 * (s.size // 128 // N + 2) + 2 * s.size + 4096
+        out = np.zeros(cap, np.uint8)
+        n = self.lib.refb_coder_g1(p(s, P8), s.size, N, p(f, P16), f.size // 256, p(k, P8) if k is not None else None,
+                                   0 if k is None else k.size, p(out, P8), cap)
+        assert n > 0
+        return out[:n].tobytes()
+
+    def lut(self, freq) -> np.ndarray:
+        f = np.ascontiguousarray(freq, dtype=np.uint16)
+        out = np.zeros(4096, np.uint32)
+        self.lib.refb_lut_g1(p(f, P16), p(out, P32))
+        return out
+
+    def assembler_partie(self, couche: int, expert: int, flux) -> bytes:
+        """flux: list of (sorte, matrice, contexte, produits, bytes), as assembler_partie."""
+        descs = np.array([[f[0], f[1], f[2]] for f in flux], np.uint8).reshape(-1)
+        lg = np.array([len(f[4]) for f in flux], np.uint32)
+        pr = np.array([f[3] for f in flux], np.uint32)
+        data = np.frombuffer(b"".join(f[4] for f in flux) or b"\0", np.uint8)
+        cap = 64 + 16 * len(flux) + int(lg.sum()) + 16 * len(flux) + 8192
+        out = np.zeros(cap, np.uint8)
+        n = self.lib.refb_assembler_partie(couche, expert, len(flux), p(descs, P8), p(lg, P32), p(pr, P32),
+                                           p(data, P8), p(out, P8), cap)
+        assert n > 0
+        return out[:n].tobytes()
+
+
+def banc():
+    """The reference bench's encoder (Banc), or None when oracle/_ref/libtrc_banc.so is absent."""
+    return Banc(_BANC) if os.path.exists(_BANC) else None
