@@ -64,57 +64,61 @@ def pics():
 
 
 class Horloges:
-    """nvidia-smi clock samples while the timed region runs (the GPU named by its UUID)."""
+    """SM clock and clock-event reasons of this GPU (found by its UUID) sampled about every
+    millisecond through NVML while the timed region runs (read-only queries; the timed region
+    lasts milliseconds, shorter than nvidia-smi's sampling period)."""
 
-    def __init__(self, index):
-        self.index = index
-        self.p = None
-        self.lignes = []
+    RAISONS = [("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80)]
+
+    def __init__(self, uuid: str, index: int):
+        self.uuid, self.index = uuid, index
+        self.echantillons = []
+        self.max_mhz = None
+        self.arret = threading.Event()
+        self.t = None
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._lire, daemon=True)
+            import pynvml as N
+
+            N.nvmlInit()
+            try:
+                h = N.nvmlDeviceGetHandleByUUID(self.uuid)
+            except Exception:
+                h = N.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+
+            def lire():
+                while True:
+                    try:
+                        self.echantillons.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
+                                                  N.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        return
+                    if self.arret.wait(0.001):
+                        return
+
+            self.echantillons.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
+                                      N.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            self.t = threading.Thread(target=lire, daemon=True)
             self.t.start()
         except Exception:
-            self.p = None
+            self.t = None
         return self
 
-    def _lire(self):
-        for l in self.p.stdout:
-            self.lignes.append(l.strip())
-
     def __exit__(self, *a):
-        if self.p is not None:
-            self.p.terminate()
-            try:
-                self.p.wait(timeout=5)
-            except Exception:
-                self.p.kill()
+        self.arret.set()
+        if self.t is not None:
+            self.t.join(timeout=2)
 
     def resume(self):
-        sm, mx, raisons = [], 0.0, set()
-        noms = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in self.lignes:
-            c = [x.strip() for x in l.split(",")]
-            if len(c) < 9:
-                continue
-            try:
-                sm.append(float(c[1]))
-                mx = max(mx, float(c[2]))
-            except ValueError:
-                continue
-            for nom, v in zip(noms, c[5:9]):
-                if v.lower() == "active":
-                    raisons.add(nom)
-        if not sm:
+        if not self.echantillons:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(raisons), "samples": len(sm)}
+        sm = sorted(e[0] for e in self.echantillons)
+        raisons = sorted({nom for _, r in self.echantillons for nom, bit in self.RAISONS if r & bit})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": raisons,
+                "samples": len(sm), "source": "NVML"}
 
 
 def construire_couche(args):
@@ -218,7 +222,7 @@ def notre_bras(args):
         dist.barrier()
     t_pas = []
     uuid = str(getattr(torch.cuda.get_device_properties(lr), "uuid", ""))
-    with Horloges(f"GPU-{uuid}" if uuid and not uuid.startswith("GPU-") else (uuid or lr)) as horl:
+    with Horloges(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}", lr) as horl:
         t0 = time.time()
         for s in range(args.warmup, n_pas):
             pas_carte(s)
