@@ -63,6 +63,11 @@ def pics():
         return 6650.0, "fallback"
 
 
+# DRAM bytes (read + write) of one gate/up CODES launch measured by ncu (33.99 MB read, 512 B
+# written) for 31.76 MB of CODES_CTX streams; the rest is the delta bytes, LUTs and headers.
+TRAFIC_CODES_PORTE_HAUT = 33_993_984
+
+
 class Horloges:
     """SM clock and clock-event reasons of this GPU (found by its UUID) sampled about every
     millisecond through NVML while the timed region runs (read-only queries; the timed region
@@ -299,7 +304,11 @@ def notre_bras(args):
         "gpu_launches": args.steps * 7,
         "roofline": {"bound": "hbm", "kernel": "k_moe_codes (gate/up: CODES_CTX decode fused into the GEMV)",
                      "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
-                     "peak_source": sorte_pic, "traffic": None,
+                     "peak_source": sorte_pic,
+                     # DRAM read + write bytes of one gate/up launch, from ncu on the same launch
+                     # shape (4 routed experts of 2880 x 2880; profiles/k_moe_codes_config1_8experts.md).
+                     "traffic": TRAFIC_CODES_PORTE_HAUT, "traffic_source": "ncu dram__bytes_read.sum + "
+                     "dram__bytes_write.sum, one gate/up launch (profiles/k_moe_codes_config1_8experts.md)",
                      "algorithmic_bytes_per_launch": round(octets_dom / args.steps)},
         "phases_ms": {n: round(sum(v) / len(v), 4) for n, v in
                       zip(["router", "delta", "gate_up", "swiglu", "down", "combine"], t_phase)},
