@@ -248,6 +248,7 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
         c->x == nullptr || c->residu == nullptr || c->controle == nullptr || (!c->brut && c->luts == nullptr))
         return usage("layer descriptor: a device buffer is missing");
     if (!aligne(c->x, c->x_bf16 ? 2 : 4)) return usage("x misaligned");
+    if (!c->brut && !aligne(c->luts, 16)) return usage("LUTs misaligned (16 bytes)");
     const uint64_t besoin = tb::plan_espace(d.lignes, d.colonnes, c->k).total;
     if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
         return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);

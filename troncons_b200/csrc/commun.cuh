@@ -43,6 +43,7 @@ constexpr uint8_t SORTE_ECHELLES_BRUTES = 0x07;
 constexpr int CTL_HORS_L = 0;
 constexpr int CTL_FORMAT = 1;
 constexpr int CTL_POINTEUR = 2;
+constexpr int CTL_ATTENTE = 3;  // a bounded wait between two warps of a block gave up (never expected)
 
 // Per-warp word ring: 1024 words (2 KiB) refilled by chunks of 256 words (32 lanes x 16 B),
 // followed by a 64-word mirror of its first 64 words so that ring index + lane never wraps.
@@ -155,6 +156,37 @@ __device__ inline bool lire_entete(const Flux& f, uint32_t besoin, EnteteRans& h
 __device__ __forceinline__ void attendre_amont() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 // Lets the next kernel on the stream start its prologue.
 __device__ __forceinline__ void liberer_aval() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// ------------------------------------------------------------------ mbarriers (shared memory)
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.init.shared.b64 [%0], %1;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(b))), "r"(n)
+                 : "memory");
+}
+// Arrival with release semantics (the caller's earlier shared-memory writes are visible to a
+// thread whose wait on this phase succeeds).
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared.b64 st, [%0];\n\t}" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(b)))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_essai(uint64_t* b, uint32_t parite) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(b))), "r"(parite)
+        : "memory");
+    return ok != 0;
+}
+// Waits until the phase of parity `parite` has completed, at most ATTENTES_MAX tries (each may
+// suspend the warp for a short while); false when it gave up.
+constexpr uint32_t ATTENTES_MAX = 1u << 22;
+__device__ __forceinline__ bool mbar_attendre(uint64_t* b, uint32_t parite) {
+    for (uint32_t n = 0; n < ATTENTES_MAX; ++n)
+        if (mbar_essai(b, parite)) return true;
+    return false;
+}
 
 // ------------------------------------------------------------------ async copies
 

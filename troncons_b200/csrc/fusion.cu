@@ -6,13 +6,13 @@
 // (trc-modele/src/lib.rs:533-553, trc-ordo/src/lib.rs:1328-1367). Here, on the caller's stream:
 //   1. k_moe_delta   DELTA_j of the k routed experts -> the delta byte of every block, into the
 //                    workspace (259,200 bytes per matrix: it stays in L2);
-//   2. k_moe_codes   (gate, up) one warp per CODES_CTX tile decodes a macro-step (8 blocks, one
-//                    word per lane, table chosen by the block's scale class) into registers and
-//                    multiplies it against 2x staged in shared memory, in four stages placed
-//                    between the four sub-steps of the next macro-step's decode; the block's
-//                    scale = median + delta - 128. The codes never leave the SM. Rows are closed
-//                    where they end and at every segment end (256 blocks), giving per-(row,
-//                    segment) partials;
+//   2. k_moe_codes   (gate, up) per CODES_CTX tile, a producer warp runs the decode chain (one
+//                    word per lane and macro-step, table chosen by the block's scale class) and
+//                    hands each 32-macro-step segment of words through shared memory to a
+//                    consumer warp, which multiplies it against 2x staged in shared memory; the
+//                    block's scale = median + delta - 128. The codes never leave the SM. Rows
+//                    are closed where they end and at every segment end (256 blocks), giving
+//                    per-(row, segment) partials;
 //   3. k_moe_swiglu  gate and up rows = fold of their partials + bias; h = SwiGLU (f64);
 //   4. k_moe_codes   (down) the same on h;
 //   5. k_moe_combiner down rows + bias, then residual += ((w0 s0 + w1 s1) + ...), no FMA.
@@ -62,18 +62,36 @@ __device__ __forceinline__ bool partie_de(const Couche& c, uint32_t i, const uin
     return partie != nullptr && taille >= 64 && (reinterpret_cast<uintptr_t>(partie) & 15u) == 0;
 }
 
+// Copies n 16-byte chunks into shared memory; each thread has up to 8 loads in flight before
+// it stores (the prologues are latency-bound: a load at a time would cost one L2 round trip
+// per chunk).
+__device__ __forceinline__ void copier16(uint4* dst, const uint4* __restrict__ src, uint32_t n) {
+    uint32_t t = threadIdx.x;
+    const uint32_t pas = blockDim.x;
+    for (; t + 7u * pas < n; t += 8u * pas) {
+        uint4 v[8];
+#pragma unroll
+        for (uint32_t k = 0; k < 8u; ++k) v[k] = __ldg(src + t + k * pas);
+#pragma unroll
+        for (uint32_t k = 0; k < 8u; ++k) dst[t + k * pas] = v[k];
+    }
+    for (; t < n; t += pas) dst[t] = __ldg(src + t);
+}
+
 constexpr uint32_t DELTA_WARPS = 4;
 constexpr uint32_t MOE_WARPS = 4;
 
 // ------------------------------------------------------------------ 1. DELTA -> scales, classes
 
 __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
-    __shared__ uint32_t lut[M];
+    __shared__ __align__(16) uint32_t lut[M];
     __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_ALLOC];
-    attendre_amont();  // first kernel of the layer: every input may come from the previous kernel
-    liberer_aval();
     const Couche& c = a.c;
     const uint32_t j = blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
+    // The LUTs are an input of the layer; the routed experts come from the previous kernel.
+    copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u) * M), M / 4u);
+    attendre_amont();
+    liberer_aval();
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], B = c.colonnes[j] / 32u, nblocs = R * B;
     const uint8_t* partie;
@@ -88,8 +106,6 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     }
     const uint32_t warp0 = blockIdx.x * DELTA_WARPS;
     if (warp0 >= h.T) return;
-    const uint32_t* src = c.luts + (uint64_t(j) * 4u) * M;
-    for (uint32_t t = threadIdx.x; t < M; t += blockDim.x) lut[t] = src[t];
     __syncthreads();
     const uint32_t lut_s = adresse_partagee(lut);
     uint8_t* delta = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;
@@ -119,7 +135,25 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
 
 // ------------------------------------------------------------------ shared-memory x2 = 2 x
 
+// x2s[0..C) = 2 x, x bf16 or f32 (C a multiple of 32); 16-byte loads when x is 16-aligned.
 __device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t bf16, uint32_t C) {
+    float4* d4 = reinterpret_cast<float4*>(x2s);
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        if (bf16) {
+            const uint4* s4 = static_cast<const uint4*>(x);
+            for (uint32_t t = threadIdx.x; t < C / 8u; t += blockDim.x) {
+                const uint4 v = __ldg(s4 + t);
+                d4[2u * t] = make_float4(2.0f * __uint_as_float(v.x << 16), 2.0f * __uint_as_float(v.x & 0xFFFF0000u),
+                                         2.0f * __uint_as_float(v.y << 16), 2.0f * __uint_as_float(v.y & 0xFFFF0000u));
+                d4[2u * t + 1u] = make_float4(2.0f * __uint_as_float(v.z << 16), 2.0f * __uint_as_float(v.z & 0xFFFF0000u),
+                                              2.0f * __uint_as_float(v.w << 16), 2.0f * __uint_as_float(v.w & 0xFFFF0000u));
+            }
+        } else {
+            const float4* s4 = static_cast<const float4*>(x);
+            for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x) d4[t] = fois2(__ldg(s4 + t));
+        }
+        return;
+    }
     if (bf16) {
         const uint16_t* xb = static_cast<const uint16_t*>(x);
         for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) x2s[t] = 2.0f * __uint_as_float(uint32_t(xb[t]) << 16);
@@ -131,17 +165,16 @@ __device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t b
 
 // ------------------------------------------------------------------ 2/4. CODES_CTX decoded into the GEMV
 
-// The GEMV of one decoded macro-step (8 blocks, one word per lane) into the row partials: the
+// The GEMV of decoded macro-steps (8 blocks, one word per lane) into the row partials: the
 // block's sum (quad tree), scaled and accumulated on the current row or the next; rows closed
 // where they end, and the row in progress closed at the segment's (or the tile's) end.
 struct GemvTuile {
-    float acc, acc_s;     // current row r, next row
-    uint32_t r, fin_r;    // warp-uniform: current row, first block of the next row
+    float acc, acc_s;       // current row r, next row
+    uint32_t r, fin_r;      // warp-uniform: current row, first block of the next row
     uint32_t med_r, med_s;  // medians of rows r and r + 1 (clamped to the last row)
-    uint32_t R, B, K, voie, q;
+    uint32_t R, B, K, voie;
     float* parts;
-    const float4* x2s4;
-    const uint8_t* med;   // row medians (shared memory)
+    const uint8_t* med;     // row medians (shared memory)
 
     __device__ __forceinline__ void debut(uint32_t m0) {
         acc = 0.0f;
@@ -152,53 +185,12 @@ struct GemvTuile {
         med_s = med[min(r + 1u, R - 1u)];
     }
 
-    // The block's scale: its row's median + delta - 128 (mod 256); the row is r or r + 1.
-    __device__ __forceinline__ float echelle(uint32_t bloc, uint32_t delta) const {
-        const uint32_t e = ((bloc < fin_r ? med_r : med_s) + delta - 128u) & 255u;
-        return echelle_e8m0(e);
-    }
-
-    // Branch-free part: the block's scaled contribution.
-    __device__ __forceinline__ void accumuler(uint32_t mot, uint32_t bloc, uint32_t b, uint32_t delta, bool valide) {
-        float s = produit_quad(mot, x2s4[8u * b + q], x2s4[8u * b + 4u + q]);
-        s = somme_quad(s);
-        const float sc = echelle(bloc, delta);
+    // Block `bloc`'s quad sum s, scaled by 2^(median + delta - 256) of its row (r or r + 1).
+    __device__ __forceinline__ void accumuler(float s, uint32_t bloc, uint32_t delta, bool valide) {
         const bool cour = bloc < fin_r;
+        const float sc = echelle_e8m0(((cour ? med_r : med_s) + delta - 128u) & 255u);
         acc = (valide && cour) ? fmaf(s, sc, acc) : acc;
         acc_s = (valide && !cour) ? fmaf(s, sc, acc_s) : acc_s;
-    }
-
-    // The same, in four stages to interleave with the four sub-steps of the next decode.
-    struct Etapes {
-        float lo[4], hi[4];
-        float4 xa, xb;
-        float p;
-    };
-    template <int K>
-    __device__ __forceinline__ void etape(Etapes& e, uint32_t mot, uint32_t bloc, uint32_t b, uint32_t ekv, bool valide) {
-        if constexpr (K == 0) {
-            e.xa = x2s4[8u * b + q];
-            e.xb = x2s4[8u * b + 4u + q];
-            e2m1_mot(mot, e.lo, e.hi);
-        } else if constexpr (K == 1) {
-            float p = 0.0f;
-            p = fmaf(e.lo[0], e.xa.x, p);
-            p = fmaf(e.hi[0], e.xb.x, p);
-            p = fmaf(e.lo[1], e.xa.y, p);
-            p = fmaf(e.hi[1], e.xb.y, p);
-            p = fmaf(e.lo[2], e.xa.z, p);
-            p = fmaf(e.hi[2], e.xb.z, p);
-            p = fmaf(e.lo[3], e.xa.w, p);
-            p = fmaf(e.hi[3], e.xb.w, p);
-            e.p = p;
-        } else if constexpr (K == 2) {
-            e.p = somme_quad(e.p);
-        } else {
-            const float sc = echelle(bloc, ekv);
-            const bool cour = bloc < fin_r;
-            acc = (valide && cour) ? fmaf(e.p, sc, acc) : acc;
-            acc_s = (valide && !cour) ? fmaf(e.p, sc, acc_s) : acc_s;
-        }
     }
 
     // Row and segment closing after macro-step m (warp-uniform branches).
@@ -224,22 +216,54 @@ struct GemvTuile {
     }
 };
 
+// Decode and multiply run in different warps of a block: MOE_PAIRES producer warps each
+// decode one CODES_CTX tile (the bare rANS chain, one word per lane and macro-step, table
+// chosen by the block's scale class), writing the words and the blocks' delta bytes into a
+// segment buffer in shared memory (one segment = 32 macro-steps, double-buffered); the paired
+// consumer warp multiplies each finished segment while the next one decodes. One hand-off per
+// segment, through two mbarriers per buffer (full: 32 producer lanes arrive; empty: 32 consumer
+// lanes arrive), every wait bounded.
+constexpr uint32_t MOE_PAIRES = 4;
+constexpr uint32_t SEG_TAMPONS = 2;
+constexpr uint32_t SEG_MOTS = SEGMENT_MACRO * 32u;  // words of one segment buffer
+constexpr uint32_t SEG_DELTAS = SEGMENT_MACRO * 8u;  // delta bytes of one segment buffer
+
 // Shared bytes for the row medians of the largest matrix (16-aligned so that 2x stays aligned).
 __host__ __device__ __forceinline__ uint32_t medianes_octets(const Couche& c) {
     return (max(c.lignes[0], c.lignes[2]) + 15u) & ~15u;
 }
 
-__global__ void __launch_bounds__(MOE_WARPS * 32, 1) k_moe_codes(ArgsMoe a) {
+// Dynamic shared memory of k_moe_codes: 3 LUTs, the producers' word rings, the segment
+// buffers (words, deltas), the medians, 2x, the mbarriers.
+struct DispositionCodes {
+    uint32_t anneaux, mots, deltas, med, x2, barrieres, total;
+};
+__host__ __device__ __forceinline__ DispositionCodes disposition_codes(const Couche& c) {
+    DispositionCodes d;
+    const uint32_t cmax = max(c.colonnes[0], c.colonnes[2]);
+    d.anneaux = 3u * M * 4u;
+    d.mots = d.anneaux + MOE_PAIRES * ANNEAU_ALLOC * 2u;
+    d.deltas = d.mots + MOE_PAIRES * SEG_TAMPONS * SEG_MOTS * 4u;
+    d.med = d.deltas + MOE_PAIRES * SEG_TAMPONS * SEG_DELTAS;
+    d.x2 = d.med + medianes_octets(c);
+    d.barrieres = d.x2 + 4u * ((cmax + 3u) & ~3u);
+    d.total = d.barrieres + MOE_PAIRES * 2u * SEG_TAMPONS * 8u;
+    return d;
+}
+
+__device__ __forceinline__ uint32_t classe_delta(uint32_t d) { return d < 128u ? 0u : (d == 128u ? 1u : 2u); }
+
+__global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
+    const uint32_t warp = threadIdx.x >> 5, paire = warp % MOE_PAIRES;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
     const uint8_t* partie;
     uint64_t taille;
-    Flux fc;
+    Flux fc, fm;
     EnteteRans h;
-    Flux fm;
     const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
                      trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
                      R <= 8192u && lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
@@ -247,92 +271,134 @@ __global__ void __launch_bounds__(MOE_WARPS * 32, 1) k_moe_codes(ArgsMoe a) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
         return;
     }
-    const uint32_t warp0 = blockIdx.x * MOE_WARPS;
+    const uint32_t warp0 = blockIdx.x * MOE_PAIRES;
     if (warp0 >= h.T) return;
-    uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);                                  // [3][M]
-    uint16_t* anneaux = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u);                 // [W][ANNEAU_ALLOC]
-    uint8_t* med = dyn + 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u;                    // [medianes_octets]
-    float* x2s = reinterpret_cast<float*>(med + medianes_octets(c));
-    {
-        const uint4* src = reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M);
-        uint4* dst = reinterpret_cast<uint4*>(lut);
-        for (uint32_t t = threadIdx.x; t < 3u * M / 4u; t += blockDim.x) dst[t] = src[t];
-    }
-    for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
+    const DispositionCodes dc = disposition_codes(c);
+    uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);
+    uint8_t* med = dyn + dc.med;
+    float* x2s = reinterpret_cast<float*>(dyn + dc.x2);
+    uint64_t* barrieres = reinterpret_cast<uint64_t*>(dyn + dc.barrieres);
+    copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M),
+             3u * M / 4u);
+    if (fm.p + ((R + 15u) & ~15u) <= partie + taille)
+        copier16(reinterpret_cast<uint4*>(med), reinterpret_cast<const uint4*>(fm.p), (R + 15u) / 16u);
+    else
+        for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
     if (j < 2) charger_x2(x2s, c.x, c.x_bf16, C);
-    // Everything above reads inputs the layer's first kernel waited for; the scales and classes
-    // (and h for the down projection) come from the previous kernel.
+    if (threadIdx.x < MOE_PAIRES * 2u * SEG_TAMPONS) mbar_init(barrieres + threadIdx.x, 32u);
+    const uint32_t paire_t0 = warp0 + paire;
+    Decodeur d;
+    uint16_t* anneau = reinterpret_cast<uint16_t*>(dyn + dc.anneaux) + paire * ANNEAU_ALLOC;
+    // The producer starts its first tile (states, first word chunks): the part is an input of
+    // the layer, so this overlaps the previous kernel's tail.
+    if (warp < MOE_PAIRES && paire_t0 < h.T) d.debut(h, paire_t0, voie, anneau);
+    // Everything above reads inputs the layer's first kernel waited for; the delta bytes (and h
+    // for the down projection) come from the previous kernel.
     attendre_amont();
     liberer_aval();
     if (j == 2) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
-    const uint32_t lut_s = adresse_partagee(lut);
-    const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
-    GemvTuile gv;
-    gv.R = R;
-    gv.B = B;
-    gv.K = a.plan.K[j];
-    gv.voie = voie;
-    gv.q = voie & 3u;
-    gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
-    gv.x2s4 = reinterpret_cast<const float4*>(x2s);
-    gv.med = med;
+
+    uint32_t* mots = reinterpret_cast<uint32_t*>(dyn + dc.mots) + paire * SEG_TAMPONS * SEG_MOTS;  // [b][m][lane]
+    uint8_t* deltas = dyn + dc.deltas + paire * SEG_TAMPONS * SEG_DELTAS;                          // [b][m][g]
+    uint64_t* pleins = barrieres + paire * 2u * SEG_TAMPONS;
+    uint64_t* vides = pleins + SEG_TAMPONS;
     const uint32_t nmacro = h.P / 128u;
     const uint32_t g = voie >> 2;
-    uint32_t hors_l = 0, pointeur = 0;
-    Decodeur d;
-    for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * MOE_WARPS) {
-        d.debut(h, t, voie, anneaux + (threadIdx.x >> 5) * ANNEAU_ALLOC);
-        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
-        gv.debut(m0);
-        // This lane's block at macro-step m is 8 m + g, column block b; its delta read two
-        // macro-steps ahead (class -> table; with the median -> scale); the GEMV of macro-step
-        // m - 1 runs in stages between the sub-steps of macro-step m.
-        uint32_t bloc = 8u * m0 + g;
-        uint32_t b = bloc % B;
-        uint32_t ek0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
-        uint32_t ek1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
-        uint32_t mot_p, bloc_p, b_p, ek_p;
-        {
-            const uint32_t ctx = bloc < nblocs ? (ek0 < 128u ? 0u : (ek0 == 128u ? 1u : 2u)) : 0u;
-            const uint32_t ek2 = (m0 + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
-            d.avancer();
-            mot_p = d.macro(lut_s + ctx * (M * 4u));
-            bloc_p = bloc;
-            b_p = b;
-            ek_p = ek0;
-            bloc += 8u;
-            b += 8u;
-            b -= b >= B ? B : 0u;
-            ek0 = ek1;
-            ek1 = ek2;
+    const uint32_t pas_tuiles = gridDim.x * MOE_PAIRES;
+    bool abandon = false;
+
+    if (warp < MOE_PAIRES) {
+        // ---------------- producer: the decode chain
+        const uint32_t lut_s = adresse_partagee(lut);
+        const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
+        uint32_t hors_l = 0, pointeur = 0, n = 0;
+        for (uint32_t t = paire_t0; t < h.T && !abandon; t += pas_tuiles) {
+            if (t != paire_t0) d.debut(h, t, voie, anneau);
+            const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+            // This lane's block at macro-step m is 8 m + g; its delta read two macro-steps ahead.
+            uint32_t bloc = 8u * m0 + g;
+            uint32_t e0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
+            uint32_t e1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
+            for (uint32_t s0 = m0; s0 < m1; s0 += SEGMENT_MACRO, ++n) {
+                const uint32_t b = n % SEG_TAMPONS;
+                if (n >= SEG_TAMPONS && !mbar_attendre(&vides[b], ((n / SEG_TAMPONS) - 1u) & 1u)) {
+                    abandon = true;
+                    break;
+                }
+                uint32_t* mb = mots + b * SEG_MOTS;
+                uint8_t* db = deltas + b * SEG_DELTAS;
+                const uint32_t s1 = min(s0 + SEGMENT_MACRO, m1);
+                for (uint32_t m = s0; m < s1; ++m) {
+                    const uint32_t ctx = bloc < nblocs ? classe_delta(e0) : 0u;
+                    const uint32_t e2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
+                    d.avancer();
+                    mb[(m - s0) * 32u + voie] = d.macro(lut_s + ctx * (M * 4u));
+                    if ((voie & 3u) == 0) db[(m - s0) * 8u + g] = uint8_t(e0);
+                    bloc += 8u;
+                    e0 = e1;
+                    e1 = e2;
+                }
+                mbar_arrive(&pleins[b]);
+            }
+            d.bilan(hors_l, pointeur);
+            d.terminer();
         }
-        for (uint32_t m = m0 + 1; m < m1; ++m) {
-            const uint32_t ctx = bloc < nblocs ? (ek0 < 128u ? 0u : (ek0 == 128u ? 1u : 2u)) : 0u;
-            const uint32_t ek2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
-            d.avancer();
-            GemvTuile::Etapes et;
-            const bool valide_p = bloc_p < nblocs;
-            const uint32_t mot = d.macro(lut_s + ctx * (M * 4u), [&](auto k) {
-                gv.etape<decltype(k)::value>(et, mot_p, bloc_p, b_p, ek_p, valide_p);
-            });
-            gv.fermer(m - 1u, m1);
-            mot_p = mot;
-            bloc_p = bloc;
-            b_p = b;
-            ek_p = ek0;
-            bloc += 8u;
-            b += 8u;
-            b -= b >= B ? B : 0u;
-            ek0 = ek1;
-            ek1 = ek2;
+        verser_controle(controle, voie, hors_l, pointeur);
+    } else {
+        // ---------------- consumer: the GEMV of each finished segment
+        const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
+        const uint32_t q = voie & 3u;
+        GemvTuile gv;
+        gv.R = R;
+        gv.B = B;
+        gv.K = a.plan.K[j];
+        gv.voie = voie;
+        gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
+        gv.med = med;
+        uint32_t n = 0;
+        for (uint32_t t = warp0 + paire; t < h.T && !abandon; t += pas_tuiles) {
+            const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+            gv.debut(m0);
+            uint32_t bloc = 8u * m0 + g;
+            uint32_t bc = bloc % B;  // column block of `bloc` in its row
+            for (uint32_t s0 = m0; s0 < m1; s0 += SEGMENT_MACRO, ++n) {
+                const uint32_t b = n % SEG_TAMPONS;
+                if (!mbar_attendre(&pleins[b], (n / SEG_TAMPONS) & 1u)) {
+                    abandon = true;
+                    break;
+                }
+                const uint32_t* mb = mots + b * SEG_MOTS;
+                const uint8_t* db = deltas + b * SEG_DELTAS;
+                const uint32_t s1 = min(s0 + SEGMENT_MACRO, m1);
+                for (uint32_t m = s0; m < s1; m += 8u) {
+                    // Eight macro-steps' block sums at once (independent), then their ordered
+                    // accumulation with the row and segment closing.
+                    float sv[8];
+                    uint32_t dv[8];
+#pragma unroll
+                    for (uint32_t u = 0; u < 8u; ++u) {
+                        const bool ok = m + u < s1;
+                        const uint32_t mot = ok ? mb[(m + u - s0) * 32u + voie] : 0u;
+                        dv[u] = ok ? uint32_t(db[(m + u - s0) * 8u + g]) : 0u;
+                        sv[u] = somme_quad(produit_quad(mot, x2s4[8u * bc + q], x2s4[8u * bc + 4u + q]));
+                        bc += 8u;
+                        bc -= bc >= B ? B : 0u;
+                    }
+#pragma unroll
+                    for (uint32_t u = 0; u < 8u; ++u) {
+                        if (m + u < s1) {
+                            gv.accumuler(sv[u], bloc, dv[u], bloc < nblocs);
+                            gv.fermer(m + u, m1);
+                            bloc += 8u;
+                        }
+                    }
+                }
+                mbar_arrive(&vides[b]);
+            }
         }
-        gv.accumuler(mot_p, bloc_p, b_p, ek_p, bloc_p < nblocs);
-        gv.fermer(m1 - 1u, m1);
-        d.bilan(hors_l, pointeur);
-        d.terminer();
     }
-    verser_controle(controle, voie, hors_l, pointeur);
+    if (abandon && voie == 0) atomicAdd(&controle[CTL_ATTENTE], 1u);
 }
 
 // ------------------------------------------------------------------ raw parts: row-centric
@@ -461,17 +527,17 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
         if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.k), dim3(DELTA_WARPS * 32), 0,
                             flux, a)) != cudaSuccess)
             return e;
-        const size_t smem = 3u * M * 4u + MOE_WARPS * ANNEAU_ALLOC * 2u + medianes_octets(c) + 4u * cmax;
+        const size_t smem = disposition_codes(c).total;
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem))) != cudaSuccess) return e;
         marque(1);
-        const dim3 grille((tc + MOE_WARPS - 1) / MOE_WARPS, 2, c.k);
-        if ((e = lancer_pdl(k_moe_codes, grille, dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
+        const dim3 grille((tc + MOE_PAIRES - 1) / MOE_PAIRES, 2, c.k);
+        if ((e = lancer_pdl(k_moe_codes, grille, dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess) return e;
         marque(2);
         if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, c.k, 1), dim3(256), 0, flux, a)) != cudaSuccess)
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_codes, dim3(grille.x, 1, c.k), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess)
+        if ((e = lancer_pdl(k_moe_codes, dim3(grille.x, 1, c.k), dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess)
             return e;
         marque(4);
     } else {
