@@ -306,9 +306,9 @@ def notre_bras(args):
                      "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
                      "peak_source": sorte_pic,
                      # DRAM read + write bytes of one gate/up launch, from ncu on the same launch
-                     # shape (4 routed experts of 2880 x 2880; profiles/k_moe_codes_config1_8experts.md).
+                     # shape (4 routed experts of 2880 x 2880), summarised under profiles/.
                      "traffic": TRAFIC_CODES_PORTE_HAUT, "traffic_source": "ncu dram__bytes_read.sum + "
-                     "dram__bytes_write.sum, one gate/up launch (profiles/k_moe_codes_config1_8experts.md)",
+                     "dram__bytes_write.sum, one gate/up launch of the same shape (summary under profiles/)",
                      "algorithmic_bytes_per_launch": round(octets_dom / args.steps)},
         "phases_ms": {n: round(sum(v) / len(v), 4) for n, v in
                       zip(["router", "delta", "gate_up", "swiglu", "down", "combine"], t_phase)},

@@ -5,7 +5,7 @@
  * This is the drop-in boundary for the reference's kernel contract (crate trc-noyaux, struct
  * `Noyaux`, moteur/crates/trc-noyaux/src/lib.rs): the same structs, byte for byte, the same
  * argument meaning and the same error behaviour. A Rust host binds it with `extern "C"`
- * declarations. Every launch is asynchronous on the caller's stream
+ * declarations of these functions and `#[repr(C)]` twins of these structs. Every launch is asynchronous on the caller's stream
  * (`flux`, a cudaStream_t; NULL is the legacy default stream). The caller owns every device
  * buffer; the library allocates nothing on the device.
  *
@@ -197,10 +197,18 @@ typedef struct trc_moe_couche {
     uint32_t* controle;             /* device u32[4*k]: counters per active expert, zeroed by caller */
     uint32_t n_delta, n_codes;      /* macro-steps per tile the parts were encoded with (0: 256, what
                                        trc-codeur writes); they only size the grids */
+    /* Token batch and expert parallelism (all zero: one token, every expert held here). */
+    uint32_t jetons;                /* tokens (0 = 1): x is [jetons][d], residu [jetons][d], indices /
+                                       poids / controle hold jetons * k activations, token-major */
+    uint32_t expert_debut;          /* experts held by this call: [expert_debut, expert_fin); the */
+    uint32_t expert_fin;            /* others are skipped, no error (expert_fin = 0: all are held) */
+    uint32_t partiel;               /* 1: residu[b] = this call's weighted sum over its held
+                                       activations (0 when none), for a sum across GPUs; 0: residu += */
 } trc_moe_couche;
 
-/* Workspace bytes the fused layer needs for these dimensions and k (device memory the caller
- * allocates once and reuses; contents need no initialisation). */
+/* Workspace bytes the fused layer needs for these dimensions and k activations (tokens times
+ * routed experts per token; device memory the caller allocates once and reuses; contents need no
+ * initialisation). */
 uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k);
 
 /* Runs the fused layer. `espace` (256-aligned) >= trc_moe_espace_octets. Compressed parts need

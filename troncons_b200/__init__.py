@@ -64,7 +64,9 @@ class MoeCouche(C.Structure):
     _fields_ = [("parties", C.c_void_p), ("parties_octets", C.c_void_p), ("experts", C.c_uint32), ("k", C.c_uint32),
                 ("luts", C.c_void_p), ("dims", DimsExpert), ("indices", C.c_void_p), ("poids", C.c_void_p),
                 ("x", C.c_void_p), ("x_bf16", C.c_uint32), ("brut", C.c_uint32), ("residu", C.c_void_p),
-                ("controle", C.c_void_p), ("n_delta", C.c_uint32), ("n_codes", C.c_uint32)]
+                ("controle", C.c_void_p), ("n_delta", C.c_uint32), ("n_codes", C.c_uint32),
+                ("jetons", C.c_uint32), ("expert_debut", C.c_uint32), ("expert_fin", C.c_uint32),
+                ("partiel", C.c_uint32)]
 
 
 def _charger() -> C.CDLL:

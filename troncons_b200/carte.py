@@ -24,10 +24,16 @@ def _octets(b: bytes, alignement: int = 4096) -> int:
 
 
 class CoucheCarte:
+    """A layer on the device. `jetons`: tokens per call (x [jetons][d], residual [jetons][d],
+    jetons * k activations). `tenus`: the experts [debut, fin) this device holds (an
+    expert-parallel share: the other experts' parts may be None and are never read); None: all."""
+
     def __init__(self, c: Couche, k: int = 4, brut: bool = True, device: str = "cuda", n_delta: int = 0,
-                 n_codes: int = 0):
+                 n_codes: int = 0, jetons: int = 1, tenus=None):
         self.c = c
         self.k = k
+        self.jetons = jetons
+        self.tenus = tenus
         self.dims = c.dims
         self.dev = torch.device(device)
         self.n = Noyaux()
@@ -37,28 +43,31 @@ class CoucheCarte:
             self.parties_b, self.adresses_b, self.tailles_b = self._monter(c.parties_brutes)
         else:
             self.parties_b = None
-        self.octets_compresses = [len(p) for p in c.parties]
+        self.octets_compresses = [len(p) if p is not None else 0 for p in c.parties]
         self.luts = torch.from_numpy(c.luts.view(np.int32).copy()).to(self.dev)
         self.wr = torch.from_numpy(c.wr).to(self.dev)
         self.br = torch.from_numpy(c.br).to(self.dev)
-        self.logits = torch.zeros(E, dtype=torch.float32, device=self.dev)
-        self.idx = torch.zeros(k, dtype=torch.int32, device=self.dev)
-        self.poids = torch.zeros(k, dtype=torch.float32, device=self.dev)
-        self.controle = torch.zeros(4 * k, dtype=torch.int32, device=self.dev)
-        self.espace = torch.empty(espace_octets(self.dims, k) + 256, dtype=torch.uint8, device=self.dev)
+        self.logits = torch.zeros(jetons, E, dtype=torch.float32, device=self.dev)
+        self.idx = torch.zeros(jetons * k, dtype=torch.int32, device=self.dev)
+        self.poids = torch.zeros(jetons * k, dtype=torch.float32, device=self.dev)
+        self.controle = torch.zeros(4 * jetons * k, dtype=torch.int32, device=self.dev)
+        self.espace = torch.empty(espace_octets(self.dims, jetons * k) + 256, dtype=torch.uint8, device=self.dev)
         self.n_delta, self.n_codes = n_delta, n_codes
         d = self.dims
         self.R0, self.C0, self.R2 = d.lignes[0], d.colonnes[0], d.lignes[2]
 
     def _monter(self, parties):
+        """Uploads the parts (None: an expert not held here, address and size 0)."""
+        parties = [p if p is not None else b"" for p in parties]
         tailles = [len(p) for p in parties]
         decal = np.cumsum([0] + [_octets(p) for p in parties])
-        buf = np.zeros(int(decal[-1]), np.uint8)
+        buf = np.zeros(max(int(decal[-1]), 1), np.uint8)
         for i, p in enumerate(parties):
             buf[decal[i]:decal[i] + len(p)] = np.frombuffer(p, np.uint8)
         t = torch.from_numpy(buf).to(self.dev)
         base = t.data_ptr()
-        adresses = torch.tensor([base + int(o) for o in decal[:-1]], dtype=torch.int64, device=self.dev)
+        adresses = torch.tensor([base + int(o) if len(p) else 0 for o, p in zip(decal[:-1], parties)],
+                                dtype=torch.int64, device=self.dev)
         tl = torch.tensor(tailles, dtype=torch.int64, device=self.dev)
         return t, adresses, tl
 
@@ -66,18 +75,22 @@ class CoucheCarte:
         """Device view (tensor slice) of expert x's part."""
         src = self.c.parties_brutes if brute else self.c.parties
         buf = self.parties_b if brute else self.parties
-        o = sum(_octets(p) for p in src[:x])
+        o = sum(_octets(p) for p in src[:x] if p is not None)
         return buf[o:o + len(src[x])]
 
     def routeur(self, x: torch.Tensor, flux=None) -> None:
-        self.n.routeur(self.wr, self.br, x, x.dtype == torch.bfloat16, self.c.experts, self.C0, self.k, self.logits,
-                       self.idx, self.poids, flux)
+        """The router of every token of x ([jetons][d] or [d]): logits, top-k, weights."""
+        xs = x.reshape(self.jetons, self.C0)
+        k = self.k
+        for b in range(self.jetons):
+            self.n.routeur(self.wr, self.br, xs[b], x.dtype == torch.bfloat16, self.c.experts, self.C0, k,
+                           self.logits[b], self.idx[b * k:(b + 1) * k], self.poids[b * k:(b + 1) * k], flux)
 
-    def descripteur(self, x: torch.Tensor, residu: torch.Tensor, brute: bool) -> MoeCouche:
-        if x.numel() != self.C0 or not x.is_contiguous() or x.device.type != "cuda":
-            raise ValueError(f"x: {self.C0} contiguous elements on the device expected")
-        if residu.numel() != self.R2 or residu.dtype != torch.float32 or not residu.is_contiguous():
-            raise ValueError(f"residual: {self.R2} contiguous f32 expected")
+    def descripteur(self, x: torch.Tensor, residu: torch.Tensor, brute: bool, partiel: bool = False) -> MoeCouche:
+        if x.numel() != self.jetons * self.C0 or not x.is_contiguous() or x.device.type != "cuda":
+            raise ValueError(f"x: {self.jetons} x {self.C0} contiguous elements on the device expected")
+        if residu.numel() != self.jetons * self.R2 or residu.dtype != torch.float32 or not residu.is_contiguous():
+            raise ValueError(f"residual: {self.jetons} x {self.R2} contiguous f32 expected")
         desc = MoeCouche()
         if brute:
             desc.parties, desc.parties_octets = self.adresses_b.data_ptr(), self.tailles_b.data_ptr()
@@ -95,6 +108,10 @@ class CoucheCarte:
         desc.residu = residu.data_ptr()
         desc.controle = self.controle.data_ptr()
         desc.n_delta, desc.n_codes = self.n_delta, self.n_codes
+        desc.jetons = self.jetons
+        if self.tenus is not None:
+            desc.expert_debut, desc.expert_fin = self.tenus
+        desc.partiel = int(partiel)
         return desc
 
     def _espace(self):
@@ -103,11 +120,12 @@ class CoucheCarte:
         return self.espace[d:]
 
     def couche(self, x: torch.Tensor, residu: torch.Tensor, brute: bool = False, flux=None, routeur: bool = True,
-               evenements=None):
-        """Router then the fused layer; `residu` (f32) is updated in place."""
+               evenements=None, partiel: bool = False):
+        """Router then the fused layer; `residu` (f32) is updated in place (partiel: overwritten
+        with this device's share of the combine)."""
         if routeur:
             self.routeur(x, flux)
-        self._desc = self.descripteur(x, residu, brute)  # keep it alive while the launch reads it
+        self._desc = self.descripteur(x, residu, brute, partiel)  # keep it alive while the launch reads it
         self.n.moe_couche(self._desc, self._espace(), flux, evenements)
 
     # ---------------------------------------------------------------- decode-then-multiply

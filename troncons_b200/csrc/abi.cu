@@ -236,6 +236,10 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
     if (int s = verifier_dims(&c->dims)) return s;
     const trc_dims_expert& d = c->dims;
     if (c->k == 0 || c->k > 8 || c->k > c->experts) return usage("k = %u of %u experts", c->k, c->experts);
+    const uint32_t jetons = c->jetons ? c->jetons : 1u;
+    if (jetons > 128) return usage("%u tokens (128 at most)", jetons);
+    if (c->expert_fin != 0 && (c->expert_debut >= c->expert_fin || c->expert_fin > c->experts))
+        return usage("held experts [%u, %u) of %u", c->expert_debut, c->expert_fin, c->experts);
     if (d.lignes[0] != d.lignes[1] || d.colonnes[0] != d.colonnes[1] || d.colonnes[2] != d.lignes[0] ||
         d.lignes[2] != d.colonnes[0])
         return usage("gate/up/down shapes do not chain (hidden -> ffn -> hidden)");
@@ -249,7 +253,7 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
         return usage("layer descriptor: a device buffer is missing");
     if (!aligne(c->x, c->x_bf16 ? 2 : 4)) return usage("x misaligned");
     if (!c->brut && !aligne(c->luts, 16)) return usage("LUTs misaligned (16 bytes)");
-    const uint64_t besoin = tb::plan_espace(d.lignes, d.colonnes, c->k).total;
+    const uint64_t besoin = tb::plan_espace(d.lignes, d.colonnes, c->k * jetons).total;
     if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
         return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
     tb::Couche k{};
@@ -271,6 +275,10 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
     k.controle = c->controle;
     k.n_delta = c->n_delta;
     k.n_codes = c->n_codes;
+    k.jetons = jetons;
+    k.expert_debut = c->expert_debut;
+    k.expert_fin = c->expert_fin;
+    k.partiel = c->partiel ? 1u : 0u;
     SUR_LE_FLUX(flux);
     return statut(tb::lancer_moe(k, espace, static_cast<cudaStream_t>(flux),
                                  reinterpret_cast<cudaEvent_t const*>(evenements)));

@@ -53,7 +53,18 @@ struct ArgsMoe {
     uint32_t j0;  // first matrix of this launch (0: gate and up; 2: down)
 };
 
-// The part of active expert i, if it is addressable.
+// Whether activation i's expert is held by this call (others are skipped: no work, no error).
+__device__ __forceinline__ bool tenu(const Couche& c, uint32_t i) {
+    const uint32_t e = c.indices[i];
+    return c.expert_fin == 0 || (e >= c.expert_debut && e < c.expert_fin);
+}
+
+// Activation i's input: its token's x.
+__device__ __forceinline__ const void* x_de(const Couche& c, uint32_t i) {
+    return static_cast<const uint8_t*>(c.x) + uint64_t(i / c.k) * c.colonnes[0] * (c.x_bf16 ? 2u : 4u);
+}
+
+// The part of activation i's expert, if it is addressable.
 __device__ __forceinline__ bool partie_de(const Couche& c, uint32_t i, const uint8_t*& partie, uint64_t& taille) {
     const uint32_t e = c.indices[i];
     if (e >= c.experts) return false;
@@ -92,6 +103,7 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u) * M), M / 4u);
     attendre_amont();
     liberer_aval();
+    if (!tenu(c, i)) return;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], B = c.colonnes[j] / 32u, nblocs = R * B;
     const uint8_t* partie;
@@ -258,6 +270,7 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
     const uint32_t warp = threadIdx.x >> 5, paire = warp % MOE_PAIRES;
+    if (!tenu(c, i)) return;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
     const uint8_t* partie;
@@ -284,7 +297,7 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
         copier16(reinterpret_cast<uint4*>(med), reinterpret_cast<const uint4*>(fm.p), (R + 15u) / 16u);
     else
         for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
-    if (j < 2) charger_x2(x2s, c.x, c.x_bf16, C);
+    if (j < 2) charger_x2(x2s, x_de(c, i), c.x_bf16, C);
     if (threadIdx.x < MOE_PAIRES * 2u * SEG_TAMPONS) mbar_init(barrieres + threadIdx.x, 32u);
     const uint32_t paire_t0 = warp0 + paire;
     Decodeur d;
@@ -409,6 +422,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
     liberer_aval();
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
+    if (!tenu(c, i)) return;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
     const uint8_t* partie;
@@ -423,7 +437,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
     }
     float* x2s = reinterpret_cast<float*>(dyn);
     if (j < 2)
-        charger_x2(x2s, c.x, c.x_bf16, C);
+        charger_x2(x2s, x_de(c, i), c.x_bf16, C);
     else
         charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
@@ -447,6 +461,9 @@ __global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
     __shared__ const float* biais[2];
     const Couche& c = a.c;
     const uint32_t i = blockIdx.y;
+    attendre_amont();
+    liberer_aval();
+    if (!tenu(c, i)) return;
     if (threadIdx.x < 2) {
         const uint8_t* partie;
         uint64_t taille;
@@ -458,8 +475,6 @@ __global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
                        : nullptr;
     }
     __syncthreads();
-    attendre_amont();
-    liberer_aval();
     const uint32_t R = c.lignes[0], r = blockIdx.x * 256u + threadIdx.x;
     if (r >= R) return;
     float* h = reinterpret_cast<float*>(a.espace + a.plan.h) + uint64_t(i) * R;
@@ -477,33 +492,48 @@ __global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
 
 // ------------------------------------------------------------------ 5. down rows, combine
 
+// Token b = blockIdx.y: s = ((w0 s0 + w1 s1) + w2 s2) + ... over its activations held here, in
+// slot order, products and sums rounded separately (passe.cuh:611-622); residu[b] += s, or, when
+// the call is partial (its experts are one share of an expert-parallel layer), residu[b] = s
+// (0 when no activation of the token is held here) for the cross-GPU sum.
 __global__ void __launch_bounds__(256) k_moe_combiner(ArgsMoe a) {
     __shared__ const float* biais[8];
+    __shared__ uint32_t tenus;
     const Couche& c = a.c;
+    const uint32_t b = blockIdx.y, i0 = b * c.k;
+    attendre_amont();
+    liberer_aval();
     if (threadIdx.x < c.k) {
         const uint8_t* partie;
         uint64_t taille;
         Flux fb;
-        biais[threadIdx.x] = (partie_de(c, threadIdx.x, partie, taille) && trouver_flux(partie, taille, SORTE_BIAIS, 2, fb) &&
+        const uint32_t i = i0 + threadIdx.x;
+        const bool t = tenu(c, i);
+        biais[threadIdx.x] = (t && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_BIAIS, 2, fb) &&
                               fb.longueur >= 4u * c.lignes[2])
                                  ? reinterpret_cast<const float*>(fb.p)
                                  : nullptr;
+        const uint32_t v = __ballot_sync(__activemask(), t);
+        if (threadIdx.x == 0) tenus = v;
     }
     __syncthreads();
-    attendre_amont();
-    liberer_aval();
     const uint32_t R = c.lignes[2], r = blockIdx.x * 256u + threadIdx.x;
     if (r >= R) return;
     const uint32_t B = c.colonnes[2] / 32u, K = a.plan.K[2];
     const float* parts = reinterpret_cast<const float*>(a.espace + a.plan.parts[2]);
     float s = 0.0f;
-    for (uint32_t i = 0; i < c.k; ++i) {
-        const float b = biais[i] != nullptr ? biais[i][r] : 0.0f;
-        const float si = finir_ligne(parts + (uint64_t(i) * R + r) * K, r, B) + b;
+    bool premier = true;
+    for (uint32_t u = 0; u < c.k; ++u) {
+        if (!((tenus >> u) & 1u)) continue;
+        const uint32_t i = i0 + u;
+        const float bi = biais[u] != nullptr ? biais[u][r] : 0.0f;
+        const float si = finir_ligne(parts + (uint64_t(i) * R + r) * K, r, B) + bi;
         const float p = __fmul_rn(c.poids[i], si);
-        s = i == 0 ? p : __fadd_rn(s, p);
+        s = premier ? p : __fadd_rn(s, p);
+        premier = false;
     }
-    c.residu[r] = __fadd_rn(c.residu[r], s);
+    float* res = c.residu + uint64_t(b) * R;
+    res[r] = c.partiel ? s : __fadd_rn(res[r], s);
 }
 
 // ------------------------------------------------------------------ launcher
@@ -512,7 +542,8 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
     auto marque = [&](int i) {
         if (ev != nullptr && ev[i] != nullptr) cudaEventRecord(ev[i], flux);
     };
-    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, c.k), 0};
+    const uint32_t na = activations(c);
+    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, na), 0};
     const uint32_t nd = c.n_delta ? c.n_delta : 256u, nc = c.n_codes ? c.n_codes : 256u;
     uint32_t td = 1, tc = 1;
     for (int j = 0; j < 3; ++j) {
@@ -524,20 +555,20 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
     cudaError_t e;
     marque(0);
     if (!c.brut) {
-        if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.k), dim3(DELTA_WARPS * 32), 0,
+        if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, na), dim3(DELTA_WARPS * 32), 0,
                             flux, a)) != cudaSuccess)
             return e;
         const size_t smem = disposition_codes(c).total;
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem))) != cudaSuccess) return e;
         marque(1);
-        const dim3 grille((tc + MOE_PAIRES - 1) / MOE_PAIRES, 2, c.k);
+        const dim3 grille((tc + MOE_PAIRES - 1) / MOE_PAIRES, 2, na);
         if ((e = lancer_pdl(k_moe_codes, grille, dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess) return e;
         marque(2);
-        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, c.k, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_codes, dim3(grille.x, 1, c.k), dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess)
+        if ((e = lancer_pdl(k_moe_codes, dim3(grille.x, 1, na), dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess)
             return e;
         marque(4);
     } else {
@@ -546,16 +577,16 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
         const uint32_t rmax = std::max(c.lignes[0], c.lignes[2]);
         const uint32_t gx = (rmax + MOE_WARPS - 1) / MOE_WARPS;
         marque(1);
-        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 2, c.k), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
+        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 2, na), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
         marque(2);
-        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, c.k, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 1, c.k), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
+        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 1, na), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
         marque(4);
     }
-    if ((e = lancer_pdl(k_moe_combiner, dim3((c.lignes[2] + 255) / 256), dim3(256), 0, flux, a)) != cudaSuccess) return e;
+    if ((e = lancer_pdl(k_moe_combiner, dim3((c.lignes[2] + 255) / 256, c.jetons), dim3(256), 0, flux, a)) != cudaSuccess) return e;
     marque(5);
     return cudaGetLastError();
 }

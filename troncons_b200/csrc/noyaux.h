@@ -34,13 +34,19 @@ struct Couche {
     float* residu;
     uint32_t* controle;
     uint32_t n_delta, n_codes;
+    uint32_t jetons;                    // tokens (>= 1): activation i = token i / k, slot i % k
+    uint32_t expert_debut, expert_fin;  // experts held here ([debut, fin); fin = 0: all)
+    uint32_t partiel;                   // 1: the combine writes this call's sum, not residu +=
 };
+
+// Activations of a call: tokens x routed experts per token.
+__host__ __device__ __forceinline__ uint32_t activations(const Couche& c) { return c.k * c.jetons; }
 
 // Workspace of the fused layer (offsets in bytes from its 256-aligned base).
 struct Espace {
-    uint64_t ek[3];      // u16 (scale | class << 8) per block, per matrix, times k
-    uint64_t parts[3];   // f32 per-segment row partials [k][R][K] per matrix
-    uint64_t h;          // f32 [k][lignes[0]] SwiGLU output
+    uint64_t ek[3];      // delta byte per block, per matrix, times the activations
+    uint64_t parts[3];   // f32 per-segment row partials [activation][R][K] per matrix
+    uint64_t h;          // f32 [activation][lignes[0]] SwiGLU output
     uint64_t total;
     uint32_t K[3];       // partial slots per row
 };

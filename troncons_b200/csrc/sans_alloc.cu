@@ -59,7 +59,7 @@ cudaError_t adresse_espace_fixe(void** p) {
 
 extern "C" int trc_moe_couche_sans_alloc(const trc_moe_couche* couche, void* flux) {
     if (couche == nullptr) return tb::erreur_usage("layer descriptor absent");
-    const uint64_t besoin = trc_moe_espace_octets(&couche->dims, couche->k);
+    const uint64_t besoin = trc_moe_espace_octets(&couche->dims, couche->k * (couche->jetons ? couche->jetons : 1u));
     if (besoin > ESPACE_FIXE_OCTETS) {
         char m[256];
         snprintf(m, sizeof m,
