@@ -325,6 +325,144 @@ def notre_bras(args):
         print(json.dumps(ligne), flush=True)
 
 
+def bras_ep(args):
+    """N > 1: the expert-parallel layer (config 3). Rank r holds experts partage(128, r, N) (16
+    per GPU at 8); a step is a batch of N tokens (one per GPU on average: weak scaling), the
+    router replicated on every rank, the fused layer on the rank's share, then the combine's SUM
+    all-reduce over NCCL. Times are the max over ranks; bytes are what all ranks read."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+    from troncons_b200.parallele import CoucheEP, partage, reduire_comptes
+
+    r, w, lr = rang()
+    torch.cuda.set_device(lr)
+    dev = torch.device("cuda", lr)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    jetons = w
+    t0 = time.time()
+    c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=False, n_delta=args.n_delta,
+                 n_codes=args.n_codes, tenus=partage(args.experts, r, w), reduire=reduire_comptes(device=dev))
+    t_gen = time.time() - t0
+    ep = CoucheEP(c, r, w, k=args.k, jetons=jetons)
+    C0, R2 = c.dims.colonnes[0], c.dims.lignes[2]
+    n_pas = args.warmup + args.steps
+    rng = np.random.default_rng(args.graine)  # the same tokens on every rank
+    xs = torch.from_numpy(rng.standard_normal((n_pas, jetons, C0)).astype(np.float32)).to(torch.bfloat16)
+    res0 = torch.from_numpy(rng.standard_normal((n_pas, jetons, R2)).astype(np.float32))
+    xs_dev, res_dev = xs.cuda(), res0.cuda()
+    x_hote, res_hote = xs.pin_memory(), res0.pin_memory()
+    res_sortie = torch.empty_like(res_hote).pin_memory()
+    x_buf = torch.empty(jetons, C0, dtype=torch.bfloat16, device="cuda")
+    residu = torch.empty(jetons, R2, dtype=torch.float32, device="cuda")
+    vidange = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB > L2 (126 MB)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    idx_journal = torch.zeros(n_pas, jetons * args.k, dtype=torch.int32, device="cuda")
+    partiel = r != 0
+
+    # The rank's local step (router of the N tokens + its fused share) is captured in a CUDA
+    # graph; the all-reduce is issued after each replay.
+    x_buf.copy_(xs_dev[0])
+    residu.copy_(res_dev[0])
+    for _ in range(3):
+        ep.local(x_buf, residu, partiel)
+    torch.cuda.synchronize()
+    graphe = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graphe):
+        ep.local(x_buf, residu, partiel)
+    torch.cuda.synchronize()
+
+    def pas(s, hote=False):
+        vidange.zero_()
+        ev[0].record()
+        if hote:
+            x_buf.copy_(x_hote[s], non_blocking=True)
+            residu.copy_(res_hote[s], non_blocking=True)
+        else:
+            x_buf.copy_(xs_dev[s])
+            residu.copy_(res_dev[s])
+        graphe.replay()
+        dist.all_reduce(residu, op=dist.ReduceOp.SUM)
+        if hote:
+            res_sortie[s].copy_(residu, non_blocking=True)
+        ev[1].record()
+        idx_journal[s].copy_(ep.carte.idx)
+
+    for s in range(args.warmup):
+        pas(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t_pas = []
+    uuid = str(getattr(torch.cuda.get_device_properties(lr), "uuid", ""))
+    with Horloges(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}", lr) as horl:
+        for s in range(args.warmup, n_pas):
+            pas(s)
+            torch.cuda.synchronize()
+            t_pas.append(ev[0].elapsed_time(ev[1]))
+    assert (ep.carte.controle.cpu().numpy() == 0).all(), "integrity counters set during the bench"
+    dist.barrier()
+    e2e = []
+    for s in range(n_pas):
+        pas(s, hote=True)
+        torch.cuda.synchronize()
+        if s >= args.warmup:
+            e2e.append(ev[0].elapsed_time(ev[1]))
+    del graphe
+
+    # Bytes this rank read per step: the parts of its held activations, the router (read by
+    # every rank), LUTs, x and the residual's read and write.
+    idx = idx_journal.cpu().numpy()
+    debut, fin = ep.tenus
+    E = c.experts
+    fixe = 4 * E * C0 + 4 * E + 3 * 4 * 4 * 4096 + jetons * (2 * C0 + 2 * 4 * R2)
+    octets = sum(sum(int.from_bytes(c.parties[int(e)][12:16], "little") for e in idx[s] if debut <= e < fin) + fixe
+                 for s in range(args.warmup, n_pas))
+    tt = torch.tensor([sum(t_pas), sum(e2e)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    oc = torch.tensor([float(octets)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(oc, op=dist.ReduceOp.SUM)
+    t_total_ms, t_e2e_ms, octets_tous = float(tt[0]), float(tt[1]), float(oc[0])
+    clocks = horl.resume()
+    dist.barrier()
+    dist.destroy_process_group()
+    if r != 0:
+        return
+    ligne = {
+        "metric": METRIQUE,
+        "value": round(octets_tous / (t_total_ms * 1e-3) / 1e9, 2),
+        "unit": UNITE,
+        "n_gpus": w,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8",
+        "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
+        "config": {
+            "workload": f"config 3: expert-parallel gpt-oss-120b MoE layer, {args.experts} experts "
+                        f"({fin - debut} per GPU), top-{args.k}, batch {jetons} tokens (one per GPU), x bf16[2880], "
+                        "router f32 replicated, combine by NCCL all-reduce of the batch's f32 residual",
+            "experts": args.experts, "k": args.k, "tokens_per_step": jetons, "n_delta": args.n_delta,
+            "n_codes": args.n_codes, "l2": "flushed between steps (256 MB written)",
+            "bytes_per_step": round(octets_tous / args.steps), "parallelism": f"ep{w}",
+        },
+        "e2e": {"value": round(octets_tous / (t_e2e_ms * 1e-3) / 1e9, 2), "unit": UNITE,
+                "h2d_bytes_per_step": jetons * (2 * C0 + 4 * R2), "d2h_bytes_per_step": jetons * 4 * R2},
+        "gpu_launches": args.steps * (2 * jetons + 5),
+        "roofline": None,
+        "clocks": clocks,
+        "generation_s": round(t_gen, 1),
+    }
+    print(json.dumps(ligne), flush=True)
+
+
 def base_cpu(c, args, bornes_s: float, pas_min: int = 3):
     """The reference's path on host cores (oracle/couche_cpu.c), all cores, a bounded sample."""
     import numpy as np
@@ -396,6 +534,8 @@ def main():
     args = arguments()
     if args.impl == "reference":
         bras_reference(args)
+    elif rang()[1] > 1:
+        bras_ep(args)
     else:
         notre_bras(args)
 

@@ -166,10 +166,11 @@ int64_t trc_coder_partie_brute(const uint8_t* const* blocs, const uint8_t* const
 /* Seeded synthetic MXFP4 matrices: per row sigma = 0.02 * exp(0.3 N(0,1)), weights N(0, sigma),
  * per 32-block E8M0 = floor(log2 max|w|) - 2 (+127), E2M1 round-to-nearest-even with the sign
  * kept (so -0 codes exist, as in gpt-oss's GGUF), biases N(0, 0.01) rounded to bf16 and stored
- * as f32. n matrices of R x C, stream `graine` + matrix index; blocs: n*R*(C/32)*17 bytes,
- * biais: n*R floats. Runs on up to `fils` host threads (0: all). */
-int trc_synth_matrices(uint64_t graine, uint32_t lignes, uint32_t colonnes, uint32_t n, uint8_t* blocs, float* biais,
-                       int fils);
+ * as f32. Matrices premier .. premier + n - 1 of R x C, each drawn from the stream (`graine`,
+ * matrix index, row) so a matrix does not depend on which others are drawn with it; blocs:
+ * n*R*(C/32)*17 bytes, biais: n*R floats. Runs on up to `fils` host threads (0: all). */
+int trc_synth_matrices(uint64_t graine, uint32_t lignes, uint32_t colonnes, uint32_t premier, uint32_t n,
+                       uint8_t* blocs, float* biais, int fils);
 
 /* ---------------------------------------------------------------- new: the fused MoE layer */
 

@@ -1,0 +1,72 @@
+"""GPU, two or more devices: the expert-parallel layer over NCCL against the single-GPU layer.
+
+Two ranks (one process per GPU) each draw and encode only their half of a layer's experts,
+build the layer's tables from the counts summed over NCCL, then run expert-parallel steps on a
+batch of 2 tokens: router on every rank, the fused layer on the rank's share (rank 0 adds into
+the residual, rank 1 writes its share alone), one SUM all-reduce. Rank 0 also runs the whole
+layer on one GPU; the two agree within 1e-5 max|residual| (the same terms summed in another
+order) and route the same experts. Skipped with fewer than two GPUs."""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _port_libre() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rang(rang, monde, port):
+    import torch.distributed as dist
+
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+    from troncons_b200.carte import CoucheCarte
+    from troncons_b200.parallele import CoucheEP, partage, reduire_comptes
+
+    torch.cuda.set_device(rang)
+    dev = torch.device("cuda", rang)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rang, world_size=monde,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        dims = T.DimsExpert.de([256, 256, 512], [512, 512, 256])
+        part = S.couche(77, dims, 8, brut=False, tenus=partage(8, rang, monde), reduire=reduire_comptes(device=dev))
+        ep = CoucheEP(part, rang, monde, k=4, jetons=2)
+        toute = CoucheCarte(S.couche(77, dims, 8, brut=False), k=4, brut=False, jetons=2) if rang == 0 else None
+        rng = np.random.default_rng(3)
+        for _ in range(6):
+            x = torch.from_numpy(rng.standard_normal((2, 512)).astype(np.float32)).to(torch.bfloat16).cuda()
+            r0 = torch.from_numpy(rng.standard_normal((2, 512)).astype(np.float32)).cuda()
+            r = r0.clone()
+            ep.carte.controle.zero_()
+            ep.etape(x, r)
+            torch.cuda.synchronize()
+            assert (ep.carte.controle == 0).all()
+            if rang == 0:
+                rt = r0.clone()
+                toute.couche(x, rt)
+                torch.cuda.synchronize()
+                assert torch.equal(toute.idx, ep.carte.idx)
+                a, b = r.cpu().numpy(), rt.cpu().numpy()
+                assert np.abs(a - b).max() <= 1e-5 * max(1.0, np.abs(b).max())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_deux_gpus_egale_un_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_rang, args=(2, _port_libre()), nprocs=2, join=True, start_method="spawn")

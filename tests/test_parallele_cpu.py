@@ -1,0 +1,120 @@
+"""CPU: the expert-parallel host logic (troncons_b200/parallele.py), with two `gloo` ranks.
+
+- shares are contiguous, disjoint, cover every expert, and differ in size by at most one;
+- two ranks that each draw and encode only their experts, summing the layer's counts with an
+  all-reduce, build exactly the single-process layer: same tables, same parts, byte for byte;
+- one expert-parallel step (rank 0 adds its share into the residual, the other writes its share
+  alone, then a SUM all-reduce) gives both ranks the whole layer's result, on a small dense MoE
+  computed in numpy (the same terms as a single process, summed in another order: 1e-6)."""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from troncons_b200.parallele import partage  # noqa: E402
+
+
+@pytest.mark.parametrize("experts", [128, 8, 10, 129])
+@pytest.mark.parametrize("monde", [1, 2, 3, 4, 8])
+def test_partage(experts, monde):
+    s = [partage(experts, r, monde) for r in range(monde)]
+    assert s[0][0] == 0 and s[-1][1] == experts
+    assert all(a[1] == b[0] for a, b in zip(s, s[1:]))
+    tailles = [f - d for d, f in s]
+    assert max(tailles) - min(tailles) <= 1 and min(tailles) >= 1
+
+
+def test_partage_refuse():
+    with pytest.raises(ValueError):
+        partage(4, 0, 8)
+    with pytest.raises(ValueError):
+        partage(8, 2, 2)
+
+
+def _port_libre() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _moe_dense(rng, E, d, jetons, k):
+    W = rng.standard_normal((E, d, d)).astype(np.float32)
+    Wr = rng.standard_normal((E, d)).astype(np.float32)
+    x = rng.standard_normal((jetons, d)).astype(np.float32)
+    r0 = rng.standard_normal((jetons, d)).astype(np.float32)
+    logits = x @ Wr.T
+    idx = np.argsort(-logits, axis=1, kind="stable")[:, :k]
+    w = np.exp(np.take_along_axis(logits, idx, 1) - logits.max(1, keepdims=True))
+    w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+    return W, x, r0, idx, w
+
+
+def _somme_locale(W, x, idx, w, debut, fin):
+    """Per token, the slot-ordered weighted sum over the activations whose expert is held."""
+    jetons, d = x.shape
+    s = np.zeros((jetons, d), np.float32)
+    for b in range(jetons):
+        premier = True
+        for u in range(idx.shape[1]):
+            e = int(idx[b, u])
+            if not debut <= e < fin:
+                continue
+            p = np.float32(w[b, u]) * (W[e] @ x[b]).astype(np.float32)
+            s[b] = p if premier else s[b] + p
+            premier = False
+    return s
+
+
+def _travail(rang, monde, port):
+    import torch.distributed as dist
+
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+    from troncons_b200.parallele import etape_ep, reduire_comptes
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rang, world_size=monde,
+                            timeout=timedelta(seconds=60))
+    try:
+        # 1. the layer drawn by shares equals the layer drawn at once
+        dims = T.DimsExpert.de([64, 64, 96], [96, 96, 64])
+        tenus = partage(8, rang, monde)
+        part = S.couche(41, dims, 8, brut=False, tenus=tenus, reduire=reduire_comptes(), fils=2)
+        toute = S.couche(41, dims, 8, brut=False, fils=2)
+        assert (part.freqs == toute.freqs).all(), "tables differ"
+        for e in range(8):
+            if tenus[0] <= e < tenus[1]:
+                assert part.parties[e] == toute.parties[e], f"part of expert {e} differs"
+            else:
+                assert part.parties[e] is None
+
+        # 2. one expert-parallel step on a small dense MoE
+        rng = np.random.default_rng(7)  # the same draw on every rank
+        W, x, r0, idx, w = _moe_dense(rng, 8, 16, 3, 4)
+        residu = torch.from_numpy(r0.copy())
+
+        def local(r, partiel):
+            s = torch.from_numpy(_somme_locale(W, x, idx, w, *tenus))
+            if partiel:
+                r.copy_(s)
+            else:
+                r.add_(s)
+
+        etape_ep(local, residu, rang)
+        attendu = r0 + _somme_locale(W, x, idx, w, 0, 8)
+        assert np.abs(residu.numpy() - attendu).max() <= 1e-6 * max(1.0, np.abs(attendu).max()) * 8
+    finally:
+        dist.destroy_process_group()
+
+
+def test_deux_rangs_gloo():
+    import torch.multiprocessing as mp
+
+    port = _port_libre()
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    mp.start_processes(_travail, args=(2, port), nprocs=2, join=True, start_method="spawn")

@@ -94,7 +94,7 @@ def _charger() -> C.CDLL:
         "trc_comptes_matrice": (i32, [vp, u32, u32, i32, vp]),
         "trc_coder_partie": (i64, [vp, vp, pd, vp, i32, C.c_uint16, C.c_uint16, u32, u32, vp, sz, C.POINTER(u32)]),
         "trc_coder_partie_brute": (i64, [vp, vp, pd, C.c_uint16, C.c_uint16, vp, sz, C.POINTER(u32)]),
-        "trc_synth_matrices": (i32, [u64, u32, u32, u32, vp, vp, i32]),
+        "trc_synth_matrices": (i32, [u64, u32, u32, u32, u32, vp, vp, i32]),
         "trc_moe_espace_octets": (u64, [pd, u32]),
         "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),

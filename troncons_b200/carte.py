@@ -39,7 +39,7 @@ class CoucheCarte:
         self.n = Noyaux()
         E = c.experts
         self.parties, self.adresses, self.tailles = self._monter(c.parties)
-        if brut and c.parties_brutes and c.parties_brutes[0] is not None:
+        if brut and any(p is not None for p in c.parties_brutes):
             self.parties_b, self.adresses_b, self.tailles_b = self._monter(c.parties_brutes)
         else:
             self.parties_b = None

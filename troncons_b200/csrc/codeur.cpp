@@ -354,13 +354,13 @@ int64_t trc_coder_partie_brute(const uint8_t* const* blocs, const uint8_t* const
     return assembler(couche, expert, flux, sortie, capacite, utiles);
 }
 
-int trc_synth_matrices(uint64_t graine, uint32_t lignes, uint32_t colonnes, uint32_t n, uint8_t* blocs, float* biais,
-                       int fils) {
+int trc_synth_matrices(uint64_t graine, uint32_t lignes, uint32_t colonnes, uint32_t premier, uint32_t n,
+                       uint8_t* blocs, float* biais, int fils) {
     if (!blocs || !biais || lignes == 0 || colonnes == 0 || colonnes % 32) return TRC_ERR_USAGE;
     const uint32_t B = colonnes / 32;
     parallele(n * lignes, fils, [&](uint32_t t) {
         const uint32_t x = t / lignes, r = t % lignes;
-        Alea a{graine * 0x9E3779B97F4A7C15ull ^ (uint64_t(x) << 32) ^ r};
+        Alea a{graine * 0x9E3779B97F4A7C15ull ^ (uint64_t(premier + x) << 32) ^ r};
         a.suivant();
         const double sigma = 0.02 * std::exp(0.3 * a.normale());
         uint8_t* ligne = blocs + (size_t(x) * lignes + r) * B * 17;

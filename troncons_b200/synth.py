@@ -24,30 +24,45 @@ def _p(a: np.ndarray) -> int:
     return a.ctypes.data
 
 
-def matrices(graine: int, lignes: int, colonnes: int, n: int, fils: int = 0):
-    """n synthetic MXFP4 matrices: (blocs uint8[n, R*B*17], biais float32[n, R])."""
+def matrices(graine: int, lignes: int, colonnes: int, n: int, fils: int = 0, premier: int = 0):
+    """Synthetic MXFP4 matrices premier .. premier + n - 1: (blocs uint8[n, R*B*17], biais
+    float32[n, R]); matrix x is the same whichever others are drawn with it."""
     B = colonnes // 32
     blocs = np.empty((n, lignes * B * 17), np.uint8)
     biais = np.empty((n, lignes), np.float32)
-    r = lib.trc_synth_matrices(graine, lignes, colonnes, n, _p(blocs), _p(biais), fils)
+    r = lib.trc_synth_matrices(graine, lignes, colonnes, premier, n, _p(blocs), _p(biais), fils)
     if r != 0:
         raise ValueError("synthetic generation refused its arguments")
     return blocs, biais
 
 
-def tables(blocs_j: list, dims: DimsExpert, canonique: bool = True) -> np.ndarray:
-    """The layer's frequency tables u16[3][4][256] from all experts' counts."""
-    freqs = np.zeros((3, 4, 256), np.uint16)
+def comptes(blocs_j: list, dims: DimsExpert, canonique: bool = True) -> np.ndarray:
+    """The symbol counts u64[3][4][256] (DELTA, CODES k = 0, 1, 2 per matrix) of the experts in
+    blocs_j (bins/trc-codeur/src/coder.rs:207-240 counts all experts of a layer)."""
+    c = np.zeros((3, 4, 256), np.uint64)
     for j in range(3):
         R, B = dims.lignes[j], dims.colonnes[j] // 32
-        comptes = np.zeros((4, 256), np.uint64)
+        cj = np.zeros((4, 256), np.uint64)
         for x in range(blocs_j[j].shape[0]):
-            lib.trc_comptes_matrice(_p(blocs_j[j][x]), R, B, int(canonique), _p(comptes))
+            lib.trc_comptes_matrice(_p(blocs_j[j][x]), R, B, int(canonique), _p(cj))
+        c[j] = cj
+    return c
+
+
+def tables_de_comptes(c: np.ndarray) -> np.ndarray:
+    """Frequencies u16[3][4][256] from counts u64[3][4][256]."""
+    freqs = np.zeros((3, 4, 256), np.uint16)
+    for j in range(3):
         for t in range(4):
             f = np.zeros(256, np.uint16)
-            lib.trc_table_depuis_comptes(_p(np.ascontiguousarray(comptes[t])), 1, _p(f))
+            lib.trc_table_depuis_comptes(_p(np.ascontiguousarray(c[j, t])), 1, _p(f))
             freqs[j, t] = f
     return freqs
+
+
+def tables(blocs_j: list, dims: DimsExpert, canonique: bool = True) -> np.ndarray:
+    """The layer's frequency tables u16[3][4][256] from all experts' counts."""
+    return tables_de_comptes(comptes(blocs_j, dims, canonique))
 
 
 def luts(freqs: np.ndarray) -> np.ndarray:
@@ -101,42 +116,55 @@ def coder_partie_brute(blocs3, biais3, dims: DimsExpert, couche: int = 0, expert
 @dataclass
 class Couche:
     """A synthetic MoE layer: E experts (blocks, biases), the layer's tables and LUTs, each
-    expert's v1.2 part and raw part, and a router (f32 [E][C] weights, f32 biases)."""
+    expert's v1.2 part and raw part, and a router (f32 [E][C] weights, f32 biases). When only a
+    share of the experts is held here, `premier` is the first one, blocs / biais hold the share
+    only and the other experts' parts are None."""
 
     dims: DimsExpert
     experts: int
-    blocs: list = field(default_factory=list)    # [j] uint8[E, R*B*17]
-    biais: list = field(default_factory=list)    # [j] float32[E, R]
+    blocs: list = field(default_factory=list)    # [j] uint8[held, R*B*17]
+    biais: list = field(default_factory=list)    # [j] float32[held, R]
     freqs: np.ndarray = None
     luts: np.ndarray = None
     parties: list = field(default_factory=list)
     parties_brutes: list = field(default_factory=list)
     wr: np.ndarray = None
     br: np.ndarray = None
+    premier: int = 0
 
 
 def couche(graine: int, dims: DimsExpert, experts: int, canonique: bool = True, brut: bool = True,
-           n_delta: int = 256, n_codes: int = 256, fils: int = 0) -> Couche:
-    c = Couche(dims=dims, experts=experts)
+           n_delta: int = 256, n_codes: int = 256, fils: int = 0, tenus=None, reduire=None) -> Couche:
+    """A seeded layer. `tenus` = (debut, fin): draw and encode only experts [debut, fin) (an
+    expert-parallel share); `reduire`: a function summing the counts u64[3][4][256] over every
+    share of the layer, so that every share builds the same tables from all experts."""
+    debut, fin = tenus if tenus is not None else (0, experts)
+    c = Couche(dims=dims, experts=experts, premier=debut)
     for j in range(3):
-        bl, bi = matrices(graine * 7 + j, dims.lignes[j], dims.colonnes[j], experts, fils)
+        bl, bi = matrices(graine * 7 + j, dims.lignes[j], dims.colonnes[j], fin - debut, fils, premier=debut)
         c.blocs.append(bl)
         c.biais.append(bi)
-    c.freqs = tables(c.blocs, dims, canonique)
+    cpt = comptes(c.blocs, dims, canonique)
+    if reduire is not None:
+        cpt = np.ascontiguousarray(reduire(cpt), dtype=np.uint64)
+    c.freqs = tables_de_comptes(cpt)
     c.luts = luts(c.freqs)
     nf = fils if fils > 0 else (os.cpu_count() or 1)
 
     def un(x):
         b3 = [c.blocs[j][x] for j in range(3)]
         i3 = [c.biais[j][x] for j in range(3)]
-        p = coder_partie(b3, i3, dims, c.freqs, canonique, 0, x, n_delta, n_codes)
-        q = coder_partie_brute(b3, i3, dims, 0, x) if brut else None
+        p = coder_partie(b3, i3, dims, c.freqs, canonique, 0, debut + x, n_delta, n_codes)
+        q = coder_partie_brute(b3, i3, dims, 0, debut + x) if brut else None
         return p, q
 
     with cf.ThreadPoolExecutor(max_workers=nf) as ex:
-        res = list(ex.map(un, range(experts)))
-    c.parties = [r[0] for r in res]
-    c.parties_brutes = [r[1] for r in res]
+        res = list(ex.map(un, range(fin - debut)))
+    c.parties = [None] * experts
+    c.parties_brutes = [None] * experts
+    for x, (p, q) in enumerate(res):
+        c.parties[debut + x] = p
+        c.parties_brutes[debut + x] = q
     rng = np.random.default_rng(graine)
     c.wr = (rng.standard_normal((experts, dims.colonnes[0])) * 0.02).astype(np.float32)
     c.br = np.zeros(experts, np.float32)
@@ -153,7 +181,7 @@ def slot_attendu(c: Couche, x: int, canonique: bool = True) -> np.ndarray:
     for j in range(3):
         R, Cc = d.lignes[j], d.colonnes[j]
         nb = R * (Cc // 32)
-        bl = c.blocs[j][x].reshape(nb, 17)
+        bl = c.blocs[j][x - c.premier].reshape(nb, 17)
         ech = bl[:, 0]
         qs = bl[:, 1:].reshape(-1)
         if canonique:
@@ -166,6 +194,6 @@ def slot_attendu(c: Couche, x: int, canonique: bool = True) -> np.ndarray:
         pas = (b_off + 4 * R + 255) & ~255
         out[base:base + nb * 16] = qs
         out[base + e_off:base + e_off + nb] = ech
-        out[base + b_off:base + b_off + 4 * R] = c.biais[j][x].view(np.uint8)
+        out[base + b_off:base + b_off + 4 * R] = c.biais[j][x - c.premier].view(np.uint8)
         base += pas
     return out
