@@ -414,6 +414,156 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     if (abandon && voie == 0) atomicAdd(&controle[CTL_ATTENTE], 1u);
 }
 
+// Second form of the same launch, for launches with more tiles than the producer / consumer
+// form keeps in flight (2 x MOE_PAIRES per SM): one warp per tile both decodes and multiplies,
+// DENSE_WARPS warps per block sharing the LUTs, 24 tiles per SM. The product of macro-step m - 1
+// runs in stages between the four sub-steps of macro-step m's decode. Same partials, same bits.
+constexpr uint32_t DENSE_WARPS = 12;
+
+struct DispositionDense {
+    uint32_t anneaux, med, x2, total;
+};
+__host__ __device__ __forceinline__ DispositionDense disposition_dense(const Couche& c) {
+    DispositionDense d;
+    const uint32_t cmax = max(c.colonnes[0], c.colonnes[2]);
+    d.anneaux = 3u * M * 4u;
+    d.med = d.anneaux + DENSE_WARPS * ANNEAU_ALLOC * 2u;
+    d.x2 = d.med + medianes_octets(c);
+    d.total = d.x2 + 4u * ((cmax + 3u) & ~3u);
+    return d;
+}
+
+// A word's quad sum against 2x in three stages: loads and conversions; the fmaf chain; the quad
+// tree (the order of produit_quad + somme_quad).
+struct ProduitEtage {
+    float lo[4], hi[4];
+    float4 xa, xb;
+    float p;
+    template <int K>
+    __device__ __forceinline__ void etape(uint32_t mot, const float4* x2s4, uint32_t b, uint32_t q) {
+        if constexpr (K == 0) {
+            xa = x2s4[8u * b + q];
+            xb = x2s4[8u * b + 4u + q];
+            e2m1_mot(mot, lo, hi);
+        } else if constexpr (K == 1) {
+            float t = 0.0f;
+            t = fmaf(lo[0], xa.x, t);
+            t = fmaf(hi[0], xb.x, t);
+            t = fmaf(lo[1], xa.y, t);
+            t = fmaf(hi[1], xb.y, t);
+            t = fmaf(lo[2], xa.z, t);
+            t = fmaf(hi[2], xb.z, t);
+            t = fmaf(lo[3], xa.w, t);
+            t = fmaf(hi[3], xb.w, t);
+            p = t;
+        } else if constexpr (K == 2) {
+            p = somme_quad(p);
+        }
+    }
+};
+
+__global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const Couche& c = a.c;
+    const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    if (!tenu(c, i)) return;
+    uint32_t* controle = c.controle + 4u * i;
+    const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
+    const uint8_t* partie;
+    uint64_t taille;
+    Flux fc, fm;
+    EnteteRans h;
+    const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+                     R <= 8192u && lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const uint32_t warp0 = blockIdx.x * DENSE_WARPS;
+    if (warp0 >= h.T) return;
+    const DispositionDense dd = disposition_dense(c);
+    uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);
+    uint16_t* anneau = reinterpret_cast<uint16_t*>(dyn + dd.anneaux) + warp * ANNEAU_ALLOC;
+    uint8_t* med = dyn + dd.med;
+    float* x2s = reinterpret_cast<float*>(dyn + dd.x2);
+    copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M),
+             3u * M / 4u);
+    if (fm.p + ((R + 15u) & ~15u) <= partie + taille)
+        copier16(reinterpret_cast<uint4*>(med), reinterpret_cast<const uint4*>(fm.p), (R + 15u) / 16u);
+    else
+        for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
+    if (j < 2) charger_x2(x2s, x_de(c, i), c.x_bf16, C);
+    const uint32_t t0 = warp0 + warp;
+    Decodeur d;
+    if (t0 < h.T) d.debut(h, t0, voie, anneau);  // the part is a layer input: start before the wait
+    attendre_amont();
+    liberer_aval();
+    if (j == 2) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    __syncthreads();
+
+    const uint32_t lut_s = adresse_partagee(lut);
+    const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
+    const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
+    const uint32_t q = voie & 3u, g = voie >> 2;
+    GemvTuile gv;
+    gv.R = R;
+    gv.B = B;
+    gv.K = a.plan.K[j];
+    gv.voie = voie;
+    gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
+    gv.med = med;
+    const uint32_t nmacro = h.P / 128u;
+    uint32_t hors_l = 0, pointeur = 0;
+    for (uint32_t t = t0; t < h.T; t += gridDim.x * DENSE_WARPS) {
+        if (t != t0) d.debut(h, t, voie, anneau);
+        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+        gv.debut(m0);
+        // This lane's block at macro-step m is 8 m + g, column block b; its delta read two
+        // macro-steps ahead.
+        uint32_t bloc = 8u * m0 + g;
+        uint32_t b = bloc % B;
+        uint32_t e0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
+        uint32_t e1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
+        uint32_t mot_p = 0, bloc_p = bloc, b_p = b, e_p = 0;
+        for (uint32_t m = m0; m < m1; ++m) {
+            const uint32_t ctx = bloc < nblocs ? classe_delta(e0) : 0u;
+            const uint32_t e2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
+            d.avancer();
+            uint32_t mot;
+            if (m == m0) {
+                mot = d.macro(lut_s + ctx * (M * 4u));
+            } else {
+                ProduitEtage pe = {};
+                const bool valide_p = bloc_p < nblocs;
+                mot = d.macro(lut_s + ctx * (M * 4u), [&](auto k) {
+                    constexpr int K = decltype(k)::value;
+                    if constexpr (K < 3)
+                        pe.etape<K>(mot_p, x2s4, b_p, q);
+                    else
+                        gv.accumuler(pe.p, bloc_p, e_p, valide_p);
+                });
+                gv.fermer(m - 1u, m1);
+            }
+            mot_p = mot;
+            bloc_p = bloc;
+            b_p = b;
+            e_p = e0;
+            bloc += 8u;
+            b += 8u;
+            b -= b >= B ? B : 0u;
+            e0 = e1;
+            e1 = e2;
+        }
+        gv.accumuler(somme_quad(produit_quad(mot_p, x2s4[8u * b_p + q], x2s4[8u * b_p + 4u + q])), bloc_p, e_p,
+                     bloc_p < nblocs);
+        gv.fermer(m1 - 1u, m1);
+        d.bilan(hors_l, pointeur);
+        d.terminer();
+    }
+    verser_controle(controle, voie, hors_l, pointeur);
+}
+
 // ------------------------------------------------------------------ raw parts: row-centric
 
 __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
@@ -558,18 +708,33 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
         if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, na), dim3(DELTA_WARPS * 32), 0,
                             flux, a)) != cudaSuccess)
             return e;
-        const size_t smem = disposition_codes(c).total;
-        if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem))) != cudaSuccess) return e;
+        // Producer / consumer pairs while the launch's tiles fit them at once (lowest latency per
+        // tile); past that, one warp per tile with three times as many tiles in flight.
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const uint64_t places = uint64_t(sms) * 2u * MOE_PAIRES;
+        auto codes = [&](uint32_t matrices) -> cudaError_t {
+            if (uint64_t(na) * matrices * tc <= places) {
+                const size_t smem = disposition_codes(c).total;
+                cudaError_t e2 = assurer_smem(reinterpret_cast<const void*>(k_moe_codes), int(smem));
+                if (e2 != cudaSuccess) return e2;
+                return lancer_pdl(k_moe_codes, dim3((tc + MOE_PAIRES - 1) / MOE_PAIRES, matrices, na),
+                                  dim3(MOE_PAIRES * 64), smem, flux, a);
+            }
+            const size_t smem = disposition_dense(c).total;
+            cudaError_t e2 = assurer_smem(reinterpret_cast<const void*>(k_moe_codes_dense), int(smem));
+            if (e2 != cudaSuccess) return e2;
+            return lancer_pdl(k_moe_codes_dense, dim3((tc + DENSE_WARPS - 1) / DENSE_WARPS, matrices, na),
+                              dim3(DENSE_WARPS * 32), smem, flux, a);
+        };
         marque(1);
-        const dim3 grille((tc + MOE_PAIRES - 1) / MOE_PAIRES, 2, na);
-        if ((e = lancer_pdl(k_moe_codes, grille, dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess) return e;
+        if ((e = codes(2)) != cudaSuccess) return e;
         marque(2);
         if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_codes, dim3(grille.x, 1, na), dim3(MOE_PAIRES * 64), smem, flux, a)) != cudaSuccess)
-            return e;
+        if ((e = codes(1)) != cudaSuccess) return e;
         marque(4);
     } else {
         const size_t smem = 4u * cmax;
