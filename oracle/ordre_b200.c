@@ -79,28 +79,36 @@ void ord_gemv(const uint8_t* codes, const uint8_t* echelles, const float* biais,
     }
 }
 
-/* Router logits in troncons_b200's order (C a multiple of 4). */
+/* Router logits in troncons_b200's order (C a multiple of 4): per row, the float4 chunks split
+ * into 4 quarters of ceil(C/16) chunks; per quarter, 32 lanes' fmaf chains over chunks
+ * start + lane + 32 i, an xor butterfly; ((q0 + q1) + (q2 + q3)) + bias. */
 void ord_gemv_f32(const float* W, const float* x, const float* biais, uint32_t R, uint32_t C, float* y) {
-    const uint32_t C4 = C / 4;
+    const uint32_t C4 = C / 4, Q = (C4 + 3) / 4;
     for (uint32_t r = 0; r < R; ++r) {
-        float a[32];
-        for (uint32_t l = 0; l < 32; ++l) {
-            float acc = 0.0f;
-            for (uint32_t c = l; c < C4; c += 32) {
-                const float* w = W + (uint64_t)r * C + 4 * c;
-                const float* xx = x + 4 * c;
-                acc = fmaf(w[0], xx[0], acc);
-                acc = fmaf(w[1], xx[1], acc);
-                acc = fmaf(w[2], xx[2], acc);
-                acc = fmaf(w[3], xx[3], acc);
+        float p[4];
+        for (uint32_t q = 0; q < 4; ++q) {
+            const uint32_t c0 = q * Q, c1 = c0 + Q < C4 ? c0 + Q : C4;
+            float a[32];
+            for (uint32_t l = 0; l < 32; ++l) {
+                float acc = 0.0f;
+                for (uint32_t c = c0 + l; c < c1; c += 32) {
+                    const float* w = W + (uint64_t)r * C + 4 * c;
+                    const float* xx = x + 4 * c;
+                    acc = fmaf(w[0], xx[0], acc);
+                    acc = fmaf(w[1], xx[1], acc);
+                    acc = fmaf(w[2], xx[2], acc);
+                    acc = fmaf(w[3], xx[3], acc);
+                }
+                a[l] = acc;
             }
-            a[l] = acc;
+            for (uint32_t d = 16; d > 0; d >>= 1) {
+                float b[32];
+                for (uint32_t l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ d];
+                memcpy(a, b, sizeof a);
+            }
+            p[q] = a[0];
         }
-        for (uint32_t d = 16; d > 0; d >>= 1) {
-            float b[32];
-            for (uint32_t l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ d];
-            memcpy(a, b, sizeof a);
-        }
-        y[r] = biais ? a[0] + biais[r] : a[0];
+        const float s = (p[0] + p[1]) + (p[2] + p[3]);
+        y[r] = biais ? s + biais[r] : s;
     }
 }

@@ -5,8 +5,8 @@
 // MXFP4: one warp per row (row-centric, no cross-warp reduction), the reduction order of
 // mxfp4.cuh, so a slot GEMV gives the bits of the fused path. x is read through L1 (the same
 // x for every row) and doubled in registers.
-// Router: one warp per row; lane l takes float4 chunks l, l+32, ... in an fmaf chain, then an
-// xor butterfly over 16, 8, 4, 2, 1; x may be f32 or bf16 (converted exactly).
+// Router: one block per row, its float4 chunks split in quarters over 4 warps (order at
+// k_gemv_f32); x may be f32 or bf16 (converted exactly).
 #include <cuda_bf16.h>
 
 #include "commun.cuh"
@@ -57,19 +57,24 @@ __device__ __forceinline__ float4 charger_x4(const void* x, uint32_t x_bf16, uin
     return __ldg(reinterpret_cast<const float4*>(x) + c);
 }
 
-__global__ void __launch_bounds__(256) k_gemv_f32(const float* __restrict__ w, const void* __restrict__ x, uint32_t x_bf16,
-                                                  const float* __restrict__ biais, float* __restrict__ y, uint32_t R,
-                                                  uint32_t C) {
+// One block per row, 4 warps: warp q takes the q-th quarter of the row's float4 chunks
+// (Q = ceil(C/16) chunks each), lane l the chunks q Q + l, + 32, ... in an fmaf chain (x, y, z, w);
+// xor butterfly 16 .. 1 in each warp; y = ((p0 + p1) + (p2 + p3)) + b. Every lane's loads (at
+// most 6 float4 for C = 2880) are in flight together.
+constexpr uint32_t F32_QUARTS = 4;
+
+__global__ void __launch_bounds__(F32_QUARTS * 32) k_gemv_f32(const float* __restrict__ w, const void* __restrict__ x,
+                                                             uint32_t x_bf16, const float* __restrict__ biais,
+                                                             float* __restrict__ y, uint32_t R, uint32_t C) {
+    __shared__ float parts[F32_QUARTS];
     attendre_amont();
     liberer_aval();
-    const uint32_t voie = threadIdx.x & 31u;
-    const uint32_t r = blockIdx.x * 8u + (threadIdx.x >> 5);
-    if (r >= R) return;
-    const uint32_t C4 = C / 4u;
+    const uint32_t r = blockIdx.x, voie = threadIdx.x & 31u, q = threadIdx.x >> 5;
+    const uint32_t C4 = C / 4u, Q = (C4 + F32_QUARTS - 1u) / F32_QUARTS, c0 = q * Q, c1 = min(C4, c0 + Q);
     const float4* w4 = reinterpret_cast<const float4*>(w) + uint64_t(r) * C4;
     float acc = 0.0f;
 #pragma unroll 8
-    for (uint32_t c = voie; c < C4; c += 32u) {
+    for (uint32_t c = c0 + voie; c < c1; c += 32u) {
         const float4 a = __ldcs(w4 + c);
         const float4 b = charger_x4(x, x_bf16, c);
         acc = fmaf(a.x, b.x, acc);
@@ -79,7 +84,12 @@ __global__ void __launch_bounds__(256) k_gemv_f32(const float* __restrict__ w, c
     }
 #pragma unroll
     for (int dd = 16; dd > 0; dd >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, dd);
-    if (voie == 0) y[r] = biais != nullptr ? acc + biais[r] : acc;
+    if (voie == 0) parts[q] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0 && r < R) {
+        const float s = (parts[0] + parts[1]) + (parts[2] + parts[3]);
+        y[r] = biais != nullptr ? s + biais[r] : s;
+    }
 }
 
 cudaError_t lancer_gemv(const void* matrice, const float* x, float* y, uint32_t R, uint32_t C, cudaStream_t flux) {
@@ -94,7 +104,7 @@ cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_m
 
 cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
                             uint32_t C, cudaStream_t flux) {
-    return lancer_pdl(k_gemv_f32, dim3((R + 7) / 8), dim3(256), 0, flux, w, x, x_bf16, biais, y, R, C);
+    return lancer_pdl(k_gemv_f32, dim3(R), dim3(F32_QUARTS * 32), 0, flux, w, x, x_bf16, biais, y, R, C);
 }
 
 }  // namespace tb
