@@ -120,6 +120,38 @@ __device__ inline bool trouver_flux(const uint8_t* partie, uint64_t taille, uint
     return false;
 }
 
+// The same lookup by a whole warp: lane l reads descriptors l, l + 32, ... together (one round
+// trip for up to 32 streams, where trouver_flux waits for one descriptor after the other). Every
+// lane of a converged warp calls it with the same arguments and gets the same result.
+__device__ inline bool trouver_flux_warp(const uint8_t* partie, uint64_t taille, uint8_t sorte, uint32_t matrice,
+                                         Flux& f) {
+    const uint32_t voie = threadIdx.x & 31u;
+    const uint4 tete = *reinterpret_cast<const uint4*>(partie);
+    if (tete.x != MAGIE_PARTIE0) return false;
+    if ((tete.z & 0xFFu) != 0) return false;  // level 0
+    const uint32_t n_flux = tete.z >> 16;
+    const uint32_t utiles = tete.w;
+    if (utiles > taille || n_flux > 255u || 64u + 16u * n_flux > utiles) return false;
+    for (uint32_t base = 0; base < n_flux; base += 32u) {
+        const uint32_t i = base + voie;
+        const uint4 e = i < n_flux ? *reinterpret_cast<const uint4*>(partie + 64 + 16 * i) : make_uint4(0u, 0u, 0u, 0u);
+        const bool ok = i < n_flux && (e.x & 0xFFu) == sorte && ((e.x >> 8) & 0xFFu) == matrice;
+        const uint32_t v = __ballot_sync(0xFFFFFFFFu, ok);
+        if (v != 0) {
+            const int src = __ffs(v) - 1;
+            const uint32_t dec = __shfl_sync(0xFFFFFFFFu, e.y, src);
+            const uint32_t lon = __shfl_sync(0xFFFFFFFFu, e.z, src);
+            const uint32_t pro = __shfl_sync(0xFFFFFFFFu, e.w, src);
+            if ((dec & 15u) != 0 || uint64_t(dec) + lon > utiles) return false;
+            f.p = partie + dec;
+            f.longueur = lon;
+            f.produits = pro;
+            return true;
+        }
+    }
+    return false;
+}
+
 // A validated rANS stream header (rans.rs:231-280; commun.cuh:146-165 of the reference).
 struct EnteteRans {
     uint32_t P, N, T, W;

@@ -81,8 +81,8 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
     const uint32_t B = C / 32u, nblocs = R * B;
     Flux fd, fm, fb;
     EnteteRans h;
-    const bool bon = B > 0 && R > 0 && trouver_flux(partie, taille, SORTE_DELTA, j, fd) &&
-                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && trouver_flux(partie, taille, SORTE_BIAIS, j, fb) &&
+    const bool bon = B > 0 && R > 0 && trouver_flux_warp(partie, taille, SORTE_DELTA, j, fd) &&
+                     trouver_flux_warp(partie, taille, SORTE_MEDIANES, j, fm) && trouver_flux_warp(partie, taille, SORTE_BIAIS, j, fb) &&
                      fm.produits == R && fm.longueur >= R && fb.produits == 4u * R && fb.longueur >= 4u * R &&
                      lire_entete(fd, nblocs, h);
     if (!bon) {
@@ -162,8 +162,8 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
     const uint32_t B = C / 32u, nblocs = R * B;
     Flux fc, fm;
     EnteteRans h;
-    const bool bon = B > 0 && R > 0 && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
-                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+    const bool bon = B > 0 && R > 0 && trouver_flux_warp(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                     trouver_flux_warp(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
                      lire_entete(fc, nblocs * 16u, h);
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
@@ -241,8 +241,8 @@ __global__ void __launch_bounds__(256) k_copier_brut(const uint8_t* partie, uint
     const uint32_t R = choisir(dims.lignes, j), C = choisir(dims.colonnes, j);
     const uint32_t B = C / 32u, nblocs = R * B;
     Flux fe, fc, fb;
-    const bool bon = B > 0 && R > 0 && trouver_flux(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
-                     trouver_flux(partie, taille, SORTE_CODES_BRUTS, j, fc) && trouver_flux(partie, taille, SORTE_BIAIS, j, fb) &&
+    const bool bon = B > 0 && R > 0 && trouver_flux_warp(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
+                     trouver_flux_warp(partie, taille, SORTE_CODES_BRUTS, j, fc) && trouver_flux_warp(partie, taille, SORTE_BIAIS, j, fb) &&
                      fe.produits == nblocs && fe.longueur >= nblocs && fc.produits == 16u * nblocs &&
                      fc.longueur >= 16u * nblocs && fb.produits == 4u * R && fb.longueur >= 4u * R;
     if (!bon) {

@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     uint64_t taille;
     Flux fd;
     EnteteRans h;
-    const bool bon = partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_DELTA, j, fd) &&
+    const bool bon = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_DELTA, j, fd) &&
                      lire_entete(fd, nblocs, h);
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
@@ -277,8 +277,8 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     uint64_t taille;
     Flux fc, fm;
     EnteteRans h;
-    const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
-                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+    const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                     trouver_flux_warp(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
                      R <= 8192u && lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
@@ -473,8 +473,8 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     uint64_t taille;
     Flux fc, fm;
     EnteteRans h;
-    const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_CODES_CTX, j, fc) &&
-                     trouver_flux(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
+    const bool bon = B >= 8u && partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                     trouver_flux_warp(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R && fm.longueur >= R &&
                      R <= 8192u && lire_entete(fc, nblocs * 16u, h) && (h.N % SEGMENT_MACRO) == 0;
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
@@ -578,8 +578,8 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
     const uint8_t* partie;
     uint64_t taille;
     Flux fe, fc;
-    const bool bon = B > 0 && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
-                     trouver_flux(partie, taille, SORTE_CODES_BRUTS, j, fc) && fe.produits == nblocs &&
+    const bool bon = B > 0 && partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
+                     trouver_flux_warp(partie, taille, SORTE_CODES_BRUTS, j, fc) && fe.produits == nblocs &&
                      fe.longueur >= nblocs && fc.produits == 16u * nblocs && fc.longueur >= 16u * nblocs;
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
@@ -610,21 +610,21 @@ __device__ __forceinline__ float swiglu_f64(float g, float u) {
 __global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
     __shared__ const float* biais[2];
     const Couche& c = a.c;
-    const uint32_t i = blockIdx.y;
-    attendre_amont();
-    liberer_aval();
+    const uint32_t i = blockIdx.y, warp = threadIdx.x >> 5;
+    // The routed experts were written several kernels back, and the parts are layer inputs:
+    // warp j finds BIAIS_j before the wait (the partials come from the previous kernel).
     if (!tenu(c, i)) return;
-    if (threadIdx.x < 2) {
+    if (warp < 2) {
         const uint8_t* partie;
         uint64_t taille;
         Flux fb;
-        const uint32_t j = threadIdx.x;
-        biais[j] = (partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_BIAIS, j, fb) &&
-                    fb.longueur >= 4u * c.lignes[j])
-                       ? reinterpret_cast<const float*>(fb.p)
-                       : nullptr;
+        const bool ok = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_BIAIS, warp, fb) &&
+                        fb.longueur >= 4u * c.lignes[warp];
+        if ((threadIdx.x & 31u) == 0) biais[warp] = ok ? reinterpret_cast<const float*>(fb.p) : nullptr;
     }
     __syncthreads();
+    attendre_amont();
+    liberer_aval();
     const uint32_t R = c.lignes[0], r = blockIdx.x * 256u + threadIdx.x;
     if (r >= R) return;
     float* h = reinterpret_cast<float*>(a.espace + a.plan.h) + uint64_t(i) * R;
@@ -650,23 +650,27 @@ __global__ void __launch_bounds__(256) k_moe_combiner(ArgsMoe a) {
     __shared__ const float* biais[8];
     __shared__ uint32_t tenus;
     const Couche& c = a.c;
-    const uint32_t b = blockIdx.y, i0 = b * c.k;
-    attendre_amont();
-    liberer_aval();
-    if (threadIdx.x < c.k) {
+    const uint32_t b = blockIdx.y, i0 = b * c.k, warp = threadIdx.x >> 5;
+    // Warp u finds slot u's BIAIS_2 before the wait (the routed experts were written several
+    // kernels back; the down partials come from the previous kernel).
+    if (threadIdx.x == 0) tenus = 0;
+    __syncthreads();
+    if (warp < c.k) {
         const uint8_t* partie;
         uint64_t taille;
         Flux fb;
-        const uint32_t i = i0 + threadIdx.x;
+        const uint32_t i = i0 + warp;
         const bool t = tenu(c, i);
-        biais[threadIdx.x] = (t && partie_de(c, i, partie, taille) && trouver_flux(partie, taille, SORTE_BIAIS, 2, fb) &&
-                              fb.longueur >= 4u * c.lignes[2])
-                                 ? reinterpret_cast<const float*>(fb.p)
-                                 : nullptr;
-        const uint32_t v = __ballot_sync(__activemask(), t);
-        if (threadIdx.x == 0) tenus = v;
+        const bool ok = t && partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_BIAIS, 2, fb) &&
+                        fb.longueur >= 4u * c.lignes[2];
+        if ((threadIdx.x & 31u) == 0) {
+            biais[warp] = ok ? reinterpret_cast<const float*>(fb.p) : nullptr;
+            if (t) atomicOr(&tenus, 1u << warp);
+        }
     }
     __syncthreads();
+    attendre_amont();
+    liberer_aval();
     const uint32_t R = c.lignes[2], r = blockIdx.x * 256u + threadIdx.x;
     if (r >= R) return;
     const uint32_t B = c.colonnes[2] / 32u, K = a.plan.K[2];
