@@ -69,21 +69,24 @@ TRAFIC_CODES_PORTE_HAUT = 34_041_856
 
 
 class Horloges:
-    """SM clock and clock-event reasons of this GPU (found by its UUID) sampled about every
-    millisecond through NVML while the timed region runs (read-only queries; the timed region
-    lasts milliseconds, shorter than nvidia-smi's sampling period)."""
+    """SM clock and clock-event reasons of this GPU (found by its UUID) sampled through NVML
+    while the timed region runs (read-only queries): one sample on entry, one every `periode`
+    seconds, one on exit. NVML queries take the driver's locks, so only one process samples
+    (`actif`), and not faster than needed: CUDA calls of the timed loop must not wait on them."""
 
     RAISONS = [("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
                ("sw_power_cap", 0x4), ("hw_power_brake_slowdown", 0x80)]
 
-    def __init__(self, uuid: str, index: int):
-        self.uuid, self.index = uuid, index
+    def __init__(self, uuid: str, index: int, actif: bool = True, periode: float = 0.02):
+        self.uuid, self.index, self.actif, self.periode = uuid, index, actif, periode
         self.echantillons = []
         self.max_mhz = None
         self.arret = threading.Event()
         self.t = None
 
     def __enter__(self):
+        if not self.actif:
+            return self
         try:
             import pynvml as N
 
@@ -101,9 +104,10 @@ class Horloges:
                                                   N.nvmlDeviceGetCurrentClocksEventReasons(h)))
                     except Exception:
                         return
-                    if self.arret.wait(0.001):
+                    if self.arret.wait(self.periode):
                         return
 
+            self.h, self.N = h, N
             self.echantillons.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
                                       N.nvmlDeviceGetCurrentClocksEventReasons(h)))
             self.t = threading.Thread(target=lire, daemon=True)
@@ -116,6 +120,11 @@ class Horloges:
         self.arret.set()
         if self.t is not None:
             self.t.join(timeout=2)
+            try:
+                self.echantillons.append((self.N.nvmlDeviceGetClockInfo(self.h, self.N.NVML_CLOCK_SM),
+                                          self.N.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+            except Exception:
+                pass
 
     def resume(self):
         if not self.echantillons:
@@ -396,10 +405,13 @@ def bras_ep(args):
     for s in range(args.warmup):
         pas(s)
     torch.cuda.synchronize()
-    dist.barrier()
     t_pas = []
     uuid = str(getattr(torch.cuda.get_device_properties(lr), "uuid", ""))
-    with Horloges(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}", lr) as horl:
+    with Horloges(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}", lr, actif=(r == 0)) as horl:
+        # The sampler starts (NVML initialisation) before the barrier: every rank enters the
+        # timed steps together.
+        dist.barrier()
+        torch.cuda.synchronize()
         for s in range(args.warmup, n_pas):
             pas(s)
             torch.cuda.synchronize()
