@@ -123,6 +123,62 @@ int trc_swiglu_oai(const float* g, size_t g_octets, const float* u, size_t u_oct
 int trc_combiner(float* residu, size_t residu_octets, const float* sorties, size_t sorties_octets, uint32_t pas,
                  const float* poids, size_t poids_octets, uint32_t n, uint32_t d, void* flux);
 
+/* ---------------------------------------------------------------- attention side of a layer */
+
+/* YaRN parameters, 48 bytes, the layout of `abi::ParamsRope` (trc-noyaux/src/abi.rs:228-249):
+ * gpt-oss: base 150000, facteur 32, ctx_origine 4096, beta_rapide 32, beta_lent 1, dim_tete 64. */
+typedef struct trc_params_rope {
+    double base;        /* theta */
+    double facteur;     /* s */
+    double ctx_origine; /* L0 */
+    double beta_rapide;
+    double beta_lent;
+    uint32_t dim_tete;  /* d (even, <= 128) */
+    uint32_t variante;  /* 0: OpenAI's ramp ends; 1: llama.cpp's rounded ends */
+} trc_params_rope;
+
+/* Attention of one position, 32 bytes, the layout of `abi::ParamsAttention` (abi.rs:254-290). */
+typedef struct trc_params_attention {
+    uint32_t tetes;     /* query heads (64) */
+    uint32_t tetes_kv;  /* key / value heads (8) */
+    uint32_t dim_tete;  /* 64 (the only value accepted) */
+    uint32_t debut;     /* first position read */
+    uint32_t fin;       /* current position + 1 */
+    uint32_t anneau;    /* 0: full cache (case = position); else case = position mod anneau */
+    float echelle;      /* 1/sqrt(d) */
+    uint32_t reserve;
+} trc_params_attention;
+
+/* y = W x (+ b), W Q8_0 (ggml blocks of 34 bytes: f16 d, 32 x i8), rows of colonnes/32 blocks,
+ * W 16-aligned; x f32 16-aligned; `biais` may be NULL. Replaces `Noyaux::gemv_q8_0`
+ * (lib.rs:291-305; passe.cuh:57-97, 222-231), bit for bit: per lane l, blocks l, l + 32, ...;
+ * in a block an fmaf chain over the 32 codes, then fmaf(d, s, acc); xor butterfly; + b. */
+int trc_gemv_q8_0(const void* w, size_t w_octets, const float* x, size_t x_octets, const float* biais,
+                  size_t biais_octets, float* y, size_t y_octets, uint32_t lignes, uint32_t colonnes, void* flux);
+
+/* RMSNorm of `lignes` vectors of n: y = x w / sqrt(sum x^2 / n + eps), sums in f64 (fixed tree
+ * over 256 threads), y rounded once; y may be x. Replaces `Noyaux::rmsnorm` (lib.rs:322-330). */
+int trc_rmsnorm(const float* x, size_t x_octets, const float* w, size_t w_octets, float* y, size_t y_octets, uint32_t n,
+                uint32_t lignes, float eps, void* flux);
+
+/* YaRN rotation (NEOX halves) of q (tetes_q heads) and k (tetes_k heads) in place at `position`,
+ * angle, sine, cosine and rotation in f64. Replaces `Noyaux::rope_yarn` (lib.rs:334-345). */
+int trc_rope_yarn(float* q, size_t q_octets, float* k, size_t k_octets, uint32_t tetes_q, uint32_t tetes_k,
+                  uint32_t position, const trc_params_rope* p, void* flux);
+
+/* k, v (f32[dkv]) into case `case_kv` of a layer's f16 caches ([case][kv head][d], round to
+ * nearest even). Replaces `Noyaux::ecrire_kv` (lib.rs:348-358). */
+int trc_ecrire_kv(const float* k, size_t k_octets, const float* v, size_t v_octets, uint16_t* cache_k,
+                  size_t cache_k_octets, uint16_t* cache_v, size_t cache_v_octets, uint32_t dkv, uint32_t case_kv,
+                  void* flux);
+
+/* Decode attention of one position, every query head, over the cases `p` describes, the head's
+ * sink (`puits` f32[tetes]) in the softmax's denominator; sortie f32[tetes * 64]. At most 8,192
+ * positions. Replaces `Noyaux::attention` (lib.rs:362-380; passe.cuh:316-371). */
+int trc_attention(const float* q, size_t q_octets, const uint16_t* cache_k, size_t cache_k_octets, const uint16_t* cache_v,
+                  size_t cache_v_octets, const float* puits, size_t puits_octets, float* sortie, size_t sortie_octets,
+                  const trc_params_attention* p, void* flux);
+
 /* ---------------------------------------------------------------- host helpers (no device) */
 
 /* Normalises counts to 12-bit frequencies summing to 4096 (trc-codec/src/rans.rs:83-127);

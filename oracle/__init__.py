@@ -65,6 +65,13 @@ def _charger() -> C.CDLL:
         "orc_decoder_matrice_v10": (C.c_int, [P8, C.c_size_t, C.c_uint8, C.c_uint32, C.c_uint32, P32, P8, P8, PF, C.POINTER(Bilan), C.POINTER(Bilan)]),
         "orc_decoder_expert": (C.c_int, [P8, C.c_size_t, P32, P32, P32, P8, P32]),
         "orc_disposition": (None, [C.c_uint32, C.c_uint32, P64, P64, P64]),
+        "orc_f16_depuis_f32": (None, [PF, P16, C.c_uint64]),
+        "orc_f32_depuis_f16": (None, [P16, PF, C.c_uint64]),
+        "orc_gemv_q8_0": (None, [P8, PF, PF, C.c_uint32, C.c_uint32, PF]),
+        "orc_rmsnorm": (None, [PF, PF, PF, C.c_uint32, C.c_uint32, C.c_float]),
+        "orc_rope_yarn": (None, [PF, PF, C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
+        "orc_ecrire_kv": (None, [PF, PF, P16, P16, C.c_uint32, C.c_uint32]),
+        "orc_attention": (None, [PF, P16, P16, PF, PF, C.c_void_p, PF]),
         "orc_gemv_f64": (None, [P8, P8, PF, PD, C.c_uint32, C.c_uint32, PD]),
         "orc_routeur_topk": (None, [PF, C.c_uint32, C.c_uint32, P32, PF]),
         "orc_swiglu": (None, [PF, PF, PF, C.c_uint32]),
@@ -296,6 +303,59 @@ def couche_moe_cpu(parties, luts, lignes, colonnes, Wr, br, x, k: int, residu, n
     return res, idx, w
 
 
+# ---------------------------------------------------------------- attention side (passe.cuh)
+
+def f16(x) -> np.ndarray:
+    """f32 -> binary16 bits, round to nearest even."""
+    a = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.zeros(a.size, np.uint16)
+    lib.orc_f16_depuis_f32(p(a, PF), p(out, P16), a.size)
+    return out
+
+
+def gemv_q8_0(W, x, biais, R: int, C_: int) -> np.ndarray:
+    w = np.ascontiguousarray(W, dtype=np.uint8).reshape(-1)
+    xf = np.ascontiguousarray(x, dtype=np.float32)
+    bi = None if biais is None else np.ascontiguousarray(biais, dtype=np.float32)
+    y = np.zeros(R, np.float32)
+    lib.orc_gemv_q8_0(p(w, P8), p(xf, PF), p(bi, PF) if bi is not None else None, R, C_, p(y, PF))
+    return y
+
+
+def rmsnorm(x, w, n: int, lignes: int, eps: float) -> np.ndarray:
+    xf = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    wf = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.zeros_like(xf)
+    lib.orc_rmsnorm(p(xf, PF), p(wf, PF), p(y, PF), n, lignes, eps)
+    return y
+
+
+def rope_yarn(q, k, tetes_q: int, tetes_k: int, position: int, params) -> tuple:
+    """params: a ctypes structure with the layout of trc_params_rope."""
+    qf = np.array(q, dtype=np.float32, copy=True).reshape(-1)
+    kf = np.array(k, dtype=np.float32, copy=True).reshape(-1)
+    lib.orc_rope_yarn(p(qf, PF), p(kf, PF), tetes_q, tetes_k, position, C.addressof(params))
+    return qf, kf
+
+
+def ecrire_kv(k, v, cache_k, cache_v, dkv: int, case_kv: int) -> None:
+    kf = np.ascontiguousarray(k, dtype=np.float32)
+    vf = np.ascontiguousarray(v, dtype=np.float32)
+    lib.orc_ecrire_kv(p(kf, PF), p(vf, PF), p(cache_k, P16), p(cache_v, P16), dkv, case_kv)
+
+
+def attention(q, cache_k, cache_v, puits, params) -> np.ndarray:
+    """params: a ctypes structure with the layout of trc_params_attention."""
+    qf = np.ascontiguousarray(q, dtype=np.float32)
+    ck = np.ascontiguousarray(cache_k, dtype=np.uint16)
+    cv = np.ascontiguousarray(cache_v, dtype=np.uint16)
+    pf = np.ascontiguousarray(puits, dtype=np.float32)
+    out = np.zeros(params.tetes * 64, np.float32)
+    scores = np.zeros(max(params.fin - params.debut, 1), np.float32)
+    lib.orc_attention(p(qf, PF), p(ck, P16), p(cv, P16), p(pf, PF), p(out, PF), C.addressof(params), p(scores, PF))
+    return out
+
+
 def ref():
     """The reference's own CUDA kernels (oracle/_ref/libtrc_ref.so), or None when absent."""
     if not os.path.exists(_REF):
@@ -312,6 +372,11 @@ def ref():
         "ref_routeur_topk": [vp, C.c_uint32, C.c_uint32, vp, vp, vp],
         "ref_swiglu": [vp, vp, vp, C.c_uint32, vp],
         "ref_combiner": [vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint32, vp],
+        "ref_gemv_q8_0": [vp, vp, vp, vp, C.c_uint32, C.c_uint32, vp],
+        "ref_rmsnorm": [vp, vp, vp, C.c_uint32, C.c_uint32, C.c_float, vp],
+        "ref_rope_yarn": [vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp, vp],
+        "ref_ecrire_kv": [vp, vp, vp, vp, C.c_uint32, C.c_uint32, vp],
+        "ref_attention": [vp, vp, vp, vp, vp, vp, vp],
     }.items():
         f = getattr(r, nom)
         f.restype = C.c_int

@@ -89,3 +89,34 @@ extern "C" int ref_combiner(float* residu, const float* sorties, uint32_t pas, c
     combiner<<<(d + 255) / 256, 256, 0, (cudaStream_t)flux>>>(residu, sorties, pas, poids, n, d);
     return (int)cudaGetLastError();
 }
+
+// ---- the attention side (passe.cuh:222-371), with the reference's grids (lib.rs:291-381)
+
+extern "C" int ref_gemv_q8_0(const void* W, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                             void* flux) {
+    gemv_q8_0<<<(R + 31) / 32, 256, 0, (cudaStream_t)flux>>>((const uint8_t*)W, x, biais, y, R, C);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ref_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t lignes, float eps, void* flux) {
+    rmsnorm<<<lignes, 256, 0, (cudaStream_t)flux>>>(x, w, y, n, eps);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ref_rope_yarn(float* q, float* k, uint32_t tetes_q, uint32_t tetes_k, uint32_t position,
+                             const trc::ParamsRope* p, void* flux) {
+    rope_yarn<<<tetes_q + tetes_k, p->dim_tete / 2, 0, (cudaStream_t)flux>>>(q, k, tetes_q, tetes_k, position, *p);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ref_ecrire_kv(const float* k, const float* v, unsigned short* ck, unsigned short* cv, uint32_t dkv,
+                             uint32_t case_kv, void* flux) {
+    ecrire_kv<<<(dkv + 255) / 256, 256, 0, (cudaStream_t)flux>>>(k, v, ck, cv, dkv, case_kv);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ref_attention(const float* q, const unsigned short* ck, const unsigned short* cv, const float* puits,
+                             float* sortie, const trc::ParamsAttention* p, void* flux) {
+    attention<<<p->tetes, 256, 4 * (p->fin - p->debut), (cudaStream_t)flux>>>(q, ck, cv, puits, sortie, *p);
+    return (int)cudaGetLastError();
+}

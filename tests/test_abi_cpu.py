@@ -2,7 +2,7 @@
 
 - the library loads and exports every function include/troncons_b200.h declares;
 - the header's structs have the reference's frozen sizes (DimsExpert 24 B, DescGemv 32 B,
-  DescDecodage 32 B: trc-noyaux/src/abi.rs:305-313) and the Python mirrors have the header's
+  DescDecodage 32 B, ParamsRope 48 B, ParamsAttention 32 B: trc-noyaux/src/abi.rs:305-323) and the Python mirrors have the header's
   layout, field by field (a C program compiled against the header prints sizeof / offsetof);
 - bad sizes, shapes and alignments are refused with TRC_ERR_USAGE and a message, before
   anything is launched, as `Noyaux` refuses them with `Erreur::Usage`
@@ -44,6 +44,8 @@ _STRUCTS = {
     "trc_desc_gemv": (T.DescGemv, 32),
     "trc_desc_decodage": (T.DescDecodage, 32),
     "trc_moe_couche": (T.MoeCouche, None),
+    "trc_params_rope": (T.ParamsRope, 48),
+    "trc_params_attention": (T.ParamsAttention, 32),
 }
 
 
@@ -139,3 +141,21 @@ def test_espace_grandit_avec_k():
     e = [T.espace_octets(d, k) for k in range(1, 9)]
     assert all(b > a for a, b in zip(e, e[1:]))
     assert e[3] == 3_432_960 and e[7] == 6_865_920
+
+
+def test_refus_attention():
+    import troncons_b200 as T2
+
+    p = T2.ParamsAttention.gpt_oss(300, 128)
+    p.dim_tete = 32
+    v = C.c_void_p(4096)
+    assert T.lib.trc_attention(v, 1 << 20, v, 1 << 20, v, 1 << 20, v, 1 << 20, v, 1 << 20, C.byref(p), None) == T.TRC_ERR_USAGE
+    p = T2.ParamsAttention.gpt_oss(300, 128)
+    p.debut = 0  # 301 positions in a ring of 128 cases
+    assert T.lib.trc_attention(v, 1 << 20, v, 1 << 20, v, 1 << 20, v, 1 << 20, v, 1 << 20, C.byref(p), None) == T.TRC_ERR_USAGE
+    assert "ring" in _erreur()
+    r = T2.ParamsRope.gpt_oss()
+    r.dim_tete = 65
+    assert T.lib.trc_rope_yarn(v, 1 << 20, v, 1 << 20, 64, 8, 0, C.byref(r), None) == T.TRC_ERR_USAGE
+    # a KV case past the cache
+    assert T.lib.trc_ecrire_kv(v, 2048, v, 2048, v, 1024, v, 1024, 512, 1, None) == T.TRC_ERR_USAGE

@@ -58,6 +58,33 @@ class DescDecodage(C.Structure):
     _fields_ = [("partie", C.c_uint64), ("emplacement", C.c_uint64), ("luts", C.c_uint64), ("controle", C.c_uint64)]
 
 
+class ParamsRope(C.Structure):
+    """trc_params_rope (48 bytes; abi.rs:228-249)."""
+
+    _fields_ = [("base", C.c_double), ("facteur", C.c_double), ("ctx_origine", C.c_double),
+                ("beta_rapide", C.c_double), ("beta_lent", C.c_double), ("dim_tete", C.c_uint32),
+                ("variante", C.c_uint32)]
+
+    @classmethod
+    def gpt_oss(cls) -> "ParamsRope":
+        return cls(150000.0, 32.0, 4096.0, 32.0, 1.0, 64, 0)
+
+
+class ParamsAttention(C.Structure):
+    """trc_params_attention (32 bytes; abi.rs:254-290)."""
+
+    _fields_ = [("tetes", C.c_uint32), ("tetes_kv", C.c_uint32), ("dim_tete", C.c_uint32), ("debut", C.c_uint32),
+                ("fin", C.c_uint32), ("anneau", C.c_uint32), ("echelle", C.c_float), ("reserve", C.c_uint32)]
+
+    @classmethod
+    def gpt_oss(cls, position: int, fenetre: int) -> "ParamsAttention":
+        """Position `position` of a gpt-oss layer: sliding (fenetre = 128, the even layers) or full
+        (fenetre = 0) (abi.rs:278-283)."""
+        fin = position + 1
+        debut = max(0, fin - fenetre) if fenetre > 0 else 0
+        return cls(64, 8, 64, debut, fin, fenetre, 0.125, 0)
+
+
 class MoeCouche(C.Structure):
     """The fused MoE layer descriptor (trc_moe_couche)."""
 
@@ -99,6 +126,11 @@ def _charger() -> C.CDLL:
         "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
         "trc_moe_couche_sans_alloc": (i32, [C.POINTER(MoeCouche), vp]),
+        "trc_gemv_q8_0": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
+        "trc_rmsnorm": (i32, [vp, sz, vp, sz, vp, sz, u32, u32, C.c_float, vp]),
+        "trc_rope_yarn": (i32, [vp, sz, vp, sz, u32, u32, u32, C.POINTER(ParamsRope), vp]),
+        "trc_ecrire_kv": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
+        "trc_attention": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, vp, sz, C.POINTER(ParamsAttention), vp]),
         "trc_routeur": (i32, [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, vp]),
     }
     for nom, (res, args) in sig.items():
@@ -221,6 +253,33 @@ class Noyaux:
         else:
             ev = (C.c_void_p * 6)(*[int(v) if v else None for v in evenements])
             verifier(lib.trc_moe_couche_chrono(C.byref(desc), e.adresse, e.octets, _flux(flux), ev))
+
+    # ---------------------------------------------------------------- attention side
+
+    def gemv_q8_0(self, w, x, biais, y, lignes: int, colonnes: int, flux=None) -> None:
+        wv, xv, bv, yv = _v(w), _v(x), _v(biais), _v(y)
+        verifier(lib.trc_gemv_q8_0(wv.adresse, wv.octets, xv.adresse, xv.octets, bv.adresse or None, bv.octets,
+                                   yv.adresse, yv.octets, lignes, colonnes, _flux(flux)))
+
+    def rmsnorm(self, x, w, y, n: int, lignes: int, eps: float, flux=None) -> None:
+        xv, wv, yv = _v(x), _v(w), _v(y)
+        verifier(lib.trc_rmsnorm(xv.adresse, xv.octets, wv.adresse, wv.octets, yv.adresse, yv.octets, n, lignes, eps,
+                                 _flux(flux)))
+
+    def rope_yarn(self, q, k, tetes_q: int, tetes_k: int, position: int, p: ParamsRope, flux=None) -> None:
+        qv, kv = _v(q), _v(k)
+        verifier(lib.trc_rope_yarn(qv.adresse, qv.octets, kv.adresse, kv.octets, tetes_q, tetes_k, position,
+                                   C.byref(p), _flux(flux)))
+
+    def ecrire_kv(self, k, v, cache_k, cache_v, dkv: int, case_kv: int, flux=None) -> None:
+        a, b, ck, cv = _v(k), _v(v), _v(cache_k), _v(cache_v)
+        verifier(lib.trc_ecrire_kv(a.adresse, a.octets, b.adresse, b.octets, ck.adresse, ck.octets, cv.adresse,
+                                   cv.octets, dkv, case_kv, _flux(flux)))
+
+    def attention(self, q, cache_k, cache_v, puits, sortie, p: ParamsAttention, flux=None) -> None:
+        qv, ck, cv, pv, sv = _v(q), _v(cache_k), _v(cache_v), _v(puits), _v(sortie)
+        verifier(lib.trc_attention(qv.adresse, qv.octets, ck.adresse, ck.octets, cv.adresse, cv.octets, pv.adresse,
+                                   pv.octets, sv.adresse, sv.octets, C.byref(p), _flux(flux)))
 
     def moe_couche_sans_alloc(self, desc: MoeCouche, flux=None) -> None:
         """The fused layer on the library's fixed 8 MiB device workspace (no workspace argument,

@@ -284,6 +284,80 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
                                  reinterpret_cast<cudaEvent_t const*>(evenements)));
 }
 
+// ---------------------------------------------------------------- attention side (lib.rs:291-381)
+
+int trc_gemv_q8_0(const void* w, size_t w_octets, const float* x, size_t x_octets, const float* biais,
+                  size_t biais_octets, float* y, size_t y_octets, uint32_t lignes, uint32_t colonnes, void* flux) {
+    if (lignes == 0 || colonnes == 0 || colonnes % 32 != 0) return usage("shape %u x %u", lignes, colonnes);
+    if (colonnes > 16384) return usage("%u columns (16,384 at most)", colonnes);
+    const uint64_t octets = uint64_t(lignes) * (colonnes / 32) * 34;
+    if (w == nullptr || w_octets < octets || !aligne(w, 16))
+        return usage("Q8_0 matrix of %zu bytes, %llu needed (16-aligned)", w_octets, (unsigned long long)octets);
+    if (x == nullptr || x_octets < 4ull * colonnes || !aligne(x, 16)) return usage("x too short or not aligned on 16");
+    if (y == nullptr || y_octets < 4ull * lignes) return usage("y too short");
+    if (biais != nullptr && biais_octets < 4ull * lignes) return usage("bias too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_gemv_q8_0(w, x, biais, y, lignes, colonnes, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_rmsnorm(const float* x, size_t x_octets, const float* w, size_t w_octets, float* y, size_t y_octets, uint32_t n,
+                uint32_t lignes, float eps, void* flux) {
+    if (n == 0 || lignes == 0) return usage("rmsnorm of %u x %u", lignes, n);
+    const uint64_t o = 4ull * n * lignes;
+    if (x == nullptr || y == nullptr || w == nullptr || x_octets < o || y_octets < o || w_octets < 4ull * n)
+        return usage("rmsnorm: views too short");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_rmsnorm(x, w, y, n, lignes, eps, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_rope_yarn(float* q, size_t q_octets, float* k, size_t k_octets, uint32_t tetes_q, uint32_t tetes_k,
+                  uint32_t position, const trc_params_rope* p, void* flux) {
+    if (p == nullptr) return usage("rope parameters absent");
+    if (p->dim_tete == 0 || p->dim_tete % 2 != 0 || p->dim_tete > 128) return usage("head dimension %u", p->dim_tete);
+    if (p->variante > 1) return usage("YaRN variant %u", p->variante);
+    const uint64_t d = p->dim_tete;
+    if ((tetes_q && (q == nullptr || q_octets < 4 * d * tetes_q)) || (tetes_k && (k == nullptr || k_octets < 4 * d * tetes_k)))
+        return usage("rope: views too short");
+    if (tetes_q + tetes_k == 0) return TRC_OK;
+    tb::ParamsRope r{p->base, p->facteur, p->ctx_origine, p->beta_rapide, p->beta_lent, p->dim_tete, p->variante};
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_rope_yarn(q, k, tetes_q, tetes_k, position, r, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_ecrire_kv(const float* k, size_t k_octets, const float* v, size_t v_octets, uint16_t* cache_k,
+                  size_t cache_k_octets, uint16_t* cache_v, size_t cache_v_octets, uint32_t dkv, uint32_t case_kv,
+                  void* flux) {
+    if (dkv == 0) return usage("dkv is 0");
+    const uint64_t fin = 2ull * (uint64_t(case_kv) + 1) * dkv;
+    if (k == nullptr || v == nullptr || k_octets < 4ull * dkv || v_octets < 4ull * dkv) return usage("k or v too short");
+    if (cache_k == nullptr || cache_v == nullptr || cache_k_octets < fin || cache_v_octets < fin)
+        return usage("case %u outside the cache", case_kv);
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_ecrire_kv(k, v, cache_k, cache_v, dkv, case_kv, static_cast<cudaStream_t>(flux)));
+}
+
+int trc_attention(const float* q, size_t q_octets, const uint16_t* cache_k, size_t cache_k_octets, const uint16_t* cache_v,
+                  size_t cache_v_octets, const float* puits, size_t puits_octets, float* sortie, size_t sortie_octets,
+                  const trc_params_attention* p, void* flux) {
+    if (p == nullptr) return usage("attention parameters absent");
+    if (p->dim_tete != 64 || p->tetes_kv == 0 || p->tetes % p->tetes_kv != 0)
+        return usage("heads %u / %u of dimension %u", p->tetes, p->tetes_kv, p->dim_tete);
+    if (p->fin < p->debut || p->fin - p->debut > 8192) return usage("positions [%u, %u)", p->debut, p->fin);
+    if (p->anneau != 0 && p->fin - p->debut > p->anneau) return usage("more positions than cases in the ring");
+    const uint64_t cases = p->anneau ? p->anneau : p->fin;
+    const uint64_t dkv = uint64_t(p->tetes_kv) * 64;
+    if (cache_k == nullptr || cache_v == nullptr || cache_k_octets < 2 * cases * dkv || cache_v_octets < 2 * cases * dkv)
+        return usage("cache too short");
+    if (!aligne(cache_k, 16)) return usage("key cache not aligned on 16");
+    if (q == nullptr || sortie == nullptr || puits == nullptr || q_octets < 256ull * p->tetes ||
+        sortie_octets < 256ull * p->tetes || puits_octets < 4ull * p->tetes)
+        return usage("attention: views too short");
+    if (p->tetes == 0 || p->fin == p->debut) return TRC_OK;
+    tb::ParamsAttention a{p->tetes, p->tetes_kv, p->dim_tete, p->debut, p->fin, p->anneau, p->echelle, p->reserve};
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_attention(q, cache_k, cache_v, puits, sortie, a, static_cast<cudaStream_t>(flux)));
+}
+
 int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts, uint32_t colonnes,
                 uint32_t k, float* logits, uint32_t* indices, float* poids, void* flux) {
     if (experts == 0 || experts > 256 || k == 0 || k > 8 || k > experts) return usage("top-%u of %u", k, experts);

@@ -1,0 +1,299 @@
+// troncons_b200 — the attention side of a gpt-oss layer at batch 1: Q8_0 GEMV, RMSNorm, YaRN
+// rotation, KV-cache write, attention of one position with sinks and the sliding window (the
+// reference's passe.cuh kernels gemv_q8_0, rmsnorm, rope_yarn, ecrire_kv, attention, launched by
+// `Noyaux` in trc-noyaux/src/lib.rs:291-381).
+//
+// Each kernel keeps the reference's arithmetic order, element by element, so that its outputs
+// are bit-identical to the reference kernels' on the same GPU (the same CUDA math functions,
+// called, not restated); the memory side is this library's own:
+//   k_gemv_q8_0   a warp per row stages the row's 34-byte blocks (C/32 of them, rows 2-aligned
+//                 only) with coalesced 16-byte loads into shared memory, and x once per block;
+//                 lane l then takes blocks l, l + 32, ... : s = sum_i q_i x_i (fmaf chain, i in
+//                 order), acc = fmaf(d, s, acc); xor butterfly 16 .. 1; + bias (passe.cuh:57-97);
+//   k_rmsnorm     per thread, the f64 fma chain of squares over i = t, t + 256, ...; fixed tree
+//                 over 256; y = x r w in f64 rounded once (passe.cuh:250-272);
+//   k_rope_yarn   NEOX halves, YaRN inv_freq and concentration in f64 (the published YaRN
+//                 formula, passe.cuh:146-169, 280-301);
+//   k_ecrire_kv   f32 -> f16 round-to-nearest-even into the position's case (passe.cuh:305-314);
+//   k_attention   one query head per block: scores (fmaf chain over d, then x 1/sqrt(d)), max with
+//                 the head's sink, exp, z = tree sum + exp(sink - m), values by 4 groups of
+//                 positions j = g mod 4 in order, ((g0 + g1) + (g2 + g3)) / z (passe.cuh:316-371).
+#include <cuda_fp16.h>
+
+#include "commun.cuh"
+#include "noyaux.h"
+
+namespace tb {
+
+__device__ __forceinline__ float f16_f32(uint32_t bits) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits))); }
+
+// ------------------------------------------------------------------ Q8_0 GEMV
+
+constexpr uint32_t Q8_BLOC = 34;       // f16 d, then 32 x i8 (ggml's block_q8_0)
+constexpr uint32_t Q8_WARPS = 8;
+
+__host__ __device__ __forceinline__ uint32_t q8_tampon(uint32_t C) {
+    return ((C / 32u) * Q8_BLOC + 16u + 15u) & ~15u;  // a row plus its 16-byte misalignment
+}
+
+__global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __restrict__ W, const float* __restrict__ x,
+                                                           const float* __restrict__ biais, float* __restrict__ y,
+                                                           uint32_t R, uint32_t C) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const uint32_t voie = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t B = C / 32u, octets = B * Q8_BLOC, tampon = q8_tampon(C);
+    float* xs = reinterpret_cast<float*>(dyn);
+    uint8_t* ligne = dyn + 4u * C + warp * tampon;
+    attendre_amont();
+    liberer_aval();
+    for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x)
+        reinterpret_cast<float4*>(xs)[t] = __ldg(reinterpret_cast<const float4*>(x) + t);
+    __syncthreads();
+    for (uint32_t r = blockIdx.x * Q8_WARPS + warp; r < R; r += gridDim.x * Q8_WARPS) {
+        const uint64_t debut = uint64_t(r) * octets;
+        const uint64_t a0 = debut & ~uint64_t(15);
+        const uint32_t dec = uint32_t(debut - a0);
+        const uint32_t n16 = (dec + octets + 15u) / 16u;
+        // The row's bytes, 16 at a time from the 16-byte boundary at or below its start (W is
+        // 16-aligned: the host checks it); the first and last chunks may hold bytes of the
+        // neighbouring rows, and bytes past the matrix are never read.
+        const uint64_t fin_mat = uint64_t(R) * octets;
+        for (uint32_t i = voie; i < n16; i += 32u) {
+            const uint64_t a = a0 + 16u * i;
+            uint4 v;
+            if (a + 16u <= fin_mat) {
+                v = __ldcs(reinterpret_cast<const uint4*>(W + a));
+            } else {
+                uint32_t o[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    if (a + k < fin_mat) o[k >> 2] |= uint32_t(W[a + k]) << (8 * (k & 3));
+                v = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+            *reinterpret_cast<uint4*>(ligne + 16u * i) = v;
+        }
+        __syncwarp();
+        float acc = 0.0f;
+        for (uint32_t b = voie; b < B; b += 32u) {
+            const uint16_t* blk = reinterpret_cast<const uint16_t*>(ligne + dec + b * Q8_BLOC);
+            const float d = f16_f32(blk[0]);
+            const float* xv = xs + 32u * b;
+            float s = 0.0f;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+                const uint32_t w = blk[1 + t];
+                s = fmaf(float(int8_t(w & 0xFFu)), xv[2 * t], s);
+                s = fmaf(float(int8_t(w >> 8)), xv[2 * t + 1], s);
+            }
+            acc = fmaf(d, s, acc);
+        }
+#pragma unroll
+        for (int dd = 16; dd > 0; dd >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, dd);
+        if (voie == 0) y[r] = biais != nullptr ? acc + biais[r] : acc;
+        __syncwarp();
+    }
+}
+
+// ------------------------------------------------------------------ RMSNorm
+
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, float* y,
+                                                 uint32_t n, float eps) {
+    __shared__ double part[256];
+    attendre_amont();
+    liberer_aval();
+    const uint32_t t = threadIdx.x;
+    const float* xr = x + uint64_t(blockIdx.x) * n;
+    float* yr = y + uint64_t(blockIdx.x) * n;
+    double s = 0.0;
+    for (uint32_t i = t; i < n; i += 256u) {
+        const double v = xr[i];
+        s = fma(v, v, s);
+    }
+    part[t] = s;
+    __syncthreads();
+#pragma unroll
+    for (uint32_t k = 128; k > 0; k >>= 1) {
+        if (t < k) part[t] += part[t + k];
+        __syncthreads();
+    }
+    const double r = 1.0 / sqrt(part[0] / double(n) + double(eps));
+    // y may be x: each thread writes only the elements it read itself.
+    for (uint32_t i = t; i < n; i += 256u) yr[i] = float(double(xr[i]) * r * double(w[i]));
+}
+
+// ------------------------------------------------------------------ YaRN rotation
+
+// YaRN (Peng et al., 2023) for pair i of a head of dimension d: frequency base^(2i/d); the
+// ramp between the pair indices where a rotation makes beta_fast and beta_slow turns over the
+// original context decides between the interpolated 1/(s f) and the extrapolated 1/f; the
+// attention concentration is 0.1 ln(s) + 1. `variante` 1 rounds the ramp's ends (floor / ceil,
+// clamped), as llama.cpp does.
+__device__ inline double yarn_inv_freq(const ParamsRope& p, uint32_t i, double& concentration) {
+    const uint32_t demi = p.dim_tete / 2u;
+    const double freq = pow(p.base, double(2u * i) / double(p.dim_tete));
+    if (p.facteur <= 1.0) {
+        concentration = 1.0;
+        return 1.0 / freq;
+    }
+    concentration = 0.1 * log(p.facteur) + 1.0;
+    const double deux_pi = 6.283185307179586476925286766559;
+    double bas = double(demi) * log(p.ctx_origine / (p.beta_rapide * deux_pi)) / log(p.base);
+    double haut = double(demi) * log(p.ctx_origine / (p.beta_lent * deux_pi)) / log(p.base);
+    if (p.variante == 1u) {
+        bas = fmax(floor(bas), 0.0);
+        haut = fmin(ceil(haut), double(p.dim_tete - 1u));
+    }
+    const double interpolation = 1.0 / (p.facteur * freq);
+    const double extrapolation = 1.0 / freq;
+    const double rampe = fmin(fmax((double(i) - bas) / (haut - bas), 0.0), 1.0);
+    const double masque = 1.0 - rampe;
+    return interpolation * (1.0 - masque) + extrapolation * masque;
+}
+
+__global__ void __launch_bounds__(64) k_rope_yarn(float* __restrict__ q, float* __restrict__ k, uint32_t tetes_q,
+                                                  uint32_t tetes_k, uint32_t position, ParamsRope p) {
+    attendre_amont();
+    liberer_aval();
+    const uint32_t demi = p.dim_tete / 2u, i = threadIdx.x;
+    if (i >= demi || blockIdx.x >= tetes_q + tetes_k) return;
+    double m;
+    const double inv = yarn_inv_freq(p, i, m);
+    double s, c;
+    sincos(double(position) * inv, &s, &c);
+    c *= m;
+    s *= m;
+    float* v = blockIdx.x < tetes_q ? q + uint64_t(blockIdx.x) * p.dim_tete : k + uint64_t(blockIdx.x - tetes_q) * p.dim_tete;
+    const double a = v[i], b = v[i + demi];
+    v[i] = float(a * c - b * s);
+    v[i + demi] = float(b * c + a * s);
+}
+
+// ------------------------------------------------------------------ KV cache
+
+__global__ void __launch_bounds__(256) k_ecrire_kv(const float* __restrict__ k, const float* __restrict__ v,
+                                                   uint16_t* __restrict__ cache_k, uint16_t* __restrict__ cache_v,
+                                                   uint32_t dkv, uint32_t case_kv) {
+    attendre_amont();
+    liberer_aval();
+    const uint32_t i = blockIdx.x * 256u + threadIdx.x;
+    if (i >= dkv) return;
+    const uint64_t o = uint64_t(case_kv) * dkv + i;
+    cache_k[o] = __half_as_ushort(__float2half_rn(k[i]));
+    cache_v[o] = __half_as_ushort(__float2half_rn(v[i]));
+}
+
+// ------------------------------------------------------------------ attention of one position
+
+constexpr uint32_t ATT_FILS = 256;
+constexpr uint32_t ATT_DIM = 64;
+
+template <bool MAX>
+__device__ __forceinline__ float arbre_bloc(float* part, float v) {
+    const uint32_t t = threadIdx.x;
+    part[t] = v;
+    __syncthreads();
+#pragma unroll
+    for (uint32_t k = ATT_FILS / 2; k > 0; k >>= 1) {
+        if (t < k) part[t] = MAX ? fmaxf(part[t], part[t + k]) : part[t] + part[t + k];
+        __syncthreads();
+    }
+    const float r = part[0];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(ATT_FILS) k_attention(const float* __restrict__ q, const uint16_t* __restrict__ cache_k,
+                                                        const uint16_t* __restrict__ cache_v, const float* __restrict__ puits,
+                                                        float* __restrict__ sortie, ParamsAttention p) {
+    extern __shared__ float scores[];
+    __shared__ float qs[ATT_DIM];
+    __shared__ float part[ATT_FILS];
+    __shared__ float groupes[4][ATT_DIM];
+    attendre_amont();
+    liberer_aval();
+    const uint32_t t = threadIdx.x, h = blockIdx.x;
+    const uint32_t hk = h / (p.tetes / p.tetes_kv);
+    const uint32_t dkv = p.tetes_kv * ATT_DIM;
+    const uint32_t n = p.fin - p.debut;
+    if (t < ATT_DIM) qs[t] = q[uint64_t(h) * ATT_DIM + t];
+    __syncthreads();
+    for (uint32_t j = t; j < n; j += ATT_FILS) {
+        const uint32_t pos = p.debut + j;
+        const uint32_t c = p.anneau ? pos % p.anneau : pos;
+        const uint4* kr = reinterpret_cast<const uint4*>(cache_k + uint64_t(c) * dkv + uint64_t(hk) * ATT_DIM);
+        uint4 w[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) w[b] = __ldg(kr + b);
+        float s = 0.0f;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const uint32_t mots[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                s = fmaf(qs[8 * b + 2 * u], f16_f32(mots[u] & 0xFFFFu), s);
+                s = fmaf(qs[8 * b + 2 * u + 1], f16_f32(mots[u] >> 16), s);
+            }
+        }
+        scores[j] = s * p.echelle;
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (uint32_t j = t; j < n; j += ATT_FILS) m = fmaxf(m, scores[j]);
+    const float puits_h = puits[h];
+    m = fmaxf(arbre_bloc<true>(part, m), puits_h);
+    float z = 0.0f;
+    for (uint32_t j = t; j < n; j += ATT_FILS) {
+        const float e = expf(scores[j] - m);
+        scores[j] = e;
+        z += e;
+    }
+    z = arbre_bloc<false>(part, z) + expf(puits_h - m);
+    const uint32_t dd = t & (ATT_DIM - 1u), g = t / ATT_DIM;
+    float a = 0.0f;
+    for (uint32_t j = g; j < n; j += 4u) {
+        const uint32_t pos = p.debut + j;
+        const uint32_t c = p.anneau ? pos % p.anneau : pos;
+        a = fmaf(scores[j], f16_f32(__ldg(cache_v + uint64_t(c) * dkv + uint64_t(hk) * ATT_DIM + dd)), a);
+    }
+    groupes[g][dd] = a;
+    __syncthreads();
+    if (t < ATT_DIM)
+        sortie[uint64_t(h) * ATT_DIM + t] = ((groupes[0][t] + groupes[1][t]) + (groupes[2][t] + groupes[3][t])) / z;
+}
+
+// ------------------------------------------------------------------ launchers
+
+cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                             cudaStream_t flux) {
+    const size_t smem = 4u * C + Q8_WARPS * q8_tampon(C);
+    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_q8_0), int(smem));
+    if (e != cudaSuccess) return e;
+    const uint32_t blocs = std::min<uint32_t>((R + Q8_WARPS - 1) / Q8_WARPS, 148u * 8u);
+    return lancer_pdl(k_gemv_q8_0, dim3(blocs), dim3(Q8_WARPS * 32), smem, flux, static_cast<const uint8_t*>(w), x, biais,
+                      y, R, C);
+}
+
+cudaError_t lancer_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t lignes, float eps,
+                           cudaStream_t flux) {
+    return lancer_pdl(k_rmsnorm, dim3(lignes), dim3(256), 0, flux, x, w, y, n, eps);
+}
+
+cudaError_t lancer_rope_yarn(float* q, float* k, uint32_t tetes_q, uint32_t tetes_k, uint32_t position, const ParamsRope& p,
+                             cudaStream_t flux) {
+    return lancer_pdl(k_rope_yarn, dim3(tetes_q + tetes_k), dim3(p.dim_tete / 2u), 0, flux, q, k, tetes_q, tetes_k, position, p);
+}
+
+cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t dkv, uint32_t case_kv,
+                             cudaStream_t flux) {
+    return lancer_pdl(k_ecrire_kv, dim3((dkv + 255) / 256), dim3(256), 0, flux, k, v, ck, cv, dkv, case_kv);
+}
+
+cudaError_t lancer_attention(const float* q, const uint16_t* ck, const uint16_t* cv, const float* puits, float* sortie,
+                             const ParamsAttention& p, cudaStream_t flux) {
+    const size_t smem = 4u * (p.fin - p.debut);
+    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_attention), int(smem));
+    if (e != cudaSuccess) return e;
+    return lancer_pdl(k_attention, dim3(p.tetes), dim3(ATT_FILS), smem, flux, q, ck, cv, puits, sortie, p);
+}
+
+}  // namespace tb

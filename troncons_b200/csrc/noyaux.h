@@ -67,6 +67,27 @@ cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, c
                             cudaStream_t flux);
 cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEvent_t const* ev = nullptr);
 
+// Attention side (mirrors of trc_params_rope, 48 bytes, and trc_params_attention, 32 bytes).
+struct ParamsRope {
+    double base, facteur, ctx_origine, beta_rapide, beta_lent;
+    uint32_t dim_tete, variante;
+};
+struct ParamsAttention {
+    uint32_t tetes, tetes_kv, dim_tete, debut, fin, anneau;
+    float echelle;
+    uint32_t reserve;
+};
+cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                             cudaStream_t flux);
+cudaError_t lancer_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t lignes, float eps,
+                           cudaStream_t flux);
+cudaError_t lancer_rope_yarn(float* q, float* k, uint32_t tetes_q, uint32_t tetes_k, uint32_t position, const ParamsRope& p,
+                             cudaStream_t flux);
+cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t dkv, uint32_t case_kv,
+                             cudaStream_t flux);
+cudaError_t lancer_attention(const float* q, const uint16_t* ck, const uint16_t* cv, const float* puits, float* sortie,
+                             const ParamsAttention& p, cudaStream_t flux);
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 cudaError_t assurer_smem(const void* noyau, int octets);
 
