@@ -6,8 +6,9 @@
 // Each kernel keeps the reference's arithmetic order, element by element, so that its outputs
 // are bit-identical to the reference kernels' on the same GPU (the same CUDA math functions,
 // called, not restated); the memory side is this library's own:
-//   k_gemv_q8_0   a warp per row stages the row's 34-byte blocks (C/32 of them, rows 2-aligned
-//                 only) with coalesced 16-byte loads into shared memory, and x once per block;
+//   k_gemv_q8_0   persistent warps stage rows of 34-byte blocks (C/32 of them, rows 2-aligned
+//                 only) with coalesced 16-byte cp.async into shared memory, the next row while
+//                 the current one is multiplied; x is staged once per block;
 //                 lane l then takes blocks l, l + 32, ... : s = sum_i q_i x_i (fmaf chain, i in
 //                 order), acc = fmaf(d, s, acc); xor butterfly 16 .. 1; + bias (passe.cuh:57-97);
 //   k_rmsnorm     per thread, the f64 fma chain of squares over i = t, t + 256, ...; fixed tree
@@ -32,8 +33,25 @@ __device__ __forceinline__ float f16_f32(uint32_t bits) { return __half2float(__
 constexpr uint32_t Q8_BLOC = 34;       // f16 d, then 32 x i8 (ggml's block_q8_0)
 constexpr uint32_t Q8_WARPS = 8;
 
+// Shared bytes of the padded x (one word per 32), rounded to 16 so the row buffers stay aligned.
+__host__ __device__ __forceinline__ uint32_t q8_x_octets(uint32_t C) { return (4u * (C + C / 32u) + 15u) & ~15u; }
+
 __host__ __device__ __forceinline__ uint32_t q8_tampon(uint32_t C) {
     return ((C / 32u) * Q8_BLOC + 16u + 15u) & ~15u;  // a row plus its 16-byte misalignment
+}
+
+// Copies a row's bytes [debut, debut + octets) of W (16-aligned) into `ligne` as 16-byte chunks
+// from the boundary at or below `debut`, asynchronously (cp.async; bytes past the matrix read 0).
+__device__ __forceinline__ void q8_charger_ligne(uint8_t* ligne, const uint8_t* W, uint64_t debut, uint32_t octets,
+                                                 uint64_t fin_mat, uint32_t voie) {
+    const uint64_t a0 = debut & ~uint64_t(15);
+    const uint32_t n16 = uint32_t((debut - a0) + octets + 15u) / 16u;
+    for (uint32_t i = voie; i < n16; i += 32u) {
+        const uint64_t a = a0 + 16u * i;
+        const uint64_t reste = a >= fin_mat ? 0u : fin_mat - a;
+        const uint32_t utiles = reste < 16u ? uint32_t(reste) : 16u;
+        cp_async16(ligne + 16u * i, utiles ? W + a : W, utiles);
+    }
 }
 
 __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __restrict__ W, const float* __restrict__ x,
@@ -42,42 +60,42 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __re
     extern __shared__ __align__(16) uint8_t dyn[];
     const uint32_t voie = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t B = C / 32u, octets = B * Q8_BLOC, tampon = q8_tampon(C);
-    float* xs = reinterpret_cast<float*>(dyn);
-    uint8_t* ligne = dyn + 4u * C + warp * tampon;
+    float* xs = reinterpret_cast<float*>(dyn);                     // [C + C / 32]
+    uint8_t* lignes = dyn + q8_x_octets(C) + warp * 2u * tampon;  // two row buffers per warp
+    const uint64_t fin_mat = uint64_t(R) * octets;
+    const uint32_t pas = gridDim.x * Q8_WARPS;
+    uint32_t r = blockIdx.x * Q8_WARPS + warp;
+    // The weights are an input of the call: the first row is requested before the wait.
+    if (r < R) q8_charger_ligne(lignes, W, uint64_t(r) * octets, octets, fin_mat, voie);
+    cp_async_commit();
     attendre_amont();
     liberer_aval();
-    for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x)
-        reinterpret_cast<float4*>(xs)[t] = __ldg(reinterpret_cast<const float4*>(x) + t);
+    // x padded by one word per 32 (xs[c + c / 32]): lane l reads x[32 b + i] for b = l, l + 32,
+    // ..., so unpadded all 32 lanes would hit one shared-memory bank.
+    for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + t);
+        const uint32_t c = 4u * t, o = c + c / 32u;
+        xs[o] = v.x;
+        xs[o + 1] = v.y;
+        xs[o + 2] = v.z;
+        xs[o + 3] = v.w;
+    }
     __syncthreads();
-    for (uint32_t r = blockIdx.x * Q8_WARPS + warp; r < R; r += gridDim.x * Q8_WARPS) {
-        const uint64_t debut = uint64_t(r) * octets;
-        const uint64_t a0 = debut & ~uint64_t(15);
-        const uint32_t dec = uint32_t(debut - a0);
-        const uint32_t n16 = (dec + octets + 15u) / 16u;
-        // The row's bytes, 16 at a time from the 16-byte boundary at or below its start (W is
-        // 16-aligned: the host checks it); the first and last chunks may hold bytes of the
-        // neighbouring rows, and bytes past the matrix are never read.
-        const uint64_t fin_mat = uint64_t(R) * octets;
-        for (uint32_t i = voie; i < n16; i += 32u) {
-            const uint64_t a = a0 + 16u * i;
-            uint4 v;
-            if (a + 16u <= fin_mat) {
-                v = __ldcs(reinterpret_cast<const uint4*>(W + a));
-            } else {
-                uint32_t o[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    if (a + k < fin_mat) o[k >> 2] |= uint32_t(W[a + k]) << (8 * (k & 3));
-                v = make_uint4(o[0], o[1], o[2], o[3]);
-            }
-            *reinterpret_cast<uint4*>(ligne + 16u * i) = v;
-        }
+    for (uint32_t n = 0; r < R; r += pas, ++n) {
+        // The next row goes into the other buffer while this one is multiplied.
+        const uint32_t rs = r + pas;
+        if (rs < R) q8_charger_ligne(lignes + ((n + 1u) & 1u) * tampon, W, uint64_t(rs) * octets, octets, fin_mat, voie);
+        cp_async_commit();
+        cp_async_wait<1>();
         __syncwarp();
+        const uint8_t* ligne = lignes + (n & 1u) * tampon;
+        const uint64_t debut = uint64_t(r) * octets;
+        const uint32_t dec = uint32_t(debut - (debut & ~uint64_t(15)));
         float acc = 0.0f;
         for (uint32_t b = voie; b < B; b += 32u) {
             const uint16_t* blk = reinterpret_cast<const uint16_t*>(ligne + dec + b * Q8_BLOC);
             const float d = f16_f32(blk[0]);
-            const float* xv = xs + 32u * b;
+            const float* xv = xs + 33u * b;
             float s = 0.0f;
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
@@ -90,8 +108,9 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __re
 #pragma unroll
         for (int dd = 16; dd > 0; dd >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, dd);
         if (voie == 0) y[r] = biais != nullptr ? acc + biais[r] : acc;
-        __syncwarp();
+        __syncwarp();  // this buffer is refilled two rows from now
     }
+    cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -223,7 +242,7 @@ __global__ void __launch_bounds__(ATT_FILS) k_attention(const float* __restrict_
         const uint4* kr = reinterpret_cast<const uint4*>(cache_k + uint64_t(c) * dkv + uint64_t(hk) * ATT_DIM);
         uint4 w[8];
 #pragma unroll
-        for (int b = 0; b < 8; ++b) w[b] = __ldg(kr + b);
+        for (int b = 0; b < 8; ++b) w[b] = kr[b];
         float s = 0.0f;
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
@@ -249,11 +268,25 @@ __global__ void __launch_bounds__(ATT_FILS) k_attention(const float* __restrict_
     }
     z = arbre_bloc<false>(part, z) + expf(puits_h - m);
     const uint32_t dd = t & (ATT_DIM - 1u), g = t / ATT_DIM;
+    const uint16_t* vcol = cache_v + uint64_t(hk) * ATT_DIM + dd;
     float a = 0.0f;
-    for (uint32_t j = g; j < n; j += 4u) {
+    uint32_t j = g;
+    // Eight positions' values loaded before their (ordered) fmaf chain.
+    for (; j + 28u < n; j += 32u) {
+        float vv[8];
+#pragma unroll
+        for (uint32_t u = 0; u < 8u; ++u) {
+            const uint32_t pos = p.debut + j + 4u * u;
+            const uint32_t c = p.anneau ? pos % p.anneau : pos;
+            vv[u] = f16_f32(vcol[uint64_t(c) * dkv]);
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 8u; ++u) a = fmaf(scores[j + 4u * u], vv[u], a);
+    }
+    for (; j < n; j += 4u) {
         const uint32_t pos = p.debut + j;
         const uint32_t c = p.anneau ? pos % p.anneau : pos;
-        a = fmaf(scores[j], f16_f32(__ldg(cache_v + uint64_t(c) * dkv + uint64_t(hk) * ATT_DIM + dd)), a);
+        a = fmaf(scores[j], f16_f32(vcol[uint64_t(c) * dkv]), a);
     }
     groupes[g][dd] = a;
     __syncthreads();
@@ -265,10 +298,13 @@ __global__ void __launch_bounds__(ATT_FILS) k_attention(const float* __restrict_
 
 cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
                              cudaStream_t flux) {
-    const size_t smem = 4u * C + Q8_WARPS * q8_tampon(C);
+    const size_t smem = q8_x_octets(C) + Q8_WARPS * 2u * q8_tampon(C);
     cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_q8_0), int(smem));
     if (e != cudaSuccess) return e;
-    const uint32_t blocs = std::min<uint32_t>((R + Q8_WARPS - 1) / Q8_WARPS, 148u * 8u);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t par_sm = std::max<uint32_t>(1u, std::min<uint32_t>(4u, uint32_t(200000 / smem)));
+    const uint32_t blocs = std::min<uint32_t>((R + Q8_WARPS - 1) / Q8_WARPS, uint32_t(sms) * par_sm);
     return lancer_pdl(k_gemv_q8_0, dim3(blocs), dim3(Q8_WARPS * 32), smem, flux, static_cast<const uint8_t*>(w), x, biais,
                       y, R, C);
 }
