@@ -147,7 +147,15 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
 
 // ------------------------------------------------------------------ shared-memory x2 = 2 x
 
-// x2s[0..C) = 2 x, x bf16 or f32 (C a multiple of 32); 16-byte loads when x is 16-aligned.
+// 2x in shared memory, padded: the 8 float4 of 32-column block b (x2[32 b + 4 k .. + 3], k = 0..7)
+// at float4 index 12 b + k. A quarter-warp's 8 lanes read one float4 each from two neighbouring
+// blocks; 12 float4 (192 bytes) per block put those blocks 16 banks apart, where 8 (128 bytes)
+// would put them on the same banks.
+constexpr uint32_t X2_PAS = 12;
+__host__ __device__ __forceinline__ uint32_t x2_octets(uint32_t C) { return (C / 32u) * X2_PAS * 16u; }
+__device__ __forceinline__ uint32_t x2_indice(uint32_t i) { return X2_PAS * (i / 8u) + (i % 8u); }  // float4 i of 2x
+
+// The padded 2x of x (bf16 or f32, C a multiple of 32); 16-byte loads when x is 16-aligned.
 __device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t bf16, uint32_t C) {
     float4* d4 = reinterpret_cast<float4*>(x2s);
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
@@ -155,23 +163,20 @@ __device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t b
             const uint4* s4 = static_cast<const uint4*>(x);
             for (uint32_t t = threadIdx.x; t < C / 8u; t += blockDim.x) {
                 const uint4 v = __ldg(s4 + t);
-                d4[2u * t] = make_float4(2.0f * __uint_as_float(v.x << 16), 2.0f * __uint_as_float(v.x & 0xFFFF0000u),
-                                         2.0f * __uint_as_float(v.y << 16), 2.0f * __uint_as_float(v.y & 0xFFFF0000u));
-                d4[2u * t + 1u] = make_float4(2.0f * __uint_as_float(v.z << 16), 2.0f * __uint_as_float(v.z & 0xFFFF0000u),
-                                              2.0f * __uint_as_float(v.w << 16), 2.0f * __uint_as_float(v.w & 0xFFFF0000u));
+                d4[x2_indice(2u * t)] = make_float4(2.0f * __uint_as_float(v.x << 16), 2.0f * __uint_as_float(v.x & 0xFFFF0000u),
+                                                    2.0f * __uint_as_float(v.y << 16), 2.0f * __uint_as_float(v.y & 0xFFFF0000u));
+                d4[x2_indice(2u * t + 1u)] = make_float4(2.0f * __uint_as_float(v.z << 16), 2.0f * __uint_as_float(v.z & 0xFFFF0000u),
+                                                         2.0f * __uint_as_float(v.w << 16), 2.0f * __uint_as_float(v.w & 0xFFFF0000u));
             }
         } else {
             const float4* s4 = static_cast<const float4*>(x);
-            for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x) d4[t] = fois2(__ldg(s4 + t));
+            for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x) d4[x2_indice(t)] = fois2(__ldg(s4 + t));
         }
         return;
     }
-    if (bf16) {
-        const uint16_t* xb = static_cast<const uint16_t*>(x);
-        for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) x2s[t] = 2.0f * __uint_as_float(uint32_t(xb[t]) << 16);
-    } else {
-        const float* xf = static_cast<const float*>(x);
-        for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) x2s[t] = 2.0f * xf[t];
+    for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) {
+        const float v = bf16 ? __uint_as_float(uint32_t(static_cast<const uint16_t*>(x)[t]) << 16) : static_cast<const float*>(x)[t];
+        x2s[4u * x2_indice(t / 4u) + (t % 4u)] = 2.0f * v;
     }
 }
 
@@ -258,7 +263,7 @@ __host__ __device__ __forceinline__ DispositionCodes disposition_codes(const Cou
     d.deltas = d.mots + MOE_PAIRES * SEG_TAMPONS * SEG_MOTS * 4u;
     d.med = d.deltas + MOE_PAIRES * SEG_TAMPONS * SEG_DELTAS;
     d.x2 = d.med + medianes_octets(c);
-    d.barrieres = d.x2 + 4u * ((cmax + 3u) & ~3u);
+    d.barrieres = d.x2 + x2_octets(cmax);
     d.total = d.barrieres + MOE_PAIRES * 2u * SEG_TAMPONS * 8u;
     return d;
 }
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
                         const bool ok = m + u < s1;
                         const uint32_t mot = ok ? mb[(m + u - s0) * 32u + voie] : 0u;
                         dv[u] = ok ? uint32_t(db[(m + u - s0) * 8u + g]) : 0u;
-                        sv[u] = somme_quad(produit_quad(mot, x2s4[8u * bc + q], x2s4[8u * bc + 4u + q]));
+                        sv[u] = somme_quad(produit_quad(mot, x2s4[X2_PAS * bc + q], x2s4[X2_PAS * bc + 4u + q]));
                         bc += 8u;
                         bc -= bc >= B ? B : 0u;
                     }
@@ -429,7 +434,7 @@ __host__ __device__ __forceinline__ DispositionDense disposition_dense(const Cou
     d.anneaux = 3u * M * 4u;
     d.med = d.anneaux + DENSE_WARPS * ANNEAU_ALLOC * 2u;
     d.x2 = d.med + medianes_octets(c);
-    d.total = d.x2 + 4u * ((cmax + 3u) & ~3u);
+    d.total = d.x2 + x2_octets(cmax);
     return d;
 }
 
@@ -442,8 +447,8 @@ struct ProduitEtage {
     template <int K>
     __device__ __forceinline__ void etape(uint32_t mot, const float4* x2s4, uint32_t b, uint32_t q) {
         if constexpr (K == 0) {
-            xa = x2s4[8u * b + q];
-            xb = x2s4[8u * b + 4u + q];
+            xa = x2s4[X2_PAS * b + q];
+            xb = x2s4[X2_PAS * b + 4u + q];
             e2m1_mot(mot, lo, hi);
         } else if constexpr (K == 1) {
             float t = 0.0f;
@@ -555,7 +560,7 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
             e0 = e1;
             e1 = e2;
         }
-        gv.accumuler(somme_quad(produit_quad(mot_p, x2s4[8u * b_p + q], x2s4[8u * b_p + 4u + q])), bloc_p, e_p,
+        gv.accumuler(somme_quad(produit_quad(mot_p, x2s4[X2_PAS * b_p + q], x2s4[X2_PAS * b_p + 4u + q])), bloc_p, e_p,
                      bloc_p < nblocs);
         gv.fermer(m1 - 1u, m1);
         d.bilan(hors_l, pointeur);
@@ -592,7 +597,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
         charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
     const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
-    auto x2f4 = [x2s4](uint32_t t) { return x2s4[t]; };
+    auto x2f4 = [x2s4](uint32_t t) { return x2s4[x2_indice(t)]; };
     const uint32_t K = a.plan.K[j];
     float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
     for (uint32_t r = blockIdx.x * MOE_WARPS + (threadIdx.x >> 5); r < R; r += gridDim.x * MOE_WARPS)
@@ -741,7 +746,7 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
         if ((e = codes(1)) != cudaSuccess) return e;
         marque(4);
     } else {
-        const size_t smem = 4u * cmax;
+        const size_t smem = x2_octets(cmax);
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_brut), int(smem))) != cudaSuccess) return e;
         const uint32_t rmax = std::max(c.lignes[0], c.lignes[2]);
         const uint32_t gx = (rmax + MOE_WARPS - 1) / MOE_WARPS;
