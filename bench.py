@@ -47,6 +47,8 @@ def arguments():
     a.add_argument("--n-delta", type=int, default=256, help="macro-steps per DELTA tile the parts are encoded with")
     a.add_argument("--n-codes", type=int, default=256, help="macro-steps per CODES_CTX tile")
     a.add_argument("--no-cpu-baseline", action="store_true")
+    a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
+                   help="N > 1: the combine's exchange in the combine kernel over NVLink (pairs) or by NCCL")
     return a.parse_args()
 
 
@@ -358,7 +360,7 @@ def bras_ep(args):
     c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=False, n_delta=args.n_delta,
                  n_codes=args.n_codes, tenus=partage(args.experts, r, w), reduire=reduire_comptes(device=dev))
     t_gen = time.time() - t0
-    ep = CoucheEP(c, r, w, k=args.k, jetons=jetons)
+    ep = CoucheEP(c, r, w, k=args.k, jetons=jetons, echange=args.echange)
     C0, R2 = c.dims.colonnes[0], c.dims.lignes[2]
     n_pas = args.warmup + args.steps
     rng = np.random.default_rng(args.graine)  # the same tokens on every rank
@@ -374,16 +376,19 @@ def bras_ep(args):
     idx_journal = torch.zeros(n_pas, jetons * args.k, dtype=torch.int32, device="cuda")
     partiel = r != 0
 
-    # The rank's local step (router of the N tokens + its fused share) is captured in a CUDA
-    # graph; the all-reduce is issued after each replay.
+    # The step is captured in a CUDA graph: with the "pairs" exchange the whole step (router,
+    # fused share, combine and exchange in one kernel); with "nccl", the local part, and the
+    # all-reduce is issued after each replay.
+    paires = ep.echange == "pairs"
     x_buf.copy_(xs_dev[0])
     residu.copy_(res_dev[0])
     for _ in range(3):
-        ep.local(x_buf, residu, partiel)
+        ep.etape(x_buf, residu) if paires else ep.local(x_buf, residu, partiel)
     torch.cuda.synchronize()
+    dist.barrier()
     graphe = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graphe):
-        ep.local(x_buf, residu, partiel)
+        ep.etape(x_buf, residu) if paires else ep.local(x_buf, residu, partiel)
     torch.cuda.synchronize()
 
     def pas(s, hote=False):
@@ -396,7 +401,8 @@ def bras_ep(args):
             x_buf.copy_(xs_dev[s])
             residu.copy_(res_dev[s])
         graphe.replay()
-        dist.all_reduce(residu, op=dist.ReduceOp.SUM)
+        if not paires:
+            dist.all_reduce(residu, op=dist.ReduceOp.SUM)
         if hote:
             res_sortie[s].copy_(residu, non_blocking=True)
         ev[1].record()
@@ -460,14 +466,15 @@ def bras_ep(args):
         "config": {
             "workload": f"config 3: expert-parallel gpt-oss-120b MoE layer, {args.experts} experts "
                         f"({fin - debut} per GPU), top-{args.k}, batch {jetons} tokens (one per GPU), x bf16[2880], "
-                        "router f32 replicated, combine by NCCL all-reduce of the batch's f32 residual",
+                        "router f32 replicated, " + ("combine and its exchange in one kernel over NVLink peer "
+                        "memory" if paires else "combine by NCCL all-reduce of the batch's f32 residual"),
             "experts": args.experts, "k": args.k, "tokens_per_step": jetons, "n_delta": args.n_delta,
             "n_codes": args.n_codes, "l2": "flushed between steps (256 MB written)",
-            "bytes_per_step": round(octets_tous / args.steps), "parallelism": f"ep{w}",
+            "bytes_per_step": round(octets_tous / args.steps), "parallelism": f"ep{w}", "exchange": ep.echange,
         },
         "e2e": {"value": round(octets_tous / (t_e2e_ms * 1e-3) / 1e9, 2), "unit": UNITE,
                 "h2d_bytes_per_step": jetons * (2 * C0 + 4 * R2), "d2h_bytes_per_step": jetons * 4 * R2},
-        "gpu_launches": args.steps * (2 * jetons + 5),
+        "gpu_launches": args.steps * (2 * jetons + 5),  # the all-reduce (nccl) is NCCL's
         "roofline": None,
         "clocks": clocks,
         "generation_s": round(t_gen, 1),

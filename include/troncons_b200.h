@@ -261,7 +261,27 @@ typedef struct trc_moe_couche {
     uint32_t expert_fin;            /* others are skipped, no error (expert_fin = 0: all are held) */
     uint32_t partiel;               /* 1: residu[b] = this call's weighted sum over its held
                                        activations (0 when none), for a sum across GPUs; 0: residu += */
+    const struct trc_echange_pairs* echange; /* host pointer or NULL: the combine's sum across
+                                       GPUs done by the combine kernel itself over peer memory */
 } trc_moe_couche;
+
+/* The combine's exchange between the GPUs of an expert-parallel layer, in the combine kernel:
+ * each rank's combine writes its share of every token's weighted sum into its slot of every
+ * rank's exchange buffer (peer stores over NVLink), raises a flag there, waits for every rank's
+ * flag on its own buffer (bounded: a wait that gives up counts in controle[3] of activation 0
+ * and leaves the residual unchanged), then adds the shares in rank order: every rank ends with
+ * the same residual, bit for bit. The buffers are one per rank, of trc_echange_octets bytes,
+ * mapped in every rank's address space (e.g. symmetric memory), zeroed once before the first
+ * call; every rank calls the layer the same number of times, with the same tokens. */
+typedef struct trc_echange_pairs {
+    uint64_t tampons[8];  /* device addresses, in this process, of the exchange buffers of ranks
+                             0 .. monde-1 (tampons[rang] is this rank's own) */
+    uint32_t rang;        /* this rank */
+    uint32_t monde;       /* ranks (2 .. 8) */
+} trc_echange_pairs;
+
+/* Bytes of one rank's exchange buffer for these dimensions, tokens per call and ranks. */
+uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32_t monde);
 
 /* Workspace bytes the fused layer needs for these dimensions and k activations (tokens times
  * routed experts per token; device memory the caller allocates once and reuses; contents need no

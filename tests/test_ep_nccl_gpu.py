@@ -1,11 +1,14 @@
-"""GPU, two or more devices: the expert-parallel layer over NCCL against the single-GPU layer.
+"""GPU, two or more devices: the expert-parallel layer against the single-GPU layer.
 
 Two ranks (one process per GPU) each draw and encode only their half of a layer's experts,
 build the layer's tables from the counts summed over NCCL, then run expert-parallel steps on a
-batch of 2 tokens: router on every rank, the fused layer on the rank's share (rank 0 adds into
-the residual, rank 1 writes its share alone), one SUM all-reduce. Rank 0 also runs the whole
-layer on one GPU; the two agree within 1e-5 max|residual| (the same terms summed in another
-order) and route the same experts. Skipped with fewer than two GPUs."""
+batch of 2 tokens: router on every rank, the fused layer on the rank's share, and the combine's
+exchange, either NCCL (rank 0 adds into the residual, rank 1 writes its share alone, one SUM
+all-reduce) or "pairs" (the combine kernel writes its share into every rank's symmetric buffer
+over NVLink and sums the shares in rank order itself). Rank 0 also runs the whole layer on one
+GPU; they agree within 1e-5 max|residual| (the same terms summed in another order) and route
+the same experts. With "pairs" both ranks hold the same residual bits, step after step, also
+when the step is replayed from a CUDA graph. Skipped with fewer than two GPUs."""
 import os
 import socket
 from datetime import timedelta
@@ -25,7 +28,7 @@ def _port_libre() -> int:
     return p
 
 
-def _rang(rang, monde, port):
+def _rang(rang, monde, port, echange="nccl"):
     import torch.distributed as dist
 
     import troncons_b200 as T
@@ -41,7 +44,7 @@ def _rang(rang, monde, port):
     try:
         dims = T.DimsExpert.de([256, 256, 512], [512, 512, 256])
         part = S.couche(77, dims, 8, brut=False, tenus=partage(8, rang, monde), reduire=reduire_comptes(device=dev))
-        ep = CoucheEP(part, rang, monde, k=4, jetons=2)
+        ep = CoucheEP(part, rang, monde, k=4, jetons=2, echange=echange)
         toute = CoucheCarte(S.couche(77, dims, 8, brut=False), k=4, brut=False, jetons=2) if rang == 0 else None
         rng = np.random.default_rng(3)
         for _ in range(6):
@@ -59,14 +62,41 @@ def _rang(rang, monde, port):
                 assert torch.equal(toute.idx, ep.carte.idx)
                 a, b = r.cpu().numpy(), rt.cpu().numpy()
                 assert np.abs(a - b).max() <= 1e-5 * max(1.0, np.abs(b).max())
+            if echange == "pairs":
+                tous = [torch.zeros_like(r) for _ in range(monde)]
+                dist.all_gather(tous, r)
+                assert all(torch.equal(tous[0].view(torch.int32), t.view(torch.int32)) for t in tous)
+        if echange == "pairs":
+            # the same step replayed from a CUDA graph: the exchange's sequence lives on the device
+            xs = torch.zeros(2, 512, dtype=torch.bfloat16, device="cuda")
+            rs = torch.zeros(2, 512, dtype=torch.float32, device="cuda")
+            graphe = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graphe):
+                ep.etape(xs, rs)
+            for _ in range(3):
+                x = torch.from_numpy(rng.standard_normal((2, 512)).astype(np.float32)).to(torch.bfloat16).cuda()
+                r0 = torch.from_numpy(rng.standard_normal((2, 512)).astype(np.float32)).cuda()
+                xs.copy_(x)
+                rs.copy_(r0)
+                graphe.replay()
+                torch.cuda.synchronize()
+                assert (ep.carte.controle == 0).all()
+                if rang == 0:
+                    rt = r0.clone()
+                    toute.couche(x, rt)
+                    torch.cuda.synchronize()
+                    a, b = rs.cpu().numpy(), rt.cpu().numpy()
+                    assert np.abs(a - b).max() <= 1e-5 * max(1.0, np.abs(b).max())
+            del graphe
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_deux_gpus_egale_un_gpu():
+@pytest.mark.parametrize("echange", ["nccl", "pairs"])
+def test_ep_deux_gpus_egale_un_gpu(echange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
 
-    mp.start_processes(_rang, args=(2, _port_libre()), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rang, args=(2, _port_libre(), echange), nprocs=2, join=True, start_method="spawn")

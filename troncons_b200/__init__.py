@@ -85,6 +85,13 @@ class ParamsAttention(C.Structure):
         return cls(64, 8, 64, debut, fin, fenetre, 0.125, 0)
 
 
+class EchangePairs(C.Structure):
+    """trc_echange_pairs: every rank's exchange buffer (device addresses in this process), this
+    rank, the number of ranks."""
+
+    _fields_ = [("tampons", C.c_uint64 * 8), ("rang", C.c_uint32), ("monde", C.c_uint32)]
+
+
 class MoeCouche(C.Structure):
     """The fused MoE layer descriptor (trc_moe_couche)."""
 
@@ -93,7 +100,7 @@ class MoeCouche(C.Structure):
                 ("x", C.c_void_p), ("x_bf16", C.c_uint32), ("brut", C.c_uint32), ("residu", C.c_void_p),
                 ("controle", C.c_void_p), ("n_delta", C.c_uint32), ("n_codes", C.c_uint32),
                 ("jetons", C.c_uint32), ("expert_debut", C.c_uint32), ("expert_fin", C.c_uint32),
-                ("partiel", C.c_uint32)]
+                ("partiel", C.c_uint32), ("echange", C.c_void_p)]
 
 
 def _charger() -> C.CDLL:
@@ -126,6 +133,7 @@ def _charger() -> C.CDLL:
         "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
         "trc_moe_couche_sans_alloc": (i32, [C.POINTER(MoeCouche), vp]),
+        "trc_echange_octets": (u64, [pd, u32, u32]),
         "trc_gemv_q8_0": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
         "trc_rmsnorm": (i32, [vp, sz, vp, sz, vp, sz, u32, u32, C.c_float, vp]),
         "trc_rope_yarn": (i32, [vp, sz, vp, sz, u32, u32, u32, C.POINTER(ParamsRope), vp]),
@@ -287,6 +295,11 @@ class Noyaux:
         layer. Calls that may overlap in time on one device race on that workspace; the first
         call on each device looks its address up, so make it before any stream capture."""
         verifier(lib.trc_moe_couche_sans_alloc(C.byref(desc), _flux(flux)))
+
+
+def echange_octets(dims: DimsExpert, jetons: int, monde: int) -> int:
+    """Bytes of one rank's exchange buffer (trc_echange_octets)."""
+    return int(lib.trc_echange_octets(C.byref(dims), jetons, monde))
 
 
 def espace_octets(dims: DimsExpert, k: int) -> int:

@@ -86,7 +86,8 @@ class CoucheCarte:
             self.n.routeur(self.wr, self.br, xs[b], x.dtype == torch.bfloat16, self.c.experts, self.C0, k,
                            self.logits[b], self.idx[b * k:(b + 1) * k], self.poids[b * k:(b + 1) * k], flux)
 
-    def descripteur(self, x: torch.Tensor, residu: torch.Tensor, brute: bool, partiel: bool = False) -> MoeCouche:
+    def descripteur(self, x: torch.Tensor, residu: torch.Tensor, brute: bool, partiel: bool = False,
+                    echange=None) -> MoeCouche:
         if x.numel() != self.jetons * self.C0 or not x.is_contiguous() or x.device.type != "cuda":
             raise ValueError(f"x: {self.jetons} x {self.C0} contiguous elements on the device expected")
         if residu.numel() != self.jetons * self.R2 or residu.dtype != torch.float32 or not residu.is_contiguous():
@@ -112,6 +113,7 @@ class CoucheCarte:
         if self.tenus is not None:
             desc.expert_debut, desc.expert_fin = self.tenus
         desc.partiel = int(partiel)
+        desc.echange = C.addressof(echange) if echange is not None else None
         return desc
 
     def _espace(self):
@@ -120,12 +122,13 @@ class CoucheCarte:
         return self.espace[d:]
 
     def couche(self, x: torch.Tensor, residu: torch.Tensor, brute: bool = False, flux=None, routeur: bool = True,
-               evenements=None, partiel: bool = False):
+               evenements=None, partiel: bool = False, echange=None):
         """Router then the fused layer; `residu` (f32) is updated in place (partiel: overwritten
-        with this device's share of the combine)."""
+        with this device's share of the combine; echange: an EchangePairs, the shares of every
+        GPU summed by the combine kernel over peer memory)."""
         if routeur:
             self.routeur(x, flux)
-        self._desc = self.descripteur(x, residu, brute, partiel)  # keep it alive while the launch reads it
+        self._desc = self.descripteur(x, residu, brute, partiel, echange)  # alive while the launch reads it
         self.n.moe_couche(self._desc, self._espace(), flux, evenements)
 
     # ---------------------------------------------------------------- decode-then-multiply

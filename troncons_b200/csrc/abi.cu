@@ -221,6 +221,11 @@ int trc_combiner(float* residu, size_t residu_octets, const float* sorties, size
     return statut(tb::lancer_combiner(residu, sorties, pas, poids, n, d, static_cast<cudaStream_t>(flux)));
 }
 
+uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32_t monde) {
+    if (dims == nullptr || monde == 0) return 0;
+    return tb::disposition_echange(dims->lignes[2], jetons ? jetons : 1u, monde).total;
+}
+
 uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k) {
     if (dims == nullptr || k == 0) return 0;
     return tb::plan_espace(dims->lignes, dims->colonnes, k).total;
@@ -279,6 +284,17 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
     k.expert_debut = c->expert_debut;
     k.expert_fin = c->expert_fin;
     k.partiel = c->partiel ? 1u : 0u;
+    if (c->echange != nullptr) {
+        const trc_echange_pairs& e = *c->echange;
+        if (e.monde < 2 || e.monde > 8 || e.rang >= e.monde) return usage("exchange: rank %u of %u", e.rang, e.monde);
+        if (c->partiel) return usage("exchange and partial combine together");
+        for (uint32_t q = 0; q < e.monde; ++q) {
+            if (e.tampons[q] == 0 || (e.tampons[q] & 255u) != 0) return usage("exchange buffer of rank %u absent or not 256-aligned", q);
+            k.ech.tampons[q] = e.tampons[q];
+        }
+        k.ech.rang = e.rang;
+        k.ech.monde = e.monde;
+    }
     SUR_LE_FLUX(flux);
     return statut(tb::lancer_moe(k, espace, static_cast<cudaStream_t>(flux),
                                  reinterpret_cast<cudaEvent_t const*>(evenements)));

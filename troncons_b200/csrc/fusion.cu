@@ -647,10 +647,13 @@ __global__ void __launch_bounds__(256) k_moe_swiglu(ArgsMoe a) {
 
 // ------------------------------------------------------------------ 5. down rows, combine
 
+__device__ void echanger(const Couche& c, uint32_t b, uint32_t r, uint32_t R, float s, float* res);
+
 // Token b = blockIdx.y: s = ((w0 s0 + w1 s1) + w2 s2) + ... over its activations held here, in
 // slot order, products and sums rounded separately (passe.cuh:611-622); residu[b] += s, or, when
 // the call is partial (its experts are one share of an expert-parallel layer), residu[b] = s
-// (0 when no activation of the token is held here) for the cross-GPU sum.
+// (0 when no activation of the token is held here) for the cross-GPU sum; or, with an exchange,
+// the shares of every GPU summed here over peer memory (echanger).
 __global__ void __launch_bounds__(256) k_moe_combiner(ArgsMoe a) {
     __shared__ const float* biais[8];
     __shared__ uint32_t tenus;
@@ -677,22 +680,87 @@ __global__ void __launch_bounds__(256) k_moe_combiner(ArgsMoe a) {
     attendre_amont();
     liberer_aval();
     const uint32_t R = c.lignes[2], r = blockIdx.x * 256u + threadIdx.x;
-    if (r >= R) return;
     const uint32_t B = c.colonnes[2] / 32u, K = a.plan.K[2];
     const float* parts = reinterpret_cast<const float*>(a.espace + a.plan.parts[2]);
     float s = 0.0f;
-    bool premier = true;
-    for (uint32_t u = 0; u < c.k; ++u) {
-        if (!((tenus >> u) & 1u)) continue;
-        const uint32_t i = i0 + u;
-        const float bi = biais[u] != nullptr ? biais[u][r] : 0.0f;
-        const float si = finir_ligne(parts + (uint64_t(i) * R + r) * K, r, B) + bi;
-        const float p = __fmul_rn(c.poids[i], si);
-        s = premier ? p : __fadd_rn(s, p);
-        premier = false;
+    if (r < R) {
+        bool premier = true;
+        for (uint32_t u = 0; u < c.k; ++u) {
+            if (!((tenus >> u) & 1u)) continue;
+            const uint32_t i = i0 + u;
+            const float bi = biais[u] != nullptr ? biais[u][r] : 0.0f;
+            const float si = finir_ligne(parts + (uint64_t(i) * R + r) * K, r, B) + bi;
+            const float p = __fmul_rn(c.poids[i], si);
+            s = premier ? p : __fadd_rn(s, p);
+            premier = false;
+        }
     }
     float* res = c.residu + uint64_t(b) * R;
-    res[r] = c.partiel ? s : __fadd_rn(res[r], s);
+    if (c.ech.monde < 2) {
+        if (r < R) res[r] = c.partiel ? s : __fadd_rn(res[r], s);
+        return;
+    }
+    echanger(c, b, r, R, s, res);
+}
+
+// ------------------------------------------------------------------ the combine's sum across GPUs
+
+__device__ __forceinline__ void st_release_sys(uint32_t* a, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+
+// This rank's share s of token b, row r, into its slot on every rank; flags; a bounded wait for
+// every rank's flag on this rank's buffer; then the shares summed in rank order (the same bits
+// on every rank) and added to the residual. Every thread of the block calls it (barriers).
+constexpr uint32_t ECHANGE_ATTENTES_MAX = 1u << 24;  // about 1.5 s with the 100 ns pauses
+
+__device__ void echanger(const Couche& c, uint32_t b, uint32_t r, uint32_t R, float s, float* res) {
+    __shared__ uint32_t bon;
+    const Echange& e = c.ech;
+    const DispositionEchange d = disposition_echange(R, c.jetons, e.monde);
+    const uint32_t blk = b * gridDim.x + blockIdx.x;
+    if (r < R)
+        for (uint32_t q = 0; q < e.monde; ++q)
+            reinterpret_cast<float*>(e.tampons[q] + d.slots)[(uint64_t(e.rang) * c.jetons + b) * R + r] = s;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t* attendu = reinterpret_cast<uint32_t*>(e.tampons[e.rang] + d.attendus) + blk;
+        const uint32_t seq = *attendu + 1u;
+        for (uint32_t q = 0; q < e.monde; ++q)
+            st_release_sys(reinterpret_cast<uint32_t*>(e.tampons[q] + d.flags) + uint64_t(e.rang) * d.blocs + blk, seq);
+        const uint32_t* mes = reinterpret_cast<const uint32_t*>(e.tampons[e.rang] + d.flags);
+        uint32_t ok = 1;
+        for (uint32_t q = 0; q < e.monde && ok; ++q) {
+            uint32_t n = 0;
+            while (ld_acquire_sys(mes + uint64_t(q) * d.blocs + blk) != seq) {
+                if (++n >= ECHANGE_ATTENTES_MAX) {
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(100);
+            }
+        }
+        if (ok) *attendu = seq;
+        bon = ok;
+    }
+    __syncthreads();
+    if (!bon) {
+        if (threadIdx.x == 0) atomicAdd(&c.controle[CTL_ATTENTE], 1u);
+        return;
+    }
+    __threadfence();
+    if (r < R) {
+        const float* sl = reinterpret_cast<const float*>(e.tampons[e.rang] + d.slots);
+        float t = sl[uint64_t(b) * R + r];
+        for (uint32_t q = 1; q < e.monde; ++q) t = __fadd_rn(t, sl[(uint64_t(q) * c.jetons + b) * R + r]);
+        res[r] = __fadd_rn(res[r], t);
+    }
 }
 
 // ------------------------------------------------------------------ launcher

@@ -20,6 +20,28 @@ struct DescGemv {
     uint32_t lignes, colonnes;
 };
 
+// The combine's exchange across GPUs (mirror of trc_echange_pairs; monde < 2: none).
+struct Echange {
+    uint64_t tampons[8];
+    uint32_t rang, monde;
+};
+
+// One rank's exchange buffer: slots [monde][jetons][R] f32 (rank q's share in slot q), flags
+// [monde][blocs] u32 (rank q's flag for combine block b), the expected sequence per block.
+struct DispositionEchange {
+    uint64_t slots, flags, attendus, total;
+    uint32_t blocs;
+};
+__host__ __device__ __forceinline__ DispositionEchange disposition_echange(uint32_t R, uint32_t jetons, uint32_t monde) {
+    DispositionEchange d;
+    d.blocs = ((R + 255u) / 256u) * jetons;
+    d.slots = 0;
+    d.flags = (uint64_t(monde) * jetons * R * 4u + 255u) & ~uint64_t(255);
+    d.attendus = (d.flags + uint64_t(monde) * d.blocs * 4u + 255u) & ~uint64_t(255);
+    d.total = (d.attendus + uint64_t(d.blocs) * 4u + 255u) & ~uint64_t(255);
+    return d;
+}
+
 // The fused layer, as the kernels see it (mirror of trc_moe_couche).
 struct Couche {
     const uint64_t* parties;
@@ -37,6 +59,7 @@ struct Couche {
     uint32_t jetons;                    // tokens (>= 1): activation i = token i / k, slot i % k
     uint32_t expert_debut, expert_fin;  // experts held here ([debut, fin); fin = 0: all)
     uint32_t partiel;                   // 1: the combine writes this call's sum, not residu +=
+    Echange ech;                        // the combine's sum across GPUs over peer memory
 };
 
 // Activations of a call: tokens x routed experts per token.
