@@ -311,10 +311,13 @@ int trc_moe_couche_chrono(const trc_moe_couche* couche, void* espace, size_t esp
  * in the area needs zeroing. Results and launches are those of trc_moe_couche_fusionnee. */
 int trc_moe_couche_sans_alloc(const trc_moe_couche* couche, void* flux);
 
-/* Router of the layer: logits = Wr x + br (f32 weights [experts][colonnes]; x bf16 or f32),
- * then top-k and f64 softmax as trc_routeur_topk. `logits` f32[experts] is written too. */
+/* Router of the layer for `jetons` tokens (x [jetons][colonnes], bf16 or f32): logits = Wr x + br
+ * (f32 weights [experts][colonnes]), then top-k and f64 softmax as trc_routeur_topk, token by
+ * token: logits f32[jetons][experts], indices u32[jetons][k], poids f32[jetons][k]. Two launches
+ * whatever the number of tokens. */
 int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts,
-                uint32_t colonnes, uint32_t k, float* logits, uint32_t* indices, float* poids, void* flux);
+                uint32_t colonnes, uint32_t k, uint32_t jetons, float* logits, uint32_t* indices, float* poids,
+                void* flux);
 
 #ifdef __cplusplus
 }

@@ -139,7 +139,7 @@ def _charger() -> C.CDLL:
         "trc_rope_yarn": (i32, [vp, sz, vp, sz, u32, u32, u32, C.POINTER(ParamsRope), vp]),
         "trc_ecrire_kv": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
         "trc_attention": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, vp, sz, C.POINTER(ParamsAttention), vp]),
-        "trc_routeur": (i32, [vp, vp, vp, u32, u32, u32, u32, vp, vp, vp, vp]),
+        "trc_routeur": (i32, [vp, vp, vp, u32, u32, u32, u32, u32, vp, vp, vp, vp]),
     }
     for nom, (res, args) in sig.items():
         f = getattr(lib, nom)
@@ -248,9 +248,9 @@ class Noyaux:
     # ---------------------------------------------------------------- new entry points
 
     def routeur(self, wr, br, x, x_bf16: bool, experts: int, colonnes: int, k: int, logits, indices, poids,
-                flux=None) -> None:
+                flux=None, jetons: int = 1) -> None:
         verifier(lib.trc_routeur(_v(wr).adresse, _v(br).adresse or None, _v(x).adresse, int(x_bf16), experts, colonnes,
-                                 k, _v(logits).adresse, _v(indices).adresse, _v(poids).adresse, _flux(flux)))
+                                 k, jetons, _v(logits).adresse, _v(indices).adresse, _v(poids).adresse, _flux(flux)))
 
     def moe_couche(self, desc: MoeCouche, espace, flux=None, evenements=None) -> None:
         """The fused layer; `evenements`: 6 raw cudaEvent_t handles (ints) recorded between its

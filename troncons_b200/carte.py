@@ -80,11 +80,8 @@ class CoucheCarte:
 
     def routeur(self, x: torch.Tensor, flux=None) -> None:
         """The router of every token of x ([jetons][d] or [d]): logits, top-k, weights."""
-        xs = x.reshape(self.jetons, self.C0)
-        k = self.k
-        for b in range(self.jetons):
-            self.n.routeur(self.wr, self.br, xs[b], x.dtype == torch.bfloat16, self.c.experts, self.C0, k,
-                           self.logits[b], self.idx[b * k:(b + 1) * k], self.poids[b * k:(b + 1) * k], flux)
+        self.n.routeur(self.wr, self.br, x, x.dtype == torch.bfloat16, self.c.experts, self.C0, self.k, self.logits,
+                       self.idx, self.poids, flux, jetons=self.jetons)
 
     def descripteur(self, x: torch.Tensor, residu: torch.Tensor, brute: bool, partiel: bool = False,
                     echange=None) -> MoeCouche:

@@ -375,16 +375,17 @@ int trc_attention(const float* q, size_t q_octets, const uint16_t* cache_k, size
 }
 
 int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts, uint32_t colonnes,
-                uint32_t k, float* logits, uint32_t* indices, float* poids, void* flux) {
+                uint32_t k, uint32_t jetons, float* logits, uint32_t* indices, float* poids, void* flux) {
     if (experts == 0 || experts > 256 || k == 0 || k > 8 || k > experts) return usage("top-%u of %u", k, experts);
+    if (jetons == 0 || jetons > 128) return usage("%u tokens (1 to 128)", jetons);
     if (colonnes == 0 || colonnes % 4 != 0) return usage("%u columns (a multiple of 4)", colonnes);
     if (wr == nullptr || !aligne(wr, 16) || x == nullptr || !aligne(x, x_bf16 ? 8 : 16) || logits == nullptr ||
         indices == nullptr || poids == nullptr)
         return usage("router: a buffer is missing or misaligned");
     SUR_LE_FLUX(flux);
     cudaStream_t s = static_cast<cudaStream_t>(flux);
-    cudaError_t e = tb::lancer_gemv_f32(wr, x, x_bf16 ? 1u : 0u, br, logits, experts, colonnes, s);
-    if (e == cudaSuccess) e = tb::lancer_topk(logits, experts, k, indices, poids, nullptr, 0, s);
+    cudaError_t e = tb::lancer_gemv_f32(wr, x, x_bf16 ? 1u : 0u, br, logits, experts, colonnes, s, jetons);
+    if (e == cudaSuccess) e = tb::lancer_topk(logits, experts, k, indices, poids, nullptr, 0, s, jetons);
     return statut(e);
 }
 

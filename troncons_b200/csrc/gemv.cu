@@ -63,13 +63,16 @@ __device__ __forceinline__ float4 charger_x4(const void* x, uint32_t x_bf16, uin
 // most 6 float4 for C = 2880) are in flight together.
 constexpr uint32_t F32_QUARTS = 4;
 
-__global__ void __launch_bounds__(F32_QUARTS * 32) k_gemv_f32(const float* __restrict__ w, const void* __restrict__ x,
+__global__ void __launch_bounds__(F32_QUARTS * 32) k_gemv_f32(const float* __restrict__ w, const void* x,
                                                              uint32_t x_bf16, const float* __restrict__ biais,
-                                                             float* __restrict__ y, uint32_t R, uint32_t C) {
+                                                             float* y, uint32_t R, uint32_t C) {
     __shared__ float parts[F32_QUARTS];
     attendre_amont();
     liberer_aval();
     const uint32_t r = blockIdx.x, voie = threadIdx.x & 31u, q = threadIdx.x >> 5;
+    // Token blockIdx.y of a batch: its x and its y.
+    x = static_cast<const uint8_t*>(x) + uint64_t(blockIdx.y) * C * (x_bf16 ? 2u : 4u);
+    y += uint64_t(blockIdx.y) * R;
     const uint32_t C4 = C / 4u, Q = (C4 + F32_QUARTS - 1u) / F32_QUARTS, c0 = q * Q, c1 = min(C4, c0 + Q);
     const float4* w4 = reinterpret_cast<const float4*>(w) + uint64_t(r) * C4;
     float acc = 0.0f;
@@ -103,8 +106,8 @@ cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_m
 }
 
 cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
-                            uint32_t C, cudaStream_t flux) {
-    return lancer_pdl(k_gemv_f32, dim3(R), dim3(F32_QUARTS * 32), 0, flux, w, x, x_bf16, biais, y, R, C);
+                            uint32_t C, cudaStream_t flux, uint32_t jetons) {
+    return lancer_pdl(k_gemv_f32, dim3(R, jetons), dim3(F32_QUARTS * 32), 0, flux, w, x, x_bf16, biais, y, R, C);
 }
 
 }  // namespace tb

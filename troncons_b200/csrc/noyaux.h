@@ -82,9 +82,9 @@ cudaError_t lancer_copier_brut(const void* partie, uint64_t taille, void* emplac
 cudaError_t lancer_gemv(const void* matrice, const float* x, float* y, uint32_t R, uint32_t C, cudaStream_t flux);
 cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_max, cudaStream_t flux);
 cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
-                            uint32_t C, cudaStream_t flux);
+                            uint32_t C, cudaStream_t flux, uint32_t jetons = 1);
 cudaError_t lancer_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids, uint32_t* boite,
-                        uint32_t sequence, cudaStream_t flux);
+                        uint32_t sequence, cudaStream_t flux, uint32_t jetons = 1);
 cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, cudaStream_t flux);
 cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, const float* poids, uint32_t n, uint32_t d,
                             cudaStream_t flux);

@@ -14,11 +14,14 @@ __device__ __forceinline__ bool meilleur(float va, uint32_t ia, float vb, uint32
 // One warp. E <= 256, k <= 8: lane l holds logits l, l+32, ..., each round takes the warp's best
 // among those not yet taken. Weights: m = the first chosen value, e_r = exp(v_r - m) in f64,
 // z = sum in order, w_r = float(e_r / z) (passe.cuh:455-514; ops.rs:123-131).
-__global__ void __launch_bounds__(32) k_topk(const float* __restrict__ logits, uint32_t E, uint32_t k,
-                                             uint32_t* __restrict__ indices, float* __restrict__ poids, uint32_t* boite,
-                                             uint32_t sequence) {
+__global__ void __launch_bounds__(32) k_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids,
+                                             uint32_t* boite, uint32_t sequence) {
     attendre_amont();
     liberer_aval();
+    // Token blockIdx.x of a batch (the mailbox is for a single token).
+    logits += uint64_t(blockIdx.x) * E;
+    indices += uint64_t(blockIdx.x) * k;
+    poids += uint64_t(blockIdx.x) * k;
     const uint32_t voie = threadIdx.x;
     float v[8];
     uint32_t pris = 0;
@@ -106,8 +109,9 @@ __global__ void __launch_bounds__(256) k_combiner(float* __restrict__ residu, co
 }
 
 cudaError_t lancer_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids, uint32_t* boite,
-                        uint32_t sequence, cudaStream_t flux) {
-    return lancer_pdl(k_topk, dim3(1), dim3(32), 0, flux, logits, E, k, indices, poids, boite, sequence);
+                        uint32_t sequence, cudaStream_t flux, uint32_t jetons) {
+    return lancer_pdl(k_topk, dim3(jetons), dim3(32), 0, flux, logits, E, k, indices, poids, jetons == 1 ? boite : nullptr,
+                      sequence);
 }
 
 cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, cudaStream_t flux) {
