@@ -189,29 +189,38 @@ struct GemvTuile {
     float acc, acc_s;       // current row r, next row
     uint32_t r, fin_r;      // warp-uniform: current row, first block of the next row
     uint32_t med_r, med_s;  // medians of rows r and r + 1 (clamped to the last row)
+    uint32_t evt;           // the next macro-step after which a row or a segment closes
     uint32_t R, B, K, voie;
     float* parts;
     const uint8_t* med;     // row medians (shared memory)
+    const float* puiss;     // 2^(e - 128) for e = 0..255 (shared memory, echelle_e8m0)
 
-    __device__ __forceinline__ void debut(uint32_t m0) {
+    // The macro-step, from m on, that ends row r, segment m / 32 or the tile.
+    __device__ __forceinline__ uint32_t prochain(uint32_t m, uint32_t m1) const {
+        return min(min((fin_r - 1u) / 8u, m | (SEGMENT_MACRO - 1u)), m1 - 1u);
+    }
+
+    __device__ __forceinline__ void debut(uint32_t m0, uint32_t m1) {
         acc = 0.0f;
         acc_s = 0.0f;
         r = (8u * m0) / B;
         fin_r = (r + 1u) * B;
         med_r = med[min(r, R - 1u)];
         med_s = med[min(r + 1u, R - 1u)];
+        evt = prochain(m0, m1);
     }
 
     // Block `bloc`'s quad sum s, scaled by 2^(median + delta - 256) of its row (r or r + 1).
     __device__ __forceinline__ void accumuler(float s, uint32_t bloc, uint32_t delta, bool valide) {
         const bool cour = bloc < fin_r;
-        const float sc = echelle_e8m0(((cour ? med_r : med_s) + delta - 128u) & 255u);
+        const float sc = puiss[((cour ? med_r : med_s) + delta - 128u) & 255u];
         acc = (valide && cour) ? fmaf(s, sc, acc) : acc;
         acc_s = (valide && !cour) ? fmaf(s, sc, acc_s) : acc_s;
     }
 
-    // Row and segment closing after macro-step m (warp-uniform branches).
+    // Row and segment closing after macro-step m (warp-uniform): nothing to do before evt.
     __device__ __forceinline__ void fermer(uint32_t m, uint32_t m1) {
+        if (m != evt) return;
         const uint32_t seg = m / SEGMENT_MACRO;
         if (fin_r <= 8u * m + 8u) {  // row r ends in this macro-step
             const float P = arbre8(acc);
@@ -230,8 +239,14 @@ struct GemvTuile {
             }
             acc = 0.0f;
         }
+        if (m + 1u < m1) evt = prochain(m + 1u, m1);
     }
 };
+
+// The table of block scales: 2^(e - 128) for the 256 E8M0 values (echelle_e8m0's, exactly).
+__device__ __forceinline__ void charger_puissances(float* puiss) {
+    for (uint32_t t = threadIdx.x; t < 256u; t += blockDim.x) puiss[t] = echelle_e8m0(t);
+}
 
 // Decode and multiply run in different warps of a block: MOE_PAIRES producer warps each
 // decode one CODES_CTX tile (the bare rANS chain, one word per lane and macro-step, table
@@ -253,7 +268,7 @@ __host__ __device__ __forceinline__ uint32_t medianes_octets(const Couche& c) {
 // Dynamic shared memory of k_moe_codes: 3 LUTs, the producers' word rings, the segment
 // buffers (words, deltas), the medians, 2x, the mbarriers.
 struct DispositionCodes {
-    uint32_t anneaux, mots, deltas, med, x2, barrieres, total;
+    uint32_t anneaux, mots, deltas, med, puiss, x2, barrieres, total;
 };
 __host__ __device__ __forceinline__ DispositionCodes disposition_codes(const Couche& c) {
     DispositionCodes d;
@@ -262,7 +277,8 @@ __host__ __device__ __forceinline__ DispositionCodes disposition_codes(const Cou
     d.mots = d.anneaux + MOE_PAIRES * ANNEAU_ALLOC * 2u;
     d.deltas = d.mots + MOE_PAIRES * SEG_TAMPONS * SEG_MOTS * 4u;
     d.med = d.deltas + MOE_PAIRES * SEG_TAMPONS * SEG_DELTAS;
-    d.x2 = d.med + medianes_octets(c);
+    d.puiss = d.med + medianes_octets(c);
+    d.x2 = d.puiss + 1024u;
     d.barrieres = d.x2 + x2_octets(cmax);
     d.total = d.barrieres + MOE_PAIRES * 2u * SEG_TAMPONS * 8u;
     return d;
@@ -294,8 +310,10 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     const DispositionCodes dc = disposition_codes(c);
     uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);
     uint8_t* med = dyn + dc.med;
+    float* puiss = reinterpret_cast<float*>(dyn + dc.puiss);
     float* x2s = reinterpret_cast<float*>(dyn + dc.x2);
     uint64_t* barrieres = reinterpret_cast<uint64_t*>(dyn + dc.barrieres);
+    charger_puissances(puiss);
     copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M),
              3u * M / 4u);
     if (fm.p + ((R + 15u) & ~15u) <= partie + taille)
@@ -374,10 +392,11 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
         gv.voie = voie;
         gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
         gv.med = med;
+        gv.puiss = puiss;
         uint32_t n = 0;
         for (uint32_t t = warp0 + paire; t < h.T && !abandon; t += pas_tuiles) {
             const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
-            gv.debut(m0);
+            gv.debut(m0, m1);
             uint32_t bloc = 8u * m0 + g;
             uint32_t bc = bloc % B;  // column block of `bloc` in its row
             for (uint32_t s0 = m0; s0 < m1; s0 += SEGMENT_MACRO, ++n) {
@@ -426,14 +445,15 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
 constexpr uint32_t DENSE_WARPS = 12;
 
 struct DispositionDense {
-    uint32_t anneaux, med, x2, total;
+    uint32_t anneaux, med, puiss, x2, total;
 };
 __host__ __device__ __forceinline__ DispositionDense disposition_dense(const Couche& c) {
     DispositionDense d;
     const uint32_t cmax = max(c.colonnes[0], c.colonnes[2]);
     d.anneaux = 3u * M * 4u;
     d.med = d.anneaux + DENSE_WARPS * ANNEAU_ALLOC * 2u;
-    d.x2 = d.med + medianes_octets(c);
+    d.puiss = d.med + medianes_octets(c);
+    d.x2 = d.puiss + 1024u;
     d.total = d.x2 + x2_octets(cmax);
     return d;
 }
@@ -491,7 +511,9 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);
     uint16_t* anneau = reinterpret_cast<uint16_t*>(dyn + dd.anneaux) + warp * ANNEAU_ALLOC;
     uint8_t* med = dyn + dd.med;
+    float* puiss = reinterpret_cast<float*>(dyn + dd.puiss);
     float* x2s = reinterpret_cast<float*>(dyn + dd.x2);
+    charger_puissances(puiss);
     copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M),
              3u * M / 4u);
     if (fm.p + ((R + 15u) & ~15u) <= partie + taille)
@@ -518,12 +540,13 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     gv.voie = voie;
     gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
     gv.med = med;
+    gv.puiss = puiss;
     const uint32_t nmacro = h.P / 128u;
     uint32_t hors_l = 0, pointeur = 0;
     for (uint32_t t = t0; t < h.T; t += gridDim.x * DENSE_WARPS) {
         if (t != t0) d.debut(h, t, voie, anneau);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
-        gv.debut(m0);
+        gv.debut(m0, m1);
         // This lane's block at macro-step m is 8 m + g, column block b; its delta read two
         // macro-steps ahead.
         uint32_t bloc = 8u * m0 + g;
