@@ -228,6 +228,23 @@ int64_t trc_coder_partie_brute(const uint8_t* const* blocs, const uint8_t* const
 int trc_synth_matrices(uint64_t graine, uint32_t lignes, uint32_t colonnes, uint32_t premier, uint32_t n,
                        uint8_t* blocs, float* biais, int fils);
 
+/* ---------------------------------------------------------------- encoder on the GPU */
+
+/* Scratch bytes of trc_coder_flux_gpu for P source bytes in tiles of N macro-steps. */
+uint64_t trc_coder_flux_gpu_espace(uint32_t P, uint32_t N);
+
+/* One geometry-1 rANS stream of the P bytes at `src` (device, P a multiple of 128, 4-aligned) in
+ * tiles of N macro-steps, on the GPU: byte for byte what trc-codec's coder writes
+ * (rans.rs:296-334). Table of byte n: kappa[n / 16] when `kappa` (device u8[n_kappa]) is given
+ * and n / 16 < n_kappa, else 0; `freqs`: device u16[n_tables][256] (n_tables 1..4), each summing
+ * to 4096. The stream goes to `sortie` (device, 16-aligned) if it fits in `capacite` bytes;
+ * *octets (device u64) receives its size (0 when a byte has no slot in its table or its context
+ * has no table). `espace`: device scratch of trc_coder_flux_gpu_espace bytes, 256-aligned.
+ * Asynchronous on `flux`; the caller reads *octets after synchronising. */
+int trc_coder_flux_gpu(const uint8_t* src, uint32_t P, uint32_t N, const uint8_t* kappa, uint32_t n_kappa,
+                       const uint16_t* freqs, uint32_t n_tables, uint8_t* sortie, size_t capacite, uint64_t* octets,
+                       void* espace, size_t espace_octets, void* flux);
+
 /* ---------------------------------------------------------------- new: the fused MoE layer */
 
 /* One MoE layer of one token, fused: routed experts' DELTA -> scales, CODES_CTX decoded in

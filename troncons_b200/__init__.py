@@ -134,6 +134,8 @@ def _charger() -> C.CDLL:
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
         "trc_moe_couche_sans_alloc": (i32, [C.POINTER(MoeCouche), vp]),
         "trc_echange_octets": (u64, [pd, u32, u32]),
+        "trc_coder_flux_gpu_espace": (u64, [u32, u32]),
+        "trc_coder_flux_gpu": (i32, [vp, u32, u32, vp, u32, vp, u32, vp, sz, vp, vp, sz, vp]),
         "trc_gemv_q8_0": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
         "trc_rmsnorm": (i32, [vp, sz, vp, sz, vp, sz, u32, u32, C.c_float, vp]),
         "trc_rope_yarn": (i32, [vp, sz, vp, sz, u32, u32, u32, C.POINTER(ParamsRope), vp]),
@@ -295,6 +297,31 @@ class Noyaux:
         layer. Calls that may overlap in time on one device race on that workspace; the first
         call on each device looks its address up, so make it before any stream capture."""
         verifier(lib.trc_moe_couche_sans_alloc(C.byref(desc), _flux(flux)))
+
+
+def coder_flux_gpu(src, freqs, kappa=None, N: int = 256, flux=None) -> bytes:
+    """A geometry-1 stream encoded on the GPU (trc_coder_flux_gpu): `src` a CUDA uint8 tensor of
+    P bytes (P a multiple of 128), `freqs` a CUDA uint16 tensor [n_tables][256], `kappa` a CUDA
+    uint8 tensor of per-16-byte-block contexts or None. Returns the stream's bytes (synchronises)."""
+    import torch
+
+    P = src.numel()
+    T = (P // 128 + N - 1) // N
+    cap = 16 + 132 * T + 2 * P + 4096
+    sortie = torch.zeros(cap, dtype=torch.uint8, device=src.device)
+    octets = torch.zeros(1, dtype=torch.int64, device=src.device)
+    n_esp = int(lib.trc_coder_flux_gpu_espace(P, N))
+    espace = torch.empty(n_esp + 256, dtype=torch.uint8, device=src.device)
+    e = espace.data_ptr() + (-espace.data_ptr()) % 256
+    n_tables = freqs.numel() // 256
+    verifier(lib.trc_coder_flux_gpu(src.data_ptr(), P, N, kappa.data_ptr() if kappa is not None else None,
+                                    kappa.numel() if kappa is not None else 0, freqs.data_ptr(), n_tables,
+                                    sortie.data_ptr(), cap, octets.data_ptr(), e, n_esp, _flux(flux)))
+    torch.cuda.current_stream().synchronize() if flux is None else flux.synchronize()
+    n = int(octets.item())
+    if n == 0 or n > cap:
+        raise ValueError("encoding failed (a symbol absent from its table, or too long)")
+    return sortie[:n].cpu().numpy().tobytes()
 
 
 def echange_octets(dims: DimsExpert, jetons: int, monde: int) -> int:

@@ -221,6 +221,29 @@ int trc_combiner(float* residu, size_t residu_octets, const float* sorties, size
     return statut(tb::lancer_combiner(residu, sorties, pas, poids, n, d, static_cast<cudaStream_t>(flux)));
 }
 
+uint64_t trc_coder_flux_gpu_espace(uint32_t P, uint32_t N) {
+    if (N == 0) return 0;
+    return tb::coder_flux_espace(P, N);
+}
+
+int trc_coder_flux_gpu(const uint8_t* src, uint32_t P, uint32_t N, const uint8_t* kappa, uint32_t n_kappa,
+                       const uint16_t* freqs, uint32_t n_tables, uint8_t* sortie, size_t capacite, uint64_t* octets,
+                       void* espace, size_t espace_octets, void* flux) {
+    if (P == 0 || P % 128 != 0 || N == 0 || N > 65535) return usage("P = %u (a multiple of 128), N = %u", P, N);
+    if ((uint64_t(P) / 128 + N - 1) / N > 65535) return usage("more than 65,535 tiles");
+    if (n_tables == 0 || n_tables > 4) return usage("%u tables (1 to 4)", n_tables);
+    if (src == nullptr || !aligne(src, 4) || freqs == nullptr || !aligne(freqs, 2) || sortie == nullptr ||
+        !aligne(sortie, 16) || octets == nullptr || !aligne(octets, 8))
+        return usage("encoder: a buffer is missing or misaligned");
+    if (kappa == nullptr && n_kappa != 0) return usage("contexts absent");
+    if (espace == nullptr || !aligne(espace, 256) || espace_octets < tb::coder_flux_espace(P, N))
+        return usage("encoder scratch of %zu bytes, %llu needed (256-aligned)", espace_octets,
+                     (unsigned long long)tb::coder_flux_espace(P, N));
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_coder_flux(src, P, N, kappa, n_kappa, freqs, n_tables, sortie, capacite, octets,
+                                        static_cast<uint8_t*>(espace), static_cast<cudaStream_t>(flux)));
+}
+
 uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32_t monde) {
     if (dims == nullptr || monde == 0) return 0;
     return tb::disposition_echange(dims->lignes[2], jetons ? jetons : 1u, monde).total;

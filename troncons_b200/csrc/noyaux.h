@@ -111,6 +111,12 @@ cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint1
 cudaError_t lancer_attention(const float* q, const uint16_t* ck, const uint16_t* cv, const float* puits, float* sortie,
                              const ParamsAttention& p, cudaStream_t flux);
 
+// GPU encoder of one geometry-1 stream (codeur_gpu.cu).
+uint64_t coder_flux_espace(uint32_t P, uint32_t N);
+cudaError_t lancer_coder_flux(const uint8_t* src, uint32_t P, uint32_t N, const uint8_t* kappa, uint32_t n_kappa,
+                              const uint16_t* freqs, uint32_t n_tables, uint8_t* sortie, uint64_t capacite, uint64_t* octets,
+                              uint8_t* espace, cudaStream_t flux);
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 cudaError_t assurer_smem(const void* noyau, int octets);
 
