@@ -245,6 +245,37 @@ int trc_coder_flux_gpu(const uint8_t* src, uint32_t P, uint32_t N, const uint8_t
                        const uint16_t* freqs, uint32_t n_tables, uint8_t* sortie, size_t capacite, uint64_t* octets,
                        void* espace, size_t espace_octets, void* flux);
 
+/* One expert of a GPU encode batch: 72 bytes, in device memory. */
+typedef struct trc_desc_codage {
+    uint64_t blocs[3]; /* device: matrix j's R*B 17-byte MXFP4 blocks [e, qs x 16], beta order */
+    uint64_t biais[3]; /* device: matrix j's f32[R] biases (4-aligned) */
+    uint64_t sortie;   /* device: the part (16-aligned) */
+    uint64_t capacite; /* bytes available at sortie */
+    uint32_t expert;   /* the expert number in the part header */
+    uint32_t reserve;  /* 0 */
+} trc_desc_codage;
+
+/* Scratch bytes of trc_coder_parties_gpu for n experts of shape `dims`. */
+uint64_t trc_coder_parties_gpu_espace(const trc_dims_expert* dims, uint32_t n, uint32_t n_delta, uint32_t n_codes);
+
+/* The level-0 parts of n experts on the GPU: per expert the part trc_coder_partie writes, byte for
+ * byte (coder.rs:243-313, trc-codec lib.rs:348-428, trc-format lib.rs:882-908). freqs: device
+ * u16[3][4][256], the layer's tables; octets: device u64[2n], [2e] the part's length (a multiple
+ * of 4096; 0 when a symbol has no slot in its table), [2e + 1] its useful bytes. Expert e's part
+ * is written at descs[e].sortie only when its length fits descs[e].capacite (zeros included: the
+ * whole length is written). espace: device scratch of trc_coder_parties_gpu_espace bytes,
+ * 256-aligned. Asynchronous on `flux`. */
+int trc_coder_parties_gpu(const trc_desc_codage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
+                          const uint16_t* freqs, int canonique, uint16_t couche, uint32_t n_delta, uint32_t n_codes,
+                          uint64_t* octets, size_t octets_octets, void* espace, size_t espace_octets, void* flux);
+
+/* The symbol counts of n experts added into `comptes` (device u64[3][4][256]: per matrix j,
+ * [0] DELTA, [1 + k] CODES_CTX of scale class k, padding counted): trc_comptes_matrice on the
+ * GPU for every matrix of every expert of the batch (lib.rs:393-401). Only blocs[] of the
+ * descriptors is read. Asynchronous on `flux`. */
+int trc_comptes_gpu(const trc_desc_codage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
+                    int canonique, uint64_t* comptes, size_t comptes_octets, void* flux);
+
 /* ---------------------------------------------------------------- new: the fused MoE layer */
 
 /* One MoE layer of one token, fused: routed experts' DELTA -> scales, CODES_CTX decoded in

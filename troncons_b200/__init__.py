@@ -52,6 +52,13 @@ class DescGemv(C.Structure):
                 ("colonnes", C.c_uint32)]
 
 
+class DescCodage(C.Structure):
+    """One expert of a GPU encode batch (trc_desc_codage): 72 bytes."""
+
+    _fields_ = [("blocs", C.c_uint64 * 3), ("biais", C.c_uint64 * 3), ("sortie", C.c_uint64), ("capacite", C.c_uint64),
+                ("expert", C.c_uint32), ("reserve", C.c_uint32)]
+
+
 class DescDecodage(C.Structure):
     """One expert of a decode batch (abi.rs:32-53): 32 bytes."""
 
@@ -136,6 +143,9 @@ def _charger() -> C.CDLL:
         "trc_echange_octets": (u64, [pd, u32, u32]),
         "trc_coder_flux_gpu_espace": (u64, [u32, u32]),
         "trc_coder_flux_gpu": (i32, [vp, u32, u32, vp, u32, vp, u32, vp, sz, vp, vp, sz, vp]),
+        "trc_coder_parties_gpu_espace": (u64, [pd, u32, u32, u32]),
+        "trc_coder_parties_gpu": (i32, [vp, sz, u32, pd, vp, i32, C.c_uint16, u32, u32, vp, sz, vp, sz, vp]),
+        "trc_comptes_gpu": (i32, [vp, sz, u32, pd, i32, vp, sz, vp]),
         "trc_gemv_q8_0": (i32, [vp, sz, vp, sz, vp, sz, vp, sz, u32, u32, vp]),
         "trc_rmsnorm": (i32, [vp, sz, vp, sz, vp, sz, u32, u32, C.c_float, vp]),
         "trc_rope_yarn": (i32, [vp, sz, vp, sz, u32, u32, u32, C.POINTER(ParamsRope), vp]),

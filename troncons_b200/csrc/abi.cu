@@ -244,6 +244,62 @@ int trc_coder_flux_gpu(const uint8_t* src, uint32_t P, uint32_t N, const uint8_t
                                         static_cast<uint8_t*>(espace), static_cast<cudaStream_t>(flux)));
 }
 
+static_assert(sizeof(trc_desc_codage) == 72 && sizeof(tb::DescCodage) == 72, "trc_desc_codage layout");
+
+namespace {
+
+int sms_du_device() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+int verifier_lot_codage(const trc_desc_codage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims) {
+    if (const int r = verifier_dims(dims)) return r;
+    if (n == 0 || n > 65535) return usage("%u experts (1 to 65,535)", n);
+    if (descs == nullptr || !aligne(descs, 8) || descs_octets < sizeof(trc_desc_codage) * size_t(n))
+        return usage("descriptors: %zu bytes for %u experts, or misaligned", descs_octets, n);
+    return TRC_OK;
+}
+
+}  // namespace
+
+uint64_t trc_coder_parties_gpu_espace(const trc_dims_expert* dims, uint32_t n, uint32_t n_delta, uint32_t n_codes) {
+    if (dims == nullptr || n == 0 || n_delta == 0 || n_codes == 0) return 0;
+    return tb::coder_parties_espace(dims_de(dims), n, n_delta, n_codes);
+}
+
+int trc_coder_parties_gpu(const trc_desc_codage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
+                          const uint16_t* freqs, int canonique, uint16_t couche, uint32_t n_delta, uint32_t n_codes,
+                          uint64_t* octets, size_t octets_octets, void* espace, size_t espace_octets, void* flux) {
+    if (const int r = verifier_lot_codage(descs, descs_octets, n, dims)) return r;
+    if (n_delta == 0 || n_delta > 65535 || n_codes == 0 || n_codes > 65535)
+        return usage("tiles of %u / %u macro-steps (1 to 65,535)", n_delta, n_codes);
+    for (int j = 0; j < 3; ++j) {
+        const uint64_t nb = uint64_t(dims->lignes[j]) * (dims->colonnes[j] / 32);
+        if ((nb + 127) / 128 / n_delta >= 65535 || (16 * nb + 127) / 128 / n_codes >= 65535)
+            return usage("matrix %d: more than 65,535 tiles", j);
+    }
+    if (freqs == nullptr || !aligne(freqs, 2)) return usage("tables absent or misaligned");
+    if (octets == nullptr || !aligne(octets, 8) || octets_octets < 16ull * n) return usage("octets: u64[2n] needed");
+    const uint64_t besoin = tb::coder_parties_espace(dims_de(dims), n, n_delta, n_codes);
+    if (espace == nullptr || !aligne(espace, 256) || espace_octets < besoin)
+        return usage("encoder scratch of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_coder_parties(reinterpret_cast<const tb::DescCodage*>(descs), n, dims_de(dims), freqs,
+                                           canonique != 0, couche, n_delta, n_codes, octets,
+                                           static_cast<uint8_t*>(espace), sms_du_device(), static_cast<cudaStream_t>(flux)));
+}
+
+int trc_comptes_gpu(const trc_desc_codage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
+                    int canonique, uint64_t* comptes, size_t comptes_octets, void* flux) {
+    if (const int r = verifier_lot_codage(descs, descs_octets, n, dims)) return r;
+    if (comptes == nullptr || !aligne(comptes, 8) || comptes_octets < 3 * 4 * 256 * 8) return usage("counts: u64[3][4][256] needed");
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_comptes(reinterpret_cast<const tb::DescCodage*>(descs), n, dims_de(dims), canonique != 0,
+                                     comptes, sms_du_device(), static_cast<cudaStream_t>(flux)));
+}
+
 uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32_t monde) {
     if (dims == nullptr || monde == 0) return 0;
     return tb::disposition_echange(dims->lignes[2], jetons ? jetons : 1u, monde).total;

@@ -20,6 +20,12 @@ struct DescGemv {
     uint32_t lignes, colonnes;
 };
 
+// One expert of a GPU encode batch (mirror of trc_desc_codage, 72 bytes).
+struct DescCodage {
+    uint64_t blocs[3], biais[3], sortie, capacite;
+    uint32_t expert, reserve;
+};
+
 // The combine's exchange across GPUs (mirror of trc_echange_pairs; monde < 2: none).
 struct Echange {
     uint64_t tampons[8];
@@ -116,6 +122,13 @@ uint64_t coder_flux_espace(uint32_t P, uint32_t N);
 cudaError_t lancer_coder_flux(const uint8_t* src, uint32_t P, uint32_t N, const uint8_t* kappa, uint32_t n_kappa,
                               const uint16_t* freqs, uint32_t n_tables, uint8_t* sortie, uint64_t capacite, uint64_t* octets,
                               uint8_t* espace, cudaStream_t flux);
+// Level-0 parts of n experts on the GPU (codeur_gpu.cu), and the layer's symbol counts.
+uint64_t coder_parties_espace(const Dims& dims, uint32_t n, uint32_t n_delta, uint32_t n_codes);
+cudaError_t lancer_coder_parties(const DescCodage* descs, uint32_t n, const Dims& dims, const uint16_t* freqs,
+                                 bool canonique, uint16_t couche, uint32_t n_delta, uint32_t n_codes, uint64_t* octets,
+                                 uint8_t* espace, int sms, cudaStream_t flux);
+cudaError_t lancer_comptes(const DescCodage* descs, uint32_t n, const Dims& dims, bool canonique, uint64_t* comptes,
+                           int sms, cudaStream_t flux);
 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
 cudaError_t assurer_smem(const void* noyau, int octets);

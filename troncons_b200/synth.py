@@ -98,6 +98,76 @@ def coder_partie(blocs3, biais3, dims: DimsExpert, freqs: np.ndarray, canonique:
     return out[:n].tobytes()
 
 
+def _descs_gpu(blocs, biais, experts, sorties, capacite):
+    import torch
+
+    from . import DescCodage
+
+    n = len(blocs)
+    d = (DescCodage * n)()
+    for e in range(n):
+        for j in range(3):
+            assert blocs[e][j].is_cuda and blocs[e][j].dtype == torch.uint8 and blocs[e][j].is_contiguous()
+            assert biais[e][j].is_cuda and biais[e][j].dtype == torch.float32 and biais[e][j].is_contiguous()
+            d[e].blocs[j] = blocs[e][j].data_ptr()
+            d[e].biais[j] = biais[e][j].data_ptr()
+        d[e].sortie = sorties[e].data_ptr() if sorties is not None else 0
+        d[e].capacite = capacite
+        d[e].expert = experts[e]
+    brut = np.frombuffer(bytes(d), np.uint8)
+    return torch.from_numpy(brut.copy()).cuda()
+
+
+def comptes_gpu(blocs, dims: DimsExpert, canonique: bool = True, comptes=None):
+    """trc_comptes_gpu: the symbol counts u64[3][4][256] of the experts whose blocks are the CUDA
+    tensors blocs[e][j], added into `comptes` (a CUDA int64 tensor, or a new one); returns it."""
+    import torch
+
+    from . import verifier
+
+    n = len(blocs)
+    z = [[torch.zeros(1, dtype=torch.float32, device="cuda")] * 3] * n
+    descs = _descs_gpu(blocs, z, [0] * n, None, 0)
+    if comptes is None:
+        comptes = torch.zeros(3 * 4 * 256, dtype=torch.int64, device="cuda")
+    verifier(lib.trc_comptes_gpu(descs.data_ptr(), descs.numel(), n, C.byref(dims), int(canonique), comptes.data_ptr(),
+                                 comptes.numel() * 8, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.current_stream().synchronize()
+    return comptes
+
+
+def coder_parties_gpu(blocs, biais, dims: DimsExpert, freqs, canonique: bool = True, couche: int = 0, experts=None,
+                      n_delta: int = 256, n_codes: int = 256) -> list:
+    """trc_coder_parties_gpu: the level-0 parts of the experts whose blocks and biases are the
+    CUDA tensors blocs[e][j], biais[e][j], with the layer's tables `freqs` (u16[3][4][256]).
+    Returns each part's bytes (synchronises)."""
+    import torch
+
+    from . import verifier
+
+    n = len(blocs)
+    experts = list(range(n)) if experts is None else experts
+    cap = 2 * sum(b.numel() for b in blocs[0]) + 4 * sum(b.numel() for b in biais[0]) + (1 << 16)
+    sorties = [torch.empty(cap, dtype=torch.uint8, device="cuda") for _ in range(n)]
+    descs = _descs_gpu(blocs, biais, experts, sorties, cap)
+    f = torch.from_numpy(np.ascontiguousarray(freqs, np.uint16).reshape(-1).view(np.int16)).cuda()
+    octets = torch.zeros(2 * n, dtype=torch.int64, device="cuda")
+    n_esp = int(lib.trc_coder_parties_gpu_espace(C.byref(dims), n, n_delta, n_codes))
+    espace = torch.empty(n_esp + 256, dtype=torch.uint8, device="cuda")
+    e0 = espace.data_ptr() + (-espace.data_ptr()) % 256
+    verifier(lib.trc_coder_parties_gpu(descs.data_ptr(), descs.numel(), n, C.byref(dims), f.data_ptr(), int(canonique),
+                                       couche, n_delta, n_codes, octets.data_ptr(), octets.numel() * 8, e0, n_esp,
+                                       torch.cuda.current_stream().cuda_stream))
+    torch.cuda.current_stream().synchronize()
+    o = octets.cpu().numpy()
+    parts = []
+    for e in range(n):
+        if o[2 * e] == 0 or o[2 * e] > cap:
+            raise ValueError(f"expert {e}: encoding failed (a symbol absent from its table, or too long)")
+        parts.append(sorties[e][:int(o[2 * e])].cpu().numpy().tobytes())
+    return parts
+
+
 def coder_partie_brute(blocs3, biais3, dims: DimsExpert, couche: int = 0, expert: int = 0) -> bytes:
     """The same expert's raw part (9 streams, origin bytes)."""
     b = [np.ascontiguousarray(x) for x in blocs3]
