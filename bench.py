@@ -154,16 +154,17 @@ def octets_pas(c, idx, k):
     return utiles + 4 * E * C + 4 * E + 3 * 4 * 4 * 4096 + 2 * C + 2 * 4 * c.dims.lignes[2]
 
 
-def octets_codes_porte_haut(c, idx, k):
-    """Compressed CODES_CTX bytes of gate and up of the routed experts: what the dominant
-    launch (k_moe_codes, gate/up) must stream from HBM."""
+def octets_codes_dominant(c, idx, k, matrices=(0, 1, 2)):
+    """Compressed CODES_CTX bytes of `matrices` of the routed experts: what the dominant launch
+    (k_moe_codes_dense: gate/up decoded into the GEMV, down decoded alongside) must stream from
+    HBM."""
     total = 0
     for e in idx[:k]:
         p = c.parties[int(e)]
         n = int.from_bytes(p[10:12], "little")
         for i in range(n):
             d = p[64 + 16 * i:80 + 16 * i]
-            if d[0] == 0x04 and d[1] in (0, 1):
+            if d[0] == 0x04 and d[1] in matrices:
                 total += int.from_bytes(d[8:12], "little")
     return total
 
@@ -248,7 +249,7 @@ def notre_bras(args):
     assert (cc.controle.cpu().numpy() == 0).all(), "integrity counters set during the bench"
     idx = idx_journal.cpu().numpy()
     octets = sum(octets_pas(c, idx[s], args.k) for s in range(args.warmup, n_pas))
-    octets_dom = sum(octets_codes_porte_haut(c, idx[s], args.k) for s in range(args.warmup, n_pas))
+    octets_dom = sum(octets_codes_dominant(c, idx[s], args.k) for s in range(args.warmup, n_pas))
     t_total_ms = sum(t_pas)
 
     # ---- phases: the same steps launched eagerly, events recorded between the layer's kernels

@@ -336,7 +336,15 @@ uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32
  * initialisation). */
 uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k);
 
-/* Runs the fused layer. `espace` (256-aligned) >= trc_moe_espace_octets. Compressed parts need
+/* Workspace bytes with which the fused layer overlaps the down projection's decode with gate/up
+ * (k <= 8 activations; beyond, trc_moe_espace_octets): the down codes then go through the
+ * workspace, 16 bytes per MXFP4 block and activation (16.6 MB more for gpt-oss at k = 4). Given
+ * at least this, the layer takes that schedule; given less (but at least trc_moe_espace_octets),
+ * the sequential one. Both give the same bits. */
+uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t k);
+
+/* Runs the fused layer. `espace` (256-aligned) >= trc_moe_espace_octets (see
+ * trc_moe_espace_recouvrant_octets for the faster schedule). Compressed parts need
  * CODES_CTX tiles whose N is a multiple of 32 (trc-codeur writes 256); other N are counted as
  * format errors (decode them with trc_decoder_expert instead). */
 int trc_moe_couche_fusionnee(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);

@@ -4,8 +4,9 @@
   exact and weights within 1e-6 of the f64 softmax (ARCHITECTURE.md 5.6), the reference's
   tie-break known answer and mailbox protocol (trc-noyaux/tests/passe.rs:303-321);
 - SwiGLU within 1e-6 of f64, combine bit for bit against the same sum on the host (no FMA);
-- the exactness invariant: the fused compressed layer, the fused raw layer and the
-  decode-then-multiply sequence give the same bits, step after step;
+- the exactness invariant: the fused compressed layer (both schedules: down decoded alongside
+  gate/up, or after SwiGLU), the fused raw layer and the decode-then-multiply sequence give the
+  same bits, step after step;
 - the layer against the CPU port of the path within a stated tolerance."""
 import numpy as np
 import pytest
@@ -109,14 +110,17 @@ def _trois_chemins(cc, x, residu0):
     return r_f.cpu().numpy(), r_b.cpu().numpy(), r_d.cpu().numpy()
 
 
+@pytest.mark.parametrize("recouvrement", [True, False])
 @pytest.mark.parametrize("nom,k", [("couche_petite", 4), ("couche_gpt_oss", 4), ("couche_gpt_oss", 8)])
-def test_compresse_brut_decode_au_bit(nom, k, request):
+def test_compresse_brut_decode_au_bit(nom, k, recouvrement, request):
     """k = 8 on the gpt-oss shapes has more CODES_CTX tiles (8 x 2 x 127) than the producer /
-    consumer form holds at once: the launch takes the one-warp-per-tile form."""
+    consumer form holds at once: the launch takes the one-warp-per-tile form. Both schedules:
+    the down projection decoded alongside gate/up (its GEMV later, from the decoded words), and
+    the sequential one (its decode fused into its GEMV after SwiGLU)."""
     from troncons_b200.carte import CoucheCarte
 
     c = request.getfixturevalue(nom)
-    cc = CoucheCarte(c, k=k)
+    cc = CoucheCarte(c, k=k, recouvrement=recouvrement)
     cc.preparer_decodee()
     rng = np.random.default_rng(4)
     n_pas = 16 if nom == "couche_gpt_oss" else 64

@@ -137,6 +137,7 @@ def _charger() -> C.CDLL:
         "trc_coder_partie_brute": (i64, [vp, vp, pd, C.c_uint16, C.c_uint16, vp, sz, C.POINTER(u32)]),
         "trc_synth_matrices": (i32, [u64, u32, u32, u32, u32, vp, vp, i32]),
         "trc_moe_espace_octets": (u64, [pd, u32]),
+        "trc_moe_espace_recouvrant_octets": (u64, [pd, u32]),
         "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
         "trc_moe_couche_sans_alloc": (i32, [C.POINTER(MoeCouche), vp]),
@@ -341,3 +342,8 @@ def echange_octets(dims: DimsExpert, jetons: int, monde: int) -> int:
 
 def espace_octets(dims: DimsExpert, k: int) -> int:
     return int(lib.trc_moe_espace_octets(C.byref(dims), k))
+
+
+def espace_recouvrant_octets(dims: DimsExpert, k: int) -> int:
+    """The workspace with which the down projection's decode overlaps gate/up (k <= 8)."""
+    return int(lib.trc_moe_espace_recouvrant_octets(C.byref(dims), k))

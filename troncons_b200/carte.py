@@ -15,7 +15,8 @@ import ctypes as C
 import numpy as np
 import torch
 
-from . import DescDecodage, DescGemv, DimsExpert, MoeCouche, Noyaux, espace_octets, taille_emplacement
+from . import (DescDecodage, DescGemv, DimsExpert, MoeCouche, Noyaux, espace_octets, espace_recouvrant_octets,
+               taille_emplacement)
 from .synth import Couche
 
 
@@ -26,10 +27,12 @@ def _octets(b: bytes, alignement: int = 4096) -> int:
 class CoucheCarte:
     """A layer on the device. `jetons`: tokens per call (x [jetons][d], residual [jetons][d],
     jetons * k activations). `tenus`: the experts [debut, fin) this device holds (an
-    expert-parallel share: the other experts' parts may be None and are never read); None: all."""
+    expert-parallel share: the other experts' parts may be None and are never read); None: all.
+    `recouvrement`: a workspace large enough for the schedule that decodes the down projection
+    alongside gate/up (up to 8 activations); else the sequential schedule's."""
 
     def __init__(self, c: Couche, k: int = 4, brut: bool = True, device: str = "cuda", n_delta: int = 0,
-                 n_codes: int = 0, jetons: int = 1, tenus=None):
+                 n_codes: int = 0, jetons: int = 1, tenus=None, recouvrement: bool = True):
         self.c = c
         self.k = k
         self.jetons = jetons
@@ -51,7 +54,8 @@ class CoucheCarte:
         self.idx = torch.zeros(jetons * k, dtype=torch.int32, device=self.dev)
         self.poids = torch.zeros(jetons * k, dtype=torch.float32, device=self.dev)
         self.controle = torch.zeros(4 * jetons * k, dtype=torch.int32, device=self.dev)
-        self.espace = torch.empty(espace_octets(self.dims, jetons * k) + 256, dtype=torch.uint8, device=self.dev)
+        taille = (espace_recouvrant_octets if recouvrement else espace_octets)(self.dims, jetons * k)
+        self.espace = torch.empty(taille + 256, dtype=torch.uint8, device=self.dev)
         self.n_delta, self.n_codes = n_delta, n_codes
         d = self.dims
         self.R0, self.C0, self.R2 = d.lignes[0], d.colonnes[0], d.lignes[2]

@@ -310,6 +310,12 @@ uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k) {
     return tb::plan_espace(dims->lignes, dims->colonnes, k).total;
 }
 
+uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t k) {
+    if (dims == nullptr || k == 0) return 0;
+    const tb::Espace e = tb::plan_espace(dims->lignes, dims->colonnes, k);
+    return k <= tb::RECOUVRE_MAX ? e.total_recouvrant : e.total;
+}
+
 int trc_moe_couche_fusionnee(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
     return trc_moe_couche_chrono(c, espace, espace_octets, flux, nullptr);
 }
@@ -375,7 +381,7 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
         k.ech.monde = e.monde;
     }
     SUR_LE_FLUX(flux);
-    return statut(tb::lancer_moe(k, espace, static_cast<cudaStream_t>(flux),
+    return statut(tb::lancer_moe(k, espace, espace_octets, static_cast<cudaStream_t>(flux),
                                  reinterpret_cast<cudaEvent_t const*>(evenements)));
 }
 

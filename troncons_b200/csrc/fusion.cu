@@ -43,6 +43,10 @@ Espace plan_espace(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_
     e.h = p;
     p = al256(p + 4ull * lignes[0] * k);
     e.total = p;
+    const uint64_t nb2 = uint64_t(lignes[2]) * (colonnes[2] / 32u);
+    e.cd = p;
+    p = al256(p + 16ull * nb2 * k);
+    e.total_recouvrant = p;
     return e;
 }
 
@@ -50,7 +54,8 @@ struct ArgsMoe {
     Couche c;
     uint8_t* espace;
     Espace plan;
-    uint32_t j0;  // first matrix of this launch (0: gate and up; 2: down)
+    uint32_t j0;     // first matrix of this launch (0: gate and up; 2: down)
+    uint32_t seuls;  // the down projection's codes are decoded with gate/up, into the workspace
 };
 
 // Whether activation i's expert is held by this call (others are skipped: no work, no error).
@@ -90,7 +95,8 @@ __device__ __forceinline__ void copier16(uint4* dst, const uint4* __restrict__ s
 }
 
 constexpr uint32_t DELTA_WARPS = 4;
-constexpr uint32_t MOE_WARPS = 4;
+constexpr uint32_t MOE_WARPS = 8;  // k_moe_brut: warps per block (one row at a time each)
+constexpr uint32_t BRUT_BLOCS_SM = 3;  // its blocks per SM: the grid is one wave of them
 
 // ------------------------------------------------------------------ 1. DELTA -> scales, classes
 
@@ -526,13 +532,43 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     if (t0 < h.T) d.debut(h, t0, voie, anneau);  // the part is a layer input: start before the wait
     attendre_amont();
     liberer_aval();
-    if (j == 2) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    const bool seul = j == 2 && a.seuls != 0u;  // decode only: h does not exist yet
+    if (j == 2 && !seul) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
 
     const uint32_t lut_s = adresse_partagee(lut);
     const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
     const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
     const uint32_t q = voie & 3u, g = voie >> 2;
+    const uint32_t nmacro = h.P / 128u;
+    uint32_t hors_l = 0, pointeur = 0;
+    if (seul) {
+        // The down projection's tiles while gate/up multiply: the words go to the workspace in
+        // stream order (word 32 m + lane = bytes 4 (32 m + lane) .. + 3 of the codes); k_moe_bas
+        // multiplies them once h exists.
+        uint32_t* cd = reinterpret_cast<uint32_t*>(a.espace + a.plan.cd) + uint64_t(i) * 4u * nblocs;
+        for (uint32_t t = t0; t < h.T; t += gridDim.x * DENSE_WARPS) {
+            if (t != t0) d.debut(h, t, voie, anneau);
+            const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+            uint32_t bloc = 8u * m0 + g;
+            uint32_t e0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
+            uint32_t e1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
+            for (uint32_t m = m0; m < m1; ++m) {
+                const uint32_t ctx = bloc < nblocs ? classe_delta(e0) : 0u;
+                const uint32_t e2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
+                d.avancer();
+                const uint32_t mot = d.macro(lut_s + ctx * (M * 4u));
+                if (bloc < nblocs) cd[m * 32u + voie] = mot;
+                bloc += 8u;
+                e0 = e1;
+                e1 = e2;
+            }
+            d.bilan(hors_l, pointeur);
+            d.terminer();
+        }
+        verser_controle(controle, voie, hors_l, pointeur);
+        return;
+    }
     GemvTuile gv;
     gv.R = R;
     gv.B = B;
@@ -541,8 +577,6 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * gv.K;
     gv.med = med;
     gv.puiss = puiss;
-    const uint32_t nmacro = h.P / 128u;
-    uint32_t hors_l = 0, pointeur = 0;
     for (uint32_t t = t0; t < h.T; t += gridDim.x * DENSE_WARPS) {
         if (t != t0) d.debut(h, t, voie, anneau);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
@@ -594,7 +628,7 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
 
 // ------------------------------------------------------------------ raw parts: row-centric
 
-__global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
+__global__ void __launch_bounds__(MOE_WARPS * 32, BRUT_BLOCS_SM) k_moe_brut(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     attendre_amont();
     liberer_aval();
@@ -625,6 +659,90 @@ __global__ void __launch_bounds__(MOE_WARPS * 32) k_moe_brut(ArgsMoe a) {
     float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
     for (uint32_t r = blockIdx.x * MOE_WARPS + (threadIdx.x >> 5); r < R; r += gridDim.x * MOE_WARPS)
         ligne_segments(fc.p, fe.p, x2f4, r, B, voie, parts + uint64_t(r) * K);
+}
+
+// ------------------------------------------------------------------ 4'. down, from decoded words
+
+// The down projection's GEMV once h exists, on the words k_moe_codes_dense decoded alongside
+// gate/up (workspace, stream order): one warp per segment (32 macro-steps), the product and the
+// row / segment closing of the fused kernels (GemvTuile; segments are where tiles close rows
+// too), so the partials are those of the fused down launch, bit for bit. Scales from the
+// medians and the delta bytes of k_moe_delta.
+constexpr uint32_t BAS_WARPS = 8;
+constexpr uint32_t BAS_LOT = 16;  // macro-steps loaded before any is used
+
+__host__ __device__ __forceinline__ uint32_t bas_octets(const Couche& c) {
+    return medianes_octets(c) + 1024u + x2_octets(c.colonnes[2]);
+}
+
+__global__ void __launch_bounds__(BAS_WARPS * 32) k_moe_bas(ArgsMoe a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const Couche& c = a.c;
+    const uint32_t i = blockIdx.z, voie = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    if (!tenu(c, i)) return;
+    const uint32_t R = c.lignes[2], C = c.colonnes[2], B = C / 32u, nblocs = R * B;
+    const uint32_t nmacro = (nblocs + 7u) / 8u;
+    const uint32_t seg0 = blockIdx.x * BAS_WARPS;
+    if (seg0 * SEGMENT_MACRO >= nmacro) return;
+    const uint8_t* partie;
+    uint64_t taille;
+    Flux fm;
+    const bool bon = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_MEDIANES, 2, fm) &&
+                     fm.produits == R && fm.longueur >= R;
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&c.controle[4u * i + CTL_FORMAT], 1u);
+        return;
+    }
+    uint8_t* med = dyn;
+    float* puiss = reinterpret_cast<float*>(dyn + medianes_octets(c));
+    float* x2s = reinterpret_cast<float*>(dyn + medianes_octets(c) + 1024u);
+    charger_puissances(puiss);
+    if (fm.p + ((R + 15u) & ~15u) <= partie + taille)
+        copier16(reinterpret_cast<uint4*>(med), reinterpret_cast<const uint4*>(fm.p), (R + 15u) / 16u);
+    else
+        for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
+    attendre_amont();
+    liberer_aval();
+    charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    __syncthreads();
+    const uint32_t seg = seg0 + warp;
+    if (seg * SEGMENT_MACRO >= nmacro) return;
+    const uint32_t m0 = seg * SEGMENT_MACRO, m1 = min(m0 + SEGMENT_MACRO, nmacro);
+    const uint32_t* __restrict__ cd = reinterpret_cast<const uint32_t*>(a.espace + a.plan.cd) + uint64_t(i) * 4u * nblocs;
+    const uint8_t* __restrict__ ek = a.espace + a.plan.ek[2] + uint64_t(i) * nblocs;
+    const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
+    const uint32_t q = voie & 3u, g = voie >> 2;
+    GemvTuile gv;
+    gv.R = R;
+    gv.B = B;
+    gv.K = a.plan.K[2];
+    gv.voie = voie;
+    gv.parts = reinterpret_cast<float*>(a.espace + a.plan.parts[2]) + uint64_t(i) * R * gv.K;
+    gv.med = med;
+    gv.puiss = puiss;
+    gv.debut(m0, m1);
+    uint32_t bloc = 8u * m0 + g, b = bloc % B;
+    for (uint32_t mb = m0; mb < m1; mb += BAS_LOT) {
+        uint32_t mots[BAS_LOT], es[BAS_LOT];
+#pragma unroll
+        for (uint32_t u = 0; u < BAS_LOT; ++u) {
+            const uint32_t bu = bloc + 8u * u;
+            const bool v = mb + u < m1 && bu < nblocs;
+            mots[u] = v ? __ldg(cd + (mb + u) * 32u + voie) : 0u;
+            es[u] = v ? uint32_t(__ldg(ek + bu)) : 0u;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < BAS_LOT; ++u) {
+            const uint32_t m = mb + u;
+            if (m >= m1) break;
+            const float sq = somme_quad(produit_quad(mots[u], x2s4[X2_PAS * b + q], x2s4[X2_PAS * b + 4u + q]));
+            gv.accumuler(sq, bloc, es[u], bloc < nblocs);
+            gv.fermer(m, m1);
+            bloc += 8u;
+            b += 8u;
+            b -= b >= B ? B : 0u;
+        }
+    }
 }
 
 // ------------------------------------------------------------------ 3. SwiGLU of the gate/up rows
@@ -788,12 +906,23 @@ __device__ void echanger(const Couche& c, uint32_t b, uint32_t r, uint32_t R, fl
 
 // ------------------------------------------------------------------ launcher
 
-cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEvent_t const* ev) {
+// One wave of k_moe_brut blocks over `plans` (matrices x activations) grid planes, each warp
+// looping over its rows; no more blocks per plane than its rows need.
+static uint32_t grille_brut(uint32_t R, uint32_t plans) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t vague = (uint32_t(sms) * BRUT_BLOCS_SM + plans - 1) / plans;
+    return std::max(1u, std::min((R + MOE_WARPS - 1) / MOE_WARPS, vague));
+}
+
+cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cudaStream_t flux, cudaEvent_t const* ev) {
     auto marque = [&](int i) {
         if (ev != nullptr && ev[i] != nullptr) cudaEventRecord(ev[i], flux);
     };
     const uint32_t na = activations(c);
-    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, na), 0};
+    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, na), 0, 0};
+    // The down projection's decode overlaps gate/up when the workspace holds its codes.
+    a.seuls = (!c.brut && na <= RECOUVRE_MAX && espace_octets >= a.plan.total_recouvrant) ? 1u : 0u;
     const uint32_t nd = c.n_delta ? c.n_delta : 256u, nc = c.n_codes ? c.n_codes : 256u;
     uint32_t td = 1, tc = 1;
     for (int j = 0; j < 3; ++j) {
@@ -828,19 +957,40 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
                               dim3(DENSE_WARPS * 32), smem, flux, a);
         };
         marque(1);
-        if ((e = codes(2)) != cudaSuccess) return e;
-        marque(2);
-        if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
-            return e;
-        marque(3);
-        a.j0 = 2;
-        if ((e = codes(1)) != cudaSuccess) return e;
-        marque(4);
+        if (a.seuls) {
+            // gate/up fused with the GEMV, down decoded alone, in one launch; the down GEMV from
+            // the decoded words once h exists (k_moe_bas: the same partials).
+            const size_t smem = disposition_dense(c).total;
+            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes_dense), int(smem))) != cudaSuccess) return e;
+            if ((e = lancer_pdl(k_moe_codes_dense, dim3((tc + DENSE_WARPS - 1) / DENSE_WARPS, 3, na),
+                                dim3(DENSE_WARPS * 32), smem, flux, a)) != cudaSuccess)
+                return e;
+            marque(2);
+            if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+                return e;
+            marque(3);
+            const size_t smem_b = bas_octets(c);
+            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_bas), int(smem_b))) != cudaSuccess) return e;
+            const uint64_t nseg = (uint64_t(c.lignes[2]) * (c.colonnes[2] / 32u) + 8u * SEGMENT_MACRO - 1u) / (8u * SEGMENT_MACRO);
+            if ((e = lancer_pdl(k_moe_bas, dim3(uint32_t((nseg + BAS_WARPS - 1) / BAS_WARPS), 1, na), dim3(BAS_WARPS * 32),
+                                smem_b, flux, a)) != cudaSuccess)
+                return e;
+            marque(4);
+        } else {
+            if ((e = codes(2)) != cudaSuccess) return e;
+            marque(2);
+            if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+                return e;
+            marque(3);
+            a.j0 = 2;
+            if ((e = codes(1)) != cudaSuccess) return e;
+            marque(4);
+        }
     } else {
         const size_t smem = x2_octets(cmax);
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_brut), int(smem))) != cudaSuccess) return e;
         const uint32_t rmax = std::max(c.lignes[0], c.lignes[2]);
-        const uint32_t gx = (rmax + MOE_WARPS - 1) / MOE_WARPS;
+        const uint32_t gx = grille_brut(rmax, 2u * na);
         marque(1);
         if ((e = lancer_pdl(k_moe_brut, dim3(gx, 2, na), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
         marque(2);
@@ -848,7 +998,9 @@ cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEve
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_brut, dim3(gx, 1, na), dim3(MOE_WARPS * 32), smem, flux, a)) != cudaSuccess) return e;
+        if ((e = lancer_pdl(k_moe_brut, dim3(grille_brut(c.lignes[2], na), 1, na), dim3(MOE_WARPS * 32), smem, flux, a)) !=
+            cudaSuccess)
+            return e;
         marque(4);
     }
     if ((e = lancer_pdl(k_moe_combiner, dim3((c.lignes[2] + 255) / 256, c.jetons), dim3(256), 0, flux, a)) != cudaSuccess) return e;

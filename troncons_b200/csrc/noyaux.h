@@ -76,9 +76,14 @@ struct Espace {
     uint64_t ek[3];      // delta byte per block, per matrix, times the activations
     uint64_t parts[3];   // f32 per-segment row partials [activation][R][K] per matrix
     uint64_t h;          // f32 [activation][lignes[0]] SwiGLU output
-    uint64_t total;
+    uint64_t total;      // the sequential schedule's workspace
+    uint64_t cd;         // the overlapped schedule's decoded down codes (16 bytes per block and
+    uint64_t total_recouvrant;  // activation), and its workspace
     uint32_t K[3];       // partial slots per row
 };
+// Activations up to which the down projection's decode may overlap gate/up (its codes then go
+// through the workspace: 16.6 MB for gpt-oss at k = 4).
+constexpr uint32_t RECOUVRE_MAX = 8;
 Espace plan_espace(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t k);
 
 cudaError_t lancer_decodage(const DescDecodage* descs, uint32_t n, const void* partie, uint64_t taille, void* emplacement,
@@ -94,7 +99,7 @@ cudaError_t lancer_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* i
 cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, cudaStream_t flux);
 cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, const float* poids, uint32_t n, uint32_t d,
                             cudaStream_t flux);
-cudaError_t lancer_moe(const Couche& c, void* espace, cudaStream_t flux, cudaEvent_t const* ev = nullptr);
+cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cudaStream_t flux, cudaEvent_t const* ev = nullptr);
 
 // Attention side (mirrors of trc_params_rope, 48 bytes, and trc_params_attention, 32 bytes).
 struct ParamsRope {
