@@ -47,6 +47,11 @@ def arguments():
     a.add_argument("--n-delta", type=int, default=256, help="macro-steps per DELTA tile the parts are encoded with")
     a.add_argument("--n-codes", type=int, default=256, help="macro-steps per CODES_CTX tile")
     a.add_argument("--no-cpu-baseline", action="store_true")
+    a.add_argument("--sequentiel", action="store_true",
+                   help="the sequential schedule (down decoded after SwiGLU, fused into its GEMV) instead of "
+                        "the one that decodes down alongside gate/up")
+    a.add_argument("--codeur", action="store_true",
+                   help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
                    help="N > 1: the combine's exchange in the combine kernel over NVLink (pairs) or by NCCL")
     return a.parse_args()
@@ -65,9 +70,12 @@ def pics():
         return 6650.0, "fallback"
 
 
-# DRAM bytes (read + write) of one gate/up CODES launch measured by ncu (34.03 MB read, 13 KB
-# written) for 31.76 MB of CODES_CTX streams; the rest is the delta bytes, LUTs and headers.
-TRAFIC_CODES_PORTE_HAUT = 34_041_856
+# DRAM bytes (read + write) of the dominant launch measured by ncu on the same launch shape (4
+# routed experts of 2880 x 2880): the decode launch of the overlapped schedule (gate/up decoded
+# into their GEMV, down decoded alongside: 3 x 4 CODES_CTX streams; 51.01 MB read, 1.08 MB
+# written for 47.64 MB of streams), and the sequential schedule's gate/up launch (34.03 MB
+# read, 13 KB written for 31.76 MB of streams).
+TRAFIC_CODES = {"recouvrant": 52_086_528, "sequentiel": 34_041_856}
 
 
 class Horloges:
@@ -186,7 +194,8 @@ def notre_bras(args):
     from troncons_b200.carte import CoucheCarte
 
     c, t_gen = construire_couche(args)
-    cc = CoucheCarte(c, k=args.k, brut=False, n_delta=args.n_delta, n_codes=args.n_codes)
+    cc = CoucheCarte(c, k=args.k, brut=False, n_delta=args.n_delta, n_codes=args.n_codes,
+                     recouvrement=not args.sequentiel)
     n_pas = args.warmup + args.steps
     rng = np.random.default_rng(args.graine + r)
     xs = torch.from_numpy(rng.standard_normal((n_pas, c.dims.colonnes[0])).astype(np.float32)).to(torch.bfloat16)
@@ -249,7 +258,9 @@ def notre_bras(args):
     assert (cc.controle.cpu().numpy() == 0).all(), "integrity counters set during the bench"
     idx = idx_journal.cpu().numpy()
     octets = sum(octets_pas(c, idx[s], args.k) for s in range(args.warmup, n_pas))
-    octets_dom = sum(octets_codes_dominant(c, idx[s], args.k) for s in range(args.warmup, n_pas))
+    ordo = "sequentiel" if args.sequentiel else "recouvrant"
+    matrices_dom = (0, 1) if args.sequentiel else (0, 1, 2)
+    octets_dom = sum(octets_codes_dominant(c, idx[s], args.k, matrices_dom) for s in range(args.warmup, n_pas))
     t_total_ms = sum(t_pas)
 
     # ---- phases: the same steps launched eagerly, events recorded between the layer's kernels
@@ -307,6 +318,7 @@ def notre_bras(args):
             "workload": "config 1: one gpt-oss-120b MoE layer, batch 1, 128 experts, top-4, x bf16[2880], "
                         "router f32 128x2880, SwiGLU alpha 1.702 limit 7, weights resident as .trc v1.2 parts",
             "experts": args.experts, "k": args.k, "n_delta": args.n_delta, "n_codes": args.n_codes,
+            "schedule": ordo,
             "l2": "flushed between steps (256 MB written)", "bytes_per_step": round(octets / args.steps),
             "parallelism": f"replicas x{w}",
         },
@@ -314,13 +326,17 @@ def notre_bras(args):
                 "h2d_bytes_per_step": 2 * c.dims.colonnes[0] + 4 * c.dims.lignes[2],
                 "d2h_bytes_per_step": 4 * c.dims.lignes[2]},
         "gpu_launches": args.steps * 7,
-        "roofline": {"bound": "hbm", "kernel": "k_moe_codes (gate/up: CODES_CTX decode fused into the GEMV)",
+        "roofline": {"bound": "hbm",
+                     "kernel": ("k_moe_codes / k_moe_codes_dense (gate/up: CODES_CTX decode fused into the GEMV)"
+                                if args.sequentiel else
+                                "k_moe_codes_dense (gate/up CODES_CTX decoded into their GEMV, down CODES_CTX "
+                                "decoded alongside)"),
                      "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
                      "peak_source": sorte_pic,
-                     # DRAM read + write bytes of one gate/up launch, from ncu on the same launch
-                     # shape (4 routed experts of 2880 x 2880), summarised under profiles/.
-                     "traffic": TRAFIC_CODES_PORTE_HAUT, "traffic_source": "ncu dram__bytes_read.sum + "
-                     "dram__bytes_write.sum, one gate/up launch of the same shape (summary under profiles/)",
+                     # DRAM read + write bytes of that launch, from ncu on the same launch shape
+                     # (4 routed experts of 2880 x 2880), summarised under profiles/.
+                     "traffic": TRAFIC_CODES[ordo], "traffic_source": "ncu dram__bytes_read.sum + "
+                     "dram__bytes_write.sum, one launch of the same shape (summary under profiles/)",
                      "algorithmic_bytes_per_launch": round(octets_dom / args.steps)},
         "phases_ms": {n: round(sum(v) / len(v), 4) for n, v in
                       zip(["router", "delta", "gate_up", "swiglu", "down", "combine"], t_phase)},
@@ -550,8 +566,83 @@ def bras_reference(args):
     print(json.dumps(ligne), flush=True)
 
 
+def bras_codeur(args):
+    """The GPU `.trc` encoder on `--experts` gpt-oss-shaped experts (one process, one GPU): the
+    layer's symbol counts (trc_comptes_gpu), then every expert's level-0 part in one call
+    (trc_coder_parties_gpu), timed with CUDA events over --steps calls after --warmup; expert
+    0's part checked byte for byte against the CPU encoder, which is timed on one expert."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+
+    dims = T.DimsExpert.gpt_oss()
+    n = args.experts
+    hote = [S.matrices(args.graine + j, dims.lignes[j], dims.colonnes[j], n) for j in range(3)]
+    blocs = [[torch.from_numpy(hote[j][0][e]).cuda() for j in range(3)] for e in range(n)]
+    biais = [[torch.from_numpy(hote[j][1][e]).cuda() for j in range(3)] for e in range(n)]
+    source = sum(b.numel() for b in blocs[0]) * n
+    cap = 2 * sum(b.numel() for b in blocs[0]) + (1 << 16)
+    sorties = [torch.empty(cap, dtype=torch.uint8, device="cuda") for _ in range(n)]
+    descs = S._descs_gpu(blocs, biais, list(range(n)), sorties, cap)
+    comptes = torch.zeros(3 * 4 * 256, dtype=torch.int64, device="cuda")
+    fl = torch.cuda.current_stream().cuda_stream
+
+    def compter():
+        T.verifier(T.lib.trc_comptes_gpu(descs.data_ptr(), descs.numel(), n, C.byref(dims), 1, comptes.data_ptr(),
+                                         comptes.numel() * 8, fl))
+
+    compter()
+    torch.cuda.synchronize()
+    freqs = S.tables_de_comptes(comptes.cpu().numpy().astype(np.uint64).reshape(3, 4, 256))
+    f = torch.from_numpy(freqs.reshape(-1).view(np.int16)).cuda()
+    octets = torch.zeros(2 * n, dtype=torch.int64, device="cuda")
+    n_esp = int(T.lib.trc_coder_parties_gpu_espace(C.byref(dims), n, 256, 256))
+    esp = torch.empty(n_esp + 256, dtype=torch.uint8, device="cuda")
+    e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
+
+    def coder():
+        T.verifier(T.lib.trc_coder_parties_gpu(descs.data_ptr(), descs.numel(), n, C.byref(dims), f.data_ptr(), 1, 0,
+                                               256, 256, octets.data_ptr(), octets.numel() * 8, e0, n_esp, fl))
+
+    def chrono(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    ms_comptes, ms_coder = chrono(compter), chrono(coder)
+    o = octets.cpu().numpy()
+    t0 = time.perf_counter()
+    attendu = S.coder_partie([hote[j][0][0] for j in range(3)], [hote[j][1][0] for j in range(3)], dims, freqs, expert=0)
+    cpu_s = time.perf_counter() - t0
+    assert sorties[0][:int(o[0])].cpu().numpy().tobytes() == attendu, "GPU part differs from the CPU encoder's"
+    print(json.dumps({
+        "metric": "GPU .trc encoder: MXFP4 source bytes encoded into level-0 v1.2 parts per second",
+        "value": round(source / (ms_coder * 1e-3) / 1e9, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_coder, 4), "higher_is_better": True,
+        "dtype": "u8", "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts)",
+        "config": {"workload": f"{n} experts of 3 x 2880 x 2880 MXFP4 (one call), tiles of 256 macro-steps",
+                   "source_bytes": source, "part_bytes": int(o[0::2].sum())},
+        "comptes": {"ms": round(ms_comptes, 4), "GBps": round(source / (ms_comptes * 1e-3) / 1e9, 2)},
+        "cpu_encoder_one_expert_s": round(cpu_s, 4), "gpu_ms_per_expert": round(ms_coder / n, 4),
+        "identical_to_cpu_encoder": True}), flush=True)
+
+
 def main():
     args = arguments()
+    if args.codeur:
+        bras_codeur(args)
+        return
     if args.impl == "reference":
         bras_reference(args)
     elif rang()[1] > 1:

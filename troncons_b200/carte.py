@@ -28,11 +28,12 @@ class CoucheCarte:
     """A layer on the device. `jetons`: tokens per call (x [jetons][d], residual [jetons][d],
     jetons * k activations). `tenus`: the experts [debut, fin) this device holds (an
     expert-parallel share: the other experts' parts may be None and are never read); None: all.
-    `recouvrement`: a workspace large enough for the schedule that decodes the down projection
-    alongside gate/up (up to 8 activations); else the sequential schedule's."""
+    `recouvrement`: a workspace large enough for the fastest schedule (decode-only launches whose
+    GEMVs follow, up to 8 activations); else the sequential schedule's. `espace`: a workspace of
+    exactly that many bytes instead (the schedule follows from its size)."""
 
     def __init__(self, c: Couche, k: int = 4, brut: bool = True, device: str = "cuda", n_delta: int = 0,
-                 n_codes: int = 0, jetons: int = 1, tenus=None, recouvrement: bool = True):
+                 n_codes: int = 0, jetons: int = 1, tenus=None, recouvrement: bool = True, espace: int = 0):
         self.c = c
         self.k = k
         self.jetons = jetons
@@ -54,7 +55,7 @@ class CoucheCarte:
         self.idx = torch.zeros(jetons * k, dtype=torch.int32, device=self.dev)
         self.poids = torch.zeros(jetons * k, dtype=torch.float32, device=self.dev)
         self.controle = torch.zeros(4 * jetons * k, dtype=torch.int32, device=self.dev)
-        taille = (espace_recouvrant_octets if recouvrement else espace_octets)(self.dims, jetons * k)
+        taille = espace or (espace_recouvrant_octets if recouvrement else espace_octets)(self.dims, jetons * k)
         self.espace = torch.empty(taille + 256, dtype=torch.uint8, device=self.dev)
         self.n_delta, self.n_codes = n_delta, n_codes
         d = self.dims
