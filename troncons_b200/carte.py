@@ -29,7 +29,7 @@ class CoucheCarte:
     jetons * k activations). `tenus`: the experts [debut, fin) this device holds (an
     expert-parallel share: the other experts' parts may be None and are never read); None: all.
     `recouvrement`: a workspace large enough for the fastest schedule (decode-only launches whose
-    GEMVs follow, up to 8 activations); else the sequential schedule's. `espace`: a workspace of
+    GEMVs follow, up to 32 activations); else the sequential schedule's. `espace`: a workspace of
     exactly that many bytes instead (the schedule follows from its size)."""
 
     def __init__(self, c: Couche, k: int = 4, brut: bool = True, device: str = "cuda", n_delta: int = 0,
