@@ -276,6 +276,76 @@ int trc_coder_parties_gpu(const trc_desc_codage* descs, size_t descs_octets, uin
 int trc_comptes_gpu(const trc_desc_codage* descs, size_t descs_octets, uint32_t n, const trc_dims_expert* dims,
                     int canonique, uint64_t* comptes, size_t comptes_octets, void* flux);
 
+/* ---------------------------------------------------------------- the expert cache (trc-cache) */
+
+/* The two-tier expert cache of the streaming path (moteur/crates/trc-cache/src/lib.rs:105-301):
+ * `emplacements` device slots, `tiedes` host entries of coded parts (0: no host tier), an LRU
+ * (politiques.rs:47-160) or Belady (politiques.rs:162-260, it reads the future from the trace it
+ * is given: replays only) order per tier. Host code; not thread-safe. */
+typedef struct trc_cache trc_cache;
+
+#define TRC_POLITIQUE_LRU 0u
+#define TRC_POLITIQUE_BELADY 1u
+
+#define TRC_DECISION_SUCCES 0u        /* the expert is (or will be, in flight) in `emplacement` */
+#define TRC_DECISION_DEFAUT_RAM 1u    /* device miss; its coded part is in host entry `tiede` */
+#define TRC_DECISION_DEFAUT_DISQUE 2u /* full miss: read it (into host entry `tiede` if >= 0) */
+
+/* Decision (lib.rs:73-82): 16 bytes. */
+typedef struct trc_decision {
+    uint32_t sorte;       /* TRC_DECISION_* */
+    uint32_t emplacement; /* device slot */
+    int32_t tiede;        /* host entry, or -1 */
+    uint32_t reserve;
+} trc_decision;
+
+/* Compteurs (lib.rs:85-99) plus the host tier's evictions: succes_vram + succes_ram +
+ * defauts_disque = accesses; bytes are counted only after trc_cache_fixer_tailles. */
+typedef struct trc_compteurs_cache {
+    uint64_t succes_vram, succes_ram, defauts_disque, octets_disque, octets_copies, evictions, evictions_ram;
+} trc_compteurs_cache;
+
+/* A routing trace's dimensions (trace.rs:27-41), or its error: erreur 1 = a malformed line
+ * (erreur_ligne), 2 = an expert out of [0, E) (erreur_expert), 3 = empty. */
+typedef struct trc_trace_dims {
+    uint32_t experts, couches, k, jetons;
+    uint32_t erreur, erreur_ligne, erreur_expert, reserve;
+} trc_trace_dims;
+
+/* A new cache (Cache::nouveau). Belady needs the trace it will replay: choix[T][L][k] ids
+ * (ignored for LRU). `casser` != 0: the policies are not told of hits (the reference's broken
+ * policy witness: LRU becomes FIFO). NULL on a usage error. */
+trc_cache* trc_cache_nouveau(uint32_t emplacements, uint32_t tiedes, uint32_t politique, const uint16_t* choix,
+                             uint32_t jetons, uint16_t couches, uint16_t k, uint32_t casser);
+void trc_cache_detruire(trc_cache* cache);
+/* Part sizes per (layer, expert): tailles[couche * experts + expert] (Cache::fixer_tailles). */
+int trc_cache_fixer_tailles(trc_cache* cache, const uint64_t* tailles, uint16_t couches, uint16_t experts);
+/* Serves layer `couche`'s experts at instant t (Cache::demander): pins them, one decision each,
+ * in order. TRC_ERR_USAGE when a miss finds no free or evictable slot (the cache is then
+ * unusable, as after the reference's panic). */
+int trc_cache_demander(trc_cache* cache, uint16_t couche, const uint16_t* experts, uint32_t n, uint64_t t,
+                       trc_decision* decisions);
+/* The slot's part has landed (Cache::pret): in flight -> present. */
+int trc_cache_pret(trc_cache* cache, uint32_t emplacement);
+/* The layer's GEMVs are done (Cache::liberer): its experts are unpinned. */
+int trc_cache_liberer(trc_cache* cache, uint16_t couche);
+void trc_cache_compteurs(const trc_cache* cache, trc_compteurs_cache* sortie);
+/* A slot's state: 0 free, 1 in flight, 2 present; niveau 1 (exact) unless free. */
+int trc_cache_etat(const trc_cache* cache, uint32_t emplacement, uint32_t* etat, uint32_t* niveau);
+/* couche << 16 | expert of a slot's occupant, or -1. */
+int64_t trc_cache_occupant(const trc_cache* cache, uint32_t emplacement);
+/* The device slot / host entry of an expert, or -1. */
+int64_t trc_cache_emplacement_de(const trc_cache* cache, uint16_t couche, uint16_t expert);
+int64_t trc_cache_tiede_de(const trc_cache* cache, uint16_t couche, uint16_t expert);
+/* The pinned experts (couche << 16 | expert) in pinning order; returns their count. */
+uint32_t trc_cache_epingles(const trc_cache* cache, uint32_t* ids, uint32_t capacite);
+/* rejouer (lib.rs:272-301): the trace through a new cache, counted in accesses. */
+int trc_rejouer(const uint16_t* choix, uint32_t jetons, uint16_t couches, uint16_t k, uint32_t emplacements,
+                uint32_t tiedes, uint32_t politique, uint32_t casser, trc_compteurs_cache* sortie);
+/* Trace::depuis_texte (trace.rs:43-133): dims (or the error) into *dims; the T * L * k ids into
+ * `choix` when capacite (in ids) allows. */
+int trc_trace_lire(const char* texte, size_t n, trc_trace_dims* dims, uint16_t* choix, size_t capacite);
+
 /* ---------------------------------------------------------------- new: the fused MoE layer */
 
 /* One MoE layer of one token, fused: routed experts' DELTA -> scales, CODES_CTX decoded in
