@@ -346,6 +346,56 @@ int trc_rejouer(const uint16_t* choix, uint32_t jetons, uint16_t couches, uint16
  * `choix` when capacite (in ids) allows. */
 int trc_trace_lire(const char* texte, size_t n, trc_trace_dims* dims, uint16_t* choix, size_t capacite);
 
+/* ---------------------------------------------------------------- the streaming executor (trc-ordo) */
+
+/* MoE layers whose experts' parts live in host memory and come to the GPU on demand
+ * (trc-ordo's on-demand step, moteur/crates/trc-ordo/src/lib.rs:1054-1367): a pool of
+ * `emplacements` device slots holding parts, managed by the LRU expert cache; per layer call the
+ * routed experts are served, each miss copied from the host tier on the executor's copy stream
+ * (after the last launch that read its slot), and the fused layer runs on the compute stream
+ * once the copies landed. The caller owns every buffer; the executor creates its copy stream,
+ * events and a small pinned staging area. Host code; one thread. */
+typedef struct trc_flux trc_flux;
+
+typedef struct trc_flux_config {
+    uint32_t couches, experts;   /* layers, experts per layer (<= 65,535 each) */
+    uint32_t k, jetons_max;      /* routed experts per token (1..8), tokens per call (1..128) */
+    trc_dims_expert dims;
+    uint32_t emplacements;       /* device part slots, >= k * jetons_max */
+    uint32_t n_delta, n_codes;   /* tile lengths of the parts (0: 256) */
+    uint32_t reserve;
+    uint64_t taille_emplacement; /* bytes per slot: >= every part, a multiple of 256 */
+    uint64_t emplacements_carte; /* device: emplacements * taille_emplacement bytes, 256-aligned */
+    uint64_t parties_hote;       /* host: u64 [couches][experts], each part's address in host memory
+                                    (pinned for the copies to overlap) */
+    uint64_t tailles_parties;    /* host: u64 [couches][experts], their sizes */
+    uint64_t luts;               /* device: u32 [couches][3][4][4096] */
+    uint64_t routeurs;           /* device: f32 [couches][experts][colonnes[0]], or 0 (imposed routing) */
+    uint64_t biais_routeurs;     /* device: f32 [couches][experts] */
+    uint64_t espace;             /* device workspace, trc_flux_espace_octets bytes, 256-aligned */
+    uint64_t flux;               /* the compute stream (cudaStream_t) */
+} trc_flux_config;
+
+/* One layer call: distinct experts served, hits, misses, bytes copied, host wait for the router. */
+typedef struct trc_flux_stats {
+    uint32_t uniques, succes, defauts, reserve;
+    uint64_t octets_copies;
+    double attente_routeur_s;
+} trc_flux_stats;
+
+uint64_t trc_flux_espace_octets(const trc_flux_config* config);
+trc_flux* trc_flux_nouveau(const trc_flux_config* config);
+void trc_flux_detruire(trc_flux* flux);
+/* Layer `couche` on x [jetons][d] (bf16 or f32), residu [jetons][d] f32 updated in place. The
+ * routing: experts_imposes / poids_imposes (host [jetons][k]) when given (a routing trace),
+ * else the layer's router (the host waits for it). The cache's instant is pas * couches +
+ * couche, pas counting calls of the last layer. Asynchronous except for that wait. */
+int trc_flux_couche(trc_flux* flux, uint32_t couche, const void* x, uint32_t x_bf16, float* residu, uint32_t jetons,
+                    const uint32_t* experts_imposes, const float* poids_imposes, trc_flux_stats* stats);
+int trc_flux_compteurs(const trc_flux* flux, trc_compteurs_cache* sortie);
+/* The integrity counters u32[4 * k * jetons_max] accumulated over every call (synchronous copy). */
+int trc_flux_controle(const trc_flux* flux, uint32_t* sortie, uint32_t n);
+
 /* ---------------------------------------------------------------- new: the fused MoE layer */
 
 /* One MoE layer of one token, fused: routed experts' DELTA -> scales, CODES_CTX decoded in
