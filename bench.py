@@ -50,6 +50,11 @@ def arguments():
     a.add_argument("--sequentiel", action="store_true",
                    help="the sequential schedule (down decoded after SwiGLU, fused into its GEMV) instead of "
                         "the one that decodes down alongside gate/up")
+    a.add_argument("--flux", action="store_true",
+                   help="measure the streaming executor on the reference engine's gpt-oss-120b routing trace "
+                        "(parts in pinned host memory, --emplacements device slots)")
+    a.add_argument("--emplacements", type=int, default=326,
+                   help="device part slots of the streaming executor (326: the reference engine's run)")
     a.add_argument("--codeur", action="store_true",
                    help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
@@ -638,8 +643,85 @@ def bras_codeur(args):
         "identical_to_cpu_encoder": True}), flush=True)
 
 
+def bras_flux(args):
+    """The streaming executor (trc_flux_*) on the gpt-oss-120b routing trace the reference's engine
+    wrote (708 tokens x 36 layers x top-4 of 128 experts, tests/golden/traces_boucle.npz): every
+    layer's parts in pinned host memory (one layer's 128 synthetic gpt-oss experts, shared by the 36
+    layers: each (layer, expert) is still its own cache entry and its own copy), --emplacements
+    device slots managed by the LRU expert cache, routing imposed from the trace (weights 1/4).
+    Timed with CUDA events on the compute stream over the whole trace, from a cold cache, as the
+    reference's run was; the cache counts are compared with that run's counters."""
+    import numpy as np
+    import torch
+
+    import troncons_b200.flux as F
+
+    c, t_gen = construire_couche(args)
+    with open(os.path.join(RACINE, "tests", "golden", "traces_boucle.json")) as f:
+        gold = json.load(f)["t120-boucle"]
+    choix = np.load(os.path.join(RACINE, "tests", "golden", "traces_boucle.npz"))["t120_boucle"]
+    T_, L, k = choix.shape
+    if args.steps < T_:
+        T_ = args.steps
+    tampon, adr, tailles = F.tiers_hote(c.parties)
+    luts = torch.from_numpy(np.tile(c.luts.view(np.int32), L)).cuda()
+    fl = F.Flux(c.dims, L, c.experts, k, args.emplacements, np.tile(adr, L), np.tile(tailles, L), luts)
+    x = torch.zeros(1, c.dims.colonnes[0], dtype=torch.bfloat16, device="cuda")
+    r = torch.zeros(1, c.dims.lignes[2], dtype=torch.float32, device="cuda")
+    w = np.full((1, k), 0.25, np.float32)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    octets, t0 = 0, time.time()
+    a.record()
+    for t in range(T_):
+        for l in range(L):
+            octets += fl.couche(l, x, r, choix[t, l].reshape(1, k), w).octets_copies
+    b.record()
+    torch.cuda.synchronize()
+    mur = time.time() - t0
+    ms = a.elapsed_time(b)
+    cpt = fl.compteurs()
+    assert (fl.controle() == 0).all(), "integrity counters set"
+    # The copy engine's own rate: one pinned 1 GiB host-to-device copy, best of 3.
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    pic = 0.0
+    for _ in range(3):
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        pic = max(pic, (1 << 30) / (a.elapsed_time(b) * 1e-3) / 1e9)
+    del src, dst
+    ligne = {
+        "metric": "streaming MoE layers: tokens per second over the reference engine's gpt-oss-120b routing trace",
+        "value": round(T_ / (ms * 1e-3), 2), "unit": "tokens/s", "n_gpus": 1, "steps": T_, "warmup": 0,
+        "ms_per_step": round(ms / T_, 4), "higher_is_better": True, "dtype": "u8",
+        "data": "synthetic gpt-oss-120b-shaped experts (.trc v1.2) in pinned host memory; routing from the "
+                "reference engine's trace",
+        "config": {"workload": f"{T_} tokens x {L} MoE layers, top-{k} of {c.experts}, {args.emplacements} device "
+                               "part slots (LRU), cold start", "emplacements": args.emplacements},
+        "ms_per_layer": round(ms / (T_ * L), 4),
+        "h2d": {"bytes": int(octets), "GBps": round(octets / (ms * 1e-3) / 1e9, 2),
+                "peak_GBps": round(pic, 2), "peak_source": "one pinned 1 GiB host-to-device copy, best of 3",
+                "frac": round(octets / (ms * 1e-3) / 1e9 / pic, 4)},
+        "cache": {"acces": cpt.acces(), "succes": cpt.succes_vram, "defauts": cpt.defauts_disque,
+                  "evictions": cpt.evictions},
+        "wall_s": round(mur, 3), "generation_s": round(t_gen, 1),
+    }
+    if T_ == choix.shape[0]:
+        ref = next((x for x in gold["resultats"] if x["emplacements"] == args.emplacements), None)
+        if ref is not None:
+            ligne["cache_equals_reference_engine"] = (cpt.succes_vram, cpt.defauts_disque, cpt.evictions) == (
+                ref["succes_vram"], ref["defauts_disque"], ref["evictions"])
+    print(json.dumps(ligne), flush=True)
+
+
 def main():
     args = arguments()
+    if args.flux:
+        bras_flux(args)
+        return
     if args.codeur:
         bras_codeur(args)
         return
