@@ -55,6 +55,9 @@ def arguments():
                         "(parts in pinned host memory, --emplacements device slots)")
     a.add_argument("--emplacements", type=int, default=326,
                    help="device part slots of the streaming executor (326: the reference engine's run)")
+    a.add_argument("--prefill", type=int, default=0,
+                   help="measure a batch of this many positions (1..128) through the fused layer and "
+                        "through the layer par flux (each routed expert decoded once for the batch)")
     a.add_argument("--codeur", action="store_true",
                    help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
@@ -717,8 +720,72 @@ def bras_flux(args):
     print(json.dumps(ligne), flush=True)
 
 
+def bras_prefill(args):
+    """One gpt-oss-120b MoE layer (128 resident experts, top-4) on a batch of --prefill positions:
+    router then the fused layer (each activation decodes its expert's tiles), and router then the
+    layer par flux (each distinct routed expert decoded once for the batch), both captured in a
+    CUDA graph, timed with CUDA events over --steps replays after --warmup, L2 flushed between
+    replays; the two residuals are checked bit for bit on every step."""
+    import numpy as np
+    import torch
+
+    from troncons_b200.carte import CoucheCarte
+
+    P = args.prefill
+    c, t_gen = construire_couche(args)
+    cc = CoucheCarte(c, k=args.k, brut=False, jetons=P, n_delta=args.n_delta, n_codes=args.n_codes)
+    d, R2 = c.dims.colonnes[0], c.dims.lignes[2]
+    rng = np.random.default_rng(args.graine)
+    x = torch.from_numpy(rng.standard_normal((P, d)).astype(np.float32)).to(torch.bfloat16).cuda()
+    r0 = torch.from_numpy(rng.standard_normal((P, R2)).astype(np.float32)).cuda()
+    rf, rp = r0.clone(), r0.clone()
+    vidange = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        cc.couche(x, rf)
+        cc.couche_par_flux(x, rp)
+    torch.cuda.synchronize()
+    graphes = {}
+    for nom, f in (("fusionnee", lambda: cc.couche(x, rf)), ("par_flux", lambda: cc.couche_par_flux(x, rp))):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            f()
+        graphes[nom] = g
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    temps = {"fusionnee": [], "par_flux": []}
+    egaux = True
+    for s in range(args.warmup + args.steps):
+        for nom in ("fusionnee", "par_flux"):
+            (rf if nom == "fusionnee" else rp).copy_(r0)
+            vidange.zero_()
+            a.record()
+            graphes[nom].replay()
+            b.record()
+            torch.cuda.synchronize()
+            if s >= args.warmup:
+                temps[nom].append(a.elapsed_time(b))
+        egaux &= bool(torch.equal(rf.view(torch.int32), rp.view(torch.int32)))
+    assert (cc.controle.cpu().numpy() == 0).all()
+    ms = {n: sum(v) / len(v) for n, v in temps.items()}
+    idx = cc.idx.cpu().numpy()
+    print(json.dumps({
+        "metric": "MoE layer over a batch of positions: positions per second, layer par flux",
+        "value": round(P / (ms["par_flux"] * 1e-3), 1), "unit": "positions/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms["par_flux"], 4), "higher_is_better": True, "dtype": "u8",
+        "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
+        "config": {"workload": f"one gpt-oss-120b MoE layer, {P} positions, 128 experts, top-{args.k}",
+                   "distinct_experts": int(len(np.unique(idx))), "l2": "flushed between replays"},
+        "fused_ms_per_step": round(ms["fusionnee"], 4),
+        "fused_positions_per_s": round(P / (ms["fusionnee"] * 1e-3), 1),
+        "speedup_vs_fused": round(ms["fusionnee"] / ms["par_flux"], 3),
+        "bit_identical_to_fused": egaux, "generation_s": round(t_gen, 1)}), flush=True)
+    del graphes
+
+
 def main():
     args = arguments()
+    if args.prefill:
+        bras_prefill(args)
+        return
     if args.flux:
         bras_flux(args)
         return

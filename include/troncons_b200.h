@@ -469,6 +469,20 @@ uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t 
  * format errors (decode them with trc_decoder_expert instead). */
 int trc_moe_couche_fusionnee(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);
 
+/* Workspace bytes of trc_moe_couche_par_flux for these dimensions, experts per layer and
+ * activations (tokens x k): a decoded slot per distinct routed expert (at most
+ * min(activations, experts); 13,254,144 bytes each for gpt-oss) and per-activation vectors. */
+uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t experts, uint32_t activations);
+
+/* The layer over a batch of positions "par flux" (the reference's prefill by stream,
+ * trc-modele/src/lib.rs:607-717, trc-ordo/src/lib.rs:782-981): each distinct routed expert is
+ * decoded once for the whole batch into a slot of the workspace, then applied to every position
+ * routed to it with the token-by-token arithmetic, so the residuals are bit-identical to
+ * trc_moe_couche_fusionnee's on the same descriptor. Compressed parts of every expert on this
+ * device (no brut, no expert share, no exchange). The controle of an activation receives its
+ * expert's decode counters. */
+int trc_moe_couche_par_flux(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);
+
 /* trc_moe_couche_fusionnee, recording evenements[0..5] (cudaEvent_t, each may be NULL) on the
  * stream: before the DELTA phase, after it, after gate/up, after SwiGLU, after down, after the
  * combine (raw parts: no DELTA phase, [1] is recorded with [0]). For timing each phase with CUDA

@@ -1,0 +1,62 @@
+"""GPU: the layer "par flux" (trc_moe_couche_par_flux, the reference's prefill by stream): each
+distinct routed expert decoded once for the batch, then applied to every position routed to it.
+
+Its residuals equal the fused layer's bit for bit (the token-by-token arithmetic: the
+reference's proposition 5, layer-by-layer order = token-by-token order) on the same routing,
+for batches of 1 to 128 positions, k = 4 and 8, the small and gpt-oss shapes; a routed expert
+whose part is absent is counted as a format error of every activation routed to it."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _deux(cc, x, r0):
+    rf, rp = r0.clone(), r0.clone()
+    cc.controle.zero_()
+    cc.couche(x, rf)
+    ctl_f = cc.controle.clone()
+    cc.controle.zero_()
+    cc.couche_par_flux(x, rp, routeur=False)
+    torch.cuda.synchronize()
+    return rf, rp, ctl_f, cc.controle.clone()
+
+
+@pytest.mark.parametrize("nom,k,jetons", [("couche_petite", 4, 1), ("couche_petite", 4, 7), ("couche_petite", 4, 128),
+                                          ("couche_petite", 8, 33), ("couche_gpt_oss", 4, 16),
+                                          ("couche_gpt_oss", 8, 5)])
+def test_par_flux_egale_la_couche_fusionnee(nom, k, jetons, request):
+    from troncons_b200.carte import CoucheCarte
+
+    c = request.getfixturevalue(nom)
+    cc = CoucheCarte(c, k=k, brut=False, jetons=jetons)
+    rng = np.random.default_rng(17 + jetons + k)
+    d = c.dims.colonnes[0]
+    for pas in range(3):
+        x = torch.from_numpy(rng.standard_normal((jetons, d)).astype(np.float32)).to(torch.bfloat16).cuda()
+        r0 = torch.from_numpy(rng.standard_normal((jetons, c.dims.lignes[2])).astype(np.float32)).cuda()
+        rf, rp, ctl_f, ctl_p = _deux(cc, x, r0)
+        assert (ctl_f == 0).all() and (ctl_p == 0).all()
+        assert torch.equal(rf.view(torch.int32), rp.view(torch.int32)), f"step {pas}"
+
+
+def test_par_flux_expert_absent_compte(couche_petite):
+    """Expert 3's part is absent: the activations routed to it are counted as format errors and
+    left out of their positions' sums; the others are unaffected."""
+    from troncons_b200.carte import CoucheCarte
+
+    cc = CoucheCarte(couche_petite, k=4, brut=False, jetons=4)
+    cc.adresses[3] = 0
+    idx = np.array([[0, 1, 2, 4], [3, 5, 6, 7], [1, 3, 0, 2], [4, 5, 6, 7]], np.int32)
+    cc.idx.copy_(torch.from_numpy(idx.reshape(-1)))
+    cc.poids.copy_(torch.full((16,), 0.25))
+    x = torch.ones(4, 512, dtype=torch.bfloat16, device="cuda")
+    r = torch.zeros(4, couche_petite.dims.lignes[2], dtype=torch.float32, device="cuda")
+    cc.controle.zero_()
+    cc.couche_par_flux(x, r, routeur=False)
+    torch.cuda.synchronize()
+    ctl = cc.controle.cpu().numpy().reshape(16, 4)
+    touche = (idx.reshape(-1) == 3)
+    assert (ctl[touche, 1] >= 1).all() and (ctl[~touche, 1] == 0).all()
+    assert torch.isfinite(r).all()

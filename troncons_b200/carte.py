@@ -133,6 +133,22 @@ class CoucheCarte:
         self._desc = self.descripteur(x, residu, brute, partiel, echange)  # alive while the launch reads it
         self.n.moe_couche(self._desc, self._espace(), flux, evenements)
 
+    def couche_par_flux(self, x: torch.Tensor, residu: torch.Tensor, flux=None, routeur: bool = True):
+        """Router then the layer "par flux" (trc_moe_couche_par_flux): each distinct routed expert
+        decoded once for the batch; the residuals are the fused layer's bits."""
+        from . import lib, verifier
+
+        if routeur:
+            self.routeur(x, flux)
+        if getattr(self, "_espace_pf", None) is None:
+            n = int(lib.trc_moe_par_flux_espace_octets(C.byref(self.dims), self.c.experts, self.jetons * self.k))
+            self._espace_pf = torch.empty(n + 256, dtype=torch.uint8, device=self.dev)
+            self._n_pf = n
+        e = self._espace_pf.data_ptr() + (-self._espace_pf.data_ptr()) % 256
+        self._desc_pf = self.descripteur(x, residu, False)
+        f = (flux or torch.cuda.current_stream()).cuda_stream
+        verifier(lib.trc_moe_couche_par_flux(C.byref(self._desc_pf), e, self._n_pf, f))
+
     # ---------------------------------------------------------------- decode-then-multiply
 
     def preparer_decodee(self):

@@ -305,23 +305,10 @@ uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32
     return tb::disposition_echange(dims->lignes[2], jetons ? jetons : 1u, monde).total;
 }
 
-uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k) {
-    if (dims == nullptr || k == 0) return 0;
-    return tb::plan_espace(dims->lignes, dims->colonnes, k).total;
-}
+namespace {
 
-uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t k) {
-    if (dims == nullptr || k == 0) return 0;
-    const tb::Espace e = tb::plan_espace(dims->lignes, dims->colonnes, k);
-    return k <= tb::RECOUVRE_MAX ? e.total_recouvrant : e.total;
-}
-
-int trc_moe_couche_fusionnee(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
-    return trc_moe_couche_chrono(c, espace, espace_octets, flux, nullptr);
-}
-
-int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux,
-                          void* const* evenements) {
+// The descriptor's checks (Noyaux's usage rules for the layer's launches) and its translation.
+int couche_de(const trc_moe_couche* c, tb::Couche& k) {
     if (c == nullptr) return usage("layer descriptor absent");
     if (int s = verifier_dims(&c->dims)) return s;
     const trc_dims_expert& d = c->dims;
@@ -343,10 +330,7 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
         return usage("layer descriptor: a device buffer is missing");
     if (!aligne(c->x, c->x_bf16 ? 2 : 4)) return usage("x misaligned");
     if (!c->brut && !aligne(c->luts, 16)) return usage("LUTs misaligned (16 bytes)");
-    const uint64_t besoin = tb::plan_espace(d.lignes, d.colonnes, c->k * jetons).total;
-    if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
-        return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
-    tb::Couche k{};
+    k = tb::Couche{};
     k.parties = c->parties;
     k.parties_octets = c->parties_octets;
     k.experts = c->experts;
@@ -380,9 +364,53 @@ int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_o
         k.ech.rang = e.rang;
         k.ech.monde = e.monde;
     }
+    return TRC_OK;
+}
+
+}  // namespace
+
+uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k) {
+    if (dims == nullptr || k == 0) return 0;
+    return tb::plan_espace(dims->lignes, dims->colonnes, k).total;
+}
+
+uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t k) {
+    if (dims == nullptr || k == 0) return 0;
+    const tb::Espace e = tb::plan_espace(dims->lignes, dims->colonnes, k);
+    return k <= tb::RECOUVRE_MAX ? e.total_recouvrant : e.total;
+}
+
+int trc_moe_couche_fusionnee(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
+    return trc_moe_couche_chrono(c, espace, espace_octets, flux, nullptr);
+}
+
+int trc_moe_couche_chrono(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux,
+                          void* const* evenements) {
+    tb::Couche k;
+    if (const int r = couche_de(c, k)) return r;
+    const uint64_t besoin = tb::plan_espace(k.lignes, k.colonnes, c->k * k.jetons).total;
+    if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
+        return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
     SUR_LE_FLUX(flux);
     return statut(tb::lancer_moe(k, espace, espace_octets, static_cast<cudaStream_t>(flux),
                                  reinterpret_cast<cudaEvent_t const*>(evenements)));
+}
+
+uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t experts, uint32_t activations) {
+    if (dims == nullptr || experts == 0 || activations == 0) return 0;
+    return tb::plan_par_flux(dims->lignes, dims->colonnes, experts, activations).total;
+}
+
+int trc_moe_couche_par_flux(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
+    tb::Couche k;
+    if (const int r = couche_de(c, k)) return r;
+    if (k.brut || k.expert_fin != 0 || k.partiel || k.ech.monde != 0)
+        return usage("par flux: compressed parts of every expert on this device only (no raw parts, share or exchange)");
+    const uint64_t besoin = tb::plan_par_flux(k.lignes, k.colonnes, k.experts, k.k * k.jetons).total;
+    if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
+        return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_par_flux(k, espace, static_cast<cudaStream_t>(flux)));
 }
 
 // ---------------------------------------------------------------- attention side (lib.rs:291-381)

@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
     const uint32_t* luts;
     uint32_t* controle;
     choisir_expert(a, partie, taille, emplacement, luts, controle);
+    if (partie == nullptr) return;  // a batch entry with no expert (batches sized for their most)
     const uint32_t j = blockIdx.y, voie = threadIdx.x & 31u;
     const uint32_t R = choisir(a.dims.lignes, j), C = choisir(a.dims.colonnes, j);
     const uint32_t B = C / 32u, nblocs = R * B;
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
     const uint32_t* luts;
     uint32_t* controle;
     choisir_expert(a, partie, taille, emplacement, luts, controle);
+    if (partie == nullptr) return;  // a batch entry with no expert (batches sized for their most)
     const uint32_t j = blockIdx.y, voie = threadIdx.x & 31u;
     const uint32_t R = choisir(a.dims.lignes, j), C = choisir(a.dims.colonnes, j);
     const uint32_t B = C / 32u, nblocs = R * B;

@@ -152,39 +152,7 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
 }
 
 // ------------------------------------------------------------------ shared-memory x2 = 2 x
-
-// 2x in shared memory, padded: the 8 float4 of 32-column block b (x2[32 b + 4 k .. + 3], k = 0..7)
-// at float4 index 12 b + k. A quarter-warp's 8 lanes read one float4 each from two neighbouring
-// blocks; 12 float4 (192 bytes) per block put those blocks 16 banks apart, where 8 (128 bytes)
-// would put them on the same banks.
-constexpr uint32_t X2_PAS = 12;
-__host__ __device__ __forceinline__ uint32_t x2_octets(uint32_t C) { return (C / 32u) * X2_PAS * 16u; }
-__device__ __forceinline__ uint32_t x2_indice(uint32_t i) { return X2_PAS * (i / 8u) + (i % 8u); }  // float4 i of 2x
-
-// The padded 2x of x (bf16 or f32, C a multiple of 32); 16-byte loads when x is 16-aligned.
-__device__ __forceinline__ void charger_x2(float* x2s, const void* x, uint32_t bf16, uint32_t C) {
-    float4* d4 = reinterpret_cast<float4*>(x2s);
-    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
-        if (bf16) {
-            const uint4* s4 = static_cast<const uint4*>(x);
-            for (uint32_t t = threadIdx.x; t < C / 8u; t += blockDim.x) {
-                const uint4 v = __ldg(s4 + t);
-                d4[x2_indice(2u * t)] = make_float4(2.0f * __uint_as_float(v.x << 16), 2.0f * __uint_as_float(v.x & 0xFFFF0000u),
-                                                    2.0f * __uint_as_float(v.y << 16), 2.0f * __uint_as_float(v.y & 0xFFFF0000u));
-                d4[x2_indice(2u * t + 1u)] = make_float4(2.0f * __uint_as_float(v.z << 16), 2.0f * __uint_as_float(v.z & 0xFFFF0000u),
-                                                         2.0f * __uint_as_float(v.w << 16), 2.0f * __uint_as_float(v.w & 0xFFFF0000u));
-            }
-        } else {
-            const float4* s4 = static_cast<const float4*>(x);
-            for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x) d4[x2_indice(t)] = fois2(__ldg(s4 + t));
-        }
-        return;
-    }
-    for (uint32_t t = threadIdx.x; t < C; t += blockDim.x) {
-        const float v = bf16 ? __uint_as_float(uint32_t(static_cast<const uint16_t*>(x)[t]) << 16) : static_cast<const float*>(x)[t];
-        x2s[4u * x2_indice(t / 4u) + (t % 4u)] = 2.0f * v;
-    }
-}
+// (X2_PAS, x2_octets, x2_indice, charger_x2: mxfp4.cuh)
 
 // ------------------------------------------------------------------ 2/4. CODES_CTX decoded into the GEMV
 

@@ -81,6 +81,15 @@ struct Espace {
     uint64_t total_recouvrant;  // activation), and its workspace
     uint32_t K[3];       // partial slots per row
 };
+// Workspace of the layer "par flux" (par_flux.cu): decoded slots of the batch's distinct
+// experts, the decode batch, the grouping, per-activation gate / up / h / down outputs.
+struct EspaceParFlux {
+    uint64_t slots, descs, nu, ordre, slot_de, debut, liste, ctl, g, u, h, y, total, taille_slot;
+    uint32_t U;  // slots: min(activations, experts)
+};
+EspaceParFlux plan_par_flux(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts, uint32_t na);
+cudaError_t lancer_par_flux(const Couche& c, void* espace, cudaStream_t flux);
+
 // Activations up to which the down projection's decode may overlap gate/up (its codes then go
 // through the workspace: 4.15 MB per activation for gpt-oss; measured faster than the
 // sequential schedule at 4, 8, 16 and 32 activations on one GPU).
