@@ -30,6 +30,20 @@ namespace {
 
 constexpr uint32_t RING = 8;
 
+// Up to three host-to-device moves in one launch, from mapped pinned memory: the layer's part
+// table and the imposed routing. A kernel, not a copy: a copy on the compute stream would wait
+// in the copy engine's queue behind the large part copies already issued for later layers.
+struct Transferts {
+    uint4* dst[3];
+    const uint4* src[3];
+    uint32_t n[3];  // 16-byte words
+};
+
+__global__ void __launch_bounds__(256) k_transferer(Transferts t) {
+    for (int i = 0; i < 3; ++i)
+        for (uint32_t w = threadIdx.x; w < t.n[i]; w += blockDim.x) t.dst[i][w] = t.src[i][w];
+}
+
 struct Disposition {
     uint64_t table, idx, poids, logits, controle, moe, total;
 };
@@ -63,7 +77,9 @@ struct trc_flux {
     cudaStream_t calcul = nullptr, copie = nullptr;
     cudaEvent_t fin[RING] = {}, copies[RING] = {}, routeur = nullptr;
     bool fin_utilise[RING] = {};
-    uint8_t* hote = nullptr;  // pinned staging: per ring entry [table 16 E][idx 4 na][poids 4 na]; then idx read back
+    uint8_t* hote = nullptr;  // mapped pinned staging: per ring entry [table 16 E][idx][poids] (16-aligned);
+                              // then the router's indices read back
+    uint8_t* hote_carte = nullptr;  // its device address
     uint64_t pas_hote = 0;
     uint64_t appel = 0, pas = 0;
     std::vector<int64_t> lecteur;  // per slot: the last call whose layer read it (-1: none)
@@ -126,14 +142,15 @@ trc_flux* trc_flux_nouveau(const trc_flux_config* c) {
                        reinterpret_cast<const uint64_t*>(c->parties_hote) + uint64_t(c->couches) * c->experts);
     f->tailles.assign(tailles, tailles + uint64_t(c->couches) * c->experts);
     const uint64_t na = uint64_t(c->jetons_max) * c->k;
-    f->pas_hote = tb::al256(16ull * c->experts + 8 * na);
+    f->pas_hote = tb::al256(16ull * c->experts + 2 * ((4 * na + 15) / 16 * 16));
     cudaError_t e = cudaStreamCreateWithFlags(&f->copie, cudaStreamNonBlocking);
     for (uint32_t i = 0; i < RING && e == cudaSuccess; ++i) {
         e = cudaEventCreateWithFlags(&f->fin[i], cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f->copies[i], cudaEventDisableTiming);
     }
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f->routeur, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaHostAlloc(&f->hote, f->pas_hote * RING + 4 * na, cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaHostAlloc(&f->hote, f->pas_hote * RING + 4 * na, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&f->hote_carte), f->hote, 0);
     // The table starts empty (every address 0) and the integrity counters at 0.
     uint8_t* esp = reinterpret_cast<uint8_t*>(c->espace);
     if (e == cudaSuccess) e = cudaMemsetAsync(esp + f->d.table, 0, 16ull * c->couches * c->experts, f->calcul);
@@ -163,8 +180,10 @@ int trc_flux_couche(trc_flux* f, uint32_t couche, const void* x, uint32_t x_bf16
     float* poids_dev = reinterpret_cast<float*>(esp + f->d.poids);
     const uint32_t r = uint32_t(f->appel % RING);
     uint8_t* st = f->hote + r * f->pas_hote;
+    const uint64_t n16 = (4ull * na + 15) / 16;  // 16-byte words of idx, and of poids
     uint32_t* idx_st = reinterpret_cast<uint32_t*>(st + 16ull * E);
-    float* poids_st = reinterpret_cast<float*>(st + 16ull * E + 4ull * na);
+    float* poids_st = reinterpret_cast<float*>(st + 16ull * E + 16 * n16);
+    uint8_t* st_carte = f->hote_carte + r * f->pas_hote;
     uint32_t* idx_lu = reinterpret_cast<uint32_t*>(f->hote + f->pas_hote * RING);
     trc_flux_stats s{};
     cudaError_t e;
@@ -179,10 +198,7 @@ int trc_flux_couche(trc_flux* f, uint32_t couche, const void* x, uint32_t x_bf16
             if (experts_imposes[i] >= E) return usage("streaming layer: an imposed expert is out of range");
         std::memcpy(idx_st, experts_imposes, 4ull * na);
         std::memcpy(poids_st, poids_imposes, 4ull * na);
-        if ((e = cudaMemcpyAsync(idx_dev, idx_st, 4ull * na, cudaMemcpyHostToDevice, f->calcul)) != cudaSuccess ||
-            (e = cudaMemcpyAsync(poids_dev, poids_st, 4ull * na, cudaMemcpyHostToDevice, f->calcul)) != cudaSuccess)
-            return tb::erreur_cuda(e);
-        experts = experts_imposes;
+        experts = experts_imposes;  // moved to the device with the part table (step 4)
     } else {
         const float* wr = reinterpret_cast<const float*>(c.routeurs) + uint64_t(couche) * E * c.dims.colonnes[0];
         const float* br = reinterpret_cast<const float*>(c.biais_routeurs) + uint64_t(couche) * E;
@@ -244,8 +260,20 @@ int trc_flux_couche(trc_flux* f, uint32_t couche, const void* x, uint32_t x_bf16
         tab[E + uniques[j]] = f->tailles[uint64_t(couche) * E + uniques[j]];
     }
     uint64_t* table_dev = reinterpret_cast<uint64_t*>(esp + f->d.table) + 2ull * couche * E;
-    if ((e = cudaMemcpyAsync(table_dev, tab, 16ull * E, cudaMemcpyHostToDevice, f->calcul)) != cudaSuccess)
-        return tb::erreur_cuda(e);
+    Transferts tr{};
+    tr.dst[0] = reinterpret_cast<uint4*>(table_dev);
+    tr.src[0] = reinterpret_cast<const uint4*>(st_carte);
+    tr.n[0] = E;
+    if (experts_imposes != nullptr) {
+        tr.dst[1] = reinterpret_cast<uint4*>(idx_dev);
+        tr.src[1] = reinterpret_cast<const uint4*>(st_carte + 16ull * E);
+        tr.n[1] = uint32_t(n16);
+        tr.dst[2] = reinterpret_cast<uint4*>(poids_dev);
+        tr.src[2] = reinterpret_cast<const uint4*>(st_carte + 16ull * E + 16 * n16);
+        tr.n[2] = uint32_t(n16);
+    }
+    k_transferer<<<1, 256, 0, f->calcul>>>(tr);
+    if ((e = cudaGetLastError()) != cudaSuccess) return tb::erreur_cuda(e);
     trc_moe_couche m{};
     m.parties = table_dev;
     m.parties_octets = table_dev + E;
