@@ -154,3 +154,34 @@ def test_couche_contre_le_port_cpu(couche_gpt_oss):
         g = r.cpu().numpy()
         # Tolerance: f32 sums of 2,880 terms in two orders (a few ulps of the row magnitudes).
         assert np.abs(g - res_cpu).max() <= 1e-4 * max(1.0, np.abs(res_cpu).max())
+
+
+@pytest.mark.parametrize("jetons,n_codes", [(1, 32), (3, 64), (8, 256)])
+def test_ordonnancements_au_bit(couche_gpt_oss, jetons, n_codes):
+    """The same layer through both schedules (the workspace's size picks one): the sequential
+    (down decoded into its GEMV after SwiGLU) and the overlapped (down decoded alongside gate/up,
+    its GEMV later on the decoded words) give the same residual bits, for 4 to 32 activations and
+    tiles of 32, 64 and 256 macro-steps (parts re-encoded with that tile length)."""
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+    from troncons_b200.carte import CoucheCarte
+
+    c = S.couche(20261201, T.DimsExpert.gpt_oss(), 8, brut=False, n_delta=n_codes, n_codes=n_codes) \
+        if n_codes != 256 else couche_gpt_oss
+    d = c.dims
+    na = 4 * jetons
+    seq = T.espace_octets(d, na)
+    rec = T.espace_recouvrant_octets(d, na)
+    assert rec > seq
+    cs = CoucheCarte(c, k=4, brut=False, jetons=jetons, n_delta=n_codes, n_codes=n_codes, espace=seq)
+    cr = CoucheCarte(c, k=4, brut=False, jetons=jetons, n_delta=n_codes, n_codes=n_codes, espace=rec)
+    rng = np.random.default_rng(jetons + n_codes)
+    for _ in range(3):
+        x = torch.from_numpy(rng.standard_normal((jetons, d.colonnes[0])).astype(np.float32)).to(torch.bfloat16).cuda()
+        r0 = torch.from_numpy(rng.standard_normal((jetons, d.lignes[2])).astype(np.float32)).cuda()
+        a, b = r0.clone(), r0.clone()
+        cs.couche(x, a)
+        cr.couche(x, b)
+        torch.cuda.synchronize()
+        assert (cs.controle == 0).all() and (cr.controle == 0).all()
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))

@@ -16,6 +16,11 @@
 //   3. k_moe_swiglu  gate and up rows = fold of their partials + bias; h = SwiGLU (f64);
 //   4. k_moe_codes   (down) the same on h;
 //   5. k_moe_combiner down rows + bias, then residual += ((w0 s0 + w1 s1) + ...), no FMA.
+// That is the sequential schedule. Given a workspace that holds the down projection's decoded
+// words (up to 32 activations), the overlapped schedule runs 2 and 4's decode in ONE launch of
+// k_moe_codes_dense (gate/up tiles decoded into their GEMV, down tiles decoded alone into the
+// workspace), then 3, then k_moe_bas (the down GEMV on those words, segment by segment, with the
+// same closing), then 5: the down chain runs during gate/up. Both give the same bits.
 // The raw path (`brut`) replaces 1-2 and 4 by k_moe_brut, a row-centric GEMV on CODES_BRUTS /
 // ECHELLES_BRUTES writing the same partials, so compressed and raw parts give the same bits.
 // Integrity counters go to controle[4 i ..] of active expert i (format errors included).
