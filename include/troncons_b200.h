@@ -396,6 +396,66 @@ int trc_flux_compteurs(const trc_flux* flux, trc_compteurs_cache* sortie);
 /* The integrity counters u32[4 * k * jetons_max] accumulated over every call (synchronous copy). */
 int trc_flux_controle(const trc_flux* flux, uint32_t* sortie, uint32_t n);
 
+/* ---------------------------------------------------------------- the whole decode step (trc-modele) */
+
+/* Row `ligne` of a Q8_0 matrix (34-byte blocks) of `colonnes` columns into y f32[colonnes],
+ * exact. Replaces `Noyaux::ligne_q8_0` (trc-noyaux/src/lib.rs:478-486; passe.cuh:623-634). */
+int trc_ligne_q8_0(const void* w, size_t w_octets, uint32_t ligne, uint32_t colonnes, float* y, size_t y_octets, void* flux);
+
+/* Index of the largest of n floats into *sortie (u32): ties to the smallest index, a NaN never
+ * chosen (all NaN: 0xFFFFFFFF). Replaces `Noyaux::argmax` (lib.rs:488-496; passe.cuh:636-669). */
+int trc_argmax(const float* v, size_t v_octets, uint32_t n, uint32_t* sortie, size_t sortie_octets, void* flux);
+
+/* One layer's tensors on the device (the reference's `Couche` of trc-modele/src/lib.rs:400-418):
+ * 152 bytes. f32 vectors, Q8_0 matrices, f16 KV caches of `anneau` cases (sliding layers) or of
+ * the context; the experts' parts table (u64 addresses and sizes) and the layer's LUTs. */
+typedef struct trc_modele_couche {
+    uint64_t attn_norm, wq, bq, wk, bk, wv, bv, wo, bo, puits, post_norm, wr, br;
+    uint64_t cache_k, cache_v;
+    uint64_t parties, parties_octets, luts;
+    uint32_t anneau, reserve;
+} trc_modele_couche;
+
+/* The model (`Hyper` + the resident tensors, trc-modele/src/lib.rs:60-83, 342-356): 176 bytes. */
+typedef struct trc_modele_config {
+    uint32_t couches, d, tetes, tetes_kv, dim_tete, experts, k, vocab, contexte;
+    uint32_t brut;             /* 1: the parts are raw (ECHELLES_BRUTES / CODES_BRUTS / BIAIS) */
+    uint32_t n_delta, n_codes; /* tile lengths of the parts (0: 256) */
+    float eps;
+    uint32_t reserve;
+    trc_params_rope rope;
+    trc_dims_expert dims;
+    uint64_t couches_desc;     /* host: trc_modele_couche[couches] */
+    uint64_t enchassement;     /* device: Q8_0 [vocab][d] */
+    uint64_t norme_sortie;     /* device: f32 [d] */
+    uint64_t sortie;           /* device: Q8_0 [vocab][d] */
+    uint64_t espace;           /* device workspace, trc_modele_espace_octets bytes, 256-aligned */
+    uint64_t espace_octets;
+} trc_modele_config;
+
+uint64_t trc_modele_espace_octets(const trc_modele_config* m);
+/* Device addresses of the last step's logits (f32[vocab]), greedy token (u32) and the MoE
+ * integrity counters (u32[4 k], accumulated; zero them with the workspace). */
+int trc_modele_sorties(const trc_modele_config* m, uint64_t* logits, uint64_t* jeton, uint64_t* controle);
+/* One token at `position` (Modele::enchasser, debut_couche + the fused layer per layer,
+ * sortie; trc-modele/src/lib.rs:476-568), asynchronous on `flux`; sortie = 0 skips the
+ * unembedding (a context token). */
+int trc_modele_pas(const trc_modele_config* m, uint32_t jeton, uint32_t position, uint32_t sortie, void* flux);
+
+/* Seeded synthetic tensors on the GPU (inputs of tests and benches; no counterpart): R x C
+ * MXFP4 as 17-byte blocks + f32 biases (row sigma 0.02 LogNormal(0, 0.3), E8M0 floor(log2 max)
+ * - 2, E2M1 to nearest, biases N(0, 0.01) rounded to bf16); R x C Q8_0 of N(0, 0.02); n f32
+ * moyenne + ecart N(0, 1). `matrice` / `flux_id` name the stream of draws. */
+int trc_synth_mxfp4_gpu(uint8_t* blocs, float* biais, uint32_t lignes, uint32_t colonnes, uint64_t graine,
+                        uint64_t matrice, void* flux);
+int trc_synth_q8_0_gpu(uint8_t* w, uint32_t lignes, uint32_t colonnes, uint64_t graine, uint64_t matrice, void* flux);
+int trc_synth_f32_gpu(float* y, uint64_t n, uint64_t graine, uint64_t flux_id, float moyenne, float ecart, void* flux);
+/* Raw parts of n experts from their blocks (descs: blocs, biais, sortie, expert), `taille`
+ * bytes each: `entete` (the header and stream table trc_coder_partie_brute writes, with any
+ * expert number) then the streams at its offsets, zeros elsewhere. */
+int trc_parties_brutes_gpu(const trc_desc_codage* descs, uint32_t n, const trc_dims_expert* dims, const uint8_t* entete,
+                           uint32_t entete_octets, uint64_t taille, void* flux);
+
 /* ---------------------------------------------------------------- new: the fused MoE layer */
 
 /* One MoE layer of one token, fused: routed experts' DELTA -> scales, CODES_CTX decoded in

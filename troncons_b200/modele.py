@@ -1,0 +1,287 @@
+"""The whole decode step of a gpt-oss-shaped model over the C-ABI (``trc_modele_pas``), on seeded
+synthetic weights drawn and encoded on the GPU: the reference's ``Modele`` (trc-modele/src/
+lib.rs:342-568) with this library's kernels, the fused MoE layer in place of decode + GEMVs."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import DescCodage, DimsExpert, ParamsRope, lib, verifier
+
+_u64, _u32, _vp, _sz, _i32 = C.c_uint64, C.c_uint32, C.c_void_p, C.c_size_t, C.c_int
+
+
+class ModeleCouche(C.Structure):
+    """trc_modele_couche: 152 bytes."""
+    _fields_ = [(n, C.c_uint64) for n in ("attn_norm", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "puits",
+                                            "post_norm", "wr", "br", "cache_k", "cache_v", "parties",
+                                            "parties_octets", "luts")] + [("anneau", C.c_uint32), ("reserve", C.c_uint32)]
+
+
+class ModeleConfig(C.Structure):
+    """trc_modele_config: 176 bytes."""
+    _fields_ = [(n, C.c_uint32) for n in ("couches", "d", "tetes", "tetes_kv", "dim_tete", "experts", "k", "vocab",
+                                            "contexte", "brut", "n_delta", "n_codes")] + [
+        ("eps", C.c_float), ("reserve", C.c_uint32), ("rope", ParamsRope), ("dims", DimsExpert),
+        ("couches_desc", C.c_uint64), ("enchassement", C.c_uint64), ("norme_sortie", C.c_uint64),
+        ("sortie", C.c_uint64), ("espace", C.c_uint64), ("espace_octets", C.c_uint64)]
+
+
+for _n, (_r, _a) in {
+    "trc_ligne_q8_0": (_i32, [_vp, _sz, _u32, _u32, _vp, _sz, _vp]),
+    "trc_argmax": (_i32, [_vp, _sz, _u32, _vp, _sz, _vp]),
+    "trc_modele_espace_octets": (_u64, [_vp]),
+    "trc_modele_sorties": (_i32, [_vp, _vp, _vp, _vp]),
+    "trc_modele_pas": (_i32, [_vp, _u32, _u32, _u32, _vp]),
+    "trc_synth_mxfp4_gpu": (_i32, [_vp, _vp, _u32, _u32, _u64, _u64, _vp]),
+    "trc_synth_q8_0_gpu": (_i32, [_vp, _u32, _u32, _u64, _u64, _vp]),
+    "trc_synth_f32_gpu": (_i32, [_vp, _u64, _u64, _u64, C.c_float, C.c_float, _vp]),
+    "trc_parties_brutes_gpu": (_i32, [_vp, _u32, _vp, _vp, _u32, _u64, _vp]),
+}.items():
+    getattr(lib, _n).restype = _r
+    getattr(lib, _n).argtypes = _a
+
+
+def _ident(*a) -> int:
+    """A deterministic 48-bit id of a tensor's name (the stream of its draws)."""
+    import hashlib
+
+    return int.from_bytes(hashlib.blake2b(repr(a).encode(), digest_size=6).digest(), "little")
+
+
+def _flux():
+    import torch
+
+    return torch.cuda.current_stream().cuda_stream
+
+
+def synth_q8_0(R: int, C_: int, graine: int, matrice: int):
+    import torch
+
+    w = torch.empty(R * (C_ // 32) * 34, dtype=torch.uint8, device="cuda")
+    verifier(lib.trc_synth_q8_0_gpu(w.data_ptr(), R, C_, graine, matrice, _flux()))
+    return w
+
+
+def synth_f32(n: int, graine: int, flux_id: int, moyenne: float, ecart: float):
+    import torch
+
+    y = torch.empty(n, dtype=torch.float32, device="cuda")
+    verifier(lib.trc_synth_f32_gpu(y.data_ptr(), n, graine, flux_id, moyenne, ecart, _flux()))
+    return y
+
+
+def entete_brute(dims: DimsExpert) -> tuple:
+    """The header and stream table of a raw part (trc_coder_partie_brute's layout) and the part's
+    size: ECHELLES_BRUTES (0x07), CODES_BRUTS (0x06), BIAIS (0x02) per matrix, each stream at an
+    offset aligned to 16, zeros up to a multiple of 4096."""
+    flux = []
+    for j in range(3):
+        R, B = dims.lignes[j], dims.colonnes[j] // 32
+        flux += [(0x07, j, R * B), (0x06, j, 16 * R * B), (0x02, j, 4 * R)]
+    p = 64 + 16 * len(flux)
+    dec = []
+    for _, _, n in flux:
+        p = (p + 15) // 16 * 16
+        dec.append(p)
+        p += n
+    utiles, total = p, (p + 4095) // 4096 * 4096
+    h = np.zeros(64 + 16 * len(flux), np.uint8)
+    h[0:4] = np.frombuffer(np.uint32(0x30435254).tobytes(), np.uint8)
+    h[9] = 3
+    h[10:12] = np.frombuffer(np.uint16(len(flux)).tobytes(), np.uint8)
+    h[12:16] = np.frombuffer(np.uint32(utiles).tobytes(), np.uint8)
+    for i, ((sorte, j, n), o) in enumerate(zip(flux, dec)):
+        e = 64 + 16 * i
+        h[e], h[e + 1], h[e + 2] = sorte, j, 0xFF
+        h[e + 4:e + 16] = np.frombuffer(np.array([o, n, n], np.uint32).tobytes(), np.uint8)
+    return h, total
+
+
+class Modele:
+    """A synthetic gpt-oss-shaped model (seeded; every tensor drawn on the GPU): `couches` layers of
+    attention (Q8_0, GQA tetes / tetes_kv, head 64, sinks, YaRN, sliding window `fenetre` on even
+    layers) and a MoE of `experts` MXFP4 experts of shape `dims`, top-`k`, their parts encoded as
+    .trc v1.2 on the GPU (`compresse`) and / or raw (`brut`); Q8_0 embedding and unembedding of
+    `vocab` rows. `pas` runs one token through trc_modele_pas on the chosen parts."""
+
+    def __init__(self, couches: int, d: int, tetes: int, tetes_kv: int, experts: int, k: int, vocab: int,
+                 contexte: int, ffn: int, fenetre: int = 128, graine: int = 1, compresse: bool = True,
+                 brut: bool = False, lot: int = 32, eps: float = 1e-5, rope: ParamsRope | None = None):
+        import torch
+
+        import troncons_b200.synth as S
+
+        self.couches, self.d, self.tetes, self.tetes_kv, self.dt = couches, d, tetes, tetes_kv, 64
+        self.experts, self.k, self.vocab, self.contexte, self.fenetre = experts, k, vocab, contexte, fenetre
+        self.graine, self.eps = graine, eps
+        self.rope = rope or ParamsRope.gpt_oss()
+        self.dims = DimsExpert.de([ffn, ffn, d], [d, d, ffn])
+        dq, dkv = tetes * 64, tetes_kv * 64
+        g = graine
+        ident = _ident
+        self._garde = []
+        self.tenseurs = []
+        for l in range(couches):
+            t = {
+                "attn_norm": synth_f32(d, g, ident("an", l), 1.0, 0.02),
+                "wq": synth_q8_0(dq, d, g, ident("wq", l)), "bq": synth_f32(dq, g, ident("bq", l), 0.0, 0.01),
+                "wk": synth_q8_0(dkv, d, g, ident("wk", l)), "bk": synth_f32(dkv, g, ident("bk", l), 0.0, 0.01),
+                "wv": synth_q8_0(dkv, d, g, ident("wv", l)), "bv": synth_f32(dkv, g, ident("bv", l), 0.0, 0.01),
+                "wo": synth_q8_0(d, dq, g, ident("wo", l)), "bo": synth_f32(d, g, ident("bo", l), 0.0, 0.01),
+                "puits": synth_f32(tetes, g, ident("pu", l), 0.0, 1.0),
+                "post_norm": synth_f32(d, g, ident("pn", l), 1.0, 0.02),
+                "wr": synth_f32(experts * d, g, ident("wr", l), 0.0, 0.02),
+                "br": synth_f32(experts, g, ident("br", l), 0.0, 0.01),
+            }
+            cases = fenetre if (l % 2 == 0 and fenetre) else contexte
+            t["anneau"] = fenetre if (l % 2 == 0 and fenetre) else 0
+            t["cache_k"] = torch.zeros(cases * dkv, dtype=torch.int16, device="cuda")
+            t["cache_v"] = torch.zeros(cases * dkv, dtype=torch.int16, device="cuda")
+            self.tenseurs.append(t)
+        self.enchassement = synth_q8_0(vocab, d, g, ident("emb"))
+        self.sortie_w = synth_q8_0(vocab, d, g, ident("out"))
+        self.norme_sortie = synth_f32(d, g, ident("on"), 1.0, 0.02)
+        # experts: draw every expert of a layer on the GPU, count, tables, encode in batches
+        self.parties = {"compresse": [], "brut": []}
+        taille_src = sum(self.dims.lignes[j] * (self.dims.colonnes[j] // 32) * 17 for j in range(3))
+        blocs = [[torch.empty(self.dims.lignes[j] * (self.dims.colonnes[j] // 32) * 17, dtype=torch.uint8,
+                              device="cuda") for j in range(3)] for _ in range(experts)]
+        biais = [[torch.empty(self.dims.lignes[j], dtype=torch.float32, device="cuda") for j in range(3)]
+                 for _ in range(experts)]
+        self.luts = []
+        entete, taille_brute = entete_brute(self.dims)
+        entete_dev = torch.from_numpy(entete).cuda()
+        for l in range(couches):
+            for e in range(experts):
+                for j in range(3):
+                    verifier(lib.trc_synth_mxfp4_gpu(blocs[e][j].data_ptr(), biais[e][j].data_ptr(),
+                                                     self.dims.lignes[j], self.dims.colonnes[j], g,
+                                                     ident("ex", l, e, j), _flux()))
+            if compresse:
+                cpt = S.comptes_gpu(blocs, self.dims)
+                freqs = S.tables_de_comptes(cpt.cpu().numpy().astype(np.uint64).reshape(3, 4, 256))
+                self.luts.append(torch.from_numpy(S.luts(freqs).view(np.int32)).cuda())
+                self.parties["compresse"].append(self._encoder(blocs, biais, freqs, l, lot, taille_src))
+            else:
+                self.luts.append(torch.zeros(3 * 4 * 4096, dtype=torch.int32, device="cuda"))
+            if brut:
+                self.parties["brut"].append(self._bruts(blocs, biais, entete_dev, taille_brute))
+        del blocs, biais
+        torch.cuda.synchronize()
+        self.actifs = "compresse" if compresse else "brut"
+        self._monter()
+
+    def _encoder(self, blocs, biais, freqs, couche: int, lot: int, taille_src: int):
+        """The layer's experts encoded on the GPU in batches of `lot`, then packed back to back
+        (each part 4096-aligned) in one buffer: (buffer, addresses u64[E], sizes u64[E])."""
+        import torch
+
+        import troncons_b200.synth as S
+
+        f = torch.from_numpy(np.ascontiguousarray(freqs, np.uint16).reshape(-1).view(np.int16)).cuda()
+        cap = (taille_src * 11 // 10 + (1 << 16) + 4095) // 4096 * 4096
+        morceaux, tailles = [], []
+        for e0 in range(0, self.experts, lot):
+            n = min(lot, self.experts - e0)
+            sorties = torch.empty(n * cap, dtype=torch.uint8, device="cuda")
+            descs = S._descs_gpu(blocs[e0:e0 + n], biais[e0:e0 + n], list(range(e0, e0 + n)),
+                                 [sorties[i * cap:(i + 1) * cap] for i in range(n)], cap)
+            octets = torch.zeros(2 * n, dtype=torch.int64, device="cuda")
+            n_esp = int(lib.trc_coder_parties_gpu_espace(C.byref(self.dims), n, 256, 256))
+            esp = torch.empty(n_esp + 256, dtype=torch.uint8, device="cuda")
+            verifier(lib.trc_coder_parties_gpu(descs.data_ptr(), descs.numel(), n, C.byref(self.dims), f.data_ptr(), 1,
+                                               couche, 256, 256, octets.data_ptr(), octets.numel() * 8,
+                                               esp.data_ptr() + (-esp.data_ptr()) % 256, n_esp, _flux()))
+            o = octets.cpu().numpy()
+            for i in range(n):
+                if o[2 * i] == 0 or o[2 * i] > cap:
+                    raise RuntimeError(f"layer {couche}, expert {e0 + i}: part not encoded ({o[2 * i]} bytes)")
+                morceaux.append(sorties[i * cap:i * cap + int(o[2 * i])])
+                tailles.append(int(o[2 * i]))
+            self._garde.append((sorties, descs, esp))
+        tampon = torch.empty(sum(tailles), dtype=torch.uint8, device="cuda")
+        p, adr = 0, []
+        for m, t in zip(morceaux, tailles):
+            tampon[p:p + t].copy_(m)
+            adr.append(tampon.data_ptr() + p)
+            p += t
+        self._garde = []
+        return tampon, np.array(adr, np.uint64), np.array(tailles, np.uint64)
+
+    def _bruts(self, blocs, biais, entete_dev, taille: int):
+        import torch
+
+        import troncons_b200.synth as S
+
+        tampon = torch.empty(self.experts * taille, dtype=torch.uint8, device="cuda")
+        descs = S._descs_gpu(blocs, biais, list(range(self.experts)),
+                             [tampon[e * taille:(e + 1) * taille] for e in range(self.experts)], taille)
+        verifier(lib.trc_parties_brutes_gpu(descs.data_ptr(), self.experts, C.byref(self.dims), entete_dev.data_ptr(),
+                                            entete_dev.numel(), taille, _flux()))
+        torch.cuda.synchronize()
+        adr = np.array([tampon.data_ptr() + e * taille for e in range(self.experts)], np.uint64)
+        return tampon, adr, np.full(self.experts, taille, np.uint64)
+
+    def _monter(self):
+        """The descriptor of the parts chosen by self.actifs, and the workspace."""
+        import torch
+
+        self._tables = []
+        self.desc_couches = (ModeleCouche * self.couches)()
+        for l, t in enumerate(self.tenseurs):
+            _, adr, tailles = self.parties[self.actifs][l]
+            ta = torch.from_numpy(adr.view(np.int64)).cuda()
+            tt = torch.from_numpy(tailles.view(np.int64)).cuda()
+            self._tables.append((ta, tt))
+            c = self.desc_couches[l]
+            for n in ("attn_norm", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "puits", "post_norm", "wr", "br",
+                      "cache_k", "cache_v"):
+                setattr(c, n, t[n].data_ptr())
+            c.parties, c.parties_octets, c.luts = ta.data_ptr(), tt.data_ptr(), self.luts[l].data_ptr()
+            c.anneau = t["anneau"]
+        m = ModeleConfig()
+        m.couches, m.d, m.tetes, m.tetes_kv, m.dim_tete = self.couches, self.d, self.tetes, self.tetes_kv, 64
+        m.experts, m.k, m.vocab, m.contexte = self.experts, self.k, self.vocab, self.contexte
+        m.brut = int(self.actifs == "brut")
+        m.eps = self.eps
+        m.rope = self.rope
+        m.dims = self.dims
+        m.couches_desc = C.addressof(self.desc_couches)
+        m.enchassement, m.norme_sortie, m.sortie = (self.enchassement.data_ptr(), self.norme_sortie.data_ptr(),
+                                                    self.sortie_w.data_ptr())
+        n = int(lib.trc_modele_espace_octets(C.byref(m)))
+        self.espace = torch.zeros(n + 256, dtype=torch.uint8, device="cuda")
+        m.espace = self.espace.data_ptr() + (-self.espace.data_ptr()) % 256
+        m.espace_octets = n
+        self.config = m
+        lg, jt, ct = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        verifier(lib.trc_modele_sorties(C.byref(m), C.byref(lg), C.byref(jt), C.byref(ct)))
+        self._sorties = (lg.value, jt.value, ct.value)
+
+    def choisir(self, actifs: str) -> None:
+        """Run on the compressed ("compresse") or raw ("brut") parts; the KV caches are cleared."""
+        if not self.parties[actifs]:
+            raise ValueError(f"no {actifs} parts in this model")
+        self.actifs = actifs
+        for t in self.tenseurs:
+            t["cache_k"].zero_()
+            t["cache_v"].zero_()
+        self._monter()
+
+    def pas(self, jeton: int, position: int, sortie: bool = True, flux=None) -> None:
+        verifier(lib.trc_modele_pas(C.byref(self.config), jeton, position, int(sortie),
+                                    (flux.cuda_stream if flux is not None else _flux())))
+
+    def vues(self):
+        """(logits f32[vocab], token u32[1], controle u32[4k]) as torch tensors on the workspace."""
+        import torch
+
+        o0 = self._sorties[0] - self.espace.data_ptr()
+        o1 = self._sorties[1] - self.espace.data_ptr()
+        o2 = self._sorties[2] - self.espace.data_ptr()
+        lg = self.espace[o0:o0 + 4 * self.vocab].view(torch.float32)
+        jt = self.espace[o1:o1 + 4].view(torch.int32)
+        ct = self.espace[o2:o2 + 16 * self.k].view(torch.int32)
+        return lg, jt, ct
