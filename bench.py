@@ -58,6 +58,13 @@ def arguments():
     a.add_argument("--prefill", type=int, default=0,
                    help="measure a batch of this many positions (1..128) through the fused layer and "
                         "through the layer par flux (each routed expert decoded once for the batch)")
+    a.add_argument("--modele", action="store_true",
+                   help="the whole gpt-oss-120b decode step (config 2): tokens/s after a context of --contexte "
+                        "tokens; with --exactitude N, N greedy steps from .trc v1.2 then from raw parts (config 4)")
+    a.add_argument("--contexte", type=int, default=2048)
+    a.add_argument("--sans-modele", action="store_true", help="skip the whole-model tokens/s in the default line")
+    a.add_argument("--exactitude", type=int, default=0)
+    a.add_argument("--couches", type=int, default=36)
     a.add_argument("--codeur", action="store_true",
                    help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
@@ -354,6 +361,16 @@ def notre_bras(args):
     }
     if r == 0 and w == 1 and not args.no_cpu_baseline:
         ligne["cpu_baseline"] = base_cpu(c, args, bornes_s=12.0)
+    if w == 1 and not args.sans_modele:
+        # The headline metric's second half: the whole gpt-oss-120b decode step (config 2).
+        del cc, c
+        torch.cuda.empty_cache()
+        try:
+            mod = mesurer_modele(args, 16, 3, 0)
+            ligne["modele"] = {k: mod[k] for k in ("metric", "value", "unit", "ms_per_step", "config", "roofline",
+                                                    "generation_s", "context_s")}
+        except Exception as ex:  # reported, not hidden: the layer's line stands on its own
+            ligne["modele"] = {"unavailable": f"{type(ex).__name__}: {ex}"[:300]}
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -781,8 +798,112 @@ def bras_prefill(args):
     del graphes
 
 
+def bras_modele(args):
+    """Prints mesurer_modele's line (see there)."""
+    print(json.dumps(mesurer_modele(args, args.steps, args.warmup, args.exactitude)), flush=True)
+
+
+def mesurer_modele(args, steps: int, warmup: int, exactitude: int) -> dict:
+    """Config 2 (and 4): a seeded synthetic gpt-oss-120b (36 layers, d 2880, 64 / 8 heads of 64,
+    sinks, YaRN, even layers sliding over 128, 128 experts top-4 of 2880 x 2880 MXFP4 as .trc v1.2
+    parts, Q8_0 attention, embedding and unembedding of 201,088 rows) drawn and encoded on the GPU,
+    all resident in HBM. The context: --contexte seeded token ids through the step (no
+    unembedding), then --steps greedy steps timed with CUDA events after --warmup. With
+    --exactitude N: N greedy steps from the context on the .trc parts, then on the raw parts of
+    the same weights; every step's logits compared bit for bit (the exactness invariant)."""
+    import hashlib
+
+    import numpy as np
+    import torch
+
+    import troncons_b200.modele as M
+
+    t0 = time.time()
+    m = M.Modele(couches=args.couches, d=2880, tetes=64, tetes_kv=8, experts=args.experts, k=args.k, vocab=201088,
+                 contexte=args.contexte + warmup + max(steps, exactitude) + 1, ffn=2880, fenetre=128,
+                 graine=args.graine, compresse=True, brut=exactitude > 0)
+    torch.cuda.synchronize()
+    t_gen = time.time() - t0
+    rng = np.random.default_rng(args.graine)
+    contexte = rng.integers(0, 201088, args.contexte)
+    lg, jt, ct = m.vues()
+
+    def prefixe():
+        for p, j in enumerate(contexte):
+            m.pas(int(j), p, sortie=False)
+        torch.cuda.synchronize()
+
+    t1 = time.time()
+    prefixe()
+    t_ctx = time.time() - t1
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    pos = args.contexte
+    j = int(contexte[-1])
+    for _ in range(warmup):
+        m.pas(j, pos)
+        pos += 1
+    torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(steps):
+        m.pas(j, pos)
+        pos += 1
+    ev[1].record()
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / steps
+    assert (ct.cpu().numpy() == 0).all(), "integrity counters set"
+    # algorithmic bytes of a token at the timed positions: 4 routed experts' parts per layer (the
+    # mean part), the attention's Q8_0 and f32 tensors, the router, the KV cache read, the
+    # unembedding
+    parts = [float(np.mean(m.parties["compresse"][l][2])) for l in range(m.couches)]
+    dq, dkv = 64 * 64, 8 * 64
+    att = (dq + 2 * dkv) * 2880 // 32 * 34 + 2880 * dq // 32 * 34 + 4 * (dq + 2 * dkv + 2880 + 64 + 2 * 2880)
+    routeur = 4 * 128 * 2880 + 4 * 128
+    kv = sum(2 * 2 * dkv * (min(128, pos) if l % 2 == 0 else pos) for l in range(m.couches))
+    octets = m.k * sum(parts) + m.couches * (att + routeur) + kv + 201088 * 2880 // 32 * 34 + 4 * 2880
+    pic, sorte_pic = pics()
+    ligne = {
+        "metric": "gpt-oss-120b decode tokens/s (whole step, batch 1, synthetic weights)",
+        "value": round(1000.0 / ms, 2), "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "u8",
+        "data": "synthetic seeded gpt-oss-120b-shaped weights drawn and encoded on the GPU (.trc v1.2 parts)",
+        "config": {"workload": f"config 2: {m.couches} layers, 128 experts top-4, vocab 201,088, context "
+                               f"{args.contexte} seeded tokens, greedy", "positions": [args.contexte, pos]},
+        "roofline": {"bound": "hbm", "algorithmic_bytes_per_token": int(octets),
+                     "achieved": round(octets / (ms * 1e-3) / 1e9, 2), "peak": pic, "unit": "GB/s",
+                     "frac": round(octets / (ms * 1e-3) / 1e9 / pic, 4), "peak_source": sorte_pic},
+        "generation_s": round(t_gen, 1), "context_s": round(t_ctx, 1),
+    }
+    if exactitude:
+        empreintes, jetons = {}, {}
+        for actifs in ("compresse", "brut"):
+            m.choisir(actifs)
+            lg, jt, ct = m.vues()
+            ct.zero_()
+            prefixe()
+            h = hashlib.sha256()
+            j, js = int(contexte[-1]), []
+            for s in range(exactitude):
+                m.pas(j, args.contexte + s)
+                z = lg.cpu().numpy()
+                h.update(z.tobytes())
+                j = int(jt.cpu().numpy()[0])
+                js.append(j)
+            assert (ct.cpu().numpy() == 0).all()
+            empreintes[actifs], jetons[actifs] = h.hexdigest(), js
+        ligne["exactitude"] = {"steps": exactitude, "logits_sha256_compresse": empreintes["compresse"],
+                               "logits_sha256_brut": empreintes["brut"],
+                               "bit_identical": empreintes["compresse"] == empreintes["brut"],
+                               "tokens_identical": jetons["compresse"] == jetons["brut"]}
+    del m
+    torch.cuda.empty_cache()
+    return ligne
+
+
 def main():
     args = arguments()
+    if args.modele:
+        bras_modele(args)
+        return
     if args.prefill:
         bras_prefill(args)
         return
