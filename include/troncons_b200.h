@@ -569,6 +569,38 @@ int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16
                 uint32_t colonnes, uint32_t k, uint32_t jetons, float* logits, uint32_t* indices, float* poids,
                 void* flux);
 
+/* ---------------------------------------------------------------- the quality judge (trc-juge) */
+
+/* u16 words of one `.kld` logit entry of n_vocab logits: 2 ceil(n_vocab / 2) + 4
+ * (`kld::mots_par_entree`, trc-juge/src/kld.rs:27-29). */
+uint64_t trc_juge_mots_par_entree(uint32_t n_vocab);
+
+/* Codes n_positions rows of logits (f32, or f64 when f64 = 1; row-major [n_positions][n_vocab])
+ * into consecutive `.kld` entries (sortie: n_positions x trc_juge_mots_par_entree words, the
+ * file's layout), the rule of `kld::coder_entree` (kld.rs:148-186) with every intermediate in
+ * f64. One launch. */
+int trc_juge_coder(const void* logits, uint32_t f64, size_t logits_octets, uint32_t n_positions, uint32_t n_vocab,
+                   uint16_t* sortie, size_t sortie_octets, void* flux);
+
+/* One judged position (`stats::Position`, trc-juge/src/stats.rs:24-33): 48 bytes. */
+typedef struct {
+    double kl;               /* KL(P || Q) over log p_i > -16 */
+    double nll_q, nll_p;     /* NLL of the next token under Q and under P */
+    double dp;               /* q(next) - p(next) */
+    uint32_t premier_p, premier_q;  /* argmax, ties to the first index */
+    uint32_t meme_premier;   /* premier_p == premier_q */
+    uint32_t suivant_valide; /* 0: the next token was >= n_vocab (NLLs and dp are NaN) */
+} trc_juge_position;
+
+/* KL, first choice and NLLs of n_positions positions: P = coded entries (n_positions x nv words);
+ * Q per `mode`: 0 = coded entries, taken as log-probabilities without renormalisation
+ * (`stats::position_decodee`, stats.rs:33-39); 1 = raw f32 logits [n_positions][n_vocab]; 2 = raw
+ * f64 logits (both renormalised by their log-sum-exp: `stats::position`, stats.rs:36-85).
+ * suivants u32[n_positions] = the next token of each position. One launch. */
+int trc_juge_positions(const uint16_t* p, size_t p_octets, const void* q, size_t q_octets, uint32_t mode,
+                       const uint32_t* suivants, size_t suivants_octets, uint32_t n_positions, uint32_t n_vocab,
+                       trc_juge_position* sortie, size_t sortie_octets, void* flux);
+
 #ifdef __cplusplus
 }
 #endif

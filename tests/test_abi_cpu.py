@@ -16,6 +16,7 @@ import subprocess
 import pytest
 
 import troncons_b200 as T
+import troncons_b200.juge as J
 
 RACINE = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ENTETE = os.path.join(RACINE, "include", "troncons_b200.h")
@@ -46,6 +47,7 @@ _STRUCTS = {
     "trc_moe_couche": (T.MoeCouche, None),
     "trc_params_rope": (T.ParamsRope, 48),
     "trc_params_attention": (T.ParamsAttention, 32),
+    "trc_juge_position": (J.JugePosition, 48),
 }
 
 

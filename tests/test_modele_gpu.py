@@ -102,7 +102,7 @@ def test_contre_le_port_cpu(petit):
     caches = [[np.zeros(t["cache_k"].size, np.uint16), np.zeros(t["cache_v"].size, np.uint16)] for t in h]
     lg, jt, _ = m.vues()
     j = 1
-    for pos in range(12):
+    for pos in range(20):  # past the sliding layers' ring of 16 cases
         m.pas(j, pos)
         torch.cuda.synchronize()
         z_gpu = lg.cpu().numpy().copy()
@@ -135,121 +135,22 @@ def test_contre_le_port_cpu(petit):
 
 # ---------------------------------------------------------------- against an fp64 evaluation
 
-E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
-
-
-def _q8_0_f64(w, R, C_):
-    b = np.asarray(w, np.uint8).reshape(R, C_ // 32, 34)
-    d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
-    return (d * b[:, :, 2:].view(np.int8).astype(np.float64)).reshape(R, C_)
-
-
-def _experts_f64(part, luts, dims):
-    """The three matrices and biases of an expert, in f64, from its decoded slot (oracle)."""
-    import oracle as O
-    import troncons_b200 as T
-
-    slot, ctl = O.decoder_expert(part, luts, list(dims.lignes), list(dims.colonnes), T.taille_emplacement(dims))
-    assert (ctl == 0).all()
-    out, base = [], 0
-    for j in range(3):
-        R, C_ = dims.lignes[j], dims.colonnes[j]
-        e_off, b_off, pas = O.disposition(R, C_)
-        nb = R * (C_ // 32)
-        m = slot[base:base + pas]
-        codes = m[:16 * nb].reshape(nb, 16)
-        ech = m[e_off:e_off + nb].astype(np.int64)
-        biais = m[b_off:b_off + 4 * R].view(np.float32).astype(np.float64)
-        lo, hi = codes & 15, codes >> 4
-        nib = np.concatenate([lo, hi], axis=1).astype(np.int64)  # element i: low nibble of byte i, 16 + i: high
-        val = E2M1[nib & 7] * np.where(nib & 8, -1.0, 1.0) * np.ldexp(1.0, (ech - 127))[:, None]
-        out.append((val.reshape(R, C_), biais))
-        base += pas
-    return out
-
-
-def _rope_f64(v, tetes, position, p):
-    d, demi = p.dim_tete, p.dim_tete // 2
-    i = np.arange(demi, dtype=np.float64)
-    freq = p.base ** (2 * i / d)
-    if p.facteur > 1.0:
-        conc = 0.1 * np.log(p.facteur) + 1.0
-        bas = demi * np.log(p.ctx_origine / (p.beta_rapide * 2 * np.pi)) / np.log(p.base)
-        haut = demi * np.log(p.ctx_origine / (p.beta_lent * 2 * np.pi)) / np.log(p.base)
-        rampe = np.clip((i - bas) / (haut - bas), 0.0, 1.0)
-        inv = (1.0 / (p.facteur * freq)) * rampe + (1.0 / freq) * (1.0 - rampe)
-    else:
-        conc, inv = 1.0, 1.0 / freq
-    c, s = np.cos(position * inv) * conc, np.sin(position * inv) * conc
-    v = v.reshape(tetes, d)
-    a, b = v[:, :demi].copy(), v[:, demi:].copy()
-    return np.concatenate([a * c - b * s, b * c + a * s], axis=1).reshape(-1)
-
-
 def test_contre_une_evaluation_f64(petit):
-    """The model's logits against the same model evaluated in f64 on the host (storage formats
-    kept: Q8_0, MXFP4, the f16 KV cache): max|dz| <= 1e-4 max|z| and the same greedy token."""
+    """The model's logits against the same model evaluated in f64 on the host (oracle/modele_f64:
+    the storage formats kept: Q8_0, MXFP4, the f16 KV cache): max|dz| <= 1e-4 max|z| and the same
+    greedy token at every step."""
+    from oracle.modele_f64 import ModeleF64
+
     m = petit
     m.choisir("compresse")
-    L, d, dq, dkv, H, Hk = m.couches, m.d, m.tetes * 64, m.tetes_kv * 64, m.tetes, m.tetes_kv
-    h = [{n: (v.cpu().numpy() if torch.is_tensor(v) else v) for n, v in t.items()} for t in m.tenseurs]
-    W = []
-    for l in range(L):
-        t = h[l]
-        tampon, adr, tailles = m.parties["compresse"][l]
-        base, brut = tampon.data_ptr(), tampon.cpu().numpy()
-        lut = m.luts[l].cpu().numpy().view(np.uint32)
-        ex = [_experts_f64(brut[int(a) - base:int(a) - base + int(s)].tobytes(), lut, m.dims)
-              for a, s in zip(adr, tailles)]
-        W.append({"q": _q8_0_f64(t["wq"], dq, d), "k": _q8_0_f64(t["wk"], dkv, d), "v": _q8_0_f64(t["wv"], dkv, d),
-                  "o": _q8_0_f64(t["wo"], d, dq), "r": t["wr"].astype(np.float64).reshape(m.experts, d), "ex": ex})
-    emb = _q8_0_f64(m.enchassement.cpu().numpy(), m.vocab, d)
-    wout = _q8_0_f64(m.sortie_w.cpu().numpy(), m.vocab, d)
-    cache = [[np.zeros((t["cache_k"].size // dkv, dkv)), np.zeros((t["cache_v"].size // dkv, dkv))] for t in h]
-    f64 = lambda a: np.asarray(a, np.float64)  # noqa: E731
-    rms = lambda x, w: x * f64(w) / np.sqrt(np.mean(x * x) + np.float64(np.float32(m.eps)))  # noqa: E731
+    ref = ModeleF64(m, kv16=True)
     lg, jt, _ = m.vues()
     j = 3
-    for pos in range(10):
+    for pos in range(24):  # past the sliding layers' ring of 16 cases
         m.pas(j, pos)
         torch.cuda.synchronize()
         z_gpu = lg.cpu().numpy().astype(np.float64)
-        x = emb[j].copy()
-        for l in range(L):
-            t, w = h[l], W[l]
-            hh = rms(x, t["attn_norm"])
-            q = w["q"] @ hh + f64(t["bq"])
-            k = w["k"] @ hh + f64(t["bk"])
-            v = w["v"] @ hh + f64(t["bv"])
-            q, k = _rope_f64(q, H, pos, m.rope), _rope_f64(k, Hk, pos, m.rope)
-            an = t["anneau"]
-            case = pos % an if an else pos
-            cache[l][0][case] = k.astype(np.float16).astype(np.float64)
-            cache[l][1][case] = v.astype(np.float16).astype(np.float64)
-            debut = max(0, pos + 1 - an) if an else 0
-            cases = [(p % an if an else p) for p in range(debut, pos + 1)]
-            a = np.zeros(dq)
-            for hq in range(H):
-                hk = hq // (H // Hk)
-                K = cache[l][0][cases, hk * 64:(hk + 1) * 64]
-                V = cache[l][1][cases, hk * 64:(hk + 1) * 64]
-                sc = K @ q[hq * 64:(hq + 1) * 64] * 0.125
-                mx = max(sc.max(), t["puits"][hq])
-                e = np.exp(sc - mx)
-                a[hq * 64:(hq + 1) * 64] = (e @ V) / (e.sum() + np.exp(t["puits"][hq] - mx))
-            x = x + w["o"] @ a + f64(t["bo"])
-            h2 = rms(x, t["post_norm"])
-            lr = w["r"] @ h2 + f64(t["br"])
-            top = sorted(range(m.experts), key=lambda e_: (-lr[e_], e_))[:m.k]
-            p = np.exp(lr[top] - lr[top].max())
-            p /= p.sum()
-            for wi, e_ in zip(p, top):
-                (Wg, bg), (Wu, bu), (Wd, bd) = w["ex"][e_]
-                g = np.minimum(Wg @ h2 + bg, 7.0)
-                u = np.clip(Wu @ h2 + bu, -7.0, 7.0)
-                act = g / (1.0 + np.exp(-1.702 * g)) * (u + 1.0)
-                x = x + wi * (Wd @ act + bd)
-        z = wout @ rms(x, m.norme_sortie.cpu().numpy())
+        z = ref.pas(j, pos)
         assert np.abs(z_gpu - z).max() <= 1e-4 * np.abs(z).max(), f"step {pos}: {np.abs(z_gpu - z).max()}"
         assert int(np.argmax(z)) == int(jt.cpu().numpy()[0]), f"step {pos}"
         j = int(jt.cpu().numpy()[0])
