@@ -489,6 +489,12 @@ def bras_ep(args):
     t_total_ms, t_e2e_ms, octets_tous = float(tt[0]), float(tt[1]), float(oc[0])
     clocks = horl.resume()
     dist.barrier()
+    modele = None
+    echange = ep.echange
+    if not args.sans_modele:
+        del ep, c, xs_dev, res_dev, vidange
+        torch.cuda.empty_cache()
+        modele = mesurer_modele_ep(args, 16, 3)
     dist.destroy_process_group()
     if r != 0:
         return
@@ -512,7 +518,7 @@ def bras_ep(args):
                         "memory" if paires else "combine by NCCL all-reduce of the batch's f32 residual"),
             "experts": args.experts, "k": args.k, "tokens_per_step": jetons, "n_delta": args.n_delta,
             "n_codes": args.n_codes, "l2": "flushed between steps (256 MB written)",
-            "bytes_per_step": round(octets_tous / args.steps), "parallelism": f"ep{w}", "exchange": ep.echange,
+            "bytes_per_step": round(octets_tous / args.steps), "parallelism": f"ep{w}", "exchange": echange,
         },
         "e2e": {"value": round(octets_tous / (t_e2e_ms * 1e-3) / 1e9, 2), "unit": UNITE,
                 "h2d_bytes_per_step": jetons * (2 * C0 + 4 * R2), "d2h_bytes_per_step": jetons * 4 * R2},
@@ -521,7 +527,77 @@ def bras_ep(args):
         "clocks": clocks,
         "generation_s": round(t_gen, 1),
     }
+    if modele is not None:
+        ligne["modele"] = modele
     print(json.dumps(ligne), flush=True)
+
+
+def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
+    """Config 3, the whole model expert-parallel (every rank of the torchrun group calls it): a
+    seeded synthetic gpt-oss-120b, each rank holding its share of every layer's experts
+    (partage: 16 of 128 at 8 GPUs, drawn and encoded on its GPU, the tables from the counts summed
+    over NCCL) and a replica of the dense weights; one sequence per rank (a batch of N): its own
+    --contexte seeded tokens through the step, then `steps` greedy steps timed with CUDA events
+    after `warmup`, every rank in step (two NCCL collectives per layer: the MoE inputs gathered,
+    the shares' sums scattered back). tokens/s = N x steps / the max over ranks of the timed
+    region."""
+    import datetime  # noqa: F401
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from troncons_b200.parallele import ModeleEP
+
+    r, w, _ = rang()
+    t0 = time.time()
+    ep = ModeleEP(r, w, echange="nccl", couches=args.couches, d=2880, tetes=64, tetes_kv=8, experts=args.experts, k=args.k,
+                  vocab=201088, contexte=args.contexte + warmup + steps + 1, ffn=2880, fenetre=128, graine=args.graine,
+                  compresse=True, brut=False)
+    torch.cuda.synchronize()
+    t_gen = time.time() - t0
+    contexte = np.random.default_rng(args.graine + 1000 * r).integers(0, 201088, args.contexte)
+    lg, jt, ct = ep.m.vues()
+    ct.zero_()
+    ep.controle.zero_()
+    dist.barrier()
+    t1 = time.time()
+    for p, j in enumerate(contexte):
+        ep.pas(int(j), p, sortie=False)
+    torch.cuda.synchronize()
+    t_ctx = time.time() - t1
+    pos, j = args.contexte, int(contexte[-1])
+    for _ in range(warmup):
+        ep.pas(j, pos)
+        j = int(jt.cpu().numpy()[0])
+        pos += 1
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev[0].record()
+    for _ in range(steps):
+        ep.pas(j, pos)  # the greedy token stays on the device: the same token is fed (no host sync)
+        pos += 1
+    ev[1].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ev[0].elapsed_time(ev[1])], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0]) / steps
+    ok = torch.tensor([int((ep.controle.cpu().numpy() == 0).all())], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok[0]):
+        raise RuntimeError("integrity counters set during the expert-parallel model steps")
+    debut, fin = ep.tenus
+    del ep
+    torch.cuda.empty_cache()
+    return {"metric": f"gpt-oss-120b decode tokens/s (whole step, expert-parallel over {w} GPUs, batch {w})",
+            "value": round(w * 1000.0 / ms, 2), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": steps,
+            "warmup": warmup, "batch": w, "experts_per_gpu": fin - debut,
+            "workload": f"config 3: {args.couches} layers, {args.experts} experts top-{args.k} ({fin - debut} per GPU), "
+                        f"one sequence per GPU, context {args.contexte} seeded tokens, attention on each sequence's "
+                        "GPU, MoE inputs all-gathered and the shares' sums reduce-scattered over NCCL per layer",
+            "exchange": "nccl",
+            "generation_s": round(t_gen, 1), "context_s": round(t_ctx, 1)}
 
 
 def base_cpu(c, args, bornes_s: float, pas_min: int = 3):

@@ -442,6 +442,22 @@ int trc_modele_sorties(const trc_modele_config* m, uint64_t* logits, uint64_t* j
  * unembedding (a context token). */
 int trc_modele_pas(const trc_modele_config* m, uint32_t jeton, uint32_t position, uint32_t sortie, void* flux);
 
+/* The step in phases, for a caller that puts an exchange between them (the expert-parallel
+ * model: the MoE input of every rank's token gathered, the layer run on each rank's expert
+ * share, the sums scattered back). trc_modele_pas = debut, then per layer attention + moe, then
+ * fin, launch for launch.
+ *   debut:     x <- row `jeton` of the embedding (Modele::enchasser, lib.rs:476-480);
+ *   attention: layer `couche`'s attention side at `position`, x += o, then h2 <- RMSNorm(x), the
+ *              MoE's input (Modele::debut_couche, lib.rs:482-531);
+ *   moe:       router, top-k, the fused layer on h2, x += the weighted experts (fin_couche);
+ *   fin:       RMSNorm, unembedding, greedy token (Modele::sortie, lib.rs:555-568).
+ * trc_modele_etat gives the device addresses of x and h2 (f32[d] each) in the workspace. */
+int trc_modele_debut(const trc_modele_config* m, uint32_t jeton, void* flux);
+int trc_modele_attention(const trc_modele_config* m, uint32_t couche, uint32_t position, void* flux);
+int trc_modele_moe(const trc_modele_config* m, uint32_t couche, void* flux);
+int trc_modele_fin(const trc_modele_config* m, void* flux);
+int trc_modele_etat(const trc_modele_config* m, uint64_t* x, uint64_t* h2);
+
 /* Seeded synthetic tensors on the GPU (inputs of tests and benches; no counterpart): R x C
  * MXFP4 as 17-byte blocks + f32 biases (row sigma 0.02 LogNormal(0, 0.3), E8M0 floor(log2 max)
  * - 2, E2M1 to nearest, biases N(0, 0.01) rounded to bf16); R x C Q8_0 of N(0, 0.02); n f32

@@ -1,0 +1,110 @@
+"""GPU: the expert-parallel whole model (troncons_b200.parallele.ModeleEP), on a small synthetic
+gpt-oss-shaped model (2 layers, 8 experts top-4).
+
+- one rank: the phased step (trc_modele_debut / attention / moe-on-a-share / fin, the router and
+  the fused layer called for the batch, the share's sum added on the host side's stream) gives
+  trc_modele_pas's logits bit for bit, 24 greedy steps (past the sliding layers' ring), from the
+  .trc parts and from the raw parts;
+- two ranks (one process per GPU, NCCL for the MoE inputs' all-gather; the combine's exchange by
+  NVLink peer stores in the combine kernel, or by an NCCL reduce-scatter): each rank holds half
+  of every layer's experts and runs its own sequence; its logits agree with the one-GPU model run on that sequence within 1e-5 of
+  max|z| (the same experts' terms summed in another order across the GPUs) with the same greedy
+  token; the shares' parts are byte for byte the whole model's (tables from the counts summed
+  over NCCL). Skipped with fewer than two GPUs."""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+FORME = dict(couches=2, d=256, tetes=8, tetes_kv=2, experts=8, k=4, vocab=512, contexte=64, ffn=256, fenetre=16,
+             graine=13, compresse=True, brut=True)
+
+
+def _suite(m_pas, vues, jetons):
+    lg, jt, ct = vues()
+    ct.zero_()
+    out = []
+    for t, j in enumerate(jetons):
+        m_pas(int(j), t)
+        torch.cuda.synchronize()
+        out.append((lg.cpu().numpy().copy(), int(jt.cpu().numpy()[0])))
+    assert (ct.cpu().numpy() == 0).all()
+    return out
+
+
+def test_un_rang_egale_le_pas():
+    import troncons_b200.modele as M
+    from troncons_b200.parallele import ModeleEP
+
+    ep = ModeleEP(0, 1, **FORME)
+    m = M.Modele(**FORME)
+    jetons = np.random.default_rng(4).integers(0, 512, 24)
+    for actifs in ("compresse", "brut"):
+        ep.choisir(actifs)
+        m.choisir(actifs)
+        ep.controle.zero_()
+        a = _suite(ep.pas, ep.m.vues, jetons)
+        assert (ep.controle == 0).all()
+        b = _suite(m.pas, m.vues, jetons)
+        for t, ((za, ja), (zb, jb)) in enumerate(zip(a, b)):
+            assert np.array_equal(za.view(np.int32), zb.view(np.int32)) and ja == jb, f"{actifs} step {t}"
+
+
+def _port_libre() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rang(rang, monde, port, echange):
+    import torch.distributed as dist
+
+    import troncons_b200.modele as M
+    from troncons_b200.parallele import ModeleEP
+
+    torch.cuda.set_device(rang)
+    dev = torch.device("cuda", rang)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rang, world_size=monde,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        ep = ModeleEP(rang, monde, echange=echange, **FORME)
+        seul = M.Modele(**FORME)
+        # the share's parts are the whole model's, byte for byte
+        for l in range(FORME["couches"]):
+            tp, adr, tailles = ep.m.parties["compresse"][l]
+            tt, adr_t, tailles_t = seul.parties["compresse"][l]
+            for e in range(*ep.tenus):
+                a = tp[int(adr[e]) - tp.data_ptr():int(adr[e]) - tp.data_ptr() + int(tailles[e])]
+                b = tt[int(adr_t[e]) - tt.data_ptr():int(adr_t[e]) - tt.data_ptr() + int(tailles_t[e])]
+                assert torch.equal(a, b), (l, e)
+            assert all(adr[e] == 0 for e in range(FORME["experts"]) if not ep.tenus[0] <= e < ep.tenus[1])
+        jetons = np.random.default_rng(100 + rang).integers(0, 512, 20)  # each rank its own sequence
+        for actifs in ("compresse", "brut"):
+            ep.choisir(actifs)
+            seul.choisir(actifs)
+            a = _suite(ep.pas, ep.m.vues, jetons)
+            b = _suite(seul.pas, seul.vues, jetons)
+            for t, ((za, ja), (zb, jb)) in enumerate(zip(a, b)):
+                assert np.abs(za - zb).max() <= 1e-5 * np.abs(zb).max(), f"rank {rang} {actifs} step {t}"
+                assert ja == jb, f"rank {rang} {actifs} step {t}"
+        assert (ep.controle == 0).all()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("echange", ["pairs", "nccl"])
+def test_deux_rangs_egalent_un_gpu(echange):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_rang, args=(2, _port_libre(), echange), nprocs=2, join=True, start_method="spawn")

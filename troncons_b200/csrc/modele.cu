@@ -272,6 +272,101 @@ DispositionModele disposition_modele(const trc_modele_config& m) {
     return d;
 }
 
+// The checks every entry of the step makes (descriptor, shapes, workspace), then the stream's
+// device.
+int verifier_modele(const trc_modele_config* m, DispositionModele& d, void* flux) {
+    if (m == nullptr || m->couches == 0 || m->couches_desc == 0 || m->espace == 0 || m->enchassement == 0)
+        return tb::erreur_usage("model: descriptor incomplete");
+    if (m->dim_tete != 64 || m->tetes % m->tetes_kv != 0 || m->d % 32 != 0 || m->k == 0 || m->k > 8)
+        return tb::erreur_usage("model: attention or routing shape not supported");
+    d = disposition_modele(*m);
+    if (m->espace_octets < d.total || m->espace % 256 != 0) return tb::erreur_usage("model: workspace too small or misaligned");
+    if (cudaError_t e = tb::aligner_device(flux)) return tb::erreur_cuda(e);
+    return TRC_OK;
+}
+
+#define ESSAI(x)                                       \
+    do {                                               \
+        if (cudaError_t e_ = (x)) return e_;           \
+    } while (0)
+
+// Layer l's attention side for the token in x at `position` (Modele::debut_couche, trc-modele/
+// src/lib.rs:476-531): RMSNorm, q / k / v, YaRN, the KV write, attention, x += o; then the
+// post-attention RMSNorm into h2, the MoE's input.
+cudaError_t etape_attention(const trc_modele_config& m, const DispositionModele& d, uint8_t* esp, uint32_t l,
+                            uint32_t position, cudaStream_t f) {
+    auto F = [&](uint64_t o) { return reinterpret_cast<float*>(esp + o); };
+    auto P = [](uint64_t a) { return reinterpret_cast<const float*>(a); };
+    const uint32_t D = m.d, dq = m.tetes * m.dim_tete, dkv = m.tetes_kv * m.dim_tete;
+    const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(m.couches_desc)[l];
+    tb::ParamsRope rope;
+    std::memcpy(&rope, &m.rope, sizeof rope);
+    ESSAI(tb::lancer_rmsnorm(F(d.x), P(c.attn_norm), F(d.h), D, 1, m.eps, f));
+    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wq), F(d.h), P(c.bq), F(d.q), dq, D, f));
+    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wk), F(d.h), P(c.bk), F(d.k), dkv, D, f));
+    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wv), F(d.h), P(c.bv), F(d.v), dkv, D, f));
+    ESSAI(tb::lancer_rope_yarn(F(d.q), F(d.k), m.tetes, m.tetes_kv, position, rope, f));
+    const uint32_t case_kv = c.anneau ? position % c.anneau : position;
+    ESSAI(tb::lancer_ecrire_kv(F(d.k), F(d.v), reinterpret_cast<uint16_t*>(c.cache_k), reinterpret_cast<uint16_t*>(c.cache_v),
+                               dkv, case_kv, f));
+    tb::ParamsAttention pa{};
+    pa.tetes = m.tetes;
+    pa.tetes_kv = m.tetes_kv;
+    pa.dim_tete = m.dim_tete;
+    pa.fin = position + 1;
+    pa.debut = c.anneau && pa.fin > c.anneau ? pa.fin - c.anneau : 0;
+    pa.anneau = c.anneau;
+    pa.echelle = 1.0f / std::sqrt(float(m.dim_tete));
+    ESSAI(tb::lancer_attention(F(d.q), reinterpret_cast<const uint16_t*>(c.cache_k),
+                               reinterpret_cast<const uint16_t*>(c.cache_v), P(c.puits), F(d.a), pa, f));
+    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wo), F(d.a), P(c.bo), F(d.o), D, dq, f));
+    ESSAI(tb::lancer_combiner(F(d.x), F(d.o), D, nullptr, 1, D, f));
+    ESSAI(tb::lancer_rmsnorm(F(d.x), P(c.post_norm), F(d.h2), D, 1, m.eps, f));
+    return cudaSuccess;
+}
+
+// Layer l's MoE for the token (Modele::fin_couche, lib.rs:533-553): router logits, top-k
+// softmax, then the fused layer (x += the weighted experts).
+cudaError_t etape_moe(const trc_modele_config& m, const DispositionModele& d, uint8_t* esp, uint32_t l, cudaStream_t f) {
+    auto F = [&](uint64_t o) { return reinterpret_cast<float*>(esp + o); };
+    auto P = [](uint64_t a) { return reinterpret_cast<const float*>(a); };
+    const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(m.couches_desc)[l];
+    ESSAI(tb::lancer_gemv_f32(P(c.wr), F(d.h2), 0u, P(c.br), F(d.lr), m.experts, m.d, f));
+    ESSAI(tb::lancer_topk(F(d.lr), m.experts, m.k, reinterpret_cast<uint32_t*>(esp + d.idx), F(d.pw), nullptr, 0, f));
+    tb::Couche k{};
+    k.parties = reinterpret_cast<const uint64_t*>(c.parties);
+    k.parties_octets = reinterpret_cast<const uint64_t*>(c.parties_octets);
+    k.experts = m.experts;
+    k.k = m.k;
+    k.luts = reinterpret_cast<const uint32_t*>(c.luts);
+    for (int j = 0; j < 3; ++j) {
+        k.lignes[j] = m.dims.lignes[j];
+        k.colonnes[j] = m.dims.colonnes[j];
+    }
+    k.indices = reinterpret_cast<const uint32_t*>(esp + d.idx);
+    k.poids = F(d.pw);
+    k.x = F(d.h2);
+    k.x_bf16 = 0;
+    k.brut = m.brut ? 1u : 0u;
+    k.residu = F(d.x);
+    k.controle = reinterpret_cast<uint32_t*>(esp + d.controle);
+    k.n_delta = m.n_delta;
+    k.n_codes = m.n_codes;
+    k.jetons = 1;
+    return tb::lancer_moe(k, esp + d.moe, d.total - d.moe, f);
+}
+
+// After the last layer (Modele::sortie, lib.rs:555-568): RMSNorm, the Q8_0 unembedding, the greedy
+// token.
+cudaError_t etape_sortie(const trc_modele_config& m, const DispositionModele& d, uint8_t* esp, cudaStream_t f) {
+    auto F = [&](uint64_t o) { return reinterpret_cast<float*>(esp + o); };
+    ESSAI(tb::lancer_rmsnorm(F(d.x), reinterpret_cast<const float*>(m.norme_sortie), F(d.h), m.d, 1, m.eps, f));
+    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(m.sortie), F(d.h), nullptr, F(d.z), m.vocab, m.d, f));
+    return tb::lancer_argmax(F(d.z), m.vocab, reinterpret_cast<uint32_t*>(esp + d.jeton), f);
+}
+
+#undef ESSAI
+
 }  // namespace
 
 extern "C" {
@@ -352,81 +447,64 @@ int trc_modele_sorties(const trc_modele_config* m, uint64_t* logits, uint64_t* j
 // One token (Modele::enchasser + debut_couche/fin_couche per layer + sortie, trc-modele/src/
 // lib.rs:476-568). `sortie` = 0 skips the unembedding (a context token).
 int trc_modele_pas(const trc_modele_config* m, uint32_t jeton, uint32_t position, uint32_t sortie, void* flux) {
-    if (m == nullptr || m->couches == 0 || m->couches_desc == 0 || m->espace == 0 || m->enchassement == 0)
-        return tb::erreur_usage("model: descriptor incomplete");
+    DispositionModele d;
+    if (int r = verifier_modele(m, d, flux)) return r;
     if (jeton >= m->vocab || position >= m->contexte) return tb::erreur_usage("model: token or position out of range");
-    if (m->dim_tete != 64 || m->tetes % m->tetes_kv != 0 || m->d % 32 != 0 || m->k == 0 || m->k > 8)
-        return tb::erreur_usage("model: attention or routing shape not supported");
-    const DispositionModele d = disposition_modele(*m);
-    if (m->espace_octets < d.total || m->espace % 256 != 0) return tb::erreur_usage("model: workspace too small or misaligned");
-    if (cudaError_t e = tb::aligner_device(flux)) return tb::erreur_cuda(e);
     const cudaStream_t f = static_cast<cudaStream_t>(flux);
     uint8_t* esp = reinterpret_cast<uint8_t*>(m->espace);
-    auto F = [&](uint64_t o) { return reinterpret_cast<float*>(esp + o); };
-    const uint32_t D = m->d, dq = m->tetes * m->dim_tete, dkv = m->tetes_kv * m->dim_tete;
-    tb::ParamsRope rope;
-    std::memcpy(&rope, &m->rope, sizeof rope);
-    cudaError_t e;
-#define ESSAI(x)                                      \
-    do {                                              \
-        if ((e = (x)) != cudaSuccess) return tb::erreur_cuda(e); \
-    } while (0)
-    ESSAI(tb::lancer_ligne_q8_0(reinterpret_cast<const void*>(m->enchassement), jeton, D, F(d.x), f));
-    const trc_modele_couche* couches = reinterpret_cast<const trc_modele_couche*>(m->couches_desc);
-    for (uint32_t l = 0; l < m->couches; ++l) {
-        const trc_modele_couche& c = couches[l];
-        auto P = [](uint64_t a) { return reinterpret_cast<const float*>(a); };
-        ESSAI(tb::lancer_rmsnorm(F(d.x), P(c.attn_norm), F(d.h), D, 1, m->eps, f));
-        ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wq), F(d.h), P(c.bq), F(d.q), dq, D, f));
-        ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wk), F(d.h), P(c.bk), F(d.k), dkv, D, f));
-        ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wv), F(d.h), P(c.bv), F(d.v), dkv, D, f));
-        ESSAI(tb::lancer_rope_yarn(F(d.q), F(d.k), m->tetes, m->tetes_kv, position, rope, f));
-        const uint32_t case_kv = c.anneau ? position % c.anneau : position;
-        ESSAI(tb::lancer_ecrire_kv(F(d.k), F(d.v), reinterpret_cast<uint16_t*>(c.cache_k), reinterpret_cast<uint16_t*>(c.cache_v),
-                                   dkv, case_kv, f));
-        tb::ParamsAttention pa{};
-        pa.tetes = m->tetes;
-        pa.tetes_kv = m->tetes_kv;
-        pa.dim_tete = m->dim_tete;
-        pa.fin = position + 1;
-        pa.debut = c.anneau && pa.fin > c.anneau ? pa.fin - c.anneau : 0;
-        pa.anneau = c.anneau;
-        pa.echelle = 1.0f / std::sqrt(float(m->dim_tete));
-        ESSAI(tb::lancer_attention(F(d.q), reinterpret_cast<const uint16_t*>(c.cache_k),
-                                   reinterpret_cast<const uint16_t*>(c.cache_v), P(c.puits), F(d.a), pa, f));
-        ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wo), F(d.a), P(c.bo), F(d.o), D, dq, f));
-        ESSAI(tb::lancer_combiner(F(d.x), F(d.o), D, nullptr, 1, D, f));
-        ESSAI(tb::lancer_rmsnorm(F(d.x), P(c.post_norm), F(d.h2), D, 1, m->eps, f));
-        ESSAI(tb::lancer_gemv_f32(P(c.wr), F(d.h2), 0u, P(c.br), F(d.lr), m->experts, D, f));
-        ESSAI(tb::lancer_topk(F(d.lr), m->experts, m->k, reinterpret_cast<uint32_t*>(esp + d.idx), F(d.pw), nullptr, 0, f));
-        tb::Couche k{};
-        k.parties = reinterpret_cast<const uint64_t*>(c.parties);
-        k.parties_octets = reinterpret_cast<const uint64_t*>(c.parties_octets);
-        k.experts = m->experts;
-        k.k = m->k;
-        k.luts = reinterpret_cast<const uint32_t*>(c.luts);
-        for (int j = 0; j < 3; ++j) {
-            k.lignes[j] = m->dims.lignes[j];
-            k.colonnes[j] = m->dims.colonnes[j];
-        }
-        k.indices = reinterpret_cast<const uint32_t*>(esp + d.idx);
-        k.poids = F(d.pw);
-        k.x = F(d.h2);
-        k.x_bf16 = 0;
-        k.brut = m->brut ? 1u : 0u;
-        k.residu = F(d.x);
-        k.controle = reinterpret_cast<uint32_t*>(esp + d.controle);
-        k.n_delta = m->n_delta;
-        k.n_codes = m->n_codes;
-        k.jetons = 1;
-        ESSAI(tb::lancer_moe(k, esp + d.moe, d.total - d.moe, f));
+    cudaError_t e = tb::lancer_ligne_q8_0(reinterpret_cast<const void*>(m->enchassement), jeton, m->d,
+                                          reinterpret_cast<float*>(esp + d.x), f);
+    for (uint32_t l = 0; l < m->couches && e == cudaSuccess; ++l) {
+        e = etape_attention(*m, d, esp, l, position, f);
+        if (e == cudaSuccess) e = etape_moe(*m, d, esp, l, f);
     }
-    if (sortie) {
-        ESSAI(tb::lancer_rmsnorm(F(d.x), reinterpret_cast<const float*>(m->norme_sortie), F(d.h), D, 1, m->eps, f));
-        ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(m->sortie), F(d.h), nullptr, F(d.z), m->vocab, D, f));
-        ESSAI(tb::lancer_argmax(F(d.z), m->vocab, reinterpret_cast<uint32_t*>(esp + d.jeton), f));
-    }
-#undef ESSAI
+    if (e == cudaSuccess && sortie) e = etape_sortie(*m, d, esp, f);
+    return e == cudaSuccess ? TRC_OK : tb::erreur_cuda(e);
+}
+
+int trc_modele_debut(const trc_modele_config* m, uint32_t jeton, void* flux) {
+    DispositionModele d;
+    if (int r = verifier_modele(m, d, flux)) return r;
+    if (jeton >= m->vocab) return tb::erreur_usage("model: token out of range");
+    uint8_t* esp = reinterpret_cast<uint8_t*>(m->espace);
+    if (cudaError_t e = tb::lancer_ligne_q8_0(reinterpret_cast<const void*>(m->enchassement), jeton, m->d,
+                                              reinterpret_cast<float*>(esp + d.x), static_cast<cudaStream_t>(flux)))
+        return tb::erreur_cuda(e);
+    return TRC_OK;
+}
+
+int trc_modele_attention(const trc_modele_config* m, uint32_t couche, uint32_t position, void* flux) {
+    DispositionModele d;
+    if (int r = verifier_modele(m, d, flux)) return r;
+    if (couche >= m->couches || position >= m->contexte) return tb::erreur_usage("model: layer or position out of range");
+    if (cudaError_t e = etape_attention(*m, d, reinterpret_cast<uint8_t*>(m->espace), couche, position,
+                                        static_cast<cudaStream_t>(flux)))
+        return tb::erreur_cuda(e);
+    return TRC_OK;
+}
+
+int trc_modele_moe(const trc_modele_config* m, uint32_t couche, void* flux) {
+    DispositionModele d;
+    if (int r = verifier_modele(m, d, flux)) return r;
+    if (couche >= m->couches) return tb::erreur_usage("model: layer out of range");
+    if (cudaError_t e = etape_moe(*m, d, reinterpret_cast<uint8_t*>(m->espace), couche, static_cast<cudaStream_t>(flux)))
+        return tb::erreur_cuda(e);
+    return TRC_OK;
+}
+
+int trc_modele_fin(const trc_modele_config* m, void* flux) {
+    DispositionModele d;
+    if (int r = verifier_modele(m, d, flux)) return r;
+    if (cudaError_t e = etape_sortie(*m, d, reinterpret_cast<uint8_t*>(m->espace), static_cast<cudaStream_t>(flux)))
+        return tb::erreur_cuda(e);
+    return TRC_OK;
+}
+
+int trc_modele_etat(const trc_modele_config* m, uint64_t* x, uint64_t* h2) {
+    if (m == nullptr || m->espace == 0) return tb::erreur_usage("model absent");
+    const DispositionModele d = disposition_modele(*m);
+    if (x) *x = m->espace + d.x;
+    if (h2) *h2 = m->espace + d.h2;
     return TRC_OK;
 }
 

@@ -34,6 +34,11 @@ for _n, (_r, _a) in {
     "trc_modele_espace_octets": (_u64, [_vp]),
     "trc_modele_sorties": (_i32, [_vp, _vp, _vp, _vp]),
     "trc_modele_pas": (_i32, [_vp, _u32, _u32, _u32, _vp]),
+    "trc_modele_debut": (_i32, [_vp, _u32, _vp]),
+    "trc_modele_attention": (_i32, [_vp, _u32, _u32, _vp]),
+    "trc_modele_moe": (_i32, [_vp, _u32, _vp]),
+    "trc_modele_fin": (_i32, [_vp, _vp]),
+    "trc_modele_etat": (_i32, [_vp, _vp, _vp]),
     "trc_synth_mxfp4_gpu": (_i32, [_vp, _vp, _u32, _u32, _u64, _u64, _vp]),
     "trc_synth_q8_0_gpu": (_i32, [_vp, _u32, _u32, _u64, _u64, _vp]),
     "trc_synth_f32_gpu": (_i32, [_vp, _u64, _u64, _u64, C.c_float, C.c_float, _vp]),
@@ -108,7 +113,13 @@ class Modele:
 
     def __init__(self, couches: int, d: int, tetes: int, tetes_kv: int, experts: int, k: int, vocab: int,
                  contexte: int, ffn: int, fenetre: int = 128, graine: int = 1, compresse: bool = True,
-                 brut: bool = False, lot: int = 32, eps: float = 1e-5, rope: ParamsRope | None = None):
+                 brut: bool = False, lot: int = 32, eps: float = 1e-5, rope: ParamsRope | None = None,
+                 tenus: tuple | None = None, reduire=None):
+        """`tenus` = (debut, fin): draw and encode only the experts [debut, fin) of every layer (an
+        expert-parallel share; the others' parts are absent), their rANS tables built from the
+        counts of all experts when `reduire` sums the share's counts over the ranks (an
+        all-reduce: parallele.reduire_comptes), so every share's parts are byte for byte those of
+        the whole model."""
         import torch
 
         import troncons_b200.synth as S
@@ -143,39 +154,46 @@ class Modele:
         self.enchassement = synth_q8_0(vocab, d, g, ident("emb"))
         self.sortie_w = synth_q8_0(vocab, d, g, ident("out"))
         self.norme_sortie = synth_f32(d, g, ident("on"), 1.0, 0.02)
-        # experts: draw every expert of a layer on the GPU, count, tables, encode in batches
+        # experts: draw the held experts of a layer on the GPU, count, tables, encode in batches
+        self.tenus = tuple(tenus) if tenus is not None else (0, experts)
+        if not 0 <= self.tenus[0] < self.tenus[1] <= experts:
+            raise ValueError(f"expert share {self.tenus} of {experts}")
+        ids = list(range(*self.tenus))
         self.parties = {"compresse": [], "brut": []}
         taille_src = sum(self.dims.lignes[j] * (self.dims.colonnes[j] // 32) * 17 for j in range(3))
         blocs = [[torch.empty(self.dims.lignes[j] * (self.dims.colonnes[j] // 32) * 17, dtype=torch.uint8,
-                              device="cuda") for j in range(3)] for _ in range(experts)]
+                              device="cuda") for j in range(3)] for _ in ids]
         biais = [[torch.empty(self.dims.lignes[j], dtype=torch.float32, device="cuda") for j in range(3)]
-                 for _ in range(experts)]
+                 for _ in ids]
         self.luts = []
         entete, taille_brute = entete_brute(self.dims)
         entete_dev = torch.from_numpy(entete).cuda()
         for l in range(couches):
-            for e in range(experts):
+            for i, e in enumerate(ids):
                 for j in range(3):
-                    verifier(lib.trc_synth_mxfp4_gpu(blocs[e][j].data_ptr(), biais[e][j].data_ptr(),
+                    verifier(lib.trc_synth_mxfp4_gpu(blocs[i][j].data_ptr(), biais[i][j].data_ptr(),
                                                      self.dims.lignes[j], self.dims.colonnes[j], g,
                                                      ident("ex", l, e, j), _flux()))
             if compresse:
-                cpt = S.comptes_gpu(blocs, self.dims)
-                freqs = S.tables_de_comptes(cpt.cpu().numpy().astype(np.uint64).reshape(3, 4, 256))
+                cpt = S.comptes_gpu(blocs, self.dims).cpu().numpy().astype(np.uint64).reshape(3, 4, 256)
+                if reduire is not None:
+                    cpt = reduire(cpt)
+                freqs = S.tables_de_comptes(cpt)
                 self.luts.append(torch.from_numpy(S.luts(freqs).view(np.int32)).cuda())
-                self.parties["compresse"].append(self._encoder(blocs, biais, freqs, l, lot, taille_src))
+                self.parties["compresse"].append(self._encoder(blocs, biais, freqs, l, lot, taille_src, ids))
             else:
                 self.luts.append(torch.zeros(3 * 4 * 4096, dtype=torch.int32, device="cuda"))
             if brut:
-                self.parties["brut"].append(self._bruts(blocs, biais, entete_dev, taille_brute))
+                self.parties["brut"].append(self._bruts(blocs, biais, entete_dev, taille_brute, ids))
         del blocs, biais
         torch.cuda.synchronize()
         self.actifs = "compresse" if compresse else "brut"
         self._monter()
 
-    def _encoder(self, blocs, biais, freqs, couche: int, lot: int, taille_src: int):
-        """The layer's experts encoded on the GPU in batches of `lot`, then packed back to back
-        (each part 4096-aligned) in one buffer: (buffer, addresses u64[E], sizes u64[E])."""
+    def _encoder(self, blocs, biais, freqs, couche: int, lot: int, taille_src: int, ids: list):
+        """The layer's held experts `ids` encoded on the GPU in batches of `lot`, then packed back to
+        back (each part 4096-aligned) in one buffer: (buffer, addresses u64[E], sizes u64[E]), 0
+        for the experts not held."""
         import torch
 
         import troncons_b200.synth as S
@@ -183,10 +201,10 @@ class Modele:
         f = torch.from_numpy(np.ascontiguousarray(freqs, np.uint16).reshape(-1).view(np.int16)).cuda()
         cap = (taille_src * 11 // 10 + (1 << 16) + 4095) // 4096 * 4096
         morceaux, tailles = [], []
-        for e0 in range(0, self.experts, lot):
-            n = min(lot, self.experts - e0)
+        for e0 in range(0, len(ids), lot):
+            n = min(lot, len(ids) - e0)
             sorties = torch.empty(n * cap, dtype=torch.uint8, device="cuda")
-            descs = S._descs_gpu(blocs[e0:e0 + n], biais[e0:e0 + n], list(range(e0, e0 + n)),
+            descs = S._descs_gpu(blocs[e0:e0 + n], biais[e0:e0 + n], ids[e0:e0 + n],
                                  [sorties[i * cap:(i + 1) * cap] for i in range(n)], cap)
             octets = torch.zeros(2 * n, dtype=torch.int64, device="cuda")
             n_esp = int(lib.trc_coder_parties_gpu_espace(C.byref(self.dims), n, 256, 256))
@@ -197,32 +215,35 @@ class Modele:
             o = octets.cpu().numpy()
             for i in range(n):
                 if o[2 * i] == 0 or o[2 * i] > cap:
-                    raise RuntimeError(f"layer {couche}, expert {e0 + i}: part not encoded ({o[2 * i]} bytes)")
+                    raise RuntimeError(f"layer {couche}, expert {ids[e0 + i]}: part not encoded ({o[2 * i]} bytes)")
                 morceaux.append(sorties[i * cap:i * cap + int(o[2 * i])])
                 tailles.append(int(o[2 * i]))
             self._garde.append((sorties, descs, esp))
         tampon = torch.empty(sum(tailles), dtype=torch.uint8, device="cuda")
-        p, adr = 0, []
-        for m, t in zip(morceaux, tailles):
+        p = 0
+        adr, octets = np.zeros(self.experts, np.uint64), np.zeros(self.experts, np.uint64)
+        for e, m, t in zip(ids, morceaux, tailles):
             tampon[p:p + t].copy_(m)
-            adr.append(tampon.data_ptr() + p)
+            adr[e], octets[e] = tampon.data_ptr() + p, t
             p += t
         self._garde = []
-        return tampon, np.array(adr, np.uint64), np.array(tailles, np.uint64)
+        return tampon, adr, octets
 
-    def _bruts(self, blocs, biais, entete_dev, taille: int):
+    def _bruts(self, blocs, biais, entete_dev, taille: int, ids: list):
         import torch
 
         import troncons_b200.synth as S
 
-        tampon = torch.empty(self.experts * taille, dtype=torch.uint8, device="cuda")
-        descs = S._descs_gpu(blocs, biais, list(range(self.experts)),
-                             [tampon[e * taille:(e + 1) * taille] for e in range(self.experts)], taille)
-        verifier(lib.trc_parties_brutes_gpu(descs.data_ptr(), self.experts, C.byref(self.dims), entete_dev.data_ptr(),
+        n = len(ids)
+        tampon = torch.empty(n * taille, dtype=torch.uint8, device="cuda")
+        descs = S._descs_gpu(blocs, biais, ids, [tampon[i * taille:(i + 1) * taille] for i in range(n)], taille)
+        verifier(lib.trc_parties_brutes_gpu(descs.data_ptr(), n, C.byref(self.dims), entete_dev.data_ptr(),
                                             entete_dev.numel(), taille, _flux()))
         torch.cuda.synchronize()
-        adr = np.array([tampon.data_ptr() + e * taille for e in range(self.experts)], np.uint64)
-        return tampon, adr, np.full(self.experts, taille, np.uint64)
+        adr, octets = np.zeros(self.experts, np.uint64), np.zeros(self.experts, np.uint64)
+        for i, e in enumerate(ids):
+            adr[e], octets[e] = tampon.data_ptr() + i * taille, taille
+        return tampon, adr, octets
 
     def _monter(self):
         """The descriptor of the parts chosen by self.actifs, and the workspace."""

@@ -62,6 +62,30 @@ def etape_ep(calcul_local, residu, rang: int, groupe=None) -> None:
     dist.all_reduce(residu, op=dist.ReduceOp.SUM, group=groupe)
 
 
+def monter_paires(dims, jetons: int, rang: int, monde: int, groupe=None):
+    """The combine's exchange buffers: one symmetric-memory buffer per rank (torch.distributed's),
+    mapped in every rank's address space, zeroed on every rank before any exchange. Returns
+    (buffer, handle, EchangePairs) (keep the first two alive as long as the third is used)."""
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm
+
+    from . import EchangePairs, echange_octets
+
+    g = groupe if groupe is not None else dist.group.WORLD
+    n = echange_octets(dims, jetons, monde)
+    tampon = symm.empty(n, dtype=torch.uint8, device=torch.device("cuda", torch.cuda.current_device()))
+    tampon.zero_()
+    poignee = symm.rendezvous(tampon, g)
+    ptrs = [int(p) for p in poignee.buffer_ptrs]
+    if len(ptrs) != monde or any(p % 256 for p in ptrs):
+        raise RuntimeError(f"symmetric memory: {len(ptrs)} buffers for {monde} ranks, or misaligned")
+    paires = EchangePairs((C.c_uint64 * 8)(*(ptrs + [0] * (8 - len(ptrs)))), rang, monde)
+    torch.cuda.synchronize()
+    dist.barrier(group=groupe)  # every buffer zeroed before any rank's first exchange
+    return tampon, poignee, paires
+
+
 class CoucheEP:
     """This rank's share of a layer on its GPU: the parts of its experts, the layer's LUTs and
     the router; `etape` runs router + fused share + the combine's exchange on the current stream."""
@@ -78,24 +102,7 @@ class CoucheEP:
             self._monter_paires(c, jetons)
 
     def _monter_paires(self, c, jetons: int) -> None:
-        import torch
-        import torch.distributed as dist
-        import torch.distributed._symmetric_memory as symm
-
-        from . import EchangePairs, echange_octets
-
-        groupe = self.groupe if self.groupe is not None else dist.group.WORLD
-        n = echange_octets(c.dims, jetons, self.monde)
-        self.tampon = symm.empty(n, dtype=torch.uint8, device=torch.device("cuda", torch.cuda.current_device()))
-        self.tampon.zero_()
-        self.poignee = symm.rendezvous(self.tampon, groupe)
-        ptrs = [int(p) for p in self.poignee.buffer_ptrs]
-        if len(ptrs) != self.monde or any(p % 256 for p in ptrs):
-            raise RuntimeError(f"symmetric memory: {len(ptrs)} buffers for {self.monde} ranks, or misaligned")
-        tampons = (C.c_uint64 * 8)(*(ptrs + [0] * (8 - len(ptrs))))
-        self.paires = EchangePairs(tampons, self.rang, self.monde)
-        torch.cuda.synchronize()
-        dist.barrier(group=self.groupe)  # every buffer zeroed before any rank's first exchange
+        self.tampon, self.poignee, self.paires = monter_paires(c.dims, jetons, self.rang, self.monde, self.groupe)
 
     def local(self, x, residu, partiel: bool, flux=None) -> None:
         self.carte.couche(x, residu, flux=flux, partiel=partiel)
@@ -108,3 +115,131 @@ class CoucheEP:
             etape_ep(lambda r, p: self.local(x, r, p, flux), residu, self.rang, self.groupe)
         else:
             self.carte.couche(x, residu, flux=flux)
+
+
+class ModeleEP:
+    """The expert-parallel decode step of a whole gpt-oss model: one process per GPU, one
+    sequence per rank (a batch of `monde` sequences), each rank holding its contiguous share of
+    every layer's experts (16 of 128 at 8 GPUs) and a replica of the dense weights.
+
+    Per layer (the phases of trc_modele_pas, with the exchange between them): the attention side
+    of the rank's own token (trc_modele_attention: its KV cache stays on its GPU); an all-gather
+    of the MoE inputs h2 ([monde][d] f32, NCCL); the router on every token (replicated, identical
+    on every rank); the fused layer on the rank's share for every token; then the combine's
+    exchange. "nccl" (the default): each token's share written alone (partiel), a SUM
+    reduce-scatter, added into x. "pairs": the combine kernel writes each token's share into every
+    rank's symmetric buffer over NVLink peer stores and adds all ranks' shares in rank order into
+    [monde][d] rows, this rank's row holding its x (copied in before, out after); measured 3 %
+    slower on the whole model at 2 GPUs (the copies and the zeroing; the step waits on the busiest
+    rank's share either way). Then the rank's unembedding and greedy token.
+
+    The weighted experts' sum is the single-GPU combine's terms in another order (the shares
+    summed across ranks), so the logits agree with the one-GPU model within f32 rounding, not
+    bit for bit; with one rank the step is trc_modele_pas's bits."""
+
+    def __init__(self, rang: int, monde: int, groupe=None, echange: str = "nccl", **modele):
+        import torch
+
+        from . import espace_recouvrant_octets
+        from .modele import Modele
+
+        self.rang, self.monde, self.groupe = rang, monde, groupe
+        if echange not in ("pairs", "nccl"):
+            raise ValueError(f"exchange {echange!r}: 'pairs' or 'nccl'")
+        self.echange = echange if monde > 1 else "aucun"
+        self.tenus = partage(modele["experts"], rang, monde)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.m = Modele(**modele, tenus=self.tenus, reduire=reduire_comptes(groupe, dev) if monde > 1 else None)
+        m = self.m
+        f32 = torch.float32
+        self.h2_tous = torch.empty(monde * m.d, dtype=f32, device=dev)
+        self.y_tous = torch.empty(monde * m.d, dtype=f32, device=dev)
+        self.y = torch.empty(m.d, dtype=f32, device=dev)
+        self.logits_routeur = torch.empty(monde * m.experts, dtype=f32, device=dev)
+        self.idx = torch.empty(monde * m.k, dtype=torch.int32, device=dev)
+        self.poids = torch.empty(monde * m.k, dtype=f32, device=dev)
+        self.controle = torch.zeros(monde * m.k * 4, dtype=torch.int32, device=dev)
+        n = espace_recouvrant_octets(m.dims, monde * m.k)
+        self._espace = torch.empty(n + 256, dtype=torch.uint8, device=dev)
+        self.espace_octets = n
+        if self.echange == "pairs":
+            self.tampon, self.poignee, self.paires = monter_paires(m.dims, monde, rang, monde, groupe)
+        self._monter()
+
+    def _monter(self) -> None:
+        import torch
+
+        from . import MoeCouche, lib, verifier
+
+        m = self.m
+        x, h2 = C.c_uint64(), C.c_uint64()
+        verifier(lib.trc_modele_etat(C.byref(m.config), C.byref(x), C.byref(h2)))
+        base = m.espace.data_ptr()
+        self.x = m.espace[x.value - base:x.value - base + 4 * m.d].view(torch.float32)
+        self.h2 = m.espace[h2.value - base:h2.value - base + 4 * m.d].view(torch.float32)
+        entree = self.h2 if self.monde == 1 else self.h2_tous
+        self.descs = []
+        for l in range(m.couches):
+            ta, tt = m._tables[l]
+            d = MoeCouche()
+            d.parties, d.parties_octets = ta.data_ptr(), tt.data_ptr()
+            d.experts, d.k, d.luts, d.dims = m.experts, m.k, m.luts[l].data_ptr(), m.dims
+            d.indices, d.poids = self.idx.data_ptr(), self.poids.data_ptr()
+            d.x, d.x_bf16, d.brut = entree.data_ptr(), 0, int(m.actifs == "brut")
+            d.residu, d.controle = self.y_tous.data_ptr(), self.controle.data_ptr()
+            d.n_delta = d.n_codes = 0
+            d.jetons = self.monde
+            d.expert_debut, d.expert_fin = self.tenus
+            if self.echange == "pairs":
+                d.partiel, d.echange = 0, C.addressof(self.paires)
+            else:
+                d.partiel = 1
+            self.descs.append(d)
+        self._entree = entree
+        self._ligne = self.y_tous.view(self.monde, m.d)[self.rang]
+
+    def choisir(self, actifs: str) -> None:
+        """Run on the compressed or raw parts; the KV caches are cleared."""
+        self.m.choisir(actifs)
+        self._monter()
+
+    def pas(self, jeton: int, position: int, sortie: bool = True, flux=None) -> None:
+        """This rank's token `jeton` at `position`; every rank calls it once per step (the
+        collectives pair them up). Logits and greedy token in m.vues()."""
+        import torch
+        import torch.distributed as dist
+
+        from . import lib, verifier
+
+        m, cfg = self.m, C.byref(self.m.config)
+        s = flux or torch.cuda.current_stream()
+        f = s.cuda_stream
+        e = self._espace.data_ptr()
+        e += (-e) % 256
+        verifier(lib.trc_modele_debut(cfg, jeton, f))
+        with torch.cuda.stream(s):
+            if self.echange == "pairs":
+                # the exchange adds every rank's shares into all N rows of y_tous; this rank's row
+                # carries its x through the layer, the other rows restart from 0 every step
+                self.y_tous.zero_()
+            for l in range(m.couches):
+                t = m.tenseurs[l]
+                verifier(lib.trc_modele_attention(cfg, l, position, f))
+                if self.monde > 1:
+                    dist.all_gather_into_tensor(self.h2_tous, self.h2, group=self.groupe)
+                verifier(lib.trc_routeur(t["wr"].data_ptr(), t["br"].data_ptr(), self._entree.data_ptr(), 0, m.experts,
+                                         m.d, m.k, self.monde, self.logits_routeur.data_ptr(), self.idx.data_ptr(),
+                                         self.poids.data_ptr(), f))
+                if self.echange == "pairs":
+                    self._ligne.copy_(self.x)
+                    verifier(lib.trc_moe_couche_fusionnee(C.byref(self.descs[l]), e, self.espace_octets, f))
+                    self.x.copy_(self._ligne)
+                else:
+                    verifier(lib.trc_moe_couche_fusionnee(C.byref(self.descs[l]), e, self.espace_octets, f))
+                    if self.monde > 1:
+                        dist.reduce_scatter_tensor(self.y, self.y_tous, op=dist.ReduceOp.SUM, group=self.groupe)
+                        self.x.add_(self.y)
+                    else:
+                        self.x.add_(self.y_tous)
+        if sortie:
+            verifier(lib.trc_modele_fin(cfg, f))
