@@ -67,6 +67,9 @@ def arguments():
     a.add_argument("--couches", type=int, default=36)
     a.add_argument("--codeur", action="store_true",
                    help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
+    a.add_argument("--par-rang", type=int, default=1,
+                   help="sequences per GPU in the expert-parallel whole-model measurement (batch = GPUs x this); "
+                        "with --modele on one GPU, a batch of this many sequences")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
                    help="N > 1: the combine's exchange in the combine kernel over NVLink (pairs) or by NCCL")
     return a.parse_args()
@@ -550,51 +553,60 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
     from troncons_b200.parallele import ModeleEP
 
     r, w, _ = rang()
+    b = args.par_rang
     t0 = time.time()
-    ep = ModeleEP(r, w, echange="nccl", couches=args.couches, d=2880, tetes=64, tetes_kv=8, experts=args.experts, k=args.k,
-                  vocab=201088, contexte=args.contexte + warmup + steps + 1, ffn=2880, fenetre=128, graine=args.graine,
-                  compresse=True, brut=False)
+    ep = ModeleEP(r, w, echange="nccl", par_rang=b, couches=args.couches, d=2880, tetes=64, tetes_kv=8,
+                  experts=args.experts, k=args.k, vocab=201088, contexte=args.contexte + warmup + steps + 1, ffn=2880,
+                  fenetre=128, graine=args.graine, compresse=True, brut=False)
     torch.cuda.synchronize()
     t_gen = time.time() - t0
-    contexte = np.random.default_rng(args.graine + 1000 * r).integers(0, 201088, args.contexte)
-    lg, jt, ct = ep.m.vues()
-    ct.zero_()
+    # each sequence its own seeded context
+    contexte = np.random.default_rng(args.graine + 1000 * r).integers(0, 201088, (b, args.contexte))
+    vues = [ep.vues(i) for i in range(b)]
+    for _, _, ct in vues:
+        ct.zero_()
     ep.controle.zero_()
-    dist.barrier()
+
+    def barriere():
+        if w > 1:
+            dist.barrier()
+
+    barriere()
     t1 = time.time()
-    for p, j in enumerate(contexte):
-        ep.pas(int(j), p, sortie=False)
+    for p in range(args.contexte):
+        ep.pas(contexte[:, p], p, sortie=False)
     torch.cuda.synchronize()
     t_ctx = time.time() - t1
-    pos, j = args.contexte, int(contexte[-1])
+    pos, j = args.contexte, contexte[:, -1].copy()
     for _ in range(warmup):
         ep.pas(j, pos)
-        j = int(jt.cpu().numpy()[0])
+        j = np.array([int(v[1].cpu().numpy()[0]) for v in vues])
         pos += 1
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     torch.cuda.synchronize()
-    dist.barrier()
+    barriere()
     ev[0].record()
     for _ in range(steps):
-        ep.pas(j, pos)  # the greedy token stays on the device: the same token is fed (no host sync)
+        ep.pas(j, pos)  # the greedy tokens stay on the device: the same tokens are fed (no host sync)
         pos += 1
     ev[1].record()
     torch.cuda.synchronize()
     t = torch.tensor([ev[0].elapsed_time(ev[1])], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0]) / steps
     ok = torch.tensor([int((ep.controle.cpu().numpy() == 0).all())], device="cuda")
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if w > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    ms = float(t[0]) / steps
     if not int(ok[0]):
         raise RuntimeError("integrity counters set during the expert-parallel model steps")
     debut, fin = ep.tenus
     del ep
     torch.cuda.empty_cache()
-    return {"metric": f"gpt-oss-120b decode tokens/s (whole step, expert-parallel over {w} GPUs, batch {w})",
-            "value": round(w * 1000.0 / ms, 2), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": steps,
-            "warmup": warmup, "batch": w, "experts_per_gpu": fin - debut,
+    return {"metric": f"gpt-oss-120b decode tokens/s (whole step, expert-parallel over {w} GPUs, batch {w * b})",
+            "value": round(w * b * 1000.0 / ms, 2), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": steps,
+            "warmup": warmup, "batch": w * b, "sequences_per_gpu": b, "experts_per_gpu": fin - debut, "n_gpus": w,
             "workload": f"config 3: {args.couches} layers, {args.experts} experts top-{args.k} ({fin - debut} per GPU), "
-                        f"one sequence per GPU, context {args.contexte} seeded tokens, attention on each sequence's "
+                        f"{b} sequence(s) per GPU, context {args.contexte} seeded tokens, attention on each sequence's "
                         "GPU, MoE inputs all-gathered and the shares' sums reduce-scattered over NCCL per layer",
             "exchange": "nccl",
             "generation_s": round(t_gen, 1), "context_s": round(t_ctx, 1)}
@@ -875,7 +887,11 @@ def bras_prefill(args):
 
 
 def bras_modele(args):
-    """Prints mesurer_modele's line (see there)."""
+    """Prints mesurer_modele's line (see there); with --par-rang B > 1, mesurer_modele_ep's
+    measurement of a batch of B sequences on this one GPU."""
+    if args.par_rang > 1:
+        print(json.dumps(mesurer_modele_ep(args, args.steps, args.warmup)), flush=True)
+        return
     print(json.dumps(mesurer_modele(args, args.steps, args.warmup, args.exactitude)), flush=True)
 
 

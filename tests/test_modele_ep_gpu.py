@@ -10,7 +10,10 @@ gpt-oss-shaped model (2 layers, 8 experts top-4).
   of every layer's experts and runs its own sequence; its logits agree with the one-GPU model run on that sequence within 1e-5 of
   max|z| (the same experts' terms summed in another order across the GPUs) with the same greedy
   token; the shares' parts are byte for byte the whole model's (tables from the counts summed
-  over NCCL). Skipped with fewer than two GPUs."""
+  over NCCL); the same with two sequences per rank (a batch of 4). Skipped with fewer than two
+  GPUs;
+- several sequences on one rank (the router and the fused layer called for the batch): each
+  sequence's logits are the model's on that sequence alone, bit for bit."""
 import os
 import socket
 from datetime import timedelta
@@ -55,6 +58,31 @@ def test_un_rang_egale_le_pas():
             assert np.array_equal(za.view(np.int32), zb.view(np.int32)) and ja == jb, f"{actifs} step {t}"
 
 
+def test_un_rang_plusieurs_sequences():
+    """Three sequences on one rank (the router and the fused layer called for the 3 tokens):
+    each sequence's logits are those of the model run on that sequence alone, bit for bit."""
+    import troncons_b200.modele as M
+    from troncons_b200.parallele import ModeleEP
+
+    ep = ModeleEP(0, 1, par_rang=3, **FORME)
+    m = M.Modele(**FORME)
+    jetons = np.random.default_rng(8).integers(0, 512, (3, 20))
+    ep.choisir("compresse")
+    vues = [ep.vues(i) for i in range(3)]
+    z = [[] for _ in range(3)]
+    for t in range(20):
+        ep.pas(jetons[:, t], t)
+        torch.cuda.synchronize()
+        for i in range(3):
+            z[i].append(vues[i][0].cpu().numpy().copy())
+    assert (ep.controle == 0).all()
+    for i in range(3):
+        m.choisir("compresse")
+        b = _suite(m.pas, m.vues, jetons[i])
+        for t in range(20):
+            assert np.array_equal(z[i][t].view(np.int32), b[t][0].view(np.int32)), f"sequence {i} step {t}"
+
+
 def _port_libre() -> int:
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -95,6 +123,25 @@ def _rang(rang, monde, port, echange):
             for t, ((za, ja), (zb, jb)) in enumerate(zip(a, b)):
                 assert np.abs(za - zb).max() <= 1e-5 * np.abs(zb).max(), f"rank {rang} {actifs} step {t}"
                 assert ja == jb, f"rank {rang} {actifs} step {t}"
+        assert (ep.controle == 0).all()
+        # two sequences per rank: a batch of 4 tokens over 2 GPUs
+        del ep
+        ep = ModeleEP(rang, monde, echange=echange, par_rang=2, **FORME)
+        ep.choisir("compresse")
+        seul.choisir("compresse")
+        jetons = np.random.default_rng(200 + rang).integers(0, 512, (2, 16))
+        vues = [ep.vues(i) for i in range(2)]
+        z = [[] for _ in range(2)]
+        for t in range(16):
+            ep.pas(jetons[:, t], t)
+            torch.cuda.synchronize()
+            for i in range(2):
+                z[i].append(vues[i][0].cpu().numpy().copy())
+        for i in range(2):
+            seul.choisir("compresse")
+            b = _suite(seul.pas, seul.vues, jetons[i])
+            for t in range(16):
+                assert np.abs(z[i][t] - b[t][0]).max() <= 1e-5 * np.abs(b[t][0]).max(), f"rank {rang} seq {i} step {t}"
         assert (ep.controle == 0).all()
         dist.barrier()
     finally:

@@ -250,16 +250,25 @@ class Modele:
         import torch
 
         self._tables = []
-        self.desc_couches = (ModeleCouche * self.couches)()
-        for l, t in enumerate(self.tenseurs):
+        for l in range(self.couches):
             _, adr, tailles = self.parties[self.actifs][l]
-            ta = torch.from_numpy(adr.view(np.int64)).cuda()
-            tt = torch.from_numpy(tailles.view(np.int64)).cuda()
-            self._tables.append((ta, tt))
-            c = self.desc_couches[l]
-            for n in ("attn_norm", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "puits", "post_norm", "wr", "br",
-                      "cache_k", "cache_v"):
+            self._tables.append((torch.from_numpy(adr.view(np.int64)).cuda(),
+                                 torch.from_numpy(tailles.view(np.int64)).cuda()))
+        self.desc_couches, self.config, self.espace, self._sorties = self._config(
+            [(t["cache_k"], t["cache_v"]) for t in self.tenseurs])
+
+    def _config(self, caches):
+        """(layer descriptors, trc_modele_config, workspace, output addresses) of a sequence whose
+        KV caches are `caches` [(k, v)] per layer, over this model's weights and chosen parts."""
+        import torch
+
+        desc = (ModeleCouche * self.couches)()
+        for l, t in enumerate(self.tenseurs):
+            ta, tt = self._tables[l]
+            c = desc[l]
+            for n in ("attn_norm", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "puits", "post_norm", "wr", "br"):
                 setattr(c, n, t[n].data_ptr())
+            c.cache_k, c.cache_v = caches[l][0].data_ptr(), caches[l][1].data_ptr()
             c.parties, c.parties_octets, c.luts = ta.data_ptr(), tt.data_ptr(), self.luts[l].data_ptr()
             c.anneau = t["anneau"]
         m = ModeleConfig()
@@ -269,17 +278,16 @@ class Modele:
         m.eps = self.eps
         m.rope = self.rope
         m.dims = self.dims
-        m.couches_desc = C.addressof(self.desc_couches)
+        m.couches_desc = C.addressof(desc)
         m.enchassement, m.norme_sortie, m.sortie = (self.enchassement.data_ptr(), self.norme_sortie.data_ptr(),
                                                     self.sortie_w.data_ptr())
         n = int(lib.trc_modele_espace_octets(C.byref(m)))
-        self.espace = torch.zeros(n + 256, dtype=torch.uint8, device="cuda")
-        m.espace = self.espace.data_ptr() + (-self.espace.data_ptr()) % 256
+        espace = torch.zeros(n + 256, dtype=torch.uint8, device="cuda")
+        m.espace = espace.data_ptr() + (-espace.data_ptr()) % 256
         m.espace_octets = n
-        self.config = m
         lg, jt, ct = C.c_uint64(), C.c_uint64(), C.c_uint64()
         verifier(lib.trc_modele_sorties(C.byref(m), C.byref(lg), C.byref(jt), C.byref(ct)))
-        self._sorties = (lg.value, jt.value, ct.value)
+        return desc, m, espace, (lg.value, jt.value, ct.value)
 
     def choisir(self, actifs: str) -> None:
         """Run on the compressed ("compresse") or raw ("brut") parts; the KV caches are cleared."""
@@ -297,12 +305,40 @@ class Modele:
 
     def vues(self):
         """(logits f32[vocab], token u32[1], controle u32[4k]) as torch tensors on the workspace."""
+        return _vues(self.espace, self._sorties, self.vocab, self.k)
+
+
+def _vues(espace, sorties, vocab: int, k: int):
+    import torch
+
+    o0, o1, o2 = (a - espace.data_ptr() for a in sorties)
+    return (espace[o0:o0 + 4 * vocab].view(torch.float32), espace[o1:o1 + 4].view(torch.int32),
+            espace[o2:o2 + 16 * k].view(torch.int32))
+
+
+class Sequence:
+    """Another sequence over a Modele's weights and parts: its own KV caches and workspace, the
+    same step (trc_modele_pas and its phases) on its own descriptor. `monter` follows the model's
+    current choice of parts (call it after Modele.choisir); `effacer` clears the caches."""
+
+    def __init__(self, m: Modele):
         import torch
 
-        o0 = self._sorties[0] - self.espace.data_ptr()
-        o1 = self._sorties[1] - self.espace.data_ptr()
-        o2 = self._sorties[2] - self.espace.data_ptr()
-        lg = self.espace[o0:o0 + 4 * self.vocab].view(torch.float32)
-        jt = self.espace[o1:o1 + 4].view(torch.int32)
-        ct = self.espace[o2:o2 + 16 * self.k].view(torch.int32)
-        return lg, jt, ct
+        self.m = m
+        self.caches = [(torch.zeros_like(t["cache_k"]), torch.zeros_like(t["cache_v"])) for t in m.tenseurs]
+        self.monter()
+
+    def monter(self) -> None:
+        self.desc_couches, self.config, self.espace, self._sorties = self.m._config(self.caches)
+
+    def effacer(self) -> None:
+        for k, v in self.caches:
+            k.zero_()
+            v.zero_()
+
+    def pas(self, jeton: int, position: int, sortie: bool = True, flux=None) -> None:
+        verifier(lib.trc_modele_pas(C.byref(self.config), jeton, position, int(sortie),
+                                    (flux.cuda_stream if flux is not None else _flux())))
+
+    def vues(self):
+        return _vues(self.espace, self._sorties, self.m.vocab, self.m.k)

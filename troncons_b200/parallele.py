@@ -118,52 +118,57 @@ class CoucheEP:
 
 
 class ModeleEP:
-    """The expert-parallel decode step of a whole gpt-oss model: one process per GPU, one
-    sequence per rank (a batch of `monde` sequences), each rank holding its contiguous share of
+    """The expert-parallel decode step of a whole gpt-oss model: one process per GPU, `par_rang`
+    sequences per rank (a batch of monde x par_rang), each rank holding its contiguous share of
     every layer's experts (16 of 128 at 8 GPUs) and a replica of the dense weights.
 
     Per layer (the phases of trc_modele_pas, with the exchange between them): the attention side
-    of the rank's own token (trc_modele_attention: its KV cache stays on its GPU); an all-gather
-    of the MoE inputs h2 ([monde][d] f32, NCCL); the router on every token (replicated, identical
-    on every rank); the fused layer on the rank's share for every token; then the combine's
-    exchange. "nccl" (the default): each token's share written alone (partiel), a SUM
-    reduce-scatter, added into x. "pairs": the combine kernel writes each token's share into every
-    rank's symmetric buffer over NVLink peer stores and adds all ranks' shares in rank order into
-    [monde][d] rows, this rank's row holding its x (copied in before, out after); measured 3 %
-    slower on the whole model at 2 GPUs (the copies and the zeroing; the step waits on the busiest
-    rank's share either way). Then the rank's unembedding and greedy token.
+    of each of the rank's tokens (trc_modele_attention on its sequence: the KV caches stay on the
+    rank's GPU); an all-gather of the MoE inputs h2 ([monde x par_rang][d] f32, NCCL); the router
+    on every token (replicated, identical on every rank); the fused layer on the rank's share for
+    every token; then the combine's exchange. "nccl" (the default): each token's share written
+    alone (partiel), a SUM reduce-scatter, added into each sequence's x. "pairs": the combine
+    kernel writes each token's share into every rank's symmetric buffer over NVLink peer stores
+    and adds all ranks' shares in rank order into [tokens][d] rows, this rank's rows holding its
+    sequences' x (copied in before, out after); measured 3 % slower on the whole model at 2 GPUs
+    (the copies and the zeroing; the step waits on the busiest rank's share either way). Then each
+    sequence's unembedding and greedy token.
 
     The weighted experts' sum is the single-GPU combine's terms in another order (the shares
     summed across ranks), so the logits agree with the one-GPU model within f32 rounding, not
-    bit for bit; with one rank the step is trc_modele_pas's bits."""
+    bit for bit; with one rank and one sequence the step is trc_modele_pas's bits."""
 
-    def __init__(self, rang: int, monde: int, groupe=None, echange: str = "nccl", **modele):
+    def __init__(self, rang: int, monde: int, groupe=None, echange: str = "nccl", par_rang: int = 1, **modele):
         import torch
 
         from . import espace_recouvrant_octets
-        from .modele import Modele
+        from .modele import Modele, Sequence
 
-        self.rang, self.monde, self.groupe = rang, monde, groupe
+        self.rang, self.monde, self.groupe, self.b = rang, monde, groupe, par_rang
         if echange not in ("pairs", "nccl"):
             raise ValueError(f"exchange {echange!r}: 'pairs' or 'nccl'")
+        if not 1 <= par_rang or monde * par_rang > 128:
+            raise ValueError(f"{par_rang} sequences per rank on {monde} ranks: 1 to 128 tokens per step")
         self.echange = echange if monde > 1 else "aucun"
         self.tenus = partage(modele["experts"], rang, monde)
         dev = torch.device("cuda", torch.cuda.current_device())
         self.m = Modele(**modele, tenus=self.tenus, reduire=reduire_comptes(groupe, dev) if monde > 1 else None)
-        m = self.m
+        self.sequences = [self.m] + [Sequence(self.m) for _ in range(par_rang - 1)]
+        m, n_tok = self.m, monde * par_rang
         f32 = torch.float32
-        self.h2_tous = torch.empty(monde * m.d, dtype=f32, device=dev)
-        self.y_tous = torch.empty(monde * m.d, dtype=f32, device=dev)
-        self.y = torch.empty(m.d, dtype=f32, device=dev)
-        self.logits_routeur = torch.empty(monde * m.experts, dtype=f32, device=dev)
-        self.idx = torch.empty(monde * m.k, dtype=torch.int32, device=dev)
-        self.poids = torch.empty(monde * m.k, dtype=f32, device=dev)
-        self.controle = torch.zeros(monde * m.k * 4, dtype=torch.int32, device=dev)
-        n = espace_recouvrant_octets(m.dims, monde * m.k)
+        self.h2_locaux = torch.empty(par_rang * m.d, dtype=f32, device=dev)
+        self.h2_tous = torch.empty(n_tok * m.d, dtype=f32, device=dev)
+        self.y_tous = torch.empty(n_tok * m.d, dtype=f32, device=dev)
+        self.y = torch.empty(par_rang * m.d, dtype=f32, device=dev)
+        self.logits_routeur = torch.empty(n_tok * m.experts, dtype=f32, device=dev)
+        self.idx = torch.empty(n_tok * m.k, dtype=torch.int32, device=dev)
+        self.poids = torch.empty(n_tok * m.k, dtype=f32, device=dev)
+        self.controle = torch.zeros(n_tok * m.k * 4, dtype=torch.int32, device=dev)
+        n = espace_recouvrant_octets(m.dims, n_tok * m.k)
         self._espace = torch.empty(n + 256, dtype=torch.uint8, device=dev)
         self.espace_octets = n
         if self.echange == "pairs":
-            self.tampon, self.poignee, self.paires = monter_paires(m.dims, monde, rang, monde, groupe)
+            self.tampon, self.poignee, self.paires = monter_paires(m.dims, n_tok, rang, monde, groupe)
         self._monter()
 
     def _monter(self) -> None:
@@ -171,13 +176,18 @@ class ModeleEP:
 
         from . import MoeCouche, lib, verifier
 
-        m = self.m
-        x, h2 = C.c_uint64(), C.c_uint64()
-        verifier(lib.trc_modele_etat(C.byref(m.config), C.byref(x), C.byref(h2)))
-        base = m.espace.data_ptr()
-        self.x = m.espace[x.value - base:x.value - base + 4 * m.d].view(torch.float32)
-        self.h2 = m.espace[h2.value - base:h2.value - base + 4 * m.d].view(torch.float32)
-        entree = self.h2 if self.monde == 1 else self.h2_tous
+        m, d_ = self.m, self.m.d
+        self.x, self.h2 = [], []
+        for q in self.sequences:
+            x, h2 = C.c_uint64(), C.c_uint64()
+            verifier(lib.trc_modele_etat(C.byref(q.config), C.byref(x), C.byref(h2)))
+            base = q.espace.data_ptr()
+            self.x.append(q.espace[x.value - base:x.value - base + 4 * d_].view(torch.float32))
+            self.h2.append(q.espace[h2.value - base:h2.value - base + 4 * d_].view(torch.float32))
+        # the MoE's input: this rank's h2 itself (one rank, one sequence), its sequences' h2
+        # side by side (one rank), or every rank's (gathered)
+        self._entree = self.h2[0] if (self.monde, self.b) == (1, 1) else (
+            self.h2_locaux if self.monde == 1 else self.h2_tous)
         self.descs = []
         for l in range(m.couches):
             ta, tt = m._tables[l]
@@ -185,61 +195,81 @@ class ModeleEP:
             d.parties, d.parties_octets = ta.data_ptr(), tt.data_ptr()
             d.experts, d.k, d.luts, d.dims = m.experts, m.k, m.luts[l].data_ptr(), m.dims
             d.indices, d.poids = self.idx.data_ptr(), self.poids.data_ptr()
-            d.x, d.x_bf16, d.brut = entree.data_ptr(), 0, int(m.actifs == "brut")
+            d.x, d.x_bf16, d.brut = self._entree.data_ptr(), 0, int(m.actifs == "brut")
             d.residu, d.controle = self.y_tous.data_ptr(), self.controle.data_ptr()
             d.n_delta = d.n_codes = 0
-            d.jetons = self.monde
+            d.jetons = self.monde * self.b
             d.expert_debut, d.expert_fin = self.tenus
             if self.echange == "pairs":
                 d.partiel, d.echange = 0, C.addressof(self.paires)
             else:
                 d.partiel = 1
             self.descs.append(d)
-        self._entree = entree
-        self._ligne = self.y_tous.view(self.monde, m.d)[self.rang]
+        rangs = self.y_tous.view(self.monde * self.b, d_)
+        self._lignes = [rangs[self.rang * self.b + i] for i in range(self.b)]
 
     def choisir(self, actifs: str) -> None:
-        """Run on the compressed or raw parts; the KV caches are cleared."""
+        """Run on the compressed or raw parts; every sequence's KV caches are cleared."""
         self.m.choisir(actifs)
+        for q in self.sequences[1:]:
+            q.effacer()
+            q.monter()
         self._monter()
 
-    def pas(self, jeton: int, position: int, sortie: bool = True, flux=None) -> None:
-        """This rank's token `jeton` at `position`; every rank calls it once per step (the
-        collectives pair them up). Logits and greedy token in m.vues()."""
+    def vues(self, i: int = 0):
+        """(logits, greedy token, controle) of this rank's sequence i (see Modele.vues)."""
+        return self.sequences[i].vues()
+
+    def pas(self, jetons, position: int, sortie: bool = True, flux=None) -> None:
+        """This rank's tokens (an int, or one per sequence) at `position` (the same for all of the
+        rank's sequences); every rank calls it once per step (the collectives pair them up)."""
         import torch
         import torch.distributed as dist
 
         from . import lib, verifier
 
-        m, cfg = self.m, C.byref(self.m.config)
+        jetons = [int(jetons)] if np.isscalar(jetons) else [int(j) for j in jetons]
+        if len(jetons) != self.b:
+            raise ValueError(f"{len(jetons)} tokens for {self.b} sequences")
+        m, d_ = self.m, self.m.d
+        cfgs = [C.byref(q.config) for q in self.sequences]
         s = flux or torch.cuda.current_stream()
         f = s.cuda_stream
         e = self._espace.data_ptr()
         e += (-e) % 256
-        verifier(lib.trc_modele_debut(cfg, jeton, f))
+        for cfg, j in zip(cfgs, jetons):
+            verifier(lib.trc_modele_debut(cfg, j, f))
         with torch.cuda.stream(s):
             if self.echange == "pairs":
-                # the exchange adds every rank's shares into all N rows of y_tous; this rank's row
-                # carries its x through the layer, the other rows restart from 0 every step
+                # the exchange adds every rank's shares into all rows of y_tous; this rank's rows
+                # carry its sequences' x through the layer, the other rows restart from 0 every step
                 self.y_tous.zero_()
             for l in range(m.couches):
                 t = m.tenseurs[l]
-                verifier(lib.trc_modele_attention(cfg, l, position, f))
+                for i, cfg in enumerate(cfgs):
+                    verifier(lib.trc_modele_attention(cfg, l, position, f))
+                    if self._entree is not self.h2[0]:
+                        self.h2_locaux[i * d_:(i + 1) * d_].copy_(self.h2[i])
                 if self.monde > 1:
-                    dist.all_gather_into_tensor(self.h2_tous, self.h2, group=self.groupe)
+                    dist.all_gather_into_tensor(self.h2_tous, self.h2_locaux, group=self.groupe)
                 verifier(lib.trc_routeur(t["wr"].data_ptr(), t["br"].data_ptr(), self._entree.data_ptr(), 0, m.experts,
-                                         m.d, m.k, self.monde, self.logits_routeur.data_ptr(), self.idx.data_ptr(),
-                                         self.poids.data_ptr(), f))
+                                         d_, m.k, self.monde * self.b, self.logits_routeur.data_ptr(),
+                                         self.idx.data_ptr(), self.poids.data_ptr(), f))
                 if self.echange == "pairs":
-                    self._ligne.copy_(self.x)
+                    for i in range(self.b):
+                        self._lignes[i].copy_(self.x[i])
                     verifier(lib.trc_moe_couche_fusionnee(C.byref(self.descs[l]), e, self.espace_octets, f))
-                    self.x.copy_(self._ligne)
+                    for i in range(self.b):
+                        self.x[i].copy_(self._lignes[i])
+                    continue
+                verifier(lib.trc_moe_couche_fusionnee(C.byref(self.descs[l]), e, self.espace_octets, f))
+                if self.monde > 1:
+                    dist.reduce_scatter_tensor(self.y, self.y_tous, op=dist.ReduceOp.SUM, group=self.groupe)
+                    for i in range(self.b):
+                        self.x[i].add_(self.y[i * d_:(i + 1) * d_])
                 else:
-                    verifier(lib.trc_moe_couche_fusionnee(C.byref(self.descs[l]), e, self.espace_octets, f))
-                    if self.monde > 1:
-                        dist.reduce_scatter_tensor(self.y, self.y_tous, op=dist.ReduceOp.SUM, group=self.groupe)
-                        self.x.add_(self.y)
-                    else:
-                        self.x.add_(self.y_tous)
+                    for i in range(self.b):
+                        self.x[i].add_(self._lignes[i])
         if sortie:
-            verifier(lib.trc_modele_fin(cfg, f))
+            for cfg in cfgs:
+                verifier(lib.trc_modele_fin(cfg, f))
