@@ -458,6 +458,14 @@ int trc_modele_moe(const trc_modele_config* m, uint32_t couche, void* flux);
 int trc_modele_fin(const trc_modele_config* m, void* flux);
 int trc_modele_etat(const trc_modele_config* m, uint64_t* x, uint64_t* h2);
 
+/* trc_modele_attention for n sequences of one model at the same position (each its own KV caches
+ * and workspace, the same weights: checked), the q / k / v and output Q8_0 GEMVs launched once
+ * for the n tokens (each weight row read once); every sequence gets trc_modele_attention's bits.
+ * `espace`: trc_modele_lot_espace_octets(m, n) bytes, 256-aligned. */
+uint64_t trc_modele_lot_espace_octets(const trc_modele_config* m, uint32_t n);
+int trc_modele_attention_lot(const trc_modele_config* const* sequences, uint32_t n, uint32_t couche, uint32_t position,
+                             void* espace, size_t espace_octets, void* flux);
+
 /* Seeded synthetic tensors on the GPU (inputs of tests and benches; no counterpart): R x C
  * MXFP4 as 17-byte blocks + f32 biases (row sigma 0.02 LogNormal(0, 0.3), E8M0 floor(log2 max)
  * - 2, E2M1 to nearest, biases N(0, 0.01) rounded to bf16); R x C Q8_0 of N(0, 0.02); n f32

@@ -58,25 +58,27 @@ def test_un_rang_egale_le_pas():
             assert np.array_equal(za.view(np.int32), zb.view(np.int32)) and ja == jb, f"{actifs} step {t}"
 
 
-def test_un_rang_plusieurs_sequences():
-    """Three sequences on one rank (the router and the fused layer called for the 3 tokens):
+@pytest.mark.parametrize("b", [3, 9])
+def test_un_rang_plusieurs_sequences(b):
+    """b sequences on one rank (their attention sides batched: trc_modele_attention_lot, the Q8_0
+    GEMVs by launches of up to 8 tokens; the router and the fused layer called for the b tokens):
     each sequence's logits are those of the model run on that sequence alone, bit for bit."""
     import troncons_b200.modele as M
     from troncons_b200.parallele import ModeleEP
 
-    ep = ModeleEP(0, 1, par_rang=3, **FORME)
+    ep = ModeleEP(0, 1, par_rang=b, **FORME)
     m = M.Modele(**FORME)
-    jetons = np.random.default_rng(8).integers(0, 512, (3, 20))
+    jetons = np.random.default_rng(8).integers(0, 512, (b, 20))
     ep.choisir("compresse")
-    vues = [ep.vues(i) for i in range(3)]
-    z = [[] for _ in range(3)]
+    vues = [ep.vues(i) for i in range(b)]
+    z = [[] for _ in range(b)]
     for t in range(20):
         ep.pas(jetons[:, t], t)
         torch.cuda.synchronize()
-        for i in range(3):
+        for i in range(b):
             z[i].append(vues[i][0].cpu().numpy().copy())
     assert (ep.controle == 0).all()
-    for i in range(3):
+    for i in range(b):
         m.choisir("compresse")
         b = _suite(m.pas, m.vues, jetons[i])
         for t in range(20):

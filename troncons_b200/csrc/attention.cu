@@ -54,14 +54,18 @@ __device__ __forceinline__ void q8_charger_ligne(uint8_t* ligne, const uint8_t* 
     }
 }
 
+// J tokens at once (x [J][C], y [J][R]): each row is staged once and multiplied by the J vectors,
+// each token's sums in the single-token order (the same bits as J separate launches).
+template <int J>
 __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __restrict__ W, const float* __restrict__ x,
                                                            const float* __restrict__ biais, float* __restrict__ y,
                                                            uint32_t R, uint32_t C) {
     extern __shared__ __align__(16) uint8_t dyn[];
     const uint32_t voie = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t B = C / 32u, octets = B * Q8_BLOC, tampon = q8_tampon(C);
-    float* xs = reinterpret_cast<float*>(dyn);                     // [C + C / 32]
-    uint8_t* lignes = dyn + q8_x_octets(C) + warp * 2u * tampon;  // two row buffers per warp
+    const uint32_t xp = q8_x_octets(C) / 4u;                            // floats per staged token
+    float* xs = reinterpret_cast<float*>(dyn);                          // [J][C + C / 32 (+ pad)]
+    uint8_t* lignes = dyn + J * q8_x_octets(C) + warp * 2u * tampon;  // two row buffers per warp
     const uint64_t fin_mat = uint64_t(R) * octets;
     const uint32_t pas = gridDim.x * Q8_WARPS;
     uint32_t r = blockIdx.x * Q8_WARPS + warp;
@@ -72,9 +76,10 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __re
     liberer_aval();
     // x padded by one word per 32 (xs[c + c / 32]): lane l reads x[32 b + i] for b = l, l + 32,
     // ..., so unpadded all 32 lanes would hit one shared-memory bank.
-    for (uint32_t t = threadIdx.x; t < C / 4u; t += blockDim.x) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + t);
-        const uint32_t c = 4u * t, o = c + c / 32u;
+    for (uint32_t t = threadIdx.x; t < J * (C / 4u); t += blockDim.x) {
+        const uint32_t jt = t / (C / 4u), tt = t - jt * (C / 4u);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x + uint64_t(jt) * C) + tt);
+        const uint32_t c = 4u * tt, o = jt * xp + c + c / 32u;
         xs[o] = v.x;
         xs[o + 1] = v.y;
         xs[o + 2] = v.z;
@@ -91,23 +96,35 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __re
         const uint8_t* ligne = lignes + (n & 1u) * tampon;
         const uint64_t debut = uint64_t(r) * octets;
         const uint32_t dec = uint32_t(debut - (debut & ~uint64_t(15)));
-        float acc = 0.0f;
+        float acc[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[j] = 0.0f;
         for (uint32_t b = voie; b < B; b += 32u) {
             const uint16_t* blk = reinterpret_cast<const uint16_t*>(ligne + dec + b * Q8_BLOC);
             const float d = f16_f32(blk[0]);
             const float* xv = xs + 33u * b;
-            float s = 0.0f;
+            float s[J];
+#pragma unroll
+            for (int j = 0; j < J; ++j) s[j] = 0.0f;
 #pragma unroll
             for (int t = 0; t < 16; ++t) {
                 const uint32_t w = blk[1 + t];
-                s = fmaf(float(int8_t(w & 0xFFu)), xv[2 * t], s);
-                s = fmaf(float(int8_t(w >> 8)), xv[2 * t + 1], s);
+                const float q0 = float(int8_t(w & 0xFFu)), q1 = float(int8_t(w >> 8));
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    s[j] = fmaf(q0, xv[j * xp + 2 * t], s[j]);
+                    s[j] = fmaf(q1, xv[j * xp + 2 * t + 1], s[j]);
+                }
             }
-            acc = fmaf(d, s, acc);
+#pragma unroll
+            for (int j = 0; j < J; ++j) acc[j] = fmaf(d, s[j], acc[j]);
         }
 #pragma unroll
-        for (int dd = 16; dd > 0; dd >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, dd);
-        if (voie == 0) y[r] = biais != nullptr ? acc + biais[r] : acc;
+        for (int j = 0; j < J; ++j) {
+#pragma unroll
+            for (int dd = 16; dd > 0; dd >>= 1) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], dd);
+            if (voie == 0) y[uint64_t(j) * R + r] = biais != nullptr ? acc[j] + biais[r] : acc[j];
+        }
         __syncwarp();  // this buffer is refilled two rows from now
     }
     cp_async_wait<0>();
@@ -296,17 +313,46 @@ __global__ void __launch_bounds__(ATT_FILS) k_attention(const float* __restrict_
 
 // ------------------------------------------------------------------ launchers
 
-cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
-                             cudaStream_t flux) {
-    const size_t smem = q8_x_octets(C) + Q8_WARPS * 2u * q8_tampon(C);
-    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_q8_0), int(smem));
+template <int J>
+static cudaError_t lancer_q8_0_j(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                                 cudaStream_t flux) {
+    const size_t smem = J * q8_x_octets(C) + Q8_WARPS * 2u * q8_tampon(C);
+    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_q8_0<J>), int(smem));
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint32_t par_sm = std::max<uint32_t>(1u, std::min<uint32_t>(4u, uint32_t(200000 / smem)));
     const uint32_t blocs = std::min<uint32_t>((R + Q8_WARPS - 1) / Q8_WARPS, uint32_t(sms) * par_sm);
-    return lancer_pdl(k_gemv_q8_0, dim3(blocs), dim3(Q8_WARPS * 32), smem, flux, static_cast<const uint8_t*>(w), x, biais,
-                      y, R, C);
+    return lancer_pdl(k_gemv_q8_0<J>, dim3(blocs), dim3(Q8_WARPS * 32), smem, flux, static_cast<const uint8_t*>(w), x,
+                      biais, y, R, C);
+}
+
+cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                             cudaStream_t flux) {
+    return lancer_q8_0_j<1>(w, x, biais, y, R, C, flux);
+}
+
+// n tokens (x [n][C], y [n][R]) by launches of up to Q8_LOT_MAX tokens.
+cudaError_t lancer_gemv_q8_0_lot(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                                 uint32_t n, cudaStream_t flux) {
+    for (uint32_t j0 = 0; j0 < n; j0 += Q8_LOT_MAX) {
+        const uint32_t m = std::min(Q8_LOT_MAX, n - j0);
+        const float* xj = x + uint64_t(j0) * C;
+        float* yj = y + uint64_t(j0) * R;
+        cudaError_t e;
+        switch (m) {
+            case 1: e = lancer_q8_0_j<1>(w, xj, biais, yj, R, C, flux); break;
+            case 2: e = lancer_q8_0_j<2>(w, xj, biais, yj, R, C, flux); break;
+            case 3: e = lancer_q8_0_j<3>(w, xj, biais, yj, R, C, flux); break;
+            case 4: e = lancer_q8_0_j<4>(w, xj, biais, yj, R, C, flux); break;
+            case 5: e = lancer_q8_0_j<5>(w, xj, biais, yj, R, C, flux); break;
+            case 6: e = lancer_q8_0_j<6>(w, xj, biais, yj, R, C, flux); break;
+            case 7: e = lancer_q8_0_j<7>(w, xj, biais, yj, R, C, flux); break;
+            default: e = lancer_q8_0_j<8>(w, xj, biais, yj, R, C, flux); break;
+        }
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t lancer_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t lignes, float eps,

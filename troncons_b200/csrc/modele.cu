@@ -365,6 +365,77 @@ cudaError_t etape_sortie(const trc_modele_config& m, const DispositionModele& d,
     return tb::lancer_argmax(F(d.z), m.vocab, reinterpret_cast<uint32_t*>(esp + d.jeton), f);
 }
 
+// The batch workspace of n sequences' attention sides: f32 rows [n][d] / [n][dq] / [n][dkv].
+struct DispositionLot {
+    uint64_t h, q, k, v, a, o, total;
+};
+
+DispositionLot disposition_lot(const trc_modele_config& m, uint32_t n) {
+    DispositionLot d{};
+    const uint64_t dq = uint64_t(m.tetes) * m.dim_tete, dkv = uint64_t(m.tetes_kv) * m.dim_tete;
+    uint64_t p = 0;
+    auto zone = [&](uint64_t& z, uint64_t octets) {
+        z = p;
+        p = tb::al256(p + octets);
+    };
+    zone(d.h, 4ull * n * m.d);
+    zone(d.q, 4ull * n * dq);
+    zone(d.k, 4ull * n * dkv);
+    zone(d.v, 4ull * n * dkv);
+    zone(d.a, 4ull * n * dq);
+    zone(d.o, 4ull * n * m.d);
+    d.total = p;
+    return d;
+}
+
+// Layer l's attention side for n sequences at the same position: what etape_attention does for
+// each, with the four Q8_0 GEMVs once for all n tokens (each row of weights read once; every
+// token's sums in the single-token order, so each sequence gets etape_attention's bits).
+cudaError_t etape_attention_lot(const trc_modele_config* const* seqs, uint32_t n, uint32_t l, uint32_t position,
+                                uint8_t* lot, cudaStream_t f) {
+    const trc_modele_config& m = *seqs[0];
+    const DispositionLot b = disposition_lot(m, n);
+    auto L = [&](uint64_t o) { return reinterpret_cast<float*>(lot + o); };
+    auto P = [](uint64_t a) { return reinterpret_cast<const float*>(a); };
+    auto X = [&](uint32_t i, uint64_t DispositionModele::*z) {
+        return reinterpret_cast<float*>(seqs[i]->espace + disposition_modele(*seqs[i]).*z);
+    };
+    const uint32_t D = m.d, dq = m.tetes * m.dim_tete, dkv = m.tetes_kv * m.dim_tete;
+    const trc_modele_couche& c0 = reinterpret_cast<const trc_modele_couche*>(m.couches_desc)[l];
+    tb::ParamsRope rope;
+    std::memcpy(&rope, &m.rope, sizeof rope);
+    for (uint32_t i = 0; i < n; ++i)
+        ESSAI(tb::lancer_rmsnorm(X(i, &DispositionModele::x), P(c0.attn_norm), L(b.h) + uint64_t(i) * D, D, 1, m.eps, f));
+    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wq), L(b.h), P(c0.bq), L(b.q), dq, D, n, f));
+    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wk), L(b.h), P(c0.bk), L(b.k), dkv, D, n, f));
+    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wv), L(b.h), P(c0.bv), L(b.v), dkv, D, n, f));
+    for (uint32_t i = 0; i < n; ++i) {
+        const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(seqs[i]->couches_desc)[l];
+        float* q = L(b.q) + uint64_t(i) * dq;
+        float* k = L(b.k) + uint64_t(i) * dkv;
+        ESSAI(tb::lancer_rope_yarn(q, k, m.tetes, m.tetes_kv, position, rope, f));
+        const uint32_t case_kv = c.anneau ? position % c.anneau : position;
+        ESSAI(tb::lancer_ecrire_kv(k, L(b.v) + uint64_t(i) * dkv, reinterpret_cast<uint16_t*>(c.cache_k),
+                                   reinterpret_cast<uint16_t*>(c.cache_v), dkv, case_kv, f));
+        tb::ParamsAttention pa{};
+        pa.tetes = m.tetes;
+        pa.tetes_kv = m.tetes_kv;
+        pa.dim_tete = m.dim_tete;
+        pa.fin = position + 1;
+        pa.debut = c.anneau && pa.fin > c.anneau ? pa.fin - c.anneau : 0;
+        pa.anneau = c.anneau;
+        pa.echelle = 1.0f / std::sqrt(float(m.dim_tete));
+        ESSAI(tb::lancer_attention(q, reinterpret_cast<const uint16_t*>(c.cache_k), reinterpret_cast<const uint16_t*>(c.cache_v),
+                                   P(c.puits), L(b.a) + uint64_t(i) * dq, pa, f));
+    }
+    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wo), L(b.a), P(c0.bo), L(b.o), D, dq, n, f));
+    for (uint32_t i = 0; i < n; ++i) {
+        ESSAI(tb::lancer_combiner(X(i, &DispositionModele::x), L(b.o) + uint64_t(i) * D, D, nullptr, 1, D, f));
+        ESSAI(tb::lancer_rmsnorm(X(i, &DispositionModele::x), P(c0.post_norm), X(i, &DispositionModele::h2), D, 1, m.eps, f));
+    }
+    return cudaSuccess;
+}
+
 #undef ESSAI
 
 }  // namespace
@@ -479,6 +550,39 @@ int trc_modele_attention(const trc_modele_config* m, uint32_t couche, uint32_t p
     if (couche >= m->couches || position >= m->contexte) return tb::erreur_usage("model: layer or position out of range");
     if (cudaError_t e = etape_attention(*m, d, reinterpret_cast<uint8_t*>(m->espace), couche, position,
                                         static_cast<cudaStream_t>(flux)))
+        return tb::erreur_cuda(e);
+    return TRC_OK;
+}
+
+uint64_t trc_modele_lot_espace_octets(const trc_modele_config* m, uint32_t n) {
+    if (m == nullptr || n == 0) return 0;
+    return disposition_lot(*m, n).total;
+}
+
+int trc_modele_attention_lot(const trc_modele_config* const* sequences, uint32_t n, uint32_t couche, uint32_t position,
+                             void* espace, size_t espace_octets, void* flux) {
+    if (sequences == nullptr || n == 0 || espace == nullptr) return tb::erreur_usage("model batch: sequences or workspace missing");
+    DispositionModele d;
+    for (uint32_t i = 0; i < n; ++i)
+        if (int r = verifier_modele(sequences[i], d, flux)) return r;
+    const trc_modele_config& m = *sequences[0];
+    if (couche >= m.couches || position >= m.contexte) return tb::erreur_usage("model batch: layer or position out of range");
+    if (espace_octets < disposition_lot(m, n).total || reinterpret_cast<uintptr_t>(espace) % 256 != 0)
+        return tb::erreur_usage("model batch: workspace too small or misaligned");
+    // one model: the same shapes and the same layer weights (each its own caches and workspace)
+    const trc_modele_couche& c0 = reinterpret_cast<const trc_modele_couche*>(m.couches_desc)[couche];
+    for (uint32_t i = 1; i < n; ++i) {
+        const trc_modele_config& s = *sequences[i];
+        const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(s.couches_desc)[couche];
+        if (s.d != m.d || s.tetes != m.tetes || s.tetes_kv != m.tetes_kv || s.couches != m.couches ||
+            std::memcmp(&s.rope, &m.rope, sizeof m.rope) != 0 || s.eps != m.eps || c.wq != c0.wq || c.wk != c0.wk ||
+            c.wv != c0.wv || c.wo != c0.wo || c.bq != c0.bq || c.bk != c0.bk || c.bv != c0.bv || c.bo != c0.bo ||
+            c.attn_norm != c0.attn_norm || c.post_norm != c0.post_norm || c.puits != c0.puits || c.anneau != c0.anneau)
+            return tb::erreur_usage("model batch: the sequences are not of one model");
+        if (c.cache_k == c0.cache_k || s.espace == m.espace) return tb::erreur_usage("model batch: two sequences share a cache or workspace");
+    }
+    if (cudaError_t e = etape_attention_lot(sequences, n, couche, position, static_cast<uint8_t*>(espace),
+                                            static_cast<cudaStream_t>(flux)))
         return tb::erreur_cuda(e);
     return TRC_OK;
 }

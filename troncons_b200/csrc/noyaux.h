@@ -121,6 +121,9 @@ struct ParamsAttention {
     float echelle;
     uint32_t reserve;
 };
+constexpr uint32_t Q8_LOT_MAX = 8;  // tokens per launch of the batched Q8_0 GEMV
+cudaError_t lancer_gemv_q8_0_lot(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
+                                 uint32_t n, cudaStream_t flux);
 cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, float* y, uint32_t R, uint32_t C,
                              cudaStream_t flux);
 cudaError_t lancer_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t lignes, float eps,

@@ -39,6 +39,8 @@ for _n, (_r, _a) in {
     "trc_modele_moe": (_i32, [_vp, _u32, _vp]),
     "trc_modele_fin": (_i32, [_vp, _vp]),
     "trc_modele_etat": (_i32, [_vp, _vp, _vp]),
+    "trc_modele_lot_espace_octets": (_u64, [_vp, _u32]),
+    "trc_modele_attention_lot": (_i32, [_vp, _u32, _u32, _u32, _vp, _sz, _vp]),
     "trc_synth_mxfp4_gpu": (_i32, [_vp, _vp, _u32, _u32, _u64, _u64, _vp]),
     "trc_synth_q8_0_gpu": (_i32, [_vp, _u32, _u32, _u64, _u64, _vp]),
     "trc_synth_f32_gpu": (_i32, [_vp, _u64, _u64, _u64, C.c_float, C.c_float, _vp]),

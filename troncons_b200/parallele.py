@@ -123,8 +123,8 @@ class ModeleEP:
     every layer's experts (16 of 128 at 8 GPUs) and a replica of the dense weights.
 
     Per layer (the phases of trc_modele_pas, with the exchange between them): the attention side
-    of each of the rank's tokens (trc_modele_attention on its sequence: the KV caches stay on the
-    rank's GPU); an all-gather of the MoE inputs h2 ([monde x par_rang][d] f32, NCCL); the router
+    of the rank's tokens (trc_modele_attention, or trc_modele_attention_lot for several sequences:
+    their Q8_0 GEMVs launched once for all of them; the KV caches stay on the rank's GPU); an all-gather of the MoE inputs h2 ([monde x par_rang][d] f32, NCCL); the router
     on every token (replicated, identical on every rank); the fused layer on the rank's share for
     every token; then the combine's exchange. "nccl" (the default): each token's share written
     alone (partiel), a SUM reduce-scatter, added into each sequence's x. "pairs": the combine
@@ -169,6 +169,12 @@ class ModeleEP:
         self.espace_octets = n
         if self.echange == "pairs":
             self.tampon, self.poignee, self.paires = monter_paires(m.dims, n_tok, rang, monde, groupe)
+        if par_rang > 1:
+            from .modele import lib as _lib
+
+            n_lot = int(_lib.trc_modele_lot_espace_octets(C.byref(m.config), par_rang))
+            self._lot = torch.empty(n_lot + 256, dtype=torch.uint8, device=dev)
+            self._lot_octets = n_lot
         self._monter()
 
     def _monter(self) -> None:
@@ -207,6 +213,7 @@ class ModeleEP:
             self.descs.append(d)
         rangs = self.y_tous.view(self.monde * self.b, d_)
         self._lignes = [rangs[self.rang * self.b + i] for i in range(self.b)]
+        self._configs = (C.c_void_p * self.b)(*[C.addressof(q.config) for q in self.sequences])
 
     def choisir(self, actifs: str) -> None:
         """Run on the compressed or raw parts; every sequence's KV caches are cleared."""
@@ -244,11 +251,18 @@ class ModeleEP:
                 # the exchange adds every rank's shares into all rows of y_tous; this rank's rows
                 # carry its sequences' x through the layer, the other rows restart from 0 every step
                 self.y_tous.zero_()
+            lot = 0
+            if self.b > 1:
+                lot = self._lot.data_ptr()
+                lot += (-lot) % 256
             for l in range(m.couches):
                 t = m.tenseurs[l]
-                for i, cfg in enumerate(cfgs):
-                    verifier(lib.trc_modele_attention(cfg, l, position, f))
-                    if self._entree is not self.h2[0]:
+                if self.b > 1:  # the sequences' attention sides together (weights read once)
+                    verifier(lib.trc_modele_attention_lot(self._configs, self.b, l, position, lot, self._lot_octets, f))
+                else:
+                    verifier(lib.trc_modele_attention(cfgs[0], l, position, f))
+                if self._entree is not self.h2[0]:
+                    for i in range(self.b):
                         self.h2_locaux[i * d_:(i + 1) * d_].copy_(self.h2[i])
                 if self.monde > 1:
                     dist.all_gather_into_tensor(self.h2_tous, self.h2_locaux, group=self.groupe)
