@@ -70,6 +70,12 @@ def arguments():
     a.add_argument("--par-rang", type=int, default=1,
                    help="sequences per GPU in the expert-parallel whole-model measurement (batch = GPUs x this); "
                         "with --modele on one GPU, a batch of this many sequences")
+    a.add_argument("--sans-couche", action="store_true",
+                   help="N > 1: measure the expert-parallel whole model only (its own line)")
+    a.add_argument("--zipf", type=float, default=0.0,
+                   help="whole model: Zipf(s)-shaped expert popularity from a seeded router bias (0: uniform)")
+    a.add_argument("--placement", choices=["aleatoire", "equilibre"], default="aleatoire",
+                   help="with --zipf: the popular experts numbered at random, or interleaved over the GPUs' shares")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
                    help="N > 1: the combine's exchange in the combine kernel over NVLink (pairs) or by NCCL")
     return a.parse_args()
@@ -400,6 +406,13 @@ def bras_ep(args):
     torch.cuda.set_device(lr)
     dev = torch.device("cuda", lr)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.sans_couche:  # the expert-parallel whole model alone, its own line
+        modele = mesurer_modele_ep(args, args.steps, args.warmup)
+        dist.barrier()
+        dist.destroy_process_group()
+        if r == 0:
+            print(json.dumps(modele), flush=True)
+        return
     jetons = w
     t0 = time.time()
     c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=False, n_delta=args.n_delta,
@@ -550,14 +563,15 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
     import torch
     import torch.distributed as dist
 
-    from troncons_b200.parallele import ModeleEP
+    from troncons_b200.parallele import ModeleEP, partage
 
     r, w, _ = rang()
     b = args.par_rang
     t0 = time.time()
     ep = ModeleEP(r, w, echange="nccl", par_rang=b, couches=args.couches, d=2880, tetes=64, tetes_kv=8,
-                  experts=args.experts, k=args.k, vocab=201088, contexte=args.contexte + warmup + steps + 1, ffn=2880,
-                  fenetre=128, graine=args.graine, compresse=True, brut=False)
+                  experts=args.experts, k=args.k, vocab=201088, contexte=args.contexte + warmup + steps + 2, ffn=2880,
+                  fenetre=128, graine=args.graine, compresse=True, brut=False, zipf=args.zipf,
+                  placement=args.placement)
     torch.cuda.synchronize()
     t_gen = time.time() - t0
     # each sequence its own seeded context
@@ -599,12 +613,23 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
     ms = float(t[0]) / steps
     if not int(ok[0]):
         raise RuntimeError("integrity counters set during the expert-parallel model steps")
+    # one more step, untimed, with every layer's routing kept: the activations each GPU's share
+    # holds, per layer (the busiest GPU's count against the mean)
+    journal = []
+    ep.pas(j, pos, journal=journal)
+    torch.cuda.synchronize()
+    parts = np.array([np.bincount(np.array([partage(args.experts, q, w)[0] for q in range(w)]).searchsorted(
+        x.cpu().numpy(), side="right") - 1, minlength=w) for x in journal])
+    charge = {"activations_per_layer": int(parts.sum(1)[0]), "busiest_gpu_mean": round(float(parts.max(1).mean()), 2),
+              "mean_per_gpu": round(float(parts.sum(1)[0]) / w, 2)}
     debut, fin = ep.tenus
     del ep
     torch.cuda.empty_cache()
     return {"metric": f"gpt-oss-120b decode tokens/s (whole step, expert-parallel over {w} GPUs, batch {w * b})",
             "value": round(w * b * 1000.0 / ms, 2), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": steps,
             "warmup": warmup, "batch": w * b, "sequences_per_gpu": b, "experts_per_gpu": fin - debut, "n_gpus": w,
+            "popularity": ({"zipf": args.zipf, "placement": args.placement} if args.zipf > 0 else "uniform"),
+            "load": charge,
             "workload": f"config 3: {args.couches} layers, {args.experts} experts top-{args.k} ({fin - debut} per GPU), "
                         f"{b} sequence(s) per GPU, context {args.contexte} seeded tokens, attention on each sequence's "
                         "GPU, MoE inputs all-gathered and the shares' sums reduce-scattered over NCCL per layer",

@@ -63,6 +63,24 @@ def _flux():
     return torch.cuda.current_stream().cuda_stream
 
 
+def biais_zipf(experts: int, s: float, placement: str, rangs: int, graine: int, couche: int) -> np.ndarray:
+    """The router bias (f32[experts]) that gives layer `couche` Zipf(s)-shaped expert popularity:
+    -s ln(1 + q) for the expert of popularity rank q (0 the most popular), experts numbered by
+    `placement` (see Modele)."""
+    q = np.arange(experts)
+    if placement == "aleatoire":
+        expert = np.random.default_rng([graine, couche, 0x5A1F]).permutation(experts)
+    elif placement == "equilibre":
+        if experts % rangs:
+            raise ValueError(f"{experts} experts over {rangs} ranks")
+        expert = (q % rangs) * (experts // rangs) + q // rangs
+    else:
+        raise ValueError(f"placement {placement!r}: 'aleatoire' or 'equilibre'")
+    b = np.zeros(experts, np.float32)
+    b[expert] = (-s * np.log1p(q)).astype(np.float32)
+    return b
+
+
 def synth_q8_0(R: int, C_: int, graine: int, matrice: int):
     import torch
 
@@ -116,12 +134,20 @@ class Modele:
     def __init__(self, couches: int, d: int, tetes: int, tetes_kv: int, experts: int, k: int, vocab: int,
                  contexte: int, ffn: int, fenetre: int = 128, graine: int = 1, compresse: bool = True,
                  brut: bool = False, lot: int = 32, eps: float = 1e-5, rope: ParamsRope | None = None,
-                 tenus: tuple | None = None, reduire=None):
+                 tenus: tuple | None = None, reduire=None, zipf: float = 0.0, placement: str = "aleatoire",
+                 rangs: int = 1):
         """`tenus` = (debut, fin): draw and encode only the experts [debut, fin) of every layer (an
         expert-parallel share; the others' parts are absent), their rANS tables built from the
         counts of all experts when `reduire` sums the share's counts over the ranks (an
         all-reduce: parallele.reduire_comptes), so every share's parts are byte for byte those of
-        the whole model."""
+        the whole model.
+
+        `zipf` = s > 0 skews the experts' popularity: every layer's router bias gets
+        -s ln(1 + rank), rank the expert's place in a popularity order, so that top-k routing
+        picks experts with Zipf(s)-shaped frequencies. `placement` numbers the experts in that
+        order: "aleatoire" (a seeded permutation per layer) or "equilibre" (popularity rank q goes
+        to expert (q mod rangs) (E / rangs) + q div rangs: each of `rangs` contiguous shares holds
+        every rangs-th most popular expert, a balanced load for expert parallelism)."""
         import torch
 
         import troncons_b200.synth as S
@@ -148,6 +174,8 @@ class Modele:
                 "wr": synth_f32(experts * d, g, ident("wr", l), 0.0, 0.02),
                 "br": synth_f32(experts, g, ident("br", l), 0.0, 0.01),
             }
+            if zipf > 0:
+                t["br"] += torch.from_numpy(biais_zipf(experts, zipf, placement, rangs, graine, l)).cuda()
             cases = fenetre if (l % 2 == 0 and fenetre) else contexte
             t["anneau"] = fenetre if (l % 2 == 0 and fenetre) else 0
             t["cache_k"] = torch.zeros(cases * dkv, dtype=torch.int16, device="cuda")

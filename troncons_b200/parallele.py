@@ -151,6 +151,7 @@ class ModeleEP:
             raise ValueError(f"{par_rang} sequences per rank on {monde} ranks: 1 to 128 tokens per step")
         self.echange = echange if monde > 1 else "aucun"
         self.tenus = partage(modele["experts"], rang, monde)
+        modele.setdefault("rangs", monde)  # the balanced placement of a skewed popularity
         dev = torch.device("cuda", torch.cuda.current_device())
         self.m = Modele(**modele, tenus=self.tenus, reduire=reduire_comptes(groupe, dev) if monde > 1 else None)
         self.sequences = [self.m] + [Sequence(self.m) for _ in range(par_rang - 1)]
@@ -227,9 +228,10 @@ class ModeleEP:
         """(logits, greedy token, controle) of this rank's sequence i (see Modele.vues)."""
         return self.sequences[i].vues()
 
-    def pas(self, jetons, position: int, sortie: bool = True, flux=None) -> None:
+    def pas(self, jetons, position: int, sortie: bool = True, flux=None, journal: list | None = None) -> None:
         """This rank's tokens (an int, or one per sequence) at `position` (the same for all of the
-        rank's sequences); every rank calls it once per step (the collectives pair them up)."""
+        rank's sequences); every rank calls it once per step (the collectives pair them up).
+        `journal`: a list that receives a device copy of every layer's routed experts."""
         import torch
         import torch.distributed as dist
 
@@ -269,6 +271,8 @@ class ModeleEP:
                 verifier(lib.trc_routeur(t["wr"].data_ptr(), t["br"].data_ptr(), self._entree.data_ptr(), 0, m.experts,
                                          d_, m.k, self.monde * self.b, self.logits_routeur.data_ptr(),
                                          self.idx.data_ptr(), self.poids.data_ptr(), f))
+                if journal is not None:
+                    journal.append(self.idx.clone())
                 if self.echange == "pairs":
                     for i in range(self.b):
                         self._lignes[i].copy_(self.x[i])
