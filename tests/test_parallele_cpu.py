@@ -118,3 +118,29 @@ def test_deux_rangs_gloo():
     port = _port_libre()
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     mp.start_processes(_travail, args=(2, port), nprocs=2, join=True, start_method="spawn")
+
+
+@pytest.mark.parametrize("placement", ["aleatoire", "equilibre"])
+def test_popularite_zipf(placement):
+    """The router bias of a Zipf(s)-skewed synthetic model: -s ln(1 + q) for popularity rank q,
+    every rank used once; "equilibre" puts the monde most popular experts on monde different
+    shares, share r holding exactly the ranks q = r mod monde; "aleatoire" a seeded
+    permutation, different per layer."""
+    from troncons_b200.modele import biais_zipf
+
+    E, monde, s = 128, 8, 1.1
+    b = biais_zipf(E, s, placement, monde, 7, 3)
+    assert b.dtype == np.float32 and b.shape == (E,)
+    assert np.allclose(np.sort(b)[::-1], -s * np.log1p(np.arange(E)), rtol=0, atol=1e-6)
+    ordre = np.argsort(-b, kind="stable")
+    parts = [partage(E, r, monde) for r in range(monde)]
+    rang_de = lambda e: next(r for r, (d, f) in enumerate(parts) if d <= e < f)  # noqa: E731
+    if placement == "equilibre":
+        assert sorted(rang_de(int(e)) for e in ordre[:monde]) == list(range(monde))
+        for r, (d, f) in enumerate(parts):
+            q = sorted(int(np.where(ordre == e)[0][0]) for e in range(d, f))
+            assert all(x % monde == r for x in q)
+    else:
+        assert not np.array_equal(b, biais_zipf(E, s, placement, monde, 7, 4))
+    with pytest.raises(ValueError):
+        biais_zipf(E, s, "autre", monde, 7, 3)
