@@ -358,6 +358,53 @@ struct Decodeur {
         return m;
     }
 
+    // ---- look-ahead form, for streams whose lanes all read one table (DELTA) ----
+    // The sub-step above waits for the LUT entry of the new state before the next one starts.
+    // Here every lane carries, besides the LUT entry `e` of its state, the ring word at
+    // (pointer + lane) and that word's LUT entry: a lane that renormalises takes both from the
+    // lane of its rank (two shuffles), a lane that does not has the entry of y in flight since y
+    // was known, so the table lookup overlaps the ballot and shuffle instead of following them.
+    // The words are those of pas(), in the same order: the same states, bytes and pointer.
+    // The ring word of a macro-step's first sub-step is read at the end of the previous one,
+    // before avancer(): at most 128 + 31 words past that macro-step's start, so inside the
+    // chunk after the pointer's, which avancer() keeps landed; the chunk avancer() refills is
+    // behind the pointer.
+    struct Avance {
+        uint32_t e, wp, lp;
+    };
+
+    // After debut(): the first sub-step's entries.
+    __device__ __forceinline__ void debut_avance(uint32_t lut_s, Avance& s) {
+        s.e = lds32(lut_s + 4u * (x & (M - 1u)));
+        s.wp = lds16(anneau_s + 2u * ((pa & (ANNEAU_MOTS - 1u)) + voie));
+        s.lp = lds32(lut_s + 4u * (s.wp & (M - 1u)));
+    }
+
+    __device__ __forceinline__ uint32_t pas_avance(uint32_t lut_s, Avance& s) {
+        const uint32_t e = s.e;
+        const uint32_t y = (((e >> 8) & 0xFFFu) + 1u) * (x >> 12) + (e >> 20);
+        const uint32_t ey = lds32(lut_s + 4u * (y & (M - 1u)));
+        const bool besoin = y < L;
+        const uint32_t vote = __ballot_sync(0xFFFFFFFFu, besoin);
+        const uint32_t rang = __popc(vote & masque_inf);
+        const uint32_t w = __shfl_sync(0xFFFFFFFFu, s.wp, rang);
+        const uint32_t ew = __shfl_sync(0xFFFFFFFFu, s.lp, rang);
+        x = besoin ? __byte_perm(w, y, 0x5410) : y;
+        s.e = besoin ? ew : ey;
+        pa += __popc(vote);
+        s.wp = lds16(anneau_s + 2u * ((pa & (ANNEAU_MOTS - 1u)) + voie));
+        s.lp = lds32(lut_s + 4u * (s.wp & (M - 1u)));
+        return e;
+    }
+
+    __device__ __forceinline__ uint32_t macro_avance(uint32_t lut_s, Avance& s) {
+        uint32_t m = pas_avance(lut_s, s);
+        m = __byte_perm(m, pas_avance(lut_s, s), 0x0040);
+        m = __byte_perm(m, pas_avance(lut_s, s), 0x0410);
+        m = __byte_perm(m, pas_avance(lut_s, s), 0x4210);
+        return m;
+    }
+
     // End-of-tile integrity: lanes off L; the word pointer must end at the tile's end.
     __device__ __forceinline__ void bilan(uint32_t& hors_l, uint32_t& pointeur) const {
         hors_l += x != L ? 1u : 0u;

@@ -137,11 +137,13 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     Decodeur d;
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * DELTA_WARPS) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
+        Decodeur::Avance av;
+        d.debut_avance(lut_s, av);  // one table for every lane: the look-ahead form
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         // Word w = 32 m + lane is the delta of blocks 4w .. 4w + 3, stored as it comes.
         for (uint32_t m = m0; m < m1; ++m) {
             d.avancer();
-            const uint32_t mot = d.macro(lut_s);
+            const uint32_t mot = d.macro_avance(lut_s, av);
             const uint32_t b0 = 4u * (m * 32u + voie);
             if (b0 + 3u < nblocs) {
                 *reinterpret_cast<uint32_t*>(delta + b0) = mot;
