@@ -405,6 +405,20 @@ struct Decodeur {
         return m;
     }
 
+    // With the caller's independent work f(Etape<k>) after sub-step k (as macro(lut_s, f)).
+    template <typename F>
+    __device__ __forceinline__ uint32_t macro_avance(uint32_t lut_s, Avance& s, F&& f) {
+        uint32_t m = pas_avance(lut_s, s);
+        f(Etape<0>{});
+        m = __byte_perm(m, pas_avance(lut_s, s), 0x0040);
+        f(Etape<1>{});
+        m = __byte_perm(m, pas_avance(lut_s, s), 0x0410);
+        f(Etape<2>{});
+        m = __byte_perm(m, pas_avance(lut_s, s), 0x4210);
+        f(Etape<3>{});
+        return m;
+    }
+
     // End-of-tile integrity: lanes off L; the word pointer must end at the tile's end.
     __device__ __forceinline__ void bilan(uint32_t& hors_l, uint32_t& pointeur) const {
         hors_l += x != L ? 1u : 0u;

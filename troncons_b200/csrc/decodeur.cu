@@ -120,12 +120,14 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
         uint32_t b0 = 4u * (m0 * 32u + voie);
         LignesDelta lg;
         lg.debut(b0, B);
+        Decodeur::Avance av;
+        d.debut_avance(lut_s, av);  // one table for every lane: the look-ahead form
         d.avancer();
-        uint32_t mot_p = d.macro(lut_s);
+        uint32_t mot_p = d.macro_avance(lut_s, av);
         for (uint32_t m = m0 + 1; m < m1; ++m) {
             d.avancer();
             uint32_t sortie = 0;
-            const uint32_t mot = d.macro(lut_s, [&](auto k) {
+            const uint32_t mot = d.macro_avance(lut_s, av, [&](auto k) {
                 constexpr int K = decltype(k)::value;  // block 4w + K of the previous word
                 const uint32_t rk = lg.rang(K);
                 const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
