@@ -72,6 +72,9 @@ def arguments():
                         "with --modele on one GPU, a batch of this many sequences")
     a.add_argument("--sans-couche", action="store_true",
                    help="N > 1: measure the expert-parallel whole model only (its own line)")
+    a.add_argument("--moe", choices=["fusionnee", "par_flux"], default="fusionnee",
+                   help="expert-parallel whole model: the fused layer, or the layer par flux (each held expert "
+                        "decoded once per step)")
     a.add_argument("--zipf", type=float, default=0.0,
                    help="whole model: Zipf(s)-shaped expert popularity from a seeded router bias (0: uniform)")
     a.add_argument("--placement", choices=["aleatoire", "equilibre"], default="aleatoire",
@@ -568,7 +571,7 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
     r, w, _ = rang()
     b = args.par_rang
     t0 = time.time()
-    ep = ModeleEP(r, w, echange="nccl", par_rang=b, couches=args.couches, d=2880, tetes=64, tetes_kv=8,
+    ep = ModeleEP(r, w, echange="nccl", par_rang=b, moe=args.moe, couches=args.couches, d=2880, tetes=64, tetes_kv=8,
                   experts=args.experts, k=args.k, vocab=201088, contexte=args.contexte + warmup + steps + 2, ffn=2880,
                   fenetre=128, graine=args.graine, compresse=True, brut=False, zipf=args.zipf,
                   placement=args.placement)
@@ -629,6 +632,7 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
             "value": round(w * b * 1000.0 / ms, 2), "unit": "tokens/s", "ms_per_step": round(ms, 4), "steps": steps,
             "warmup": warmup, "batch": w * b, "sequences_per_gpu": b, "experts_per_gpu": fin - debut, "n_gpus": w,
             "popularity": ({"zipf": args.zipf, "placement": args.placement} if args.zipf > 0 else "uniform"),
+            "moe": args.moe,
             "load": charge,
             "workload": f"config 3: {args.couches} layers, {args.experts} experts top-{args.k} ({fin - debut} per GPU), "
                         f"{b} sequence(s) per GPU, context {args.contexte} seeded tokens, attention on each sequence's "

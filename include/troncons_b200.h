@@ -562,9 +562,10 @@ uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t ex
  * trc-modele/src/lib.rs:607-717, trc-ordo/src/lib.rs:782-981): each distinct routed expert is
  * decoded once for the whole batch into a slot of the workspace, then applied to every position
  * routed to it with the token-by-token arithmetic, so the residuals are bit-identical to
- * trc_moe_couche_fusionnee's on the same descriptor. Compressed parts of every expert on this
- * device (no brut, no expert share, no exchange). The controle of an activation receives its
- * expert's decode counters. */
+ * trc_moe_couche_fusionnee's on the same descriptor. Compressed parts (no brut) and no exchange;
+ * an expert share (expert_debut / expert_fin: the other experts' activations left out) and
+ * partiel (each position's share of the sum written alone) are those of the fused layer. The
+ * controle of an activation receives its expert's decode counters. */
 int trc_moe_couche_par_flux(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);
 
 /* trc_moe_couche_fusionnee, recording evenements[0..5] (cudaEvent_t, each may be NULL) on the

@@ -58,15 +58,16 @@ def test_un_rang_egale_le_pas():
             assert np.array_equal(za.view(np.int32), zb.view(np.int32)) and ja == jb, f"{actifs} step {t}"
 
 
-@pytest.mark.parametrize("b", [3, 9])
-def test_un_rang_plusieurs_sequences(b):
+@pytest.mark.parametrize("b,moe", [(3, "fusionnee"), (9, "fusionnee"), (9, "par_flux")])
+def test_un_rang_plusieurs_sequences(b, moe):
     """b sequences on one rank (their attention sides batched: trc_modele_attention_lot, the Q8_0
-    GEMVs by launches of up to 8 tokens; the router and the fused layer called for the b tokens):
-    each sequence's logits are those of the model run on that sequence alone, bit for bit."""
+    GEMVs by launches of up to 8 tokens; the router and the fused layer, or the layer par flux,
+    called for the b tokens): each sequence's logits are those of the model run on that sequence
+    alone, bit for bit."""
     import troncons_b200.modele as M
     from troncons_b200.parallele import ModeleEP
 
-    ep = ModeleEP(0, 1, par_rang=b, **FORME)
+    ep = ModeleEP(0, 1, par_rang=b, moe=moe, **FORME)
     m = M.Modele(**FORME)
     jetons = np.random.default_rng(8).integers(0, 512, (b, 20))
     ep.choisir("compresse")
@@ -93,7 +94,7 @@ def _port_libre() -> int:
     return p
 
 
-def _rang(rang, monde, port, echange):
+def _rang(rang, monde, port, echange, moe):
     import torch.distributed as dist
 
     import troncons_b200.modele as M
@@ -105,7 +106,7 @@ def _rang(rang, monde, port, echange):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rang, world_size=monde,
                             timeout=timedelta(seconds=60), device_id=dev)
     try:
-        ep = ModeleEP(rang, monde, echange=echange, **FORME)
+        ep = ModeleEP(rang, monde, echange=echange, moe=moe, **FORME)
         seul = M.Modele(**FORME)
         # the share's parts are the whole model's, byte for byte
         for l in range(FORME["couches"]):
@@ -128,7 +129,7 @@ def _rang(rang, monde, port, echange):
         assert (ep.controle == 0).all()
         # two sequences per rank: a batch of 4 tokens over 2 GPUs
         del ep
-        ep = ModeleEP(rang, monde, echange=echange, par_rang=2, **FORME)
+        ep = ModeleEP(rang, monde, echange=echange, par_rang=2, moe=moe, **FORME)
         ep.choisir("compresse")
         seul.choisir("compresse")
         jetons = np.random.default_rng(200 + rang).integers(0, 512, (2, 16))
@@ -150,10 +151,10 @@ def _rang(rang, monde, port, echange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("echange", ["pairs", "nccl"])
-def test_deux_rangs_egalent_un_gpu(echange):
+@pytest.mark.parametrize("echange,moe", [("pairs", "fusionnee"), ("nccl", "fusionnee"), ("nccl", "par_flux")])
+def test_deux_rangs_egalent_un_gpu(echange, moe):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
 
-    mp.start_processes(_rang, args=(2, _port_libre(), echange), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rang, args=(2, _port_libre(), echange, moe), nprocs=2, join=True, start_method="spawn")

@@ -60,3 +60,30 @@ def test_par_flux_expert_absent_compte(couche_petite):
     touche = (idx.reshape(-1) == 3)
     assert (ctl[touche, 1] >= 1).all() and (ctl[~touche, 1] == 0).all()
     assert torch.isfinite(r).all()
+
+
+@pytest.mark.parametrize("jetons,tenus", [(16, (2, 6)), (40, (0, 3)), (9, (5, 8))])
+def test_par_flux_sur_une_part_partielle(couche_petite, jetons, tenus):
+    """An expert share with the partial combine (the expert-parallel layer's form): par flux
+    writes the fused layer's bits, each position's share of the sum alone, with no counter set
+    for the activations of experts held elsewhere."""
+    from troncons_b200.carte import CoucheCarte
+
+    cc = CoucheCarte(couche_petite, k=4, brut=False, jetons=jetons, tenus=tenus)
+    rng = np.random.default_rng(jetons)
+    d = couche_petite.dims.colonnes[0]
+    for pas in range(2):
+        x = torch.from_numpy(rng.standard_normal((jetons, d)).astype(np.float32)).to(torch.bfloat16).cuda()
+        r0 = torch.from_numpy(rng.standard_normal((jetons, couche_petite.dims.lignes[2])).astype(np.float32)).cuda()
+        rf, rp = r0.clone(), r0.clone()
+        cc.controle.zero_()
+        cc.couche(x, rf, partiel=True)
+        ctl_f = cc.controle.clone()
+        cc.controle.zero_()
+        cc.couche_par_flux(x, rp, routeur=False, partiel=True)
+        torch.cuda.synchronize()
+        assert (ctl_f == 0).all() and (cc.controle == 0).all()
+        assert torch.equal(rf.view(torch.int32), rp.view(torch.int32)), f"step {pas}"
+        idx = cc.idx.cpu().numpy().reshape(jetons, 4)
+        sans = ~((idx >= tenus[0]) & (idx < tenus[1])).any(1)
+        assert (rp[torch.from_numpy(sans).cuda()] == 0).all()

@@ -133,9 +133,11 @@ class CoucheCarte:
         self._desc = self.descripteur(x, residu, brute, partiel, echange)  # alive while the launch reads it
         self.n.moe_couche(self._desc, self._espace(), flux, evenements)
 
-    def couche_par_flux(self, x: torch.Tensor, residu: torch.Tensor, flux=None, routeur: bool = True):
+    def couche_par_flux(self, x: torch.Tensor, residu: torch.Tensor, flux=None, routeur: bool = True,
+                        partiel: bool = False):
         """Router then the layer "par flux" (trc_moe_couche_par_flux): each distinct routed expert
-        decoded once for the batch; the residuals are the fused layer's bits."""
+        decoded once for the batch; the residuals are the fused layer's bits (also on the share
+        `tenus`, and with `partiel`: the share's sum written alone)."""
         from . import lib, verifier
 
         if routeur:
@@ -145,7 +147,7 @@ class CoucheCarte:
             self._espace_pf = torch.empty(n + 256, dtype=torch.uint8, device=self.dev)
             self._n_pf = n
         e = self._espace_pf.data_ptr() + (-self._espace_pf.data_ptr()) % 256
-        self._desc_pf = self.descripteur(x, residu, False)
+        self._desc_pf = self.descripteur(x, residu, False, partiel)
         f = (flux or torch.cuda.current_stream()).cuda_stream
         verifier(lib.trc_moe_couche_par_flux(C.byref(self._desc_pf), e, self._n_pf, f))
 

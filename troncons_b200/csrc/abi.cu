@@ -404,8 +404,8 @@ uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t ex
 int trc_moe_couche_par_flux(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
     tb::Couche k;
     if (const int r = couche_de(c, k)) return r;
-    if (k.brut || k.expert_fin != 0 || k.partiel || k.ech.monde != 0)
-        return usage("par flux: compressed parts of every expert on this device only (no raw parts, share or exchange)");
+    if (k.brut || k.ech.monde != 0)
+        return usage("par flux: compressed parts only, and no exchange (an expert share with partiel is accepted)");
     const uint64_t besoin = tb::plan_par_flux(k.lignes, k.colonnes, k.experts, k.k * k.jetons).total;
     if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
         return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);

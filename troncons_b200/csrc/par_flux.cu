@@ -81,6 +81,12 @@ __device__ __forceinline__ T* zone(const ArgsParFlux& a, uint64_t off) {
 
 // One block: counts per expert, the distinct experts in ascending order, their lists of
 // activations (stable: by activation index), the decode descriptors (empty past the last).
+// Expert e is held on this device: every expert, or those of the share [expert_debut, expert_fin)
+// (the fused layer's rule for an expert-parallel share).
+__device__ __forceinline__ bool tient(const Couche& c, uint32_t e) {
+    return c.expert_fin == 0 || (e >= c.expert_debut && e < c.expert_fin);
+}
+
 __global__ void __launch_bounds__(1024) k_grouper(ArgsParFlux a) {
     __shared__ uint32_t part[1024];
     __shared__ uint32_t base_u, base_a;
@@ -98,7 +104,7 @@ __global__ void __launch_bounds__(1024) k_grouper(ArgsParFlux a) {
     __syncthreads();
     for (uint32_t i = tid; i < na; i += 1024u) {
         const uint32_t e = c.indices[i];
-        if (e < E) atomicAdd(&cpt[e], 1u);
+        if (e < E && tient(c, e)) atomicAdd(&cpt[e], 1u);
     }
     __syncthreads();
     // exclusive scans over the experts: distinct index u and first activation of each
@@ -143,7 +149,7 @@ __global__ void __launch_bounds__(1024) k_grouper(ArgsParFlux a) {
     // each activation's place in its expert's list: the activations before it with the same expert
     for (uint32_t i = tid; i < na; i += 1024u) {
         const uint32_t e = c.indices[i];
-        if (e >= E) continue;
+        if (e >= E || !tient(c, e)) continue;
         uint32_t rang = 0;
         for (uint32_t i2 = 0; i2 < i; ++i2) rang += c.indices[i2] == e ? 1u : 0u;
         liste[debut[cpt[e]] + rang] = i;
@@ -289,7 +295,9 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 2) k_gemv_flux(ArgsParFlux a) {
 // Position b = blockIdx.y: residu[b] += ((w0 y0 + w1 y1) + w2 y2) + ... over its k routed slots
 // in slot order, products and sums rounded separately (passe.cuh:611-622); an activation whose
 // expert had no part is left out and counted. Block x = 0 also adds each distinct expert's
-// decode counters to the controle of every activation routed to it.
+// decode counters to the controle of every activation routed to it. On an expert share, the
+// activations of experts not held are left out (not counted), and with `partiel` residu[b] = the
+// sum alone (0 when no activation of the position is held), as the fused layer's partial combine.
 __global__ void __launch_bounds__(256) k_combiner_flux(ArgsParFlux a) {
     attendre_amont();
     liberer_aval();
@@ -301,7 +309,8 @@ __global__ void __launch_bounds__(256) k_combiner_flux(ArgsParFlux a) {
         const uint32_t act = b * c.k + threadIdx.x / 4u, w = threadIdx.x % 4u;
         const uint32_t e = c.indices[act];
         const uint32_t u = e < c.experts ? slot_de[e] : NUL32;
-        const uint32_t v = u != NUL32 ? ctl[4u * u + w] : (w == CTL_FORMAT ? 1u : 0u);
+        const bool ailleurs = e < c.experts && !tient(c, e);  // held by another device
+        const uint32_t v = u != NUL32 ? ctl[4u * u + w] : (w == CTL_FORMAT && !ailleurs ? 1u : 0u);
         if (v != 0u) atomicAdd(&c.controle[4u * act + w], v);
     }
     if (i >= d) return;
@@ -317,7 +326,7 @@ __global__ void __launch_bounds__(256) k_combiner_flux(ArgsParFlux a) {
         premier = false;
     }
     float* res = c.residu + uint64_t(b) * d;
-    res[i] = __fadd_rn(res[i], s);
+    res[i] = c.partiel ? s : __fadd_rn(res[i], s);
 }
 
 cudaError_t lancer_par_flux(const Couche& c, void* espace, cudaStream_t flux) {

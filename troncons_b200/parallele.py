@@ -96,6 +96,9 @@ class CoucheEP:
         self.rang, self.monde, self.groupe = rang, monde, groupe
         self.tenus = partage(c.experts, rang, monde)
         self.carte = CoucheCarte(c, k=k, brut=False, jetons=jetons, tenus=self.tenus)
+        if moe not in ("fusionnee", "par_flux") or (moe == "par_flux" and echange == "pairs" and monde > 1):
+            raise ValueError(f"MoE form {moe!r}: 'fusionnee', or 'par_flux' (with the NCCL exchange)")
+        self.moe = moe
         self.echange = echange if monde > 1 else "aucun"
         self.paires = None
         if self.echange == "pairs":
@@ -126,7 +129,8 @@ class ModeleEP:
     of the rank's tokens (trc_modele_attention, or trc_modele_attention_lot for several sequences:
     their Q8_0 GEMVs launched once for all of them; the KV caches stay on the rank's GPU); an all-gather of the MoE inputs h2 ([monde x par_rang][d] f32, NCCL); the router
     on every token (replicated, identical on every rank); the fused layer on the rank's share for
-    every token; then the combine's exchange. "nccl" (the default): each token's share written
+    every token (or, with moe="par_flux", the layer par flux: each held expert routed to by any of
+    the step's tokens decoded once, the same bits); then the combine's exchange. "nccl" (the default): each token's share written
     alone (partiel), a SUM reduce-scatter, added into each sequence's x. "pairs": the combine
     kernel writes each token's share into every rank's symmetric buffer over NVLink peer stores
     and adds all ranks' shares in rank order into [tokens][d] rows, this rank's rows holding its
@@ -138,7 +142,8 @@ class ModeleEP:
     summed across ranks), so the logits agree with the one-GPU model within f32 rounding, not
     bit for bit; with one rank and one sequence the step is trc_modele_pas's bits."""
 
-    def __init__(self, rang: int, monde: int, groupe=None, echange: str = "nccl", par_rang: int = 1, **modele):
+    def __init__(self, rang: int, monde: int, groupe=None, echange: str = "nccl", par_rang: int = 1,
+                 moe: str = "fusionnee", **modele):
         import torch
 
         from . import espace_recouvrant_octets
@@ -149,6 +154,9 @@ class ModeleEP:
             raise ValueError(f"exchange {echange!r}: 'pairs' or 'nccl'")
         if not 1 <= par_rang or monde * par_rang > 128:
             raise ValueError(f"{par_rang} sequences per rank on {monde} ranks: 1 to 128 tokens per step")
+        if moe not in ("fusionnee", "par_flux") or (moe == "par_flux" and echange == "pairs" and monde > 1):
+            raise ValueError(f"MoE form {moe!r}: 'fusionnee', or 'par_flux' (with the NCCL exchange)")
+        self.moe = moe
         self.echange = echange if monde > 1 else "aucun"
         self.tenus = partage(modele["experts"], rang, monde)
         modele.setdefault("rangs", monde)  # the balanced placement of a skewed popularity
@@ -165,7 +173,12 @@ class ModeleEP:
         self.idx = torch.empty(n_tok * m.k, dtype=torch.int32, device=dev)
         self.poids = torch.empty(n_tok * m.k, dtype=f32, device=dev)
         self.controle = torch.zeros(n_tok * m.k * 4, dtype=torch.int32, device=dev)
-        n = espace_recouvrant_octets(m.dims, n_tok * m.k)
+        if moe == "par_flux":
+            from . import lib as _l
+
+            n = int(_l.trc_moe_par_flux_espace_octets(C.byref(m.dims), m.experts, n_tok * m.k))
+        else:
+            n = espace_recouvrant_octets(m.dims, n_tok * m.k)
         self._espace = torch.empty(n + 256, dtype=torch.uint8, device=dev)
         self.espace_octets = n
         if self.echange == "pairs":
@@ -280,7 +293,8 @@ class ModeleEP:
                     for i in range(self.b):
                         self.x[i].copy_(self._lignes[i])
                     continue
-                verifier(lib.trc_moe_couche_fusionnee(C.byref(self.descs[l]), e, self.espace_octets, f))
+                couche = lib.trc_moe_couche_par_flux if self.moe == "par_flux" else lib.trc_moe_couche_fusionnee
+                verifier(couche(C.byref(self.descs[l]), e, self.espace_octets, f))
                 if self.monde > 1:
                     dist.reduce_scatter_tensor(self.y, self.y_tous, op=dist.ReduceOp.SUM, group=self.groupe)
                     for i in range(self.b):
