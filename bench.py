@@ -23,7 +23,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -555,13 +554,13 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
     """Config 3, the whole model expert-parallel (every rank of the torchrun group calls it): a
     seeded synthetic gpt-oss-120b, each rank holding its share of every layer's experts
     (partage: 16 of 128 at 8 GPUs, drawn and encoded on its GPU, the tables from the counts summed
-    over NCCL) and a replica of the dense weights; one sequence per rank (a batch of N): its own
-    --contexte seeded tokens through the step, then `steps` greedy steps timed with CUDA events
-    after `warmup`, every rank in step (two NCCL collectives per layer: the MoE inputs gathered,
-    the shares' sums scattered back). tokens/s = N x steps / the max over ranks of the timed
-    region."""
-    import datetime  # noqa: F401
-
+    over NCCL) and a replica of the dense weights; --par-rang sequences per rank (a batch of N x
+    par-rang; one GPU and par-rang > 1: the batch on that GPU), each its own --contexte seeded
+    tokens through the step, then `steps` greedy steps timed with CUDA events after `warmup`,
+    every rank in step (two NCCL collectives per layer: the MoE inputs gathered, the shares' sums
+    scattered back), the MoE by the fused layer or par flux (--moe), the router biased for Zipf
+    popularity with --zipf. tokens/s = batch x steps / the max over ranks of the timed region;
+    after the timing, one more step records each GPU's activations per layer ("load")."""
     import numpy as np
     import torch
     import torch.distributed as dist

@@ -7,7 +7,7 @@ import ctypes as C
 
 import numpy as np
 
-from . import DescCodage, DimsExpert, ParamsRope, lib, verifier
+from . import DimsExpert, ParamsRope, lib, verifier
 
 _u64, _u32, _vp, _sz, _i32 = C.c_uint64, C.c_uint32, C.c_void_p, C.c_size_t, C.c_int
 
