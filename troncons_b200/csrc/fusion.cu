@@ -99,7 +99,7 @@ __device__ __forceinline__ void copier16(uint4* dst, const uint4* __restrict__ s
     for (; t < n; t += pas) dst[t] = __ldg(src + t);
 }
 
-constexpr uint32_t DELTA_WARPS = 4;
+constexpr uint32_t DELTA_WARPS = 1;  // one DELTA tile per block: each chain alone on its SM
 constexpr uint32_t MOE_WARPS = 8;  // k_moe_brut: warps per block (one row at a time each)
 constexpr uint32_t BRUT_BLOCS_SM = 3;  // its blocks per SM: the grid is one wave of them
 
