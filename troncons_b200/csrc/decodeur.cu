@@ -43,7 +43,7 @@ __device__ __forceinline__ void choisir_expert(const ArgsDecodage& a, const uint
     }
 }
 
-constexpr uint32_t ECH_WARPS = 4;
+constexpr uint32_t ECH_WARPS = 1;  // one DELTA tile per block: each chain alone on its SM
 constexpr uint32_t CODES_WARPS = 8;
 
 // Scales of the 4 blocks of a DELTA word: e = (med[r] + delta - 128) mod 256, to the slot.
