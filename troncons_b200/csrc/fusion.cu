@@ -421,9 +421,12 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
 
 // Second form of the same launch, for launches with more tiles than the producer / consumer
 // form keeps in flight (2 x MOE_PAIRES per SM): one warp per tile both decodes and multiplies,
-// DENSE_WARPS warps per block sharing the LUTs, 24 tiles per SM. The product of macro-step m - 1
-// runs in stages between the four sub-steps of macro-step m's decode. Same partials, same bits.
-constexpr uint32_t DENSE_WARPS = 12;
+// DENSE_WARPS warps per block sharing the LUTs, up to two blocks per SM. The product of
+// macro-step m - 1 runs in stages between the four sub-steps of macro-step m's decode. Same
+// partials, same bits. 11 warps: a config-1 launch (3 x 4 matrices of 127 tiles) is 144 blocks,
+// one per SM with at most 11 tiles each, where blocks of 12 were 132, 12 tiles on each of 132
+// SMs and 16 SMs idle; the chains run faster with fewer tiles per SM.
+constexpr uint32_t DENSE_WARPS = 11;
 
 struct DispositionDense {
     uint32_t anneaux, med, puiss, x2, total;
