@@ -144,3 +144,21 @@ def test_popularite_zipf(placement):
         assert not np.array_equal(b, biais_zipf(E, s, placement, monde, 7, 4))
     with pytest.raises(ValueError):
         biais_zipf(E, s, "autre", monde, 7, 3)
+
+
+@pytest.mark.parametrize("kw,motif", [
+    (dict(echange="autre"), "exchange"),
+    (dict(par_rang=0), "sequences per rank"),
+    (dict(par_rang=65, monde=2), "128 tokens"),
+    (dict(moe="autre"), "MoE form"),
+    (dict(moe="par_flux", echange="pairs", monde=2), "MoE form"),
+])
+def test_modele_ep_refuse(kw, motif):
+    """The expert-parallel model's arguments are checked before anything is drawn on a device:
+    the exchange, the sequences per rank (1 to 128 tokens per step over the ranks), the MoE form
+    (par flux has no peer-store exchange)."""
+    from troncons_b200.parallele import ModeleEP
+
+    monde = kw.pop("monde", 1)
+    with pytest.raises(ValueError, match=motif):
+        ModeleEP(0, monde, experts=8, **kw)
