@@ -156,3 +156,12 @@ def test_formats_rust():
     assert J._exp_rust(-3.5e12, 6) == "-3.500000e12"
     assert J._exp_rust(float("nan"), 6) == "NaN" and J._exp_rust(float("inf"), 6) == "inf"
     assert J._fix_rust(2.5, 6) == "2.500000"
+
+
+def test_ligne_de_commande_usage(capsys):
+    """The command line names its two sub-commands and refuses anything else (exit status 2)."""
+    assert J.main([]) == 2
+    assert J.main(["reference"]) == 2
+    assert "kl|comparer" in capsys.readouterr().err
+    assert J._args(["--base", "p.kld", "--test", "q.kld", "--fenetres", "3", "--drapeau"]) == {
+        "base": "p.kld", "test": "q.kld", "fenetres": "3"}
