@@ -34,7 +34,7 @@ METRIQUE = "fused rANS+MXFP4 GEMV GB/s vs HBM peak; gpt-oss-120b tok/s at 1/2/4/
 UNITE = "GB/s"
 
 
-def arguments():
+def arguments(argv=None):
     a = argparse.ArgumentParser()
     a.add_argument("--gpus", type=int, default=1)
     a.add_argument("--steps", type=int, default=30)
@@ -80,7 +80,7 @@ def arguments():
                    help="with --zipf: the popular experts numbered at random, or interleaved over the GPUs' shares")
     a.add_argument("--echange", choices=["pairs", "nccl"], default="pairs",
                    help="N > 1: the combine's exchange in the combine kernel over NVLink (pairs) or by NCCL")
-    return a.parse_args()
+    return a.parse_args(argv)
 
 
 def rang():
@@ -389,6 +389,14 @@ def notre_bras(args):
         print(json.dumps(ligne), flush=True)
 
 
+def couche_ep(args, c, r: int, w: int):
+    """This rank's share of the layer for the expert-parallel arm: the bench's arguments (k,
+    exchange, MoE form) checked and passed through; a batch of w tokens (one per GPU on average)."""
+    from troncons_b200.parallele import CoucheEP
+
+    return CoucheEP(c, r, w, k=args.k, jetons=w, echange=args.echange, moe=args.moe)
+
+
 def bras_ep(args):
     """N > 1: the expert-parallel layer (config 3). Rank r holds experts partage(128, r, N) (16
     per GPU at 8); a step is a batch of N tokens (one per GPU on average: weak scaling), the
@@ -402,7 +410,7 @@ def bras_ep(args):
 
     import troncons_b200 as T
     import troncons_b200.synth as S
-    from troncons_b200.parallele import CoucheEP, partage, reduire_comptes
+    from troncons_b200.parallele import partage, reduire_comptes
 
     r, w, lr = rang()
     torch.cuda.set_device(lr)
@@ -420,7 +428,7 @@ def bras_ep(args):
     c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=False, n_delta=args.n_delta,
                  n_codes=args.n_codes, tenus=partage(args.experts, r, w), reduire=reduire_comptes(device=dev))
     t_gen = time.time() - t0
-    ep = CoucheEP(c, r, w, k=args.k, jetons=jetons, echange=args.echange)
+    ep = couche_ep(args, c, r, w)
     C0, R2 = c.dims.colonnes[0], c.dims.lignes[2]
     n_pas = args.warmup + args.steps
     rng = np.random.default_rng(args.graine)  # the same tokens on every rank

@@ -100,3 +100,33 @@ def test_ep_deux_gpus_egale_un_gpu(echange):
     import torch.multiprocessing as mp
 
     mp.start_processes(_rang, args=(2, _port_libre(), echange), nprocs=2, join=True, start_method="spawn")
+
+
+@pytest.mark.parametrize("moe", ["fusionnee", "par_flux"])
+def test_ep_un_rang_egale_la_couche(moe):
+    """One rank holding every expert (no process group, no exchange): the expert-parallel layer's
+    step is the fused layer's (trc_moe_couche_fusionnee) bit for bit, for either MoE form (par
+    flux gives the fused layer's bits), step after step. Runs on a one-GPU box, so a fault in the
+    layer's construction or step cannot hide behind the two-GPU skip."""
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+    from troncons_b200.carte import CoucheCarte
+    from troncons_b200.parallele import CoucheEP
+
+    torch.cuda.set_device(0)
+    dims = T.DimsExpert.de([256, 256, 512], [512, 512, 256])
+    c = S.couche(78, dims, 8, brut=False)
+    ep = CoucheEP(c, 0, 1, k=4, jetons=3, moe=moe)
+    assert ep.echange == "aucun" and ep.carte.tenus == (0, 8)
+    toute = CoucheCarte(c, k=4, brut=False, jetons=3)
+    rng = np.random.default_rng(5)
+    for _ in range(4):
+        x = torch.from_numpy(rng.standard_normal((3, 512)).astype(np.float32)).to(torch.bfloat16).cuda()
+        r0 = torch.from_numpy(rng.standard_normal((3, 512)).astype(np.float32)).cuda()
+        r, rt = r0.clone(), r0.clone()
+        ep.etape(x, r)
+        toute.couche(x, rt)
+        torch.cuda.synchronize()
+        assert (ep.carte.controle == 0).all() and (toute.controle == 0).all()
+        assert torch.equal(ep.carte.idx, toute.idx)
+        assert torch.equal(r.view(torch.int32), rt.view(torch.int32))

@@ -162,3 +162,73 @@ def test_modele_ep_refuse(kw, motif):
     monde = kw.pop("monde", 1)
     with pytest.raises(ValueError, match=motif):
         ModeleEP(0, monde, experts=8, **kw)
+
+
+class _CarteFactice:
+    """Stands in for CoucheCarte (which uploads to a GPU): records what the layer asks of it."""
+
+    def __init__(self, c, k, brut, jetons, tenus):
+        self.k, self.jetons, self.tenus, self.appels = k, jetons, tenus, []
+
+    def couche(self, x, residu, flux=None, partiel=False, echange=None):
+        self.appels.append(("fusionnee", partiel, echange))
+
+    def couche_par_flux(self, x, residu, flux=None, partiel=False):
+        self.appels.append(("par_flux", partiel, None))
+
+
+def _couche_factice(experts=128):
+    from types import SimpleNamespace
+
+    return SimpleNamespace(experts=experts, dims=None)
+
+
+@pytest.mark.parametrize("kw,motif", [
+    (dict(echange="autre"), "exchange"),
+    (dict(moe="autre"), "MoE form"),
+    (dict(moe="par_flux", echange="pairs", monde=2), "MoE form"),
+    (dict(k=9), "k = 9"),
+    (dict(k=0), "k = 0"),
+    (dict(jetons=0), "tokens"),
+    (dict(rang=2, monde=2), "rank 2 of 2"),
+])
+def test_couche_ep_refuse(kw, motif, monkeypatch):
+    """The expert-parallel layer refuses bad arguments before any device work (its CoucheCarte
+    is never built)."""
+    import troncons_b200.carte as carte
+    from troncons_b200.parallele import CoucheEP
+
+    monkeypatch.setattr(carte, "CoucheCarte", lambda *a, **k: pytest.fail("device work before the checks"))
+    rang, monde = kw.pop("rang", 0), kw.pop("monde", 1)
+    with pytest.raises(ValueError, match=motif):
+        CoucheEP(_couche_factice(), rang, monde, **kw)
+
+
+@pytest.mark.parametrize("argv,forme,echange", [
+    (["--gpus", "2"], "fusionnee", "pairs"),
+    (["--gpus", "2", "--echange", "nccl", "--moe", "par_flux"], "par_flux", "nccl"),
+    (["--gpus", "8", "--echange", "nccl"], "fusionnee", "nccl"),
+])
+def test_bras_ep_construit_la_couche(argv, forme, echange, monkeypatch):
+    """bench.py's expert-parallel arm builds its layer from the command line (the path every
+    `bench.py --gpus N` run with N > 1 takes) and steps it: the share, the exchange and the MoE
+    form reach the layer, the right half of the layer runs. CoucheCarte and the symmetric-memory
+    rendezvous are replaced by fakes, so no GPU is needed."""
+    import bench
+    import troncons_b200.carte as carte
+    import troncons_b200.parallele as P
+
+    monkeypatch.setattr(carte, "CoucheCarte", _CarteFactice)
+    monkeypatch.setattr(P, "monter_paires", lambda dims, jetons, r, w, g=None: (None, None, "paires"))
+    args = bench.arguments(argv)
+    w = args.gpus
+    for r in (0, w - 1):
+        ep = bench.couche_ep(args, _couche_factice(args.experts), r, w)
+        assert ep.carte.tenus == P.partage(128, r, w) and ep.carte.jetons == w and ep.carte.k == args.k
+        assert ep.echange == echange and ep.moe == forme
+        if echange == "pairs":
+            ep.etape(None, None)
+            assert ep.carte.appels == [("fusionnee", False, "paires")]
+        else:
+            ep.local(None, None, r != 0)
+            assert ep.carte.appels == [(forme, r != 0, None)]

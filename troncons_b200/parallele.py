@@ -52,6 +52,26 @@ def reduire_comptes(groupe=None, device=None):
     return reduire
 
 
+ECHANGES = ("pairs", "nccl")
+FORMES_MOE = ("fusionnee", "par_flux")
+
+
+def verifier_arguments_ep(experts: int, rang: int, monde: int, k: int, jetons: int, echange: str,
+                          moe: str) -> None:
+    """Refuses a bad expert-parallel configuration before any device work (ValueError): the rank
+    and share, k in 1..8, at least one token, a known exchange, and a known MoE form (par flux
+    only with the NCCL exchange when several ranks share the layer)."""
+    partage(experts, rang, monde)
+    if not 1 <= k <= 8:
+        raise ValueError(f"k = {k}: 1 to 8 routed experts per token")
+    if jetons < 1:
+        raise ValueError(f"{jetons} tokens per step")
+    if echange not in ECHANGES:
+        raise ValueError(f"exchange {echange!r}: one of {ECHANGES}")
+    if moe not in FORMES_MOE or (moe == "par_flux" and echange == "pairs" and monde > 1):
+        raise ValueError(f"MoE form {moe!r}: 'fusionnee', or 'par_flux' (with the NCCL exchange)")
+
+
 def etape_ep(calcul_local, residu, rang: int, groupe=None) -> None:
     """One expert-parallel step: `calcul_local(residu, partiel)` runs this rank's share of the
     layer on `residu` ([tokens][d] f32; rank 0 adds into it, the others overwrite it with their
@@ -90,16 +110,16 @@ class CoucheEP:
     """This rank's share of a layer on its GPU: the parts of its experts, the layer's LUTs and
     the router; `etape` runs router + fused share + the combine's exchange on the current stream."""
 
-    def __init__(self, c, rang: int, monde: int, k: int = 4, jetons: int = 1, groupe=None, echange: str = "pairs"):
+    def __init__(self, c, rang: int, monde: int, k: int = 4, jetons: int = 1, groupe=None, echange: str = "pairs",
+                 moe: str = "fusionnee"):
+        verifier_arguments_ep(c.experts, rang, monde, k, jetons, echange, moe)
         from .carte import CoucheCarte
 
         self.rang, self.monde, self.groupe = rang, monde, groupe
         self.tenus = partage(c.experts, rang, monde)
-        self.carte = CoucheCarte(c, k=k, brut=False, jetons=jetons, tenus=self.tenus)
-        if moe not in ("fusionnee", "par_flux") or (moe == "par_flux" and echange == "pairs" and monde > 1):
-            raise ValueError(f"MoE form {moe!r}: 'fusionnee', or 'par_flux' (with the NCCL exchange)")
         self.moe = moe
         self.echange = echange if monde > 1 else "aucun"
+        self.carte = CoucheCarte(c, k=k, brut=False, jetons=jetons, tenus=self.tenus)
         self.paires = None
         if self.echange == "pairs":
             self._monter_paires(c, jetons)
@@ -108,7 +128,10 @@ class CoucheEP:
         self.tampon, self.poignee, self.paires = monter_paires(c.dims, jetons, self.rang, self.monde, self.groupe)
 
     def local(self, x, residu, partiel: bool, flux=None) -> None:
-        self.carte.couche(x, residu, flux=flux, partiel=partiel)
+        if self.moe == "par_flux":
+            self.carte.couche_par_flux(x, residu, flux=flux, partiel=partiel)
+        else:
+            self.carte.couche(x, residu, flux=flux, partiel=partiel)
 
     def etape(self, x, residu, flux=None) -> None:
         """One step: every rank ends with the whole layer's residual."""
@@ -117,7 +140,7 @@ class CoucheEP:
         elif self.echange == "nccl":
             etape_ep(lambda r, p: self.local(x, r, p, flux), residu, self.rang, self.groupe)
         else:
-            self.carte.couche(x, residu, flux=flux)
+            self.local(x, residu, False, flux)
 
 
 class ModeleEP:
@@ -150,12 +173,9 @@ class ModeleEP:
         from .modele import Modele, Sequence
 
         self.rang, self.monde, self.groupe, self.b = rang, monde, groupe, par_rang
-        if echange not in ("pairs", "nccl"):
-            raise ValueError(f"exchange {echange!r}: 'pairs' or 'nccl'")
         if not 1 <= par_rang or monde * par_rang > 128:
             raise ValueError(f"{par_rang} sequences per rank on {monde} ranks: 1 to 128 tokens per step")
-        if moe not in ("fusionnee", "par_flux") or (moe == "par_flux" and echange == "pairs" and monde > 1):
-            raise ValueError(f"MoE form {moe!r}: 'fusionnee', or 'par_flux' (with the NCCL exchange)")
+        verifier_arguments_ep(modele["experts"], rang, monde, modele.get("k", 4), monde * par_rang, echange, moe)
         self.moe = moe
         self.echange = echange if monde > 1 else "aucun"
         self.tenus = partage(modele["experts"], rang, monde)
