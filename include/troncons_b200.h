@@ -581,7 +581,8 @@ int trc_moe_couche_chrono(const trc_moe_couche* couche, void* espace, size_t esp
  * is a fixed 8 MiB (8,388,608-byte) area of this library's device memory, one per device: a layer
  * whose trc_moe_espace_octets exceeds it is refused with TRC_ERR_USAGE before any launch. Nothing
  * is allocated. The first call on each device looks up the area's address there, so make it
- * before any stream capture. All calls on a device share the area: calls that may overlap in
+ * before any stream capture; that address is kept for the process's life, so do not call this on
+ * a device reset (cudaDeviceReset) since its first call there. All calls on a device share the area: calls that may overlap in
  * time (different streams, different threads) race on it; calls on one stream are safe. Nothing
  * in the area needs zeroing. Results and launches are those of trc_moe_couche_fusionnee. */
 int trc_moe_couche_sans_alloc(const trc_moe_couche* couche, void* flux);

@@ -12,7 +12,7 @@ import numpy as np
 
 ICI = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ICI, "..", ".."))
-REF = "/root/reference/mesures/moteur"
+REF = os.path.join(os.environ.get("TRONCONS_REF", "/root/reference"), "mesures", "moteur")
 
 
 def main():

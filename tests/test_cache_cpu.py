@@ -22,7 +22,7 @@ from troncons_b200 import ErreurUsage
 from troncons_b200.cache import Cache, ErreurTrace, Trace, lire_trace, rejouer
 
 ICI = os.path.dirname(os.path.abspath(__file__))
-REF_O3 = "/root/reference/mesures/moteur/O/journaux/o3"
+REF_O3 = os.path.join(os.environ.get("TRONCONS_REF", "/root/reference"), "mesures/moteur/O/journaux/o3")
 M64 = (1 << 64) - 1
 
 

@@ -76,3 +76,15 @@ def test_deux_appels_comme_l_espace_du_demandeur(nom, k, request, noyaux):
     for i, ((ra, ia, wa), (rb, ib, wb)) in enumerate(zip(attendus, obtenus)):
         assert torch.equal(ia, ib.cpu()) and torch.equal(wa, wb.cpu()), f"call {i}: routing differs"
         assert torch.equal(ra.view(torch.int32), rb.cpu().view(torch.int32)), f"call {i}: residual differs"
+
+
+@pytest.mark.parametrize("k,jetons,motif", [(9, 1, "k = 9"), (0, 1, "k = 0"), (4, 129, "129 tokens")])
+def test_refuse_k_et_jetons_d_abord(k, jetons, motif):
+    """A bad k or token count is reported as itself, before the workspace size is worked out."""
+    desc = T.MoeCouche()
+    desc.dims = T.DimsExpert.de([256, 256, 512], [512, 512, 256])
+    desc.k = k
+    desc.experts = 8
+    desc.jetons = jetons
+    assert T.lib.trc_moe_couche_sans_alloc(C.byref(desc), None) == T.TRC_ERR_USAGE
+    assert motif in T.lib.trc_derniere_erreur().decode()

@@ -7,7 +7,9 @@
 // The workspace is one area of this library's own device memory, declared below as a static
 // device array of ESPACE_FIXE_OCTETS bytes, so it exists as soon as the library's module is
 // loaded on a device; nothing here calls an allocator. Its address on a device is looked up once
-// per device (the first call on that device, with the device current) and kept.
+// per device (the first call on that device, with the device current) and kept for the life of
+// the process: after a cudaDeviceReset of that device the kept address is stale, so the entry
+// point must not be called on a device that was reset since its first call there.
 //
 // Every call on a device uses the same area. Calls on one stream run one after another and are
 // safe; calls that can overlap in time on one device (two streams, or two host threads with
@@ -59,9 +61,20 @@ cudaError_t adresse_espace_fixe(void** p) {
 
 extern "C" int trc_moe_couche_sans_alloc(const trc_moe_couche* couche, void* flux) {
     if (couche == nullptr) return tb::erreur_usage("layer descriptor absent");
-    const uint64_t besoin = trc_moe_espace_octets(&couche->dims, couche->k * (couche->jetons ? couche->jetons : 1u));
+    // k and the token count first, with trc_moe_couche_fusionnee's rules and messages, so that a
+    // bad one is reported as itself and not as a workspace size.
+    char m[256];
+    if (couche->k == 0 || couche->k > 8 || couche->k > couche->experts) {
+        snprintf(m, sizeof m, "k = %u of %u experts", couche->k, couche->experts);
+        return tb::erreur_usage(m);
+    }
+    const uint32_t jetons = couche->jetons ? couche->jetons : 1u;
+    if (jetons > 128) {
+        snprintf(m, sizeof m, "%u tokens (128 at most)", jetons);
+        return tb::erreur_usage(m);
+    }
+    const uint64_t besoin = trc_moe_espace_octets(&couche->dims, couche->k * jetons);
     if (besoin > ESPACE_FIXE_OCTETS) {
-        char m[256];
         snprintf(m, sizeof m,
                  "layer needs %llu bytes of workspace; the fixed area holds %zu (use trc_moe_couche_fusionnee with a "
                  "workspace of its size)",
