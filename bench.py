@@ -171,6 +171,30 @@ class Horloges:
                 "samples": len(sm), "source": "NVML"}
 
 
+def config_couche(args, ordo: str, parallelisme: str) -> dict:
+    """Config 1's `config` object, the same keys in both arms."""
+    return {
+        "workload": "config 1: one gpt-oss-120b MoE layer, batch 1, 128 experts, top-4, x bf16[2880], "
+                    "router f32 128x2880, SwiGLU alpha 1.702 limit 7, weights resident as .trc v1.2 parts",
+        "experts": args.experts, "k": args.k, "n_delta": args.n_delta, "n_codes": args.n_codes,
+        "schedule": ordo, "l2": "flushed between steps (256 MB written)", "parallelism": parallelisme,
+    }
+
+
+def entrees_couche(args, C0: int, R2: int, rang_: int = 0):
+    """The steps' inputs, the same draws in both arms: x f32 values already rounded to bf16
+    ([steps][C0]) and the residuals ([steps][R2])."""
+    import numpy as np
+
+    rng = np.random.default_rng(args.graine + rang_)
+    n_pas = args.warmup + args.steps
+    xs = rng.standard_normal((n_pas, C0)).astype(np.float32)
+    res0 = rng.standard_normal((n_pas, R2)).astype(np.float32)
+    u = xs.view(np.uint32).astype(np.uint64)
+    xs = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+    return xs, res0
+
+
 def construire_couche(args):
     import troncons_b200 as T
     import troncons_b200.synth as S
@@ -223,11 +247,11 @@ def notre_bras(args):
     cc = CoucheCarte(c, k=args.k, brut=False, n_delta=args.n_delta, n_codes=args.n_codes,
                      recouvrement=not args.sequentiel)
     n_pas = args.warmup + args.steps
-    rng = np.random.default_rng(args.graine + r)
-    xs = torch.from_numpy(rng.standard_normal((n_pas, c.dims.colonnes[0])).astype(np.float32)).to(torch.bfloat16)
+    xs_np, res_np = entrees_couche(args, c.dims.colonnes[0], c.dims.lignes[2], r)
+    xs = torch.from_numpy(xs_np).to(torch.bfloat16)  # exact: the values are bf16 already
     xs_dev = xs.cuda()
     x_hote = xs.pin_memory()
-    res0 = torch.from_numpy(rng.standard_normal((n_pas, c.dims.lignes[2])).astype(np.float32))
+    res0 = torch.from_numpy(res_np)
     res_hote = res0.pin_memory()
     res_sortie = torch.empty_like(res_hote).pin_memory()
     residu = torch.empty(c.dims.lignes[2], dtype=torch.float32, device="cuda")
@@ -340,14 +364,7 @@ def notre_bras(args):
         "vs_baseline": None,
         "dtype": "u8",
         "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
-        "config": {
-            "workload": "config 1: one gpt-oss-120b MoE layer, batch 1, 128 experts, top-4, x bf16[2880], "
-                        "router f32 128x2880, SwiGLU alpha 1.702 limit 7, weights resident as .trc v1.2 parts",
-            "experts": args.experts, "k": args.k, "n_delta": args.n_delta, "n_codes": args.n_codes,
-            "schedule": ordo,
-            "l2": "flushed between steps (256 MB written)", "bytes_per_step": round(octets / args.steps),
-            "parallelism": f"replicas x{w}",
-        },
+        "config": dict(config_couche(args, ordo, f"replicas x{w}"), bytes_per_step=round(octets / args.steps)),
         "e2e": {"value": round(w * octets / (t_e2e_ms * 1e-3) / 1e9, 2), "unit": UNITE,
                 "h2d_bytes_per_step": 2 * c.dims.colonnes[0] + 4 * c.dims.lignes[2],
                 "d2h_bytes_per_step": 4 * c.dims.lignes[2]},
@@ -372,6 +389,7 @@ def notre_bras(args):
     }
     if r == 0 and w == 1 and not args.no_cpu_baseline:
         ligne["cpu_baseline"] = base_cpu(c, args, bornes_s=12.0)
+        ligne["config0"] = config0_cpu(c.parties, c.luts, list(c.dims.lignes), list(c.dims.colonnes))
     if w == 1 and not args.sans_modele:
         # The headline metric's second half: the whole gpt-oss-120b decode step (config 2).
         del cc, c
@@ -648,68 +666,113 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
             "generation_s": round(t_gen, 1), "context_s": round(t_ctx, 1)}
 
 
-def base_cpu(c, args, bornes_s: float, pas_min: int = 3):
-    """The reference's path on host cores (oracle/couche_cpu.c), all cores, a bounded sample."""
-    import numpy as np
-
-    import oracle as O
-
-    rng = np.random.default_rng(args.graine)
-    n_fils = os.cpu_count() or 1
-    octets, t, n = 0, 0.0, 0
-    while n < pas_min or t < bornes_s:
-        x = rng.standard_normal(c.dims.colonnes[0]).astype(np.float32)
-        r0 = rng.standard_normal(c.dims.lignes[2]).astype(np.float32)
-        t0 = time.perf_counter()
-        _, idx, _ = O.couche_moe_cpu(c.parties, c.luts, c.dims.lignes, c.dims.colonnes, c.wr, c.br, x, args.k, r0, n_fils)
-        t += time.perf_counter() - t0
-        octets += octets_pas(c, idx, args.k)
-        n += 1
-        if n >= 200:
-            break
-    cpu = ""
+def modele_cpu() -> str:
     try:
         with open("/proc/cpuinfo") as f:
-            cpu = next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), "")
+            return next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), "")
     except Exception:
-        pass
-    return {"value": round(octets / t / 1e9, 3), "unit": UNITE, "cores": n_fils, "kind": "port",
-            "sample": f"{n} layer steps (router, decode of the 4 routed experts, GEMVs, SwiGLU, combine), "
-                      f"{round(t, 1)} s; CPU: {cpu}"}
+        return ""
+
+
+def octets_pas_parties(parties, idx, k, E, C, R2):
+    """octets_pas for a list of parts (the reference arm has no product layer object)."""
+    utiles = sum(int.from_bytes(parties[int(e)][12:16], "little") for e in idx[:k])
+    return utiles + 4 * E * C + 4 * E + 3 * 4 * 4 * 4096 + 2 * C + 2 * 4 * R2
+
+
+def pas_cpu(parties, luts, lignes, colonnes, wr, br, args, bornes_s: float, pas_min: int, n_pas: int = 0):
+    """The reference's path on host cores (oracle/couche_cpu.c: router, decode of the routed
+    experts, GEMVs, SwiGLU, combine), all threads, on the bench's bf16 inputs: (seconds, bytes,
+    steps). n_pas: exactly that many steps after args.warmup; else at least pas_min steps and
+    bornes_s seconds (at most 200)."""
+    import oracle as O
+
+    n_fils = os.cpu_count() or 1
+    total = n_pas + args.warmup if n_pas else 200 + args.warmup
+    xs, res0 = entrees_couche(args, colonnes[0], lignes[2])
+    t, octets, n = 0.0, 0, 0
+    for s in range(total):
+        i = s % len(xs)
+        t0 = time.perf_counter()
+        _, idx, _ = O.couche_moe_cpu(parties, luts, lignes, colonnes, wr, br, xs[i], args.k, res0[i], n_fils)
+        dt = time.perf_counter() - t0
+        if s < args.warmup:
+            continue
+        t += dt
+        octets += octets_pas_parties(parties, idx, args.k, len(parties), colonnes[0], lignes[2])
+        n += 1
+        if not n_pas and n >= pas_min and t >= bornes_s:
+            break
+    return t, octets, n
+
+
+def base_cpu(c, args, bornes_s: float, pas_min: int = 3):
+    """cpu_baseline of the GPU arm's line: pas_cpu on the same parts, a bounded sample."""
+    t, octets, n = pas_cpu(c.parties, c.luts, list(c.dims.lignes), list(c.dims.colonnes), c.wr, c.br, args, bornes_s,
+                           pas_min)
+    return {"value": round(octets / t / 1e9, 3), "unit": UNITE, "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{n} layer steps on the bench's bf16 inputs (router, decode of the 4 routed experts, GEMVs, "
+                      f"SwiGLU, combine), {round(t, 1)} s; CPU: {modele_cpu()}"}
+
+
+def config0_cpu(parties, luts, lignes, colonnes, bornes_s: float = 6.0) -> dict:
+    """Config 0: the reference's CPU decoder (decoder_avec per tile, decoder_matrice_v10 per
+    matrix, restated in oracle/couche_cpu.c) on one gate + up pair (matrices 0 and 1 of expert 0),
+    parallel over (matrix, tile) on every host thread; decoded GB/s = 2 x (16 nb + nb) bytes of
+    MXFP4 codes and scales per pair (8,812,800 B for 2880 x 2880)."""
+    import oracle as O
+
+    n_fils = os.cpu_count() or 1
+    decodes = sum(17 * lignes[j] * (colonnes[j] // 32) for j in (0, 1))
+    lus = 0
+    p = parties[0]
+    nf = int.from_bytes(p[10:12], "little")
+    for i in range(nf):
+        d = p[64 + 16 * i:80 + 16 * i]
+        if d[0] in (0x03, 0x04) and d[1] in (0, 1):
+            lus += int.from_bytes(d[8:12], "little")
+    O.decoder_matrices_cpu(p, luts, lignes, colonnes, (0, 1), n_fils)  # warm-up
+    t, n = 0.0, 0
+    while n < 3 or t < bornes_s:
+        t0 = time.perf_counter()
+        O.decoder_matrices_cpu(p, luts, lignes, colonnes, (0, 1), n_fils)
+        t += time.perf_counter() - t0
+        n += 1
+    return {"metric": "decoded GB/s on host cores (config 0: one gate+up pair, .trc v1.2)",
+            "value": round(n * decodes / t / 1e9, 3), "unit": "GB/s", "decoded_bytes_per_pair": decodes,
+            "compressed_bytes_per_pair": lus, "passes": n, "seconds": round(t, 2), "cores": n_fils,
+            "nproc": os.cpu_count(), "cpu": modele_cpu(), "kind": "port",
+            "source": "oracle/couche_cpu.c orc_decoder_matrices_cpu (rans.rs:388-451, trc-codec/src/lib.rs:190-218)"}
 
 
 def bras_reference(args):
+    """The reference arm: the reference's CPU path (restated in oracle/) on host cores, on the
+    GPU arm's config-1 workload. Its layer is built by the oracle alone (oracle.CoucheOracle:
+    the same weights, tables and parts as the product's generator, byte for byte), so no product
+    library is loaded; x is the GPU arm's bf16 input."""
     r, w, _ = rang()
     if r != 0:
         return
-    c, t_gen = construire_couche(args)
-    import numpy as np
-
     import oracle as O
 
-    rng = np.random.default_rng(args.graine)
+    t0 = time.time()
+    d = [2880, 2880, 2880]
+    c = O.CoucheOracle(args.graine, d, d, args.experts, args.n_delta, args.n_codes)
+    t_gen = time.time() - t0
     n_fils = os.cpu_count() or 1
-    mesures = []
-    for s in range(args.warmup + args.steps):
-        x = rng.standard_normal(c.dims.colonnes[0]).astype(np.float32)
-        r0 = rng.standard_normal(c.dims.lignes[2]).astype(np.float32)
-        t0 = time.perf_counter()
-        _, idx, _ = O.couche_moe_cpu(c.parties, c.luts, c.dims.lignes, c.dims.colonnes, c.wr, c.br, x, args.k, r0, n_fils)
-        dt = time.perf_counter() - t0
-        if s >= args.warmup:
-            mesures.append((dt, octets_pas(c, idx, args.k)))
-    t = sum(m[0] for m in mesures)
-    v = round(sum(m[1] for m in mesures) / t / 1e9, 3)
+    t, octets, n = pas_cpu(c.parties, c.luts, c.lignes, c.colonnes, c.wr, c.br, args, 0.0, 0, n_pas=args.steps)
+    v = round(octets / t / 1e9, 3)
     ligne = {
         "impl": "reference", "metric": METRIQUE, "value": v, "unit": UNITE, "n_gpus": w, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * t / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
-        "config": {"workload": "config 1 (one MoE layer, batch 1, 128 experts, top-4) on host cores",
-                   "experts": args.experts, "k": args.k},
+        "config": dict(config_couche(args, "reference CPU path: decode then multiply, OpenMP over tiles and rows",
+                                     f"{n_fils} host threads"), bytes_per_step=round(octets / args.steps)),
         "cpu_baseline": {"value": v, "unit": UNITE, "cores": n_fils, "kind": "port",
-                         "sample": f"{args.steps} layer steps after {args.warmup} warm-up, {round(t, 2)} s"},
+                         "sample": f"{n} layer steps after {args.warmup} warm-up, {round(t, 2)} s; CPU: {modele_cpu()}"},
         "e2e": {"value": v, "unit": UNITE, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config0": config0_cpu(c.parties, c.luts, c.lignes, c.colonnes),
         "generation_s": round(t_gen, 1),
     }
     print(json.dumps(ligne), flush=True)

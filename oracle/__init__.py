@@ -41,7 +41,8 @@ class Bilan(C.Structure):
 
 def construire() -> None:
     """Builds liboracle.so (gcc) when it is missing or older than its sources."""
-    sources = [os.path.join(ICI, f) for f in ("trc_oracle.c", "ordre_b200.c", "couche_cpu.c")]
+    sources = [os.path.join(ICI, f) for f in ("trc_oracle.c", "ordre_b200.c", "couche_cpu.c", "attention_cpu.c",
+                                              "couche_synth.c")]
     if os.path.exists(_LIB) and all(os.path.getmtime(_LIB) >= os.path.getmtime(s) for s in sources):
         return
     subprocess.run(["make", "-C", ICI, "all"], check=True, capture_output=True)
@@ -80,6 +81,12 @@ def _charger() -> C.CDLL:
         "ord_gemv_f32": (None, [PF, PF, PF, C.c_uint32, C.c_uint32, PF]),
         "orc_couche_moe_cpu": (C.c_int, [C.POINTER(P8), C.POINTER(C.c_size_t), C.c_uint32, P32, P32, P32,
                                          PF, PF, PF, C.c_uint32, PF, P32, PF, C.c_int]),
+        "orc_decoder_matrices_cpu": (C.c_int, [P8, C.c_size_t, P32, P32, P32, C.c_uint32, P32, C.POINTER(P8),
+                                               C.POINTER(P8), C.c_int]),
+        "orc_synth_matrices": (C.c_int, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P8, PF, C.c_int]),
+        "orc_comptes_couche": (None, [C.c_void_p * 3, P32, P32, C.c_uint32, C.c_int, P64]),
+        "orc_coder_couche": (None, [C.c_void_p * 3, C.c_void_p * 3, P32, P32, C.c_uint32, C.c_uint32, P16, C.c_int,
+                                    C.c_uint32, C.c_uint32, P8, C.c_size_t, P64]),
     }
     for nom, (res, args) in sig.items():
         f = getattr(lib, nom)
@@ -303,6 +310,25 @@ def couche_moe_cpu(parties, luts, lignes, colonnes, Wr, br, x, k: int, residu, n
     return res, idx, w
 
 
+def decoder_matrices_cpu(partie: bytes, luts, lignes, colonnes, mats=(0, 1), n_fils: int = 0):
+    """Config 0's CPU decode of matrices `mats` of one part, parallel over (matrix, tile) on
+    `n_fils` host threads (0: all): [(codes uint8[16 R B], scales uint8[R B])]."""
+    b = np.frombuffer(partie, np.uint8)
+    l = np.ascontiguousarray(luts, dtype=np.uint32).reshape(-1)
+    lg = np.array(list(lignes), np.uint32)
+    cl = np.array(list(colonnes), np.uint32)
+    ms = np.array(list(mats), np.uint32)
+    codes = [np.empty(16 * int(lg[j]) * (int(cl[j]) // 32), np.uint8) for j in mats]
+    ech = [np.empty(int(lg[j]) * (int(cl[j]) // 32), np.uint8) for j in mats]
+    pc = (P8 * len(mats))(*[p(a, P8) for a in codes])
+    pe = (P8 * len(mats))(*[p(a, P8) for a in ech])
+    r = lib.orc_decoder_matrices_cpu(p(b, P8), b.size, p(l, P32), p(lg, P32), p(cl, P32), len(mats), p(ms, P32), pc,
+                                     pe, n_fils)
+    if r != 0:
+        raise ValueError(f"CPU decode failed ({r})")
+    return list(zip(codes, ech))
+
+
 # ---------------------------------------------------------------- attention side (passe.cuh)
 
 def f16(x) -> np.ndarray:
@@ -432,3 +458,59 @@ class Banc:
 def banc():
     """The reference bench's encoder (Banc), or None when oracle/_ref/libtrc_banc.so is absent."""
     return Banc(_BANC) if os.path.exists(_BANC) else None
+
+
+# ---------------------------------------------------------------- a synthetic layer on host cores
+
+def synth_matrices(graine: int, lignes: int, colonnes: int, n: int, premier: int = 0, fils: int = 0):
+    """The bench workload's MXFP4 matrices premier .. premier + n - 1 of `graine` (blocs
+    uint8[n, R*B*17], biais float32[n, R]), drawn by the oracle (oracle/couche_synth.c)."""
+    B = colonnes // 32
+    blocs = np.empty((n, lignes * B * 17), np.uint8)
+    biais = np.empty((n, lignes), np.float32)
+    if lib.orc_synth_matrices(graine, lignes, colonnes, premier, n, p(blocs, P8), p(biais, PF), fils) != 0:
+        raise ValueError("synthetic generation refused its arguments")
+    return blocs, biais
+
+
+class CoucheOracle:
+    """A seeded MoE layer built with the oracle alone (no product library): its experts' blocks
+    and biases, the layer's frequency tables and LUTs (u32[3][4][4096]), each expert's level-0
+    v1.2 part, and the router (f32 [E][C] weights N(0, 0.02), zero biases). The same seeds give
+    the same layer as the product's troncons_b200.synth.couche, part for part."""
+
+    def __init__(self, graine: int, lignes, colonnes, experts: int, n_delta: int = 256, n_codes: int = 256,
+                 canonique: bool = True):
+        self.lignes, self.colonnes, self.experts = list(lignes), list(colonnes), experts
+        self.blocs, self.biais = [], []
+        for j in range(3):
+            b, bi = synth_matrices(graine * 7 + j, self.lignes[j], self.colonnes[j], experts)
+            self.blocs.append(b)
+            self.biais.append(bi)
+        lg = np.array(self.lignes, np.uint32)
+        cl = np.array(self.colonnes, np.uint32)
+        pb = (C.c_void_p * 3)(*[b.ctypes.data for b in self.blocs])
+        pbi = (C.c_void_p * 3)(*[b.ctypes.data for b in self.biais])
+        comptes = np.zeros(3 * 4 * 256, np.uint64)
+        lib.orc_comptes_couche(pb, p(lg, P32), p(cl, P32), experts, int(canonique), p(comptes, P64))
+        self.freqs = np.stack([table_depuis_comptes(comptes[256 * i:256 * (i + 1)]) for i in range(12)]).reshape(3, 4, 256)
+        self.luts = np.concatenate([lut(self.freqs[j, t]) for j in range(3) for t in range(4)])
+        cap = 2 * sum(b.shape[1] for b in self.blocs) + 4 * sum(b.shape[1] for b in self.biais) + (1 << 16)
+        sorties = np.zeros((experts, cap), np.uint8)
+        octets = np.zeros(experts, np.uint64)
+        f = np.ascontiguousarray(self.freqs, np.uint16).reshape(-1)
+        lib.orc_coder_couche(pb, pbi, p(lg, P32), p(cl, P32), experts, 0, p(f, P16), int(canonique), n_delta, n_codes,
+                             p(sorties, P8), cap, p(octets, P64))
+        if (octets == 0).any():
+            raise ValueError(f"experts {np.where(octets == 0)[0][:8].tolist()}: encoding failed")
+        self.parties = [sorties[x, :int(octets[x])].tobytes() for x in range(experts)]
+        rng = np.random.default_rng(graine)
+        self.wr = (rng.standard_normal((experts, self.colonnes[0])) * 0.02).astype(np.float32)
+        self.br = np.zeros(experts, np.float32)
+
+
+def bf16(x) -> np.ndarray:
+    """f32 values rounded to bf16 (nearest, ties to even), kept as f32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)

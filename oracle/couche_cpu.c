@@ -181,3 +181,76 @@ int orc_couche_moe_cpu(const uint8_t* const* parties, const size_t* tailles, uin
     free(s);
     return faute ? -4 : 0;
 }
+
+/* Config 0's CPU decode: matrices mats[0 .. n - 1] of one expert's level-0 part decoded into
+ * codes[i] (16 R B bytes, canonical when v1.2) and echelles[i] (R B E8M0 bytes), parallel over
+ * (matrix, rANS tile) on every host thread: the DELTA tiles of all matrices, then the scales,
+ * then the CODES_CTX tiles (trc-codec decoder_matrice_v10, lib.rs:190-218, with rans.rs:388-451
+ * per tile). Returns 0, or a negative value on a format error or a corrupted stream. */
+int orc_decoder_matrices_cpu(const uint8_t* partie, size_t taille, const uint32_t* luts, const uint32_t* lignes,
+                             const uint32_t* colonnes, uint32_t n, const uint32_t* mats, uint8_t* const* codes,
+                             uint8_t* const* echelles, int n_fils) {
+    if (n == 0 || n > 3) return -1;
+    if (n_fils > 0) omp_set_num_threads(n_fils);
+    matrice_cpu m[3];
+    for (uint32_t a = 0; a < n; ++a) {
+        const uint8_t j = (uint8_t)mats[a];
+        uint32_t d[4], l[4], p[4];
+        for (uint8_t s = 1; s <= 4; ++s)
+            if (orc_trouver_flux(partie, taille, s, j, &d[s - 1], &l[s - 1], &p[s - 1]) != 0) return -2;
+        m[a].med = partie + d[0];
+        m[a].fd = partie + d[2];
+        m[a].ld = l[2];
+        m[a].fc = partie + d[3];
+        m[a].lc = l[3];
+        if (orc_flux_valide(m[a].fd, m[a].ld) || orc_flux_valide(m[a].fc, m[a].lc)) return -3;
+        m[a].Pd = lu32c(m[a].fd);
+        m[a].Td = lu32c(m[a].fd + 8);
+        m[a].Pc = lu32c(m[a].fc);
+        m[a].Tc = lu32c(m[a].fc + 8);
+        if ((size_t)m[a].Pc < 16 * (size_t)lignes[j] * (colonnes[j] / 32)) return -3;
+    }
+    uint8_t* delta[3];
+    uint8_t* kappa[3];
+    uint8_t* tampon[3];
+    for (uint32_t a = 0; a < n; ++a) {
+        delta[a] = (uint8_t*)malloc(m[a].Pd);
+        kappa[a] = (uint8_t*)malloc(m[a].Pd);
+        tampon[a] = (uint8_t*)malloc(m[a].Pc);
+    }
+    uint32_t taches = 0;
+    for (uint32_t a = 0; a < n; ++a) taches += m[a].Td;
+    int faute = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(| : faute)
+    for (uint32_t t = 0; t < taches; ++t) {
+        uint32_t a = 0, r = t;
+        while (r >= m[a].Td) r -= m[a].Td, ++a;
+        orc_bilan bl;
+        orc_decoder_tuiles(m[a].fd, m[a].ld, NULL, 0, luts + (size_t)mats[a] * 4 * 4096, 1, r, r + 1, delta[a], &bl);
+        faute |= (bl.voies_hors_l || bl.tuiles_mots_faux) ? 1 : 0;
+    }
+    for (uint32_t a = 0; a < n; ++a) {
+        const uint32_t Bj = colonnes[mats[a]] / 32;
+        const size_t nbj = (size_t)lignes[mats[a]] * Bj;
+        for (size_t i = 0; i < m[a].Pd; ++i) kappa[a][i] = delta[a][i] < 128 ? 0 : (delta[a][i] == 128 ? 1 : 2);
+        for (size_t beta = 0; beta < nbj; ++beta) echelles[a][beta] = (uint8_t)(m[a].med[beta / Bj] + delta[a][beta] - 128);
+    }
+    taches = 0;
+    for (uint32_t a = 0; a < n; ++a) taches += m[a].Tc;
+#pragma omp parallel for schedule(dynamic, 1) reduction(| : faute)
+    for (uint32_t t = 0; t < taches; ++t) {
+        uint32_t a = 0, r = t;
+        while (r >= m[a].Tc) r -= m[a].Tc, ++a;
+        orc_bilan bl;
+        orc_decoder_tuiles(m[a].fc, m[a].lc, kappa[a], m[a].Pd, luts + (size_t)mats[a] * 4 * 4096 + 4096, 3, r, r + 1,
+                           tampon[a], &bl);
+        faute |= (bl.voies_hors_l || bl.tuiles_mots_faux) ? 1 : 0;
+    }
+    for (uint32_t a = 0; a < n; ++a) {
+        memcpy(codes[a], tampon[a], 16 * (size_t)lignes[mats[a]] * (colonnes[mats[a]] / 32));
+        free(delta[a]);
+        free(kappa[a]);
+        free(tampon[a]);
+    }
+    return faute ? -4 : 0;
+}
