@@ -46,6 +46,9 @@ def arguments(argv=None):
     a.add_argument("--n-delta", type=int, default=256, help="macro-steps per DELTA tile the parts are encoded with")
     a.add_argument("--n-codes", type=int, default=256, help="macro-steps per CODES_CTX tile")
     a.add_argument("--no-cpu-baseline", action="store_true")
+    a.add_argument("--sans-legs", action="store_true",
+                   help="skip config 1's other measurements (raw layer, DELTA decoded ahead, decode then multiply "
+                        "with ours and the reference's kernels, all experts at once)")
     a.add_argument("--sequentiel", action="store_true",
                    help="the sequential schedule (down decoded after SwiGLU, fused into its GEMV) instead of "
                         "the one that decodes down alongside gate/up")
@@ -195,12 +198,12 @@ def entrees_couche(args, C0: int, R2: int, rang_: int = 0):
     return xs, res0
 
 
-def construire_couche(args):
+def construire_couche(args, brut: bool = False):
     import troncons_b200 as T
     import troncons_b200.synth as S
 
     t0 = time.time()
-    c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=False, n_delta=args.n_delta,
+    c = S.couche(args.graine, T.DimsExpert.gpt_oss(), args.experts, brut=brut, n_delta=args.n_delta,
                  n_codes=args.n_codes)
     return c, time.time() - t0
 
@@ -243,8 +246,8 @@ def notre_bras(args):
     import troncons_b200 as T  # noqa: F401
     from troncons_b200.carte import CoucheCarte
 
-    c, t_gen = construire_couche(args)
-    cc = CoucheCarte(c, k=args.k, brut=False, n_delta=args.n_delta, n_codes=args.n_codes,
+    c, t_gen = construire_couche(args, brut=not args.sans_legs)
+    cc = CoucheCarte(c, k=args.k, brut=not args.sans_legs, n_delta=args.n_delta, n_codes=args.n_codes,
                      recouvrement=not args.sequentiel)
     n_pas = args.warmup + args.steps
     xs_np, res_np = entrees_couche(args, c.dims.colonnes[0], c.dims.lignes[2], r)
@@ -375,7 +378,7 @@ def notre_bras(args):
                                 "k_moe_codes_dense (gate/up CODES_CTX decoded into their GEMV, down CODES_CTX "
                                 "decoded alongside)"),
                      "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
-                     "peak_source": sorte_pic,
+                     "peak_source": sorte_pic, "frac_8tbs": round(atteint / 8000.0, 4),
                      # DRAM read + write bytes of that launch, from ncu on the same launch shape
                      # (4 routed experts of 2880 x 2880), summarised under profiles/.
                      "traffic": TRAFIC_CODES[ordo], "traffic_source": "ncu dram__bytes_read.sum + "
@@ -387,6 +390,10 @@ def notre_bras(args):
         "wall_s_timed_region": round(mur, 3),
         "generation_s": round(t_gen, 1),
     }
+    ligne["step_frac_of_peak"] = round(octets / (t_total_ms * 1e-3) / 1e9 / pic, 4)
+    ligne["step_frac_of_8tbs"] = round(octets / (t_total_ms * 1e-3) / 1e12 / 8.0, 4)
+    if w == 1 and not args.sans_legs:
+        ligne.update(legs_couche(args, c, cc, xs_dev, res_dev, idx, vidange, pic))
     if r == 0 and w == 1 and not args.no_cpu_baseline:
         ligne["cpu_baseline"] = base_cpu(c, args, bornes_s=12.0)
         ligne["config0"] = config0_cpu(c.parties, c.luts, list(c.dims.lignes), list(c.dims.colonnes))
@@ -405,6 +412,194 @@ def notre_bras(args):
         dist.destroy_process_group()
     if r == 0:
         print(json.dumps(ligne), flush=True)
+
+
+def octets_flux(p: bytes, sortes, matrices) -> int:
+    """Bytes of the streams of a part whose kind is in `sortes` and matrix in `matrices`."""
+    n = int.from_bytes(p[10:12], "little")
+    total = 0
+    for i in range(n):
+        d = p[64 + 16 * i:80 + 16 * i]
+        if d[0] in sortes and d[1] in matrices:
+            total += int.from_bytes(d[8:12], "little")
+    return total
+
+
+def chrono_etapes(etape, preparer, n_pas: int, warmup: int, vidange, graphe: bool = True):
+    """Device time (ms) of `etape()` per step, after `preparer(s)` set step s's inputs and L2
+    was flushed; the step is captured in a CUDA graph when `graphe`. Returns per-step times of
+    the n_pas - warmup timed steps."""
+    import torch
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    preparer(0)
+    for _ in range(2):
+        etape()
+    torch.cuda.synchronize()
+    g = None
+    if graphe:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            etape()
+        torch.cuda.synchronize()
+    t = []
+    for s in range(n_pas):
+        vidange.zero_()
+        preparer(s)
+        ev[0].record()
+        g.replay() if g is not None else etape()
+        ev[1].record()
+        torch.cuda.synchronize()
+        if s >= warmup:
+            t.append(ev[0].elapsed_time(ev[1]))
+    del g
+    return t
+
+
+def legs_couche(args, c, cc, xs_dev, res_dev, idx, vidange, pic: float) -> dict:
+    """The other measurements of config 1, on the same layer, inputs and routed experts, L2
+    flushed between steps (each a named object of the default line):
+    - raw_layer: the fused layer on the raw parts (k_moe_brut), with the roofline of its gate/up
+      launch (CODES_BRUTS + ECHELLES_BRUTES of gate and up: a pure HBM stream);
+    - delta_predecoded: the compressed layer with every expert's DELTA decoded once ahead
+      (trc_moe_predecoder_deltas), its bytes counted instead of the DELTA streams;
+    - decode_then_gemv: the reference's operator sequence (decoder_lot into slots, gemv_lot,
+      swiglu_oai, gemv_lot, combiner) on the step's routed experts, with this library's kernels
+      and with the reference's own kernels compiled for sm_100a (oracle/_ref, a reported
+      baseline like cpu_baseline), against the fused layer without its router;
+    - throughput_all_experts: every one of the layer's 128 experts active in one call (32
+      tokens x top-4, one activation per expert), the decode launches in throughput mode."""
+    import numpy as np
+    import torch
+
+    import troncons_b200 as T
+    from troncons_b200.carte import CoucheCarte
+
+    n_pas = args.warmup + args.steps
+    k = args.k
+    x_buf = torch.empty(c.dims.colonnes[0], dtype=torch.bfloat16, device="cuda")
+    residu = torch.empty(c.dims.lignes[2], dtype=torch.float32, device="cuda")
+
+    def prep(s):
+        x_buf.copy_(xs_dev[s])
+        residu.copy_(res_dev[s])
+
+    fixe = 4 * c.experts * c.dims.colonnes[0] + 4 * c.experts + 2 * c.dims.colonnes[0] + 8 * c.dims.lignes[2]
+    out = {}
+    steps = range(args.warmup, n_pas)
+
+    # -- raw parts
+    t = chrono_etapes(lambda: cc.couche(x_buf, residu, brute=True), prep, n_pas, args.warmup, vidange)
+    octets = sum(sum(int.from_bytes(c.parties_brutes[int(e)][12:16], "little") for e in idx[s]) + fixe for s in steps)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    ph = []
+    for s in range(n_pas):
+        vidange.zero_()
+        prep(s)
+        ev[0].record()
+        cc.couche(x_buf, residu, brute=True, evenements=[e.cuda_event for e in ev[1:7]])
+        torch.cuda.synchronize()
+        if s >= args.warmup:
+            ph.append(ev[2].elapsed_time(ev[3]))
+    brut_gu = sum(octets_flux(c.parties_brutes[int(e)], (0x05, 0x06), (0, 1)) for s in steps for e in idx[s])
+    ach = brut_gu / args.steps / (np.mean(ph) * 1e-3) / 1e9
+    out["raw_layer"] = {
+        "value": round(octets / (sum(t) * 1e-3) / 1e9, 2), "unit": UNITE, "ms_per_step": round(sum(t) / args.steps, 4),
+        "bytes_per_step": round(octets / args.steps),
+        "roofline": {"bound": "hbm", "kernel": "k_moe_brut (gate/up: CODES_BRUTS + ECHELLES_BRUTES of the routed experts)",
+                     "achieved": round(ach, 1), "peak": pic, "unit": "GB/s", "frac": round(ach / pic, 4),
+                     "frac_8tbs": round(ach / 8000.0, 4), "ms": round(float(np.mean(ph)), 4),
+                     "algorithmic_bytes_per_launch": round(brut_gu / args.steps)}}
+
+    # -- DELTA decoded ahead
+    cc.predecoder_deltas()
+    torch.cuda.synchronize()
+    assert (cc.controle_deltas == 0).all()
+    t = chrono_etapes(lambda: cc.couche(x_buf, residu), prep, n_pas, args.warmup, vidange)
+    octets = sum(sum(int.from_bytes(c.parties[int(e)][12:16], "little") - octets_flux(c.parties[int(e)], (0x03,), (0, 1, 2))
+                     for e in idx[s]) + k * sum(c.dims.lignes[j] * (c.dims.colonnes[j] // 32) for j in range(3)) + fixe
+                 for s in steps)
+    out["delta_predecoded"] = {
+        "value": round(octets / (sum(t) * 1e-3) / 1e9, 2), "unit": UNITE, "ms_per_step": round(sum(t) / args.steps, 4),
+        "bytes_per_step": round(octets / args.steps),
+        "note": "DELTA streams replaced by the decoded delta bytes (one per 32-block), decoded once at load: "
+                "99.5 MB per 128-expert layer resident"}
+    cc.deltas = None
+
+    # -- decode then multiply: ours and the reference's kernels, the fused layer without router
+    cc.preparer_decodee()
+    descs = [cc.descripteurs_decodee(idx[s]) for s in range(n_pas)]
+    cc.routeur(x_buf)
+    cour = [None]
+
+    def prep_d(s):
+        prep(s)
+        cour[0] = descs[s]
+
+    t_nous = chrono_etapes(lambda: cc.sequence_decodee(cour[0], x_buf, residu), prep_d, n_pas, args.warmup, vidange,
+                           graphe=False)
+    t_fus = chrono_etapes(lambda: cc.couche(x_buf, residu, routeur=False), prep, n_pas, args.warmup, vidange)
+    octets = sum(sum(int.from_bytes(c.parties[int(e)][12:16], "little") for e in idx[s]) + fixe for s in steps)
+    d = {"fused_layer_ms": round(sum(t_fus) / args.steps, 4), "ours_ms": round(sum(t_nous) / args.steps, 4),
+         "ours_value": round(octets / (sum(t_nous) * 1e-3) / 1e9, 2),
+         "fused_value": round(octets / (sum(t_fus) * 1e-3) / 1e9, 2), "unit": UNITE,
+         "note": "the step's routed experts known on the host; no router in either time"}
+    try:
+        import oracle as O
+
+        ref = O.ref()
+    except Exception:
+        ref = None
+    if ref is not None:
+        dims6 = np.array(list(c.dims.lignes) + list(c.dims.colonnes), np.uint32)
+        f = torch.cuda.current_stream().cuda_stream
+        p6 = dims6.ctypes.data_as(O.P32)
+
+        def ref_seq():
+            dd, dg, ddn = cour[0]
+            cc.x32.copy_(x_buf.float())
+            assert ref.ref_decoder_lot(dd.data_ptr(), k, p6, f) == 0
+            assert ref.ref_gemv_lot(dg.data_ptr(), 2 * k, cc.R0, f) == 0
+            assert ref.ref_swiglu(cc.g.data_ptr(), cc.u.data_ptr(), cc.h.data_ptr(), k * cc.R0, f) == 0
+            assert ref.ref_gemv_lot(ddn.data_ptr(), k, cc.R2, f) == 0
+            assert ref.ref_combiner(residu.data_ptr(), cc.s.data_ptr(), cc.R2, cc.poids.data_ptr(), k, cc.R2, f) == 0
+
+        t_ref = chrono_etapes(ref_seq, prep_d, n_pas, args.warmup, vidange, graphe=False)
+        d["reference_kernels_ms"] = round(sum(t_ref) / args.steps, 4)
+        d["reference_kernels_value"] = round(octets / (sum(t_ref) * 1e-3) / 1e9, 2)
+        d["reference_kernels"] = "trc-noyaux/noyaux/noyaux.cu compiled unchanged for sm_100a (oracle/_ref)"
+    else:
+        d["reference_kernels"] = "unavailable: oracle/_ref/libtrc_ref.so not built"
+    out["decode_then_gemv"] = d
+
+    # -- throughput mode: the 128 experts active at once
+    E = c.experts
+    if E % k == 0 and E // k <= 128:
+        jt = E // k
+        ct = CoucheCarte(c, k=k, brut=False, jetons=jt)
+        perm = np.random.default_rng(args.graine).permutation(E).astype(np.int32)
+        ct.idx.copy_(torch.from_numpy(perm))
+        ct.poids.fill_(1.0 / k)
+        xt = torch.zeros(jt, c.dims.colonnes[0], dtype=torch.bfloat16, device="cuda")
+        rt = torch.zeros(jt, c.dims.lignes[2], dtype=torch.float32, device="cuda")
+
+        def prep_t(s):
+            xt.copy_(xs_dev[s].expand(jt, -1))
+            rt.copy_(res_dev[s].expand(jt, -1))
+
+        t = chrono_etapes(lambda: ct.couche(xt, rt, routeur=False), prep_t, n_pas, args.warmup, vidange)
+        assert (ct.controle == 0).all()
+        tout = sum(int.from_bytes(p[12:16], "little") for p in c.parties)
+        codes = sum(octets_flux(p, (0x04,), (0, 1, 2)) for p in c.parties)
+        ms = sum(t) / args.steps
+        out["throughput_all_experts"] = {
+            "value": round(tout / (ms * 1e-3) / 1e9, 2), "unit": UNITE, "ms_per_step": round(ms, 4),
+            "activations": E, "bytes_per_step": tout, "codes_ctx_bytes": codes,
+            "frac": round(tout / (ms * 1e-3) / 1e9 / pic, 4), "frac_8tbs": round(tout / (ms * 1e-3) / 1e12 / 8.0, 4),
+            "note": "every expert of the layer decoded and multiplied in one call (sequential schedule, one warp "
+                    "per tile): where the rANS decode chain sits when the GPU is full of tiles"}
+        del ct
+    return out
 
 
 def couche_ep(args, c, r: int, w: int):

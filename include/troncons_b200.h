@@ -515,6 +515,9 @@ typedef struct trc_moe_couche {
                                        activations (0 when none), for a sum across GPUs; 0: residu += */
     const struct trc_echange_pairs* echange; /* host pointer or NULL: the combine's sum across
                                        GPUs done by the combine kernel itself over peer memory */
+    const uint8_t* deltas;          /* device or NULL: the delta bytes of every expert of the layer,
+                                       decoded ahead by trc_moe_predecoder_deltas (then the layer
+                                       skips its DELTA phase; same results); ignored when brut */
 } trc_moe_couche;
 
 /* The combine's exchange between the GPUs of an expert-parallel layer, in the combine kernel:
@@ -567,6 +570,21 @@ uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t ex
  * partiel (each position's share of the sum written alone) are those of the fused layer. The
  * controle of an activation receives its expert's decode counters. */
 int trc_moe_couche_par_flux(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);
+
+/* New: bytes of a layer's delta bytes decoded ahead (trc_moe_predecoder_deltas): one byte per
+ * 32-block of each matrix and expert, 256-aligned per matrix (3 x 259,200 x 128 = 99.5 MB for a
+ * gpt-oss-120b layer of 128 experts, against about 76.8 MB of DELTA streams). */
+uint64_t trc_moe_deltas_octets(const trc_dims_expert* dims, uint32_t experts);
+
+/* New: decodes the DELTA stream of every matrix of every expert of a layer (the first half of
+ * trc-codec's decoder_matrice_v10, lib.rs:190-212, as the fused layer's DELTA phase does it)
+ * into `deltas` (trc_moe_deltas_octets bytes): the weights' scale offsets, which need no
+ * activation, decoded once at load instead of at every step. Only parties, parties_octets,
+ * experts, luts, dims and n_delta of `couche` are read; controle: device u32[4 x experts],
+ * zeroed by the caller, the counters of each expert's DELTA streams. Passing the result as
+ * couche->deltas removes the DELTA phase from trc_moe_couche_fusionnee. Async on the stream. */
+int trc_moe_predecoder_deltas(const trc_moe_couche* couche, uint8_t* deltas, uint64_t deltas_octets,
+                              uint32_t* controle, void* flux);
 
 /* trc_moe_couche_fusionnee, recording evenements[0..5] (cudaEvent_t, each may be NULL) on the
  * stream: before the DELTA phase, after it, after gate/up, after SwiGLU, after down, after the

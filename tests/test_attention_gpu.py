@@ -2,7 +2,9 @@
 and the sliding window) through the C-ABI.
 
 - against the reference's own kernels on the same GPU (oracle/_ref, passe.cuh compiled for
-  sm_100a): bit for bit, every kernel (the same arithmetic order and the same CUDA math);
+  sm_100a): bit for bit for the Q8_0 GEMV, RMSNorm, rotation and KV write (the same arithmetic
+  order and the same CUDA math); within 1e-5 of max|out| for the attention, which is split over
+  positions and merged in a cluster (another order of the same f32 sums);
 - against the CPU restatement (oracle/attention_cpu.c): bit for bit for the Q8_0 GEMV, RMSNorm
   and the KV write; the YaRN rotation and the attention call the host's libm (pow, log, sin,
   cos, expf), so within 2e-7 relative for the rotation and 1e-5 of max|out| for attention (the
@@ -145,19 +147,29 @@ def test_ecrire_kv(noyaux):
     assert (hk[129 * dkv:] == np.float16(k).view(np.uint16)).all()
 
 
-@pytest.mark.parametrize("position,fenetre", [(0, 128), (200, 128), (1000, 128), (5, 0), (2999, 0)])
-def test_attention(noyaux, position, fenetre):
+@pytest.mark.parametrize("position,fenetre,tetes,tetes_kv", [
+    (0, 128, 64, 8), (200, 128, 64, 8), (1000, 128, 64, 8), (5, 0, 64, 8), (2999, 0, 64, 8),
+    (31, 0, 64, 8), (32, 0, 64, 8), (511, 0, 64, 8), (4095, 0, 64, 8), (8191, 0, 64, 8),
+    (700, 0, 8, 8), (700, 0, 64, 1), (130, 128, 16, 4)])
+def test_attention(noyaux, position, fenetre, tetes, tetes_kv):
+    """Split over positions in slices (1 to 16 per key/value head, each staged 128 positions at a
+    time with the online rescale) and merged in a cluster: within 1e-5 of max|out| of the oracle
+    (the reference's single-pass order restated) and of the reference's own kernel, for 1 to
+    8,192 positions, the ring of a sliding layer, and 1, 4, 8 and 64 query heads per key/value
+    head."""
     import ctypes as C
 
     import troncons_b200 as T
 
-    rng = np.random.default_rng(position + fenetre)
+    rng = np.random.default_rng(position + fenetre + tetes)
     p = T.ParamsAttention.gpt_oss(position, fenetre)
+    p.tetes, p.tetes_kv = tetes, tetes_kv
+    dkv = 64 * tetes_kv
     cases = fenetre if fenetre else position + 1
-    ck, cv = _cache(rng, cases, 512)
-    q = rng.standard_normal(64 * 64).astype(np.float32)
-    puits = rng.standard_normal(64).astype(np.float32)
-    sortie = torch.zeros(64 * 64, dtype=torch.float32, device="cuda")
+    ck, cv = _cache(rng, cases, dkv)
+    q = rng.standard_normal(tetes * 64).astype(np.float32)
+    puits = rng.standard_normal(tetes).astype(np.float32)
+    sortie = torch.zeros(tetes * 64, dtype=torch.float32, device="cuda")
     qd, ckd, cvd, pd = t(q), t(ck.view(np.int16)), t(cv.view(np.int16)), t(puits)
     noyaux.attention(qd, ckd, cvd, pd, sortie, p)
     torch.cuda.synchronize()
@@ -165,9 +177,10 @@ def test_attention(noyaux, position, fenetre):
     att = O.attention(q, ck.reshape(-1), cv.reshape(-1), puits, p)
     assert np.abs(nous - att).max() <= 1e-5 * max(1.0, np.abs(att).max())
     ref = O.ref()
-    if ref is not None:
+    if ref is not None and tetes == 64 and tetes_kv == 8:
         sr = torch.zeros_like(sortie)
         assert ref.ref_attention(qd.data_ptr(), ckd.data_ptr(), cvd.data_ptr(), pd.data_ptr(), sr.data_ptr(),
                                  C.addressof(p), torch.cuda.current_stream().cuda_stream) == 0
         torch.cuda.synchronize()
-        assert torch.equal(sr.view(torch.int32), sortie.view(torch.int32))
+        r = sr.cpu().numpy()
+        assert np.abs(nous - r).max() <= 1e-5 * max(1.0, np.abs(r).max())

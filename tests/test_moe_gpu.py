@@ -8,6 +8,8 @@
   gate/up, or after SwiGLU), the fused raw layer and the decode-then-multiply sequence give the
   same bits, step after step;
 - the layer against the CPU port of the path within a stated tolerance."""
+import ctypes as C
+
 import numpy as np
 import pytest
 
@@ -185,3 +187,45 @@ def test_ordonnancements_au_bit(couche_gpt_oss, jetons, n_codes):
         torch.cuda.synchronize()
         assert (cs.controle == 0).all() and (cr.controle == 0).all()
         assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+@pytest.mark.parametrize("nom,k,jetons,recouvrement,tenus", [
+    ("couche_petite", 4, 1, True, None), ("couche_gpt_oss", 4, 1, True, None), ("couche_gpt_oss", 4, 1, False, None),
+    ("couche_gpt_oss", 8, 3, True, None), ("couche_gpt_oss", 4, 2, True, (2, 6))])
+def test_deltas_predecodes_au_bit(nom, k, jetons, recouvrement, tenus, request):
+    """Every expert's DELTA decoded once (trc_moe_predecoder_deltas): the bytes are the oracle's
+    deltas (scale - median + 128 per block, trc-codec/src/lib.rs:348-373) and the layer that reads
+    them instead of decoding DELTA gives the same residual bits as the one that decodes it, in
+    both schedules, for token batches and an expert-parallel share (partial combine)."""
+    import troncons_b200 as T
+    from troncons_b200.carte import CoucheCarte
+
+    c = request.getfixturevalue(nom)
+    d = c.dims
+    a = CoucheCarte(c, k=k, brut=False, jetons=jetons, recouvrement=recouvrement, tenus=tenus)
+    p = CoucheCarte(c, k=k, brut=False, jetons=jetons, recouvrement=recouvrement, tenus=tenus, deltas_predecodes=True)
+    torch.cuda.synchronize()
+    assert (p.controle_deltas == 0).all()
+    # The predecoded bytes: matrix j of expert e at ek[j] + e * nb_j, ek 256-aligned per matrix.
+    dl = p.deltas.cpu().numpy()
+    off = 0
+    for j in range(3):
+        nb = d.lignes[j] * (d.colonnes[j] // 32)
+        for e in (0, c.experts - 1):
+            _, delta, _ = O.preparer_matrice(c.blocs[j][e], d.lignes[j], d.colonnes[j] // 32, True)
+            assert (dl[off + e * nb:off + (e + 1) * nb] == delta[:nb]).all(), f"matrix {j} expert {e}"
+        off = (off + nb * c.experts + 255) // 256 * 256
+    assert int(T.lib.trc_moe_deltas_octets(C.byref(d), c.experts)) == off
+    rng = np.random.default_rng(9 + k + jetons)
+    for _ in range(3):
+        x = torch.from_numpy(rng.standard_normal((jetons, d.colonnes[0])).astype(np.float32)).to(torch.bfloat16).cuda()
+        r0 = torch.from_numpy(rng.standard_normal((jetons, d.lignes[2])).astype(np.float32)).cuda()
+        ra, rp = r0.clone(), r0.clone()
+        a.controle.zero_()
+        p.controle.zero_()
+        a.couche(x, ra, partiel=tenus is not None)
+        p.couche(x, rp, partiel=tenus is not None)
+        torch.cuda.synchronize()
+        assert (a.controle == 0).all() and (p.controle == 0).all()
+        assert torch.equal(a.idx, p.idx)
+        assert torch.equal(ra.view(torch.int32), rp.view(torch.int32))

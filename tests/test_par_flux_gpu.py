@@ -87,3 +87,33 @@ def test_par_flux_sur_une_part_partielle(couche_petite, jetons, tenus):
         idx = cc.idx.cpu().numpy().reshape(jetons, 4)
         sans = ~((idx >= tenus[0]) & (idx < tenus[1])).any(1)
         assert (rp[torch.from_numpy(sans).cuda()] == 0).all()
+
+
+@pytest.mark.parametrize("nom,k,jetons", [("couche_petite", 4, 12), ("couche_petite", 8, 5), ("couche_gpt_oss", 4, 6)])
+def test_par_flux_contre_l_oracle(nom, k, jetons, request):
+    """A batch of positions par flux against the oracle's CPU port of the layer, position by
+    position (oracle/couche_cpu.c: router, the reference CPU decoder, the GEMVs, SwiGLU and the
+    combine): the same routed experts, and every position's residual within 1e-4 of its max|r|
+    (the port sums the GEMV in another f32 order). Independent of the fused CUDA layer."""
+    import oracle as O
+    from troncons_b200.carte import CoucheCarte
+
+    c = request.getfixturevalue(nom)
+    cc = CoucheCarte(c, k=k, brut=False, jetons=jetons)
+    rng = np.random.default_rng(41 + jetons + k)
+    d, R2 = c.dims.colonnes[0], c.dims.lignes[2]
+    xf = rng.standard_normal((jetons, d)).astype(np.float32)
+    x = torch.from_numpy(xf).to(torch.bfloat16)
+    r0 = rng.standard_normal((jetons, R2)).astype(np.float32)
+    r = torch.from_numpy(r0.copy()).cuda()
+    cc.controle.zero_()
+    cc.couche_par_flux(x.cuda(), r)
+    torch.cuda.synchronize()
+    assert (cc.controle == 0).all()
+    rg = r.cpu().numpy()
+    idx_gpu = cc.idx.cpu().numpy().reshape(jetons, k).astype(np.uint32)
+    xb = x.float().numpy()
+    for j in range(jetons):
+        res, idx, _ = O.couche_moe_cpu(c.parties, c.luts, c.dims.lignes, c.dims.colonnes, c.wr, c.br, xb[j], k, r0[j])
+        assert (idx_gpu[j] == idx).all(), f"position {j}: other experts routed"
+        assert np.abs(rg[j] - res).max() <= 1e-4 * max(1.0, np.abs(res).max()), f"position {j}"

@@ -107,7 +107,7 @@ class MoeCouche(C.Structure):
                 ("x", C.c_void_p), ("x_bf16", C.c_uint32), ("brut", C.c_uint32), ("residu", C.c_void_p),
                 ("controle", C.c_void_p), ("n_delta", C.c_uint32), ("n_codes", C.c_uint32),
                 ("jetons", C.c_uint32), ("expert_debut", C.c_uint32), ("expert_fin", C.c_uint32),
-                ("partiel", C.c_uint32), ("echange", C.c_void_p)]
+                ("partiel", C.c_uint32), ("echange", C.c_void_p), ("deltas", C.c_void_p)]
 
 
 def _charger() -> C.CDLL:
@@ -137,6 +137,8 @@ def _charger() -> C.CDLL:
         "trc_coder_partie_brute": (i64, [vp, vp, pd, C.c_uint16, C.c_uint16, vp, sz, C.POINTER(u32)]),
         "trc_synth_matrices": (i32, [u64, u32, u32, u32, u32, vp, vp, i32]),
         "trc_moe_espace_octets": (u64, [pd, u32]),
+        "trc_moe_deltas_octets": (u64, [pd, u32]),
+        "trc_moe_predecoder_deltas": (i32, [vp, vp, u64, vp, vp]),
         "trc_moe_espace_recouvrant_octets": (u64, [pd, u32]),
         "trc_moe_par_flux_espace_octets": (u64, [pd, u32, u32]),
         "trc_moe_couche_par_flux": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),

@@ -30,10 +30,12 @@ class CoucheCarte:
     expert-parallel share: the other experts' parts may be None and are never read); None: all.
     `recouvrement`: a workspace large enough for the fastest schedule (decode-only launches whose
     GEMVs follow, up to 32 activations); else the sequential schedule's. `espace`: a workspace of
-    exactly that many bytes instead (the schedule follows from its size)."""
+    exactly that many bytes instead (the schedule follows from its size). `deltas_predecodes`:
+    decode every expert's DELTA streams once here, and skip that phase at each step."""
 
     def __init__(self, c: Couche, k: int = 4, brut: bool = True, device: str = "cuda", n_delta: int = 0,
-                 n_codes: int = 0, jetons: int = 1, tenus=None, recouvrement: bool = True, espace: int = 0):
+                 n_codes: int = 0, jetons: int = 1, tenus=None, recouvrement: bool = True, espace: int = 0,
+                 deltas_predecodes: bool = False):
         self.c = c
         self.k = k
         self.jetons = jetons
@@ -60,6 +62,27 @@ class CoucheCarte:
         self.n_delta, self.n_codes = n_delta, n_codes
         d = self.dims
         self.R0, self.C0, self.R2 = d.lignes[0], d.colonnes[0], d.lignes[2]
+        self.deltas = None
+        if deltas_predecodes:
+            self.predecoder_deltas()
+
+    def predecoder_deltas(self, flux=None) -> None:
+        """Decodes every held expert's DELTA streams once (trc_moe_predecoder_deltas); the compressed
+        layer then reads those bytes instead of decoding DELTA at each step (the same results)."""
+        from . import lib, verifier
+
+        n = int(lib.trc_moe_deltas_octets(C.byref(self.dims), self.c.experts))
+        self.deltas = torch.empty(n, dtype=torch.uint8, device=self.dev)
+        self.controle_deltas = torch.zeros(4 * self.c.experts, dtype=torch.int32, device=self.dev)
+        desc = MoeCouche()
+        desc.parties, desc.parties_octets = self.adresses.data_ptr(), self.tailles.data_ptr()
+        desc.experts = self.c.experts
+        desc.luts = self.luts.data_ptr()
+        desc.dims = self.dims
+        desc.n_delta = self.n_delta
+        f = (flux or torch.cuda.current_stream()).cuda_stream
+        verifier(lib.trc_moe_predecoder_deltas(C.byref(desc), self.deltas.data_ptr(), n, self.controle_deltas.data_ptr(),
+                                               f))
 
     def _monter(self, parties):
         """Uploads the parts (None: an expert not held here, address and size 0)."""
@@ -116,6 +139,7 @@ class CoucheCarte:
             desc.expert_debut, desc.expert_fin = self.tenus
         desc.partiel = int(partiel)
         desc.echange = C.addressof(echange) if echange is not None else None
+        desc.deltas = self.deltas.data_ptr() if (self.deltas is not None and not brute) else None
         return desc
 
     def _espace(self):
@@ -164,24 +188,20 @@ class CoucheCarte:
         self.h = torch.zeros_like(self.g)
         self.s = torch.zeros(self.k, self.R2, dtype=torch.float32, device=self.dev)
         self.x32 = torch.zeros(self.C0, dtype=torch.float32, device=self.dev)
+        self.adresses_hote = self.adresses.cpu().numpy()
 
-    def decodee(self, x: torch.Tensor, residu: torch.Tensor, flux=None):
-        """Router, then decoder_lot into slots, gemv_lot (gate, up), swiglu, gemv_lot (down),
-        combiner. Reads the router's indices on the host, as the reference's scheduler does."""
-        self.routeur(x, flux)
-        self.x32.copy_(x.float())
-        idx = self.idx.cpu().numpy()
+    def descripteurs_decodee(self, idx) -> tuple:
+        """Device descriptors of the decode-then-multiply sequence for the routed experts `idx`
+        (host integers, k of them): decoder_lot into the k slots, gemv_lot of gate and up on
+        x32, gemv_lot of down on h. Returns (decode, gate/up, down) descriptor tensors."""
         base = self.emplacements.data_ptr()
         base += (-base) % 256
         d = self.dims
         descs = (DescDecodage * self.k)()
         for i, e in enumerate(idx):
-            descs[i] = DescDecodage(int(self.adresses[int(e)].item()), base + i * self.te, self.luts.data_ptr(),
+            descs[i] = DescDecodage(int(self.adresses_hote[int(e)]), base + i * self.te, self.luts.data_ptr(),
                                     self.ctl_d.data_ptr() + 16 * i)
         dd = torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).to(self.dev)
-        self.n.decoder_lot(dd, self.k, d, flux)
-        from . import lib
-
         pas = [0, 0, 0]
         for j in range(3):
             R, Cc = d.lignes[j], d.colonnes[j]
@@ -196,13 +216,29 @@ class CoucheCarte:
                 gu[2 * i + j] = DescGemv(base + i * self.te + off[j], self.x32.data_ptr(),
                                          (self.g if j == 0 else self.u)[i].data_ptr(), d.lignes[j], d.colonnes[j])
         dg = torch.frombuffer(bytearray(bytes(gu)), dtype=torch.uint8).to(self.dev)
-        self.n.gemv_lot(dg, 2 * self.k, self.R0, flux)
-        self.n.swiglu_oai(self.g, self.u, self.h, self.k * self.R0, flux)
         dn = (DescGemv * self.k)()
         for i in range(self.k):
             dn[i] = DescGemv(base + i * self.te + off[2], self.h[i].data_ptr(), self.s[i].data_ptr(), d.lignes[2],
                              d.colonnes[2])
         ddn = torch.frombuffer(bytearray(bytes(dn)), dtype=torch.uint8).to(self.dev)
+        return dd, dg, ddn
+
+    def sequence_decodee(self, descs, x: torch.Tensor, residu: torch.Tensor, flux=None) -> None:
+        """The sequence itself on `descs` (descripteurs_decodee), with this library's kernels:
+        decoder_lot, gemv_lot (gate, up), swiglu_oai, gemv_lot (down), combiner with the router's
+        weights (self.poids)."""
+        dd, dg, ddn = descs
+        self.x32.copy_(x.float())
+        self.n.decoder_lot(dd, self.k, self.dims, flux)
+        self.n.gemv_lot(dg, 2 * self.k, self.R0, flux)
+        self.n.swiglu_oai(self.g, self.u, self.h, self.k * self.R0, flux)
         self.n.gemv_lot(ddn, self.k, self.R2, flux)
         self.n.combiner(residu, self.s, self.R2, self.poids, self.k, self.R2, flux)
-        self._garde = (dd, dg, ddn)
+
+    def decodee(self, x: torch.Tensor, residu: torch.Tensor, flux=None):
+        """Router, then decoder_lot into slots, gemv_lot (gate, up), swiglu, gemv_lot (down),
+        combiner. Reads the router's indices on the host, as the reference's scheduler does."""
+        self.routeur(x, flux)
+        idx = self.idx.cpu().numpy()
+        self._garde = self.descripteurs_decodee(idx)
+        self.sequence_decodee(self._garde, x, residu, flux)

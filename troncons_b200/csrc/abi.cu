@@ -353,6 +353,7 @@ int couche_de(const trc_moe_couche* c, tb::Couche& k) {
     k.expert_debut = c->expert_debut;
     k.expert_fin = c->expert_fin;
     k.partiel = c->partiel ? 1u : 0u;
+    k.deltas = c->brut ? nullptr : c->deltas;
     if (c->echange != nullptr) {
         const trc_echange_pairs& e = *c->echange;
         if (e.monde < 2 || e.monde > 8 || e.rang >= e.monde) return usage("exchange: rank %u of %u", e.rang, e.monde);
@@ -378,6 +379,43 @@ uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t 
     if (dims == nullptr || k == 0) return 0;
     const tb::Espace e = tb::plan_espace(dims->lignes, dims->colonnes, k);
     return k <= tb::RECOUVRE_MAX ? e.total_recouvrant : e.total;
+}
+
+uint64_t trc_moe_deltas_octets(const trc_dims_expert* dims, uint32_t experts) {
+    if (dims == nullptr || experts == 0) return 0;
+    return tb::deltas_octets(dims->lignes, dims->colonnes, experts);
+}
+
+int trc_moe_predecoder_deltas(const trc_moe_couche* c, uint8_t* deltas, uint64_t deltas_octets, uint32_t* controle,
+                              void* flux) {
+    if (c == nullptr) return usage("layer descriptor absent");
+    if (int s = verifier_dims(&c->dims)) return s;
+    if (c->experts == 0) return usage("no expert");
+    for (int j = 0; j < 3; ++j)
+        if (c->dims.colonnes[j] < 256 || c->dims.lignes[j] > 8192)
+            return usage("matrix %d: %u x %u (rows <= 8,192, columns >= 256)", j, c->dims.lignes[j], c->dims.colonnes[j]);
+    if (c->parties == nullptr || c->parties_octets == nullptr || c->luts == nullptr || controle == nullptr ||
+        deltas == nullptr)
+        return usage("predecode: a device buffer is missing");
+    if (!aligne(c->luts, 16)) return usage("LUTs misaligned (16 bytes)");
+    const uint64_t besoin = tb::deltas_octets(c->dims.lignes, c->dims.colonnes, c->experts);
+    if (deltas_octets < besoin) return usage("delta buffer of %llu bytes, %llu needed", (unsigned long long)deltas_octets,
+                                             (unsigned long long)besoin);
+    tb::Couche k{};
+    k.parties = c->parties;
+    k.parties_octets = c->parties_octets;
+    k.experts = c->experts;
+    k.k = 1;
+    k.luts = c->luts;
+    for (int j = 0; j < 3; ++j) {
+        k.lignes[j] = c->dims.lignes[j];
+        k.colonnes[j] = c->dims.colonnes[j];
+    }
+    k.controle = controle;
+    k.n_delta = c->n_delta;
+    k.jetons = 1;
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_predecoder_deltas(k, deltas, static_cast<cudaStream_t>(flux)));
 }
 
 int trc_moe_couche_fusionnee(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
@@ -477,7 +515,7 @@ int trc_attention(const float* q, size_t q_octets, const uint16_t* cache_k, size
     const uint64_t dkv = uint64_t(p->tetes_kv) * 64;
     if (cache_k == nullptr || cache_v == nullptr || cache_k_octets < 2 * cases * dkv || cache_v_octets < 2 * cases * dkv)
         return usage("cache too short");
-    if (!aligne(cache_k, 16)) return usage("key cache not aligned on 16");
+    if (!aligne(cache_k, 16) || !aligne(cache_v, 16)) return usage("key or value cache not aligned on 16");
     if (q == nullptr || sortie == nullptr || puits == nullptr || q_octets < 256ull * p->tetes ||
         sortie_octets < 256ull * p->tetes || puits_octets < 4ull * p->tetes)
         return usage("attention: views too short");

@@ -3,9 +3,9 @@
 // reference's passe.cuh kernels gemv_q8_0, rmsnorm, rope_yarn, ecrire_kv, attention, launched by
 // `Noyaux` in trc-noyaux/src/lib.rs:291-381).
 //
-// Each kernel keeps the reference's arithmetic order, element by element, so that its outputs
-// are bit-identical to the reference kernels' on the same GPU (the same CUDA math functions,
-// called, not restated); the memory side is this library's own:
+// The Q8_0 GEMV, RMSNorm, rotation and KV write keep the reference's arithmetic order, element by
+// element, so that their outputs are bit-identical to the reference kernels' on the same GPU (the
+// same CUDA math functions, called, not restated); the memory side is this library's own:
 //   k_gemv_q8_0   persistent warps stage rows of 34-byte blocks (C/32 of them, rows 2-aligned
 //                 only) with coalesced 16-byte cp.async into shared memory, the next row while
 //                 the current one is multiplied; x is staged once per block;
@@ -15,10 +15,12 @@
 //                 over 256; y = x r w in f64 rounded once (passe.cuh:250-272);
 //   k_rope_yarn   NEOX halves, YaRN inv_freq and concentration in f64 (the published YaRN
 //                 formula, passe.cuh:146-169, 280-301);
-//   k_ecrire_kv   f32 -> f16 round-to-nearest-even into the position's case (passe.cuh:305-314);
-//   k_attention   one query head per block: scores (fmaf chain over d, then x 1/sqrt(d)), max with
-//                 the head's sink, exp, z = tree sum + exp(sink - m), values by 4 groups of
-//                 positions j = g mod 4 in order, ((g0 + g1) + (g2 + g3)) / z (passe.cuh:316-371).
+//   k_ecrire_kv   f32 -> f16 round-to-nearest-even into the position's case (passe.cuh:305-314).
+// The attention itself (k_attention) is this library's own design, split over positions and
+// merged within a thread-block cluster: the same function (passe.cuh:316-371), another order of
+// the f32 sums, so it agrees with the reference's kernel and an f64 evaluation within 1e-5 of
+// max|out| rather than bit for bit.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include "commun.cuh"
@@ -220,95 +222,178 @@ __global__ void __launch_bounds__(256) k_ecrire_kv(const float* __restrict__ k, 
 
 // ------------------------------------------------------------------ attention of one position
 
+// Attention of one position, split over positions and merged inside a thread-block cluster.
+//
+// Grid (S, tetes_kv), clusters of S blocks along x: block (s, hk) takes the s-th slice of the
+// positions for the G = tetes / tetes_kv query heads that share key/value head hk, so that each
+// key and value row is read from HBM once for all G heads. A block stages up to ATT_TRANCHE
+// positions at a time (their key rows, padded to 144 bytes against bank conflicts, and value
+// rows) with 16-byte cp.async, computes the G scores of each position (fmaf chain over d, then
+// x 1/sqrt(d)), and keeps per head a running maximum m, sum z and value accumulator a over its
+// slices (online softmax: a and z rescaled by exp(m_old - m_new) when the maximum grows). The S
+// blocks then merge through distributed shared memory: block r merges heads h = r, r + S, ...
+// with the head's sink: M = max(sink, m_0 .. m_{S-1}), f_s = exp(m_s - M),
+// z = sum_s z_s f_s + exp(sink - M), out = (sum_s a_s f_s) / z, sums in slice order. The result
+// is deterministic for a given (n, S); it differs from a single-pass softmax by f32 rounding
+// (passe.cuh:316-371 defines the function: sinks, ring of cases, 1/sqrt(d) scale).
 constexpr uint32_t ATT_FILS = 256;
 constexpr uint32_t ATT_DIM = 64;
+constexpr uint32_t ATT_TRANCHE = 128;         // positions staged at once
+constexpr uint32_t ATT_K_PAS = 144;           // bytes per staged key row (128 + 16 of padding)
+constexpr uint32_t ATT_V_PAS = 128;           // bytes per staged value row
+constexpr uint32_t ATT_G_MAX = 64;            // query heads per key/value head
+constexpr uint32_t ATT_GRAPPE_MAX = 16;
 
-template <bool MAX>
-__device__ __forceinline__ float arbre_bloc(float* part, float v) {
-    const uint32_t t = threadIdx.x;
-    part[t] = v;
-    __syncthreads();
-#pragma unroll
-    for (uint32_t k = ATT_FILS / 2; k > 0; k >>= 1) {
-        if (t < k) part[t] = MAX ? fmaxf(part[t], part[t + k]) : part[t] + part[t + k];
-        __syncthreads();
-    }
-    const float r = part[0];
-    __syncthreads();
-    return r;
+__host__ __device__ constexpr uint32_t att_smem(uint32_t G) {
+    return ATT_TRANCHE * (ATT_K_PAS + ATT_V_PAS)   // key and value rows
+           + 4u * G * ATT_DIM                        // q
+           + 4u * G * ATT_TRANCHE                    // scores, then exp(score - m)
+           + 4u * G * (ATT_DIM + 3u);                // per head: a[64], m, z, rescale factor
 }
 
 __global__ void __launch_bounds__(ATT_FILS) k_attention(const float* __restrict__ q, const uint16_t* __restrict__ cache_k,
                                                         const uint16_t* __restrict__ cache_v, const float* __restrict__ puits,
                                                         float* __restrict__ sortie, ParamsAttention p) {
-    extern __shared__ float scores[];
-    __shared__ float qs[ATT_DIM];
-    __shared__ float part[ATT_FILS];
-    __shared__ float groupes[4][ATT_DIM];
-    attendre_amont();
-    liberer_aval();
-    const uint32_t t = threadIdx.x, h = blockIdx.x;
-    const uint32_t hk = h / (p.tetes / p.tetes_kv);
+    extern __shared__ __align__(16) uint8_t att_mem[];
+    namespace cg = cooperative_groups;
+    cg::cluster_group grappe = cg::this_cluster();
+    const uint32_t G = p.tetes / p.tetes_kv;
+    uint8_t* k_lignes = att_mem;
+    uint8_t* v_lignes = k_lignes + ATT_TRANCHE * ATT_K_PAS;
+    float* qs = reinterpret_cast<float*>(v_lignes + ATT_TRANCHE * ATT_V_PAS);
+    float* sc = qs + G * ATT_DIM;
+    float* acc = sc + G * ATT_TRANCHE;   // [G][64]
+    float* mx = acc + G * ATT_DIM;       // [G]
+    float* zs = mx + G;                  // [G]
+    float* fac = zs + G;                 // [G]
+
+    const uint32_t t = threadIdx.x, voie = t & 31u, w = t >> 5;
+    const uint32_t S = gridDim.x, s = blockIdx.x, hk = blockIdx.y;
     const uint32_t dkv = p.tetes_kv * ATT_DIM;
     const uint32_t n = p.fin - p.debut;
-    if (t < ATT_DIM) qs[t] = q[uint64_t(h) * ATT_DIM + t];
-    __syncthreads();
-    for (uint32_t j = t; j < n; j += ATT_FILS) {
-        const uint32_t pos = p.debut + j;
-        const uint32_t c = p.anneau ? pos % p.anneau : pos;
-        const uint4* kr = reinterpret_cast<const uint4*>(cache_k + uint64_t(c) * dkv + uint64_t(hk) * ATT_DIM);
-        uint4 w[8];
+    const uint32_t par = (n + S - 1) / S;
+    const uint32_t j0 = min(n, s * par), j1 = min(n, j0 + par);
+
+    attendre_amont();
+    liberer_aval();
+    for (uint32_t i = t; i < G * ATT_DIM; i += ATT_FILS) {
+        qs[i] = q[uint64_t(hk) * G * ATT_DIM + i];
+        acc[i] = 0.0f;
+    }
+    for (uint32_t g = t; g < G; g += ATT_FILS) {
+        mx[g] = -INFINITY;
+        zs[g] = 0.0f;
+    }
+
+    for (uint32_t a0 = j0; a0 < j1; a0 += ATT_TRANCHE) {
+        const uint32_t m = min(ATT_TRANCHE, j1 - a0);
+        __syncthreads();  // the previous slice's rows and scores are no longer read
+        // Key and value rows of positions a0 .. a0 + m - 1: 8 chunks of 16 bytes per row each.
+        for (uint32_t i = t; i < 16u * m; i += ATT_FILS) {
+            const uint32_t j = i >> 4, c16 = i & 7u;
+            const uint32_t pos = p.debut + a0 + j;
+            const uint32_t cas = p.anneau ? pos % p.anneau : pos;
+            const uint64_t src = uint64_t(cas) * dkv + uint64_t(hk) * ATT_DIM + 8u * c16;
+            if (i & 8u)
+                cp_async16(v_lignes + j * ATT_V_PAS + 16u * c16, cache_v + src, 16u);
+            else
+                cp_async16(k_lignes + j * ATT_K_PAS + 16u * c16, cache_k + src, 16u);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        // Scores: thread t takes position t mod 128 for heads t / 128, t / 128 + 2, ...
+        {
+            const uint32_t j = t % ATT_TRANCHE;
+            if (j < m) {
+                float kf[ATT_DIM];
+                const uint4* kr = reinterpret_cast<const uint4*>(k_lignes + j * ATT_K_PAS);
 #pragma unroll
-        for (int b = 0; b < 8; ++b) w[b] = kr[b];
-        float s = 0.0f;
+                for (int b = 0; b < 8; ++b) {
+                    const uint4 u = kr[b];
+                    const uint32_t mots[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const uint32_t mots[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
+                    for (int c = 0; c < 4; ++c) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&mots[c]));
+                        kf[8 * b + 2 * c] = f.x;
+                        kf[8 * b + 2 * c + 1] = f.y;
+                    }
+                }
+                for (uint32_t g = t / ATT_TRANCHE; g < G; g += ATT_FILS / ATT_TRANCHE) {
+                    const float* qg = qs + g * ATT_DIM;
+                    float v = 0.0f;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                s = fmaf(qs[8 * b + 2 * u], f16_f32(mots[u] & 0xFFFFu), s);
-                s = fmaf(qs[8 * b + 2 * u + 1], f16_f32(mots[u] >> 16), s);
+                    for (int d = 0; d < int(ATT_DIM); ++d) v = fmaf(qg[d], kf[d], v);
+                    sc[g * ATT_TRANCHE + j] = v * p.echelle;
+                }
             }
         }
-        scores[j] = s * p.echelle;
-    }
-    __syncthreads();
-    float m = -INFINITY;
-    for (uint32_t j = t; j < n; j += ATT_FILS) m = fmaxf(m, scores[j]);
-    const float puits_h = puits[h];
-    m = fmaxf(arbre_bloc<true>(part, m), puits_h);
-    float z = 0.0f;
-    for (uint32_t j = t; j < n; j += ATT_FILS) {
-        const float e = expf(scores[j] - m);
-        scores[j] = e;
-        z += e;
-    }
-    z = arbre_bloc<false>(part, z) + expf(puits_h - m);
-    const uint32_t dd = t & (ATT_DIM - 1u), g = t / ATT_DIM;
-    const uint16_t* vcol = cache_v + uint64_t(hk) * ATT_DIM + dd;
-    float a = 0.0f;
-    uint32_t j = g;
-    // Eight positions' values loaded before their (ordered) fmaf chain.
-    for (; j + 28u < n; j += 32u) {
-        float vv[8];
+        __syncthreads();
+        // Per head (warp w takes heads w, w + 8, ...): the slice's maximum, the new running
+        // maximum, exp(score - m) in place, the slice's sum, the rescale of the running values.
+        for (uint32_t g = w; g < G; g += ATT_FILS / 32u) {
+            float* sg = sc + g * ATT_TRANCHE;
+            float mt = -INFINITY;
+            for (uint32_t j = voie; j < m; j += 32u) mt = fmaxf(mt, sg[j]);
 #pragma unroll
-        for (uint32_t u = 0; u < 8u; ++u) {
-            const uint32_t pos = p.debut + j + 4u * u;
-            const uint32_t c = p.anneau ? pos % p.anneau : pos;
-            vv[u] = f16_f32(vcol[uint64_t(c) * dkv]);
+            for (int d = 16; d > 0; d >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, d));
+            const float ancien = mx[g];
+            const float nouveau = fmaxf(ancien, mt);
+            float somme = 0.0f;
+            for (uint32_t j = voie; j < m; j += 32u) {
+                const float e = expf(sg[j] - nouveau);
+                sg[j] = e;
+                somme += e;
+            }
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) somme += __shfl_xor_sync(0xFFFFFFFFu, somme, d);
+            __syncwarp();
+            if (voie == 0) {
+                const float f = expf(ancien - nouveau);  // 0 on the first slice (ancien = -inf)
+                fac[g] = f;
+                zs[g] = fmaf(zs[g], f, somme);
+                mx[g] = nouveau;
+            }
         }
-#pragma unroll
-        for (uint32_t u = 0; u < 8u; ++u) a = fmaf(scores[j + 4u * u], vv[u], a);
+        __syncthreads();
+        // Values: thread (w, voie) accumulates dimensions 2 voie, 2 voie + 1 of heads w, w + 8, ...
+        for (uint32_t g = w; g < G; g += ATT_FILS / 32u) {
+            const float* eg = sc + g * ATT_TRANCHE;
+            float a0v = 0.0f, a1v = 0.0f;
+            const uint32_t* vr = reinterpret_cast<const uint32_t*>(v_lignes) + voie;
+#pragma unroll 4
+            for (uint32_t j = 0; j < m; ++j) {
+                const uint32_t mot = vr[j * (ATT_V_PAS / 4u)];
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&mot));
+                const float e = eg[j];
+                a0v = fmaf(e, f.x, a0v);
+                a1v = fmaf(e, f.y, a1v);
+            }
+            float* ag = acc + g * ATT_DIM + 2u * voie;
+            const float f = fac[g];
+            ag[0] = fmaf(ag[0], f, a0v);
+            ag[1] = fmaf(ag[1], f, a1v);
+        }
     }
-    for (; j < n; j += 4u) {
-        const uint32_t pos = p.debut + j;
-        const uint32_t c = p.anneau ? pos % p.anneau : pos;
-        a = fmaf(scores[j], f16_f32(vcol[uint64_t(c) * dkv]), a);
-    }
-    groupes[g][dd] = a;
     __syncthreads();
-    if (t < ATT_DIM)
-        sortie[uint64_t(h) * ATT_DIM + t] = ((groupes[0][t] + groupes[1][t]) + (groupes[2][t] + groupes[3][t])) / z;
+    grappe.sync();  // every block's (m, z, a) is written and visible to the cluster
+    // Block r merges heads r, r + S, ...: 64 threads per head, four heads at a time.
+    for (uint32_t g = s + S * (t / ATT_DIM); g < G; g += S * (ATT_FILS / ATT_DIM)) {
+        const uint32_t d = t % ATT_DIM;
+        const uint32_t h = hk * G + g;
+        const float puits_h = puits[h];
+        float M = puits_h;
+        for (uint32_t b = 0; b < S; ++b) M = fmaxf(M, *grappe.map_shared_rank(mx + g, b));
+        float z = 0.0f, o = 0.0f;
+        for (uint32_t b = 0; b < S; ++b) {
+            const float f = expf(*grappe.map_shared_rank(mx + g, b) - M);
+            z = fmaf(*grappe.map_shared_rank(zs + g, b), f, z);
+            o = fmaf(*grappe.map_shared_rank(acc + g * ATT_DIM + d, b), f, o);
+        }
+        z += expf(puits_h - M);
+        sortie[uint64_t(h) * ATT_DIM + d] = o / z;
+    }
+    grappe.sync();  // no block leaves while another may still read its shared memory
 }
 
 // ------------------------------------------------------------------ launchers
@@ -372,10 +457,39 @@ cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint1
 
 cudaError_t lancer_attention(const float* q, const uint16_t* ck, const uint16_t* cv, const float* puits, float* sortie,
                              const ParamsAttention& p, cudaStream_t flux) {
-    const size_t smem = 4u * (p.fin - p.debut);
+    const uint32_t G = p.tetes / p.tetes_kv;
+    if (G == 0 || G > ATT_G_MAX || p.dim_tete != ATT_DIM) return cudaErrorInvalidValue;
+    const uint32_t n = p.fin - p.debut;
+    const size_t smem = att_smem(G);
     cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_attention), int(smem));
     if (e != cudaSuccess) return e;
-    return lancer_pdl(k_attention, dim3(p.tetes), dim3(ATT_FILS), smem, flux, q, ck, cv, puits, sortie, p);
+    static bool grappe16 = [] {
+        return cudaFuncSetAttribute(reinterpret_cast<const void*>(k_attention),
+                                    cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+    }();
+    // Slices of at least 32 positions, at most 16 (or 8 where clusters of 16 are refused) per head.
+    uint32_t S = std::max(1u, std::min(grappe16 ? ATT_GRAPPE_MAX : 8u, (n + 31u) / 32u));
+    for (;;) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S, p.tetes_kv);
+        cfg.blockDim = dim3(ATT_FILS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = flux;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        at[1].id = cudaLaunchAttributeClusterDimension;
+        at[1].val.clusterDim.x = S;
+        at[1].val.clusterDim.y = 1;
+        at[1].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 2;
+        e = cudaLaunchKernelEx(&cfg, k_attention, q, ck, cv, puits, sortie, p);
+        if (e == cudaSuccess || S <= 8) return e;
+        (void)cudaGetLastError();  // a cluster of 16 refused here: halve it
+        grappe16 = false;
+        S = 8;
+    }
 }
 
 }  // namespace tb

@@ -61,7 +61,16 @@ struct ArgsMoe {
     Espace plan;
     uint32_t j0;     // first matrix of this launch (0: gate and up; 2: down)
     uint32_t seuls;  // the down projection's codes are decoded with gate/up, into the workspace
+    uint32_t tous;   // k_moe_delta decodes every expert of the layer: activation i = expert i
+    uint64_t pre_ek[3];  // with c.deltas: offset of matrix j's delta bytes ([experts][blocks])
 };
+
+// Activation i's delta bytes of matrix j (one per block): decoded by this call into the
+// workspace, or decoded ahead for every expert of the layer (c.deltas).
+__device__ __forceinline__ const uint8_t* deltas_de(const ArgsMoe& a, uint32_t i, uint32_t j, uint32_t nblocs) {
+    if (a.c.deltas != nullptr) return a.c.deltas + a.pre_ek[j] + uint64_t(a.c.indices[i]) * nblocs;
+    return a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;
+}
 
 // Whether activation i's expert is held by this call (others are skipped: no work, no error).
 __device__ __forceinline__ bool tenu(const Couche& c, uint32_t i) {
@@ -114,15 +123,22 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u) * M), M / 4u);
     attendre_amont();
     liberer_aval();
-    if (!tenu(c, i)) return;
+    if (!a.tous && !tenu(c, i)) return;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], B = c.colonnes[j] / 32u, nblocs = R * B;
-    const uint8_t* partie;
-    uint64_t taille;
+    const uint8_t* partie = nullptr;
+    uint64_t taille = 0;
     Flux fd;
     EnteteRans h;
-    const bool bon = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_DELTA, j, fd) &&
-                     lire_entete(fd, nblocs, h);
+    bool a_partie;
+    if (a.tous) {  // every expert of the layer, in order
+        partie = reinterpret_cast<const uint8_t*>(c.parties[i]);
+        taille = c.parties_octets[i];
+        a_partie = partie != nullptr && taille >= 64 && (reinterpret_cast<uintptr_t>(partie) & 15u) == 0;
+    } else {
+        a_partie = partie_de(c, i, partie, taille);
+    }
+    const bool bon = a_partie && trouver_flux_warp(partie, taille, SORTE_DELTA, j, fd) && lire_entete(fd, nblocs, h);
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
         return;
@@ -328,7 +344,7 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     if (warp < MOE_PAIRES) {
         // ---------------- producer: the decode chain
         const uint32_t lut_s = adresse_partagee(lut);
-        const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
+        const uint8_t* __restrict__ ek = deltas_de(a, i, j, nblocs);  // delta bytes
         uint32_t hors_l = 0, pointeur = 0, n = 0;
         for (uint32_t t = paire_t0; t < h.T && !abandon; t += pas_tuiles) {
             if (t != paire_t0) d.debut(h, t, voie, anneau);
@@ -515,7 +531,7 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     __syncthreads();
 
     const uint32_t lut_s = adresse_partagee(lut);
-    const uint8_t* __restrict__ ek = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;  // delta bytes
+    const uint8_t* __restrict__ ek = deltas_de(a, i, j, nblocs);  // delta bytes
     const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
     const uint32_t q = voie & 3u, g = voie >> 2;
     const uint32_t nmacro = h.P / 128u;
@@ -687,7 +703,7 @@ __global__ void __launch_bounds__(BAS_WARPS * 32) k_moe_bas(ArgsMoe a) {
     if (seg * SEGMENT_MACRO >= nmacro) return;
     const uint32_t m0 = seg * SEGMENT_MACRO, m1 = min(m0 + SEGMENT_MACRO, nmacro);
     const uint32_t* __restrict__ cd = reinterpret_cast<const uint32_t*>(a.espace + a.plan.cd) + uint64_t(i) * 4u * nblocs;
-    const uint8_t* __restrict__ ek = a.espace + a.plan.ek[2] + uint64_t(i) * nblocs;
+    const uint8_t* __restrict__ ek = deltas_de(a, i, 2, nblocs);
     const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
     const uint32_t q = voie & 3u, g = voie >> 2;
     GemvTuile gv;
@@ -898,7 +914,11 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
         if (ev != nullptr && ev[i] != nullptr) cudaEventRecord(ev[i], flux);
     };
     const uint32_t na = activations(c);
-    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, na), 0, 0};
+    ArgsMoe a{c, static_cast<uint8_t*>(espace), plan_espace(c.lignes, c.colonnes, na), 0, 0, 0, {0, 0, 0}};
+    if (c.deltas != nullptr) {
+        const Espace pe = plan_espace(c.lignes, c.colonnes, c.experts);
+        for (int j = 0; j < 3; ++j) a.pre_ek[j] = pe.ek[j];
+    }
     // The down projection's decode overlaps gate/up when the workspace holds its codes.
     a.seuls = (!c.brut && na <= RECOUVRE_MAX && espace_octets >= a.plan.total_recouvrant) ? 1u : 0u;
     const uint32_t nd = c.n_delta ? c.n_delta : 256u, nc = c.n_codes ? c.n_codes : 256u;
@@ -912,7 +932,9 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
     cudaError_t e;
     marque(0);
     if (!c.brut) {
-        if ((e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, na), dim3(DELTA_WARPS * 32), 0,
+        // DELTA of the routed experts, unless the layer's deltas were decoded ahead.
+        if (c.deltas == nullptr &&
+            (e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, na), dim3(DELTA_WARPS * 32), 0,
                             flux, a)) != cudaSuccess)
             return e;
         // Producer / consumer pairs while the launch's tiles fit them at once (lowest latency per
@@ -984,6 +1006,27 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
     if ((e = lancer_pdl(k_moe_combiner, dim3((c.lignes[2] + 255) / 256, c.jetons), dim3(256), 0, flux, a)) != cudaSuccess) return e;
     marque(5);
     return cudaGetLastError();
+}
+
+// The delta bytes of every expert of a layer, decoded ahead into `deltas` (the layout of the
+// workspace's delta region for `experts` activations: matrix j at plan_espace(...).ek[j],
+// [expert][block]); counters per expert in controle[4 e ..].
+uint64_t deltas_octets(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts) {
+    return plan_espace(lignes, colonnes, experts).parts[0];
+}
+
+cudaError_t lancer_predecoder_deltas(const Couche& c, uint8_t* deltas, cudaStream_t flux) {
+    ArgsMoe a{c, deltas, plan_espace(c.lignes, c.colonnes, c.experts), 0, 0, 1u, {0, 0, 0}};
+    a.c.deltas = nullptr;
+    const uint32_t nd = c.n_delta ? c.n_delta : 256u;
+    uint32_t td = 1;
+    for (int j = 0; j < 3; ++j) {
+        const uint64_t nb = uint64_t(c.lignes[j]) * (c.colonnes[j] / 32u);
+        td = std::max<uint32_t>(td, uint32_t(((nb + 127) / 128 + nd - 1) / nd));
+    }
+    cudaError_t e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.experts),
+                               dim3(DELTA_WARPS * 32), 0, flux, a);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace tb

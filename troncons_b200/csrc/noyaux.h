@@ -66,6 +66,7 @@ struct Couche {
     uint32_t expert_debut, expert_fin;  // experts held here ([debut, fin); fin = 0: all)
     uint32_t partiel;                   // 1: the combine writes this call's sum, not residu +=
     Echange ech;                        // the combine's sum across GPUs over peer memory
+    const uint8_t* deltas;              // every expert's delta bytes decoded ahead, or null
 };
 
 // Activations of a call: tokens x routed experts per token.
@@ -110,6 +111,8 @@ cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, 
 cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, const float* poids, uint32_t n, uint32_t d,
                             cudaStream_t flux);
 cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cudaStream_t flux, cudaEvent_t const* ev = nullptr);
+uint64_t deltas_octets(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts);
+cudaError_t lancer_predecoder_deltas(const Couche& c, uint8_t* deltas, cudaStream_t flux);
 
 // Attention side (mirrors of trc_params_rope, 48 bytes, and trc_params_attention, 32 bytes).
 struct ParamsRope {

@@ -6,76 +6,67 @@
 
 namespace tb {
 
-// Better of two (value, index): larger value, then smaller index; a NaN is never better.
-__device__ __forceinline__ bool meilleur(float va, uint32_t ia, float vb, uint32_t ib) {
-    return va > vb || (va == vb && ia < ib);
-}
-
-// One warp. E <= 256, k <= 8: lane l holds logits l, l+32, ..., each round takes the warp's best
-// among those not yet taken. Weights: m = the first chosen value, e_r = exp(v_r - m) in f64,
-// z = sum in order, w_r = float(e_r / z) (passe.cuh:455-514; ops.rs:123-131).
-__global__ void __launch_bounds__(32) k_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids,
-                                             uint32_t* boite, uint32_t sequence) {
+// Top-k by rank. One block per token, one thread per expert (E <= 256, rounded up to whole
+// warps). Expert e's rank is the number of experts that beat it: a larger value, or the same
+// value and a smaller index; a NaN beats nothing and is never ranked, so the order over the
+// other logits (-inf included) is total and the experts of rank 0 .. k-1 are the top-k in order
+// (passe.cuh:455-514, ops.rs:123-131: value descending, index ascending, NaN never chosen; a slot
+// with no candidate left holds index 0xFFFFFFFF and value -inf). Each thread counts its rank over
+// the logits staged in shared memory, every thread reading the same word at once (a broadcast).
+// Weights: m = the slot-0 value, e_r = exp(v_r - m) in f64, z = e_0 + e_1 + ... in slot order,
+// w_r = float(e_r / z). The slots' owners write the outputs and the host-mapped mailbox
+// (indices at [1 + r], weight bits at [1 + k + r]); each fences at system scope, and after a
+// barrier one thread raises the mailbox's sequence word.
+__global__ void __launch_bounds__(256) k_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices,
+                                              float* poids, uint32_t* boite, uint32_t sequence) {
+    __shared__ float lg[256];
+    __shared__ float val_rang[8];
+    __shared__ uint32_t idx_rang[8];
     attendre_amont();
     liberer_aval();
-    // Token blockIdx.x of a batch (the mailbox is for a single token).
     logits += uint64_t(blockIdx.x) * E;
     indices += uint64_t(blockIdx.x) * k;
     poids += uint64_t(blockIdx.x) * k;
-    const uint32_t voie = threadIdx.x;
-    float v[8];
-    uint32_t pris = 0;
-#pragma unroll
-    for (uint32_t i = 0; i < 8; ++i) {
-        const uint32_t e = voie + 32u * i;
-        v[i] = e < E ? logits[e] : -INFINITY;
-        pris |= (e >= E ? 1u : 0u) << i;
+    const uint32_t e = threadIdx.x;
+    const float v = e < E ? logits[e] : __int_as_float(0x7FC00000);  // padding: a NaN, never ranked
+    lg[e] = v;
+    if (e < 8) {
+        val_rang[e] = -INFINITY;
+        idx_rang[e] = 0xFFFFFFFFu;
     }
-    float cv[8];
-    uint32_t ci[8];
-    for (uint32_t r = 0; r < k; ++r) {
-        float bv = -INFINITY;
-        uint32_t bi = 0xFFFFFFFFu;
-#pragma unroll
-        for (uint32_t i = 0; i < 8; ++i)
-            if (!((pris >> i) & 1u) && meilleur(v[i], voie + 32u * i, bv, bi)) {
-                bv = v[i];
-                bi = voie + 32u * i;
-            }
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) {
-            const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, d);
-            const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, d);
-            if (meilleur(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
-            }
+    __syncthreads();
+    if (v == v) {
+        uint32_t rang = 0;
+        for (uint32_t j = 0; j < E; ++j) {
+            const float w = lg[j];
+            rang += (w > v || (w == v && j < e)) ? 1u : 0u;
         }
-        if (bi != 0xFFFFFFFFu && (bi & 31u) == voie) pris |= 1u << (bi >> 5);
-        cv[r] = bv;
-        ci[r] = bi;
+        if (rang < k) {
+            val_rang[rang] = v;
+            idx_rang[rang] = e;
+        }
     }
-    if (voie != 0) return;
-    double ex[8];
-    const double m = cv[0];
-    double z = 0.0;
-    for (uint32_t r = 0; r < k; ++r) {
-        ex[r] = exp(double(cv[r]) - m);
-        z += ex[r];
-    }
-    for (uint32_t r = 0; r < k; ++r) {
-        const float w = float(ex[r] / z);
-        indices[r] = ci[r];
-        poids[r] = w;
+    __syncthreads();
+    if (e < k) {
+        const double m = val_rang[0];
+        double z = 0.0, mien = 0.0;
+        for (uint32_t r = 0; r < k; ++r) {
+            const double x = exp(double(val_rang[r]) - m);
+            z += x;
+            if (r == e) mien = x;
+        }
+        const float w = float(mien / z);
+        indices[e] = idx_rang[e];
+        poids[e] = w;
         if (boite != nullptr) {
-            reinterpret_cast<volatile uint32_t*>(boite)[1 + r] = ci[r];
-            reinterpret_cast<volatile uint32_t*>(boite)[1 + k + r] = __float_as_uint(w);
+            volatile uint32_t* b = boite;
+            b[1 + e] = idx_rang[e];
+            b[1 + k + e] = __float_as_uint(w);
+            __threadfence_system();
         }
     }
-    if (boite != nullptr) {
-        __threadfence_system();
-        reinterpret_cast<volatile uint32_t*>(boite)[0] = sequence;
-    }
+    __syncthreads();
+    if (e == 0 && boite != nullptr) reinterpret_cast<volatile uint32_t*>(boite)[0] = sequence;
 }
 
 // Clamped SwiGLU of gpt-oss, element-wise in f64 (passe.cuh:598-605).
@@ -110,8 +101,9 @@ __global__ void __launch_bounds__(256) k_combiner(float* __restrict__ residu, co
 
 cudaError_t lancer_topk(const float* logits, uint32_t E, uint32_t k, uint32_t* indices, float* poids, uint32_t* boite,
                         uint32_t sequence, cudaStream_t flux, uint32_t jetons) {
-    return lancer_pdl(k_topk, dim3(jetons), dim3(32), 0, flux, logits, E, k, indices, poids, jetons == 1 ? boite : nullptr,
-                      sequence);
+    const uint32_t fils = (E + 31u) / 32u * 32u;
+    return lancer_pdl(k_topk, dim3(jetons), dim3(fils), 0, flux, logits, E, k, indices, poids,
+                      jetons == 1 ? boite : nullptr, sequence);
 }
 
 cudaError_t lancer_swiglu(const float* g, const float* u, float* y, uint32_t n, cudaStream_t flux) {
