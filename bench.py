@@ -492,6 +492,9 @@ def legs_couche(args, c, cc, xs_dev, res_dev, idx, vidange, pic: float) -> dict:
     t = chrono_etapes(lambda: cc.couche(x_buf, residu, brute=True), prep, n_pas, args.warmup, vidange)
     octets = sum(sum(int.from_bytes(c.parties_brutes[int(e)][12:16], "little") for e in idx[s]) + fixe for s in steps)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    for e in ev:  # torch creates the CUDA event at its first record
+        e.record()
+    torch.cuda.synchronize()
     ph = []
     for s in range(n_pas):
         vidange.zero_()

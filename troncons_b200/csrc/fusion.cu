@@ -288,6 +288,9 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
     const uint32_t warp = threadIdx.x >> 5, paire = warp % MOE_PAIRES;
+    // The routed experts come from the router: without the DELTA launch between them (deltas
+    // decoded ahead), this launch follows the router directly and waits before reading them.
+    if (c.deltas != nullptr) attendre_amont();
     if (!tenu(c, i)) return;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
@@ -491,6 +494,7 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     extern __shared__ __align__(16) uint8_t dyn[];
     const Couche& c = a.c;
     const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    if (c.deltas != nullptr) attendre_amont();  // as in k_moe_codes: the routed experts first
     if (!tenu(c, i)) return;
     uint32_t* controle = c.controle + 4u * i;
     const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
