@@ -66,6 +66,8 @@ def arguments(argv=None):
     a.add_argument("--contexte", type=int, default=2048)
     a.add_argument("--sans-modele", action="store_true", help="skip the whole-model tokens/s in the default line")
     a.add_argument("--exactitude", type=int, default=0)
+    a.add_argument("--sans-predecodage", action="store_true",
+                   help="whole model: decode DELTA at every step instead of once at load")
     a.add_argument("--couches", type=int, default=36)
     a.add_argument("--codeur", action="store_true",
                    help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
@@ -402,9 +404,9 @@ def notre_bras(args):
         del cc, c
         torch.cuda.empty_cache()
         try:
-            mod = mesurer_modele(args, 16, 3, 0)
+            mod = mesurer_modele(args, 16, 3, 512)
             ligne["modele"] = {k: mod[k] for k in ("metric", "value", "unit", "ms_per_step", "config", "roofline",
-                                                    "generation_s", "context_s")}
+                                                    "generation_s", "context_s", "exactitude")}
         except Exception as ex:  # reported, not hidden: the layer's line stands on its own
             ligne["modele"] = {"unavailable": f"{type(ex).__name__}: {ex}"[:300]}
     if dist:
@@ -1210,7 +1212,7 @@ def mesurer_modele(args, steps: int, warmup: int, exactitude: int) -> dict:
     t0 = time.time()
     m = M.Modele(couches=args.couches, d=2880, tetes=64, tetes_kv=8, experts=args.experts, k=args.k, vocab=201088,
                  contexte=args.contexte + warmup + max(steps, exactitude) + 1, ffn=2880, fenetre=128,
-                 graine=args.graine, compresse=True, brut=exactitude > 0)
+                 graine=args.graine, compresse=True, brut=exactitude > 0, deltas_predecodes=not args.sans_predecodage)
     torch.cuda.synchronize()
     t_gen = time.time() - t0
     rng = np.random.default_rng(args.graine)
@@ -1244,6 +1246,16 @@ def mesurer_modele(args, steps: int, warmup: int, exactitude: int) -> dict:
     # mean part), the attention's Q8_0 and f32 tensors, the router, the KV cache read, the
     # unembedding
     parts = [float(np.mean(m.parties["compresse"][l][2])) for l in range(m.couches)]
+    if m.deltas:
+        # DELTA decoded ahead: the step reads the decoded delta bytes instead of the DELTA streams
+        # (the streams' size from expert 0's part table of each layer, taken as the layer's mean).
+        nbd = sum(m.dims.lignes[j] * (m.dims.colonnes[j] // 32) for j in range(3))
+        for l in range(m.couches):
+            buf, adr, _ = m.parties["compresse"][l]
+            e0 = int(np.flatnonzero(adr)[0])
+            o = int(adr[e0]) - buf.data_ptr()
+            tete = buf[o:o + 64 + 16 * 16].cpu().numpy().tobytes()
+            parts[l] += nbd - octets_flux(tete, (0x03,), (0, 1, 2))
     dq, dkv = 64 * 64, 8 * 64
     att = (dq + 2 * dkv) * 2880 // 32 * 34 + 2880 * dq // 32 * 34 + 4 * (dq + 2 * dkv + 2880 + 64 + 2 * 2880)
     routeur = 4 * 128 * 2880 + 4 * 128
@@ -1256,7 +1268,8 @@ def mesurer_modele(args, steps: int, warmup: int, exactitude: int) -> dict:
         "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "u8",
         "data": "synthetic seeded gpt-oss-120b-shaped weights drawn and encoded on the GPU (.trc v1.2 parts)",
         "config": {"workload": f"config 2: {m.couches} layers, 128 experts top-4, vocab 201,088, context "
-                               f"{args.contexte} seeded tokens, greedy", "positions": [args.contexte, pos]},
+                               f"{args.contexte} seeded tokens, greedy", "positions": [args.contexte, pos],
+                   "delta_predecoded": not args.sans_predecodage},
         "roofline": {"bound": "hbm", "algorithmic_bytes_per_token": int(octets),
                      "achieved": round(octets / (ms * 1e-3) / 1e9, 2), "peak": pic, "unit": "GB/s",
                      "frac": round(octets / (ms * 1e-3) / 1e9 / pic, 4), "peak_source": sorte_pic},

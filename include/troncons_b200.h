@@ -407,13 +407,15 @@ int trc_ligne_q8_0(const void* w, size_t w_octets, uint32_t ligne, uint32_t colo
 int trc_argmax(const float* v, size_t v_octets, uint32_t n, uint32_t* sortie, size_t sortie_octets, void* flux);
 
 /* One layer's tensors on the device (the reference's `Couche` of trc-modele/src/lib.rs:400-418):
- * 152 bytes. f32 vectors, Q8_0 matrices, f16 KV caches of `anneau` cases (sliding layers) or of
- * the context; the experts' parts table (u64 addresses and sizes) and the layer's LUTs. */
+ * 160 bytes. f32 vectors, Q8_0 matrices, f16 KV caches of `anneau` cases (sliding layers) or of
+ * the context; the experts' parts table (u64 addresses and sizes) and the layer's LUTs; `deltas`:
+ * the layer's delta bytes decoded ahead (trc_moe_predecoder_deltas) or 0. */
 typedef struct trc_modele_couche {
     uint64_t attn_norm, wq, bq, wk, bk, wv, bv, wo, bo, puits, post_norm, wr, br;
     uint64_t cache_k, cache_v;
     uint64_t parties, parties_octets, luts;
     uint32_t anneau, reserve;
+    uint64_t deltas;
 } trc_modele_couche;
 
 /* The model (`Hyper` + the resident tensors, trc-modele/src/lib.rs:60-83, 342-356): 176 bytes. */

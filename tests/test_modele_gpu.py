@@ -81,6 +81,26 @@ def test_compresse_et_brut_au_bit(petit):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"step {s}"
 
 
+def test_deltas_predecodes_au_bit(petit):
+    """The same model with every layer's DELTA decoded once at load (deltas_predecodes): 40
+    greedy steps give the logits of the model that decodes DELTA at every step, bit for bit, and
+    so those of its raw parts (the exactness invariant holds with the predecoded scales too)."""
+    import troncons_b200.modele as M
+
+    p = M.Modele(couches=2, d=256, tetes=8, tetes_kv=2, experts=8, k=4, vocab=512, contexte=64, ffn=256,
+                 fenetre=16, graine=7, compresse=True, brut=True, deltas_predecodes=True)
+    assert len(p.deltas) == 2
+    petit.choisir("compresse")
+    la, ja = _glouton(petit, 40)
+    lp, jp = _glouton(p, 40)
+    p.choisir("brut")
+    lb, jb = _glouton(p, 40)
+    assert ja == jp == jb
+    for s, (a, b, c) in enumerate(zip(la, lp, lb)):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"step {s}"
+        assert np.array_equal(a.view(np.uint32), c.view(np.uint32)), f"step {s}"
+
+
 def test_contre_le_port_cpu(petit):
     import oracle as O
     import troncons_b200 as T

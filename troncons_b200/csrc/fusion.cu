@@ -131,7 +131,8 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     Flux fd;
     EnteteRans h;
     bool a_partie;
-    if (a.tous) {  // every expert of the layer, in order
+    if (a.tous) {  // every expert of the layer, in order; one not held here (no part) is skipped
+        if (c.parties[i] == 0) return;
         partie = reinterpret_cast<const uint8_t*>(c.parties[i]);
         taille = c.parties_octets[i];
         a_partie = partie != nullptr && taille >= 64 && (reinterpret_cast<uintptr_t>(partie) & 15u) == 0;

@@ -353,6 +353,7 @@ cudaError_t etape_moe(const trc_modele_config& m, const DispositionModele& d, ui
     k.n_delta = m.n_delta;
     k.n_codes = m.n_codes;
     k.jetons = 1;
+    k.deltas = m.brut ? nullptr : reinterpret_cast<const uint8_t*>(c.deltas);
     return tb::lancer_moe(k, esp + d.moe, d.total - d.moe, f);
 }
 

@@ -13,10 +13,11 @@ _u64, _u32, _vp, _sz, _i32 = C.c_uint64, C.c_uint32, C.c_void_p, C.c_size_t, C.c
 
 
 class ModeleCouche(C.Structure):
-    """trc_modele_couche: 152 bytes."""
+    """trc_modele_couche: 160 bytes."""
     _fields_ = [(n, C.c_uint64) for n in ("attn_norm", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo", "puits",
                                             "post_norm", "wr", "br", "cache_k", "cache_v", "parties",
-                                            "parties_octets", "luts")] + [("anneau", C.c_uint32), ("reserve", C.c_uint32)]
+                                            "parties_octets", "luts")] + [("anneau", C.c_uint32), ("reserve", C.c_uint32),
+                                                                          ("deltas", C.c_uint64)]
 
 
 class ModeleConfig(C.Structure):
@@ -135,7 +136,7 @@ class Modele:
                  contexte: int, ffn: int, fenetre: int = 128, graine: int = 1, compresse: bool = True,
                  brut: bool = False, lot: int = 32, eps: float = 1e-5, rope: ParamsRope | None = None,
                  tenus: tuple | None = None, reduire=None, zipf: float = 0.0, placement: str = "aleatoire",
-                 rangs: int = 1):
+                 rangs: int = 1, deltas_predecodes: bool = False):
         """`tenus` = (debut, fin): draw and encode only the experts [debut, fin) of every layer (an
         expert-parallel share; the others' parts are absent), their rANS tables built from the
         counts of all experts when `reduire` sums the share's counts over the ranks (an
@@ -147,7 +148,11 @@ class Modele:
         picks experts with Zipf(s)-shaped frequencies. `placement` numbers the experts in that
         order: "aleatoire" (a seeded permutation per layer) or "equilibre" (popularity rank q goes
         to expert (q mod rangs) (E / rangs) + q div rangs: each of `rangs` contiguous shares holds
-        every rangs-th most popular expert, a balanced load for expert parallelism)."""
+        every rangs-th most popular expert, a balanced load for expert parallelism).
+
+        `deltas_predecodes`: every layer's DELTA streams decoded once after encoding
+        (trc_moe_predecoder_deltas, 3 x 259,200 bytes per expert), so the compressed step skips
+        the DELTA phase (the same logits)."""
         import torch
 
         import troncons_b200.synth as S
@@ -217,8 +222,35 @@ class Modele:
                 self.parties["brut"].append(self._bruts(blocs, biais, entete_dev, taille_brute, ids))
         del blocs, biais
         torch.cuda.synchronize()
+        self.deltas = []
+        if compresse and deltas_predecodes:
+            self._predecoder_deltas()
         self.actifs = "compresse" if compresse else "brut"
         self._monter()
+
+    def _predecoder_deltas(self) -> None:
+        """Each layer's held experts' DELTA decoded into self.deltas[l] (device uint8)."""
+        import torch
+
+        from . import MoeCouche
+
+        n = int(lib.trc_moe_deltas_octets(C.byref(self.dims), self.experts))
+        ctl = torch.zeros(4 * self.experts, dtype=torch.int32, device="cuda")
+        for l in range(self.couches):
+            _, adr, tailles = self.parties["compresse"][l]
+            ta = torch.from_numpy(adr.view(np.int64)).cuda()
+            tt = torch.from_numpy(tailles.view(np.int64)).cuda()
+            out = torch.empty(n, dtype=torch.uint8, device="cuda")
+            desc = MoeCouche()
+            desc.parties, desc.parties_octets = ta.data_ptr(), tt.data_ptr()
+            desc.experts = self.experts
+            desc.luts = self.luts[l].data_ptr()
+            desc.dims = self.dims
+            verifier(lib.trc_moe_predecoder_deltas(C.byref(desc), out.data_ptr(), n, ctl.data_ptr(), _flux()))
+            torch.cuda.synchronize()
+            self.deltas.append(out)
+        if int(ctl.abs().sum().item()) != 0:
+            raise RuntimeError("DELTA predecode: integrity counters set")
 
     def _encoder(self, blocs, biais, freqs, couche: int, lot: int, taille_src: int, ids: list):
         """The layer's held experts `ids` encoded on the GPU in batches of `lot`, then packed back to
@@ -301,6 +333,8 @@ class Modele:
             c.cache_k, c.cache_v = caches[l][0].data_ptr(), caches[l][1].data_ptr()
             c.parties, c.parties_octets, c.luts = ta.data_ptr(), tt.data_ptr(), self.luts[l].data_ptr()
             c.anneau = t["anneau"]
+            dl = self.deltas[l] if (self.deltas and self.actifs == "compresse") else None
+            c.deltas = dl.data_ptr() if dl is not None else 0
         m = ModeleConfig()
         m.couches, m.d, m.tetes, m.tetes_kv, m.dim_tete = self.couches, self.d, self.tetes, self.tetes_kv, 64
         m.experts, m.k, m.vocab, m.contexte = self.experts, self.k, self.vocab, self.contexte
