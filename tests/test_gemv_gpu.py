@@ -143,3 +143,34 @@ def test_refus_des_tailles_fausses(noyaux):
         noyaux.decoder_expert(petit, petit, petit, T.DimsExpert.gpt_oss(), petit)
     with pytest.raises(T.ErreurUsage):
         noyaux.gemv(petit, petit, petit, 2880, 2880)
+
+
+@pytest.mark.parametrize("formes", [
+    [(2880, 2880)] * 12,                      # decode-then-multiply's gate/up batch of six experts
+    [(16, 64), (32, 8192), (48, 96), (100, 512), (2880, 2880)],  # B = 2 / 256 / odd / R % 16 / gpt-oss
+    [(512, 256), (256, 512), (64, 7936)],
+])
+def test_lot_en_groupes_egal_l_ordre(noyaux, formes):
+    """trc_gemv_lot (rows in groups of 16 per warp, codes and scales staged by bulk copies, the
+    quads' chains in f32x2 FMAs; shapes the groups cannot take fall back to the row walk) against
+    the CPU replica of the library's reduction order, bit for bit, in one launch of mixed shapes:
+    B = 2 to 256 blocks per row, odd B, rows not a multiple of 16, one and two segments per row."""
+    import troncons_b200 as T
+
+    rng = np.random.default_rng(len(formes))
+    mats, xs, ys, attendus = [], [], [], []
+    for j, (R, C) in enumerate(formes):
+        codes, ech, biais = synth(40 + j, R, C)
+        x = rng.standard_normal(C).astype(np.float32)
+        mats.append(t(matrice_slot(codes, ech, biais, R, C)))
+        xs.append(t(x))
+        ys.append(torch.full((R,), float("nan"), dtype=torch.float32, device="cuda"))
+        attendus.append(O.ordre_gemv(codes, ech, biais, x, R, C))
+    descs = (T.DescGemv * len(formes))(*[T.DescGemv(mats[j].data_ptr(), xs[j].data_ptr(), ys[j].data_ptr(), R, C)
+                                         for j, (R, C) in enumerate(formes)])
+    dd = torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).cuda()
+    noyaux.gemv_lot(dd, len(formes), max(R for R, _ in formes))
+    torch.cuda.synchronize()
+    for j, (R, C) in enumerate(formes):
+        y = ys[j].cpu().numpy()
+        assert (y.view(np.uint32) == attendus[j].view(np.uint32)).all(), (R, C)

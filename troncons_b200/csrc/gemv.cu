@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 
 #include "commun.cuh"
+#include "gemv_groupes.cuh"
 #include "mxfp4.cuh"
 #include "noyaux.h"
 
@@ -46,6 +47,34 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv_lot(const DescGemv* __
     if (d.colonnes % 32u != 0 || d.lignes == 0) return;
     gemv_lignes(reinterpret_cast<const uint8_t*>(d.matrice), reinterpret_cast<const float*>(d.x), reinterpret_cast<float*>(d.y),
                 d.lignes, d.colonnes, blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5), gridDim.x * GEMV_WARPS);
+}
+
+// The batch of slot GEMVs in row groups (gemv_groupes.cuh) where the shapes allow: blockIdx.y
+// is the matrix, its blocks share the matrix's staged 2x, each warp takes row groups
+// blockIdx.x * W + warp, + gridDim.x * W. Other shapes take gemv_lignes (the same bits).
+__global__ void __launch_bounds__(256) k_gemv_lot_groupes(const DescGemv* __restrict__ descs) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    attendre_amont();
+    liberer_aval();
+    const DescGemv d = descs[blockIdx.y];
+    if (d.colonnes % 32u != 0 || d.lignes == 0) return;
+    const uint32_t R = d.lignes, C = d.colonnes, B = C / 32u, W = blockDim.x >> 5, warp = threadIdx.x >> 5;
+    const uint8_t* mat = reinterpret_cast<const uint8_t*>(d.matrice);
+    if (!groupes_possibles(R, B)) {
+        gemv_lignes(mat, reinterpret_cast<const float*>(d.x), reinterpret_cast<float*>(d.y), R, C,
+                    blockIdx.x * W + warp, gridDim.x * W);
+        return;
+    }
+    float4* x2g = reinterpret_cast<float4*>(dyn);
+    charger_x2_groupes(x2g, reinterpret_cast<const float*>(d.x), 0u, C);
+    __syncthreads();
+    // The warps whose staging areas fit next to the staged 2x take part (one at least: B <= 256).
+    const uint32_t Wg = max(1u, min(W, warps_groupes(C)));
+    if (warp >= Wg) return;
+    const Disposition dm = disposition_matrice(R, C);
+    uint8_t* zone = dyn + x2g_octets(C) + warp * groupe_octets_warp(B);
+    gemv_groupes<false>(mat, mat + dm.echelles, reinterpret_cast<const float*>(mat + dm.biais), x2g, R, B,
+                        reinterpret_cast<float*>(d.y), 0u, blockIdx.x * Wg + warp, gridDim.x * Wg, zone);
 }
 
 __device__ __forceinline__ float4 charger_x4(const void* x, uint32_t x_bf16, uint32_t c) {
@@ -100,9 +129,20 @@ cudaError_t lancer_gemv(const void* matrice, const float* x, float* y, uint32_t 
     return lancer_pdl(k_gemv, dim3(blocs), dim3(GEMV_WARPS * 32), 0, flux, static_cast<const uint8_t*>(matrice), x, y, R, C);
 }
 
+uint32_t sms_courant() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return uint32_t(sms);
+}
+
+// The batch in row groups: 8 warps and GRP_SMEM bytes per block (one block per SM), the SMs
+// shared out over the matrices in one wave, no more blocks than a matrix has groups.
 cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_max, cudaStream_t flux) {
-    const uint32_t blocs = std::min<uint32_t>((lignes_max + GEMV_WARPS - 1) / GEMV_WARPS, 65535u);
-    return lancer_pdl(k_gemv_lot, dim3(blocs, n, 1), dim3(GEMV_WARPS * 32), 0, flux, descs);
+    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_lot_groupes), int(GRP_SMEM));
+    if (e != cudaSuccess) return e;
+    const uint32_t groupes = (lignes_max + GRP_LIGNES - 1) / GRP_LIGNES;
+    const uint32_t bx = std::max(1u, std::min((groupes + 7u) / 8u, sms_courant() / std::max(1u, n)));
+    return lancer_pdl(k_gemv_lot_groupes, dim3(bx, n, 1), dim3(256), GRP_SMEM, flux, descs);
 }
 
 cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
