@@ -588,6 +588,29 @@ uint64_t trc_moe_deltas_octets(const trc_dims_expert* dims, uint32_t experts);
 int trc_moe_predecoder_deltas(const trc_moe_couche* couche, uint8_t* deltas, uint64_t deltas_octets,
                               uint32_t* controle, void* flux);
 
+/* ---------------------------------------------------------------- expert parallelism over NCCL */
+
+/* New (the reference is single-GPU; its combine is `combiner`, passe.cuh:611-622, driven by
+ * trc-modele/src/lib.rs:533-553): one rank's step of the expert-parallel layer, for a host with
+ * one process per GPU and an NCCL communicator `comm` (ncclComm_t) over them. The rank runs
+ * trc_moe_couche_fusionnee on the experts it holds (couche->expert_debut / expert_fin; its
+ * parts only need to be present for those) with the partial combine (rank 0 adds its share's
+ * weighted sum into the residual, the other ranks write their share's sum alone), then one NCCL
+ * SUM all-reduce of the [jetons][d] f32 residual on `flux`: every rank ends with residual + the
+ * weighted sum over all routed experts (the reference's terms, summed in another order across
+ * GPUs). Every rank calls it with the same tokens and routing (a replicated router). partiel and
+ * echange must be 0 / NULL (the call sets the first). NCCL is resolved at run time
+ * (libnccl.so.2, the host's copy when one is loaded); NCCL errors return TRC_ERR_CUDA with the
+ * text in trc_derniere_erreur. */
+int trc_moe_couche_ep(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* comm, void* flux);
+
+/* New: the communicator for a host with no NCCL binding of its own. trc_nccl_id writes a unique
+ * id (128 bytes) on one rank; after the host has sent it to every rank, each calls
+ * trc_nccl_init with its rank (blocks until all ranks have joined) and later trc_nccl_fin. */
+int trc_nccl_id(uint8_t* id, size_t id_octets);
+int trc_nccl_init(void** comm, uint32_t monde, const uint8_t* id, uint32_t rang);
+int trc_nccl_fin(void* comm);
+
 /* trc_moe_couche_fusionnee, recording evenements[0..5] (cudaEvent_t, each may be NULL) on the
  * stream: before the DELTA phase, after it, after gate/up, after SwiGLU, after down, after the
  * combine (raw parts: no DELTA phase, [1] is recorded with [0]). For timing each phase with CUDA

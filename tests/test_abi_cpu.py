@@ -161,3 +161,18 @@ def test_refus_attention():
     assert T.lib.trc_rope_yarn(v, 1 << 20, v, 1 << 20, 64, 8, 0, C.byref(r), None) == T.TRC_ERR_USAGE
     # a KV case past the cache
     assert T.lib.trc_ecrire_kv(v, 2048, v, 2048, v, 1024, v, 1024, 512, 1, None) == T.TRC_ERR_USAGE
+
+
+def test_refus_couche_ep():
+    """The expert-parallel entry refuses, before touching a device or NCCL, a missing
+    communicator and a descriptor that sets the partial combine or the peer exchange itself."""
+    import ctypes as C
+
+    desc = T.MoeCouche()
+    assert T.lib.trc_moe_couche_ep(C.byref(desc), None, 0, None, None) == T.TRC_ERR_USAGE
+    desc.partiel = 1
+    assert T.lib.trc_moe_couche_ep(C.byref(desc), None, 0, C.c_void_p(1), None) == T.TRC_ERR_USAGE
+    assert "partiel" in T.lib.trc_derniere_erreur().decode()
+    ident = (C.c_uint8 * 128)()
+    assert T.lib.trc_nccl_id(ident, 64) == T.TRC_ERR_USAGE
+    assert T.lib.trc_nccl_init(None, 2, ident, 2) == T.TRC_ERR_USAGE

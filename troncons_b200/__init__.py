@@ -138,6 +138,10 @@ def _charger() -> C.CDLL:
         "trc_synth_matrices": (i32, [u64, u32, u32, u32, u32, vp, vp, i32]),
         "trc_moe_espace_octets": (u64, [pd, u32]),
         "trc_moe_deltas_octets": (u64, [pd, u32]),
+        "trc_moe_couche_ep": (i32, [vp, vp, sz, vp, vp]),
+        "trc_nccl_id": (i32, [vp, sz]),
+        "trc_nccl_init": (i32, [C.POINTER(vp), u32, vp, u32]),
+        "trc_nccl_fin": (i32, [vp]),
         "trc_moe_predecoder_deltas": (i32, [vp, vp, u64, vp, vp]),
         "trc_moe_espace_recouvrant_octets": (u64, [pd, u32]),
         "trc_moe_par_flux_espace_octets": (u64, [pd, u32, u32]),

@@ -157,6 +157,20 @@ class CoucheCarte:
         self._desc = self.descripteur(x, residu, brute, partiel, echange)  # alive while the launch reads it
         self.n.moe_couche(self._desc, self._espace(), flux, evenements)
 
+    def couche_ep(self, x: torch.Tensor, residu: torch.Tensor, comm: int, flux=None, routeur: bool = True) -> None:
+        """Router then this rank's step of the expert-parallel layer through the C-ABI
+        (trc_moe_couche_ep): the fused layer on the experts held here (`tenus`), then the NCCL
+        SUM all-reduce of the residual over the communicator `comm` (an ncclComm_t, e.g. from
+        trc_nccl_init): every rank ends with the whole layer's result."""
+        from . import lib, verifier
+
+        if routeur:
+            self.routeur(x, flux)
+        self._desc = self.descripteur(x, residu, False)
+        e = self._espace()
+        f = (flux or torch.cuda.current_stream()).cuda_stream
+        verifier(lib.trc_moe_couche_ep(C.byref(self._desc), e.data_ptr(), e.numel(), C.c_void_p(comm), f))
+
     def couche_par_flux(self, x: torch.Tensor, residu: torch.Tensor, flux=None, routeur: bool = True,
                         partiel: bool = False):
         """Router then the layer "par flux" (trc_moe_couche_par_flux): each distinct routed expert

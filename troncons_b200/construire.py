@@ -71,7 +71,7 @@ def construire(force: bool = False, verbeux: bool = False, ptxas_v: bool = False
             if r.returncode != 0:
                 raise RuntimeError(f"build failed: {' '.join(c)}\n{r.stdout}\n{r.stderr}")
     tmp = LIB + ".tmp"
-    r = subprocess.run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-lpthread"],
+    r = subprocess.run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-lpthread", "-ldl"],
                        capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed\n{r.stdout}\n{r.stderr}")
