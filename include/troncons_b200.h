@@ -588,6 +588,24 @@ uint64_t trc_moe_deltas_octets(const trc_dims_expert* dims, uint32_t experts);
 int trc_moe_predecoder_deltas(const trc_moe_couche* couche, uint8_t* deltas, uint64_t deltas_octets,
                               uint32_t* controle, void* flux);
 
+/* ---------------------------------------------------------------- the tensor-core expert GEMM */
+
+/* New (the reference multiplies one token at a time, gemv_mxfp4, gemv.cuh:140-161; its prefill
+ * par flux applies the per-token GEMV to every position routed to an expert,
+ * trc-modele/src/lib.rs:607-717): for an expert receiving many tokens at once,
+ * y[t][r] = sum_c W[r][c] x[t][c] + biais[r] on the tensor cores (tcgen05.mma,
+ * kind::mxf8f6f4.block_scale): W the matrix in the slot / raw-part layout (codes: 16 bytes per
+ * 32-block, row-major, 16-aligned; echelles: one E8M0 byte per block; biais f32[lignes] or NULL),
+ * x [n][colonnes] f32 or bf16, quantized on the GPU to MXFP8 (E4M3 elements, one E8M0 scale per 32:
+ * 2^(floor(log2 max|x|) - 8)); f32 accumulation. n = 1 to 256 tokens (the MMA's N, padded to 16);
+ * espace: trc_gemm_mxfp4_espace_octets bytes, 256-aligned (the quantized x). Not bit-identical
+ * to the GEMV (x is quantized): within the tolerance the tests state. *erreur (device u32,
+ * zeroed by the caller) is set to 1 when a bounded wait of the kernel gave up. */
+int trc_gemm_mxfp4(const uint8_t* codes, const uint8_t* echelles, const float* biais, uint32_t lignes, uint32_t colonnes,
+                   const void* x, uint32_t x_bf16, uint32_t n, float* y, void* espace, size_t espace_octets,
+                   uint32_t* erreur, void* flux);
+uint64_t trc_gemm_mxfp4_espace_octets(uint32_t colonnes, uint32_t n);
+
 /* ---------------------------------------------------------------- expert parallelism over NCCL */
 
 /* New (the reference is single-GPU; its combine is `combiner`, passe.cuh:611-622, driven by

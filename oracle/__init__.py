@@ -514,3 +514,47 @@ def bf16(x) -> np.ndarray:
     u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
     u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
     return u.astype(np.uint32).view(np.float32)
+
+
+# ---------------------------------------------------------------- MXFP8 activations, MXFP4 GEMM (f64)
+
+def e4m3(v) -> np.ndarray:
+    """Values rounded to E4M3 (OCP FP8: bias 7, 3 mantissa bits, subnormals from 2^-9, largest 448),
+    nearest with ties to even, saturating at +-448; returned as float64."""
+    v = np.asarray(v, np.float64)
+    a = np.abs(v)
+    e = np.floor(np.log2(np.where(a > 0, a, 1.0)))
+    e = np.maximum(e, -6.0)                      # below 2^-6: the subnormal step 2^-9
+    pas = np.exp2(e - 3.0)
+    q = np.round(a / pas) * pas                  # numpy rounds halves to even
+    return np.sign(v) * np.minimum(q, 448.0)
+
+
+def mxfp8(x, ordre_mma: bool = False):
+    """x [n][C] -> (values [n][C] f64 as the quantized x, scales u8 [n][C/32]): per 32-block,
+    E = floor(log2 max|x|) - 8 (E = -127 for a zero block), scale byte E + 127, elements
+    e4m3(x / 2^E) (the OCP MX rule with E4M3's largest exponent 8). Returns the dequantized
+    values (element = e4m3(x / 2^E) * 2^E) in the natural order."""
+    x = np.asarray(x, np.float64)
+    n, C = x.shape
+    xb = x.reshape(n, C // 32, 32)
+    m = np.abs(xb).max(axis=2)
+    E = np.where(m > 0, np.floor(np.log2(np.where(m > 0, m, 1.0))) - 8, -127).clip(-127, 127)
+    q = e4m3(xb / np.exp2(E)[:, :, None]) * np.exp2(E)[:, :, None]
+    return q.reshape(n, C), (E + 127).astype(np.uint8)
+
+
+def gemm_mxfp4_f64(codes, ech, biais, x_deq, R: int, C: int) -> np.ndarray:
+    """y[n][r] = sum_c W[r][c] x_deq[n][c] + b[r] in f64, W dequantized exactly from the MXFP4
+    blocks (codes: 16 bytes per block, element i low nibble / 16 + i high nibble of byte i;
+    value K[c] 2^(e - 128), K = {0,1,2,3,4,6,8,12} signed by bit 3)."""
+    K = np.array([0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12], np.float64)
+    B = C // 32
+    cb = np.asarray(codes, np.uint8).reshape(R, B, 16)
+    w = np.concatenate([K[cb & 15], K[cb >> 4]], axis=2)          # [R][B][32], elements 0..15 then 16..31
+    w = w * np.exp2(np.asarray(ech, np.float64).reshape(R, B, 1) - 128.0)
+    W = w.reshape(R, C)
+    y = np.asarray(x_deq, np.float64) @ W.T
+    if biais is not None:
+        y = y + np.asarray(biais, np.float64)[None, :]
+    return y

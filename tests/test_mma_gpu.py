@@ -1,0 +1,78 @@
+"""GPU: the MXFP4 expert GEMM on the tensor cores (trc_gemm_mxfp4: tcgen05.mma
+kind::mxf8f6f4.block_scale, the weights' own E2M1 codes and E8M0 block scales, the activations
+quantized to MXFP8 on the GPU), for experts that receive 16 to 256 tokens at once.
+
+Tolerances, stated:
+- against an f64 GEMM of the same operands (the weights dequantized exactly, x quantized by the
+  oracle's restatement of the OCP MX rule): within 1e-5 of max|y| (the products are exact, the
+  tensor core sums them in f32);
+- against the f64 GEMM of the unquantized x (the model's arithmetic): within 3e-2 of max|y|
+  (E4M3 keeps 3 mantissa bits of each activation; 1e-2 typical)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _matrice(graine, R, Cc):
+    import troncons_b200.synth as S
+
+    bl, bi = S.matrices(graine, R, Cc, 1)
+    b = bl[0].reshape(R * (Cc // 32), 17)
+    return b[:, 1:].reshape(-1).copy(), b[:, 0].copy(), bi[0]
+
+
+def _gemm(codes, ech, biais, x, R, Cc, bf16=False):
+    import troncons_b200 as T
+
+    n = x.shape[0]
+    cd, ed, bd = (torch.from_numpy(a).cuda() for a in (codes, ech, biais))
+    xt = torch.from_numpy(x).cuda()
+    if bf16:
+        xt = xt.to(torch.bfloat16)
+    y = torch.full((n, R), float("nan"), dtype=torch.float32, device="cuda")
+    octets = int(T.lib.trc_gemm_mxfp4_espace_octets(Cc, n))
+    esp = torch.empty(octets + 256, dtype=torch.uint8, device="cuda")
+    e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    r = T.lib.trc_gemm_mxfp4(cd.data_ptr(), ed.data_ptr(), bd.data_ptr(), R, Cc, xt.data_ptr(), int(bf16), n,
+                             y.data_ptr(), e0, octets, err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert r == T.TRC_OK, T.lib.trc_derniere_erreur()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, "a bounded wait gave up"
+    return y.cpu().numpy(), (xt.float().cpu().numpy() if bf16 else x)
+
+
+@pytest.mark.parametrize("R,Cc,n", [(128, 128, 16), (256, 2880, 16), (2880, 2880, 64), (200, 96, 24),
+                                    (2880, 2880, 256), (384, 512, 100)])
+def test_gemm_contre_f64(R, Cc, n):
+    codes, ech, biais = _matrice(R + Cc + n, R, Cc)
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal((n, Cc)).astype(np.float32)
+    x[:, :32] *= 1e-3  # a block of small activations: their own scale
+    y, xs = _gemm(codes, ech, biais, x, R, Cc)
+    xq, _ = O.mxfp8(xs)
+    ref_q = O.gemm_mxfp4_f64(codes, ech, biais, xq, R, Cc)
+    m = max(1.0, np.abs(ref_q).max())
+    assert np.abs(y - ref_q).max() <= 1e-5 * m, np.abs(y - ref_q).max() / m
+    ref = O.gemm_mxfp4_f64(codes, ech, biais, xs, R, Cc)
+    assert np.abs(y - ref).max() <= 3e-2 * max(1.0, np.abs(ref).max())
+
+
+def test_gemm_bf16_et_refus():
+    import troncons_b200 as T
+
+    codes, ech, biais = _matrice(3, 256, 512)
+    x = np.random.default_rng(1).standard_normal((32, 512)).astype(np.float32)
+    y, xs = _gemm(codes, ech, biais, x, 256, 512, bf16=True)
+    xq, _ = O.mxfp8(xs)
+    ref_q = O.gemm_mxfp4_f64(codes, ech, biais, xq, 256, 512)
+    assert np.abs(y - ref_q).max() <= 1e-5 * max(1.0, np.abs(ref_q).max())
+    v = C.c_void_p(256)
+    assert T.lib.trc_gemm_mxfp4(v, v, None, 256, 100, v, 0, 16, v, v, 1 << 20, v, None) == T.TRC_ERR_USAGE
+    assert T.lib.trc_gemm_mxfp4(v, v, None, 256, 512, v, 0, 257, v, v, 1 << 20, v, None) == T.TRC_ERR_USAGE

@@ -139,6 +139,8 @@ def _charger() -> C.CDLL:
         "trc_moe_espace_octets": (u64, [pd, u32]),
         "trc_moe_deltas_octets": (u64, [pd, u32]),
         "trc_moe_couche_ep": (i32, [vp, vp, sz, vp, vp]),
+        "trc_gemm_mxfp4": (i32, [vp, vp, vp, u32, u32, vp, u32, u32, vp, vp, sz, vp, vp]),
+        "trc_gemm_mxfp4_espace_octets": (u64, [u32, u32]),
         "trc_nccl_id": (i32, [vp, sz]),
         "trc_nccl_init": (i32, [C.POINTER(vp), u32, vp, u32]),
         "trc_nccl_fin": (i32, [vp]),

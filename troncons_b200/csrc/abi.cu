@@ -381,6 +381,28 @@ uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t 
     return k <= tb::RECOUVRE_MAX ? e.total_recouvrant : e.total;
 }
 
+uint64_t trc_gemm_mxfp4_espace_octets(uint32_t colonnes, uint32_t n) {
+    if (colonnes == 0 || colonnes % 32 || n == 0 || n > 256) return 0;
+    return tb::gemm_mxfp4_espace(colonnes, n);
+}
+
+int trc_gemm_mxfp4(const uint8_t* codes, const uint8_t* echelles, const float* biais, uint32_t lignes, uint32_t colonnes,
+                   const void* x, uint32_t x_bf16, uint32_t n, float* y, void* espace, size_t espace_octets,
+                   uint32_t* erreur, void* flux) {
+    if (lignes == 0 || colonnes == 0 || colonnes % 32) return usage("%u x %u matrix (columns a multiple of 32)", lignes, colonnes);
+    if (n == 0 || n > 256) return usage("%u tokens (1 to 256)", n);
+    if (codes == nullptr || echelles == nullptr || x == nullptr || y == nullptr || espace == nullptr || erreur == nullptr)
+        return usage("gemm: a device buffer is missing");
+    if (!aligne(codes, 16) || !aligne(espace, 256) || !aligne(x, x_bf16 ? 2 : 4) || !aligne(y, 4))
+        return usage("gemm: codes 16-aligned, workspace 256-aligned");
+    if (espace_octets < tb::gemm_mxfp4_espace(colonnes, n))
+        return usage("gemm workspace of %zu bytes, %llu needed", espace_octets,
+                     (unsigned long long)tb::gemm_mxfp4_espace(colonnes, n));
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_gemm_mxfp4(codes, echelles, biais, x, x_bf16 ? 1u : 0u, y, lignes, colonnes, n,
+                                        static_cast<uint8_t*>(espace), erreur, static_cast<cudaStream_t>(flux)));
+}
+
 uint64_t trc_moe_deltas_octets(const trc_dims_expert* dims, uint32_t experts) {
     if (dims == nullptr || experts == 0) return 0;
     return tb::deltas_octets(dims->lignes, dims->colonnes, experts);

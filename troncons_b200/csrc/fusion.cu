@@ -1036,21 +1036,23 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
         if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_brut_groupes), int(GRP_SMEM))) != cudaSuccess) return e;
         int dev = 0, sms = 148;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        auto gx = [&](uint32_t R, uint32_t plans) {
+        // Warps per block: as many double-buffered staging areas as fit beside the staged 2x.
+        const uint32_t W0 = std::max(1u, warps_groupes(c.colonnes[0])), W2 = std::max(1u, warps_groupes(c.colonnes[2]));
+        auto gx = [&](uint32_t R, uint32_t plans, uint32_t W) {
             const uint32_t groupes = (R + GRP_LIGNES - 1) / GRP_LIGNES;
-            return std::max(1u, std::min((groupes + 7u) / 8u, uint32_t(sms) / plans));
+            return std::max(1u, std::min((groupes + W - 1u) / W, uint32_t(sms) / plans));
         };
         marque(1);
-        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[0], 2u * na), 2, na), dim3(256), GRP_SMEM, flux, a)) !=
-            cudaSuccess)
+        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[0], 2u * na, W0), 2, na), dim3(32u * W0), GRP_SMEM,
+                            flux, a)) != cudaSuccess)
             return e;
         marque(2);
         if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[2], na), 1, na), dim3(256), GRP_SMEM, flux, a)) !=
-            cudaSuccess)
+        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[2], na, W2), 1, na), dim3(32u * W2), GRP_SMEM, flux,
+                            a)) != cudaSuccess)
             return e;
         marque(4);
     } else {

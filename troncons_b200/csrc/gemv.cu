@@ -141,7 +141,7 @@ cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_m
     cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_lot_groupes), int(GRP_SMEM));
     if (e != cudaSuccess) return e;
     const uint32_t groupes = (lignes_max + GRP_LIGNES - 1) / GRP_LIGNES;
-    const uint32_t bx = std::max(1u, std::min((groupes + 7u) / 8u, sms_courant() / std::max(1u, n)));
+    const uint32_t bx = std::max(1u, std::min((groupes + 3u) / 4u, sms_courant() / std::max(1u, n)));
     return lancer_pdl(k_gemv_lot_groupes, dim3(bx, n, 1), dim3(256), GRP_SMEM, flux, descs);
 }
 

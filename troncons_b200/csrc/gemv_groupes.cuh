@@ -12,8 +12,8 @@
 //
 // Memory: each warp stages its group's code bytes (16 rows x B x 16 bytes, contiguous) and
 // scales (16 x B bytes) with one bulk copy each (cp.async.bulk, the TMA engine, completion on an
-// mbarrier; no multicast), then computes from shared memory; the other warps of the SM keep
-// their copies in flight meanwhile.
+// mbarrier; no multicast) into one of two buffers, and multiplies the previous group from the
+// other while that copy is in flight.
 //
 // Arithmetic per block (the order of mxfp4.cuh): quad q of the block (bytes 4q..4q+3) gives
 // p_q = fmaf chain over k = 0..3 of (low nibble of byte 4q+k) x2[32b+4q+k] then (high nibble)
@@ -38,10 +38,12 @@ __host__ __device__ __forceinline__ bool groupes_possibles(uint32_t R, uint32_t 
     return B >= 2u && B <= GRP_B_MAX && (B % 2u) == 0 && R % GRP_LIGNES == 0;
 }
 
-// Shared bytes per warp: the group's codes and scales (16-aligned), and its mbarrier.
-__host__ __device__ __forceinline__ uint32_t groupe_octets_warp(uint32_t B) {
-    return GRP_LIGNES * B * 16u + ((GRP_LIGNES * B + 15u) & ~15u) + 16u;
+// Shared bytes of one staging buffer (a group's codes and scales, 16-aligned) and per warp: two
+// buffers (the next group's copy lands while the current one is multiplied) and their mbarriers.
+__host__ __device__ __forceinline__ uint32_t groupe_tampon(uint32_t B) {
+    return GRP_LIGNES * B * 16u + ((GRP_LIGNES * B + 15u) & ~15u);
 }
+__host__ __device__ __forceinline__ uint32_t groupe_octets_warp(uint32_t B) { return 2u * groupe_tampon(B) + 16u; }
 __host__ __device__ __forceinline__ uint32_t x2g_octets(uint32_t C) { return (C / 32u) * GRP_X2_PAS * 16u; }
 
 // Dynamic shared memory of a grouped launch (one block per SM), and the warps whose staging
@@ -138,28 +140,39 @@ __device__ inline bool gemv_groupes(const uint8_t* __restrict__ codes, const uin
                                     uint32_t B, float* __restrict__ sortie, uint32_t K, uint32_t g0, uint32_t pas,
                                     uint8_t* zone) {
     const uint32_t voie = threadIdx.x & 31u, a = voie >> 3, g = voie & 7u;
-    uint8_t* zc = zone;
-    uint8_t* ze = zone + GRP_LIGNES * B * 16u;
-    uint64_t* mb = reinterpret_cast<uint64_t*>(zone + groupe_octets_warp(B) - 16u);
-    const uint32_t octets_c = GRP_LIGNES * B * 16u, octets_e = GRP_LIGNES * B;
-    const uint32_t octets_e16 = (octets_e + 15u) & ~15u;
-    if (voie == 0) mbar_init(mb, 1u);
+    const uint32_t octets_c = GRP_LIGNES * B * 16u, octets_e = GRP_LIGNES * B;  // 16 x B: a multiple of 16
+    const uint32_t tampon = groupe_tampon(B);
+    uint64_t* mb = reinterpret_cast<uint64_t*>(zone + 2u * tampon);  // mb[0], mb[1]
+    if (voie == 0) {
+        mbar_init(mb, 1u);
+        mbar_init(mb + 1, 1u);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     __syncwarp();
-    uint32_t parite = 0;
     const uint32_t ngr = R / GRP_LIGNES;
-    for (uint32_t gr = g0; gr < ngr; gr += pas) {
-        const uint32_t R0 = gr * GRP_LIGNES;
-        if (voie == 0) {
-            // The previous group's reads (all lanes, ordered by the __syncwarp below) come before
-            // the copy engine overwrites the area.
+    // Lane 0 stages group gr into buffer t (after the previous reads of that buffer, which the
+    // caller ordered with __syncwarp, as the copy engine is another proxy).
+    auto lancer = [&](uint32_t gr, uint32_t t) {
+        if (voie == 0 && gr < ngr) {
+            const uint32_t R0 = gr * GRP_LIGNES;
+            uint8_t* z = zone + t * tampon;
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            mbar_attendre_octets(mb, octets_c + octets_e16);
-            copie_bulk(zc, codes + uint64_t(R0) * B * 16u, octets_c, mb);
-            copie_bulk(ze, echelles + uint64_t(R0) * B, octets_e16, mb);
+            mbar_attendre_octets(mb + t, octets_c + octets_e);
+            copie_bulk(z, codes + uint64_t(R0) * B * 16u, octets_c, mb + t);
+            copie_bulk(z + octets_c, echelles + uint64_t(R0) * B, octets_e, mb + t);
         }
-        if (!mbar_attendre(mb, parite)) {
-            mbar_attendre(mb, parite);  // a second bounded wait for the copy still in flight
+    };
+    lancer(g0, 0u);
+    lancer(g0 + pas, 1u);
+    uint32_t parite[2] = {0u, 0u};
+    uint32_t t = 0;
+    for (uint32_t gr = g0; gr < ngr; gr += pas, t ^= 1u) {
+        const uint32_t R0 = gr * GRP_LIGNES;
+        const uint8_t* zc = zone + t * tampon;
+        const uint8_t* ze = zc + octets_c;
+        if (!mbar_attendre(mb + t, parite[t])) {
+            mbar_attendre(mb + t, parite[t]);        // second bounded waits for the copies in flight
+            mbar_attendre(mb + (t ^ 1u), parite[t ^ 1u]);
             // The group's outputs read NaN rather than stale values.
             for (uint32_t i = voie; i < GRP_LIGNES; i += 32u) {
                 if (PARTS) {
@@ -170,7 +183,7 @@ __device__ inline bool gemv_groupes(const uint8_t* __restrict__ codes, const uin
             }
             return false;
         }
-        parite ^= 1u;
+        parite[t] ^= 1u;
         // Lane (a, g): slot g of rows R0 + a + 4 i; column blocks c, c + 8, ... with
         // (R0 + a) B + c = g (mod 8).
         const uint32_t c0 = (g + 8u - ((R0 + a) * B) % 8u) % 8u;
@@ -199,7 +212,8 @@ __device__ inline bool gemv_groupes(const uint8_t* __restrict__ codes, const uin
                     acc[i][1] = fmaf(s, sc, acc[i][1]);
             }
         }
-        __syncwarp();  // every lane is done with the staged group before the next copy lands
+        __syncwarp();  // every lane is done with this buffer before the copy engine refills it
+        lancer(gr + 2u * pas, t);
 #pragma unroll
         for (uint32_t i = 0; i < 4; ++i) {
             const float P0 = arbre8_groupe(acc[i][0]);

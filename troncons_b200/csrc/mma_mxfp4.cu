@@ -1,0 +1,296 @@
+// troncons_b200 — the MXFP4 expert GEMM on the 5th-generation tensor cores, for experts that
+// receive many tokens at once (a prefill batch par flux, an expert-parallel share at batch 64):
+// Y[n][r] = sum_c W[r][c] X[n][c] + b[r], W an expert matrix in the slot / raw-part layout (16
+// code bytes and one E8M0 scale per 32-block, row-major), X f32 or bf16 activations.
+//
+// tcgen05.mma.kind::mxf8f6f4.block_scale, M = 128 rows, N = the tokens (8 to 256), K = 32 per
+// instruction: A = the weights as E2M1 with their own E8M0 block scales, B = the activations as
+// MXFP8 (E4M3 elements, one E8M0 scale per 32, the OCP MX rule: scale = 2^(floor(log2 max|x|)
+// - 8)), f32 accumulation in tensor memory. The block scales are the hardware's (one per row or
+// token and 32-block, read from tensor memory); the weights are not dequantized on CUDA cores.
+//
+// Layout of a 32-block in the K order the MMA sees. The file stores element i of a block in the
+// low nibble of byte i and element 16 + i in the high nibble. Read as a packed E2M1 vector (two
+// elements per byte, the low nibble first), those 16 bytes are the block's elements in the order
+// k' = 2i -> element i, k' = 2i + 1 -> element 16 + i. The MMA sums over K, so the activations are
+// quantized into that same order and no weight byte is moved: the two 8-byte halves of a block
+// are copied as they are into the unpacked shared-memory form of 4-bit operands (16 elements in
+// 8 bytes, then 8 bytes of padding, per 16 bytes).
+//
+// Shared memory, K-major without swizzle: 8-row x 16-byte core matrices, the next core matrix
+// along K 128 bytes further (LBO), the next 8 rows 1,024 bytes further (SBO), one chunk of 128 K
+// (four MMAs) at a time. Scale factors in tensor memory, the layout of tcgen05.cp's 32x128b
+// copies replicated to the four lane quadrants: lane (m mod 32), column m / 32 + base, byte =
+// the 32-block within the chunk (the instruction descriptor's and the address's scale-factor id).
+//
+// One CTA of 4 warps per 128-row tile: the warps stage the chunk (cp.async of the weight halves
+// and the quantized activations) and write its scale factors to tensor memory, thread 0 issues the
+// MMAs and commits them to an mbarrier that every thread waits on (bounded) before the next
+// chunk; the epilogue reads the accumulator (tcgen05.ld), adds the bias and stores Y. Every wait
+// is bounded: a wait that gives up sets the caller's error word, waits again (bounded) for the
+// MMAs in flight, frees the tensor memory and returns.
+#include <cstdint>
+
+#include "commun.cuh"
+#include "noyaux.h"
+
+namespace tb {
+
+constexpr uint32_t MMA_M = 128;        // rows per CTA (one MMA's M); chunks of 128 K (four MMAs)
+constexpr uint32_t MMA_FILS = 128;     // four warps: one per tensor-memory lane quadrant
+
+__host__ __device__ __forceinline__ uint32_t mma_n_pad(uint32_t N) { return (N + 15u) & ~15u; }
+__host__ __device__ __forceinline__ uint32_t mma_tmem_colonnes(uint32_t N) {
+    const uint32_t besoin = mma_n_pad(N) + 4u + 8u;  // accumulator, then SFA (4) and SFB (8)
+    uint32_t c = 32u;
+    while (c < besoin) c <<= 1;
+    return c;
+}
+// Shared bytes: A tile (128 rows x 128 bytes), B tile (Npad rows x 128 bytes), mbarrier, tmem base,
+// and 8 KB of slack past the tiles (never read by a correct descriptor).
+__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N) {
+    return MMA_M * 128u + mma_n_pad(N) * 128u + 32u + 8192u;
+}
+
+// Offset in a K-major no-swizzle tile of row r and byte k (0..127) of the chunk.
+__device__ __forceinline__ uint32_t mma_off(uint32_t r, uint32_t k) {
+    return (r >> 3) * 1024u + (k >> 4) * 128u + (r & 7u) * 16u + (k & 15u);
+}
+
+__device__ __forceinline__ uint64_t mma_desc(uint32_t adresse) {
+    uint64_t d = 0;
+    d |= uint64_t((adresse >> 4) & 0x3FFFu);
+    d |= uint64_t(128u >> 4) << 16;   // leading byte offset: the next core matrix along K
+    d |= uint64_t(1024u >> 4) << 32;  // stride byte offset: the next 8 rows
+    d |= uint64_t(1) << 46;           // descriptor version of sm_100
+    return d;                         // base offset 0, no swizzle
+}
+
+// Instruction descriptor: E2M1 A, E4M3 B, f32 D, K-major both, E8M0 scales, M = 128, N.
+__device__ __forceinline__ uint32_t mma_idesc(uint32_t N, uint32_t sf) {
+    uint32_t d = 0;
+    d |= (sf & 3u) << 4;          // B scale-factor id
+    d |= 5u << 7;                 // A: E2M1
+    d |= 0u << 10;                // B: E4M3
+    d |= (N >> 3) << 17;          // N / 8
+    d |= 1u << 23;                // scale format E8M0
+    d |= (MMA_M >> 4) << 24;      // M / 16
+    d |= (sf & 3u) << 29;         // A scale-factor id
+    return d;
+}
+
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(adresse_partagee(smem)), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(taddr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+
+// The weight halves of rows r0 .. r0 + 127, 32-blocks kb0 .. kb0 + nkb - 1, into the A tile.
+__device__ __forceinline__ void charger_a(uint8_t* ta, const uint8_t* codes, uint32_t R, uint32_t B, uint32_t r0,
+                                          uint32_t kb0, uint32_t nkb) {
+    for (uint32_t t = threadIdx.x; t < MMA_M * 4u * 2u; t += MMA_FILS) {
+        const uint32_t r = t >> 3, kb = (t >> 1) & 3u, h = t & 1u;
+        if (kb >= nkb || r0 + r >= R) continue;
+        const uint8_t* src = codes + (uint64_t(r0 + r) * B + kb0 + kb) * 16u + 8u * h;
+        cp_async8(ta + mma_off(r, 32u * kb + 16u * h), src);
+    }
+}
+
+// The quantized activations of the chunk (32 bytes per token and block) into the B tile.
+__device__ __forceinline__ void charger_b(uint8_t* tb_, const uint8_t* xq, uint32_t C, uint32_t N, uint32_t kb0,
+                                          uint32_t nkb) {
+    for (uint32_t t = threadIdx.x; t < N * 4u * 2u; t += MMA_FILS) {
+        const uint32_t n = t >> 3, kb = (t >> 1) & 3u, h = t & 1u;
+        if (kb >= nkb) continue;
+        cp_async16(tb_ + mma_off(n, 32u * kb + 16u * h), xq + uint64_t(n) * C + 32u * (kb0 + kb) + 16u * h, 16u);
+    }
+}
+
+// Scale bytes of row (or token) m for blocks kb0 .. kb0 + 3 (0 beyond nkb or past the rows).
+__device__ __forceinline__ uint32_t quatre_echelles(const uint8_t* ech, uint32_t m, uint32_t lignes, uint32_t B,
+                                                    uint32_t kb0, uint32_t nkb) {
+    if (m >= lignes) return 0u;
+    uint32_t v = 0;
+    for (uint32_t k = 0; k < nkb; ++k) v |= uint32_t(__ldg(ech + uint64_t(m) * B + kb0 + k)) << (8u * k);
+    return v;
+}
+
+struct ArgsMma {
+    const uint8_t* codes;  // W: 16 bytes per 32-block, row-major
+    const uint8_t* ech;    // W: E8M0 per block
+    const float* biais;    // R f32, or null
+    const uint8_t* xq;     // X quantized: [N][C] E4M3 in the blocks' MMA order
+    const uint8_t* xs;     // X scales: [N][C / 32] E8M0
+    float* y;              // [N][R]
+    uint32_t R, C, N;
+    uint32_t* erreur;      // set to 1 when a bounded wait gave up
+};
+
+__global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a) {
+    extern __shared__ __align__(1024) uint8_t dyn[];
+    const uint32_t Np = mma_n_pad(a.N);
+    uint8_t* ta = dyn;
+    uint8_t* tbt = dyn + MMA_M * 128u;
+    uint64_t* mb = reinterpret_cast<uint64_t*>(tbt + Np * 128u);
+    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mb + 1);
+    const uint32_t warp = threadIdx.x >> 5, voie = threadIdx.x & 31u;
+    const uint32_t r0 = blockIdx.x * MMA_M, B = a.C / 32u;
+    const uint32_t ncol = mma_tmem_colonnes(a.N);
+    const uint32_t col_acc = 0, col_sfa = Np, col_sfb = col_sfa + 4u;
+
+    // Padding bytes (and rows past R or N) stay zero; only the data halves are ever written.
+    for (uint32_t i = threadIdx.x; i < (MMA_M + Np) * 128u / 16u; i += MMA_FILS)
+        reinterpret_cast<uint4*>(dyn)[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        mbar_init(mb, 1u);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         adresse_partagee(tmem_base_s)),
+                     "r"(ncol)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const uint32_t tmem = *tmem_base_s;
+    attendre_amont();
+    liberer_aval();
+
+    const uint32_t nchunks = (B + 3u) / 4u;
+    uint32_t parite = 0;
+    bool ok = true;
+    const uint32_t quadrant = (warp & 3u) * 32u;
+    for (uint32_t ch = 0; ch < nchunks && ok; ++ch) {
+        const uint32_t kb0 = 4u * ch, nkb = min(4u, B - kb0);
+        charger_a(ta, a.codes, a.R, B, r0, kb0, nkb);
+        charger_b(tbt, a.xq, a.C, a.N, kb0, nkb);
+        // Scale factors: lane quadrant q, lane l, column c: rows (tokens) l + 32 c, bytes = blocks.
+        {
+            uint32_t v[4];
+#pragma unroll
+            for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.ech, r0 + voie + 32u * c, a.R, B, kb0, nkb);
+            tmem_st4(tmem + (quadrant << 16) + col_sfa, v[0], v[1], v[2], v[3]);
+#pragma unroll
+            for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.xs, voie + 32u * c, a.N, B, kb0, nkb);
+            tmem_st4(tmem + (quadrant << 16) + col_sfb, v[0], v[1], v[2], v[3]);
+            if (Np > 128u) {  // tokens 128 .. 255: four more columns
+#pragma unroll
+                for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.xs, 128u + voie + 32u * c, a.N, B, kb0, nkb);
+                tmem_st4(tmem + (quadrant << 16) + col_sfb + 4u, v[0], v[1], v[2], v[3]);
+            }
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+            for (uint32_t kb = 0; kb < nkb; ++kb) {
+                const uint64_t da = mma_desc(adresse_partagee(ta) + 256u * kb);
+                const uint64_t db = mma_desc(adresse_partagee(tbt) + 256u * kb);
+                const uint32_t idesc = mma_idesc(Np, kb);
+                const uint32_t sfa = tmem + col_sfa + (kb << 30), sfb = tmem + col_sfb + (kb << 30);
+                const uint32_t acc = (ch > 0 || kb > 0) ? 1u : 0u;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+                        tmem + col_acc),
+                    "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+                    : "memory");
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                             adresse_partagee(mb))
+                         : "memory");
+        }
+        // Every thread waits for the chunk's MMAs before its tiles and scale factors are reused.
+        ok = mbar_attendre(mb, parite);
+        parite ^= 1u;
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    }
+    if (!ok) {
+        if (threadIdx.x == 0) atomicExch(a.erreur, 1u);
+        mbar_attendre(mb, parite ^ 1u);  // a second bounded wait for the MMAs in flight
+    } else {
+        // Epilogue: warp q reads rows r0 + 32 q + lane, 8 tokens at a time.
+        const uint32_t r = r0 + quadrant + voie;
+        const float bias = (a.biais != nullptr && r < a.R) ? a.biais[r] : 0.0f;
+        for (uint32_t n0 = 0; n0 < Np; n0 += 8u) {
+            uint32_t v[8];
+            tmem_ld8(tmem + (quadrant << 16) + col_acc + n0, v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+            if (r < a.R)
+                for (uint32_t j = 0; j < 8u; ++j)
+                    if (n0 + j < a.N) a.y[uint64_t(n0 + j) * a.R + r] = __uint_as_float(v[j]) + bias;
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(ncol) : "memory");
+    }
+}
+
+// X (f32 or bf16, [N][C]) into MXFP8: per token and 32-block, E = floor(log2 max|x|) - 8 (the
+// largest E4M3 exponent), scale byte E + 127 (E = -127 for an all-zero block), elements
+// x / 2^E rounded to E4M3 (nearest even, saturating at 448), written in the block's MMA order
+// (k' = 2i <- element i, k' = 2i + 1 <- element 16 + i). One warp per (token, block).
+__global__ void __launch_bounds__(256) k_quantifier_mxfp8(const void* x, uint32_t bf16, uint32_t C, uint32_t N,
+                                                          uint8_t* xq, uint8_t* xs) {
+    attendre_amont();
+    liberer_aval();
+    const uint32_t B = C / 32u;
+    const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5), voie = threadIdx.x & 31u;
+    if (w >= N * B) return;
+    const uint32_t n = w / B, b = w % B;
+    const uint64_t i = uint64_t(n) * C + 32u * b + voie;
+    const float v = bf16 ? __uint_as_float(uint32_t(static_cast<const uint16_t*>(x)[i]) << 16) : static_cast<const float*>(x)[i];
+    float m = fabsf(v);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, d));
+    int E = -127;
+    if (m > 0.0f) {
+        const int em = int((__float_as_uint(m) >> 23) & 255u) - 127;  // floor(log2 m) (subnormals: -127)
+        E = max(-127, min(127, em - 8));
+    }
+    const float q = v * __uint_as_float(uint32_t(127 - E) << 23);  // x / 2^E, exact (|E| <= 127)
+    uint16_t paire;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(paire) : "f"(0.0f), "f"(q));
+    const uint32_t kp = voie < 16u ? 2u * voie : 2u * (voie - 16u) + 1u;
+    xq[uint64_t(n) * C + 32u * b + kp] = uint8_t(paire & 0xFFu);
+    if (voie == 0) xs[uint64_t(n) * B + b] = uint8_t(E + 127);
+}
+
+uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N) { return uint64_t(mma_n_pad(N)) * C + uint64_t(mma_n_pad(N)) * (C / 32u); }
+
+cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const float* biais, const void* x, uint32_t x_bf16,
+                              float* y, uint32_t R, uint32_t C, uint32_t N, uint8_t* espace, uint32_t* erreur,
+                              cudaStream_t flux) {
+    uint8_t* xq = espace;
+    uint8_t* xs = espace + uint64_t(mma_n_pad(N)) * C;
+    const uint32_t B = C / 32u;
+    cudaError_t e = lancer_pdl(k_quantifier_mxfp8, dim3((N * B + 7u) / 8u), dim3(256), 0, flux, x, x_bf16, C, N, xq, xs);
+    if (e != cudaSuccess) return e;
+    const uint32_t smem = mma_smem(N);
+    if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
+    ArgsMma a{codes, ech, biais, xq, xs, y, R, C, N, erreur};
+    return lancer_pdl(k_gemm_mxfp4, dim3((R + MMA_M - 1) / MMA_M), dim3(MMA_FILS), smem, flux, a);
+}
+
+}  // namespace tb
