@@ -799,7 +799,7 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
     ep = ModeleEP(r, w, echange="nccl", par_rang=b, moe=args.moe, couches=args.couches, d=2880, tetes=64, tetes_kv=8,
                   experts=args.experts, k=args.k, vocab=201088, contexte=args.contexte + warmup + steps + 2, ffn=2880,
                   fenetre=128, graine=args.graine, compresse=True, brut=False, zipf=args.zipf,
-                  placement=args.placement)
+                  placement=args.placement, deltas_predecodes=not args.sans_predecodage)
     torch.cuda.synchronize()
     t_gen = time.time() - t0
     # each sequence its own seeded context
@@ -862,7 +862,7 @@ def mesurer_modele_ep(args, steps: int, warmup: int) -> dict:
             "workload": f"config 3: {args.couches} layers, {args.experts} experts top-{args.k} ({fin - debut} per GPU), "
                         f"{b} sequence(s) per GPU, context {args.contexte} seeded tokens, attention on each sequence's "
                         "GPU, MoE inputs all-gathered and the shares' sums reduce-scattered over NCCL per layer",
-            "exchange": "nccl",
+            "exchange": "nccl", "delta_predecoded": not args.sans_predecodage,
             "generation_s": round(t_gen, 1), "context_s": round(t_ctx, 1)}
 
 

@@ -48,6 +48,7 @@ _STRUCTS = {
     "trc_params_rope": (T.ParamsRope, 48),
     "trc_params_attention": (T.ParamsAttention, 32),
     "trc_juge_position": (J.JugePosition, 48),
+    "trc_desc_gemm": (T.DescGemm, 56),
 }
 
 

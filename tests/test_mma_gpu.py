@@ -76,3 +76,36 @@ def test_gemm_bf16_et_refus():
     v = C.c_void_p(256)
     assert T.lib.trc_gemm_mxfp4(v, v, None, 256, 100, v, 0, 16, v, v, 1 << 20, v, None) == T.TRC_ERR_USAGE
     assert T.lib.trc_gemm_mxfp4(v, v, None, 256, 512, v, 0, 257, v, v, 1 << 20, v, None) == T.TRC_ERR_USAGE
+
+
+def test_lot_egal_seul():
+    """A batch of GEMMs of different shapes (trc_gemm_mxfp4_lot: one quantization launch, one MMA
+    launch with the matrix as grid y) gives each matrix's single-call bits."""
+    import troncons_b200 as T
+
+    formes = [(2880, 2880, 16), (256, 512, 64), (384, 2880, 33)]
+    rng = np.random.default_rng(77)
+    garde, descs, attendus = [], [], []
+    for j, (R, Cc, n) in enumerate(formes):
+        codes, ech, biais = _matrice(90 + j, R, Cc)
+        x = rng.standard_normal((n, Cc)).astype(np.float32)
+        y1, _ = _gemm(codes, ech, biais, x, R, Cc)
+        attendus.append(y1)
+        t = [torch.from_numpy(a).cuda() for a in (codes, ech, biais, x)]
+        y = torch.full((n, R), float("nan"), dtype=torch.float32, device="cuda")
+        garde += t + [y]
+        descs.append(T.DescGemm(t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), t[3].data_ptr(), y.data_ptr(),
+                                R, Cc, n, 0))
+    nb = len(formes)
+    dd = torch.frombuffer(bytearray(bytes((T.DescGemm * nb)(*descs))), dtype=torch.uint8).cuda()
+    octets = int(T.lib.trc_gemm_mxfp4_lot_espace_octets(2880, 64, nb))
+    esp = torch.empty(octets + 256, dtype=torch.uint8, device="cuda")
+    e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert T.lib.trc_gemm_mxfp4_lot(dd.data_ptr(), nb, 2880, 2880, 64, e0, octets, err.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream) == T.TRC_OK, T.lib.trc_derniere_erreur()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for j in range(nb):
+        y = garde[5 * j + 4].cpu().numpy()
+        assert np.array_equal(y.view(np.uint32), attendus[j].view(np.uint32)), formes[j]

@@ -92,6 +92,14 @@ class ParamsAttention(C.Structure):
         return cls(64, 8, 64, debut, fin, fenetre, 0.125, 0)
 
 
+class DescGemm(C.Structure):
+    """trc_desc_gemm (56 bytes): one matrix of a batch of tensor-core GEMMs."""
+
+    _fields_ = [("codes", C.c_uint64), ("echelles", C.c_uint64), ("biais", C.c_uint64), ("x", C.c_uint64),
+                ("y", C.c_uint64), ("lignes", C.c_uint32), ("colonnes", C.c_uint32), ("n", C.c_uint32),
+                ("x_bf16", C.c_uint32)]
+
+
 class EchangePairs(C.Structure):
     """trc_echange_pairs: every rank's exchange buffer (device addresses in this process), this
     rank, the number of ranks."""
@@ -141,6 +149,8 @@ def _charger() -> C.CDLL:
         "trc_moe_couche_ep": (i32, [vp, vp, sz, vp, vp]),
         "trc_gemm_mxfp4": (i32, [vp, vp, vp, u32, u32, vp, u32, u32, vp, vp, sz, vp, vp]),
         "trc_gemm_mxfp4_espace_octets": (u64, [u32, u32]),
+        "trc_gemm_mxfp4_lot": (i32, [vp, u32, u32, u32, u32, vp, sz, vp, vp]),
+        "trc_gemm_mxfp4_lot_espace_octets": (u64, [u32, u32, u32]),
         "trc_nccl_id": (i32, [vp, sz]),
         "trc_nccl_init": (i32, [C.POINTER(vp), u32, vp, u32]),
         "trc_nccl_fin": (i32, [vp]),

@@ -403,6 +403,26 @@ int trc_gemm_mxfp4(const uint8_t* codes, const uint8_t* echelles, const float* b
                                         static_cast<uint8_t*>(espace), erreur, static_cast<cudaStream_t>(flux)));
 }
 
+uint64_t trc_gemm_mxfp4_lot_espace_octets(uint32_t colonnes_max, uint32_t n_max, uint32_t nb) {
+    if (colonnes_max == 0 || colonnes_max % 32 || n_max == 0 || n_max > 256 || nb == 0) return 0;
+    return tb::gemm_mxfp4_lot_espace(colonnes_max, n_max, nb);
+}
+
+int trc_gemm_mxfp4_lot(const trc_desc_gemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
+                       uint32_t n_max, void* espace, size_t espace_octets, uint32_t* erreur, void* flux) {
+    static_assert(sizeof(trc_desc_gemm) == sizeof(tb::DescGemm), "trc_desc_gemm layout");
+    if (descs == nullptr || nb == 0 || nb > 65535) return usage("%u GEMM descriptors", nb);
+    if (lignes_max == 0 || colonnes_max == 0 || colonnes_max % 32) return usage("%u x %u at most", lignes_max, colonnes_max);
+    if (n_max == 0 || n_max > 256) return usage("%u tokens at most (1 to 256)", n_max);
+    if (espace == nullptr || erreur == nullptr || !aligne(espace, 256)) return usage("gemm batch: workspace 256-aligned");
+    if (espace_octets < tb::gemm_mxfp4_lot_espace(colonnes_max, n_max, nb))
+        return usage("gemm batch workspace of %zu bytes, %llu needed", espace_octets,
+                     (unsigned long long)tb::gemm_mxfp4_lot_espace(colonnes_max, n_max, nb));
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_gemm_mxfp4_lot(reinterpret_cast<const tb::DescGemm*>(descs), nb, lignes_max, colonnes_max, n_max,
+                                            static_cast<uint8_t*>(espace), erreur, static_cast<cudaStream_t>(flux)));
+}
+
 uint64_t trc_moe_deltas_octets(const trc_dims_expert* dims, uint32_t experts) {
     if (dims == nullptr || experts == 0) return 0;
     return tb::deltas_octets(dims->lignes, dims->colonnes, experts);

@@ -137,8 +137,23 @@ struct ArgsMma {
     uint32_t* erreur;      // set to 1 when a bounded wait gave up
 };
 
-__global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a) {
+// Matrix blockIdx.y of a batch: its descriptor (device) and its slice of the workspace.
+__device__ __forceinline__ ArgsMma args_du_lot(const DescGemm* __restrict__ lot, uint8_t* espace, uint64_t tranche,
+                                               uint32_t* erreur) {
+    const DescGemm d = lot[blockIdx.y];
+    uint8_t* xq = espace + tranche * blockIdx.y;
+    return ArgsMma{reinterpret_cast<const uint8_t*>(d.codes), reinterpret_cast<const uint8_t*>(d.echelles),
+                   reinterpret_cast<const float*>(d.biais), xq, xq + uint64_t(mma_n_pad(d.n)) * d.colonnes,
+                   reinterpret_cast<float*>(d.y), d.lignes, d.colonnes, d.n, erreur};
+}
+
+// One launch: `a` (lot == nullptr), or matrix blockIdx.y of a batch (its rows past its own R
+// leave the CTA idle).
+__global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const DescGemm* lot, uint8_t* espace_lot,
+                                                            uint64_t tranche) {
     extern __shared__ __align__(1024) uint8_t dyn[];
+    const ArgsMma a = lot != nullptr ? args_du_lot(lot, espace_lot, tranche, a0.erreur) : a0;
+    if (blockIdx.x * MMA_M >= a.R || a.N == 0) return;
     const uint32_t Np = mma_n_pad(a.N);
     uint8_t* ta = dyn;
     uint8_t* tbt = dyn + MMA_M * 128u;
@@ -252,9 +267,18 @@ __global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a) {
 // x / 2^E rounded to E4M3 (nearest even, saturating at 448), written in the block's MMA order
 // (k' = 2i <- element i, k' = 2i + 1 <- element 16 + i). One warp per (token, block).
 __global__ void __launch_bounds__(256) k_quantifier_mxfp8(const void* x, uint32_t bf16, uint32_t C, uint32_t N,
-                                                          uint8_t* xq, uint8_t* xs) {
+                                                          uint8_t* xq, uint8_t* xs, const DescGemm* lot, uint64_t tranche) {
     attendre_amont();
     liberer_aval();
+    if (lot != nullptr) {  // matrix blockIdx.y of a batch
+        const DescGemm d = lot[blockIdx.y];
+        x = reinterpret_cast<const void*>(d.x);
+        bf16 = d.x_bf16;
+        C = d.colonnes;
+        N = d.n;
+        xq += tranche * blockIdx.y;
+        xs = xq + uint64_t(mma_n_pad(N)) * C;
+    }
     const uint32_t B = C / 32u;
     const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5), voie = threadIdx.x & 31u;
     if (w >= N * B) return;
@@ -285,12 +309,37 @@ cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const fl
     uint8_t* xq = espace;
     uint8_t* xs = espace + uint64_t(mma_n_pad(N)) * C;
     const uint32_t B = C / 32u;
-    cudaError_t e = lancer_pdl(k_quantifier_mxfp8, dim3((N * B + 7u) / 8u), dim3(256), 0, flux, x, x_bf16, C, N, xq, xs);
+    cudaError_t e = lancer_pdl(k_quantifier_mxfp8, dim3((N * B + 7u) / 8u), dim3(256), 0, flux, x, x_bf16, C, N, xq, xs,
+                               static_cast<const DescGemm*>(nullptr), uint64_t(0));
     if (e != cudaSuccess) return e;
     const uint32_t smem = mma_smem(N);
     if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
     ArgsMma a{codes, ech, biais, xq, xs, y, R, C, N, erreur};
-    return lancer_pdl(k_gemm_mxfp4, dim3((R + MMA_M - 1) / MMA_M), dim3(MMA_FILS), smem, flux, a);
+    return lancer_pdl(k_gemm_mxfp4, dim3((R + MMA_M - 1) / MMA_M), dim3(MMA_FILS), smem, flux, a,
+                      static_cast<const DescGemm*>(nullptr), static_cast<uint8_t*>(nullptr), uint64_t(0));
+}
+
+// A batch of nb matrices (descriptors on the device; rows, columns and tokens at most
+// lignes_max, colonnes_max, n_max): one launch quantizes every matrix's x into its workspace
+// slice, one launch runs every matrix's row tiles (grid y = the matrix).
+cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
+                                  uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux) {
+    const uint64_t tranche = (gemm_mxfp4_espace(colonnes_max, n_max) + 255u) & ~uint64_t(255);
+    const uint32_t B = colonnes_max / 32u;
+    cudaError_t e = lancer_pdl(k_quantifier_mxfp8, dim3((n_max * B + 7u) / 8u, nb), dim3(256), 0, flux,
+                               static_cast<const void*>(nullptr), 0u, colonnes_max, n_max, espace,
+                               static_cast<uint8_t*>(nullptr), descs, tranche);
+    if (e != cudaSuccess) return e;
+    const uint32_t smem = mma_smem(n_max);
+    if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
+    ArgsMma a{};
+    a.erreur = erreur;
+    return lancer_pdl(k_gemm_mxfp4, dim3((lignes_max + MMA_M - 1) / MMA_M, nb), dim3(MMA_FILS), smem, flux, a, descs,
+                      espace, tranche);
+}
+
+uint64_t gemm_mxfp4_lot_espace(uint32_t colonnes_max, uint32_t n_max, uint32_t nb) {
+    return uint64_t(nb) * ((gemm_mxfp4_espace(colonnes_max, n_max) + 255u) & ~uint64_t(255));
 }
 
 }  // namespace tb

@@ -112,8 +112,15 @@ cudaError_t lancer_combiner(float* residu, const float* sorties, uint32_t pas, c
                             cudaStream_t flux);
 cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cudaStream_t flux, cudaEvent_t const* ev = nullptr);
 uint64_t deltas_octets(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts);
-// The MXFP4 expert GEMM on the tensor cores (mma_mxfp4.cu).
+// The MXFP4 expert GEMM on the tensor cores (mma_mxfp4.cu); DescGemm mirrors trc_desc_gemm.
+struct DescGemm {
+    uint64_t codes, echelles, biais, x, y;
+    uint32_t lignes, colonnes, n, x_bf16;
+};
 uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N);
+uint64_t gemm_mxfp4_lot_espace(uint32_t colonnes_max, uint32_t n_max, uint32_t nb);
+cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
+                                  uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux);
 cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const float* biais, const void* x, uint32_t x_bf16,
                               float* y, uint32_t R, uint32_t C, uint32_t N, uint8_t* espace, uint32_t* erreur,
                               cudaStream_t flux);

@@ -240,6 +240,8 @@ class ModeleEP:
             d.n_delta = d.n_codes = 0
             d.jetons = self.monde * self.b
             d.expert_debut, d.expert_fin = self.tenus
+            if m.deltas and m.actifs == "compresse":  # DELTA decoded at load
+                d.deltas = m.deltas[l].data_ptr()
             if self.echange == "pairs":
                 d.partiel, d.echange = 0, C.addressof(self.paires)
             else:
