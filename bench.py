@@ -69,6 +69,8 @@ def arguments(argv=None):
     a.add_argument("--sans-predecodage", action="store_true",
                    help="whole model: decode DELTA at every step instead of once at load")
     a.add_argument("--couches", type=int, default=36)
+    a.add_argument("--gemm", type=int, default=0,
+                   help="measure the tensor-core expert GEMM on a 16-expert share with this many tokens per expert")
     a.add_argument("--codeur", action="store_true",
                    help="measure the GPU .trc encoder instead (a layer's experts: counts, then parts)")
     a.add_argument("--par-rang", type=int, default=1,
@@ -506,7 +508,7 @@ def legs_couche(args, c, cc, xs_dev, res_dev, idx, vidange, pic: float) -> dict:
         torch.cuda.synchronize()
         if s >= args.warmup:
             ph.append(ev[2].elapsed_time(ev[3]))
-    brut_gu = sum(octets_flux(c.parties_brutes[int(e)], (0x05, 0x06), (0, 1)) for s in steps for e in idx[s])
+    brut_gu = sum(octets_flux(c.parties_brutes[int(e)], (0x06, 0x07), (0, 1)) for s in steps for e in idx[s])
     ach = brut_gu / args.steps / (np.mean(ph) * 1e-3) / 1e9
     out["raw_layer"] = {
         "value": round(octets / (sum(t) * 1e-3) / 1e9, 2), "unit": UNITE, "ms_per_step": round(sum(t) / args.steps, 4),
@@ -1124,6 +1126,118 @@ def bras_flux(args):
     print(json.dumps(ligne), flush=True)
 
 
+def bras_gemm(args):
+    """The tensor-core expert GEMM (trc_gemm_mxfp4_lot) on an expert-parallel share: 16 experts
+    of 3 x 2880 x 2880 MXFP4 matrices (raw parts' CODES_BRUTS / ECHELLES_BRUTES, as resident),
+    --gemm tokens per expert (16 at batch 64 over 8 GPUs with uniform top-4), x f32; all 48
+    GEMMs in one batched call (quantization launch + MMA launch), timed with CUDA events, L2
+    flushed between steps. Beside it the same products token by token with the row-group GEMV
+    (trc_gemv_lot over the 48 matrices, one launch per token). Roofline: HBM, the matrices'
+    bytes (0.53 B per weight) per call; FLOP/s reported beside it."""
+    import numpy as np
+    import torch
+
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+    from troncons_b200.carte import CoucheCarte
+
+    torch.cuda.set_device(rang()[2])
+    n, E = args.gemm, 16
+    t0 = time.time()
+    c = S.couche(args.graine, T.DimsExpert.gpt_oss(), E, brut=True)
+    t_gen = time.time() - t0
+    cc = CoucheCarte(c, k=args.k, brut=True)
+    R = Cc = 2880
+    rng = np.random.default_rng(args.graine)
+    x = torch.from_numpy(rng.standard_normal((E * 3, n, Cc)).astype(np.float32)).cuda()
+    y = torch.zeros(E * 3, n, R, dtype=torch.float32, device="cuda")
+    descs, gv = [], []
+    for e in range(E):
+        p = c.parties_brutes[e]
+        base = cc.partie(e, brute=True).data_ptr()
+        nf = int.from_bytes(p[10:12], "little")
+        flux = {}
+        for i in range(nf):
+            d = p[64 + 16 * i:80 + 16 * i]
+            flux[(d[0], d[1])] = int.from_bytes(d[4:8], "little")
+        for j in range(3):
+            m = 3 * e + j
+            cod, ech, bia = base + flux[(0x06, j)], base + flux[(0x07, j)], base + flux[(0x02, j)]
+            descs.append(T.DescGemm(cod, ech, bia, x[m].data_ptr(), y[m].data_ptr(), R, Cc, n, 0))
+    nb = len(descs)
+    dd = torch.frombuffer(bytearray(bytes((T.DescGemm * nb)(*descs))), dtype=torch.uint8).cuda()
+    octets = int(T.lib.trc_gemm_mxfp4_lot_espace_octets(Cc, n, nb))
+    esp = torch.empty(octets + 256, dtype=torch.uint8, device="cuda")
+    e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    vidange = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+
+    def gemm():
+        T.verifier(T.lib.trc_gemm_mxfp4_lot(dd.data_ptr(), nb, R, Cc, n, e0, octets, err.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream))
+
+    t = chrono_etapes(gemm, lambda s: None, args.warmup + args.steps, args.warmup, vidange)
+    assert int(err.item()) == 0, "a bounded wait of the GEMM gave up"
+    # the same products token by token: the slot GEMV batch reads a slot layout; the raw part's
+    # streams are not one, so compare with the raw layer's grouped GEMV through per-token GEMV
+    # descriptors over slots decoded from the parts
+    te = T.taille_emplacement(c.dims)
+    slots = torch.empty(E * te + 256, dtype=torch.uint8, device="cuda")
+    sb = slots.data_ptr() + (-slots.data_ptr()) % 256
+    te256 = (te + 255) // 256 * 256
+    ctl = torch.zeros(4 * E, dtype=torch.int32, device="cuda")
+    for e in range(E):
+        cc.n.copier_brut(cc.partie(e, brute=True), slots[(sb - slots.data_ptr()) + e * te256:][:te], c.dims,
+                         ctl[4 * e:4 * e + 4])
+    pas_m = [0, 0, 0]
+    for j in range(3):
+        nbj = R * (Cc // 32)
+        eo = (nbj * 16 + 255) & ~255
+        bo = (eo + nbj + 255) & ~255
+        pas_m[j] = (bo + 4 * R + 255) & ~255
+    off = [0, pas_m[0], pas_m[0] + pas_m[1]]
+    yg = torch.zeros(n, E * 3, R, dtype=torch.float32, device="cuda")
+    xg = x.transpose(0, 1).contiguous()  # [n][48][C]
+    lots = []
+    for tk in range(n):
+        dg = (T.DescGemv * nb)(*[T.DescGemv(sb + (m // 3) * te256 + off[m % 3], xg[tk, m].data_ptr(), yg[tk, m].data_ptr(),
+                                            R, Cc) for m in range(nb)])
+        lots.append(torch.frombuffer(bytearray(bytes(dg)), dtype=torch.uint8).cuda())
+
+    def gemv():
+        for tk in range(n):
+            cc.n.gemv_lot(lots[tk], nb, R)
+
+    t_v = chrono_etapes(gemv, lambda s: None, args.warmup + args.steps, args.warmup, vidange)
+    torch.cuda.synchronize()
+    # agreement of the two (x quantized to MXFP8 on the tensor-core side)
+    a = y.cpu().numpy()
+    b = yg.transpose(0, 1).cpu().numpy()
+    ecart = float(np.abs(a - b).max() / max(1.0, np.abs(b).max()))
+    octets_w = nb * (R * Cc // 32 * 17)
+    ms, ms_v = sum(t) / args.steps, sum(t_v) / args.steps
+    pic, sorte = pics()
+    flops = 2.0 * nb * R * Cc * n
+    ligne = {
+        "metric": "tensor-core MXFP4 expert GEMM (tcgen05 block-scaled), GB/s of weights",
+        "value": round(octets_w / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "higher_is_better": True, "dtype": "e2m1 x e4m3 -> f32",
+        "config": {"workload": f"config 3 share: {E} experts x 3 matrices 2880 x 2880 MXFP4, {n} tokens per expert "
+                               "(x f32, quantized to MXFP8 in the call)", "tokens_per_expert": n, "matrices": nb,
+                   "l2": "flushed between steps (256 MB written)"},
+        "tflops": round(flops / (ms * 1e-3) / 1e12, 2),
+        "roofline": {"bound": "hbm", "achieved": round(octets_w / (ms * 1e-3) / 1e9, 1), "peak": pic, "unit": "GB/s",
+                     "frac": round(octets_w / (ms * 1e-3) / 1e9 / pic, 4), "peak_source": sorte,
+                     "algorithmic_bytes_per_launch": octets_w},
+        "gemv_token_by_token": {"ms": round(ms_v, 4), "value": round(n * octets_w / (ms_v * 1e-3) / 1e9, 1),
+                                "unit": "GB/s (weight bytes read per token pass)",
+                                "speedup_of_gemm": round(ms_v / ms, 2)},
+        "max_rel_diff_vs_gemv": ecart,
+        "generation_s": round(t_gen, 1),
+    }
+    print(json.dumps(ligne), flush=True)
+
+
 def bras_prefill(args):
     """One gpt-oss-120b MoE layer (128 resident experts, top-4) on a batch of --prefill positions:
     router then the fused layer (each activation decodes its expert's tiles), and router then the
@@ -1314,6 +1428,9 @@ def main():
         return
     if args.codeur:
         bras_codeur(args)
+        return
+    if args.gemm:
+        bras_gemm(args)
         return
     if args.impl == "reference":
         bras_reference(args)
