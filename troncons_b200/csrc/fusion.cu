@@ -664,7 +664,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32, BRUT_BLOCS_SM) k_moe_brut(Args
 // The raw layer's GEMV in row groups (gemv_groupes.cuh): launched when every matrix's shape
 // allows it, one block of 8 warps per SM sharing the activation's staged 2x, the same partials
 // as k_moe_brut's row walk, bit for bit.
-__global__ void __launch_bounds__(256) k_moe_brut_groupes(ArgsMoe a) {
+__global__ void __launch_bounds__(128, 4) k_moe_brut_groupes(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     attendre_amont();
     liberer_aval();
@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(256) k_moe_brut_groupes(ArgsMoe a) {
     const bool bon = B > 0 && partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
                      trouver_flux_warp(partie, taille, SORTE_CODES_BRUTS, j, fc) && fe.produits == nblocs &&
                      fe.longueur >= nblocs && fc.produits == 16u * nblocs && fc.longueur >= 16u * nblocs &&
-                     (reinterpret_cast<uintptr_t>(fe.p) & 15u) == 0 && (reinterpret_cast<uintptr_t>(fc.p) & 15u) == 0;
+                     (reinterpret_cast<uintptr_t>(fc.p) & 15u) == 0;
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
         return;
@@ -690,14 +690,10 @@ __global__ void __launch_bounds__(256) k_moe_brut_groupes(ArgsMoe a) {
     else
         charger_x2_groupes(x2g, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
-    const uint32_t W = max(1u, min(blockDim.x >> 5, warps_groupes(C)));
-    if (warp >= W) return;
+    const uint32_t W = blockDim.x >> 5;
     const uint32_t K = a.plan.K[j];
     float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
-    uint8_t* zone = dyn + x2g_octets(C) + warp * groupe_octets_warp(B);
-    if (!gemv_groupes<true>(fc.p, fe.p, nullptr, x2g, R, B, parts, K, blockIdx.x * W + warp, gridDim.x * W, zone) &&
-        (threadIdx.x & 31u) == 0)
-        atomicAdd(&controle[CTL_ATTENTE], 1u);
+    gemv_groupes<true>(fc.p, fe.p, nullptr, x2g, R, B, parts, K, blockIdx.x * W + warp, gridDim.x * W);
 }
 
 // ------------------------------------------------------------------ 4'. down, from decoded words
@@ -1032,27 +1028,19 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
             marque(4);
         }
     } else if (groupes_possibles(c.lignes[0], c.colonnes[0] / 32u) && groupes_possibles(c.lignes[2], c.colonnes[2] / 32u)) {
-        // Row groups: one block of 8 warps per SM, the SMs shared out over the launch's planes.
-        if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_brut_groupes), int(GRP_SMEM))) != cudaSuccess) return e;
-        int dev = 0, sms = 148;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        // Warps per block: as many double-buffered staging areas as fit beside the staged 2x.
-        const uint32_t W0 = std::max(1u, warps_groupes(c.colonnes[0])), W2 = std::max(1u, warps_groupes(c.colonnes[2]));
-        auto gx = [&](uint32_t R, uint32_t plans, uint32_t W) {
-            const uint32_t groupes = (R + GRP_LIGNES - 1) / GRP_LIGNES;
-            return std::max(1u, std::min((groupes + W - 1u) / W, uint32_t(sms) / plans));
-        };
+        // Row groups: blocks of 4 warps, one row group per warp, the 2x staged per block.
+        const uint32_t smem = x2g_octets(cmax);
+        if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_brut_groupes), int(smem))) != cudaSuccess) return e;
+        auto gx = [&](uint32_t R) { return std::max(1u, ((R + GRP_LIGNES - 1) / GRP_LIGNES + 3u) / 4u); };
         marque(1);
-        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[0], 2u * na, W0), 2, na), dim3(32u * W0), GRP_SMEM,
-                            flux, a)) != cudaSuccess)
+        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[0]), 2, na), dim3(128), smem, flux, a)) != cudaSuccess)
             return e;
         marque(2);
         if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
             return e;
         marque(3);
         a.j0 = 2;
-        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[2], na, W2), 1, na), dim3(32u * W2), GRP_SMEM, flux,
-                            a)) != cudaSuccess)
+        if ((e = lancer_pdl(k_moe_brut_groupes, dim3(gx(c.lignes[2]), 1, na), dim3(128), smem, flux, a)) != cudaSuccess)
             return e;
         marque(4);
     } else {

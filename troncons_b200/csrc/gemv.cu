@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv_lot(const DescGemv* __
 // The batch of slot GEMVs in row groups (gemv_groupes.cuh) where the shapes allow: blockIdx.y
 // is the matrix, its blocks share the matrix's staged 2x, each warp takes row groups
 // blockIdx.x * W + warp, + gridDim.x * W. Other shapes take gemv_lignes (the same bits).
-__global__ void __launch_bounds__(256) k_gemv_lot_groupes(const DescGemv* __restrict__ descs) {
+__global__ void __launch_bounds__(128, 4) k_gemv_lot_groupes(const DescGemv* __restrict__ descs) {
     extern __shared__ __align__(16) uint8_t dyn[];
     attendre_amont();
     liberer_aval();
@@ -68,13 +68,9 @@ __global__ void __launch_bounds__(256) k_gemv_lot_groupes(const DescGemv* __rest
     float4* x2g = reinterpret_cast<float4*>(dyn);
     charger_x2_groupes(x2g, reinterpret_cast<const float*>(d.x), 0u, C);
     __syncthreads();
-    // The warps whose staging areas fit next to the staged 2x take part (one at least: B <= 256).
-    const uint32_t Wg = max(1u, min(W, warps_groupes(C)));
-    if (warp >= Wg) return;
     const Disposition dm = disposition_matrice(R, C);
-    uint8_t* zone = dyn + x2g_octets(C) + warp * groupe_octets_warp(B);
     gemv_groupes<false>(mat, mat + dm.echelles, reinterpret_cast<const float*>(mat + dm.biais), x2g, R, B,
-                        reinterpret_cast<float*>(d.y), 0u, blockIdx.x * Wg + warp, gridDim.x * Wg, zone);
+                        reinterpret_cast<float*>(d.y), 0u, blockIdx.x * W + warp, gridDim.x * W);
 }
 
 __device__ __forceinline__ float4 charger_x4(const void* x, uint32_t x_bf16, uint32_t c) {
@@ -135,14 +131,16 @@ uint32_t sms_courant() {
     return uint32_t(sms);
 }
 
-// The batch in row groups: 8 warps and GRP_SMEM bytes per block (one block per SM), the SMs
-// shared out over the matrices in one wave, no more blocks than a matrix has groups.
+// The batch in row groups: blocks of 4 warps, one row group per warp (the widest 2x staged
+// per block: 2x of up to 8,192 columns), the matrix as grid y.
+constexpr uint32_t GRP_WARPS = 4;
 cudaError_t lancer_gemv_lot(const DescGemv* descs, uint32_t n, uint32_t lignes_max, cudaStream_t flux) {
-    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_lot_groupes), int(GRP_SMEM));
+    const uint32_t smem = x2g_octets(32u * GRP_B_MAX);
+    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemv_lot_groupes), int(smem));
     if (e != cudaSuccess) return e;
     const uint32_t groupes = (lignes_max + GRP_LIGNES - 1) / GRP_LIGNES;
-    const uint32_t bx = std::max(1u, std::min((groupes + 3u) / 4u, sms_courant() / std::max(1u, n)));
-    return lancer_pdl(k_gemv_lot_groupes, dim3(bx, n, 1), dim3(256), GRP_SMEM, flux, descs);
+    const uint32_t bx = std::max(1u, (groupes + GRP_WARPS - 1u) / GRP_WARPS);
+    return lancer_pdl(k_gemv_lot_groupes, dim3(bx, n, 1), dim3(32u * GRP_WARPS), smem, flux, descs);
 }
 
 cudaError_t lancer_gemv_f32(const float* w, const void* x, uint32_t x_bf16, const float* biais, float* y, uint32_t R,
