@@ -39,18 +39,21 @@ namespace tb {
 constexpr uint32_t MMA_M = 128;        // rows per CTA (one MMA's M); chunks of 128 K (four MMAs)
 constexpr uint32_t MMA_FILS = 128;     // four warps: one per tensor-memory lane quadrant
 
+constexpr uint32_t MMA_ETAGES = 3;     // chunks in flight: loads of the next two during an MMA
+
 __host__ __device__ __forceinline__ uint32_t mma_n_pad(uint32_t N) { return (N + 15u) & ~15u; }
+// Tensor-memory columns: the accumulator (Npad), then per stage SFA (4) and SFB (8).
 __host__ __device__ __forceinline__ uint32_t mma_tmem_colonnes(uint32_t N) {
-    const uint32_t besoin = mma_n_pad(N) + 4u + 8u;  // accumulator, then SFA (4) and SFB (8)
+    const uint32_t besoin = mma_n_pad(N) + 12u * MMA_ETAGES;
     uint32_t c = 32u;
     while (c < besoin) c <<= 1;
     return c;
 }
-// Shared bytes: A tile (128 rows x 128 bytes), B tile (Npad rows x 128 bytes), mbarrier, tmem base,
-// and 8 KB of slack past the tiles (never read by a correct descriptor).
-__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N) {
-    return MMA_M * 128u + mma_n_pad(N) * 128u + 32u + 8192u;
-}
+// Shared bytes of one stage: A tile (128 rows x 128 bytes) and B tile (Npad rows x 128 bytes).
+__host__ __device__ __forceinline__ uint32_t mma_etage(uint32_t N) { return MMA_M * 128u + mma_n_pad(N) * 128u; }
+// All stages, the mbarriers and the tensor-memory base, and 8 KB of slack past the tiles (never
+// read by a correct descriptor).
+__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N) { return MMA_ETAGES * mma_etage(N) + 64u + 8192u; }
 
 // Offset in a K-major no-swizzle tile of row r and byte k (0..127) of the chunk.
 __device__ __forceinline__ uint32_t mma_off(uint32_t r, uint32_t k) {
@@ -154,21 +157,21 @@ __global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const De
     extern __shared__ __align__(1024) uint8_t dyn[];
     const ArgsMma a = lot != nullptr ? args_du_lot(lot, espace_lot, tranche, a0.erreur) : a0;
     if (blockIdx.x * MMA_M >= a.R || a.N == 0) return;
-    const uint32_t Np = mma_n_pad(a.N);
-    uint8_t* ta = dyn;
-    uint8_t* tbt = dyn + MMA_M * 128u;
-    uint64_t* mb = reinterpret_cast<uint64_t*>(tbt + Np * 128u);
-    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mb + 1);
+    const uint32_t Np = mma_n_pad(a.N), etage = mma_etage(a.N);
+    uint64_t* mb = reinterpret_cast<uint64_t*>(dyn + MMA_ETAGES * etage);  // one per stage
+    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mb + MMA_ETAGES);
     const uint32_t warp = threadIdx.x >> 5, voie = threadIdx.x & 31u;
     const uint32_t r0 = blockIdx.x * MMA_M, B = a.C / 32u;
     const uint32_t ncol = mma_tmem_colonnes(a.N);
-    const uint32_t col_acc = 0, col_sfa = Np, col_sfb = col_sfa + 4u;
+    const uint32_t col_acc = 0;
+    auto col_sfa = [Np](uint32_t e) { return Np + 12u * e; };
+    auto col_sfb = [Np](uint32_t e) { return Np + 12u * e + 4u; };
 
     // Padding bytes (and rows past R or N) stay zero; only the data halves are ever written.
-    for (uint32_t i = threadIdx.x; i < (MMA_M + Np) * 128u / 16u; i += MMA_FILS)
+    for (uint32_t i = threadIdx.x; i < MMA_ETAGES * etage / 16u; i += MMA_FILS)
         reinterpret_cast<uint4*>(dyn)[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
-        mbar_init(mb, 1u);
+        for (uint32_t e = 0; e < MMA_ETAGES; ++e) mbar_init(mb + e, 1u);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 0) {
@@ -186,41 +189,54 @@ __global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const De
     liberer_aval();
 
     const uint32_t nchunks = (B + 3u) / 4u;
-    uint32_t parite = 0;
-    bool ok = true;
     const uint32_t quadrant = (warp & 3u) * 32u;
-    for (uint32_t ch = 0; ch < nchunks && ok; ++ch) {
-        const uint32_t kb0 = 4u * ch, nkb = min(4u, B - kb0);
-        charger_a(ta, a.codes, a.R, B, r0, kb0, nkb);
-        charger_b(tbt, a.xq, a.C, a.N, kb0, nkb);
-        // Scale factors: lane quadrant q, lane l, column c: rows (tokens) l + 32 c, bytes = blocks.
-        {
+    // Chunk ch into stage ch % MMA_ETAGES: the tiles by cp.async (one commit group), the scale
+    // factors into the stage's tensor-memory columns.
+    auto charger = [&](uint32_t ch) {
+        if (ch < nchunks) {
+            const uint32_t e = ch % MMA_ETAGES, kb0 = 4u * ch, nkb = min(4u, B - kb0);
+            uint8_t* ta = dyn + e * etage;
+            charger_a(ta, a.codes, a.R, B, r0, kb0, nkb);
+            charger_b(ta + MMA_M * 128u, a.xq, a.C, a.N, kb0, nkb);
             uint32_t v[4];
 #pragma unroll
             for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.ech, r0 + voie + 32u * c, a.R, B, kb0, nkb);
-            tmem_st4(tmem + (quadrant << 16) + col_sfa, v[0], v[1], v[2], v[3]);
+            tmem_st4(tmem + (quadrant << 16) + col_sfa(e), v[0], v[1], v[2], v[3]);
 #pragma unroll
             for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.xs, voie + 32u * c, a.N, B, kb0, nkb);
-            tmem_st4(tmem + (quadrant << 16) + col_sfb, v[0], v[1], v[2], v[3]);
+            tmem_st4(tmem + (quadrant << 16) + col_sfb(e), v[0], v[1], v[2], v[3]);
             if (Np > 128u) {  // tokens 128 .. 255: four more columns
 #pragma unroll
                 for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.xs, 128u + voie + 32u * c, a.N, B, kb0, nkb);
-                tmem_st4(tmem + (quadrant << 16) + col_sfb + 4u, v[0], v[1], v[2], v[3]);
+                tmem_st4(tmem + (quadrant << 16) + col_sfb(e) + 4u, v[0], v[1], v[2], v[3]);
             }
         }
-        cp_async_commit();
-        cp_async_wait<0>();
+        cp_async_commit();  // an empty group past the last chunk keeps the group count uniform
+    };
+    // Parity of the k-th completion (k = ch / MMA_ETAGES) of stage ch % MMA_ETAGES's mbarrier.
+    auto parite = [](uint32_t ch) { return (ch / MMA_ETAGES) & 1u; };
+    bool ok = true;
+    for (uint32_t ch = 0; ch + 1u < MMA_ETAGES; ++ch) charger(ch);
+    for (uint32_t ch = 0; ch < nchunks && ok; ++ch) {
+        // Stage of chunk ch + MMA_ETAGES - 1 = the stage chunk ch - 1 used: its MMAs first.
+        if (ch >= 1u) ok = mbar_attendre(mb + (ch - 1u) % MMA_ETAGES, parite(ch - 1u));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        charger(ch + MMA_ETAGES - 1u);
+        cp_async_wait<MMA_ETAGES - 1u>();  // this thread's copies of chunk ch have landed
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
         __syncthreads();
         if (threadIdx.x == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+            const uint32_t e = ch % MMA_ETAGES, nkb = min(4u, B - 4u * ch);
+            const uint32_t ta = adresse_partagee(dyn + e * etage), tbs = ta + MMA_M * 128u;
             for (uint32_t kb = 0; kb < nkb; ++kb) {
-                const uint64_t da = mma_desc(adresse_partagee(ta) + 256u * kb);
-                const uint64_t db = mma_desc(adresse_partagee(tbt) + 256u * kb);
+                const uint64_t da = mma_desc(ta + 256u * kb);
+                const uint64_t db = mma_desc(tbs + 256u * kb);
                 const uint32_t idesc = mma_idesc(Np, kb);
-                const uint32_t sfa = tmem + col_sfa + (kb << 30), sfb = tmem + col_sfb + (kb << 30);
+                const uint32_t sfa = tmem + col_sfa(e) + (kb << 30), sfb = tmem + col_sfb(e) + (kb << 30);
                 const uint32_t acc = (ch > 0 || kb > 0) ? 1u : 0u;
                 asm volatile(
                     "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -230,17 +246,18 @@ __global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const De
                     : "memory");
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
-                             adresse_partagee(mb))
+                             adresse_partagee(mb + e))
                          : "memory");
         }
-        // Every thread waits for the chunk's MMAs before its tiles and scale factors are reused.
-        ok = mbar_attendre(mb, parite);
-        parite ^= 1u;
-        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     }
+    // The last chunk's MMAs (the accumulator's last writes: MMAs complete in order).
+    if (ok) ok = mbar_attendre(mb + (nchunks - 1u) % MMA_ETAGES, parite(nchunks - 1u));
+    cp_async_wait<0>();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.erreur, 1u);
-        mbar_attendre(mb, parite ^ 1u);  // a second bounded wait for the MMAs in flight
+        // A second bounded wait for the MMAs in flight (the last committed chunk's stage).
+        for (uint32_t e = 0; e < MMA_ETAGES; ++e) mbar_attendre(mb + e, 0u), mbar_attendre(mb + e, 1u);
     } else {
         // Epilogue: warp q reads rows r0 + 32 q + lane, 8 tokens at a time.
         const uint32_t r = r0 + quadrant + voie;
