@@ -595,7 +595,7 @@ int trc_moe_predecoder_deltas(const trc_moe_couche* couche, uint8_t* deltas, uin
  * trc-modele/src/lib.rs:607-717): for an expert receiving many tokens at once,
  * y[t][r] = sum_c W[r][c] x[t][c] + biais[r] on the tensor cores (tcgen05.mma,
  * kind::mxf8f6f4.block_scale): W the matrix in the slot / raw-part layout (codes: 16 bytes per
- * 32-block, row-major, 16-aligned; echelles: one E8M0 byte per block; biais f32[lignes] or NULL),
+ * 32-block, row-major, 16-aligned; echelles: one E8M0 byte per block, 16-aligned; biais f32[lignes] or NULL),
  * x [n][colonnes] f32 or bf16, quantized on the GPU to MXFP8 (E4M3 elements, one E8M0 scale per 32:
  * 2^(floor(log2 max|x|) - 8)); f32 accumulation. n = 1 to 256 tokens (the MMA's N, padded to 16);
  * espace: trc_gemm_mxfp4_espace_octets bytes, 256-aligned (the quantized x). Not bit-identical

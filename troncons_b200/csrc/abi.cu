@@ -393,8 +393,10 @@ int trc_gemm_mxfp4(const uint8_t* codes, const uint8_t* echelles, const float* b
     if (n == 0 || n > 256) return usage("%u tokens (1 to 256)", n);
     if (codes == nullptr || echelles == nullptr || x == nullptr || y == nullptr || espace == nullptr || erreur == nullptr)
         return usage("gemm: a device buffer is missing");
-    if (!aligne(codes, 16) || !aligne(espace, 256) || !aligne(x, x_bf16 ? 2 : 4) || !aligne(y, 4))
-        return usage("gemm: codes 16-aligned, workspace 256-aligned");
+    if (!aligne(codes, 16) || !aligne(echelles, 16) || !aligne(espace, 256) || !aligne(x, x_bf16 ? 2 : 4) ||
+        !aligne(y, 4))
+        return usage("gemm: codes and scales 16-aligned, workspace 256-aligned");
+    if (!tb::gemm_mxfp4_possible(colonnes, n)) return usage("gemm: %u columns x %u tokens exceed shared memory", colonnes, n);
     if (espace_octets < tb::gemm_mxfp4_espace(colonnes, n))
         return usage("gemm workspace of %zu bytes, %llu needed", espace_octets,
                      (unsigned long long)tb::gemm_mxfp4_espace(colonnes, n));
@@ -414,6 +416,8 @@ int trc_gemm_mxfp4_lot(const trc_desc_gemm* descs, uint32_t nb, uint32_t lignes_
     if (descs == nullptr || nb == 0 || nb > 65535) return usage("%u GEMM descriptors", nb);
     if (lignes_max == 0 || colonnes_max == 0 || colonnes_max % 32) return usage("%u x %u at most", lignes_max, colonnes_max);
     if (n_max == 0 || n_max > 256) return usage("%u tokens at most (1 to 256)", n_max);
+    if (!tb::gemm_mxfp4_possible(colonnes_max, n_max))
+        return usage("gemm batch: %u columns x %u tokens exceed shared memory", colonnes_max, n_max);
     if (espace == nullptr || erreur == nullptr || !aligne(espace, 256)) return usage("gemm batch: workspace 256-aligned");
     if (espace_octets < tb::gemm_mxfp4_lot_espace(colonnes_max, n_max, nb))
         return usage("gemm batch workspace of %zu bytes, %llu needed", espace_octets,

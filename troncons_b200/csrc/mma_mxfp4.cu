@@ -51,9 +51,15 @@ __host__ __device__ __forceinline__ uint32_t mma_tmem_colonnes(uint32_t N) {
 }
 // Shared bytes of one stage: A tile (128 rows x 128 bytes) and B tile (Npad rows x 128 bytes).
 __host__ __device__ __forceinline__ uint32_t mma_etage(uint32_t N) { return MMA_M * 128u + mma_n_pad(N) * 128u; }
-// All stages, the mbarriers and the tensor-memory base, and 8 KB of slack past the tiles (never
-// read by a correct descriptor).
-__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N) { return MMA_ETAGES * mma_etage(N) + 64u + 8192u; }
+// Scale bytes of the CTA's 128 rows and of the tokens (staged once), 16-aligned.
+__host__ __device__ __forceinline__ uint32_t mma_echelles(uint32_t N, uint32_t C) {
+    return ((MMA_M + mma_n_pad(N)) * (C / 32u) + 15u) & ~15u;
+}
+// All stages, the staged scales, the mbarriers and the tensor-memory base, and 8 KB of slack
+// past the tiles (never read by a correct descriptor).
+__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N, uint32_t C) {
+    return MMA_ETAGES * mma_etage(N) + mma_echelles(N, C) + 64u + 8192u;
+}
 
 // Offset in a K-major no-swizzle tile of row r and byte k (0..127) of the chunk.
 __device__ __forceinline__ uint32_t mma_off(uint32_t r, uint32_t k) {
@@ -120,13 +126,19 @@ __device__ __forceinline__ void charger_b(uint8_t* tb_, const uint8_t* xq, uint3
     }
 }
 
-// Scale bytes of row (or token) m for blocks kb0 .. kb0 + 3 (0 beyond nkb or past the rows).
-__device__ __forceinline__ uint32_t quatre_echelles(const uint8_t* ech, uint32_t m, uint32_t lignes, uint32_t B,
+// Scale bytes of row (or token) m of the staged scales for blocks kb0 .. kb0 + 3 (0 beyond nkb or
+// past `lignes`).
+__device__ __forceinline__ uint32_t quatre_echelles(const uint8_t* ech_s, uint32_t m, uint32_t lignes, uint32_t B,
                                                     uint32_t kb0, uint32_t nkb) {
     if (m >= lignes) return 0u;
     uint32_t v = 0;
-    for (uint32_t k = 0; k < nkb; ++k) v |= uint32_t(__ldg(ech + uint64_t(m) * B + kb0 + k)) << (8u * k);
+    for (uint32_t k = 0; k < nkb; ++k) v |= uint32_t(ech_s[m * B + kb0 + k]) << (8u * k);
     return v;
+}
+
+// n bytes (n a multiple of 16, both addresses 16-aligned) into shared memory by 16-byte cp.async.
+__device__ __forceinline__ void copier_async(uint8_t* dst, const uint8_t* src, uint32_t n) {
+    for (uint32_t t = threadIdx.x; t < n / 16u; t += blockDim.x) cp_async16(dst + 16u * t, src + 16u * t, 16u);
 }
 
 struct ArgsMma {
@@ -152,13 +164,15 @@ __device__ __forceinline__ ArgsMma args_du_lot(const DescGemm* __restrict__ lot,
 
 // One launch: `a` (lot == nullptr), or matrix blockIdx.y of a batch (its rows past its own R
 // leave the CTA idle).
-__global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const DescGemm* lot, uint8_t* espace_lot,
+__global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(ArgsMma a0, const DescGemm* lot, uint8_t* espace_lot,
                                                             uint64_t tranche) {
     extern __shared__ __align__(1024) uint8_t dyn[];
     const ArgsMma a = lot != nullptr ? args_du_lot(lot, espace_lot, tranche, a0.erreur) : a0;
     if (blockIdx.x * MMA_M >= a.R || a.N == 0) return;
     const uint32_t Np = mma_n_pad(a.N), etage = mma_etage(a.N);
-    uint64_t* mb = reinterpret_cast<uint64_t*>(dyn + MMA_ETAGES * etage);  // one per stage
+    uint8_t* ech_a = dyn + MMA_ETAGES * etage;              // the CTA's rows' scales [128][B]
+    uint8_t* ech_b = ech_a + MMA_M * (a.C / 32u);           // the tokens' scales [N][B]
+    uint64_t* mb = reinterpret_cast<uint64_t*>(dyn + MMA_ETAGES * etage + mma_echelles(a.N, a.C));  // per stage
     uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mb + MMA_ETAGES);
     const uint32_t warp = threadIdx.x >> 5, voie = threadIdx.x & 31u;
     const uint32_t r0 = blockIdx.x * MMA_M, B = a.C / 32u;
@@ -190,6 +204,19 @@ __global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const De
 
     const uint32_t nchunks = (B + 3u) / 4u;
     const uint32_t quadrant = (warp & 3u) * 32u;
+    // The scales, once: the CTA's rows (contiguous, 16-aligned: r0 B is a multiple of 16) and
+    // the tokens'; past R, a partial last tile reads rows of zeros (they are never multiplied).
+    {
+        const uint32_t lignes = min(MMA_M, a.R - r0);
+        copier_async(ech_a, a.ech + uint64_t(r0) * B, (lignes * B) & ~15u);
+        for (uint32_t i = ((lignes * B) & ~15u) + threadIdx.x; i < lignes * B; i += MMA_FILS)
+            ech_a[i] = a.ech[uint64_t(r0) * B + i];
+        copier_async(ech_b, a.xs, (a.N * B) & ~15u);
+        for (uint32_t i = ((a.N * B) & ~15u) + threadIdx.x; i < a.N * B; i += MMA_FILS) ech_b[i] = a.xs[i];
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+    }
     // Chunk ch into stage ch % MMA_ETAGES: the tiles by cp.async (one commit group), the scale
     // factors into the stage's tensor-memory columns.
     auto charger = [&](uint32_t ch) {
@@ -200,14 +227,14 @@ __global__ void __launch_bounds__(MMA_FILS, 1) k_gemm_mxfp4(ArgsMma a0, const De
             charger_b(ta + MMA_M * 128u, a.xq, a.C, a.N, kb0, nkb);
             uint32_t v[4];
 #pragma unroll
-            for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.ech, r0 + voie + 32u * c, a.R, B, kb0, nkb);
+            for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(ech_a, voie + 32u * c, a.R - r0, B, kb0, nkb);
             tmem_st4(tmem + (quadrant << 16) + col_sfa(e), v[0], v[1], v[2], v[3]);
 #pragma unroll
-            for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.xs, voie + 32u * c, a.N, B, kb0, nkb);
+            for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(ech_b, voie + 32u * c, a.N, B, kb0, nkb);
             tmem_st4(tmem + (quadrant << 16) + col_sfb(e), v[0], v[1], v[2], v[3]);
             if (Np > 128u) {  // tokens 128 .. 255: four more columns
 #pragma unroll
-                for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(a.xs, 128u + voie + 32u * c, a.N, B, kb0, nkb);
+                for (uint32_t c = 0; c < 4; ++c) v[c] = quatre_echelles(ech_b, 128u + voie + 32u * c, a.N, B, kb0, nkb);
                 tmem_st4(tmem + (quadrant << 16) + col_sfb(e) + 4u, v[0], v[1], v[2], v[3]);
             }
         }
@@ -318,6 +345,8 @@ __global__ void __launch_bounds__(256) k_quantifier_mxfp8(const void* x, uint32_
     if (voie == 0) xs[uint64_t(n) * B + b] = uint8_t(E + 127);
 }
 
+bool gemm_mxfp4_possible(uint32_t C, uint32_t N) { return mma_smem(N, C) <= 220u * 1024u; }
+
 uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N) { return uint64_t(mma_n_pad(N)) * C + uint64_t(mma_n_pad(N)) * (C / 32u); }
 
 cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const float* biais, const void* x, uint32_t x_bf16,
@@ -329,7 +358,7 @@ cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const fl
     cudaError_t e = lancer_pdl(k_quantifier_mxfp8, dim3((N * B + 7u) / 8u), dim3(256), 0, flux, x, x_bf16, C, N, xq, xs,
                                static_cast<const DescGemm*>(nullptr), uint64_t(0));
     if (e != cudaSuccess) return e;
-    const uint32_t smem = mma_smem(N);
+    const uint32_t smem = mma_smem(N, C);
     if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
     ArgsMma a{codes, ech, biais, xq, xs, y, R, C, N, erreur};
     return lancer_pdl(k_gemm_mxfp4, dim3((R + MMA_M - 1) / MMA_M), dim3(MMA_FILS), smem, flux, a,
@@ -347,7 +376,7 @@ cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t l
                                static_cast<const void*>(nullptr), 0u, colonnes_max, n_max, espace,
                                static_cast<uint8_t*>(nullptr), descs, tranche);
     if (e != cudaSuccess) return e;
-    const uint32_t smem = mma_smem(n_max);
+    const uint32_t smem = mma_smem(n_max, colonnes_max);
     if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
     ArgsMma a{};
     a.erreur = erreur;

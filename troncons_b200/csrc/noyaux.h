@@ -118,6 +118,7 @@ struct DescGemm {
     uint32_t lignes, colonnes, n, x_bf16;
 };
 uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N);
+bool gemm_mxfp4_possible(uint32_t C, uint32_t N);  // the staged tiles and scales fit shared memory
 uint64_t gemm_mxfp4_lot_espace(uint32_t colonnes_max, uint32_t n_max, uint32_t nb);
 cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
                                   uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux);
