@@ -23,10 +23,10 @@
 // copies replicated to the four lane quadrants: lane (m mod 32), column m / 32 + base, byte =
 // the 32-block within the chunk (the instruction descriptor's and the address's scale-factor id).
 //
-// One CTA of 4 warps per 128-row tile: the warps stage the chunk (cp.async of the weight halves
-// and the quantized activations) and write its scale factors to tensor memory, thread 0 issues the
-// MMAs and commits them to an mbarrier that every thread waits on (bounded) before the next
-// chunk; the epilogue reads the accumulator (tcgen05.ld), adds the bias and stores Y. Every wait
+// One CTA of 4 warps per 128-row tile: the warps stage chunks (cp.async of the weight halves and
+// the quantized activations, three or four stages, two chunks ahead) and write their scale factors
+// to tensor memory, thread 0 issues each chunk's MMAs and commits them to the stage's mbarrier,
+// which every thread waits on (bounded) before that stage is refilled; the epilogue reads the accumulator (tcgen05.ld), adds the bias and stores Y. Every wait
 // is bounded: a wait that gives up sets the caller's error word, waits again (bounded) for the
 // MMAs in flight, frees the tensor memory and returns.
 #include <cstdint>
@@ -39,12 +39,14 @@ namespace tb {
 constexpr uint32_t MMA_M = 128;        // rows per CTA (one MMA's M); chunks of 128 K (four MMAs)
 constexpr uint32_t MMA_FILS = 128;     // four warps: one per tensor-memory lane quadrant
 
-constexpr uint32_t MMA_ETAGES = 3;     // chunks in flight: loads of the next two during an MMA
+// Stages of 128 K: E = 4 where shared memory holds them, else 3. The chunk loaded at step ch is
+// ch + E - 2, into the stage chunk ch - 2 used: its MMAs, issued two steps before, are done.
+constexpr uint32_t MMA_ETAGES_MAX = 4;
 
 __host__ __device__ __forceinline__ uint32_t mma_n_pad(uint32_t N) { return (N + 15u) & ~15u; }
 // Tensor-memory columns: the accumulator (Npad), then per stage SFA (4) and SFB (8).
-__host__ __device__ __forceinline__ uint32_t mma_tmem_colonnes(uint32_t N) {
-    const uint32_t besoin = mma_n_pad(N) + 12u * MMA_ETAGES;
+__host__ __device__ __forceinline__ uint32_t mma_tmem_colonnes(uint32_t N, uint32_t E) {
+    const uint32_t besoin = mma_n_pad(N) + 12u * E;
     uint32_t c = 32u;
     while (c < besoin) c <<= 1;
     return c;
@@ -57,8 +59,11 @@ __host__ __device__ __forceinline__ uint32_t mma_echelles(uint32_t N, uint32_t C
 }
 // All stages, the staged scales, the mbarriers and the tensor-memory base, and 8 KB of slack
 // past the tiles (never read by a correct descriptor).
-__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N, uint32_t C) {
-    return MMA_ETAGES * mma_etage(N) + mma_echelles(N, C) + 64u + 8192u;
+__host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N, uint32_t C, uint32_t E) {
+    return E * mma_etage(N) + mma_echelles(N, C) + 64u + 8192u;
+}
+__host__ __device__ __forceinline__ uint32_t mma_etages(uint32_t N, uint32_t C) {
+    return mma_smem(N, C, 4u) <= 220u * 1024u ? 4u : 3u;
 }
 
 // Offset in a K-major no-swizzle tile of row r and byte k (0..127) of the chunk.
@@ -165,27 +170,27 @@ __device__ __forceinline__ ArgsMma args_du_lot(const DescGemm* __restrict__ lot,
 // One launch: `a` (lot == nullptr), or matrix blockIdx.y of a batch (its rows past its own R
 // leave the CTA idle).
 __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(ArgsMma a0, const DescGemm* lot, uint8_t* espace_lot,
-                                                            uint64_t tranche) {
+                                                            uint64_t tranche, uint32_t E) {
     extern __shared__ __align__(1024) uint8_t dyn[];
     const ArgsMma a = lot != nullptr ? args_du_lot(lot, espace_lot, tranche, a0.erreur) : a0;
     if (blockIdx.x * MMA_M >= a.R || a.N == 0) return;
     const uint32_t Np = mma_n_pad(a.N), etage = mma_etage(a.N);
-    uint8_t* ech_a = dyn + MMA_ETAGES * etage;              // the CTA's rows' scales [128][B]
+    uint8_t* ech_a = dyn + E * etage;              // the CTA's rows' scales [128][B]
     uint8_t* ech_b = ech_a + MMA_M * (a.C / 32u);           // the tokens' scales [N][B]
-    uint64_t* mb = reinterpret_cast<uint64_t*>(dyn + MMA_ETAGES * etage + mma_echelles(a.N, a.C));  // per stage
-    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mb + MMA_ETAGES);
+    uint64_t* mb = reinterpret_cast<uint64_t*>(dyn + E * etage + mma_echelles(a.N, a.C));  // per stage
+    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mb + E);
     const uint32_t warp = threadIdx.x >> 5, voie = threadIdx.x & 31u;
     const uint32_t r0 = blockIdx.x * MMA_M, B = a.C / 32u;
-    const uint32_t ncol = mma_tmem_colonnes(a.N);
+    const uint32_t ncol = mma_tmem_colonnes(a.N, E);
     const uint32_t col_acc = 0;
     auto col_sfa = [Np](uint32_t e) { return Np + 12u * e; };
     auto col_sfb = [Np](uint32_t e) { return Np + 12u * e + 4u; };
 
     // Padding bytes (and rows past R or N) stay zero; only the data halves are ever written.
-    for (uint32_t i = threadIdx.x; i < MMA_ETAGES * etage / 16u; i += MMA_FILS)
+    for (uint32_t i = threadIdx.x; i < E * etage / 16u; i += MMA_FILS)
         reinterpret_cast<uint4*>(dyn)[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
-        for (uint32_t e = 0; e < MMA_ETAGES; ++e) mbar_init(mb + e, 1u);
+        for (uint32_t e = 0; e < E; ++e) mbar_init(mb + e, 1u);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 0) {
@@ -217,11 +222,11 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(ArgsMma a0, const De
         cp_async_wait<0>();
         __syncthreads();
     }
-    // Chunk ch into stage ch % MMA_ETAGES: the tiles by cp.async (one commit group), the scale
+    // Chunk ch into stage ch % E: the tiles by cp.async (one commit group), the scale
     // factors into the stage's tensor-memory columns.
     auto charger = [&](uint32_t ch) {
         if (ch < nchunks) {
-            const uint32_t e = ch % MMA_ETAGES, kb0 = 4u * ch, nkb = min(4u, B - kb0);
+            const uint32_t e = ch % E, kb0 = 4u * ch, nkb = min(4u, B - kb0);
             uint8_t* ta = dyn + e * etage;
             charger_a(ta, a.codes, a.R, B, r0, kb0, nkb);
             charger_b(ta + MMA_M * 128u, a.xq, a.C, a.N, kb0, nkb);
@@ -240,24 +245,28 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(ArgsMma a0, const De
         }
         cp_async_commit();  // an empty group past the last chunk keeps the group count uniform
     };
-    // Parity of the k-th completion (k = ch / MMA_ETAGES) of stage ch % MMA_ETAGES's mbarrier.
-    auto parite = [](uint32_t ch) { return (ch / MMA_ETAGES) & 1u; };
+    // Parity of the k-th completion (k = ch / E) of stage ch % E's mbarrier.
+    auto parite = [E](uint32_t ch) { return (ch / E) & 1u; };
+    const uint32_t D = E - 2u;  // chunks loaded ahead
     bool ok = true;
-    for (uint32_t ch = 0; ch + 1u < MMA_ETAGES; ++ch) charger(ch);
+    for (uint32_t ch = 0; ch < D; ++ch) charger(ch);
     for (uint32_t ch = 0; ch < nchunks && ok; ++ch) {
-        // Stage of chunk ch + MMA_ETAGES - 1 = the stage chunk ch - 1 used: its MMAs first.
-        if (ch >= 1u) ok = mbar_attendre(mb + (ch - 1u) % MMA_ETAGES, parite(ch - 1u));
+        // Chunk ch + D goes into the stage chunk ch - 2 used: its MMAs first.
+        if (ch >= 2u) ok = mbar_attendre(mb + (ch - 2u) % E, parite(ch - 2u));
         if (!ok) break;
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        charger(ch + MMA_ETAGES - 1u);
-        cp_async_wait<MMA_ETAGES - 1u>();  // this thread's copies of chunk ch have landed
+        charger(ch + D);
+        if (D == 2u)  // this thread's copies of chunk ch have landed (groups ch + 1 .. ch + D may not)
+            cp_async_wait<2>();
+        else
+            cp_async_wait<1>();
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
         __syncthreads();
         if (threadIdx.x == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-            const uint32_t e = ch % MMA_ETAGES, nkb = min(4u, B - 4u * ch);
+            const uint32_t e = ch % E, nkb = min(4u, B - 4u * ch);
             const uint32_t ta = adresse_partagee(dyn + e * etage), tbs = ta + MMA_M * 128u;
             for (uint32_t kb = 0; kb < nkb; ++kb) {
                 const uint64_t da = mma_desc(ta + 256u * kb);
@@ -278,13 +287,13 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(ArgsMma a0, const De
         }
     }
     // The last chunk's MMAs (the accumulator's last writes: MMAs complete in order).
-    if (ok) ok = mbar_attendre(mb + (nchunks - 1u) % MMA_ETAGES, parite(nchunks - 1u));
+    if (ok) ok = mbar_attendre(mb + (nchunks - 1u) % E, parite(nchunks - 1u));
     cp_async_wait<0>();
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     if (!ok) {
         if (threadIdx.x == 0) atomicExch(a.erreur, 1u);
         // A second bounded wait for the MMAs in flight (the last committed chunk's stage).
-        for (uint32_t e = 0; e < MMA_ETAGES; ++e) mbar_attendre(mb + e, 0u), mbar_attendre(mb + e, 1u);
+        for (uint32_t e = 0; e < E; ++e) mbar_attendre(mb + e, 0u), mbar_attendre(mb + e, 1u);
     } else {
         // Epilogue: warp q reads rows r0 + 32 q + lane, 8 tokens at a time.
         const uint32_t r = r0 + quadrant + voie;
@@ -345,7 +354,7 @@ __global__ void __launch_bounds__(256) k_quantifier_mxfp8(const void* x, uint32_
     if (voie == 0) xs[uint64_t(n) * B + b] = uint8_t(E + 127);
 }
 
-bool gemm_mxfp4_possible(uint32_t C, uint32_t N) { return mma_smem(N, C) <= 220u * 1024u; }
+bool gemm_mxfp4_possible(uint32_t C, uint32_t N) { return mma_smem(N, C, 3u) <= 220u * 1024u; }
 
 uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N) { return uint64_t(mma_n_pad(N)) * C + uint64_t(mma_n_pad(N)) * (C / 32u); }
 
@@ -358,11 +367,11 @@ cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const fl
     cudaError_t e = lancer_pdl(k_quantifier_mxfp8, dim3((N * B + 7u) / 8u), dim3(256), 0, flux, x, x_bf16, C, N, xq, xs,
                                static_cast<const DescGemm*>(nullptr), uint64_t(0));
     if (e != cudaSuccess) return e;
-    const uint32_t smem = mma_smem(N, C);
+    const uint32_t E = mma_etages(N, C), smem = mma_smem(N, C, E);
     if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
     ArgsMma a{codes, ech, biais, xq, xs, y, R, C, N, erreur};
     return lancer_pdl(k_gemm_mxfp4, dim3((R + MMA_M - 1) / MMA_M), dim3(MMA_FILS), smem, flux, a,
-                      static_cast<const DescGemm*>(nullptr), static_cast<uint8_t*>(nullptr), uint64_t(0));
+                      static_cast<const DescGemm*>(nullptr), static_cast<uint8_t*>(nullptr), uint64_t(0), E);
 }
 
 // A batch of nb matrices (descriptors on the device; rows, columns and tokens at most
@@ -376,12 +385,12 @@ cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t l
                                static_cast<const void*>(nullptr), 0u, colonnes_max, n_max, espace,
                                static_cast<uint8_t*>(nullptr), descs, tranche);
     if (e != cudaSuccess) return e;
-    const uint32_t smem = mma_smem(n_max, colonnes_max);
+    const uint32_t E = mma_etages(n_max, colonnes_max), smem = mma_smem(n_max, colonnes_max, E);
     if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem))) != cudaSuccess) return e;
     ArgsMma a{};
     a.erreur = erreur;
     return lancer_pdl(k_gemm_mxfp4, dim3((lignes_max + MMA_M - 1) / MMA_M, nb), dim3(MMA_FILS), smem, flux, a, descs,
-                      espace, tranche);
+                      espace, tranche, E);
 }
 
 uint64_t gemm_mxfp4_lot_espace(uint32_t colonnes_max, uint32_t n_max, uint32_t nb) {
