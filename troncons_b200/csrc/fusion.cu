@@ -664,7 +664,7 @@ __global__ void __launch_bounds__(MOE_WARPS * 32, BRUT_BLOCS_SM) k_moe_brut(Args
 // The raw layer's GEMV in row groups (gemv_groupes.cuh): launched when every matrix's shape
 // allows it, one block of 8 warps per SM sharing the activation's staged 2x, the same partials
 // as k_moe_brut's row walk, bit for bit.
-__global__ void __launch_bounds__(128, 4) k_moe_brut_groupes(ArgsMoe a) {
+__global__ void __launch_bounds__(128, 3) k_moe_brut_groupes(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     attendre_amont();
     liberer_aval();

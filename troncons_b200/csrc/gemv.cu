@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv_lot(const DescGemv* __
 // The batch of slot GEMVs in row groups (gemv_groupes.cuh) where the shapes allow: blockIdx.y
 // is the matrix, its blocks share the matrix's staged 2x, each warp takes row groups
 // blockIdx.x * W + warp, + gridDim.x * W. Other shapes take gemv_lignes (the same bits).
-__global__ void __launch_bounds__(128, 4) k_gemv_lot_groupes(const DescGemv* __restrict__ descs) {
+__global__ void __launch_bounds__(128, 3) k_gemv_lot_groupes(const DescGemv* __restrict__ descs) {
     extern __shared__ __align__(16) uint8_t dyn[];
     attendre_amont();
     liberer_aval();

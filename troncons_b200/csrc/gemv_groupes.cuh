@@ -11,8 +11,8 @@
 // block in registers for the four rows.
 //
 // Memory: the code words go straight from HBM to registers, 16 bytes per lane and row-block
-// (the 8 lanes of a row read 8 neighbouring blocks: 128 contiguous bytes), one column step ahead
-// of their use; shared memory holds only the block's staged 2x, so many warps fit on an SM and
+// (the 8 lanes of a row read 8 neighbouring blocks: 128 contiguous bytes), two column steps
+// ahead of their use; shared memory holds only the block's staged 2x, so many warps fit on an SM and
 // keep their loads in flight together.
 //
 // Arithmetic per block (the order of mxfp4.cuh): quad q of the block (bytes 4q..4q+3) gives
@@ -154,36 +154,42 @@ __device__ inline void gemv_groupes(const uint8_t* __restrict__ codes, const uin
             ligne_c[i] = reinterpret_cast<const uint4*>(codes) + uint64_t(b0);
             ligne_e[i] = echelles + uint64_t(b0);
         }
-        // The four rows' blocks of column block b, loaded one column step ahead of their use.
-        uint4 w[4];
-        uint32_t e[4];
-        auto charger = [&](uint32_t b) {
+        // The four rows' blocks of column block b, loaded two column steps ahead of their use:
+        // three buffers in turn (the loop is unrolled by three so that they stay in registers).
+        struct Pas {
+            uint4 w[4];
+            uint32_t e[4];
+        };
+        auto charger = [&](Pas& p, uint32_t b) {
 #pragma unroll
             for (uint32_t i = 0; i < 4; ++i) {
-                w[i] = b < B ? __ldg(ligne_c[i] + b) : make_uint4(0, 0, 0, 0);
-                e[i] = b < B ? uint32_t(__ldg(ligne_e[i] + b)) : 0u;
+                p.w[i] = b < B ? __ldg(ligne_c[i] + b) : make_uint4(0, 0, 0, 0);
+                p.e[i] = b < B ? uint32_t(__ldg(ligne_e[i] + b)) : 0u;
             }
         };
-        charger(c0);
-        for (uint32_t b = c0; b < B; b += 8u) {
-            uint4 wc[4];
-            uint32_t ec[4];
-#pragma unroll
-            for (uint32_t i = 0; i < 4; ++i) {
-                wc[i] = w[i];
-                ec[i] = e[i];
-            }
-            charger(b + 8u);
+        auto calculer = [&](const Pas& p, uint32_t b) {
+            if (b >= B) return;
             const float4* xb = x2g + b * GRP_X2_PAS;
 #pragma unroll
             for (uint32_t i = 0; i < 4; ++i) {
-                const float s = somme_bloc(wc[i], xb);
-                const float sc = echelle_e8m0(ec[i]);
+                const float s = somme_bloc(p.w[i], xb);
+                const float sc = echelle_e8m0(p.e[i]);
                 if (b < cesure[i])
                     acc[i][0] = fmaf(s, sc, acc[i][0]);
                 else
                     acc[i][1] = fmaf(s, sc, acc[i][1]);
             }
+        };
+        Pas p0, p1, p2;
+        charger(p0, c0);
+        charger(p1, c0 + 8u);
+        for (uint32_t b = c0; b < B; b += 24u) {
+            charger(p2, b + 16u);
+            calculer(p0, b);
+            charger(p0, b + 24u);
+            calculer(p1, b + 8u);
+            charger(p1, b + 32u);
+            calculer(p2, b + 16u);
         }
 #pragma unroll
         for (uint32_t i = 0; i < 4; ++i) {
