@@ -105,10 +105,11 @@ def pics():
 
 # DRAM bytes (read + write) of the dominant launch measured by ncu on the same launch shape (4
 # routed experts of 2880 x 2880): the decode launch of the overlapped schedule (gate/up decoded
-# into their GEMV, down decoded alongside: 3 x 4 CODES_CTX streams; 51.01 MB read, 1.08 MB
-# written for 47.64 MB of streams), and the sequential schedule's gate/up launch (34.03 MB
-# read, 13 KB written for 31.76 MB of streams).
-TRAFIC_CODES = {"recouvrant": 52_086_528, "sequentiel": 34_041_856}
+# into their GEMV, down decoded alongside: 3 x 4 CODES_CTX streams; 51.02 MB read, 0.81 MB
+# written for 47.64 MB of streams, profiles/k_moe_codes_dense_config1_4experts.md), and the
+# sequential schedule's gate/up launch (34.03 MB read, 13 KB written for 31.76 MB of streams,
+# an earlier capture of that launch shape).
+TRAFIC_CODES = {"recouvrant": 51_838_208, "sequentiel": 34_041_856}
 
 
 class Horloges:

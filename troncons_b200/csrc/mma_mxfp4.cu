@@ -57,13 +57,13 @@ __host__ __device__ __forceinline__ uint32_t mma_etage(uint32_t N) { return MMA_
 __host__ __device__ __forceinline__ uint32_t mma_echelles(uint32_t N, uint32_t C) {
     return ((MMA_M + mma_n_pad(N)) * (C / 32u) + 15u) & ~15u;
 }
-// All stages, the staged scales, the mbarriers and the tensor-memory base, and 8 KB of slack
-// past the tiles (never read by a correct descriptor).
+// All stages, the staged scales, the mbarriers and the tensor-memory base.
 __host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N, uint32_t C, uint32_t E) {
-    return E * mma_etage(N) + mma_echelles(N, C) + 64u + 8192u;
+    return E * mma_etage(N) + mma_echelles(N, C) + 64u;
 }
+// Four stages where two CTAs still fit on an SM (their chunks interleave), else three.
 __host__ __device__ __forceinline__ uint32_t mma_etages(uint32_t N, uint32_t C) {
-    return mma_smem(N, C, 4u) <= 220u * 1024u ? 4u : 3u;
+    return mma_smem(N, C, 4u) <= 112u * 1024u ? 4u : 3u;
 }
 
 // Offset in a K-major no-swizzle tile of row r and byte k (0..127) of the chunk.
@@ -169,7 +169,7 @@ __device__ __forceinline__ ArgsMma args_du_lot(const DescGemm* __restrict__ lot,
 
 // One launch: `a` (lot == nullptr), or matrix blockIdx.y of a batch (its rows past its own R
 // leave the CTA idle).
-__global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(ArgsMma a0, const DescGemm* lot, uint8_t* espace_lot,
+__global__ void __launch_bounds__(MMA_FILS, 2) k_gemm_mxfp4(ArgsMma a0, const DescGemm* lot, uint8_t* espace_lot,
                                                             uint64_t tranche, uint32_t E) {
     extern __shared__ __align__(1024) uint8_t dyn[];
     const ArgsMma a = lot != nullptr ? args_du_lot(lot, espace_lot, tranche, a0.erreur) : a0;
