@@ -780,6 +780,41 @@ __global__ void __launch_bounds__(BAS_WARPS * 32) k_moe_bas(ArgsMoe a) {
     }
 }
 
+// The same down GEMV in row groups (gemv_groupes.cuh), where the shape allows: the words
+// k_moe_codes_dense stored are the down matrix's codes in their raw layout (word 32 m + lane =
+// bytes 4 (32 m + lane) .. + 3, 16 bytes per block, blocks row-major), so the raw path's GEMV
+// reads them as it reads CODES_BRUTS, with each block's scale rebuilt from its row median and
+// its delta byte. The partials are k_moe_bas's (and the raw layer's), bit for bit.
+__global__ void __launch_bounds__(128, 3) k_moe_bas_groupes(ArgsMoe a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const Couche& c = a.c;
+    const uint32_t i = blockIdx.z, warp = threadIdx.x >> 5;
+    if (!tenu(c, i)) return;
+    const uint32_t R = c.lignes[2], C = c.colonnes[2], B = C / 32u, nblocs = R * B;
+    const uint8_t* partie;
+    uint64_t taille;
+    Flux fm;
+    // The part is a layer input: its medians are found before the wait (h and the words come
+    // from the previous kernels).
+    const bool bon = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_MEDIANES, 2, fm) &&
+                     fm.produits == R && fm.longueur >= R;
+    attendre_amont();
+    liberer_aval();
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&c.controle[4u * i + CTL_FORMAT], 1u);
+        return;
+    }
+    float4* x2g = reinterpret_cast<float4*>(dyn);
+    charger_x2_groupes(x2g, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    __syncthreads();
+    const uint32_t W = blockDim.x >> 5;
+    const uint32_t K = a.plan.K[2];
+    const uint8_t* cd = a.espace + a.plan.cd + uint64_t(i) * 16u * nblocs;
+    float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[2]) + uint64_t(i) * R * K;
+    gemv_groupes<true, true>(cd, deltas_de(a, i, 2, nblocs), nullptr, x2g, R, B, parts, K, blockIdx.x * W + warp,
+                             gridDim.x * W, fm.p);
+}
+
 // ------------------------------------------------------------------ 3. SwiGLU of the gate/up rows
 
 __device__ __forceinline__ float swiglu_f64(float g, float u) {
@@ -1010,12 +1045,20 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
             if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
                 return e;
             marque(3);
-            const size_t smem_b = bas_octets(c);
-            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_bas), int(smem_b))) != cudaSuccess) return e;
-            const uint64_t nseg = (uint64_t(c.lignes[2]) * (c.colonnes[2] / 32u) + 8u * SEGMENT_MACRO - 1u) / (8u * SEGMENT_MACRO);
-            if ((e = lancer_pdl(k_moe_bas, dim3(uint32_t((nseg + BAS_WARPS - 1) / BAS_WARPS), 1, na), dim3(BAS_WARPS * 32),
-                                smem_b, flux, a)) != cudaSuccess)
-                return e;
+            if (groupes_possibles(c.lignes[2], c.colonnes[2] / 32u)) {
+                const uint32_t smem_b = x2g_octets(c.colonnes[2]);
+                if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_bas_groupes), int(smem_b))) != cudaSuccess) return e;
+                const uint32_t gx = std::max(1u, ((c.lignes[2] + GRP_LIGNES - 1) / GRP_LIGNES + 3u) / 4u);
+                if ((e = lancer_pdl(k_moe_bas_groupes, dim3(gx, 1, na), dim3(128), smem_b, flux, a)) != cudaSuccess) return e;
+            } else {
+                const size_t smem_b = bas_octets(c);
+                if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_bas), int(smem_b))) != cudaSuccess) return e;
+                const uint64_t nseg =
+                    (uint64_t(c.lignes[2]) * (c.colonnes[2] / 32u) + 8u * SEGMENT_MACRO - 1u) / (8u * SEGMENT_MACRO);
+                if ((e = lancer_pdl(k_moe_bas, dim3(uint32_t((nseg + BAS_WARPS - 1) / BAS_WARPS), 1, na),
+                                    dim3(BAS_WARPS * 32), smem_b, flux, a)) != cudaSuccess)
+                    return e;
+            }
             marque(4);
         } else {
             if ((e = codes(2)) != cudaSuccess) return e;

@@ -128,11 +128,14 @@ __device__ __forceinline__ float arbre8_groupe(float a) {
 // The groups g0, g0 + pas, ... of a matrix (codes: 16 bytes per block, row-major blocks,
 // 16-aligned; echelles: one E8M0 byte per block; R rows, B blocks per row, groupes_possibles(R,
 // B)), with the block's staged 2x `x2g`. Per row r: parts[r K + k] = the partial of its k-th
-// segment (PARTS), or y[r] = fold + bias.
-template <bool PARTS>
+// segment (PARTS), or y[r] = fold + bias. MED: `echelles` holds each block's delta byte and
+// `medianes` each row's median (the .trc v1.2 scale coding, trc-codec/src/lib.rs:206-212): the
+// block's E8M0 scale is (median + delta - 128) mod 256.
+template <bool PARTS, bool MED = false>
 __device__ inline void gemv_groupes(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ echelles,
                                     const float* __restrict__ biais, const float4* __restrict__ x2g, uint32_t R,
-                                    uint32_t B, float* __restrict__ sortie, uint32_t K, uint32_t g0, uint32_t pas) {
+                                    uint32_t B, float* __restrict__ sortie, uint32_t K, uint32_t g0, uint32_t pas,
+                                    const uint8_t* __restrict__ medianes = nullptr) {
     const uint32_t voie = threadIdx.x & 31u, a = voie >> 3, g = voie & 7u;
     const uint32_t ngr = R / GRP_LIGNES;
     for (uint32_t gr = g0; gr < ngr; gr += pas) {
@@ -144,6 +147,7 @@ __device__ inline void gemv_groupes(const uint8_t* __restrict__ codes, const uin
         uint32_t cesure[4];  // first column block of each row's second segment (B when none)
         const uint4* ligne_c[4];
         const uint8_t* ligne_e[4];
+        uint32_t decal[4];  // MED: the row's median + 128 (mod 256 once added to a delta)
 #pragma unroll
         for (uint32_t i = 0; i < 4; ++i) {
             acc[i][0] = 0.0f;
@@ -153,6 +157,7 @@ __device__ inline void gemv_groupes(const uint8_t* __restrict__ codes, const uin
             cesure[i] = min(B, (b0 / SEGMENT_BLOCS + 1u) * SEGMENT_BLOCS - b0);
             ligne_c[i] = reinterpret_cast<const uint4*>(codes) + uint64_t(b0);
             ligne_e[i] = echelles + uint64_t(b0);
+            decal[i] = MED ? uint32_t(__ldg(medianes + r)) + 128u : 0u;
         }
         // The four rows' blocks of column block b, loaded two column steps ahead of their use:
         // three buffers in turn (the loop is unrolled by three so that they stay in registers).
@@ -173,7 +178,7 @@ __device__ inline void gemv_groupes(const uint8_t* __restrict__ codes, const uin
 #pragma unroll
             for (uint32_t i = 0; i < 4; ++i) {
                 const float s = somme_bloc(p.w[i], xb);
-                const float sc = echelle_e8m0(p.e[i]);
+                const float sc = echelle_e8m0(MED ? ((p.e[i] + decal[i]) & 255u) : p.e[i]);
                 if (b < cesure[i])
                     acc[i][0] = fmaf(s, sc, acc[i][0]);
                 else
