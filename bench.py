@@ -1135,6 +1135,8 @@ def bras_gemm(args):
     flushed between steps. Beside it the same products token by token with the row-group GEMV
     (trc_gemv_lot over the 48 matrices, one launch per token). Roofline: HBM, the matrices'
     bytes (0.53 B per weight) per call; FLOP/s reported beside it."""
+    import ctypes as C
+
     import numpy as np
     import torch
 
@@ -1152,7 +1154,23 @@ def bras_gemm(args):
     rng = np.random.default_rng(args.graine)
     x = torch.from_numpy(rng.standard_normal((E * 3, n, Cc)).astype(np.float32)).cuda()
     y = torch.zeros(E * 3, n, R, dtype=torch.float32, device="cuda")
-    descs, gv = [], []
+    # the experts resident as SoA slots (codes of each matrix 256-aligned: the weight tiles come
+    # by TMA), copied from the raw parts; the same GEMMs on the raw parts' streams (their codes
+    # 16 mod 32 here: the tiles by 8-byte copies) as a second leg
+    te = T.taille_emplacement(c.dims)
+    slots = torch.empty(E * te + 256, dtype=torch.uint8, device="cuda")
+    sb = slots.data_ptr() + (-slots.data_ptr()) % 256
+    te256 = (te + 255) // 256 * 256
+    ctl = torch.zeros(4 * E, dtype=torch.int32, device="cuda")
+    for e in range(E):
+        cc.n.copier_brut(cc.partie(e, brute=True), slots[(sb - slots.data_ptr()) + e * te256:][:te], c.dims,
+                         ctl[4 * e:4 * e + 4])
+    torch.cuda.synchronize()
+    assert (ctl == 0).all()
+    nbj = R * (Cc // 32)
+    eo = (nbj * 16 + 255) & ~255
+    bo = (eo + nbj + 255) & ~255
+    descs, descs_p = [], []
     for e in range(E):
         p = c.parties_brutes[e]
         base = cc.partie(e, brute=True).data_ptr()
@@ -1163,40 +1181,33 @@ def bras_gemm(args):
             flux[(d[0], d[1])] = int.from_bytes(d[4:8], "little")
         for j in range(3):
             m = 3 * e + j
+            s0 = sb + e * te256 + j * ((bo + 4 * R + 255) & ~255)
+            descs.append(T.DescGemm(s0, s0 + eo, s0 + bo, x[m].data_ptr(), y[m].data_ptr(), R, Cc, n, 0))
             cod, ech, bia = base + flux[(0x06, j)], base + flux[(0x07, j)], base + flux[(0x02, j)]
-            descs.append(T.DescGemm(cod, ech, bia, x[m].data_ptr(), y[m].data_ptr(), R, Cc, n, 0))
+            descs_p.append(T.DescGemm(cod, ech, bia, x[m].data_ptr(), y[m].data_ptr(), R, Cc, n, 0))
     nb = len(descs)
-    dd = torch.frombuffer(bytearray(bytes((T.DescGemm * nb)(*descs))), dtype=torch.uint8).cuda()
+    hote = (T.DescGemm * nb)(*descs)  # host descriptors (copied into the launches' parameters)
+    hote_p = (T.DescGemm * nb)(*descs_p)
+    par_tma = sum(1 for d in descs if d.codes % 32 == 0)  # weight tiles by TMA (else 8-byte copies)
+    par_tma_p = sum(1 for d in descs_p if d.codes % 32 == 0)
     octets = int(T.lib.trc_gemm_mxfp4_lot_espace_octets(Cc, n, nb))
     esp = torch.empty(octets + 256, dtype=torch.uint8, device="cuda")
     e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     vidange = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
 
-    def gemm():
-        T.verifier(T.lib.trc_gemm_mxfp4_lot(dd.data_ptr(), nb, R, Cc, n, e0, octets, err.data_ptr(),
+    def gemm(h=hote):
+        T.verifier(T.lib.trc_gemm_mxfp4_lot(C.addressof(h), nb, R, Cc, n, e0, octets, err.data_ptr(),
                                             torch.cuda.current_stream().cuda_stream))
 
+    t_p = chrono_etapes(lambda: gemm(hote_p), lambda s: None, args.warmup + args.steps, args.warmup, vidange)
+    y_p = y.clone()
     t = chrono_etapes(gemm, lambda s: None, args.warmup + args.steps, args.warmup, vidange)
     assert int(err.item()) == 0, "a bounded wait of the GEMM gave up"
-    # the same products token by token: the slot GEMV batch reads a slot layout; the raw part's
-    # streams are not one, so compare with the raw layer's grouped GEMV through per-token GEMV
-    # descriptors over slots decoded from the parts
-    te = T.taille_emplacement(c.dims)
-    slots = torch.empty(E * te + 256, dtype=torch.uint8, device="cuda")
-    sb = slots.data_ptr() + (-slots.data_ptr()) % 256
-    te256 = (te + 255) // 256 * 256
-    ctl = torch.zeros(4 * E, dtype=torch.int32, device="cuda")
-    for e in range(E):
-        cc.n.copier_brut(cc.partie(e, brute=True), slots[(sb - slots.data_ptr()) + e * te256:][:te], c.dims,
-                         ctl[4 * e:4 * e + 4])
-    pas_m = [0, 0, 0]
-    for j in range(3):
-        nbj = R * (Cc // 32)
-        eo = (nbj * 16 + 255) & ~255
-        bo = (eo + nbj + 255) & ~255
-        pas_m[j] = (bo + 4 * R + 255) & ~255
-    off = [0, pas_m[0], pas_m[0] + pas_m[1]]
+    assert torch.equal(y.view(torch.int32), y_p.view(torch.int32)), "slots and raw parts: different bits"
+    # the same products token by token over the slots (the row-group GEMV batch)
+    pas_m = (bo + 4 * R + 255) & ~255
+    off = [0, pas_m, 2 * pas_m]
     yg = torch.zeros(n, E * 3, R, dtype=torch.float32, device="cuda")
     xg = x.transpose(0, 1).contiguous()  # [n][48][C]
     lots = []
@@ -1225,6 +1236,8 @@ def bras_gemm(args):
         "steps": args.steps, "warmup": args.warmup, "n_gpus": 1, "higher_is_better": True, "dtype": "e2m1 x e4m3 -> f32",
         "config": {"workload": f"config 3 share: {E} experts x 3 matrices 2880 x 2880 MXFP4, {n} tokens per expert "
                                "(x f32, quantized to MXFP8 in the call)", "tokens_per_expert": n, "matrices": nb,
+                               "weights": "resident as SoA slots (codes 256-aligned)",
+                               "weight_tiles_by_tma": par_tma,
                    "l2": "flushed between steps (256 MB written)"},
         "tflops": round(flops / (ms * 1e-3) / 1e12, 2),
         "roofline": {"bound": "hbm", "achieved": round(octets_w / (ms * 1e-3) / 1e9, 1), "peak": pic, "unit": "GB/s",
@@ -1233,6 +1246,10 @@ def bras_gemm(args):
         "gemv_token_by_token": {"ms": round(ms_v, 4), "value": round(n * octets_w / (ms_v * 1e-3) / 1e9, 1),
                                 "unit": "GB/s (weight bytes read per token pass)",
                                 "speedup_of_gemm": round(ms_v / ms, 2)},
+        "from_raw_parts": {"ms": round(sum(t_p) / args.steps, 4),
+                           "value": round(octets_w / (sum(t_p) / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",
+                           "weight_tiles_by_tma": par_tma_p,
+                           "note": "the same GEMMs on the raw parts' CODES_BRUTS / ECHELLES_BRUTES streams, same bits"},
         "max_rel_diff_vs_gemv": ecart,
         "generation_s": round(t_gen, 1),
     }

@@ -607,17 +607,20 @@ int trc_gemm_mxfp4(const uint8_t* codes, const uint8_t* echelles, const float* b
 uint64_t trc_gemm_mxfp4_espace_octets(uint32_t colonnes, uint32_t n);
 
 /* New: one matrix of a batch of trc_gemm_mxfp4 calls, 56 bytes (device addresses). Each matrix
- * must meet trc_gemm_mxfp4's rules (codes 16-aligned, colonnes a multiple of 32, 1 to 256 tokens);
- * they are not checked on the host, as the descriptors live on the device. */
+ * must meet trc_gemm_mxfp4's rules (codes and scales 16-aligned, colonnes a multiple of 32, 1 to
+ * 256 tokens); trc_gemm_mxfp4_lot checks them. Codes 32-aligned with colonnes a multiple of 64
+ * let the weight tiles come by TMA (otherwise 8-byte copies). */
 typedef struct trc_desc_gemm {
     uint64_t codes, echelles, biais, x, y;
     uint32_t lignes, colonnes, n, x_bf16;
 } trc_desc_gemm;
 
-/* New: nb tensor-core GEMMs in two launches (every x quantized, then every matrix's row tiles):
- * descs device trc_desc_gemm[nb], rows / columns / tokens of each at most lignes_max /
- * colonnes_max / n_max; espace trc_gemm_mxfp4_lot_espace_octets bytes, 256-aligned. For the
- * experts of a layer that receive many tokens (an expert-parallel share at batch 64). */
+/* New: nb tensor-core GEMMs, two launches per group of up to 48 matrices (every x quantized,
+ * then every matrix's row tiles): descs HOST trc_desc_gemm[nb] (copied into the launches'
+ * parameters with each matrix's TMA tensor maps; the caller may reuse the array on return), rows
+ * / columns / tokens of each at most lignes_max / colonnes_max / n_max; espace
+ * trc_gemm_mxfp4_lot_espace_octets bytes, 256-aligned. For the experts of a layer that receive
+ * many tokens (an expert-parallel share at batch 64). */
 int trc_gemm_mxfp4_lot(const trc_desc_gemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
                        uint32_t n_max, void* espace, size_t espace_octets, uint32_t* erreur, void* flux);
 uint64_t trc_gemm_mxfp4_lot_espace_octets(uint32_t colonnes_max, uint32_t n_max, uint32_t nb);

@@ -48,6 +48,16 @@ def couche_gpt_oss():
 
 
 @pytest.fixture(scope="session")
+def couche_impaire():
+    """A small layer whose down matrix has an odd number of blocks per row (9: 256 x 288), so
+    that its GEMVs take the row walks (k_moe_bas, k_moe_brut) instead of the row groups."""
+    import troncons_b200 as T
+    import troncons_b200.synth as S
+
+    return S.couche(11, T.DimsExpert.de([288, 288, 256], [256, 256, 288]), 8)
+
+
+@pytest.fixture(scope="session")
 def couche_petite():
     """A small layer (8 experts: gate and up 256 x 512, down 512 x 256) for quick checks."""
     import troncons_b200 as T

@@ -67,6 +67,33 @@ def test_gemm_contre_f64(R, Cc, n):
     assert np.sqrt(np.mean((y - ref) ** 2)) <= 5e-2 * np.sqrt(np.mean(ref ** 2))
 
 
+def test_tuiles_par_copies_egales_tma():
+    """Codes 16 bytes off a 32-byte boundary: the weight tiles come by 8-byte copies instead of
+    TMA (the 4-bit unpacking tensor map needs 32-aligned codes); the same bits either way."""
+    import troncons_b200 as T
+
+    R, Cc, n = 384, 2880, 48
+    codes, ech, biais = _matrice(5, R, Cc)
+    x = np.random.default_rng(6).standard_normal((n, Cc)).astype(np.float32)
+    y_tma, _ = _gemm(codes, ech, biais, x, R, Cc)
+    brut = torch.zeros(codes.size + 48, dtype=torch.uint8, device="cuda")
+    debut = (-brut.data_ptr()) % 32 + 16  # 16 mod 32
+    brut[debut:debut + codes.size] = torch.from_numpy(codes).cuda()
+    ed, bd, xt = (torch.from_numpy(a).cuda() for a in (ech, biais, x))
+    y = torch.full((n, R), float("nan"), dtype=torch.float32, device="cuda")
+    octets = int(T.lib.trc_gemm_mxfp4_espace_octets(Cc, n))
+    esp = torch.empty(octets + 256, dtype=torch.uint8, device="cuda")
+    e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert (brut.data_ptr() + debut) % 32 == 16
+    assert T.lib.trc_gemm_mxfp4(brut.data_ptr() + debut, ed.data_ptr(), bd.data_ptr(), R, Cc, xt.data_ptr(), 0, n,
+                                y.data_ptr(), e0, octets, err.data_ptr(),
+                                torch.cuda.current_stream().cuda_stream) == T.TRC_OK, T.lib.trc_derniere_erreur()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), y_tma.view(np.uint32))
+
+
 def test_gemm_bf16_et_refus():
     import troncons_b200 as T
 
@@ -100,12 +127,12 @@ def test_lot_egal_seul():
         descs.append(T.DescGemm(t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), t[3].data_ptr(), y.data_ptr(),
                                 R, Cc, n, 0))
     nb = len(formes)
-    dd = torch.frombuffer(bytearray(bytes((T.DescGemm * nb)(*descs))), dtype=torch.uint8).cuda()
+    hote = (T.DescGemm * nb)(*descs)  # host descriptors: copied into the launches' parameters
     octets = int(T.lib.trc_gemm_mxfp4_lot_espace_octets(2880, 64, nb))
     esp = torch.empty(octets + 256, dtype=torch.uint8, device="cuda")
     e0 = esp.data_ptr() + (-esp.data_ptr()) % 256
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    assert T.lib.trc_gemm_mxfp4_lot(dd.data_ptr(), nb, 2880, 2880, 64, e0, octets, err.data_ptr(),
+    assert T.lib.trc_gemm_mxfp4_lot(C.addressof(hote), nb, 2880, 2880, 64, e0, octets, err.data_ptr(),
                                     torch.cuda.current_stream().cuda_stream) == T.TRC_OK, T.lib.trc_derniere_erreur()
     torch.cuda.synchronize()
     assert int(err.item()) == 0

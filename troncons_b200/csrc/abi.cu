@@ -416,6 +416,16 @@ int trc_gemm_mxfp4_lot(const trc_desc_gemm* descs, uint32_t nb, uint32_t lignes_
     if (descs == nullptr || nb == 0 || nb > 65535) return usage("%u GEMM descriptors", nb);
     if (lignes_max == 0 || colonnes_max == 0 || colonnes_max % 32) return usage("%u x %u at most", lignes_max, colonnes_max);
     if (n_max == 0 || n_max > 256) return usage("%u tokens at most (1 to 256)", n_max);
+    for (uint32_t i = 0; i < nb; ++i) {
+        const trc_desc_gemm& d = descs[i];
+        if (d.lignes == 0 || d.lignes > lignes_max || d.colonnes == 0 || d.colonnes % 32 || d.colonnes > colonnes_max ||
+            d.n == 0 || d.n > n_max)
+            return usage("gemm batch: matrix %u is %u x %u with %u tokens (at most %u x %u, %u tokens)", i, d.lignes,
+                         d.colonnes, d.n, lignes_max, colonnes_max, n_max);
+        if (d.codes == 0 || d.echelles == 0 || d.x == 0 || d.y == 0 || d.codes % 16 || d.echelles % 16 ||
+            d.x % (d.x_bf16 ? 2 : 4) || d.y % 4)
+            return usage("gemm batch: matrix %u: a buffer missing or misaligned (codes and scales 16-aligned)", i);
+    }
     if (!tb::gemm_mxfp4_possible(colonnes_max, n_max))
         return usage("gemm batch: %u columns x %u tokens exceed shared memory", colonnes_max, n_max);
     if (espace == nullptr || erreur == nullptr || !aligne(espace, 256)) return usage("gemm batch: workspace 256-aligned");
