@@ -80,12 +80,18 @@ __host__ __device__ __forceinline__ uint32_t mma_mots_ef(uint32_t N, uint32_t C)
 __host__ __device__ __forceinline__ uint32_t mma_smem(uint32_t N, uint32_t C, uint32_t E) {
     return 1024u + E * mma_etage(N) + mma_mots_ef(N, C) + 16u * E + 16u;
 }
-__host__ __device__ __forceinline__ uint32_t mma_etages(uint32_t N, uint32_t C) {
-    for (uint32_t E = MMA_ETAGES_MAX; E >= 3u; --E)
-        if (mma_smem(N, C, E) <= 112u * 1024u) return E;
-    for (uint32_t E = MMA_ETAGES_MAX; E > 3u; --E)
-        if (mma_smem(N, C, E) <= 220u * 1024u) return E;
-    return 3u;
+// The stage count that keeps the most chunks in flight per SM (CTAs per SM x stages, up to
+// three CTAs; on a tie, more CTAs: their prologues and epilogues overlap each other's copies).
+__host__ __device__ inline uint32_t mma_etages(uint32_t N, uint32_t C) {
+    uint32_t meilleur = 3u, total = 0u;
+    for (uint32_t E = 3u; E <= MMA_ETAGES_MAX && mma_smem(N, C, E) <= 220u * 1024u; ++E) {
+        const uint32_t ctas = min(3u, (228u * 1024u) / (mma_smem(N, C, E) + 1024u));
+        if (ctas * E > total) {
+            total = ctas * E;
+            meilleur = E;
+        }
+    }
+    return meilleur;
 }
 
 // Offset of byte k (0..127) of row r in a [rows][128] tile with the 128-byte swizzle.
@@ -196,7 +202,7 @@ struct LotMma {
     uint32_t nb, premier;
 };
 
-__global__ void __launch_bounds__(MMA_FILS, 2) k_gemm_mxfp4(const __grid_constant__ LotMma lot, uint32_t E) {
+__global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(const __grid_constant__ LotMma lot, uint32_t E) {
     extern __shared__ __align__(1024) uint8_t dyn_brut[];
     uint8_t* dyn = dyn_brut + ((1024u - (adresse_partagee(dyn_brut) & 1023u)) & 1023u);  // 1,024-aligned tiles
     const uint32_t m = blockIdx.y;
@@ -225,6 +231,11 @@ __global__ void __launch_bounds__(MMA_FILS, 2) k_gemm_mxfp4(const __grid_constan
     auto col_sfa = [Np](uint32_t e) { return Np + 12u * e; };
     auto col_sfb = [Np](uint32_t e) { return Np + 12u * e + 4u; };
 
+    // Stage tiles zeroed (the 8-byte copies write only data halves and rows that exist), then
+    // ordered before the TMA writes that follow.
+    for (uint32_t i = threadIdx.x; i < E * etage / 16u; i += MMA_FILS)
+        reinterpret_cast<uint4*>(dyn)[i] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     if (threadIdx.x == 0) {
         for (uint32_t e = 0; e < E; ++e) {
             mbar_init(plein + e, MMA_PROD);  // one arrival per producer thread
@@ -241,51 +252,58 @@ __global__ void __launch_bounds__(MMA_FILS, 2) k_gemm_mxfp4(const __grid_constan
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
-    attendre_amont();
-    liberer_aval();
-    // The scale bytes of the CTA's rows and of the tokens, staged in the (not yet used) stage
-    // area, then arranged as the scale-factor words of every chunk: word (ch, m) = the bytes of
-    // blocks 4 ch .. 4 ch + 3 of row (or token) m, 0 past the row's blocks or past R (N).
-    {
-        uint8_t* ech_a = dyn;
-        uint8_t* ech_b = dyn + MMA_M * B;
-        const uint32_t lignes = min(MMA_M, R - r0);
-        if (threadIdx.x < MMA_PROD) {
-            // r0 B is a multiple of 16 (r0 is one of 128): the rows' bytes are 16-aligned
-            for (uint32_t t = threadIdx.x; t < ((lignes * B) & ~15u) / 16u; t += MMA_PROD)
-                cp_async16(ech_a + 16u * t, ech + uint64_t(r0) * B + 16u * t, 16u);
-            for (uint32_t i = ((lignes * B) & ~15u) + threadIdx.x; i < lignes * B; i += MMA_PROD)
-                ech_a[i] = ech[uint64_t(r0) * B + i];
-            for (uint32_t t = threadIdx.x; t < ((N * B) & ~15u) / 16u; t += MMA_PROD)
-                cp_async16(ech_b + 16u * t, xs + 16u * t, 16u);
-            for (uint32_t i = ((N * B) & ~15u) + threadIdx.x; i < N * B; i += MMA_PROD) ech_b[i] = xs[i];
-            cp_async_commit();
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        const uint32_t L = MMA_M + Np;
-        for (uint32_t w = threadIdx.x; w < nchunks * L; w += MMA_FILS) {
-            const uint32_t ch = w / L, mm = w % L;
-            const bool ligne = mm < MMA_M;
-            const uint32_t q = ligne ? mm : mm - MMA_M;
-            const uint8_t* src = ligne ? ech_a + q * B : ech_b + q * B;
-            uint32_t v = 0;
-            if (ligne ? q < lignes : q < N)
-                for (uint32_t k = 0; k < 4u && 4u * ch + k < B; ++k) v |= uint32_t(src[4u * ch + k]) << (8u * k);
-            mots[w] = v;
-        }
-        __syncthreads();
-        // Stage tiles zeroed: the cp.async paths write only data halves and rows that exist.
-        for (uint32_t i = threadIdx.x; i < E * etage / 16u; i += MMA_FILS)
-            reinterpret_cast<uint4*>(dyn)[i] = make_uint4(0, 0, 0, 0);
-    }
     asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const uint32_t tmem = *tmem_base_s;
+    attendre_amont();  // the quantized activations and their scales
+    liberer_aval();
     // Parity of the k-th completion (k = ch / E) of stage ch % E's barriers.
     auto parite = [E](uint32_t ch) { return (ch / E) & 1u; };
     const uint32_t L = MMA_M + Np;
+    // Stage ch's TMA copies (thread 0): the bytes announced on its "full" barrier, then issued.
+    auto tma = [&](uint32_t ch) {
+        const uint32_t e = ch % E;
+        const bool a_tma = tma_a && ch < pleins;
+        if (!a_tma && !tma_b) return;
+        uint8_t* ta = dyn + e * etage;
+        // The 4-bit unpacking copy counts the bytes it reads (64 per row of 128 elements), not
+        // the 128 per row it writes with the padding.
+        mbar_octets_attendus(plein + e, (a_tma ? MMA_M * 64u : 0u) + (tma_b ? Np * 128u : 0u));
+        if (a_tma) tma_3d(ta, &lot.ta[m], 0, int32_t(ch), int32_t(r0), plein + e);
+        if (tma_b) tma_2d(ta + MMA_M * 128u, &lot.tb[m], int32_t(128u * ch), 0, plein + e);
+    };
+    // The first stages' copies fly while the scale-factor words are built.
+    if (threadIdx.x == 0)
+        for (uint32_t ch = 0; ch < min(E, nchunks); ++ch) tma(ch);
+    // Scale-factor words of every chunk: word (ch, m) = the E8M0 bytes of blocks 4 ch .. 4 ch + 3
+    // of row m (0 past the row's blocks or past R); the tokens' words come as the quantizer
+    // wrote them ([chunk][Npad], zero past their blocks).
+    {
+        const uint32_t lignes = min(MMA_M, R - r0);
+        if (threadIdx.x < MMA_M) {
+            const uint32_t mm = threadIdx.x;
+            const uint8_t* src = ech + uint64_t(r0 + min(mm, lignes - 1u)) * B;  // 2-aligned (B even) or not
+            for (uint32_t ch = 0; ch < nchunks; ++ch) {
+                uint32_t v = 0;
+                if (mm < lignes) {
+                    if ((B & 1u) == 0 && 4u * ch + 3u < B) {
+                        const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src + 4u * ch);
+                        v = uint32_t(__ldg(s2)) | (uint32_t(__ldg(s2 + 1)) << 16);
+                    } else {
+                        for (uint32_t k = 0; k < 4u && 4u * ch + k < B; ++k) v |= uint32_t(__ldg(src + 4u * ch + k)) << (8u * k);
+                    }
+                }
+                mots[ch * L + mm] = v;
+            }
+        }
+        const uint32_t* xsw = reinterpret_cast<const uint32_t*>(xs);
+        for (uint32_t w = threadIdx.x; w < nchunks * Np; w += MMA_FILS) {
+            const uint32_t ch = w / Np, n = w - ch * Np;
+            mots[ch * L + MMA_M + n] = n < N ? xsw[w] : 0u;
+        }
+    }
+    __syncthreads();
 
     if (warp < 4u) {
         // ---------------- producers: copies and scale factors, up to E chunks ahead
@@ -301,13 +319,7 @@ __global__ void __launch_bounds__(MMA_FILS, 2) k_gemm_mxfp4(const __grid_constan
             uint8_t* ta = dyn + e * etage;
             uint8_t* tbt = ta + MMA_M * 128u;
             const bool a_tma = tma_a && ch < pleins;
-            if (threadIdx.x == 0 && (a_tma || tma_b)) {
-                // The 4-bit unpacking copy counts the bytes it reads (64 per row of 128 elements),
-                // not the 128 per row it writes with the padding.
-                mbar_octets_attendus(plein + e, (a_tma ? MMA_M * 64u : 0u) + (tma_b ? Np * 128u : 0u));
-                if (a_tma) tma_3d(ta, &lot.ta[m], 0, int32_t(ch), int32_t(r0), plein + e);
-                if (tma_b) tma_2d(tbt, &lot.tb[m], int32_t(128u * ch), 0, plein + e);
-            }
+            if (threadIdx.x == 0 && ch >= E) tma(ch);
             if (!a_tma) charger_a(ta, codes, R, B, r0, kb0, nkb);
             if (!tma_b) charger_b(tbt, xq, C, N, kb0, nkb);
             const uint32_t* mc = mots + ch * L;
@@ -422,15 +434,19 @@ __global__ void __launch_bounds__(256) k_quantifier_mxfp8(const __grid_constant_
     asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(paire) : "f"(0.0f), "f"(q));
     const uint32_t kp = voie < 16u ? 2u * voie : 2u * (voie - 16u) + 1u;
     xq[uint64_t(n) * C + 32u * b + kp] = uint8_t(paire & 0xFFu);
-    if (voie == 0) xs[uint64_t(n) * B + b] = uint8_t(E + 127);
+    // the token's scale bytes as scale-factor words: [chunk][Npad] u32, byte = the block in its
+    // chunk; the last word's bytes past the row's blocks are zero
+    if (voie == 0) xs[(uint64_t(b / 4u) * mma_n_pad(N) + n) * 4u + (b & 3u)] = uint8_t(E + 127);
+    if (voie == 1 && b == B - 1u)
+        for (uint32_t k = (b & 3u) + 1u; k < 4u; ++k) xs[(uint64_t(b / 4u) * mma_n_pad(N) + n) * 4u + k] = 0;
 }
 
-bool gemm_mxfp4_possible(uint32_t C, uint32_t N) {
-    // the scale bytes of the rows and tokens are staged in the stage area at the start
-    return C / 32u <= 384u && mma_smem(N, C, 3u) <= 220u * 1024u;
-}
+bool gemm_mxfp4_possible(uint32_t C, uint32_t N) { return mma_smem(N, C, 3u) <= 220u * 1024u; }
 
-uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N) { return uint64_t(mma_n_pad(N)) * C + uint64_t(mma_n_pad(N)) * (C / 32u); }
+// The quantized activations [Npad][C] and their scale-factor words [chunk][Npad].
+uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N) {
+    return uint64_t(mma_n_pad(N)) * C + uint64_t(mma_chunks(C)) * mma_n_pad(N) * 4u;
+}
 
 // ------------------------------------------------------------------ tensor maps (host)
 
