@@ -72,8 +72,9 @@ __host__ __device__ __forceinline__ uint32_t mma_tmem_colonnes(uint32_t N, uint3
 // Shared bytes of one stage: A tile (128 rows x 128 bytes) and B tile (Npad rows x 128 bytes).
 __host__ __device__ __forceinline__ uint32_t mma_etage(uint32_t N) { return MMA_M * 128u + mma_n_pad(N) * 128u; }
 // The scale-factor words of every chunk: [chunk][128 rows, then Npad tokens].
+__host__ __device__ __forceinline__ uint32_t mma_mots_ligne(uint32_t N) { return MMA_M + mma_n_pad(N) + 1u; }
 __host__ __device__ __forceinline__ uint32_t mma_mots_ef(uint32_t N, uint32_t C) {
-    return mma_chunks(C) * (MMA_M + mma_n_pad(N)) * 4u;
+    return (mma_chunks(C) * mma_mots_ligne(N) * 4u + 15u) & ~15u;
 }
 // 1,024 bytes of alignment slack, the stages, the scale-factor words, the mbarriers (full and
 // empty per stage, done), the tensor-memory base and the abandon flag.
@@ -231,6 +232,10 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(const __grid_constan
     auto col_sfa = [Np](uint32_t e) { return Np + 12u * e; };
     auto col_sfb = [Np](uint32_t e) { return Np + 12u * e + 4u; };
 
+    if (threadIdx.x == 0) {
+        if (tma_a) asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&lot.ta[m])) : "memory");
+        if (tma_b) asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&lot.tb[m])) : "memory");
+    }
     // Stage tiles zeroed (the 8-byte copies write only data halves and rows that exist), then
     // ordered before the TMA writes that follow.
     for (uint32_t i = threadIdx.x; i < E * etage / 16u; i += MMA_FILS)
@@ -256,11 +261,9 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(const __grid_constan
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const uint32_t tmem = *tmem_base_s;
-    attendre_amont();  // the quantized activations and their scales
-    liberer_aval();
     // Parity of the k-th completion (k = ch / E) of stage ch % E's barriers.
     auto parite = [E](uint32_t ch) { return (ch / E) & 1u; };
-    const uint32_t L = MMA_M + Np;
+    const uint32_t L = mma_mots_ligne(N);  // words per chunk (odd: the scattered stores spread over the banks)
     // Stage ch's TMA copies (thread 0): the bytes announced on its "full" barrier, then issued.
     auto tma = [&](uint32_t ch) {
         const uint32_t e = ch % E;
@@ -273,34 +276,73 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(const __grid_constan
         if (a_tma) tma_3d(ta, &lot.ta[m], 0, int32_t(ch), int32_t(r0), plein + e);
         if (tma_b) tma_2d(ta + MMA_M * 128u, &lot.tb[m], int32_t(128u * ch), 0, plein + e);
     };
-    // The first stages' copies fly while the scale-factor words are built.
-    if (threadIdx.x == 0)
-        for (uint32_t ch = 0; ch < min(E, nchunks); ++ch) tma(ch);
     // Scale-factor words of every chunk: word (ch, m) = the E8M0 bytes of blocks 4 ch .. 4 ch + 3
     // of row m (0 past the row's blocks or past R); the tokens' words come as the quantizer
-    // wrote them ([chunk][Npad], zero past their blocks).
+    // wrote them ([chunk][Npad], zero past their blocks). The weights' bytes are a layer input:
+    // their loads are issued before the wait for the quantizer, and the first stages' copies
+    // are issued while they are in flight (ahead of the copies, they do not queue behind them).
     {
         const uint32_t lignes = min(MMA_M, R - r0);
-        if (threadIdx.x < MMA_M) {
-            const uint32_t mm = threadIdx.x;
-            const uint8_t* src = ech + uint64_t(r0 + min(mm, lignes - 1u)) * B;  // 2-aligned (B even) or not
-            for (uint32_t ch = 0; ch < nchunks; ++ch) {
-                uint32_t v = 0;
-                if (mm < lignes) {
-                    if ((B & 1u) == 0 && 4u * ch + 3u < B) {
-                        const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src + 4u * ch);
-                        v = uint32_t(__ldg(s2)) | (uint32_t(__ldg(s2 + 1)) << 16);
-                    } else {
-                        for (uint32_t k = 0; k < 4u && 4u * ch + k < B; ++k) v |= uint32_t(__ldg(src + 4u * ch + k)) << (8u * k);
-                    }
+        // The CTA's rows' scale bytes are contiguous (rows r0 .. r0 + lignes - 1): consecutive
+        // threads take consecutive (row, chunk) words, each read as the aligned 32-bit words it
+        // straddles (coalesced; the scales are 16-aligned) and shifted into place; no read past
+        // the matrix's last scale byte.
+        {
+            const uint64_t base = uint64_t(r0) * B, fin = uint64_t(R) * B;
+            const uint32_t* e32 = reinterpret_cast<const uint32_t*>(ech);
+            constexpr uint32_t LOT = 24;  // all of a 2,880-column tile's words in one round trip
+            for (uint32_t t0 = threadIdx.x; t0 < lignes * nchunks; t0 += LOT * MMA_FILS) {
+                uint32_t lo[LOT], hi[LOT];
+#pragma unroll
+                for (uint32_t k = 0; k < LOT; ++k) {
+                    const uint32_t t = t0 + k * MMA_FILS;
+                    const uint32_t mm = t / nchunks, ch = t - mm * nchunks;
+                    const uint64_t o = base + uint64_t(mm) * B + 4u * ch;
+                    lo[k] = t < lignes * nchunks ? __ldg(e32 + (o >> 2)) : 0u;
+                    hi[k] = (t < lignes * nchunks && (o & 3u) != 0 && ((o >> 2) + 1u) * 4u < fin) ? __ldg(e32 + (o >> 2) + 1u) : 0u;
                 }
-                mots[ch * L + mm] = v;
+                if (t0 == threadIdx.x) {  // first round: the activations, then the first copies
+                    attendre_amont();      // the quantized activations and their scales
+                    liberer_aval();
+                    if (threadIdx.x == 0)
+                        for (uint32_t ch = 0; ch < min(E, nchunks); ++ch) tma(ch);
+                }
+#pragma unroll
+                for (uint32_t k = 0; k < LOT; ++k) {
+                    const uint32_t t = t0 + k * MMA_FILS;
+                    if (t >= lignes * nchunks) break;
+                    const uint32_t mm = t / nchunks, ch = t - mm * nchunks;
+                    const uint64_t o = base + uint64_t(mm) * B + 4u * ch;
+                    uint32_t v = __funnelshift_r(lo[k], hi[k], 8u * uint32_t(o & 3u));
+                    if (4u * ch + 4u > B) v &= (1u << (8u * (B - 4u * ch))) - 1u;  // bytes past the row's blocks
+                    mots[ch * L + mm] = v;
+                }
+            }
+            if (threadIdx.x >= lignes * nchunks) {  // a thread with no row word still waits, and thread 0 still copies
+                attendre_amont();
+                liberer_aval();
+                if (threadIdx.x == 0)
+                    for (uint32_t ch = 0; ch < min(E, nchunks); ++ch) tma(ch);
+            }
+            for (uint32_t t = lignes * nchunks + threadIdx.x; t < MMA_M * nchunks; t += MMA_FILS) {
+                const uint32_t mm = t / nchunks, ch = t - mm * nchunks;
+                mots[ch * L + mm] = 0u;  // rows past R
             }
         }
         const uint32_t* xsw = reinterpret_cast<const uint32_t*>(xs);
-        for (uint32_t w = threadIdx.x; w < nchunks * Np; w += MMA_FILS) {
-            const uint32_t ch = w / Np, n = w - ch * Np;
-            mots[ch * L + MMA_M + n] = n < N ? xsw[w] : 0u;
+        constexpr uint32_t LOTW = 4;
+        for (uint32_t w0 = threadIdx.x; w0 < nchunks * Np; w0 += LOTW * MMA_FILS) {
+            uint32_t v[LOTW];
+#pragma unroll
+            for (uint32_t k = 0; k < LOTW; ++k) {
+                const uint32_t w = w0 + k * MMA_FILS;
+                v[k] = (w < nchunks * Np && w % Np < N) ? __ldg(xsw + w) : 0u;
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < LOTW; ++k) {
+                const uint32_t w = w0 + k * MMA_FILS;
+                if (w < nchunks * Np) mots[(w / Np) * L + MMA_M + w % Np] = v[k];
+            }
         }
     }
     __syncthreads();
