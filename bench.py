@@ -1276,21 +1276,25 @@ def bras_prefill(args):
     r0 = torch.from_numpy(rng.standard_normal((P, R2)).astype(np.float32)).cuda()
     rf, rp = r0.clone(), r0.clone()
     vidange = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    legs = ("fusionnee", "par_flux") if P <= 128 else ("par_flux",)  # the fused layer takes 128 tokens at most
     for _ in range(2):
-        cc.couche(x, rf)
+        if P <= 128:
+            cc.couche(x, rf)
         cc.couche_par_flux(x, rp)
     torch.cuda.synchronize()
     graphes = {}
     for nom, f in (("fusionnee", lambda: cc.couche(x, rf)), ("par_flux", lambda: cc.couche_par_flux(x, rp))):
+        if nom not in legs:
+            continue
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             f()
         graphes[nom] = g
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    temps = {"fusionnee": [], "par_flux": []}
+    temps = {n: [] for n in legs}
     egaux = True
     for s in range(args.warmup + args.steps):
-        for nom in ("fusionnee", "par_flux"):
+        for nom in legs:
             (rf if nom == "fusionnee" else rp).copy_(r0)
             vidange.zero_()
             a.record()
@@ -1299,10 +1303,29 @@ def bras_prefill(args):
             torch.cuda.synchronize()
             if s >= args.warmup:
                 temps[nom].append(a.elapsed_time(b))
-        egaux &= bool(torch.equal(rf.view(torch.int32), rp.view(torch.int32)))
+        if P <= 128:
+            egaux &= bool(torch.equal(rf.view(torch.int32), rp.view(torch.int32)))
     assert (cc.controle.cpu().numpy() == 0).all()
+    # the same with the experts of >= 16 activations on the tensor cores (trc_moe_couche_par_flux_mma):
+    # not capturable (one wait for the routing), timed eagerly, router included
+    rm = r0.clone()
+    t_mma = []
+    for s in range(args.warmup + args.steps):
+        rm.copy_(r0)
+        vidange.zero_()
+        a.record()
+        cc.couche_par_flux(x, rm, mma_seuil=16)
+        b.record()
+        torch.cuda.synchronize()
+        if s >= args.warmup:
+            t_mma.append(a.elapsed_time(b))
+    assert int(cc.erreur_pf.item()) == 0 and (cc.controle.cpu().numpy() == 0).all()
+    dp, dm = (rp - r0).cpu().numpy(), (rm - r0).cpu().numpy()
+    ecart_mma = float(np.abs(dm - dp).max() / max(1e-30, np.abs(dp).max()))
     ms = {n: sum(v) / len(v) for n, v in temps.items()}
+    ms_mma = sum(t_mma) / len(t_mma)
     idx = cc.idx.cpu().numpy()
+    comptes = np.bincount(idx, minlength=c.experts)
     print(json.dumps({
         "metric": "MoE layer over a batch of positions: positions per second, layer par flux",
         "value": round(P / (ms["par_flux"] * 1e-3), 1), "unit": "positions/s", "n_gpus": 1, "steps": args.steps,
@@ -1310,10 +1333,18 @@ def bras_prefill(args):
         "data": "synthetic (seeded gpt-oss-120b-shaped MXFP4 experts, .trc v1.2 parts)",
         "config": {"workload": f"one gpt-oss-120b MoE layer, {P} positions, 128 experts, top-{args.k}",
                    "distinct_experts": int(len(np.unique(idx))), "l2": "flushed between replays"},
-        "fused_ms_per_step": round(ms["fusionnee"], 4),
-        "fused_positions_per_s": round(P / (ms["fusionnee"] * 1e-3), 1),
-        "speedup_vs_fused": round(ms["fusionnee"] / ms["par_flux"], 3),
-        "bit_identical_to_fused": egaux, "generation_s": round(t_gen, 1)}), flush=True)
+        "fused_ms_per_step": round(ms["fusionnee"], 4) if P <= 128 else None,
+        "fused_positions_per_s": round(P / (ms["fusionnee"] * 1e-3), 1) if P <= 128 else None,
+        "speedup_vs_fused": round(ms["fusionnee"] / ms["par_flux"], 3) if P <= 128 else None,
+        "bit_identical_to_fused": egaux if P <= 128 else None,
+        "tensor_cores": {"ms_per_step": round(ms_mma, 4), "positions_per_s": round(P / (ms_mma * 1e-3), 1),
+                         "speedup_vs_par_flux": round(ms["par_flux"] / ms_mma, 3),
+                         "experts_on_tensor_cores": int((comptes >= 16).sum()),
+                         "activations_on_tensor_cores": int(comptes[comptes >= 16].sum()),
+                         "max_rel_diff_vs_exact": ecart_mma,
+                         "note": "trc_moe_couche_par_flux_mma, experts with >= 16 activations as tcgen05 GEMMs "
+                                 "(x and h quantized to MXFP8); eager, router included, one wait for the routing"},
+        "generation_s": round(t_gen, 1)}), flush=True)
     del graphes
 
 

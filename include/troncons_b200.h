@@ -570,8 +570,25 @@ uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t ex
  * trc_moe_couche_fusionnee's on the same descriptor. Compressed parts (no brut) and no exchange;
  * an expert share (expert_debut / expert_fin: the other experts' activations left out) and
  * partiel (each position's share of the sum written alone) are those of the fused layer. The
- * controle of an activation receives its expert's decode counters. */
+ * controle of an activation receives its expert's decode counters. Up to 4,096 positions per
+ * call (the fused layer: 128). */
 int trc_moe_couche_par_flux(const trc_moe_couche* couche, void* espace, size_t espace_octets, void* flux);
+
+/* New: workspace bytes of trc_moe_couche_par_flux_mma (trc_moe_par_flux_espace_octets plus the
+ * GEMMs' quantized activations). */
+uint64_t trc_moe_par_flux_mma_espace_octets(const trc_dims_expert* dims, uint32_t experts, uint32_t activations,
+                                            uint32_t seuil);
+
+/* New: the layer par flux with every expert that receives at least `seuil` activations of the
+ * batch (16 and up is where it pays) multiplied on the tensor cores (trc_gemm_mxfp4's
+ * tcgen05 block-scaled GEMM over the expert's decoded slot, x and h quantized to MXFP8, the rows
+ * gathered and scattered through the expert's activation list); the other experts as
+ * trc_moe_couche_par_flux. Not bit-identical to it (about 3 % of the layer's output, the
+ * quantization); compressed parts only. The call waits on `flux` once, for the routing (read
+ * back to size the GEMMs): it cannot be captured in a CUDA graph. *erreur (device u32, zeroed by
+ * the caller) is set to 1 when a bounded wait of the GEMM kernel gave up. */
+int trc_moe_couche_par_flux_mma(const trc_moe_couche* couche, uint32_t seuil, void* espace, size_t espace_octets,
+                                uint32_t* erreur, void* flux);
 
 /* New: bytes of a layer's delta bytes decoded ahead (trc_moe_predecoder_deltas): one byte per
  * 32-block of each matrix and expert, 256-aligned per matrix (3 x 259,200 x 128 = 99.5 MB for a
@@ -667,7 +684,7 @@ int trc_moe_couche_chrono(const trc_moe_couche* couche, void* espace, size_t esp
  * in the area needs zeroing. Results and launches are those of trc_moe_couche_fusionnee. */
 int trc_moe_couche_sans_alloc(const trc_moe_couche* couche, void* flux);
 
-/* Router of the layer for `jetons` tokens (x [jetons][colonnes], bf16 or f32): logits = Wr x + br
+/* Router of the layer for `jetons` tokens (1 to 4,096; x [jetons][colonnes], bf16 or f32): logits = Wr x + br
  * (f32 weights [experts][colonnes]), then top-k and f64 softmax as trc_routeur_topk, token by
  * token: logits f32[jetons][experts], indices u32[jetons][k], poids f32[jetons][k]. Two launches
  * whatever the number of tokens. */

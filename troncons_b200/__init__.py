@@ -158,6 +158,8 @@ def _charger() -> C.CDLL:
         "trc_moe_espace_recouvrant_octets": (u64, [pd, u32]),
         "trc_moe_par_flux_espace_octets": (u64, [pd, u32, u32]),
         "trc_moe_couche_par_flux": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
+        "trc_moe_par_flux_mma_espace_octets": (u64, [pd, u32, u32, u32]),
+        "trc_moe_couche_par_flux_mma": (i32, [C.POINTER(MoeCouche), u32, vp, sz, vp, vp]),
         "trc_moe_couche_fusionnee": (i32, [C.POINTER(MoeCouche), vp, sz, vp]),
         "trc_moe_couche_chrono": (i32, [C.POINTER(MoeCouche), vp, sz, vp, C.POINTER(vp)]),
         "trc_moe_couche_sans_alloc": (i32, [C.POINTER(MoeCouche), vp]),

@@ -172,22 +172,35 @@ class CoucheCarte:
         verifier(lib.trc_moe_couche_ep(C.byref(self._desc), e.data_ptr(), e.numel(), C.c_void_p(comm), f))
 
     def couche_par_flux(self, x: torch.Tensor, residu: torch.Tensor, flux=None, routeur: bool = True,
-                        partiel: bool = False):
+                        partiel: bool = False, mma_seuil: int = 0):
         """Router then the layer "par flux" (trc_moe_couche_par_flux): each distinct routed expert
         decoded once for the batch; the residuals are the fused layer's bits (also on the share
-        `tenus`, and with `partiel`: the share's sum written alone)."""
+        `tenus`, and with `partiel`: the share's sum written alone). `mma_seuil` > 0: the experts
+        with at least that many activations on the tensor cores (trc_moe_couche_par_flux_mma;
+        within the quantization's tolerance, one wait on the stream for the routing)."""
         from . import lib, verifier
 
         if routeur:
             self.routeur(x, flux)
-        if getattr(self, "_espace_pf", None) is None:
-            n = int(lib.trc_moe_par_flux_espace_octets(C.byref(self.dims), self.c.experts, self.jetons * self.k))
+        cle = ("_espace_pf", mma_seuil)
+        if getattr(self, "_cle_pf", None) != cle:
+            if mma_seuil:
+                n = int(lib.trc_moe_par_flux_mma_espace_octets(C.byref(self.dims), self.c.experts, self.jetons * self.k,
+                                                                mma_seuil))
+            else:
+                n = int(lib.trc_moe_par_flux_espace_octets(C.byref(self.dims), self.c.experts, self.jetons * self.k))
             self._espace_pf = torch.empty(n + 256, dtype=torch.uint8, device=self.dev)
             self._n_pf = n
+            self._cle_pf = cle
+            self.erreur_pf = torch.zeros(1, dtype=torch.int32, device=self.dev)
         e = self._espace_pf.data_ptr() + (-self._espace_pf.data_ptr()) % 256
         self._desc_pf = self.descripteur(x, residu, False, partiel)
         f = (flux or torch.cuda.current_stream()).cuda_stream
-        verifier(lib.trc_moe_couche_par_flux(C.byref(self._desc_pf), e, self._n_pf, f))
+        if mma_seuil:
+            verifier(lib.trc_moe_couche_par_flux_mma(C.byref(self._desc_pf), mma_seuil, e, self._n_pf,
+                                                     self.erreur_pf.data_ptr(), f))
+        else:
+            verifier(lib.trc_moe_couche_par_flux(C.byref(self._desc_pf), e, self._n_pf, f))
 
     # ---------------------------------------------------------------- decode-then-multiply
 

@@ -308,13 +308,16 @@ uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32
 namespace {
 
 // The descriptor's checks (Noyaux's usage rules for the layer's launches) and its translation.
-int couche_de(const trc_moe_couche* c, tb::Couche& k) {
+// Tokens per call: 128 for the fused layer; a batch of positions par flux takes up to 4,096.
+constexpr uint32_t JETONS_MAX = 128, JETONS_MAX_PAR_FLUX = 4096;
+
+int couche_de(const trc_moe_couche* c, tb::Couche& k, uint32_t jetons_max = JETONS_MAX) {
     if (c == nullptr) return usage("layer descriptor absent");
     if (int s = verifier_dims(&c->dims)) return s;
     const trc_dims_expert& d = c->dims;
     if (c->k == 0 || c->k > 8 || c->k > c->experts) return usage("k = %u of %u experts", c->k, c->experts);
     const uint32_t jetons = c->jetons ? c->jetons : 1u;
-    if (jetons > 128) return usage("%u tokens (128 at most)", jetons);
+    if (jetons > jetons_max) return usage("%u tokens (%u at most)", jetons, jetons_max);
     if (c->expert_fin != 0 && (c->expert_debut >= c->expert_fin || c->expert_fin > c->experts))
         return usage("held experts [%u, %u) of %u", c->expert_debut, c->expert_fin, c->experts);
     if (d.lignes[0] != d.lignes[1] || d.colonnes[0] != d.colonnes[1] || d.colonnes[2] != d.lignes[0] ||
@@ -497,7 +500,8 @@ uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t ex
 
 int trc_moe_couche_par_flux(const trc_moe_couche* c, void* espace, size_t espace_octets, void* flux) {
     tb::Couche k;
-    if (const int r = couche_de(c, k)) return r;
+    if (const int r = couche_de(c, k, JETONS_MAX_PAR_FLUX)) return r;
+    if (k.experts > 1024) return usage("par flux: %u experts (1,024 at most)", k.experts);
     if (k.brut || k.ech.monde != 0)
         return usage("par flux: compressed parts only, and no exchange (an expert share with partiel is accepted)");
     const uint64_t besoin = tb::plan_par_flux(k.lignes, k.colonnes, k.experts, k.k * k.jetons).total;
@@ -505,6 +509,31 @@ int trc_moe_couche_par_flux(const trc_moe_couche* c, void* espace, size_t espace
         return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
     SUR_LE_FLUX(flux);
     return statut(tb::lancer_par_flux(k, espace, static_cast<cudaStream_t>(flux)));
+}
+
+uint64_t trc_moe_par_flux_mma_espace_octets(const trc_dims_expert* dims, uint32_t experts, uint32_t activations,
+                                            uint32_t seuil) {
+    if (dims == nullptr || experts == 0 || activations == 0 || seuil == 0) return 0;
+    return tb::par_flux_mma_octets(dims->lignes, dims->colonnes, experts, activations, seuil);
+}
+
+int trc_moe_couche_par_flux_mma(const trc_moe_couche* c, uint32_t seuil, void* espace, size_t espace_octets,
+                                uint32_t* erreur, void* flux) {
+    tb::Couche k;
+    if (const int r = couche_de(c, k, JETONS_MAX_PAR_FLUX)) return r;
+    if (k.experts > 1024) return usage("par flux: %u experts (1,024 at most)", k.experts);
+    if (k.brut || k.ech.monde != 0)
+        return usage("par flux: compressed parts only, and no exchange (an expert share with partiel is accepted)");
+    if (seuil == 0) return usage("par flux on the tensor cores: threshold 0 (at least 1 activation per expert)");
+    if (erreur == nullptr) return usage("par flux on the tensor cores: error word absent");
+    for (int j = 0; j < 3; ++j)
+        if (!tb::gemm_mxfp4_possible(k.colonnes[j], 256))
+            return usage("par flux on the tensor cores: matrix %d's %u columns exceed shared memory", j, k.colonnes[j]);
+    const uint64_t besoin = tb::par_flux_mma_octets(k.lignes, k.colonnes, k.experts, k.k * k.jetons, seuil);
+    if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
+        return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
+    SUR_LE_FLUX(flux);
+    return statut(tb::lancer_par_flux_mma(k, espace, seuil, erreur, static_cast<cudaStream_t>(flux)));
 }
 
 // ---------------------------------------------------------------- attention side (lib.rs:291-381)
@@ -584,7 +613,7 @@ int trc_attention(const float* q, size_t q_octets, const uint16_t* cache_k, size
 int trc_routeur(const float* wr, const float* br, const void* x, uint32_t x_bf16, uint32_t experts, uint32_t colonnes,
                 uint32_t k, uint32_t jetons, float* logits, uint32_t* indices, float* poids, void* flux) {
     if (experts == 0 || experts > 256 || k == 0 || k > 8 || k > experts) return usage("top-%u of %u", k, experts);
-    if (jetons == 0 || jetons > 128) return usage("%u tokens (1 to 128)", jetons);
+    if (jetons == 0 || jetons > JETONS_MAX_PAR_FLUX) return usage("%u tokens (1 to %u)", jetons, JETONS_MAX_PAR_FLUX);
     if (colonnes == 0 || colonnes % 4 != 0) return usage("%u columns (a multiple of 4)", colonnes);
     if (wr == nullptr || !aligne(wr, 16) || x == nullptr || !aligne(x, x_bf16 ? 8 : 16) || logits == nullptr ||
         indices == nullptr || poids == nullptr)

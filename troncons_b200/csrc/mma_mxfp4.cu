@@ -196,6 +196,7 @@ struct LotMma {
     CUtensorMap ta[LOT_MAX];   // A: 4-bit unpacking, (128, full chunks, rows)
     CUtensorMap tb[LOT_MAX];   // B: bytes, (columns, tokens)
     DescGemm d[LOT_MAX];
+    RenvoiGemm r[LOT_MAX];     // token n's x row and y row (gathered / scattered), or n and n
     uint8_t* espace;
     uint32_t* erreur;
     uint64_t tranche;
@@ -433,7 +434,10 @@ __global__ void __launch_bounds__(MMA_FILS, 3) k_gemm_mxfp4(const __grid_constan
             asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
             if (r < R)
                 for (uint32_t j = 0; j < 8u; ++j)
-                    if (n0 + j < N) y[uint64_t(n0 + j) * R + r] = __uint_as_float(v[j]) + bias;
+                    if (n0 + j < N) {
+                        const uint32_t ligne = lot.r[m].iy != nullptr ? lot.r[m].iy[n0 + j] : n0 + j;  // the token's y row
+                        y[uint64_t(ligne) * R + r] = __uint_as_float(v[j]) + bias;
+                    }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
@@ -461,7 +465,9 @@ __global__ void __launch_bounds__(256) k_quantifier_mxfp8(const __grid_constant_
     const uint32_t w = blockIdx.x * 8u + (threadIdx.x >> 5), voie = threadIdx.x & 31u;
     if (w >= N * B) return;
     const uint32_t n = w / B, b = w % B;
-    const uint64_t i = uint64_t(n) * C + 32u * b + voie;
+    const RenvoiGemm& rv = lot.r[blockIdx.y];
+    const uint32_t ligne = rv.ix != nullptr ? rv.ix[n] / rv.div_x : n;  // the token's x row
+    const uint64_t i = uint64_t(ligne) * C + 32u * b + voie;
     const float v = bf16 ? __uint_as_float(uint32_t(static_cast<const uint16_t*>(x)[i]) << 16) : static_cast<const float*>(x)[i];
     float mx = fabsf(v);
 #pragma unroll
@@ -547,7 +553,8 @@ bool carte_b(CUtensorMap* t, const uint8_t* xq, uint32_t C, uint32_t N) {
 // colonnes_max, n_max): per group of up to LOT_MAX matrices, one launch quantizes every x into
 // its workspace slice, one launch runs every matrix's row tiles (grid y = the matrix).
 cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
-                                  uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux) {
+                                  uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux,
+                                  const RenvoiGemm* renvois) {
     const uint64_t tranche = (gemm_mxfp4_espace(colonnes_max, n_max) + 255u) & ~uint64_t(255);
     const uint32_t E = mma_etages(n_max, colonnes_max), smem = mma_smem(n_max, colonnes_max, E);
     cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_gemm_mxfp4), int(smem));
@@ -564,6 +571,7 @@ cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t l
         for (uint32_t i = 0; i < lot->nb; ++i) {
             const DescGemm& d = descs[p + i];
             lot->d[i] = d;
+            lot->r[i] = renvois != nullptr ? renvois[p + i] : RenvoiGemm{nullptr, nullptr, 1u};
             const uint8_t* xq = espace + uint64_t(p + i) * tranche;
             if (carte_a(&lot->ta[i], d)) lot->tma_a |= uint64_t(1) << i;
             if (carte_b(&lot->tb[i], xq, d.colonnes, d.n)) lot->tma_b |= uint64_t(1) << i;

@@ -90,6 +90,11 @@ struct EspaceParFlux {
 };
 EspaceParFlux plan_par_flux(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts, uint32_t na);
 cudaError_t lancer_par_flux(const Couche& c, void* espace, cudaStream_t flux);
+// The same with the experts that have at least `seuil` activations multiplied on the tensor
+// cores (mma_mxfp4.cu); waits for the routing on the host.
+uint64_t par_flux_mma_octets(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts, uint32_t na,
+                             uint32_t seuil);
+cudaError_t lancer_par_flux_mma(const Couche& c, void* espace, uint32_t seuil, uint32_t* erreur, cudaStream_t flux);
 
 // Activations up to which the down projection's decode may overlap gate/up (its codes then go
 // through the workspace: 4.15 MB per activation for gpt-oss; measured faster than the
@@ -120,8 +125,15 @@ struct DescGemm {
 uint64_t gemm_mxfp4_espace(uint32_t C, uint32_t N);
 bool gemm_mxfp4_possible(uint32_t C, uint32_t N);  // the staged tiles and scales fit shared memory
 uint64_t gemm_mxfp4_lot_espace(uint32_t colonnes_max, uint32_t n_max, uint32_t nb);
+// Token n of a GEMM reads x row ix[n] / div_x and writes y row iy[n] (each list null: row n).
+struct RenvoiGemm {
+    const uint32_t* ix;
+    const uint32_t* iy;
+    uint32_t div_x;
+};
 cudaError_t lancer_gemm_mxfp4_lot(const DescGemm* descs, uint32_t nb, uint32_t lignes_max, uint32_t colonnes_max,
-                                  uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux);
+                                  uint32_t n_max, uint8_t* espace, uint32_t* erreur, cudaStream_t flux,
+                                  const RenvoiGemm* renvois = nullptr);
 cudaError_t lancer_gemm_mxfp4(const uint8_t* codes, const uint8_t* ech, const float* biais, const void* x, uint32_t x_bf16,
                               float* y, uint32_t R, uint32_t C, uint32_t N, uint8_t* espace, uint32_t* erreur,
                               cudaStream_t flux);

@@ -17,6 +17,9 @@
 // batch: the decode work no longer grows with the positions.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "commun.cuh"
 #include "mxfp4.cuh"
 #include "noyaux.h"
@@ -72,6 +75,8 @@ struct ArgsParFlux {
     uint8_t* espace;
     EspaceParFlux p;
     uint32_t j0;
+    uint32_t seuil;          // > 0: the experts with at least this many activations are left to the tensor cores
+    const uint32_t* petits;  // with seuil: the distinct experts below it (grid z indexes this list)
 };
 
 template <typename T>
@@ -80,7 +85,7 @@ __device__ __forceinline__ T* zone(const ArgsParFlux& a, uint64_t off) {
 }
 
 // One block: counts per expert, the distinct experts in ascending order, their lists of
-// activations (stable: by activation index), the decode descriptors (empty past the last).
+// activations (in any order), the decode descriptors (empty past the last).
 // Expert e is held on this device: every expert, or those of the share [expert_debut, expert_fin)
 // (the fused layer's rule for an expert-parallel share).
 __device__ __forceinline__ bool tient(const Couche& c, uint32_t e) {
@@ -146,13 +151,16 @@ __global__ void __launch_bounds__(1024) k_grouper(ArgsParFlux a) {
         debut[nu] = base_a;
     }
     __syncthreads();
-    // each activation's place in its expert's list: the activations before it with the same expert
+    // each activation's place in its expert's list, by a counter per distinct expert (the order
+    // within a list is free: every activation's arithmetic is its own, whatever its neighbours)
+    uint32_t* rempli = part;  // reused (the scans are done): U <= experts <= 1,024, refused above by the ABI
+    rempli[tid] = 0;
+    __syncthreads();
     for (uint32_t i = tid; i < na; i += 1024u) {
         const uint32_t e = c.indices[i];
         if (e >= E || !tient(c, e)) continue;
-        uint32_t rang = 0;
-        for (uint32_t i2 = 0; i2 < i; ++i2) rang += c.indices[i2] == e ? 1u : 0u;
-        liste[debut[cpt[e]] + rang] = i;
+        const uint32_t u = cpt[e];
+        liste[debut[u] + atomicAdd(&rempli[u], 1u)] = i;
     }
     DescDecodage* descs = zone<DescDecodage>(a, a.p.descs);
     for (uint32_t u = tid; u < U; u += 1024u) {
@@ -189,7 +197,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 2) k_gemv_flux(ArgsParFlux a) {
     attendre_amont();
     liberer_aval();
     const Couche& c = a.c;
-    const uint32_t u = blockIdx.z;
+    const uint32_t u = a.petits != nullptr ? a.petits[blockIdx.z] : blockIdx.z;
     if (u >= *zone<uint32_t>(a, a.p.nu)) return;
     const uint32_t j = a.j0 + blockIdx.y, voie = threadIdx.x & 31u, q = voie & 3u, g = voie >> 2;
     const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u;
@@ -203,6 +211,7 @@ __global__ void __launch_bounds__(PF_WARPS * 32, 2) k_gemv_flux(ArgsParFlux a) {
     const uint8_t* ech = mat + disp.echelles;
     const float* biais = reinterpret_cast<const float*>(mat + disp.biais);
     const uint32_t d0 = zone<uint32_t>(a, a.p.debut)[u], n_act = zone<uint32_t>(a, a.p.debut)[u + 1] - d0;
+    if (a.seuil != 0u && n_act >= a.seuil) return;  // this expert's activations go through the tensor cores
     const uint32_t* liste = zone<uint32_t>(a, a.p.liste) + d0;
     float* sortie = zone<float>(a, j == 0 ? a.p.g : j == 1 ? a.p.u : a.p.y);
     const uint32_t V = pf_vecteurs(C), oct = x2_octets(C);
@@ -331,7 +340,7 @@ __global__ void __launch_bounds__(256) k_combiner_flux(ArgsParFlux a) {
 
 cudaError_t lancer_par_flux(const Couche& c, void* espace, cudaStream_t flux) {
     const uint32_t na = c.jetons * c.k;
-    ArgsParFlux a{c, static_cast<uint8_t*>(espace), plan_par_flux(c.lignes, c.colonnes, c.experts, na), 0};
+    ArgsParFlux a{c, static_cast<uint8_t*>(espace), plan_par_flux(c.lignes, c.colonnes, c.experts, na), 0, 0, nullptr};
     cudaError_t e;
     if ((e = lancer_pdl(k_grouper, dim3(1), dim3(1024), 0, flux, a)) != cudaSuccess) return e;
     Dims dims;
@@ -362,6 +371,116 @@ cudaError_t lancer_par_flux(const Couche& c, void* espace, cudaStream_t flux) {
     a.j0 = 2;
     if ((e = lancer_pdl(k_gemv_flux, dim3(grille(c.lignes[2], a.p.U), 1, a.p.U), dim3(PF_WARPS * 32), smem, flux, a)) !=
         cudaSuccess)
+        return e;
+    return lancer_pdl(k_combiner_flux, dim3((c.lignes[2] + 255) / 256, c.jetons), dim3(256), 0, flux, a);
+}
+
+// ------------------------------------------------------------------ with the tensor cores
+
+// Descriptors of one GEMM per (big expert, group of up to 256 of its activations) and matrix.
+constexpr uint32_t PF_MMA_N = 256;
+
+// The GEMMs' descriptors (at most this many per matrix group) for na activations and a threshold.
+static uint32_t pf_mma_max(uint32_t na, uint32_t seuil) { return na / seuil + na / PF_MMA_N + 1u; }
+
+uint64_t par_flux_mma_octets(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_t experts, uint32_t na,
+                             uint32_t seuil) {
+    const EspaceParFlux p = plan_par_flux(lignes, colonnes, experts, na);
+    const uint32_t cmax = std::max(std::max(colonnes[0], colonnes[1]), colonnes[2]);
+    return p.total + al256(4ull * p.U) + gemm_mxfp4_lot_espace(cmax, PF_MMA_N, 2u * pf_mma_max(na, seuil));
+}
+
+// The layer par flux with the experts that have at least `seuil` activations (>= 1) multiplied
+// on the tensor cores: gate and up of their activations as GEMMs over the expert's decoded slot
+// (x rows gathered through the expert's activation list: token = activation / k), SwiGLU for
+// every activation, down as GEMMs (h rows of the activations), the outputs scattered to the
+// activations' rows; the other experts through k_gemv_flux as in lancer_par_flux. The routing is
+// read back on the host (one wait on the stream) to size the GEMMs. Not bit-identical to the
+// GEMV (the GEMM quantizes x and h to MXFP8); `erreur` (device u32) is set when a bounded wait of
+// the GEMM kernel gave up.
+cudaError_t lancer_par_flux_mma(const Couche& c, void* espace, uint32_t seuil, uint32_t* erreur, cudaStream_t flux) {
+    const uint32_t na = c.jetons * c.k;
+    ArgsParFlux a{c, static_cast<uint8_t*>(espace), plan_par_flux(c.lignes, c.colonnes, c.experts, na), 0, seuil, nullptr};
+    cudaError_t e;
+    if ((e = lancer_pdl(k_grouper, dim3(1), dim3(1024), 0, flux, a)) != cudaSuccess) return e;
+    Dims dims;
+    for (int j = 0; j < 3; ++j) {
+        dims.lignes[j] = c.lignes[j];
+        dims.colonnes[j] = c.colonnes[j];
+    }
+    if ((e = lancer_decodage(reinterpret_cast<const DescDecodage*>(a.espace + a.p.descs), a.p.U, nullptr, 0, nullptr,
+                             c.luts, dims, nullptr, flux)) != cudaSuccess)
+        return e;
+    // the groups, on the host
+    const uint32_t U = a.p.U;
+    uint32_t nu = 0;
+    std::vector<uint32_t> debut(U + 1u);
+    if ((e = cudaMemcpyAsync(&nu, a.espace + a.p.nu, 4, cudaMemcpyDeviceToHost, flux)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(debut.data(), a.espace + a.p.debut, 4ull * (U + 1u), cudaMemcpyDeviceToHost, flux)) !=
+            cudaSuccess ||
+        (e = cudaStreamSynchronize(flux)) != cudaSuccess)
+        return e;
+    nu = std::min(nu, U);
+    std::vector<DescGemm> dg[2];
+    std::vector<RenvoiGemm> rg[2];
+    std::vector<uint32_t> petits;  // the experts below the threshold: the GEMV's grid covers them alone
+    uint32_t n_max = 1;
+    for (uint32_t u = 0; u < nu; ++u) {
+        const uint32_t d0 = debut[u], n = debut[u + 1] - d0;
+        if (n < seuil) {
+            petits.push_back(u);
+            continue;
+        }
+        const uint8_t* slot = a.espace + a.p.slots + a.p.taille_slot * u;
+        for (uint32_t g0 = 0; g0 < n; g0 += PF_MMA_N) {
+            const uint32_t ng = std::min(PF_MMA_N, n - g0);
+            n_max = std::max(n_max, ng);
+            const uint32_t* liste = reinterpret_cast<const uint32_t*>(a.espace + a.p.liste) + d0 + g0;
+            for (uint32_t j = 0; j < 3; ++j) {
+                const Disposition dp = disposition(dims, j);
+                const uint8_t* mat = slot + dp.base;
+                const uint64_t x = j < 2 ? reinterpret_cast<uint64_t>(c.x) : reinterpret_cast<uint64_t>(a.espace + a.p.h);
+                const uint64_t y = reinterpret_cast<uint64_t>(a.espace + (j == 0 ? a.p.g : j == 1 ? a.p.u : a.p.y));
+                DescGemm d{reinterpret_cast<uint64_t>(mat), reinterpret_cast<uint64_t>(mat + dp.echelles),
+                           reinterpret_cast<uint64_t>(mat + dp.biais), x, y, c.lignes[j], c.colonnes[j], ng,
+                           j < 2 ? c.x_bf16 : 0u};
+                dg[j < 2 ? 0 : 1].push_back(d);
+                rg[j < 2 ? 0 : 1].push_back(RenvoiGemm{liste, liste, j < 2 ? c.k : 1u});
+            }
+        }
+    }
+    uint32_t* petits_d = reinterpret_cast<uint32_t*>(a.espace + a.p.total);
+    uint8_t* eg = a.espace + a.p.total + al256(4ull * U);  // the GEMMs' workspace (quantized activations)
+    if (!petits.empty() && (e = cudaMemcpyAsync(petits_d, petits.data(), 4ull * petits.size(), cudaMemcpyHostToDevice,
+                                                flux)) != cudaSuccess)
+        return e;
+    a.petits = petits_d;
+    const uint32_t np = uint32_t(petits.size());
+    const uint32_t rmax = std::max(c.lignes[0], c.lignes[2]), cmax = std::max(c.colonnes[0], c.colonnes[2]);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto grille = [&](uint32_t R, uint32_t plans) {
+        const uint32_t vague = (uint32_t(sms) * 4u + plans - 1u) / plans;
+        return std::max(1u, std::min((R + PF_WARPS - 1) / PF_WARPS, vague));
+    };
+    const size_t smem = size_t(pf_vecteurs(cmax)) * x2_octets(cmax);
+    if ((e = assurer_smem(reinterpret_cast<const void*>(k_gemv_flux), int(smem))) != cudaSuccess) return e;
+    if (np != 0 &&
+        (e = lancer_pdl(k_gemv_flux, dim3(grille(c.lignes[0], 2u * np), 2, np), dim3(PF_WARPS * 32), smem, flux, a)) !=
+            cudaSuccess)
+        return e;
+    if (!dg[0].empty() && (e = lancer_gemm_mxfp4_lot(dg[0].data(), uint32_t(dg[0].size()), rmax, cmax, n_max, eg, erreur,
+                                                      flux, rg[0].data())) != cudaSuccess)
+        return e;
+    if ((e = lancer_swiglu(reinterpret_cast<const float*>(a.espace + a.p.g), reinterpret_cast<const float*>(a.espace + a.p.u),
+                           reinterpret_cast<float*>(a.espace + a.p.h), na * c.lignes[0], flux)) != cudaSuccess)
+        return e;
+    a.j0 = 2;
+    if (np != 0 &&
+        (e = lancer_pdl(k_gemv_flux, dim3(grille(c.lignes[2], np), 1, np), dim3(PF_WARPS * 32), smem, flux, a)) != cudaSuccess)
+        return e;
+    if (!dg[1].empty() && (e = lancer_gemm_mxfp4_lot(dg[1].data(), uint32_t(dg[1].size()), rmax, cmax, n_max, eg, erreur,
+                                                      flux, rg[1].data())) != cudaSuccess)
         return e;
     return lancer_pdl(k_combiner_flux, dim3((c.lignes[2] + 255) / 256, c.jetons), dim3(256), 0, flux, a);
 }
