@@ -567,7 +567,8 @@ uint64_t trc_moe_par_flux_espace_octets(const trc_dims_expert* dims, uint32_t ex
  * trc-modele/src/lib.rs:607-717, trc-ordo/src/lib.rs:782-981): each distinct routed expert is
  * decoded once for the whole batch into a slot of the workspace, then applied to every position
  * routed to it with the token-by-token arithmetic, so the residuals are bit-identical to
- * trc_moe_couche_fusionnee's on the same descriptor. Compressed parts (no brut) and no exchange;
+ * trc_moe_couche_fusionnee's on the same descriptor. Compressed parts, or raw parts (brut: each
+ * distinct expert's streams copied into its slot, the same bits); no exchange;
  * an expert share (expert_debut / expert_fin: the other experts' activations left out) and
  * partiel (each position's share of the sum written alone) are those of the fused layer. The
  * controle of an activation receives its expert's decode counters. Up to 4,096 positions per
@@ -584,8 +585,9 @@ uint64_t trc_moe_par_flux_mma_espace_octets(const trc_dims_expert* dims, uint32_
  * tcgen05 block-scaled GEMM over the expert's decoded slot, x and h quantized to MXFP8, the rows
  * gathered and scattered through the expert's activation list); the other experts as
  * trc_moe_couche_par_flux. Not bit-identical to it (about 3 % of the layer's output, the
- * quantization); compressed parts only. The call waits on `flux` once, for the routing (read
- * back to size the GEMMs): it cannot be captured in a CUDA graph. *erreur (device u32, zeroed by
+ * quantization). The call waits on `flux` once, for the routing (read
+ * back to size the GEMMs): it cannot be captured in a CUDA graph. Raw parts as in
+ * trc_moe_couche_par_flux. *erreur (device u32, zeroed by
  * the caller) is set to 1 when a bounded wait of the GEMM kernel gave up. */
 int trc_moe_couche_par_flux_mma(const trc_moe_couche* couche, uint32_t seuil, void* espace, size_t espace_octets,
                                 uint32_t* erreur, void* flux);

@@ -94,7 +94,17 @@ def _port_libre() -> int:
     return p
 
 
+def _journal(rang, t0, *quoi):
+    """A rank's progress on stderr (shown by pytest when a rank fails or times out)."""
+    import sys
+    import time
+
+    print(f"[{time.time() - t0:7.2f} s] rank {rang}:", *quoi, file=sys.stderr, flush=True)
+
+
 def _rang(rang, monde, port, echange, moe):
+    import time
+
     import torch.distributed as dist
 
     import troncons_b200.modele as M
@@ -105,9 +115,12 @@ def _rang(rang, monde, port, echange, moe):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rang, world_size=monde,
                             timeout=timedelta(seconds=60), device_id=dev)
+    t0 = time.time()
     try:
         ep = ModeleEP(rang, monde, echange=echange, moe=moe, **FORME)
+        _journal(rang, t0, "expert-parallel model built")
         seul = M.Modele(**FORME)
+        _journal(rang, t0, "one-GPU model built")
         # the share's parts are the whole model's, byte for byte
         for l in range(FORME["couches"]):
             tp, adr, tailles = ep.m.parties["compresse"][l]
@@ -122,7 +135,9 @@ def _rang(rang, monde, port, echange, moe):
             ep.choisir(actifs)
             seul.choisir(actifs)
             a = _suite(ep.pas, ep.m.vues, jetons)
+            _journal(rang, t0, actifs, "expert-parallel steps done")
             b = _suite(seul.pas, seul.vues, jetons)
+            _journal(rang, t0, actifs, "one-GPU steps done")
             for t, ((za, ja), (zb, jb)) in enumerate(zip(a, b)):
                 assert np.abs(za - zb).max() <= 1e-5 * np.abs(zb).max(), f"rank {rang} {actifs} step {t}"
                 assert ja == jb, f"rank {rang} {actifs} step {t}"
@@ -130,6 +145,7 @@ def _rang(rang, monde, port, echange, moe):
         # two sequences per rank: a batch of 4 tokens over 2 GPUs
         del ep
         ep = ModeleEP(rang, monde, echange=echange, par_rang=2, moe=moe, **FORME)
+        _journal(rang, t0, "two sequences per rank: model built")
         ep.choisir("compresse")
         seul.choisir("compresse")
         jetons = np.random.default_rng(200 + rang).integers(0, 512, (2, 16))
@@ -146,6 +162,7 @@ def _rang(rang, monde, port, echange, moe):
             for t in range(16):
                 assert np.abs(z[i][t] - b[t][0]).max() <= 1e-5 * np.abs(b[t][0]).max(), f"rank {rang} seq {i} step {t}"
         assert (ep.controle == 0).all()
+        _journal(rang, t0, "done, final barrier")
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -151,3 +151,24 @@ def test_par_flux_mma_dans_la_tolerance(couche_gpt_oss, jetons, seuil):
         n_par_expert = np.bincount(cc.idx.cpu().numpy(), minlength=c.experts)
         if seuil == 28:
             assert (n_par_expert >= 28).any() and ((n_par_expert > 0) & (n_par_expert < 28)).any(), n_par_expert
+
+
+@pytest.mark.parametrize("nom,jetons,seuil", [("couche_petite", 9, 0), ("couche_gpt_oss", 16, 0), ("couche_gpt_oss", 48, 16)])
+def test_par_flux_brut_egal_compresse(nom, jetons, seuil, request):
+    """The layer par flux on raw parts (each distinct expert's streams copied into its slot)
+    gives the compressed parts' residual bits, on the exact path and on the tensor cores."""
+    from troncons_b200.carte import CoucheCarte
+
+    c = request.getfixturevalue(nom)
+    cc = CoucheCarte(c, k=4, brut=True, jetons=jetons)
+    rng = np.random.default_rng(jetons + 3)
+    d = c.dims.colonnes[0]
+    x = torch.from_numpy(rng.standard_normal((jetons, d)).astype(np.float32)).to(torch.bfloat16).cuda()
+    r0 = torch.from_numpy(rng.standard_normal((jetons, c.dims.lignes[2])).astype(np.float32)).cuda()
+    rc, rb = r0.clone(), r0.clone()
+    cc.controle.zero_()
+    cc.couche_par_flux(x, rc, mma_seuil=seuil)
+    cc.couche_par_flux(x, rb, routeur=False, mma_seuil=seuil, brute=True)
+    torch.cuda.synchronize()
+    assert (cc.controle == 0).all()
+    assert torch.equal(rc.view(torch.int32), rb.view(torch.int32))

@@ -172,7 +172,7 @@ class CoucheCarte:
         verifier(lib.trc_moe_couche_ep(C.byref(self._desc), e.data_ptr(), e.numel(), C.c_void_p(comm), f))
 
     def couche_par_flux(self, x: torch.Tensor, residu: torch.Tensor, flux=None, routeur: bool = True,
-                        partiel: bool = False, mma_seuil: int = 0):
+                        partiel: bool = False, mma_seuil: int = 0, brute: bool = False):
         """Router then the layer "par flux" (trc_moe_couche_par_flux): each distinct routed expert
         decoded once for the batch; the residuals are the fused layer's bits (also on the share
         `tenus`, and with `partiel`: the share's sum written alone). `mma_seuil` > 0: the experts
@@ -194,7 +194,7 @@ class CoucheCarte:
             self._cle_pf = cle
             self.erreur_pf = torch.zeros(1, dtype=torch.int32, device=self.dev)
         e = self._espace_pf.data_ptr() + (-self._espace_pf.data_ptr()) % 256
-        self._desc_pf = self.descripteur(x, residu, False, partiel)
+        self._desc_pf = self.descripteur(x, residu, brute, partiel)
         f = (flux or torch.cuda.current_stream()).cuda_stream
         if mma_seuil:
             verifier(lib.trc_moe_couche_par_flux_mma(C.byref(self._desc_pf), mma_seuil, e, self._n_pf,

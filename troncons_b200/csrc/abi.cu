@@ -381,7 +381,7 @@ uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k) {
 uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t k) {
     if (dims == nullptr || k == 0) return 0;
     const tb::Espace e = tb::plan_espace(dims->lignes, dims->colonnes, k);
-    return k <= tb::RECOUVRE_MAX ? e.total_recouvrant : e.total;
+    return k <= tb::RECOUVRE_MAX ? e.total_tout : e.total;
 }
 
 uint64_t trc_gemm_mxfp4_espace_octets(uint32_t colonnes, uint32_t n) {
@@ -502,8 +502,7 @@ int trc_moe_couche_par_flux(const trc_moe_couche* c, void* espace, size_t espace
     tb::Couche k;
     if (const int r = couche_de(c, k, JETONS_MAX_PAR_FLUX)) return r;
     if (k.experts > 1024) return usage("par flux: %u experts (1,024 at most)", k.experts);
-    if (k.brut || k.ech.monde != 0)
-        return usage("par flux: compressed parts only, and no exchange (an expert share with partiel is accepted)");
+    if (k.ech.monde != 0) return usage("par flux: no exchange (an expert share with partiel is accepted)");
     const uint64_t besoin = tb::plan_par_flux(k.lignes, k.colonnes, k.experts, k.k * k.jetons).total;
     if (espace == nullptr || espace_octets < besoin || !aligne(espace, 256))
         return usage("workspace of %zu bytes, %llu needed (256-aligned)", espace_octets, (unsigned long long)besoin);
@@ -522,8 +521,7 @@ int trc_moe_couche_par_flux_mma(const trc_moe_couche* c, uint32_t seuil, void* e
     tb::Couche k;
     if (const int r = couche_de(c, k, JETONS_MAX_PAR_FLUX)) return r;
     if (k.experts > 1024) return usage("par flux: %u experts (1,024 at most)", k.experts);
-    if (k.brut || k.ech.monde != 0)
-        return usage("par flux: compressed parts only, and no exchange (an expert share with partiel is accepted)");
+    if (k.ech.monde != 0) return usage("par flux: no exchange (an expert share with partiel is accepted)");
     if (seuil == 0) return usage("par flux on the tensor cores: threshold 0 (at least 1 activation per expert)");
     if (erreur == nullptr) return usage("par flux on the tensor cores: error word absent");
     for (int j = 0; j < 3; ++j)

@@ -473,6 +473,38 @@ __device__ __forceinline__ void verser_controle(uint32_t* controle, uint32_t voi
     }
 }
 
+// Matrix j of a raw part (ECHELLES_BRUTES, CODES_BRUTS, BIAIS) into its place in an SoA slot
+// (grid-stride over the block's threads and gridDim.x); a missing or short stream counts a
+// format error in controle[CTL_FORMAT] (block x 0).
+__device__ inline void copier_brut_matrice(const uint8_t* partie, uint64_t taille, uint8_t* emplacement, const Dims& dims,
+                                           uint32_t j, uint32_t* controle) {
+    const uint32_t R = choisir(dims.lignes, j), C = choisir(dims.colonnes, j);
+    const uint32_t B = C / 32u, nblocs = R * B;
+    Flux fe, fc, fb;
+    const bool bon = B > 0 && R > 0 && trouver_flux_warp(partie, taille, SORTE_ECHELLES_BRUTES, j, fe) &&
+                     trouver_flux_warp(partie, taille, SORTE_CODES_BRUTS, j, fc) && trouver_flux_warp(partie, taille, SORTE_BIAIS, j, fb) &&
+                     fe.produits == nblocs && fe.longueur >= nblocs && fc.produits == 16u * nblocs &&
+                     fc.longueur >= 16u * nblocs && fb.produits == 4u * R && fb.longueur >= 4u * R;
+    if (!bon) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&controle[CTL_FORMAT], 1u);
+        return;
+    }
+    const Disposition disp = disposition(dims, j);
+    uint8_t* mat = emplacement + disp.base;
+    const uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x, pas = gridDim.x * blockDim.x;
+    const uint4* cs = reinterpret_cast<const uint4*>(fc.p);
+    uint4* cd = reinterpret_cast<uint4*>(mat);
+    for (uint32_t i = i0; i < nblocs; i += pas) cd[i] = cs[i];
+    const uint32_t n4 = nblocs / 4u;
+    const uint32_t* es = reinterpret_cast<const uint32_t*>(fe.p);
+    uint32_t* ed = reinterpret_cast<uint32_t*>(mat + disp.echelles);
+    for (uint32_t i = i0; i < n4; i += pas) ed[i] = es[i];
+    for (uint32_t i = 4u * n4 + i0; i < nblocs; i += pas) mat[disp.echelles + i] = fe.p[i];
+    const uint32_t* bs = reinterpret_cast<const uint32_t*>(fb.p);
+    uint32_t* bd = reinterpret_cast<uint32_t*>(mat + disp.biais);
+    for (uint32_t i = i0; i < R; i += pas) bd[i] = bs[i];
+}
+
 // Scale class of a block from its scale and its row's median (4.9.3): delta = e - med + 128.
 __device__ __forceinline__ uint32_t classe_echelle(uint32_t e, uint32_t med) {
     const uint32_t d = (e - med + 128u) & 255u;

@@ -53,6 +53,11 @@ Espace plan_espace(const uint32_t lignes[3], const uint32_t colonnes[3], uint32_
     e.cd = p;
     p = al256(p + 16ull * nb2 * k);
     e.total_recouvrant = p;
+    for (int j = 0; j < 2; ++j) {
+        e.cdh[j] = p;
+        p = al256(p + 16ull * (uint64_t(lignes[j]) * (colonnes[j] / 32u)) * k);
+    }
+    e.total_tout = p;
     return e;
 }
 
@@ -61,7 +66,8 @@ struct ArgsMoe {
     uint8_t* espace;
     Espace plan;
     uint32_t j0;     // first matrix of this launch (0: gate and up; 2: down)
-    uint32_t seuls;  // the down projection's codes are decoded with gate/up, into the workspace
+    uint32_t seuls;  // 1: the down projection's codes are decoded with gate/up, into the workspace;
+                     // 2: all three matrices' codes are (their GEMVs follow, in row groups)
     uint32_t tous;   // k_moe_delta decodes every expert of the layer: activation i = expert i
     uint64_t pre_ek[3];  // with c.deltas: offset of matrix j's delta bytes ([experts][blocks])
 };
@@ -526,13 +532,13 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
         copier16(reinterpret_cast<uint4*>(med), reinterpret_cast<const uint4*>(fm.p), (R + 15u) / 16u);
     else
         for (uint32_t t = threadIdx.x; t < R; t += blockDim.x) med[t] = fm.p[t];
-    if (j < 2) charger_x2(x2s, x_de(c, i), c.x_bf16, C);
+    const bool seul = (j == 2 && a.seuls != 0u) || a.seuls == 2u;  // decode only (down: h does not exist yet)
+    if (j < 2 && !seul) charger_x2(x2s, x_de(c, i), c.x_bf16, C);
     const uint32_t t0 = warp0 + warp;
     Decodeur d;
     if (t0 < h.T) d.debut(h, t0, voie, anneau);  // the part is a layer input: start before the wait
     attendre_amont();
     liberer_aval();
-    const bool seul = j == 2 && a.seuls != 0u;  // decode only: h does not exist yet
     if (j == 2 && !seul) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
 
@@ -546,7 +552,7 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
         // The down projection's tiles while gate/up multiply: the words go to the workspace in
         // stream order (word 32 m + lane = bytes 4 (32 m + lane) .. + 3 of the codes); k_moe_bas
         // multiplies them once h exists.
-        uint32_t* cd = reinterpret_cast<uint32_t*>(a.espace + a.plan.cd) + uint64_t(i) * 4u * nblocs;
+        uint32_t* cd = reinterpret_cast<uint32_t*>(a.espace + (j == 2 ? a.plan.cd : a.plan.cdh[j])) + uint64_t(i) * 4u * nblocs;
         for (uint32_t t = t0; t < h.T; t += gridDim.x * DENSE_WARPS) {
             if (t != t0) d.debut(h, t, voie, anneau);
             const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
@@ -785,33 +791,35 @@ __global__ void __launch_bounds__(BAS_WARPS * 32) k_moe_bas(ArgsMoe a) {
 // bytes 4 (32 m + lane) .. + 3, 16 bytes per block, blocks row-major), so the raw path's GEMV
 // reads them as it reads CODES_BRUTS, with each block's scale rebuilt from its row median and
 // its delta byte. The partials are k_moe_bas's (and the raw layer's), bit for bit.
+// Matrix j = j0 + blockIdx.y: down on h, or (all three decoded first) gate and up on x.
 __global__ void __launch_bounds__(128, 3) k_moe_bas_groupes(ArgsMoe a) {
     extern __shared__ __align__(16) uint8_t dyn[];
     const Couche& c = a.c;
-    const uint32_t i = blockIdx.z, warp = threadIdx.x >> 5;
+    const uint32_t j = a.j0 + blockIdx.y, i = blockIdx.z, warp = threadIdx.x >> 5;
     if (!tenu(c, i)) return;
-    const uint32_t R = c.lignes[2], C = c.colonnes[2], B = C / 32u, nblocs = R * B;
+    const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
     const uint8_t* partie;
     uint64_t taille;
     Flux fm;
-    // The part is a layer input: its medians are found before the wait (h and the words come
-    // from the previous kernels).
-    const bool bon = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_MEDIANES, 2, fm) &&
+    // The part and x are layer inputs: the medians are found and x staged before the wait (h and
+    // the words come from the previous kernels).
+    const bool bon = partie_de(c, i, partie, taille) && trouver_flux_warp(partie, taille, SORTE_MEDIANES, j, fm) &&
                      fm.produits == R && fm.longueur >= R;
+    float4* x2g = reinterpret_cast<float4*>(dyn);
+    if (j < 2) charger_x2_groupes(x2g, x_de(c, i), c.x_bf16, C);
     attendre_amont();
     liberer_aval();
     if (!bon) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicAdd(&c.controle[4u * i + CTL_FORMAT], 1u);
         return;
     }
-    float4* x2g = reinterpret_cast<float4*>(dyn);
-    charger_x2_groupes(x2g, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
+    if (j == 2) charger_x2_groupes(x2g, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
     const uint32_t W = blockDim.x >> 5;
-    const uint32_t K = a.plan.K[2];
-    const uint8_t* cd = a.espace + a.plan.cd + uint64_t(i) * 16u * nblocs;
-    float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[2]) + uint64_t(i) * R * K;
-    gemv_groupes<true, true>(cd, deltas_de(a, i, 2, nblocs), nullptr, x2g, R, B, parts, K, blockIdx.x * W + warp,
+    const uint32_t K = a.plan.K[j];
+    const uint8_t* cd = a.espace + (j == 2 ? a.plan.cd : a.plan.cdh[j]) + uint64_t(i) * 16u * nblocs;
+    float* parts = reinterpret_cast<float*>(a.espace + a.plan.parts[j]) + uint64_t(i) * R * K;
+    gemv_groupes<true, true>(cd, deltas_de(a, i, j, nblocs), nullptr, x2g, R, B, parts, K, blockIdx.x * W + warp,
                              gridDim.x * W, fm.p);
 }
 
@@ -995,8 +1003,13 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
         const Espace pe = plan_espace(c.lignes, c.colonnes, c.experts);
         for (int j = 0; j < 3; ++j) a.pre_ek[j] = pe.ek[j];
     }
-    // The down projection's decode overlaps gate/up when the workspace holds its codes.
+    // The down projection's decode overlaps gate/up when the workspace holds its codes; with room
+    // for all three matrices' codes (and row-group shapes), every tile decodes only and the three
+    // GEMVs follow on the decoded words.
     a.seuls = (!c.brut && na <= RECOUVRE_MAX && espace_octets >= a.plan.total_recouvrant) ? 1u : 0u;
+    if (a.seuls && espace_octets >= a.plan.total_tout && groupes_possibles(c.lignes[0], c.colonnes[0] / 32u) &&
+        groupes_possibles(c.lignes[2], c.colonnes[2] / 32u))
+        a.seuls = 2u;
     const uint32_t nd = c.n_delta ? c.n_delta : 256u, nc = c.n_codes ? c.n_codes : 256u;
     uint32_t td = 1, tc = 1;
     for (int j = 0; j < 3; ++j) {
@@ -1033,7 +1046,28 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
                               dim3(DENSE_WARPS * 32), smem, flux, a);
         };
         marque(1);
-        if (a.seuls) {
+        if (a.seuls == 2u) {
+            // every tile decodes only (the three matrices in one launch), then the GEMVs in row
+            // groups on the decoded words: gate/up, SwiGLU, down
+            const size_t smem = disposition_dense(c).total;
+            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes_dense), int(smem))) != cudaSuccess) return e;
+            if ((e = lancer_pdl(k_moe_codes_dense, dim3((tc + DENSE_WARPS - 1) / DENSE_WARPS, 3, na),
+                                dim3(DENSE_WARPS * 32), smem, flux, a)) != cudaSuccess)
+                return e;
+            const uint32_t smem_g = x2g_octets(cmax);
+            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_bas_groupes), int(smem_g))) != cudaSuccess) return e;
+            auto gx = [&](uint32_t R) { return std::max(1u, ((R + GRP_LIGNES - 1) / GRP_LIGNES + 3u) / 4u); };
+            if ((e = lancer_pdl(k_moe_bas_groupes, dim3(gx(c.lignes[0]), 2, na), dim3(128), smem_g, flux, a)) != cudaSuccess)
+                return e;
+            marque(2);
+            if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
+                return e;
+            marque(3);
+            a.j0 = 2;
+            if ((e = lancer_pdl(k_moe_bas_groupes, dim3(gx(c.lignes[2]), 1, na), dim3(128), smem_g, flux, a)) != cudaSuccess)
+                return e;
+            marque(4);
+        } else if (a.seuls) {
             // gate/up fused with the GEMV, down decoded alone, in one launch; the down GEMV from
             // the decoded words once h exists (k_moe_bas: the same partials).
             const size_t smem = disposition_dense(c).total;

@@ -80,6 +80,8 @@ struct Espace {
     uint64_t total;      // the sequential schedule's workspace
     uint64_t cd;         // the overlapped schedule's decoded down codes (16 bytes per block and
     uint64_t total_recouvrant;  // activation), and its workspace
+    uint64_t cdh[2];     // the decoded gate and up codes when all three are decoded first, and
+    uint64_t total_tout;        // that schedule's workspace
     uint32_t K[3];       // partial slots per row
 };
 // Workspace of the layer "par flux" (par_flux.cu): decoded slots of the batch's distinct

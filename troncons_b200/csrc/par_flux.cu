@@ -181,6 +181,32 @@ __global__ void __launch_bounds__(1024) k_grouper(ArgsParFlux a) {
     }
 }
 
+// Raw parts: each distinct expert's matrices copied into its slot (the decode's place), matrix
+// blockIdx.y of expert blockIdx.z; an absent part was counted by k_grouper.
+__global__ void __launch_bounds__(256) k_copier_brut_flux(ArgsParFlux a, Dims dims) {
+    attendre_amont();
+    liberer_aval();
+    const Couche& c = a.c;
+    const uint32_t u = blockIdx.z;
+    if (u >= *zone<uint32_t>(a, a.p.nu)) return;
+    const uint32_t e = zone<uint32_t>(a, a.p.ordre)[u];
+    const uint8_t* partie = reinterpret_cast<const uint8_t*>(c.parties[e]);
+    if (partie == nullptr || c.parties_octets[e] < 64 || (reinterpret_cast<uintptr_t>(partie) & 15u) != 0) return;
+    copier_brut_matrice(partie, c.parties_octets[e], a.espace + a.p.slots + a.p.taille_slot * u, dims, blockIdx.y,
+                        zone<uint32_t>(a, a.p.ctl) + 4u * u);
+}
+
+// The slots of the batch's distinct experts: decoded from .trc parts, or copied from raw parts.
+static cudaError_t remplir_slots(const ArgsParFlux& a, const Dims& dims, cudaStream_t flux) {
+    if (a.c.brut) {
+        const uint32_t rmax = std::max(dims.lignes[0], dims.lignes[2]);
+        const uint32_t g = std::max(1u, std::min(64u, (rmax * 8u + 255u) / 256u));
+        return lancer_pdl(k_copier_brut_flux, dim3(g, 3, a.p.U), dim3(256), 0, flux, a, dims);
+    }
+    return lancer_decodage(reinterpret_cast<const DescDecodage*>(a.espace + a.p.descs), a.p.U, nullptr, 0, nullptr,
+                           a.c.luts, dims, nullptr, flux);
+}
+
 // The activations of one expert, one matrix: the block stages 2x of up to pf_vecteurs(C)
 // activations in shared memory (the fused kernels' padded layout), then each warp walks its rows:
 // the row's code words and scales loaded and converted once, applied to every staged activation
@@ -348,9 +374,7 @@ cudaError_t lancer_par_flux(const Couche& c, void* espace, cudaStream_t flux) {
         dims.lignes[j] = c.lignes[j];
         dims.colonnes[j] = c.colonnes[j];
     }
-    if ((e = lancer_decodage(reinterpret_cast<const DescDecodage*>(a.espace + a.p.descs), a.p.U, nullptr, 0, nullptr,
-                             c.luts, dims, nullptr, flux)) != cudaSuccess)
-        return e;
+    if ((e = remplir_slots(a, dims, flux)) != cudaSuccess) return e;
     // About two blocks per SM over the (expert, matrix) planes: each warp walks many rows, and
     // each block stages its activations once.
     int dev = 0, sms = 148;
@@ -408,9 +432,7 @@ cudaError_t lancer_par_flux_mma(const Couche& c, void* espace, uint32_t seuil, u
         dims.lignes[j] = c.lignes[j];
         dims.colonnes[j] = c.colonnes[j];
     }
-    if ((e = lancer_decodage(reinterpret_cast<const DescDecodage*>(a.espace + a.p.descs), a.p.U, nullptr, 0, nullptr,
-                             c.luts, dims, nullptr, flux)) != cudaSuccess)
-        return e;
+    if ((e = remplir_slots(a, dims, flux)) != cudaSuccess) return e;
     // the groups, on the host
     const uint32_t U = a.p.U;
     uint32_t nu = 0;
