@@ -104,12 +104,12 @@ def pics():
 
 
 # DRAM bytes (read + write) of the dominant launch measured by ncu on the same launch shape (4
-# routed experts of 2880 x 2880): the decode launch of the overlapped schedule (gate/up decoded
-# into their GEMV, down decoded alongside: 3 x 4 CODES_CTX streams; 51.02 MB read, 0.81 MB
-# written for 47.64 MB of streams, profiles/k_moe_codes_dense_config1_4experts.md), and the
-# sequential schedule's gate/up launch (34.03 MB read, 13 KB written for 31.76 MB of streams,
-# an earlier capture of that launch shape).
-TRAFIC_CODES = {"recouvrant": 51_838_208, "sequentiel": 34_041_856}
+# routed experts of 2880 x 2880): the decode launch of the overlapped schedule (every tile of the
+# 3 x 4 CODES_CTX streams decoded, the words stored for the row-group GEMVs; 51.35 MB read,
+# 9.76 MB of the stored words written back from L2, for 47.64 MB of streams,
+# profiles/k_moe_codes_dense_config1_4experts.md), and the sequential schedule's gate/up launch
+# (34.03 MB read, 13 KB written for 31.76 MB of streams, an earlier capture of that launch shape).
+TRAFIC_CODES = {"recouvrant": 61_113_856, "sequentiel": 34_041_856}
 
 
 class Horloges:
@@ -376,12 +376,12 @@ def notre_bras(args):
         "e2e": {"value": round(w * octets / (t_e2e_ms * 1e-3) / 1e9, 2), "unit": UNITE,
                 "h2d_bytes_per_step": 2 * c.dims.colonnes[0] + 4 * c.dims.lignes[2],
                 "d2h_bytes_per_step": 4 * c.dims.lignes[2]},
-        "gpu_launches": args.steps * 7,
+        "gpu_launches": args.steps * (7 if args.sequentiel else 8),
         "roofline": {"bound": "hbm",
                      "kernel": ("k_moe_codes / k_moe_codes_dense (gate/up: CODES_CTX decode fused into the GEMV)"
                                 if args.sequentiel else
-                                "k_moe_codes_dense (gate/up CODES_CTX decoded into their GEMV, down CODES_CTX "
-                                "decoded alongside)"),
+                                "k_moe_codes_dense (every CODES_CTX tile of the routed experts decoded, the words "
+                                "stored for the row-group GEMVs)"),
                      "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
                      "peak_source": sorte_pic, "frac_8tbs": round(atteint / 8000.0, 4),
                      # DRAM read + write bytes of that launch, from ncu on the same launch shape
@@ -390,7 +390,8 @@ def notre_bras(args):
                      "dram__bytes_write.sum, one launch of the same shape (summary under profiles/)",
                      "algorithmic_bytes_per_launch": round(octets_dom / args.steps)},
         "phases_ms": {n: round(sum(v) / len(v), 4) for n, v in
-                      zip(["router", "delta", "gate_up", "swiglu", "down", "combine"], t_phase)},
+                      zip(["router", "delta", "gate_up", "swiglu", "down", "combine"] if args.sequentiel else
+                          ["router", "delta", "decode", "gate_up_gemv_swiglu", "down_gemv", "combine"], t_phase)},
         "clocks": horl.resume(),
         "wall_s_timed_region": round(mur, 3),
         "generation_s": round(t_gen, 1),

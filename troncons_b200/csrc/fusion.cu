@@ -1054,12 +1054,12 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
             if ((e = lancer_pdl(k_moe_codes_dense, dim3((tc + DENSE_WARPS - 1) / DENSE_WARPS, 3, na),
                                 dim3(DENSE_WARPS * 32), smem, flux, a)) != cudaSuccess)
                 return e;
+            marque(2);  // phases: the decode launch alone, then the gate/up GEMV with SwiGLU
             const uint32_t smem_g = x2g_octets(cmax);
             if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_bas_groupes), int(smem_g))) != cudaSuccess) return e;
             auto gx = [&](uint32_t R) { return std::max(1u, ((R + GRP_LIGNES - 1) / GRP_LIGNES + 3u) / 4u); };
             if ((e = lancer_pdl(k_moe_bas_groupes, dim3(gx(c.lignes[0]), 2, na), dim3(128), smem_g, flux, a)) != cudaSuccess)
                 return e;
-            marque(2);
             if ((e = lancer_pdl(k_moe_swiglu, dim3((c.lignes[0] + 255) / 256, na, 1), dim3(256), 0, flux, a)) != cudaSuccess)
                 return e;
             marque(3);
