@@ -235,16 +235,6 @@ __device__ __forceinline__ void cp_async_wait() {
 __device__ __forceinline__ uint32_t adresse_partagee(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-    unsigned short v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
 
 // ------------------------------------------------------------------ the warp decoder
 
@@ -263,7 +253,6 @@ struct Decodeur {
     uint32_t tranche;      // chunk (256 aligned words from ga) the pointer is in
     const uint8_t* ga;     // 16-aligned address at or below mots[0]
     uint16_t* anneau;      // this warp's ring (ANNEAU_ALLOC words, shared memory)
-    uint32_t anneau_s;     // its shared-space address
     uint32_t masque_inf;   // lanes below this one
     uint32_t voie;
 
@@ -283,7 +272,6 @@ struct Decodeur {
     __device__ __forceinline__ void debut(const EnteteRans& h, uint32_t t, uint32_t v, uint16_t* ring) {
         voie = v;
         anneau = ring;
-        anneau_s = adresse_partagee(ring);
         masque_inf = (1u << voie) - 1u;
         x = h.etats[t * VOIES + voie];
         const uint32_t ptr = h.debut[t];
@@ -320,11 +308,12 @@ struct Decodeur {
         }
     }
 
-    // One sub-step; `lut_s`: shared address of the table. Returns the LUT entry (its low byte
-    // is the symbol).
-    __device__ __forceinline__ uint32_t pas(uint32_t lut_s) {
-        const uint32_t e = lds32(lut_s + 4u * (x & (M - 1u)));
-        const uint32_t pre = lds16(anneau_s + 2u * ((pa & (ANNEAU_MOTS - 1u)) + voie));
+    // One sub-step; `lut`: the table in shared memory. Returns the LUT entry (its low byte is
+    // the symbol). Plain loads (not volatile asm): the compiler schedules them, and they stay
+    // ordered after the ring refill's wait (a memory clobber).
+    __device__ __forceinline__ uint32_t pas(const uint32_t* lut) {
+        const uint32_t e = lut[x & (M - 1u)];
+        const uint32_t pre = anneau[(pa & (ANNEAU_MOTS - 1u)) + voie];
         const uint32_t y = (((e >> 8) & 0xFFFu) + 1u) * (x >> 12) + (e >> 20);
         const bool besoin = y < L;
         const uint32_t vote = __ballot_sync(0xFFFFFFFFu, besoin);
@@ -335,25 +324,25 @@ struct Decodeur {
     }
 
     // Four sub-steps: the lane's 32-bit output word (byte k = sub-step k).
-    __device__ __forceinline__ uint32_t macro(uint32_t lut_s) {
-        uint32_t m = pas(lut_s);
-        m = __byte_perm(m, pas(lut_s), 0x0040);
-        m = __byte_perm(m, pas(lut_s), 0x0410);
-        m = __byte_perm(m, pas(lut_s), 0x4210);
+    __device__ __forceinline__ uint32_t macro(const uint32_t* lut) {
+        uint32_t m = pas(lut);
+        m = __byte_perm(m, pas(lut), 0x0040);
+        m = __byte_perm(m, pas(lut), 0x0410);
+        m = __byte_perm(m, pas(lut), 0x4210);
         return m;
     }
 
     // Four sub-steps, with the caller's independent work f(Etape<k>) placed after sub-step k:
     // it fills the decode chain's latency instead of following it.
     template <typename F>
-    __device__ __forceinline__ uint32_t macro(uint32_t lut_s, F&& f) {
-        uint32_t m = pas(lut_s);
+    __device__ __forceinline__ uint32_t macro(const uint32_t* lut, F&& f) {
+        uint32_t m = pas(lut);
         f(Etape<0>{});
-        m = __byte_perm(m, pas(lut_s), 0x0040);
+        m = __byte_perm(m, pas(lut), 0x0040);
         f(Etape<1>{});
-        m = __byte_perm(m, pas(lut_s), 0x0410);
+        m = __byte_perm(m, pas(lut), 0x0410);
         f(Etape<2>{});
-        m = __byte_perm(m, pas(lut_s), 0x4210);
+        m = __byte_perm(m, pas(lut), 0x4210);
         f(Etape<3>{});
         return m;
     }
@@ -374,16 +363,16 @@ struct Decodeur {
     };
 
     // After debut(): the first sub-step's entries.
-    __device__ __forceinline__ void debut_avance(uint32_t lut_s, Avance& s) {
-        s.e = lds32(lut_s + 4u * (x & (M - 1u)));
-        s.wp = lds16(anneau_s + 2u * ((pa & (ANNEAU_MOTS - 1u)) + voie));
-        s.lp = lds32(lut_s + 4u * (s.wp & (M - 1u)));
+    __device__ __forceinline__ void debut_avance(const uint32_t* lut, Avance& s) {
+        s.e = lut[x & (M - 1u)];
+        s.wp = anneau[(pa & (ANNEAU_MOTS - 1u)) + voie];
+        s.lp = lut[s.wp & (M - 1u)];
     }
 
-    __device__ __forceinline__ uint32_t pas_avance(uint32_t lut_s, Avance& s) {
+    __device__ __forceinline__ uint32_t pas_avance(const uint32_t* lut, Avance& s) {
         const uint32_t e = s.e;
         const uint32_t y = (((e >> 8) & 0xFFFu) + 1u) * (x >> 12) + (e >> 20);
-        const uint32_t ey = lds32(lut_s + 4u * (y & (M - 1u)));
+        const uint32_t ey = lut[y & (M - 1u)];
         const bool besoin = y < L;
         const uint32_t vote = __ballot_sync(0xFFFFFFFFu, besoin);
         const uint32_t rang = __popc(vote & masque_inf);
@@ -392,29 +381,29 @@ struct Decodeur {
         x = besoin ? __byte_perm(w, y, 0x5410) : y;
         s.e = besoin ? ew : ey;
         pa += __popc(vote);
-        s.wp = lds16(anneau_s + 2u * ((pa & (ANNEAU_MOTS - 1u)) + voie));
-        s.lp = lds32(lut_s + 4u * (s.wp & (M - 1u)));
+        s.wp = anneau[(pa & (ANNEAU_MOTS - 1u)) + voie];
+        s.lp = lut[s.wp & (M - 1u)];
         return e;
     }
 
-    __device__ __forceinline__ uint32_t macro_avance(uint32_t lut_s, Avance& s) {
-        uint32_t m = pas_avance(lut_s, s);
-        m = __byte_perm(m, pas_avance(lut_s, s), 0x0040);
-        m = __byte_perm(m, pas_avance(lut_s, s), 0x0410);
-        m = __byte_perm(m, pas_avance(lut_s, s), 0x4210);
+    __device__ __forceinline__ uint32_t macro_avance(const uint32_t* lut, Avance& s) {
+        uint32_t m = pas_avance(lut, s);
+        m = __byte_perm(m, pas_avance(lut, s), 0x0040);
+        m = __byte_perm(m, pas_avance(lut, s), 0x0410);
+        m = __byte_perm(m, pas_avance(lut, s), 0x4210);
         return m;
     }
 
-    // With the caller's independent work f(Etape<k>) after sub-step k (as macro(lut_s, f)).
+    // With the caller's independent work f(Etape<k>) after sub-step k (as macro(lut, f)).
     template <typename F>
-    __device__ __forceinline__ uint32_t macro_avance(uint32_t lut_s, Avance& s, F&& f) {
-        uint32_t m = pas_avance(lut_s, s);
+    __device__ __forceinline__ uint32_t macro_avance(const uint32_t* lut, Avance& s, F&& f) {
+        uint32_t m = pas_avance(lut, s);
         f(Etape<0>{});
-        m = __byte_perm(m, pas_avance(lut_s, s), 0x0040);
+        m = __byte_perm(m, pas_avance(lut, s), 0x0040);
         f(Etape<1>{});
-        m = __byte_perm(m, pas_avance(lut_s, s), 0x0410);
+        m = __byte_perm(m, pas_avance(lut, s), 0x0410);
         f(Etape<2>{});
-        m = __byte_perm(m, pas_avance(lut_s, s), 0x4210);
+        m = __byte_perm(m, pas_avance(lut, s), 0x4210);
         f(Etape<3>{});
         return m;
     }

@@ -107,7 +107,6 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
         med = med_s;
     }
     __syncthreads();
-    const uint32_t lut_s = adresse_partagee(lut);
     uint8_t* ech = mat + disp.echelles;
     const uint32_t nmacro = h.P / 128u;
     uint32_t hors_l = 0, pointeur = 0;
@@ -121,13 +120,13 @@ __global__ void __launch_bounds__(ECH_WARPS * 32) k_echelles(ArgsDecodage a) {
         LignesDelta lg;
         lg.debut(b0, B);
         Decodeur::Avance av;
-        d.debut_avance(lut_s, av);  // one table for every lane: the look-ahead form
+        d.debut_avance(lut, av);  // one table for every lane: the look-ahead form
         d.avancer();
-        uint32_t mot_p = d.macro_avance(lut_s, av);
+        uint32_t mot_p = d.macro_avance(lut, av);
         for (uint32_t m = m0 + 1; m < m1; ++m) {
             d.avancer();
             uint32_t sortie = 0;
-            const uint32_t mot = d.macro_avance(lut_s, av, [&](auto k) {
+            const uint32_t mot = d.macro_avance(lut, av, [&](auto k) {
                 constexpr int K = decltype(k)::value;  // block 4w + K of the previous word
                 const uint32_t rk = lg.rang(K);
                 const uint32_t mk = rk < R ? uint32_t(med[rk]) : 0u;
@@ -183,7 +182,6 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
     attendre_amont();  // the scales come from k_echelles
     liberer_aval();
     __syncthreads();
-    const uint32_t lut_s = adresse_partagee(lut);
     const Disposition disp = disposition(a.dims, j);
     uint8_t* mat = emplacement + disp.base;
     uint32_t* codes = reinterpret_cast<uint32_t*>(mat);
@@ -220,7 +218,7 @@ __global__ void __launch_bounds__(CODES_WARPS * 32) k_codes(ArgsDecodage a) {
             const bool v2 = m + 2u < m1 && bloc + 16u < nblocs;
             const uint32_t e2 = v2 ? __ldg(ech + bloc + 16u) : 0u, md2 = v2 ? __ldg(med + l2) : 0u;
             d.avancer();
-            const uint32_t mot = d.macro(lut_s + ctx * (M * 4u));
+            const uint32_t mot = d.macro(lut + ctx * M);
             const uint32_t w = m * 32u + voie;
             if (w < mots_utiles) codes[w] = mot;
             bloc += 8u;

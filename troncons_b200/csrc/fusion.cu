@@ -154,7 +154,6 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     const uint32_t warp0 = blockIdx.x * DELTA_WARPS;
     if (warp0 >= h.T) return;
     __syncthreads();
-    const uint32_t lut_s = adresse_partagee(lut);
     uint8_t* delta = a.espace + a.plan.ek[j] + uint64_t(i) * nblocs;
     const uint32_t nmacro = h.P / 128u;
     uint32_t hors_l = 0, pointeur = 0;
@@ -162,12 +161,12 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * DELTA_WARPS) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
         Decodeur::Avance av;
-        d.debut_avance(lut_s, av);  // one table for every lane: the look-ahead form
+        d.debut_avance(lut, av);  // one table for every lane: the look-ahead form
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         // Word w = 32 m + lane is the delta of blocks 4w .. 4w + 3, stored as it comes.
         for (uint32_t m = m0; m < m1; ++m) {
             d.avancer();
-            const uint32_t mot = d.macro_avance(lut_s, av);
+            const uint32_t mot = d.macro_avance(lut, av);
             const uint32_t b0 = 4u * (m * 32u + voie);
             if (b0 + 3u < nblocs) {
                 *reinterpret_cast<uint32_t*>(delta + b0) = mot;
@@ -354,7 +353,6 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
 
     if (warp < MOE_PAIRES) {
         // ---------------- producer: the decode chain
-        const uint32_t lut_s = adresse_partagee(lut);
         const uint8_t* __restrict__ ek = deltas_de(a, i, j, nblocs);  // delta bytes
         uint32_t hors_l = 0, pointeur = 0, n = 0;
         for (uint32_t t = paire_t0; t < h.T && !abandon; t += pas_tuiles) {
@@ -377,7 +375,7 @@ __global__ void __launch_bounds__(MOE_PAIRES * 64, 2) k_moe_codes(ArgsMoe a) {
                     const uint32_t ctx = bloc < nblocs ? classe_delta(e0) : 0u;
                     const uint32_t e2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
                     d.avancer();
-                    mb[(m - s0) * 32u + voie] = d.macro(lut_s + ctx * (M * 4u));
+                    mb[(m - s0) * 32u + voie] = d.macro(lut + ctx * M);
                     if ((voie & 3u) == 0) db[(m - s0) * 8u + g] = uint8_t(e0);
                     bloc += 8u;
                     e0 = e1;
@@ -541,8 +539,6 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     liberer_aval();
     if (j == 2 && !seul) charger_x2(x2s, reinterpret_cast<const float*>(a.espace + a.plan.h) + uint64_t(i) * C, 0u, C);
     __syncthreads();
-
-    const uint32_t lut_s = adresse_partagee(lut);
     const uint8_t* __restrict__ ek = deltas_de(a, i, j, nblocs);  // delta bytes
     const float4* x2s4 = reinterpret_cast<const float4*>(x2s);
     const uint32_t q = voie & 3u, g = voie >> 2;
@@ -563,7 +559,7 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
                 const uint32_t ctx = bloc < nblocs ? classe_delta(e0) : 0u;
                 const uint32_t e2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
                 d.avancer();
-                const uint32_t mot = d.macro(lut_s + ctx * (M * 4u));
+                const uint32_t mot = d.macro(lut + ctx * M);
                 if (bloc < nblocs) cd[m * 32u + voie] = mot;
                 bloc += 8u;
                 e0 = e1;
@@ -600,11 +596,11 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
             d.avancer();
             uint32_t mot;
             if (m == m0) {
-                mot = d.macro(lut_s + ctx * (M * 4u));
+                mot = d.macro(lut + ctx * M);
             } else {
                 ProduitEtage pe = {};
                 const bool valide_p = bloc_p < nblocs;
-                mot = d.macro(lut_s + ctx * (M * 4u), [&](auto k) {
+                mot = d.macro(lut + ctx * M, [&](auto k) {
                     constexpr int K = decltype(k)::value;
                     if constexpr (K < 3)
                         pe.etape<K>(mot_p, x2s4, b_p, q);
