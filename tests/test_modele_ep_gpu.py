@@ -7,7 +7,7 @@ gpt-oss-shaped model (2 layers, 8 experts top-4).
   .trc parts and from the raw parts;
 - two ranks (one process per GPU, NCCL for the MoE inputs' all-gather; the combine's exchange by
   NVLink peer stores in the combine kernel, or by an NCCL reduce-scatter): each rank holds half
-  of every layer's experts and runs its own sequence; its logits agree with the one-GPU model run on that sequence within 1e-5 of
+  of every layer's experts and runs its own sequence; its logits agree with the one-GPU model run on that sequence within 1e-4 of
   max|z| (the same experts' terms summed in another order across the GPUs) with the same greedy
   token; the shares' parts are byte for byte the whole model's (tables from the counts summed
   over NCCL); the same with two sequences per rank (a batch of 4). Skipped with fewer than two
@@ -26,6 +26,13 @@ pytestmark = pytest.mark.gpu
 
 FORME = dict(couches=2, d=256, tetes=8, tetes_kv=2, experts=8, k=4, vocab=512, contexte=64, ffn=256, fenetre=16,
              graine=13, compresse=True, brut=True)
+
+
+# Two ranks against one GPU: each layer's expert terms are summed in another order across the
+# GPUs (f32 rounding, ~1e-7 of a layer's output), and the difference is carried from step to step
+# through the KV caches: measured up to 1.6e-5 of max|z| after 12 steps of a batch of two
+# sequences per rank; the bound leaves a margin over that, and the greedy tokens must agree.
+TOLERANCE_EP = 1e-4
 
 
 def _suite(m_pas, vues, jetons):
@@ -139,7 +146,7 @@ def _rang(rang, monde, port, echange, moe):
             b = _suite(seul.pas, seul.vues, jetons)
             _journal(rang, t0, actifs, "one-GPU steps done")
             for t, ((za, ja), (zb, jb)) in enumerate(zip(a, b)):
-                assert np.abs(za - zb).max() <= 1e-5 * np.abs(zb).max(), f"rank {rang} {actifs} step {t}"
+                assert np.abs(za - zb).max() <= TOLERANCE_EP * np.abs(zb).max(), f"rank {rang} {actifs} step {t}"
                 assert ja == jb, f"rank {rang} {actifs} step {t}"
         assert (ep.controle == 0).all()
         # two sequences per rank: a batch of 4 tokens over 2 GPUs
@@ -160,10 +167,14 @@ def _rang(rang, monde, port, echange, moe):
             seul.choisir("compresse")
             b = _suite(seul.pas, seul.vues, jetons[i])
             for t in range(16):
-                assert np.abs(z[i][t] - b[t][0]).max() <= 1e-5 * np.abs(b[t][0]).max(), f"rank {rang} seq {i} step {t}"
+                ecart = np.abs(z[i][t] - b[t][0]).max() / np.abs(b[t][0]).max()
+                assert ecart <= TOLERANCE_EP, f"rank {rang} seq {i} step {t}: {ecart:.3g} of max|z|"
         assert (ep.controle == 0).all()
         _journal(rang, t0, "done, final barrier")
         dist.barrier()
+    except BaseException as erreur:  # shown at once: the other rank may be waiting in a collective
+        _journal(rang, t0, "FAILED:", repr(erreur)[:2000])
+        raise
     finally:
         dist.destroy_process_group()
 
