@@ -222,8 +222,8 @@ def octets_pas(c, idx, k):
 
 def octets_codes_dominant(c, idx, k, matrices=(0, 1, 2)):
     """Compressed CODES_CTX bytes of `matrices` of the routed experts: what the dominant launch
-    (k_moe_codes_dense: gate/up decoded into the GEMV, down decoded alongside) must stream from
-    HBM."""
+    (the decode launch: k_moe_codes_plat in the overlapped schedule, k_moe_codes / _dense with
+    gate/up decoded into the GEMV in the sequential one) must stream from HBM."""
     total = 0
     for e in idx[:k]:
         p = c.parties[int(e)]
@@ -380,8 +380,8 @@ def notre_bras(args):
         "roofline": {"bound": "hbm",
                      "kernel": ("k_moe_codes / k_moe_codes_dense (gate/up: CODES_CTX decode fused into the GEMV)"
                                 if args.sequentiel else
-                                "k_moe_codes_dense (every CODES_CTX tile of the routed experts decoded, the words "
-                                "stored for the row-group GEMVs)"),
+                                "k_moe_codes_plat (every CODES_CTX tile of the routed experts decoded, the tiles "
+                                "spread evenly over the SMs, the words stored for the row-group GEMVs)"),
                      "achieved": round(atteint, 2), "peak": pic, "unit": "GB/s", "frac": round(atteint / pic, 4),
                      "peak_source": sorte_pic, "frac_8tbs": round(atteint / 8000.0, 4),
                      # DRAM read + write bytes of that launch, from ncu on the same launch shape

@@ -628,6 +628,118 @@ __global__ void __launch_bounds__(DENSE_WARPS * 32, 2) k_moe_codes_dense(ArgsMoe
     verser_controle(controle, voie, hors_l, pointeur);
 }
 
+// The decode launch of the overlapped schedule (every tile decode-only, the words stored for the
+// row-group GEMVs), with the tiles spread evenly over the SMs. Grid (bx, 3): the bx blocks of
+// matrix j (bx = SMs / 3, one block per SM) take the tiles of matrix j of every held activation
+// as one list (activation by activation, tile by tile), tile g going to block g mod bx and, in
+// it, warp g / bx (round-robin over the blocks first). Each SM then holds ceil(tiles / bx) chains
+// or one fewer, whatever the routing, where k_moe_codes_dense's blocks of a fixed width (one
+// stream's tiles each) put two blocks, 22 chains, on some SMs once the held activations pass 4:
+// an expert-parallel rank's share, batches of tokens. The words and counters are
+// k_moe_codes_dense's, tile for tile.
+constexpr uint32_t PLAT_WARPS = 22;
+
+__host__ __device__ __forceinline__ uint32_t plat_octets() {
+    return 3u * M * 4u + PLAT_WARPS * ANNEAU_ALLOC * 2u + 4u * (RECOUVRE_MAX + 1u);
+}
+
+__global__ void __launch_bounds__(PLAT_WARPS * 32, 1) k_moe_codes_plat(ArgsMoe a) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    const Couche& c = a.c;
+    const uint32_t j = blockIdx.y, voie = threadIdx.x & 31u, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const uint32_t R = c.lignes[j], C = c.colonnes[j], B = C / 32u, nblocs = R * B;
+    const uint32_t na = min(activations(c), RECOUVRE_MAX);
+    uint32_t* lut = reinterpret_cast<uint32_t*>(dyn);
+    uint16_t* anneau = reinterpret_cast<uint16_t*>(dyn + 3u * M * 4u) + warp * ANNEAU_ALLOC;
+    uint32_t* premier = reinterpret_cast<uint32_t*>(dyn + 3u * M * 4u + PLAT_WARPS * ANNEAU_ALLOC * 2u);
+    // The routed experts are known at the start unless DELTA was decoded ahead (then the previous
+    // kernel is the router's); the delta bytes are read only after the wait.
+    bool attendu = false;
+    auto attendre = [&] {
+        if (!attendu) {
+            attendre_amont();
+            liberer_aval();
+            attendu = true;
+        }
+    };
+    if (c.deltas != nullptr) attendre();
+    copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u + 1u) * M),
+             3u * M / 4u);
+    // Tiles of each activation's stream (0 when its expert is not held or its part is malformed:
+    // a malformed part counts one format error, from block 0).
+    for (uint32_t i = warp; i < na; i += W) {
+        uint32_t nt = 0;
+        if (tenu(c, i)) {
+            const uint8_t* partie;
+            uint64_t taille;
+            Flux fc, fm;
+            EnteteRans h;
+            const bool bon = B >= 8u && partie_de(c, i, partie, taille) &&
+                             trouver_flux_warp(partie, taille, SORTE_CODES_CTX, j, fc) &&
+                             trouver_flux_warp(partie, taille, SORTE_MEDIANES, j, fm) && fm.produits == R &&
+                             fm.longueur >= R && R <= 8192u && lire_entete(fc, nblocs * 16u, h) &&
+                             (h.N % SEGMENT_MACRO) == 0;
+            if (bon)
+                nt = h.T;
+            else if (voie == 0 && blockIdx.x == 0)
+                atomicAdd(&c.controle[4u * i + CTL_FORMAT], 1u);
+        }
+        if (voie == 0) premier[i + 1u] = nt;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        premier[0] = 0;
+        for (uint32_t i = 0; i < na; ++i) premier[i + 1u] += premier[i];
+    }
+    __syncthreads();
+    const uint32_t total = premier[na];
+    uint32_t i_cour = RECOUVRE_MAX, hors_l = 0, pointeur = 0;
+    for (uint32_t g = blockIdx.x + gridDim.x * warp; g < total; g += gridDim.x * W) {
+        uint32_t i = 0;
+        while (premier[i + 1u] <= g) ++i;
+        const uint32_t t = g - premier[i];
+        if (i != i_cour) {
+            if (i_cour < RECOUVRE_MAX) {
+                verser_controle(c.controle + 4u * i_cour, voie, hors_l, pointeur);
+                hors_l = pointeur = 0;
+            }
+            i_cour = i;
+        }
+        const uint8_t* partie;
+        uint64_t taille;
+        Flux fc;
+        EnteteRans h;
+        partie_de(c, i, partie, taille);
+        trouver_flux_warp(partie, taille, SORTE_CODES_CTX, j, fc);
+        lire_entete(fc, nblocs * 16u, h);
+        Decodeur d;
+        d.debut(h, t, voie, anneau);  // the part is a layer input: its first words before the wait
+        attendre();
+        const uint8_t* __restrict__ ek = deltas_de(a, i, j, nblocs);
+        uint32_t* cd = reinterpret_cast<uint32_t*>(a.espace + (j == 2 ? a.plan.cd : a.plan.cdh[j])) + uint64_t(i) * 4u * nblocs;
+        const uint32_t g8 = voie >> 2;
+        const uint32_t nmacro = h.P / 128u;
+        const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
+        uint32_t bloc = 8u * m0 + g8;
+        uint32_t e0 = bloc < nblocs ? uint32_t(__ldg(ek + bloc)) : 0u;
+        uint32_t e1 = (m0 + 1u < m1 && bloc + 8u < nblocs) ? uint32_t(__ldg(ek + bloc + 8u)) : 0u;
+        for (uint32_t m = m0; m < m1; ++m) {
+            const uint32_t ctx = bloc < nblocs ? classe_delta(e0) : 0u;
+            const uint32_t e2 = (m + 2u < m1 && bloc + 16u < nblocs) ? uint32_t(__ldg(ek + bloc + 16u)) : 0u;
+            d.avancer();
+            const uint32_t mot = d.macro(lut + ctx * M);
+            if (bloc < nblocs) cd[m * 32u + voie] = mot;
+            bloc += 8u;
+            e0 = e1;
+            e1 = e2;
+        }
+        d.bilan(hors_l, pointeur);
+        d.terminer();
+    }
+    if (i_cour < RECOUVRE_MAX) verser_controle(c.controle + 4u * i_cour, voie, hors_l, pointeur);
+    attendre();
+}
+
 // ------------------------------------------------------------------ raw parts: row-centric
 
 __global__ void __launch_bounds__(MOE_WARPS * 32, BRUT_BLOCS_SM) k_moe_brut(ArgsMoe a) {
@@ -1043,12 +1155,13 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
         };
         marque(1);
         if (a.seuls == 2u) {
-            // every tile decodes only (the three matrices in one launch), then the GEMVs in row
-            // groups on the decoded words: gate/up, SwiGLU, down
-            const size_t smem = disposition_dense(c).total;
-            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes_dense), int(smem))) != cudaSuccess) return e;
-            if ((e = lancer_pdl(k_moe_codes_dense, dim3((tc + DENSE_WARPS - 1) / DENSE_WARPS, 3, na),
-                                dim3(DENSE_WARPS * 32), smem, flux, a)) != cudaSuccess)
+            // every tile decodes only (the three matrices in one launch, the tiles spread evenly
+            // over the SMs), then the GEMVs in row groups on the decoded words: gate/up, SwiGLU,
+            // down
+            const size_t smem = plat_octets();
+            if ((e = assurer_smem(reinterpret_cast<const void*>(k_moe_codes_plat), int(smem))) != cudaSuccess) return e;
+            if ((e = lancer_pdl(k_moe_codes_plat, dim3(std::max(1, sms / 3), 3, 1), dim3(PLAT_WARPS * 32), smem, flux,
+                                a)) != cudaSuccess)
                 return e;
             marque(2);  // phases: the decode launch alone, then the gate/up GEMV with SwiGLU
             const uint32_t smem_g = x2g_octets(cmax);
