@@ -105,11 +105,11 @@ def pics():
 
 # DRAM bytes (read + write) of the dominant launch measured by ncu on the same launch shape (4
 # routed experts of 2880 x 2880): the decode launch of the overlapped schedule (every tile of the
-# 3 x 4 CODES_CTX streams decoded, the words stored for the row-group GEMVs; 51.35 MB read,
-# 9.76 MB of the stored words written back from L2, for 47.64 MB of streams,
-# profiles/k_moe_codes_dense_config1_4experts.md), and the sequential schedule's gate/up launch
+# 3 x 4 CODES_CTX streams decoded, the words stored for the row-group GEMVs; 51.27 MB read,
+# 9.50 MB of the stored words written back from L2, for 47.64 MB of streams,
+# profiles/k_moe_codes_plat_config1_4experts.md), and the sequential schedule's gate/up launch
 # (34.03 MB read, 13 KB written for 31.76 MB of streams, an earlier capture of that launch shape).
-TRAFIC_CODES = {"recouvrant": 61_113_856, "sequentiel": 34_041_856}
+TRAFIC_CODES = {"recouvrant": 60_769_792, "sequentiel": 34_041_856}
 
 
 class Horloges:
