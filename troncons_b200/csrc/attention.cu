@@ -132,6 +132,115 @@ __global__ void __launch_bounds__(Q8_WARPS * 32) k_gemv_q8_0(const uint8_t* __re
     cp_async_wait<0>();
 }
 
+// The layer's Q8_0 GEMVs that share an input in one launch (DescQ8Couche): q, k and v on
+// RMSNorm(x) (the norm recomputed by every block from x, in k_rmsnorm's order: thread t's f64 fma
+// chain over i = t, t + 256, ..., the fixed tree over 256, then each element rounded once), or the
+// output projection with the residual add folded in; or, for J tokens at once (x [J][C], matrix m's
+// y [J][lignes[m]]), q, k and v on the batch's normed rows. Rows as in k_gemv_q8_0<J>, matrix
+// after matrix: the same bits as k_rmsnorm and separate k_gemv_q8_0 launches (then k_combiner),
+// with the small k and v projections (512 rows each) riding in the q projection's launch instead
+// of each paying a launch's ramp on 64 blocks.
+static_assert(Q8_WARPS * 32 == 256, "the in-block RMSNorm follows k_rmsnorm's 256 threads");
+
+template <int J>
+__global__ void __launch_bounds__(Q8_WARPS * 32) k_q8_0_couche(DescQ8Couche d) {
+    extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ double part[256];
+    const uint32_t t = threadIdx.x, voie = t & 31u, warp = t >> 5;
+    const uint32_t C = d.C, B = C / 32u, octets = B * Q8_BLOC, tampon = q8_tampon(C);
+    const uint32_t xp = q8_x_octets(C) / 4u;  // floats per staged token
+    float* xs = reinterpret_cast<float*>(dyn);
+    uint8_t* lignes = dyn + J * q8_x_octets(C) + warp * 2u * tampon;
+    uint32_t R = 0;
+    for (uint32_t m = 0; m < d.n; ++m) R += d.lignes[m];
+    auto charger = [&](uint8_t* tampon_l, uint32_t r) {
+        uint32_t m = 0;
+        while (r >= d.lignes[m]) r -= d.lignes[m++];
+        q8_charger_ligne(tampon_l, static_cast<const uint8_t*>(d.w[m]), uint64_t(r) * octets, octets,
+                         uint64_t(d.lignes[m]) * octets, voie);
+    };
+    const uint32_t pas = gridDim.x * Q8_WARPS;
+    uint32_t r = blockIdx.x * Q8_WARPS + warp;
+    // The weights are an input of the call: the first row is requested before the wait.
+    if (r < R) charger(lignes, r);
+    cp_async_commit();
+    attendre_amont();
+    liberer_aval();
+    if (J == 1 && d.norme != nullptr) {
+        double s = 0.0;
+        for (uint32_t i = t; i < C; i += 256u) {
+            const double v = d.x[i];
+            s = fma(v, v, s);
+        }
+        part[t] = s;
+        __syncthreads();
+#pragma unroll
+        for (uint32_t k = 128; k > 0; k >>= 1) {
+            if (t < k) part[t] += part[t + k];
+            __syncthreads();
+        }
+        const double rn = 1.0 / sqrt(part[0] / double(C) + double(d.eps));
+        for (uint32_t i = t; i < C; i += 256u) {
+            const float h = float(double(d.x[i]) * rn * double(d.norme[i]));
+            xs[i + i / 32u] = h;
+            if (blockIdx.x == 0 && d.h != nullptr) d.h[i] = h;
+        }
+    } else {
+        for (uint32_t i = t; i < J * C; i += 256u) {
+            const uint32_t jt = i / C, c = i - jt * C;
+            xs[jt * xp + c + c / 32u] = d.x[i];
+        }
+    }
+    __syncthreads();
+    for (uint32_t n = 0; r < R; r += pas, ++n) {
+        const uint32_t rs = r + pas;
+        if (rs < R) charger(lignes + ((n + 1u) & 1u) * tampon, rs);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncwarp();
+        uint32_t m = 0, rl = r;
+        while (rl >= d.lignes[m]) rl -= d.lignes[m++];
+        const uint8_t* ligne = lignes + (n & 1u) * tampon;
+        const uint64_t debut = uint64_t(rl) * octets;
+        const uint32_t dec = uint32_t(debut - (debut & ~uint64_t(15)));
+        float acc[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[j] = 0.0f;
+        for (uint32_t b = voie; b < B; b += 32u) {
+            const uint16_t* blk = reinterpret_cast<const uint16_t*>(ligne + dec + b * Q8_BLOC);
+            const float dq = f16_f32(blk[0]);
+            const float* xv = xs + 33u * b;
+            float s[J];
+#pragma unroll
+            for (int j = 0; j < J; ++j) s[j] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const uint32_t w = blk[1 + k];
+                const float q0 = float(int8_t(w & 0xFFu)), q1 = float(int8_t(w >> 8));
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    s[j] = fmaf(q0, xv[j * xp + 2 * k], s[j]);
+                    s[j] = fmaf(q1, xv[j * xp + 2 * k + 1], s[j]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < J; ++j) acc[j] = fmaf(dq, s[j], acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+#pragma unroll
+            for (int dd = 16; dd > 0; dd >>= 1) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], dd);
+            if (voie == 0) {
+                const float y = d.biais[m] != nullptr ? acc[j] + d.biais[m][rl] : acc[j];
+                d.y[m][uint64_t(j) * d.lignes[m] + rl] = y;
+                if (J == 1 && d.residu != nullptr) d.residu[rl] = __fadd_rn(d.residu[rl], y);
+            }
+        }
+        __syncwarp();  // this buffer is refilled two rows from now
+    }
+    cp_async_wait<0>();
+}
+
 // ------------------------------------------------------------------ RMSNorm
 
 __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w, float* y,
@@ -434,6 +543,47 @@ cudaError_t lancer_gemv_q8_0_lot(const void* w, const float* x, const float* bia
             case 6: e = lancer_q8_0_j<6>(w, xj, biais, yj, R, C, flux); break;
             case 7: e = lancer_q8_0_j<7>(w, xj, biais, yj, R, C, flux); break;
             default: e = lancer_q8_0_j<8>(w, xj, biais, yj, R, C, flux); break;
+        }
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+template <int J>
+static cudaError_t lancer_q8_0_couche_j(const DescQ8Couche& d, uint32_t R, cudaStream_t flux) {
+    const size_t smem = J * q8_x_octets(d.C) + Q8_WARPS * 2u * q8_tampon(d.C);
+    cudaError_t e = assurer_smem(reinterpret_cast<const void*>(k_q8_0_couche<J>), int(smem));
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t par_sm = std::max<uint32_t>(1u, std::min<uint32_t>(4u, uint32_t(200000 / smem)));
+    const uint32_t blocs = std::min<uint32_t>((R + Q8_WARPS - 1) / Q8_WARPS, uint32_t(sms) * par_sm);
+    return lancer_pdl(k_q8_0_couche<J>, dim3(blocs), dim3(Q8_WARPS * 32), smem, flux, d);
+}
+
+cudaError_t lancer_q8_0_couche(const DescQ8Couche& d, cudaStream_t flux, uint32_t jetons) {
+    if (d.n == 0 || d.n > 3 || d.C % 32u != 0 || jetons == 0) return cudaErrorInvalidValue;
+    if ((d.norme != nullptr || d.residu != nullptr) && jetons != 1) return cudaErrorInvalidValue;
+    if (d.residu != nullptr && d.n != 1) return cudaErrorInvalidValue;
+    uint32_t R = 0;
+    for (uint32_t m = 0; m < d.n; ++m) R += d.lignes[m];
+    if (R == 0) return cudaSuccess;
+    // batches by launches of up to Q8_LOT_MAX tokens
+    for (uint32_t j0 = 0; j0 < jetons; j0 += Q8_LOT_MAX) {
+        const uint32_t n = std::min(Q8_LOT_MAX, jetons - j0);
+        DescQ8Couche dj = d;
+        dj.x = d.x + uint64_t(j0) * d.C;
+        for (uint32_t m = 0; m < d.n; ++m) dj.y[m] = d.y[m] + uint64_t(j0) * d.lignes[m];
+        cudaError_t e;
+        switch (n) {
+            case 1: e = lancer_q8_0_couche_j<1>(dj, R, flux); break;
+            case 2: e = lancer_q8_0_couche_j<2>(dj, R, flux); break;
+            case 3: e = lancer_q8_0_couche_j<3>(dj, R, flux); break;
+            case 4: e = lancer_q8_0_couche_j<4>(dj, R, flux); break;
+            case 5: e = lancer_q8_0_couche_j<5>(dj, R, flux); break;
+            case 6: e = lancer_q8_0_couche_j<6>(dj, R, flux); break;
+            case 7: e = lancer_q8_0_couche_j<7>(dj, R, flux); break;
+            default: e = lancer_q8_0_couche_j<8>(dj, R, flux); break;
         }
         if (e != cudaSuccess) return e;
     }

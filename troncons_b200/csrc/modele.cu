@@ -301,10 +301,27 @@ cudaError_t etape_attention(const trc_modele_config& m, const DispositionModele&
     const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(m.couches_desc)[l];
     tb::ParamsRope rope;
     std::memcpy(&rope, &m.rope, sizeof rope);
-    ESSAI(tb::lancer_rmsnorm(F(d.x), P(c.attn_norm), F(d.h), D, 1, m.eps, f));
-    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wq), F(d.h), P(c.bq), F(d.q), dq, D, f));
-    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wk), F(d.h), P(c.bk), F(d.k), dkv, D, f));
-    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wv), F(d.h), P(c.bv), F(d.v), dkv, D, f));
+    // RMSNorm and the q / k / v projections in one launch (the same bits as four)
+    tb::DescQ8Couche qkv{};
+    qkv.w[0] = reinterpret_cast<const void*>(c.wq);
+    qkv.w[1] = reinterpret_cast<const void*>(c.wk);
+    qkv.w[2] = reinterpret_cast<const void*>(c.wv);
+    qkv.biais[0] = P(c.bq);
+    qkv.biais[1] = P(c.bk);
+    qkv.biais[2] = P(c.bv);
+    qkv.y[0] = F(d.q);
+    qkv.y[1] = F(d.k);
+    qkv.y[2] = F(d.v);
+    qkv.lignes[0] = dq;
+    qkv.lignes[1] = dkv;
+    qkv.lignes[2] = dkv;
+    qkv.n = 3;
+    qkv.C = D;
+    qkv.x = F(d.x);
+    qkv.norme = P(c.attn_norm);
+    qkv.eps = m.eps;
+    qkv.h = F(d.h);
+    ESSAI(tb::lancer_q8_0_couche(qkv, f));
     ESSAI(tb::lancer_rope_yarn(F(d.q), F(d.k), m.tetes, m.tetes_kv, position, rope, f));
     const uint32_t case_kv = c.anneau ? position % c.anneau : position;
     ESSAI(tb::lancer_ecrire_kv(F(d.k), F(d.v), reinterpret_cast<uint16_t*>(c.cache_k), reinterpret_cast<uint16_t*>(c.cache_v),
@@ -319,8 +336,17 @@ cudaError_t etape_attention(const trc_modele_config& m, const DispositionModele&
     pa.echelle = 1.0f / std::sqrt(float(m.dim_tete));
     ESSAI(tb::lancer_attention(F(d.q), reinterpret_cast<const uint16_t*>(c.cache_k),
                                reinterpret_cast<const uint16_t*>(c.cache_v), P(c.puits), F(d.a), pa, f));
-    ESSAI(tb::lancer_gemv_q8_0(reinterpret_cast<const void*>(c.wo), F(d.a), P(c.bo), F(d.o), D, dq, f));
-    ESSAI(tb::lancer_combiner(F(d.x), F(d.o), D, nullptr, 1, D, f));
+    // the output projection with x += o folded in (the same bits as the GEMV, then the combine)
+    tb::DescQ8Couche o{};
+    o.w[0] = reinterpret_cast<const void*>(c.wo);
+    o.biais[0] = P(c.bo);
+    o.y[0] = F(d.o);
+    o.lignes[0] = D;
+    o.n = 1;
+    o.C = dq;
+    o.x = F(d.a);
+    o.residu = F(d.x);
+    ESSAI(tb::lancer_q8_0_couche(o, f));
     ESSAI(tb::lancer_rmsnorm(F(d.x), P(c.post_norm), F(d.h2), D, 1, m.eps, f));
     return cudaSuccess;
 }
@@ -407,9 +433,24 @@ cudaError_t etape_attention_lot(const trc_modele_config* const* seqs, uint32_t n
     std::memcpy(&rope, &m.rope, sizeof rope);
     for (uint32_t i = 0; i < n; ++i)
         ESSAI(tb::lancer_rmsnorm(X(i, &DispositionModele::x), P(c0.attn_norm), L(b.h) + uint64_t(i) * D, D, 1, m.eps, f));
-    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wq), L(b.h), P(c0.bq), L(b.q), dq, D, n, f));
-    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wk), L(b.h), P(c0.bk), L(b.k), dkv, D, n, f));
-    ESSAI(tb::lancer_gemv_q8_0_lot(reinterpret_cast<const void*>(c0.wv), L(b.h), P(c0.bv), L(b.v), dkv, D, n, f));
+    // the q / k / v projections of the n tokens in one launch per 8 tokens
+    tb::DescQ8Couche qkv{};
+    qkv.w[0] = reinterpret_cast<const void*>(c0.wq);
+    qkv.w[1] = reinterpret_cast<const void*>(c0.wk);
+    qkv.w[2] = reinterpret_cast<const void*>(c0.wv);
+    qkv.biais[0] = P(c0.bq);
+    qkv.biais[1] = P(c0.bk);
+    qkv.biais[2] = P(c0.bv);
+    qkv.y[0] = L(b.q);
+    qkv.y[1] = L(b.k);
+    qkv.y[2] = L(b.v);
+    qkv.lignes[0] = dq;
+    qkv.lignes[1] = dkv;
+    qkv.lignes[2] = dkv;
+    qkv.n = 3;
+    qkv.C = D;
+    qkv.x = L(b.h);
+    ESSAI(tb::lancer_q8_0_couche(qkv, f, n));
     for (uint32_t i = 0; i < n; ++i) {
         const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(seqs[i]->couches_desc)[l];
         float* q = L(b.q) + uint64_t(i) * dq;

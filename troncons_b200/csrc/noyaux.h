@@ -158,6 +158,26 @@ cudaError_t lancer_gemv_q8_0(const void* w, const float* x, const float* biais, 
                              cudaStream_t flux);
 cudaError_t lancer_rmsnorm(const float* x, const float* w, float* y, uint32_t n, uint32_t lignes, float eps,
                            cudaStream_t flux);
+// One launch of up to three Q8_0 GEMVs on the same input (the rows of matrix 0, then 1, then 2),
+// each row in lancer_gemv_q8_0's order: with `norme`, the input is RMSNorm(x) (lancer_rmsnorm's
+// order, recomputed by every block; block 0 also writes it to `h` when given); with `residu`
+// (one matrix), residu[r] += y[r] after y[r] is written (lancer_combiner's single-term add).
+// `jetons` tokens (x [jetons][C], y[m] [jetons][lignes[m]]; neither norme nor residu) in
+// launches of up to Q8_LOT_MAX, as lancer_gemv_q8_0_lot.
+struct DescQ8Couche {
+    const void* w[3];
+    const float* biais[3];
+    float* y[3];
+    uint32_t lignes[3];
+    uint32_t n;  // matrices
+    uint32_t C;
+    const float* x;
+    const float* norme;
+    float eps;
+    float* h;
+    float* residu;
+};
+cudaError_t lancer_q8_0_couche(const DescQ8Couche& d, cudaStream_t flux, uint32_t jetons = 1);
 cudaError_t lancer_rope_yarn(float* q, float* k, uint32_t tetes_q, uint32_t tetes_k, uint32_t position, const ParamsRope& p,
                              cudaStream_t flux);
 cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t dkv, uint32_t case_kv,
