@@ -515,7 +515,7 @@ def legs_couche(args, c, cc, xs_dev, res_dev, idx, vidange, pic: float) -> dict:
     out["raw_layer"] = {
         "value": round(octets / (sum(t) * 1e-3) / 1e9, 2), "unit": UNITE, "ms_per_step": round(sum(t) / args.steps, 4),
         "bytes_per_step": round(octets / args.steps),
-        "roofline": {"bound": "hbm", "kernel": "k_moe_brut (gate/up: CODES_BRUTS + ECHELLES_BRUTES of the routed experts)",
+        "roofline": {"bound": "hbm", "kernel": "k_moe_brut_groupes (gate/up: CODES_BRUTS + ECHELLES_BRUTES of the routed experts)",
                      "achieved": round(ach, 1), "peak": pic, "unit": "GB/s", "frac": round(ach / pic, 4),
                      "frac_8tbs": round(ach / 8000.0, 4), "ms": round(float(np.mean(ph)), 4),
                      "algorithmic_bytes_per_launch": round(brut_gu / args.steps)}}

@@ -329,6 +329,41 @@ __global__ void __launch_bounds__(256) k_ecrire_kv(const float* __restrict__ k, 
     cache_v[o] = __half_as_ushort(__float2half_rn(v[i]));
 }
 
+// The rotation and the KV write in one launch: blocks of q heads rotate as k_rope_yarn; a block of
+// kv head h rotates k's head h, then writes its f16 rounding (k_ecrire_kv's) into the position's
+// case of cache_k, and v's head h into cache_v. Element for element the same bits as the two
+// launches (q and k also keep their rotated f32 values).
+__global__ void __launch_bounds__(64) k_rope_kv(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v,
+                                                uint16_t* __restrict__ cache_k, uint16_t* __restrict__ cache_v,
+                                                uint32_t tetes_q, uint32_t tetes_k, uint32_t position, uint32_t case_kv,
+                                                ParamsRope p) {
+    attendre_amont();
+    liberer_aval();
+    const uint32_t demi = p.dim_tete / 2u, i = threadIdx.x;
+    if (i >= demi || blockIdx.x >= tetes_q + tetes_k) return;
+    double m;
+    const double inv = yarn_inv_freq(p, i, m);
+    double s, c;
+    sincos(double(position) * inv, &s, &c);
+    c *= m;
+    s *= m;
+    const bool est_k = blockIdx.x >= tetes_q;
+    const uint32_t h = est_k ? blockIdx.x - tetes_q : blockIdx.x;
+    float* t = (est_k ? k : q) + uint64_t(h) * p.dim_tete;
+    const double a = t[i], b = t[i + demi];
+    const float r0 = float(a * c - b * s), r1 = float(b * c + a * s);
+    t[i] = r0;
+    t[i + demi] = r1;
+    if (est_k) {
+        const uint64_t o = uint64_t(case_kv) * tetes_k * p.dim_tete + uint64_t(h) * p.dim_tete;
+        const float* vh = v + uint64_t(h) * p.dim_tete;
+        cache_k[o + i] = __half_as_ushort(__float2half_rn(r0));
+        cache_k[o + i + demi] = __half_as_ushort(__float2half_rn(r1));
+        cache_v[o + i] = __half_as_ushort(__float2half_rn(vh[i]));
+        cache_v[o + i + demi] = __half_as_ushort(__float2half_rn(vh[i + demi]));
+    }
+}
+
 // ------------------------------------------------------------------ attention of one position
 
 // Attention of one position, split over positions and merged inside a thread-block cluster.
@@ -598,6 +633,13 @@ cudaError_t lancer_rmsnorm(const float* x, const float* w, float* y, uint32_t n,
 cudaError_t lancer_rope_yarn(float* q, float* k, uint32_t tetes_q, uint32_t tetes_k, uint32_t position, const ParamsRope& p,
                              cudaStream_t flux) {
     return lancer_pdl(k_rope_yarn, dim3(tetes_q + tetes_k), dim3(p.dim_tete / 2u), 0, flux, q, k, tetes_q, tetes_k, position, p);
+}
+
+cudaError_t lancer_rope_kv(float* q, float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t tetes_q,
+                           uint32_t tetes_k, uint32_t position, uint32_t case_kv, const ParamsRope& p, cudaStream_t flux) {
+    if (p.dim_tete == 0 || p.dim_tete % 2u != 0 || p.dim_tete > 128u) return cudaErrorInvalidValue;
+    return lancer_pdl(k_rope_kv, dim3(tetes_q + tetes_k), dim3(p.dim_tete / 2u), 0, flux, q, k, v, ck, cv, tetes_q, tetes_k,
+                      position, case_kv, p);
 }
 
 cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t dkv, uint32_t case_kv,

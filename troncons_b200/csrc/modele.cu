@@ -322,10 +322,9 @@ cudaError_t etape_attention(const trc_modele_config& m, const DispositionModele&
     qkv.eps = m.eps;
     qkv.h = F(d.h);
     ESSAI(tb::lancer_q8_0_couche(qkv, f));
-    ESSAI(tb::lancer_rope_yarn(F(d.q), F(d.k), m.tetes, m.tetes_kv, position, rope, f));
     const uint32_t case_kv = c.anneau ? position % c.anneau : position;
-    ESSAI(tb::lancer_ecrire_kv(F(d.k), F(d.v), reinterpret_cast<uint16_t*>(c.cache_k), reinterpret_cast<uint16_t*>(c.cache_v),
-                               dkv, case_kv, f));
+    ESSAI(tb::lancer_rope_kv(F(d.q), F(d.k), F(d.v), reinterpret_cast<uint16_t*>(c.cache_k),
+                             reinterpret_cast<uint16_t*>(c.cache_v), m.tetes, m.tetes_kv, position, case_kv, rope, f));
     tb::ParamsAttention pa{};
     pa.tetes = m.tetes;
     pa.tetes_kv = m.tetes_kv;
@@ -455,10 +454,9 @@ cudaError_t etape_attention_lot(const trc_modele_config* const* seqs, uint32_t n
         const trc_modele_couche& c = reinterpret_cast<const trc_modele_couche*>(seqs[i]->couches_desc)[l];
         float* q = L(b.q) + uint64_t(i) * dq;
         float* k = L(b.k) + uint64_t(i) * dkv;
-        ESSAI(tb::lancer_rope_yarn(q, k, m.tetes, m.tetes_kv, position, rope, f));
         const uint32_t case_kv = c.anneau ? position % c.anneau : position;
-        ESSAI(tb::lancer_ecrire_kv(k, L(b.v) + uint64_t(i) * dkv, reinterpret_cast<uint16_t*>(c.cache_k),
-                                   reinterpret_cast<uint16_t*>(c.cache_v), dkv, case_kv, f));
+        ESSAI(tb::lancer_rope_kv(q, k, L(b.v) + uint64_t(i) * dkv, reinterpret_cast<uint16_t*>(c.cache_k),
+                                 reinterpret_cast<uint16_t*>(c.cache_v), m.tetes, m.tetes_kv, position, case_kv, rope, f));
         tb::ParamsAttention pa{};
         pa.tetes = m.tetes;
         pa.tetes_kv = m.tetes_kv;

@@ -180,6 +180,9 @@ struct DescQ8Couche {
 cudaError_t lancer_q8_0_couche(const DescQ8Couche& d, cudaStream_t flux, uint32_t jetons = 1);
 cudaError_t lancer_rope_yarn(float* q, float* k, uint32_t tetes_q, uint32_t tetes_k, uint32_t position, const ParamsRope& p,
                              cudaStream_t flux);
+// lancer_rope_yarn then lancer_ecrire_kv (dkv = tetes_k x dim_tete) in one launch, the same bits.
+cudaError_t lancer_rope_kv(float* q, float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t tetes_q,
+                           uint32_t tetes_k, uint32_t position, uint32_t case_kv, const ParamsRope& p, cudaStream_t flux);
 cudaError_t lancer_ecrire_kv(const float* k, const float* v, uint16_t* ck, uint16_t* cv, uint32_t dkv, uint32_t case_kv,
                              cudaStream_t flux);
 cudaError_t lancer_attention(const float* q, const uint16_t* ck, const uint16_t* cv, const float* puits, float* sortie,
