@@ -386,6 +386,47 @@ struct Decodeur {
         return e;
     }
 
+    // The look-ahead form on the table restaged as 64-bit entries {f, i - c} (lut2, from
+    // restager_lut2) with the symbols in a byte table: y = f (x >> 12) + (i - c) is one multiply-
+    // add of the loaded entry, the fields no longer extracted on the chain; the symbol is read
+    // beside it, off the chain. The same arithmetic as pas_avance, so the same states and bytes.
+    struct Avance2 {
+        uint2 e, lp;
+        uint32_t wp;
+    };
+
+    __device__ __forceinline__ void debut_avance2(const uint2* lut2, Avance2& s) {
+        s.e = lut2[x & (M - 1u)];
+        s.wp = anneau[(pa & (ANNEAU_MOTS - 1u)) + voie];
+        s.lp = lut2[s.wp & (M - 1u)];
+    }
+
+    __device__ __forceinline__ uint32_t pas_avance2(const uint2* lut2, const uint8_t* symboles, Avance2& s) {
+        const uint32_t symbole = symboles[x & (M - 1u)];
+        const uint32_t y = s.e.x * (x >> 12) + s.e.y;
+        const uint2 ey = lut2[y & (M - 1u)];
+        const bool besoin = y < L;
+        const uint32_t vote = __ballot_sync(0xFFFFFFFFu, besoin);
+        const uint32_t rang = __popc(vote & masque_inf);
+        const uint32_t w = __shfl_sync(0xFFFFFFFFu, s.wp, rang);
+        const uint32_t f = __shfl_sync(0xFFFFFFFFu, s.lp.x, rang);
+        const uint32_t b = __shfl_sync(0xFFFFFFFFu, s.lp.y, rang);
+        x = besoin ? __byte_perm(w, y, 0x5410) : y;
+        s.e = besoin ? make_uint2(f, b) : ey;
+        pa += __popc(vote);
+        s.wp = anneau[(pa & (ANNEAU_MOTS - 1u)) + voie];
+        s.lp = lut2[s.wp & (M - 1u)];
+        return symbole;
+    }
+
+    __device__ __forceinline__ uint32_t macro_avance2(const uint2* lut2, const uint8_t* symboles, Avance2& s) {
+        uint32_t m = pas_avance2(lut2, symboles, s);
+        m = __byte_perm(m, pas_avance2(lut2, symboles, s), 0x0040);
+        m = __byte_perm(m, pas_avance2(lut2, symboles, s), 0x0410);
+        m = __byte_perm(m, pas_avance2(lut2, symboles, s), 0x4210);
+        return m;
+    }
+
     __device__ __forceinline__ uint32_t macro_avance(const uint32_t* lut, Avance& s) {
         uint32_t m = pas_avance(lut, s);
         m = __byte_perm(m, pas_avance(lut, s), 0x0040);

@@ -115,6 +115,31 @@ __device__ __forceinline__ void copier16(uint4* dst, const uint4* __restrict__ s
     for (; t < n; t += pas) dst[t] = __ldg(src + t);
 }
 
+// A table of M entries s | (f - 1) << 8 | (i - c) << 20 (abi.rs:187-221's layout) restaged as
+// {f, i - c} pairs and a byte table of the symbols, for Decodeur::pas_avance2; each thread has up
+// to 8 loads of 4 entries in flight before it stores.
+__device__ __forceinline__ void restager_lut2(uint2* lut2, uint8_t* symboles, const uint32_t* __restrict__ src) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    const uint32_t pas = blockDim.x;
+    auto poser = [&](uint32_t q, const uint4 v) {
+        const uint32_t e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (uint32_t k = 0; k < 4; ++k) {
+            lut2[4u * q + k] = make_uint2(((e[k] >> 8) & 0xFFFu) + 1u, e[k] >> 20);
+            symboles[4u * q + k] = uint8_t(e[k]);
+        }
+    };
+    uint32_t t = threadIdx.x;
+    for (; t + 7u * pas < M / 4u; t += 8u * pas) {
+        uint4 v[8];
+#pragma unroll
+        for (uint32_t k = 0; k < 8u; ++k) v[k] = __ldg(s4 + t + k * pas);
+#pragma unroll
+        for (uint32_t k = 0; k < 8u; ++k) poser(t + k * pas, v[k]);
+    }
+    for (; t < M / 4u; t += pas) poser(t, __ldg(s4 + t));
+}
+
 constexpr uint32_t DELTA_WARPS = 1;  // one DELTA tile per block: each chain alone on its SM
 constexpr uint32_t MOE_WARPS = 8;  // k_moe_brut: warps per block (one row at a time each)
 constexpr uint32_t BRUT_BLOCS_SM = 3;  // its blocks per SM: the grid is one wave of them
@@ -122,12 +147,13 @@ constexpr uint32_t BRUT_BLOCS_SM = 3;  // its blocks per SM: the grid is one wav
 // ------------------------------------------------------------------ 1. DELTA -> scales, classes
 
 __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
-    __shared__ __align__(16) uint32_t lut[M];
+    __shared__ __align__(16) uint2 lut2[M];
+    __shared__ __align__(16) uint8_t symboles[M];
     __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_ALLOC];
     const Couche& c = a.c;
     const uint32_t j = blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
     // The LUTs are an input of the layer; the routed experts come from the previous kernel.
-    copier16(reinterpret_cast<uint4*>(lut), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u) * M), M / 4u);
+    restager_lut2(lut2, symboles, c.luts + (uint64_t(j) * 4u) * M);
     attendre_amont();
     liberer_aval();
     if (!a.tous && !tenu(c, i)) return;
@@ -160,13 +186,13 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     Decodeur d;
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * DELTA_WARPS) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
-        Decodeur::Avance av;
-        d.debut_avance(lut, av);  // one table for every lane: the look-ahead form
+        Decodeur::Avance2 av;
+        d.debut_avance2(lut2, av);  // one table for every lane: the look-ahead form
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         // Word w = 32 m + lane is the delta of blocks 4w .. 4w + 3, stored as it comes.
         for (uint32_t m = m0; m < m1; ++m) {
             d.avancer();
-            const uint32_t mot = d.macro_avance(lut, av);
+            const uint32_t mot = d.macro_avance2(lut2, symboles, av);
             const uint32_t b0 = 4u * (m * 32u + voie);
             if (b0 + 3u < nblocs) {
                 *reinterpret_cast<uint32_t*>(delta + b0) = mot;
