@@ -146,14 +146,23 @@ constexpr uint32_t BRUT_BLOCS_SM = 3;  // its blocks per SM: the grid is one wav
 
 // ------------------------------------------------------------------ 1. DELTA -> scales, classes
 
+// PAIRES: the table restaged as {f, i - c} pairs (39 KB of shared memory per block: the shorter
+// chain, for launches whose blocks all fit the SMs at once); otherwise the table as stored (18 KB:
+// twice as many blocks per SM when a launch runs in waves, every expert of a layer at once).
+template <bool PAIRES>
 __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
-    __shared__ __align__(16) uint2 lut2[M];
-    __shared__ __align__(16) uint8_t symboles[M];
+    __shared__ __align__(16) uint32_t lut_brute[PAIRES ? 1 : M];
+    __shared__ __align__(16) uint2 lut2[PAIRES ? M : 1];
+    __shared__ __align__(16) uint8_t symboles[PAIRES ? M : 1];
     __shared__ __align__(16) uint16_t anneaux[DELTA_WARPS][ANNEAU_ALLOC];
     const Couche& c = a.c;
     const uint32_t j = blockIdx.y, i = blockIdx.z, voie = threadIdx.x & 31u;
     // The LUTs are an input of the layer; the routed experts come from the previous kernel.
-    restager_lut2(lut2, symboles, c.luts + (uint64_t(j) * 4u) * M);
+    if constexpr (PAIRES)
+        restager_lut2(lut2, symboles, c.luts + (uint64_t(j) * 4u) * M);
+    else
+        copier16(reinterpret_cast<uint4*>(lut_brute), reinterpret_cast<const uint4*>(c.luts + (uint64_t(j) * 4u) * M),
+                 M / 4u);
     attendre_amont();
     liberer_aval();
     if (!a.tous && !tenu(c, i)) return;
@@ -186,13 +195,22 @@ __global__ void __launch_bounds__(DELTA_WARPS * 32) k_moe_delta(ArgsMoe a) {
     Decodeur d;
     for (uint32_t t = warp0 + (threadIdx.x >> 5); t < h.T; t += gridDim.x * DELTA_WARPS) {
         d.debut(h, t, voie, anneaux[threadIdx.x >> 5]);
-        Decodeur::Avance2 av;
-        d.debut_avance2(lut2, av);  // one table for every lane: the look-ahead form
+        // one table for every lane: the look-ahead form
+        Decodeur::Avance2 av2;
+        Decodeur::Avance av;
+        if constexpr (PAIRES)
+            d.debut_avance2(lut2, av2);
+        else
+            d.debut_avance(lut_brute, av);
         const uint32_t m0 = t * h.N, m1 = min(m0 + h.N, nmacro);
         // Word w = 32 m + lane is the delta of blocks 4w .. 4w + 3, stored as it comes.
         for (uint32_t m = m0; m < m1; ++m) {
             d.avancer();
-            const uint32_t mot = d.macro_avance2(lut2, symboles, av);
+            uint32_t mot;
+            if constexpr (PAIRES)
+                mot = d.macro_avance2(lut2, symboles, av2);
+            else
+                mot = d.macro_avance(lut_brute, av);
             const uint32_t b0 = 4u * (m * 32u + voie);
             if (b0 + 3u < nblocs) {
                 *reinterpret_cast<uint32_t*>(delta + b0) = mot;
@@ -1156,14 +1174,17 @@ cudaError_t lancer_moe(const Couche& c, void* espace, uint64_t espace_octets, cu
     marque(0);
     if (!c.brut) {
         // DELTA of the routed experts, unless the layer's deltas were decoded ahead.
-        if (c.deltas == nullptr &&
-            (e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, na), dim3(DELTA_WARPS * 32), 0,
-                            flux, a)) != cudaSuccess)
-            return e;
-        // Producer / consumer pairs while the launch's tiles fit them at once (lowest latency per
-        // tile); past that, one warp per tile with three times as many tiles in flight.
         int dev = 0, sms = 148;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (c.deltas == nullptr) {
+            const dim3 g((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, na);
+            e = uint64_t(g.x) * g.y * g.z <= 4ull * uint32_t(sms)
+                    ? lancer_pdl(k_moe_delta<true>, g, dim3(DELTA_WARPS * 32), 0, flux, a)
+                    : lancer_pdl(k_moe_delta<false>, g, dim3(DELTA_WARPS * 32), 0, flux, a);
+            if (e != cudaSuccess) return e;
+        }
+        // Producer / consumer pairs while the launch's tiles fit them at once (lowest latency per
+        // tile); past that, one warp per tile with three times as many tiles in flight.
         const uint64_t places = uint64_t(sms) * 2u * MOE_PAIRES;
         auto codes = [&](uint32_t matrices) -> cudaError_t {
             if (uint64_t(na) * matrices * tc <= places) {
@@ -1293,7 +1314,7 @@ cudaError_t lancer_predecoder_deltas(const Couche& c, uint8_t* deltas, cudaStrea
         const uint64_t nb = uint64_t(c.lignes[j]) * (c.colonnes[j] / 32u);
         td = std::max<uint32_t>(td, uint32_t(((nb + 127) / 128 + nd - 1) / nd));
     }
-    cudaError_t e = lancer_pdl(k_moe_delta, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.experts),
+    cudaError_t e = lancer_pdl(k_moe_delta<false>, dim3((td + DELTA_WARPS - 1) / DELTA_WARPS, 3, c.experts),
                                dim3(DELTA_WARPS * 32), 0, flux, a);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
