@@ -545,10 +545,11 @@ uint64_t trc_echange_octets(const trc_dims_expert* dims, uint32_t jetons, uint32
  * initialisation). */
 uint64_t trc_moe_espace_octets(const trc_dims_expert* dims, uint32_t k);
 
-/* Workspace bytes with which the fused layer overlaps the down projection's decode with gate/up
- * (k <= 32 activations; beyond, trc_moe_espace_octets): the down codes then go through the
- * workspace, 16 bytes per MXFP4 block and activation (16.6 MB more for gpt-oss at k = 4). Given
- * at least this, the layer takes that schedule; given less (but at least trc_moe_espace_octets),
+/* Workspace bytes with which the fused layer takes its overlapped schedule (k <= 32 activations;
+ * beyond, trc_moe_espace_octets): every CODES_CTX tile of the three matrices decoded in one
+ * launch, the decoded code words through the workspace (16 bytes per MXFP4 block and activation:
+ * 49.8 MB more for gpt-oss at k = 4, 53,199,360 bytes in all), then the GEMVs on them. Given at
+ * least this, the layer takes that schedule; given less (but at least trc_moe_espace_octets),
  * the sequential one. Both give the same bits. */
 uint64_t trc_moe_espace_recouvrant_octets(const trc_dims_expert* dims, uint32_t k);
 
